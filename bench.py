@@ -1,0 +1,614 @@
+#!/usr/bin/env python
+"""Benchmark of libstade_b200 on the configurations of BASELINE.json.
+
+Default workload: configuration C2 (the config the
+headline metric "adjoint grad-evals/sec at 1/2/4/8 B200" is quoted on for
+data parallelism): the adjoint of a 2-layer tanh MLP 784-512-10 with softmax
+cross-entropy, Float32, global mini-batch 65,536 samples. One step = one
+data-parallel gradient evaluation of the whole global batch:
+reset_accum / reset_reduced / reset_local (the generated epilogue's zeroing),
+the adjoint sweep on this rank's block of samples, and (N > 1) the NCCL sum of
+the :accum bucket and of the loss. With N GPUs each rank owns 65,536 / N
+samples (strong scaling: the grad-eval is fixed, its work is split).
+
+Also selectable with --config: heat2d (C3), affine_ls (C1), mlp2_ce_hv (C5),
+conv1d_relu_mse (C4); each is a single-GPU line (replicas at N > 1).
+
+    python bench.py [--gpus N --steps K --warmup W] [--config NAME] [--impl reference]
+
+Rank 0 prints one JSON line. Timing: W untimed warm-up steps, then exactly K
+steps between a barrier + synchronize on both sides; each step is bracketed by
+CUDA events on the launching stream and the L2 is flushed (256 MiB write)
+between steps, outside the events; the reported time is the max over ranks.
+`e2e` times the same step through the public Python / C-ABI entry points with
+the step's inputs copied from pinned host memory and the gradient and loss
+copied back, inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "stade.jl_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "adjoint grad-evals/sec at 1/2/4/8 B200; % of HBM or tensor-pipe roofline"
+UNIT = "grad-evals/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="mlp2_ce",
+                    choices=["mlp2_ce", "heat2d", "affine_ls", "mlp2_ce_hv", "conv1d_relu_mse"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="target length of the CPU-baseline sample")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock / throttle samples of this rank's GPU during the timed
+    region (200 ms period)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.lines = []
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            sel = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            sel = str(device_index)
+        self.cmd = ["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}",
+                    "--format=csv,noheader,nounits", "-lms", "200"]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if not self.proc:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        rows = []
+        for l in self.lines:
+            parts = [p.strip() for p in l.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]),
+                                 power=float(parts[3]) if parts[3] not in ("[N/A]", "") else 0.0,
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        smax = max(r["smax"] for r in rows)
+        loaded = [r for r in rows if r["power"] > 250.0] or rows
+        reasons = set()
+        for r in loaded:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def timed_loop(torch, step, steps, warmup, world, dist, flush, stream):
+    """W warm-up steps, barrier + sync, K steps each between CUDA events on the
+    launching stream with an L2 flush between steps (outside the events),
+    barrier + sync. Returns (max-over-ranks total ms, per-step ms list)."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush.add_(1)
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    per = [a.elapsed_time(b) for a, b in evs]
+    total = sum(per)
+    if world > 1:
+        t = torch.tensor([total], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total = float(t.item())
+    return total, per
+
+
+def roofline(phases, phase_work, steps, peaks, peak_src, traffic):
+    """Dominant phase by device time; achieved = algorithmic work per launch /
+    average launch time."""
+    best = None
+    for name, (ms, cnt) in phases.items():
+        if name not in phase_work or cnt == 0:
+            continue
+        if best is None or ms > best[1]:
+            best = (name, ms, cnt)
+    if best is None:
+        return None
+    name, ms, cnt = best
+    kind, work, note = phase_work[name]
+    avg_s = ms / cnt / 1e3
+    if kind == "hbm":
+        achieved = work / avg_s / 1e9
+        peak = peaks["hbm_gbs"]
+        unit = "GB/s"
+    else:
+        achieved = work / avg_s / 1e12
+        peak = peaks["bf16_tflops"]
+        unit = "TFLOP/s"
+    total_ms = sum(v[0] for v in phases.values())
+    return {"bound": "hbm" if kind == "hbm" else "tensor", "kernel": name, "achieved": achieved,
+            "peak": peak, "unit": unit, "frac": achieved / peak, "peak_source": peak_src,
+            "traffic": traffic.get(name) if traffic else None,
+            "launch_ms": ms / cnt, "share_of_step": ms / total_ms if total_ms else None,
+            "note": note}
+
+
+def load_traffic(config):
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(config, {})
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------------------
+# Workloads
+class Mlp2Ce:
+    name = "mlp2_ce"
+    dtype = "f32"
+    scaling = "strong"
+
+    def __init__(self, torch, rank, world, comm_factory):
+        import numpy as np
+        from stadeb200 import synth, kernels, ddp
+        self.torch, self.np, self.kernels, self.ddp = torch, np, kernels, ddp
+        self.world = world
+        c = synth.FULL["mlp2_ce"]
+        self.G, self.n_i, self.n_h, self.n_o = c["n_s"], c["n_i"], c["n_h"], c["n_o"]
+        rng = ddp.shard(self.G, rank, world)
+        self.n_s = len(rng)
+        lo, hi = rng.start, rng.stop
+        d = synth.mlp2_ce_inputs(self.G, self.n_i, self.n_h, self.n_o)
+        f32 = torch.float32
+        dev = "cuda"
+        self.host = {k: torch.from_numpy(v) for k, v in d.items()}
+        self.host["x"] = self.host["x"][lo * self.n_i:hi * self.n_i].contiguous()
+        self.host["y"] = self.host["y"][lo * self.n_o:hi * self.n_o].contiguous()
+        self.pinned = {k: v.pin_memory() for k, v in self.host.items()}
+        t = {k: v.to(dev) for k, v in self.host.items()}
+        S, I, H, O = self.n_s, self.n_i, self.n_h, self.n_o
+        z = lambda n: torch.zeros(n, dtype=f32, device=dev)
+        t.update(loss=z(1), xb=z(S * I), yb=z(S * O), w1b=z(I * H), b1b=z(H), w2b=z(H * O),
+                 b2b=z(O), h=z(S * H), hb=z(S * H), zz=z(S * O), zb=z(S * O), p=z(S * O),
+                 pb=z(S * O))
+        self.t = t
+        self.ws = torch.empty(kernels.mlp2_ce_b_workspace(S, I, H, O), dtype=torch.uint8, device=dev)
+        self.comm = comm_factory() if world > 1 else None
+        self.grad_host = {k: torch.empty(t[k].numel(), dtype=f32).pin_memory()
+                          for k in ("w1b", "b1b", "w2b", "b2b", "loss")}
+
+    def step(self):
+        t, d = self.t, self.ddp
+        d.mlp2_ce_b_reset_accum_(t["w1b"], t["b1b"], t["w2b"], t["b2b"])
+        d.mlp2_ce_b_reset_reduced_(t["loss"])
+        d.mlp2_ce_b_reset_local_(t["xb"], t["yb"], t["hb"], t["zb"], t["pb"])
+        self.kernels.mlp2_ce_b_cuda(t["loss"], t["lossb"], t["x"], t["xb"], t["y"], t["yb"],
+                                    t["w1"], t["w1b"], t["b1"], t["b1b"], t["w2"], t["w2b"],
+                                    t["b2"], t["b2b"], t["h"], t["hb"], t["zz"], t["zb"], t["p"],
+                                    t["pb"], self.n_s, self.n_i, self.n_h, self.n_o,
+                                    workspace=self.ws)
+        if self.comm is not None:
+            d.allreduce_sum_(self.comm, t["w1b"], t["b1b"], t["w2b"], t["b2b"])
+            d.allreduce_sum_(self.comm, t["loss"])
+
+    def e2e_step(self):
+        t, p = self.t, self.pinned
+        for k in ("x", "y", "w1", "b1", "w2", "b2"):
+            t[k].copy_(p[k], non_blocking=True)
+        self.step()
+        for k, v in self.grad_host.items():
+            v.copy_(t[k], non_blocking=True)
+
+    def e2e_bytes(self):
+        h2d = sum(self.pinned[k].numel() * 4 for k in ("x", "y", "w1", "b1", "w2", "b2"))
+        d2h = sum(v.numel() * 4 for v in self.grad_host.values())
+        return h2d, d2h
+
+    def phase_work(self):
+        S, I, H, O = self.n_s, self.n_i, self.n_h, self.n_o
+        gemm = 2.0 * S * I * H
+        return {"fwd_gemm": ("tensor", gemm, "x W1 (2 S I H flops), tanh epilogue"),
+                "w1b_gemm": ("tensor", gemm + S * H, "x^T s1b + colsum (2 S I H + S H flops)"),
+                "xb_gemm": ("tensor", gemm, "s1b W1^T (2 S I H flops)"),
+                "head": ("hbm", 4.0 * S * H * 4 + 8.0 * S * O * 4,
+                         "reads h, hb; writes s1b, hb (4 S H floats) + per-class arrays"),
+                "w2b": ("hbm", 4.0 * S * H + 4.0 * S * O, "reads h and g once")}
+
+    def config(self):
+        return {"workload": "C2 mlp2_ce_b: 2-layer tanh MLP 784-512-10 softmax cross-entropy "
+                            "adjoint, Float32, per-sample shadow-weight accumulation",
+                "global_batch": self.G, "per_rank_batch": self.n_s, "n_i": self.n_i,
+                "n_h": self.n_h, "n_o": self.n_o, "parallelism": f"dp{self.world}",
+                "l2": "flushed between timed steps (256 MiB write outside the events)"}
+
+    def cpu_baseline(self, seconds):
+        """Oracle (the restated generated sweep), OpenMP over samples, on a
+        bounded sample of the batch; scaled to grad-evals of the 65,536 batch."""
+        np = self.np
+        from oracle import oracle as orc
+        from stadeb200 import synth
+        threads = os.cpu_count() or 1
+
+        def run(m):
+            d = synth.mlp2_ce_inputs(m, self.n_i, self.n_h, self.n_o)
+            f = np.float32
+            z = lambda n: np.zeros(n, f)
+            a = dict(loss=z(1), lossb=d["lossb"], x=d["x"], xb=z(m * self.n_i), y=d["y"],
+                     yb=z(m * self.n_o), w1=d["w1"], w1b=z(self.n_i * self.n_h), b1=d["b1"],
+                     b1b=z(self.n_h), w2=d["w2"], w2b=z(self.n_h * self.n_o), b2=d["b2"],
+                     b2b=z(self.n_o), h=z(m * self.n_h), hb=z(m * self.n_h), z=z(m * self.n_o),
+                     zb=z(m * self.n_o), p=z(m * self.n_o), pb=z(m * self.n_o))
+            t0 = time.perf_counter()
+            orc.mlp2_ce_b(*a.values(), m, self.n_i, self.n_h, self.n_o, threads=threads)
+            return time.perf_counter() - t0
+
+        m0 = 64 * threads
+        t0 = run(m0)
+        m = int(min(self.G, max(m0, m0 * seconds / max(t0, 1e-3))))
+        t = run(m)
+        return {"value": (m / t) / self.G, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{m} of {self.G} samples (oracle.cc OpenMP sweep, {threads} threads), "
+                          f"{t:.2f} s, scaled to the full batch"}
+
+
+class Heat2d:
+    name = "heat2d"
+    dtype = "f64"
+    scaling = "weak"
+
+    def __init__(self, torch, rank, world, comm_factory):
+        import numpy as np
+        from stadeb200 import synth, kernels
+        self.torch, self.np, self.kernels = torch, np, kernels
+        c = synth.FULL["heat2d"]
+        self.n, self.n_step, self.alpha = c["n"], c["n_step"], c["alpha"]
+        self.world = world
+        n = self.n
+        d = synth.heat2d_inputs(n)
+        f64 = torch.float64
+        self.pinned = {"u": torch.from_numpy(d["u"]).pin_memory()}
+        z = lambda m: torch.zeros(m, dtype=f64, device="cuda")
+        self.t = dict(loss=z(1), lossb=torch.ones(1, dtype=f64, device="cuda"),
+                      u=self.pinned["u"].to("cuda"), ub=z(n * n), un=z(n * n), unb=z(n * n),
+                      alphab=z(1))
+        self.stack = kernels.initstacks_heat2d_b_cuda(n, self.n_step)
+        self.ws = torch.empty(kernels.heat2d_b_workspace(n, self.n_step), dtype=torch.uint8,
+                              device="cuda")
+        self.out_host = torch.empty(n * n, dtype=f64).pin_memory()
+        self.ab_host = torch.empty(1, dtype=f64).pin_memory()
+
+    def step(self):
+        t = self.t
+        t["ub"].zero_()
+        t["loss"].zero_()
+        t["alphab"].zero_()
+        self.kernels.heat2d_b_cuda_device(t["loss"], t["lossb"], t["u"], t["ub"], t["un"],
+                                          t["unb"], self.alpha, t["alphab"], self.n, self.n_step,
+                                          self.stack, workspace=self.ws)
+
+    def e2e_step(self):
+        self.t["u"].copy_(self.pinned["u"], non_blocking=True)
+        self.step()
+        self.out_host.copy_(self.t["ub"], non_blocking=True)
+        self.ab_host.copy_(self.t["alphab"], non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.n * self.n * 8, self.n * self.n * 8 + 8
+
+    def phase_work(self):
+        N = float(self.n) * self.n
+        return {"fwd_step": ("hbm", 16.0 * N, "read u_k, write u_k+1 (tape)"),
+                "bwd_step": ("hbm", 24.0 * N, "read unb_k, read tape u_k-1, write ub_k-1"),
+                "bwd_init": ("hbm", 32.0 * N, "read ub, unb, u_final; write seed")}
+
+    def config(self):
+        return {"workload": "C3 heat2d_b: periodic 5-point heat adjoint, 8192^2 Float64, 16 taped "
+                            "steps, alpha 0.2", "n": self.n, "n_step": self.n_step,
+                "parallelism": f"replicas{self.world}",
+                "l2": "inputs larger than L2 (512 MiB fields) and L2 flushed between steps"}
+
+    def cpu_baseline(self, seconds):
+        np = self.np
+        from oracle import oracle as orc
+        n = self.n
+        u = self.pinned["u"].numpy().copy()
+        z = lambda m: np.zeros(m, np.float64)
+        stack = z(n * n)
+        t0 = time.perf_counter()
+        orc.heat2d_b(z(1), np.ones(1), u, z(n * n), z(n * n), z(n * n), self.alpha, 0.0, n, 1, stack)
+        t = time.perf_counter() - t0
+        per_eval = t * self.n_step
+        return {"value": 1.0 / per_eval, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"1 of {self.n_step} time steps on the full {n}^2 grid (oracle.cc, "
+                          f"serial), {t:.2f} s, scaled x{self.n_step}"}
+
+
+class AffineLs:
+    name = "affine_ls"
+    dtype = "f64"
+    scaling = "weak"
+
+    def __init__(self, torch, rank, world, comm_factory):
+        import numpy as np
+        from stadeb200 import synth, kernels
+        self.torch, self.np, self.kernels = torch, np, kernels
+        c = synth.FULL["affine_ls"]
+        self.n_s, self.n_o, self.n_i = c["n_s"], c["n_o"], c["n_i"]
+        self.world = world
+        d = synth.affine_ls_inputs(self.n_s, self.n_o, self.n_i)
+        f64 = torch.float64
+        self.pinned = {k: torch.from_numpy(v).pin_memory() for k, v in d.items()}
+        t = {k: v.to("cuda") for k, v in self.pinned.items()}
+        z = lambda m: torch.zeros(m, dtype=f64, device="cuda")
+        S, O, I = self.n_s, self.n_o, self.n_i
+        t.update(loss=z(1), wb=z(O * I), bb=z(O), xb=z(S * I), tb=z(S * O), y=z(S * O), yb=z(S * O))
+        self.t = t
+        self.ws = torch.empty(kernels.affine_ls_b_workspace(S, O, I), dtype=torch.uint8,
+                              device="cuda")
+        self.grad_host = {k: torch.empty(t[k].numel(), dtype=f64).pin_memory()
+                          for k in ("wb", "bb", "loss")}
+        self.graph = None
+
+    def _eval(self):
+        t = self.t
+        for k in ("wb", "bb", "xb", "tb", "loss"):
+            t[k].zero_()
+        self.kernels.affine_ls_b_cuda(t["loss"], t["lossb"], t["w"], t["wb"], t["b"], t["bb"],
+                                      t["x"], t["xb"], t["t"], t["tb"], t["y"], t["yb"],
+                                      self.n_s, self.n_o, self.n_i, workspace=self.ws)
+
+    def step(self):
+        self._eval()
+
+    def e2e_step(self):
+        t, p = self.t, self.pinned
+        for k in ("w", "b", "x", "t"):
+            t[k].copy_(p[k], non_blocking=True)
+        self._eval()
+        for k, v in self.grad_host.items():
+            v.copy_(t[k], non_blocking=True)
+
+    def e2e_bytes(self):
+        h2d = sum(self.pinned[k].numel() * 8 for k in ("w", "b", "x", "t"))
+        return h2d, sum(v.numel() * 8 for v in self.grad_host.values())
+
+    def phase_work(self):
+        return {}
+
+    def config(self):
+        return {"workload": "C1 affine_ls_b: y = W x + b, 0.5 sum (y - t)^2 adjoint, W 64x32, "
+                            "batch 1024, Float64", "n_s": self.n_s, "n_o": self.n_o,
+                "n_i": self.n_i, "parallelism": f"replicas{self.world}",
+                "l2": "working set 1.6 MB stays in L2; L2 flushed between steps"}
+
+    def cpu_baseline(self, seconds):
+        np = self.np
+        from oracle import oracle as orc
+        d = {k: v.numpy().copy() for k, v in self.pinned.items()}
+        S, O, I = self.n_s, self.n_o, self.n_i
+        z = lambda m: np.zeros(m, np.float64)
+        reps, t = 0, 0.0
+        t0 = time.perf_counter()
+        while t < min(seconds, 3.0):
+            orc.affine_ls_b(z(1), d["lossb"], d["w"], z(O * I), d["b"], z(O), d["x"], z(S * I),
+                            d["t"], z(S * O), z(S * O), z(S * O), S, O, I)
+            reps += 1
+            t = time.perf_counter() - t0
+        return {"value": reps / t, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"{reps} full evaluations (oracle.cc, serial), {t:.2f} s"}
+
+
+WORKLOADS = {"mlp2_ce": Mlp2Ce, "heat2d": Heat2d, "affine_ls": AffineLs}
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    """The reference's CPU implementation of the path (the oracle restatement:
+    the reference's Julia cannot run on these machines), all host threads,
+    each step a bounded sample of the workload."""
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return
+    import torch  # noqa: F401  (keeps library load order as in the GPU arm)
+    cls = WORKLOADS.get(args.config)
+
+    class _NoGpu:
+        pass
+    if args.config == "mlp2_ce":
+        import numpy as np
+        from oracle import oracle as orc
+        from stadeb200 import synth
+        c = synth.FULL["mlp2_ce"]
+        G, I, H, O = c["n_s"], c["n_i"], c["n_h"], c["n_o"]
+        threads = os.cpu_count() or 1
+        m = 64 * threads
+        d = synth.mlp2_ce_inputs(m, I, H, O)
+        f = np.float32
+
+        def one():
+            z = lambda n: np.zeros(n, f)
+            a = [z(1), d["lossb"], d["x"], z(m * I), d["y"], z(m * O), d["w1"], z(I * H), d["b1"],
+                 z(H), d["w2"], z(H * O), d["b2"], z(O), z(m * H), z(m * H), z(m * O), z(m * O),
+                 z(m * O), z(m * O)]
+            t0 = time.perf_counter()
+            orc.mlp2_ce_b(*a, m, I, H, O, threads=threads)
+            return time.perf_counter() - t0
+        for _ in range(args.warmup):
+            one()
+        times = [one() for _ in range(args.steps)]
+        per_sample = sum(times) / (args.steps * m)
+        value = 1.0 / (per_sample * G)
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": per_sample * G * 1e3, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "C2 mlp2_ce_b (see the ours arm)", "global_batch": G,
+                           "parallelism": "cpu"},
+                "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                                 "sample": f"{m} of {G} samples per step (oracle.cc OpenMP "
+                                           "restatement of the generated sweep; the reference's "
+                                           "Julia is not runnable here)"},
+                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    print(json.dumps({"impl": "reference", "unavailable":
+                      f"reference arm implemented for mlp2_ce only (asked {args.config})"}))
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    from stadeb200 import _lib, ddp
+
+    def comm_factory():
+        return ddp.NcclComm(rank, world)
+
+    W = WORKLOADS[args.config](torch, rank, world, comm_factory)
+    stream = torch.cuda.current_stream()
+    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    peaks, peak_src = load_peaks()
+
+    # device-resident timed run, with the phase profiler on
+    clocks = ClockSampler(local)
+    _lib.lib().stade_reset_kernel_launches()
+    for _ in range(args.warmup):
+        W.step()
+    torch.cuda.synchronize()
+    _lib.profile_read()
+    _lib.profile_enable(True)
+    launches0 = _lib.lib().stade_kernel_launches()
+    clocks.start()
+    total_ms, per = timed_loop(torch, W.step, args.steps, 0, world, dist, flush, stream)
+    clocks.stop()
+    launches = _lib.lib().stade_kernel_launches() - launches0
+    _lib.profile_enable(False)
+    phases = _lib.profile_read()
+    ms_per_step = total_ms / args.steps
+    value = 1000.0 / ms_per_step if W.scaling == "strong" else world * 1000.0 / ms_per_step
+
+    # end to end through the public entry points with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e_ms, _ = timed_loop(torch, W.e2e_step, args.steps, args.warmup, world, dist, None, stream)
+        h2d, d2h = W.e2e_bytes()
+        ev = 1000.0 / (e_ms / args.steps)
+        if W.scaling != "strong":
+            ev *= world
+        e2e = {"value": ev, "unit": UNIT, "h2d_bytes_per_step": h2d * (world if W.scaling == "strong" else 1),
+               "d2h_bytes_per_step": d2h * (world if W.scaling == "strong" else 1),
+               "ms_per_step": e_ms / args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = W.cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None,
+                "dtype": W.dtype, "data": "synthetic (seeded, shapes and distributions of the "
+                                          "BASELINE config)",
+                "config": W.config(),
+                "roofline": roofline(phases, W.phase_work(), args.steps, peaks, peak_src,
+                                     load_traffic(args.config)),
+                "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+                "gpu_launches": launches,
+                "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
+                "step_ms_min_max": [min(per), max(per)]}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        if getattr(W, "comm", None) is not None:
+            W.comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,640 @@
+// oracle.cc -- TEST INFRASTRUCTURE ONLY. CPU restatement of the adjoint and
+// HVP sweeps that STADE.jl generates for the primals in primals.jl.
+//
+// Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg (and
+// its --impl reference arm) may load this library. The product path
+// (libstade_b200.so) never calls it.
+//
+// The reference cannot run here (it is Julia; no Julia toolchain), and the
+// generated `_b.jl` / `_hv.jl` files for these five primals do not exist in the
+// reference, so each sweep below is written by hand from STADE's generation
+// rules and the pinned generated exemplars it follows (cited per function):
+//   - the forward sweep is replayed verbatim before the backward sweep
+//     (agen_forward_body, src/STADE.jl:6323);
+//   - loops run backwards with a negated step (agen_negate_step,
+//     src/STADE.jl:4656), e.g. `for i_x2 = i_n:-1:1`;
+//   - a consumed adjoint is captured then zeroed, `__oldb_0 = vb; vb = 0.0`
+//     (agen_backward_assign, src/STADE.jl:6605; affine_loss_b.jl:16-20);
+//   - an accumulation `s = s + e` leaves sb in place and adds into e's inputs
+//     (matvec_loss_b.jl:19-26);
+//   - local scalars needed by a derivative are recomputed in the reverse
+//     iteration instead of taped (mlp1d_b.jl:43-57); overwritten array
+//     values that are needed are taped (advection_b.jl:9-10, 28-29);
+//   - derivative formulas are the der_ table's: tanh' = 1 - tanh(x)^2
+//     recomputed (src/STADE.jl:1462, mlp1d_b.jl:50), max(a, b)' =
+//     0.5 * (1 + sign(a - b)) (src/STADE.jl:1489-1501, so 0.5 at a tie),
+//     v^2' = 2 v (src/STADE.jl:1369), exp' = exp (src/STADE.jl:1391),
+//     log' = 1 / x (src/STADE.jl:1397), a / b: 1 / b and -(a / b^2)
+//     (transformer_b.jl:633-634);
+//   - every float argument is independent (src/STADE.jl:522-525), so the
+//     adjoints of inputs such as x and t are outputs too;
+//   - the HVP doubles every adjoint statement with its tangent twin
+//     (hvp_double_stmt, src/STADE.jl:6904; exemplar mlp1d_hv.jl).
+// Build flags (Makefile): -O2 -fno-fast-math -ffp-contract=off, so no fused
+// multiply-add changes the rounding of the Julia source's `a * b + c`.
+//
+// Index convention: 0-based here; the comments give the 1-based Julia loop.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace {
+
+using i64 = int64_t;
+
+template <class T> inline T jl_sign(T x) { return x > T(0) ? T(1) : (x < T(0) ? T(-1) : x); }
+// Julia's max for floats: NaN wins, then the larger value, +0.0 over -0.0.
+template <class T> inline T jl_max(T a, T b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a > b) return a;
+  if (b > a) return b;
+  return std::signbit(a) ? b : a;
+}
+inline float jl_tanh(float x) { return std::tanh(x); }
+inline double jl_tanh(double x) { return std::tanh(x); }
+inline long double jl_tanh(long double x) { return tanhl(x); }
+inline float jl_exp(float x) { return std::exp(x); }
+inline double jl_exp(double x) { return std::exp(x); }
+inline long double jl_exp(long double x) { return expl(x); }
+inline float jl_log(float x) { return std::log(x); }
+inline double jl_log(double x) { return std::log(x); }
+inline long double jl_log(long double x) { return logl(x); }
+
+// ---------------------------------------------------------------------------
+// C1 affine_ls_b. Follows affine_loss_b.jl:5-23 (per-element adjoint with
+// __oldb capture) and matvec_loss_b.jl:5-27 (flattened (sample, output) loop
+// with div/mod decode; the accumulation loop's adjoint runs i_k backwards).
+template <class T>
+void affine_ls_b(T* loss, const T* lossb, const T* w, T* wb, const T* b, T* bb,
+                 const T* x, T* xb, const T* t, T* tb, T* y, T* yb,
+                 i64 n_s, i64 n_o, i64 n_i) {
+  T s = T(0), sb = T(0);
+  // forward sweep
+  for (i64 idx = 0; idx < n_s * n_o; ++idx) {          // for idx = 1:n_s * n_o
+    const i64 i_s = idx / n_o, i_o = idx % n_o;
+    s = b[i_o];
+    for (i64 k = 0; k < n_i; ++k) s = s + w[i_o * n_i + k] * x[i_s * n_i + k];
+    y[idx] = s;
+  }
+  for (i64 idx2 = 0; idx2 < n_s * n_o; ++idx2) {
+    const T d = y[idx2] - t[idx2];
+    loss[0] = loss[0] + T(0.5) * (d * d);
+  }
+  // backward sweep
+  for (i64 idx2 = n_s * n_o - 1; idx2 >= 0; --idx2) {  // for idx2 = n_s * n_o:-1:1
+    const T cse0 = y[idx2] - t[idx2];
+    const T cse1 = (T(0.5) * (T(2) * cse0)) * lossb[0];
+    yb[idx2] = yb[idx2] + cse1;
+    tb[idx2] = tb[idx2] + -cse1;
+  }
+  for (i64 idx = n_s * n_o - 1; idx >= 0; --idx) {      // for idx = n_s * n_o:-1:1
+    const i64 i_s = idx / n_o, i_o = idx % n_o;
+    T oldb = yb[idx];
+    yb[idx] = T(0);
+    sb = sb + oldb;
+    for (i64 k = n_i - 1; k >= 0; --k) {                 // for i_k = n_i:-1:1
+      wb[i_o * n_i + k] = wb[i_o * n_i + k] + x[i_s * n_i + k] * sb;
+      xb[i_s * n_i + k] = xb[i_s * n_i + k] + w[i_o * n_i + k] * sb;
+    }
+    oldb = sb;
+    sb = T(0);
+    bb[i_o] = bb[i_o] + oldb;
+  }
+  (void)s;
+}
+
+// ---------------------------------------------------------------------------
+// C2 / C5 mlp2_ce forward pieces, shared by the adjoint and the HVP.
+template <class T>
+void mlp2_ce_forward(T* loss, const T* x, const T* y, const T* w1, const T* b1,
+                     const T* w2, const T* b2, T* h, T* z, T* p,
+                     i64 n_s, i64 n_i, i64 n_h, i64 n_o) {
+  for (i64 idx = 0; idx < n_s * n_h; ++idx) {
+    const i64 i_s = idx / n_h, j = idx % n_h;
+    T s1 = b1[j];
+    for (i64 k = 0; k < n_i; ++k) s1 = s1 + x[i_s * n_i + k] * w1[k * n_h + j];
+    h[idx] = jl_tanh(s1);
+  }
+  for (i64 idx2 = 0; idx2 < n_s * n_o; ++idx2) {
+    const i64 i_s = idx2 / n_o, c = idx2 % n_o;
+    T s2 = b2[c];
+    for (i64 k = 0; k < n_h; ++k) s2 = s2 + h[i_s * n_h + k] * w2[k * n_o + c];
+    z[idx2] = s2;
+  }
+  for (i64 i_s = 0; i_s < n_s; ++i_s) {
+    const T* zr = z + i_s * n_o;
+    T* pr = p + i_s * n_o;
+    T row_max = zr[0];
+    for (i64 c = 1; c < n_o; ++c) row_max = jl_max(row_max, zr[c]);
+    for (i64 c = 0; c < n_o; ++c) pr[c] = jl_exp(zr[c] - row_max);
+    T row_sum = T(0);
+    for (i64 c = 0; c < n_o; ++c) row_sum = row_sum + pr[c];
+    for (i64 c = 0; c < n_o; ++c)
+      loss[0] = loss[0] - y[i_s * n_o + c] * jl_log(pr[c] / row_sum);
+  }
+}
+
+// C2 mlp2_ce_b. Forward replay, then the reverse of the softmax loop (the
+// loss statement, the row_sum loop, the exp loop and the row-max chain in
+// that order, as transformer_b.jl:615-667 reverses the same softmax), then the
+// output-logit loop (an accumulation like mlp1d_b.jl:34-42), then the hidden
+// loop with s1 recomputed and tanh' = 1 - tanh(s1)^2 (mlp1d_b.jl:43-78).
+template <class T>
+void mlp2_ce_b(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
+               const T* w1, T* w1b, const T* b1, T* b1b, const T* w2, T* w2b,
+               const T* b2, T* b2b, T* h, T* hb, T* z, T* zb, T* p, T* pb,
+               i64 n_s, i64 n_i, i64 n_h, i64 n_o) {
+  mlp2_ce_forward(loss, x, y, w1, b1, w2, b2, h, z, p, n_s, n_i, n_h, n_o);
+  std::vector<T> max_tape(n_o > 0 ? n_o : 1);  // row_max before step i_c
+  T s1b = T(0), s2b = T(0), row_maxb = T(0), row_sumb = T(0);
+  // reverse of the softmax cross-entropy loop: for i_s = n_s:-1:1
+  for (i64 i_s = n_s - 1; i_s >= 0; --i_s) {
+    const T* zr = z + i_s * n_o;
+    const T* pr = p + i_s * n_o;
+    T* zbr = zb + i_s * n_o;
+    T* pbr = pb + i_s * n_o;
+    // restore the scalars of this iteration (row-max chain taped per step)
+    T row_max = zr[0];
+    for (i64 c = 1; c < n_o; ++c) { max_tape[c] = row_max; row_max = jl_max(row_max, zr[c]); }
+    T row_sum = T(0);
+    for (i64 c = 0; c < n_o; ++c) row_sum = row_sum + pr[c];
+    // loss[1] = loss[1] - y * log(p / row_sum), for i_c = n_o:-1:1
+    for (i64 c = n_o - 1; c >= 0; --c) {
+      const T q = pr[c] / row_sum;
+      yb[i_s * n_o + c] = yb[i_s * n_o + c] + -(jl_log(q)) * lossb[0];
+      const T qb = (T(1) / q) * (-(y[i_s * n_o + c]) * lossb[0]);
+      pbr[c] = pbr[c] + (T(1) / row_sum) * qb;
+      row_sumb = row_sumb + -(pr[c] / (row_sum * row_sum)) * qb;
+    }
+    // row_sum = row_sum + p[c]
+    for (i64 c = n_o - 1; c >= 0; --c) pbr[c] = pbr[c] + row_sumb;
+    row_sumb = T(0);
+    // p[c] = exp(z[c] - row_max)
+    for (i64 c = n_o - 1; c >= 0; --c) {
+      const T oldb = pbr[c];
+      pbr[c] = T(0);
+      const T cse = jl_exp(zr[c] - row_max) * oldb;
+      zbr[c] = zbr[c] + cse;
+      row_maxb = row_maxb + -cse;
+    }
+    // row_max = max(row_max, z[c]), for i_c = n_o:-1:2
+    for (i64 c = n_o - 1; c >= 1; --c) {
+      const T m_prev = max_tape[c];
+      const T oldb = row_maxb;
+      row_maxb = T(0);
+      const T zc = zr[c];
+      row_maxb = row_maxb + (T(0.5) * (T(1) + jl_sign(m_prev - zc))) * oldb;
+      zbr[c] = zbr[c] + (T(0.5) * (T(1) + jl_sign(zc - m_prev))) * oldb;
+    }
+    // row_max = z[1]
+    {
+      const T oldb = row_maxb;
+      row_maxb = T(0);
+      zbr[0] = zbr[0] + oldb;
+    }
+  }
+  // reverse of the output-logit loop: for idx2 = n_s * n_o:-1:1
+  for (i64 idx2 = n_s * n_o - 1; idx2 >= 0; --idx2) {
+    const i64 i_s = idx2 / n_o, c = idx2 % n_o;
+    T oldb = zb[idx2];
+    zb[idx2] = T(0);
+    s2b = s2b + oldb;
+    for (i64 k = n_h - 1; k >= 0; --k) {
+      w2b[k * n_o + c] = w2b[k * n_o + c] + h[i_s * n_h + k] * s2b;
+      hb[i_s * n_h + k] = hb[i_s * n_h + k] + w2[k * n_o + c] * s2b;
+    }
+    oldb = s2b;
+    s2b = T(0);
+    b2b[c] = b2b[c] + oldb;
+  }
+  // reverse of the hidden loop: for idx = n_s * n_h:-1:1
+  for (i64 idx = n_s * n_h - 1; idx >= 0; --idx) {
+    const i64 i_s = idx / n_h, j = idx % n_h;
+    T s1 = b1[j];
+    for (i64 k = 0; k < n_i; ++k) s1 = s1 + x[i_s * n_i + k] * w1[k * n_h + j];
+    T oldb = hb[idx];
+    hb[idx] = T(0);
+    const T th = jl_tanh(s1);
+    s1b = s1b + (T(1) - th * th) * oldb;
+    for (i64 k = 0; k < n_i; ++k) {
+      const T cse_w = w1[k * n_h + j];
+      const T cse_x = x[i_s * n_i + k];
+      w1b[k * n_h + j] = w1b[k * n_h + j] + cse_x * s1b;
+      xb[i_s * n_i + k] = xb[i_s * n_i + k] + cse_w * s1b;
+    }
+    oldb = s1b;
+    s1b = T(0);
+    b1b[j] = b1b[j] + oldb;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// C5 mlp2_ce_hv. Every statement of mlp2_ce_b with its tangent twin, the
+// tangent computed first from the primal values before the statement
+// (mlp1d_hv.jl: `s2d = ...` before `s2 = ...`, `__oldb_0d` with `__oldb_0`).
+template <class T>
+void mlp2_ce_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
+                const T* w1, T* w1b, const T* b1, T* b1b, const T* w2, T* w2b,
+                const T* b2, T* b2b, T* h, T* hb, T* z, T* zb, T* p, T* pb,
+                i64 n_s, i64 n_i, i64 n_h, i64 n_o,
+                T* lossd, const T* lossbd, const T* xd, T* xbd, const T* yd, T* ybd,
+                const T* w1d, T* w1bd, const T* b1d, T* b1bd, const T* w2d, T* w2bd,
+                const T* b2d, T* b2bd, T* hd, T* hbd, T* zd, T* zbd, T* pd, T* pbd) {
+  // ---- forward sweep with tangents (mlp1d_hv.jl:18-54)
+  for (i64 idx = 0; idx < n_s * n_h; ++idx) {
+    const i64 i_s = idx / n_h, j = idx % n_h;
+    T s1d = b1d[j], s1 = b1[j];
+    for (i64 k = 0; k < n_i; ++k) {
+      const T xv = x[i_s * n_i + k], wv = w1[k * n_h + j];
+      s1d = s1d + (xv * w1d[k * n_h + j] + wv * xd[i_s * n_i + k]);
+      s1 = s1 + xv * wv;
+    }
+    const T th = jl_tanh(s1);
+    hd[idx] = (T(1) - th * th) * s1d;
+    h[idx] = th;
+  }
+  for (i64 idx2 = 0; idx2 < n_s * n_o; ++idx2) {
+    const i64 i_s = idx2 / n_o, c = idx2 % n_o;
+    T s2d = b2d[c], s2 = b2[c];
+    for (i64 k = 0; k < n_h; ++k) {
+      const T hv = h[i_s * n_h + k], wv = w2[k * n_o + c];
+      s2d = s2d + (hv * w2d[k * n_o + c] + wv * hd[i_s * n_h + k]);
+      s2 = s2 + wv * hv;
+    }
+    zd[idx2] = s2d;
+    z[idx2] = s2;
+  }
+  std::vector<T> mt(n_o > 0 ? n_o : 1), mdt(n_o > 0 ? n_o : 1);
+  for (i64 i_s = 0; i_s < n_s; ++i_s) {
+    const T* zr = z + i_s * n_o; const T* zdr = zd + i_s * n_o;
+    T* pr = p + i_s * n_o; T* pdr = pd + i_s * n_o;
+    T m = zr[0], md = zdr[0];
+    for (i64 c = 1; c < n_o; ++c) {
+      const T g1 = T(0.5) * (T(1) + jl_sign(m - zr[c]));
+      const T g2 = T(0.5) * (T(1) + jl_sign(zr[c] - m));
+      md = g1 * md + g2 * zdr[c];
+      m = jl_max(m, zr[c]);
+    }
+    for (i64 c = 0; c < n_o; ++c) {
+      const T e = jl_exp(zr[c] - m);
+      pdr[c] = e * (zdr[c] - md);
+      pr[c] = e;
+    }
+    T rs = T(0), rsd = T(0);
+    for (i64 c = 0; c < n_o; ++c) { rsd = rsd + pdr[c]; rs = rs + pr[c]; }
+    for (i64 c = 0; c < n_o; ++c) {
+      const T q = pr[c] / rs;
+      const T qd = pdr[c] / rs - (pr[c] / (rs * rs)) * rsd;
+      lossd[0] = lossd[0] - (yd[i_s * n_o + c] * jl_log(q) + y[i_s * n_o + c] * (qd / q));
+      loss[0] = loss[0] - y[i_s * n_o + c] * jl_log(q);
+    }
+  }
+  // ---- backward sweep with tangents
+  T s1b = 0, s1bd = 0, s2b = 0, s2bd = 0, mb = 0, mbd = 0, rsb = 0, rsbd = 0;
+  for (i64 i_s = n_s - 1; i_s >= 0; --i_s) {
+    const T* zr = z + i_s * n_o; const T* zdr = zd + i_s * n_o;
+    const T* pr = p + i_s * n_o; const T* pdr = pd + i_s * n_o;
+    T* zbr = zb + i_s * n_o; T* zbdr = zbd + i_s * n_o;
+    T* pbr = pb + i_s * n_o; T* pbdr = pbd + i_s * n_o;
+    T m = zr[0], md = zdr[0];
+    for (i64 c = 1; c < n_o; ++c) {
+      mt[c] = m; mdt[c] = md;
+      const T g1 = T(0.5) * (T(1) + jl_sign(m - zr[c]));
+      const T g2 = T(0.5) * (T(1) + jl_sign(zr[c] - m));
+      md = g1 * md + g2 * zdr[c];
+      m = jl_max(m, zr[c]);
+    }
+    T rs = T(0), rsd = T(0);
+    for (i64 c = 0; c < n_o; ++c) { rsd = rsd + pdr[c]; rs = rs + pr[c]; }
+    const T lb = lossb[0], lbd = lossbd[0];
+    for (i64 c = n_o - 1; c >= 0; --c) {
+      const T yv = y[i_s * n_o + c], ydv = yd[i_s * n_o + c];
+      const T q = pr[c] / rs;
+      const T qd = pdr[c] / rs - (pr[c] / (rs * rs)) * rsd;
+      const T lq = jl_log(q);
+      const T lqd = qd / q;
+      ybd[i_s * n_o + c] = ybd[i_s * n_o + c] + -(lqd * lb + lq * lbd);
+      yb[i_s * n_o + c] = yb[i_s * n_o + c] + -(lq) * lb;
+      const T inv_q = T(1) / q;
+      const T inv_qd = -(qd / (q * q));
+      const T ny = -(yv) * lb;
+      const T nyd = -(ydv * lb + yv * lbd);
+      const T qbd = inv_qd * ny + inv_q * nyd;
+      const T qb = inv_q * ny;
+      const T inv_rs = T(1) / rs;
+      const T inv_rsd = -(rsd / (rs * rs));
+      pbdr[c] = pbdr[c] + (inv_rsd * qb + inv_rs * qbd);
+      pbr[c] = pbr[c] + inv_rs * qb;
+      const T pr2 = pr[c] / (rs * rs);
+      const T pr2d = pdr[c] / (rs * rs) - (pr[c] / (rs * rs)) * ((T(2) * rs * rsd) / (rs * rs));
+      rsbd = rsbd + -(pr2d * qb + pr2 * qbd);
+      rsb = rsb + -(pr2) * qb;
+    }
+    for (i64 c = n_o - 1; c >= 0; --c) {
+      pbdr[c] = pbdr[c] + rsbd;
+      pbr[c] = pbr[c] + rsb;
+    }
+    rsbd = T(0); rsb = T(0);
+    for (i64 c = n_o - 1; c >= 0; --c) {
+      const T oldbd = pbdr[c], oldb = pbr[c];
+      pbdr[c] = T(0); pbr[c] = T(0);
+      const T e = jl_exp(zr[c] - m);
+      const T ed = e * (zdr[c] - md);
+      const T csed = ed * oldb + e * oldbd;
+      const T cse = e * oldb;
+      zbdr[c] = zbdr[c] + csed;
+      zbr[c] = zbr[c] + cse;
+      mbd = mbd + -csed;
+      mb = mb + -cse;
+    }
+    for (i64 c = n_o - 1; c >= 1; --c) {
+      const T m_prev = mt[c];
+      const T oldbd = mbd, oldb = mb;
+      mbd = T(0); mb = T(0);
+      const T zc = zr[c];
+      const T g1 = T(0.5) * (T(1) + jl_sign(m_prev - zc));
+      const T g2 = T(0.5) * (T(1) + jl_sign(zc - m_prev));
+      mbd = mbd + g1 * oldbd;
+      mb = mb + g1 * oldb;
+      zbdr[c] = zbdr[c] + g2 * oldbd;
+      zbr[c] = zbr[c] + g2 * oldb;
+    }
+    {
+      const T oldbd = mbd, oldb = mb;
+      mbd = T(0); mb = T(0);
+      zbdr[0] = zbdr[0] + oldbd;
+      zbr[0] = zbr[0] + oldb;
+    }
+  }
+  for (i64 idx2 = n_s * n_o - 1; idx2 >= 0; --idx2) {
+    const i64 i_s = idx2 / n_o, c = idx2 % n_o;
+    T oldbd = zbd[idx2], oldb = zb[idx2];
+    zbd[idx2] = T(0); zb[idx2] = T(0);
+    s2bd = s2bd + oldbd;
+    s2b = s2b + oldb;
+    for (i64 k = n_h - 1; k >= 0; --k) {
+      const T hv = h[i_s * n_h + k];
+      w2bd[k * n_o + c] = w2bd[k * n_o + c] + (s2b * hd[i_s * n_h + k] + hv * s2bd);
+      w2b[k * n_o + c] = w2b[k * n_o + c] + hv * s2b;
+      const T wv = w2[k * n_o + c];
+      hbd[i_s * n_h + k] = hbd[i_s * n_h + k] + (s2b * w2d[k * n_o + c] + wv * s2bd);
+      hb[i_s * n_h + k] = hb[i_s * n_h + k] + wv * s2b;
+    }
+    oldbd = s2bd; oldb = s2b;
+    s2bd = T(0); s2b = T(0);
+    b2bd[c] = b2bd[c] + oldbd;
+    b2b[c] = b2b[c] + oldb;
+  }
+  for (i64 idx = n_s * n_h - 1; idx >= 0; --idx) {
+    const i64 i_s = idx / n_h, j = idx % n_h;
+    T s1d = b1d[j], s1 = b1[j];
+    for (i64 k = 0; k < n_i; ++k) {
+      const T xv = x[i_s * n_i + k], wv = w1[k * n_h + j];
+      s1d = s1d + (xv * w1d[k * n_h + j] + wv * xd[i_s * n_i + k]);
+      s1 = s1 + xv * wv;
+    }
+    T oldbd = hbd[idx], oldb = hb[idx];
+    hbd[idx] = T(0); hb[idx] = T(0);
+    const T th = jl_tanh(s1);
+    const T g = T(1) - th * th;
+    // mlp1d_hv.jl:108-109: s2bd += __oldb * -((2 tanh) * (g * s2d)) + g * __oldb_d
+    s1bd = s1bd + (oldb * -((T(2) * th) * (g * s1d)) + g * oldbd);
+    s1b = s1b + g * oldb;
+    oldbd = s1bd; oldb = s1b;
+    s1bd = T(0); s1b = T(0);
+    for (i64 k = 0; k < n_i; ++k) {
+      const T wdv = w1d[k * n_h + j], wv = w1[k * n_h + j];
+      const T xdv = xd[i_s * n_i + k], xv = x[i_s * n_i + k];
+      w1bd[k * n_h + j] = w1bd[k * n_h + j] + (oldb * xdv + xv * oldbd);
+      w1b[k * n_h + j] = w1b[k * n_h + j] + xv * oldb;
+      xbd[i_s * n_i + k] = xbd[i_s * n_i + k] + (oldb * wdv + wv * oldbd);
+      xb[i_s * n_i + k] = xb[i_s * n_i + k] + wv * oldb;
+    }
+    b1bd[j] = b1bd[j] + oldbd;
+    b1b[j] = b1b[j] + oldb;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// C3 heat2d_b. Time loop with a tape of the state overwritten by the copy
+// loop (advection_b.jl:1-37: slot ((i_x - 2) + (i_ - 1) * width) + 1, thread
+// loop fastest), scatter adjoint of the stencil (stencil_loss_b.jl:12-21), the
+// scalar float argument's adjoint returned by value (advection_b.jl:36).
+template <class T>
+T heat2d_b(T* loss, const T* lossb, T* u, T* ub, T* un, T* unb, T alpha, T alphab,
+           i64 n, i64 n_step, T* u_stack) {
+  const i64 nn = n * n;
+  auto nbrs = [n](i64 idx, i64& up, i64& dn, i64& lf, i64& rt) {
+    const i64 i = idx / n, j = idx % n;
+    const i64 iu = (i - 1 + n) % n, id = (i + 1) % n, jl = (j - 1 + n) % n, jr = (j + 1) % n;
+    up = iu * n + j; dn = id * n + j; lf = i * n + jl; rt = i * n + jr;
+  };
+  for (i64 it = 0; it < n_step; ++it) {                // for i_t = 1:n_step
+    for (i64 idx = 0; idx < nn; ++idx) {
+      i64 up, dn, lf, rt;
+      nbrs(idx, up, dn, lf, rt);
+      const T c = u[idx];
+      un[idx] = c + alpha * ((((u[up] + u[dn]) + u[lf]) + u[rt]) - T(4) * c);
+    }
+    for (i64 idx2 = 0; idx2 < nn; ++idx2) {
+      u_stack[idx2 + it * nn] = u[idx2];
+      u[idx2] = un[idx2];
+    }
+  }
+  for (i64 idx3 = 0; idx3 < nn; ++idx3) loss[0] = loss[0] + u[idx3] * u[idx3];
+  // backward sweep
+  for (i64 idx3 = nn - 1; idx3 >= 0; --idx3) ub[idx3] = ub[idx3] + (T(2) * u[idx3]) * lossb[0];
+  for (i64 it = n_step - 1; it >= 0; --it) {           // for i_t = n_step:-1:1
+    for (i64 idx2 = nn - 1; idx2 >= 0; --idx2) {
+      u[idx2] = u_stack[idx2 + it * nn];
+      const T oldb = ub[idx2];
+      ub[idx2] = T(0);
+      unb[idx2] = unb[idx2] + oldb;
+    }
+    for (i64 idx = nn - 1; idx >= 0; --idx) {
+      i64 up, dn, lf, rt;
+      nbrs(idx, up, dn, lf, rt);
+      const T oldb = unb[idx];
+      unb[idx] = T(0);
+      const T c = u[idx];
+      const T cse_a = alpha * oldb;
+      ub[idx] = ub[idx] + oldb;
+      alphab = alphab + ((((u[up] + u[dn]) + u[lf]) + u[rt]) - T(4) * c) * oldb;
+      ub[up] = ub[up] + cse_a;
+      ub[dn] = ub[dn] + cse_a;
+      ub[lf] = ub[lf] + cse_a;
+      ub[rt] = ub[rt] + cse_a;
+      ub[idx] = ub[idx] + T(4) * -cse_a;
+    }
+  }
+  return alphab;
+}
+
+// ---------------------------------------------------------------------------
+// C4 conv1d_relu_mse_b. Valid convolution adjoint as selfrace_conv_b.jl:5-35
+// (ab accumulated from the consumed zb, inner loops backwards, xb at the
+// self-overlapping index t + ci - 1), ReLU through max(a, 0.0) with the der_
+// partial 0.5 * (1 + sign(a - 0.0)) (src/STADE.jl:1489-1501), the local `a`
+// recomputed in the reverse iteration (mlp1d_b.jl:43-47).
+template <class T>
+void conv1d_relu_mse_b(T* loss, const T* lossb, const T* x, T* xb, const T* w, T* wb,
+                       const T* t, T* tb, T* z, T* zb, T* r, T* rb,
+                       i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  const i64 n_lo = n_l - n_k + 1;
+  const i64 nt = n_b * n_o * n_lo;
+  T a = T(0), ab = T(0);
+  auto conv_at = [&](i64 idx) {
+    const i64 i_b = idx / (n_o * n_lo), i_o = (idx / n_lo) % n_o, i_t = idx % n_lo;
+    T acc = T(0);
+    for (i64 c = 0; c < n_c; ++c)
+      for (i64 k = 0; k < n_k; ++k)
+        acc = acc + w[(i_o * n_c + c) * n_k + k] * x[(i_b * n_c + c) * n_l + i_t + k];
+    return acc;
+  };
+  for (i64 idx = 0; idx < nt; ++idx) {
+    a = conv_at(idx);
+    z[idx] = a;
+    r[idx] = jl_max(a, T(0));
+  }
+  const T inv_n = T(1) / T(nt);
+  for (i64 idx2 = 0; idx2 < nt; ++idx2) {
+    const T d = r[idx2] - t[idx2];
+    loss[0] = loss[0] + inv_n * (d * d);
+  }
+  for (i64 idx2 = nt - 1; idx2 >= 0; --idx2) {
+    const T cse0 = r[idx2] - t[idx2];
+    const T cse1 = (inv_n * (T(2) * cse0)) * lossb[0];
+    rb[idx2] = rb[idx2] + cse1;
+    tb[idx2] = tb[idx2] + -cse1;
+  }
+  for (i64 idx = nt - 1; idx >= 0; --idx) {
+    const i64 i_b = idx / (n_o * n_lo), i_o = (idx / n_lo) % n_o, i_t = idx % n_lo;
+    a = conv_at(idx);
+    T oldb = rb[idx];
+    rb[idx] = T(0);
+    ab = ab + (T(0.5) * (T(1) + jl_sign(a - T(0)))) * oldb;
+    oldb = zb[idx];
+    zb[idx] = T(0);
+    ab = ab + oldb;
+    for (i64 c = n_c - 1; c >= 0; --c) {
+      for (i64 k = n_k - 1; k >= 0; --k) {
+        const i64 xi = (i_b * n_c + c) * n_l + i_t + k;
+        const i64 wi = (i_o * n_c + c) * n_k + k;
+        wb[wi] = wb[wi] + x[xi] * ab;
+        xb[xi] = xb[xi] + w[wi] * ab;
+      }
+    }
+    ab = T(0);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Parallel CPU variants (timed CPU baseline only): samples split across host
+// threads, each with private copies of the summed shadows, then one
+// fixed-order sum. Same arithmetic per sample as the serial sweeps above.
+template <class T>
+void mlp2_ce_b_omp(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
+                   const T* w1, T* w1b, const T* b1, T* b1b, const T* w2, T* w2b,
+                   const T* b2, T* b2b, T* h, T* hb, T* z, T* zb, T* p, T* pb,
+                   i64 n_s, i64 n_i, i64 n_h, i64 n_o, int nthreads) {
+#ifdef _OPENMP
+  if (nthreads <= 0) nthreads = omp_get_max_threads();
+#else
+  nthreads = 1;
+#endif
+  const i64 nw1 = n_i * n_h, nw2 = n_h * n_o;
+  std::vector<T> part((size_t)nthreads * (nw1 + n_h + nw2 + n_o + 1), T(0));
+#pragma omp parallel num_threads(nthreads)
+  {
+#ifdef _OPENMP
+    const int tid = omp_get_thread_num();
+#else
+    const int tid = 0;
+#endif
+    T* my = part.data() + (size_t)tid * (nw1 + n_h + nw2 + n_o + 1);
+    const i64 lo = n_s * tid / nthreads, hi = n_s * (tid + 1) / nthreads;
+    if (hi > lo) {
+      const i64 m = hi - lo;
+      mlp2_ce_b(my + nw1 + n_h + nw2 + n_o, lossb, x + lo * n_i, xb + lo * n_i, y + lo * n_o,
+                yb + lo * n_o, w1, my, b1, my + nw1, w2, my + nw1 + n_h, b2,
+                my + nw1 + n_h + nw2, h + lo * n_h, hb + lo * n_h, z + lo * n_o, zb + lo * n_o,
+                p + lo * n_o, pb + lo * n_o, m, n_i, n_h, n_o);
+    }
+  }
+  for (int tid = 0; tid < nthreads; ++tid) {
+    const T* my = part.data() + (size_t)tid * (nw1 + n_h + nw2 + n_o + 1);
+    for (i64 i = 0; i < nw1; ++i) w1b[i] += my[i];
+    for (i64 i = 0; i < n_h; ++i) b1b[i] += my[nw1 + i];
+    for (i64 i = 0; i < nw2; ++i) w2b[i] += my[nw1 + n_h + i];
+    for (i64 i = 0; i < n_o; ++i) b2b[i] += my[nw1 + n_h + nw2 + i];
+    loss[0] += my[nw1 + n_h + nw2 + n_o];
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+void oracle_affine_ls_b_f64(double* loss, const double* lossb, const double* w, double* wb,
+                            const double* b, double* bb, const double* x, double* xb,
+                            const double* t, double* tb, double* y, double* yb,
+                            i64 n_s, i64 n_o, i64 n_i) {
+  affine_ls_b<double>(loss, lossb, w, wb, b, bb, x, xb, t, tb, y, yb, n_s, n_o, n_i);
+}
+void oracle_affine_ls_b_f128(long double* loss, const long double* lossb, const long double* w,
+                             long double* wb, const long double* b, long double* bb,
+                             const long double* x, long double* xb, const long double* t,
+                             long double* tb, long double* y, long double* yb,
+                             i64 n_s, i64 n_o, i64 n_i) {
+  affine_ls_b<long double>(loss, lossb, w, wb, b, bb, x, xb, t, tb, y, yb, n_s, n_o, n_i);
+}
+
+#define MLP_B_ARGS(T)                                                                      \
+  T *loss, const T *lossb, const T *x, T *xb, const T *y, T *yb, const T *w1, T *w1b,     \
+      const T *b1, T *b1b, const T *w2, T *w2b, const T *b2, T *b2b, T *h, T *hb, T *z,    \
+      T *zb, T *p, T *pb, i64 n_s, i64 n_i, i64 n_h, i64 n_o
+#define MLP_B_PASS loss, lossb, x, xb, y, yb, w1, w1b, b1, b1b, w2, w2b, b2, b2b, h, hb, z, zb, p, pb, n_s, n_i, n_h, n_o
+
+void oracle_mlp2_ce_b_f32(MLP_B_ARGS(float)) { mlp2_ce_b<float>(MLP_B_PASS); }
+void oracle_mlp2_ce_b_f64(MLP_B_ARGS(double)) { mlp2_ce_b<double>(MLP_B_PASS); }
+void oracle_mlp2_ce_b_f32_omp(MLP_B_ARGS(float), int nthreads) {
+  mlp2_ce_b_omp<float>(MLP_B_PASS, nthreads);
+}
+
+#define MLP_HV_ARGS(T)                                                                     \
+  MLP_B_ARGS(T), T *lossd, const T *lossbd, const T *xd, T *xbd, const T *yd, T *ybd,      \
+      const T *w1d, T *w1bd, const T *b1d, T *b1bd, const T *w2d, T *w2bd, const T *b2d,   \
+      T *b2bd, T *hd, T *hbd, T *zd, T *zbd, T *pd, T *pbd
+#define MLP_HV_PASS                                                                        \
+  MLP_B_PASS, lossd, lossbd, xd, xbd, yd, ybd, w1d, w1bd, b1d, b1bd, w2d, w2bd, b2d, b2bd, \
+      hd, hbd, zd, zbd, pd, pbd
+
+void oracle_mlp2_ce_hv_f64(MLP_HV_ARGS(double)) { mlp2_ce_hv<double>(MLP_HV_PASS); }
+void oracle_mlp2_ce_hv_f128(MLP_HV_ARGS(long double)) { mlp2_ce_hv<long double>(MLP_HV_PASS); }
+
+double oracle_heat2d_b_f64(double* loss, const double* lossb, double* u, double* ub, double* un,
+                           double* unb, double alpha, double alphab, i64 n, i64 n_step,
+                           double* u_stack) {
+  return heat2d_b<double>(loss, lossb, u, ub, un, unb, alpha, alphab, n, n_step, u_stack);
+}
+
+void oracle_conv1d_relu_mse_b_f32(float* loss, const float* lossb, const float* x, float* xb,
+                                  const float* w, float* wb, const float* t, float* tb,
+                                  float* z, float* zb, float* r, float* rb,
+                                  i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  conv1d_relu_mse_b<float>(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k);
+}
+void oracle_conv1d_relu_mse_b_f64(double* loss, const double* lossb, const double* x, double* xb,
+                                  const double* w, double* wb, const double* t, double* tb,
+                                  double* z, double* zb, double* r, double* rb,
+                                  i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  conv1d_relu_mse_b<double>(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k);
+}
+
+}  // extern "C"

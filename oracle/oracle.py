@@ -1,0 +1,115 @@
+"""TEST INFRASTRUCTURE ONLY: numpy/ctypes front end of the CPU oracle
+(oracle.cc), the restatement of the adjoint / HVP sweeps STADE.jl generates.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module, as the checker or as the timed CPU baseline; the product path
+(libstade_b200.so) never does.
+
+Each function takes numpy arrays, runs the oracle IN PLACE on them exactly
+as the generated code mutates its arguments, and returns what the generated
+Julia returns (nothing, or the scalar adjoint for heat2d_b).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+_lib = None
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        P, I64, D = C.c_void_p, C.c_int64, C.c_double
+        L.oracle_affine_ls_b_f64.argtypes = [P] * 12 + [I64] * 3
+        L.oracle_affine_ls_b_f128.argtypes = [P] * 12 + [I64] * 3
+        for n in ("oracle_mlp2_ce_b_f32", "oracle_mlp2_ce_b_f64"):
+            getattr(L, n).argtypes = [P] * 20 + [I64] * 4
+        L.oracle_mlp2_ce_b_f32_omp.argtypes = [P] * 20 + [I64] * 4 + [C.c_int]
+        for n in ("oracle_mlp2_ce_hv_f64", "oracle_mlp2_ce_hv_f128"):
+            getattr(L, n).argtypes = [P] * 20 + [I64] * 4 + [P] * 20
+        L.oracle_heat2d_b_f64.argtypes = [P] * 6 + [D, D, I64, I64, P]
+        L.oracle_heat2d_b_f64.restype = D
+        for n in ("oracle_conv1d_relu_mse_b_f32", "oracle_conv1d_relu_mse_b_f64"):
+            getattr(L, n).argtypes = [P] * 12 + [I64] * 5
+        for f in L.oracle_affine_ls_b_f64, L.oracle_mlp2_ce_b_f32:
+            f.restype = None
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray, dtype) -> int:
+    assert a.dtype == dtype and a.flags.c_contiguous, (a.dtype, dtype)
+    return a.ctypes.data
+
+
+def affine_ls_b(loss, lossb, w, wb, b, bb, x, xb, t, tb, y, yb, n_s, n_o, n_i, truth=False):
+    if truth:
+        ld = np.longdouble
+        arrs = [np.asarray(a, dtype=ld) for a in (loss, lossb, w, wb, b, bb, x, xb, t, tb, y, yb)]
+        lib().oracle_affine_ls_b_f128(*[_p(a, ld) for a in arrs], n_s, n_o, n_i)
+        for dst, src in zip((loss, lossb, w, wb, b, bb, x, xb, t, tb, y, yb), arrs):
+            dst[...] = src
+        return None
+    f = np.float64
+    lib().oracle_affine_ls_b_f64(*[_p(a, f) for a in (loss, lossb, w, wb, b, bb, x, xb, t, tb, y,
+                                                       yb)], n_s, n_o, n_i)
+    return None
+
+
+def mlp2_ce_b(loss, lossb, x, xb, y, yb, w1, w1b, b1, b1b, w2, w2b, b2, b2b, h, hb, z, zb, p, pb,
+              n_s, n_i, n_h, n_o, threads=None):
+    arrs = (loss, lossb, x, xb, y, yb, w1, w1b, b1, b1b, w2, w2b, b2, b2b, h, hb, z, zb, p, pb)
+    dt = arrs[0].dtype
+    if dt == np.float32:
+        if threads is not None:
+            lib().oracle_mlp2_ce_b_f32_omp(*[_p(a, dt) for a in arrs], n_s, n_i, n_h, n_o, threads)
+        else:
+            lib().oracle_mlp2_ce_b_f32(*[_p(a, dt) for a in arrs], n_s, n_i, n_h, n_o)
+    else:
+        lib().oracle_mlp2_ce_b_f64(*[_p(a, dt) for a in arrs], n_s, n_i, n_h, n_o)
+    return None
+
+
+def mlp2_ce_hv(*args, truth=False):
+    assert len(args) == 44
+    arrs, ints, tans = list(args[:20]), args[20:24], list(args[24:])
+    if truth:
+        ld = np.longdouble
+        conv = [np.asarray(a, dtype=ld) for a in arrs + tans]
+        lib().oracle_mlp2_ce_hv_f128(*[_p(a, ld) for a in conv[:20]], *ints,
+                                     *[_p(a, ld) for a in conv[20:]])
+        for dst, src in zip(arrs + tans, conv):
+            dst[...] = src
+        return None
+    f = np.float64
+    lib().oracle_mlp2_ce_hv_f64(*[_p(a, f) for a in arrs], *ints, *[_p(a, f) for a in tans])
+    return None
+
+
+def heat2d_b(loss, lossb, u, ub, un, unb, alpha, alphab, n, n_step, u_stack):
+    f = np.float64
+    return lib().oracle_heat2d_b_f64(_p(loss, f), _p(lossb, f), _p(u, f), _p(ub, f), _p(un, f),
+                                     _p(unb, f), float(alpha), float(alphab), n, n_step,
+                                     _p(u_stack, f))
+
+
+def conv1d_relu_mse_b(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k):
+    arrs = (loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb)
+    dt = arrs[0].dtype
+    fn = lib().oracle_conv1d_relu_mse_b_f32 if dt == np.float32 else lib().oracle_conv1d_relu_mse_b_f64
+    fn(*[_p(a, dt) for a in arrs], n_b, n_c, n_l, n_o, n_k)
+    return None

@@ -1,0 +1,314 @@
+// C3 heat2d_b: adjoint of n_step explicit periodic 5-point heat steps on an
+// n x n Float64 grid, with the per-step tape of the generated sweep.
+//
+// Generated sweep being replaced (restated in oracle.cc; time loop and tape of
+// test/val-corpus/advection_b.jl:1-37, scatter adjoint of
+// stencil_loss_b.jl:12-21, periodic gather of cgen_gather_loop /
+// cgen_gather_periodic_inverse, src/STADE.jl:7343-7532):
+//   forward  step t: un = u + alpha ((((u_up + u_dn) + u_lf) + u_rt) - 4 u);
+//            tape[t] = u; u = un.           loss += sum u^2
+//   backward ub += 2 u lossb; per step t (reverse): u = tape[t];
+//            unb += ub, ub = 0; scatter unb through the stencil into ub and
+//            alphab += (lap u) unb, unb = 0.
+//
+// B200 mapping. The tape IS the sequence of states: the forward step t reads
+// tape[t-1] (u for t = 1) and writes tape[t] (un for the last step), so every
+// state is written once and read once per sweep. The scatter adjoint is
+// turned into a gather (each thread owns its output cells, no atomics); in the
+// interior the five contributions are added in the order the generated
+// reverse loop adds them, so interior cells match the oracle bit for bit.
+// Each thread owns two adjacent columns (16-byte loads) over a strip of rows,
+// keeping the rows above and below in registers; horizontal neighbours come
+// from the neighbouring lanes by warp shuffle. alphab and loss are summed per
+// block, then over blocks in a fixed order.
+#include "common.cuh"
+
+namespace stade {
+namespace {
+
+constexpr int kThreads = 128;   // 128 threads x 2 columns = 256 columns per block
+constexpr int kColsPerBlock = 2 * kThreads;
+constexpr int kRowsFwd = 16;
+constexpr int kRowsBwd = 8;
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ double2 ld2(const double* __restrict__ p, int64_t row, int n, int j) {
+  return __ldg(reinterpret_cast<const double2*>(p + row * (int64_t)n + j));
+}
+
+// Horizontal neighbours of the thread's two columns (j, j+1) on one row.
+__device__ __forceinline__ void hnbrs(const double* __restrict__ p, int64_t row, int n, int j,
+                                      double2 c, int lane, double& left_of_j,
+                                      double& right_of_j1) {
+  left_of_j = __shfl_up_sync(kFull, c.y, 1);
+  right_of_j1 = __shfl_down_sync(kFull, c.x, 1);
+  if (lane == 0) left_of_j = __ldg(p + row * (int64_t)n + (j == 0 ? n - 1 : j - 1));
+  if (lane == 31 || j + 2 >= n) right_of_j1 = __ldg(p + row * (int64_t)n + (j + 2 >= n ? j + 2 - n : j + 2));
+}
+
+__device__ __forceinline__ double heat_point(double c, double up, double dn, double lf, double rt,
+                                             double alpha) {
+  // c + alpha * ((((up + dn) + lf) + rt) - 4.0 * c), two roundings per a*b+c
+  double s = __dadd_rn(__dadd_rn(__dadd_rn(up, dn), lf), rt);
+  s = __dadd_rn(s, -__dmul_rn(4.0, c));
+  return __dadd_rn(c, __dmul_rn(alpha, s));
+}
+
+// One forward step: dst = step(src); optionally copy_dst = src (tape slot 0)
+// and a per-block partial of sum(dst^2) (the loss, last step only).
+template <int R>
+__global__ void __launch_bounds__(kThreads)
+heat_fwd_kernel(const double* __restrict__ src, double* __restrict__ dst,
+                double* __restrict__ copy_dst, double alpha, int n,
+                double* __restrict__ loss_part) {
+  __shared__ double red[kThreads / 32];
+  const int lane = threadIdx.x & 31;
+  const int j_raw = blockIdx.x * kColsPerBlock + threadIdx.x * 2;
+  const bool col_ok = j_raw < n;
+  const int j = col_ok ? j_raw : n - 2;
+  const int i0 = blockIdx.y * R;
+  int row_up = i0 == 0 ? n - 1 : i0 - 1;
+  double2 up = ld2(src, row_up, n, j);
+  double2 cur = ld2(src, i0 % n, n, j);
+  double lsum = 0.0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = i0 + r;
+    const int iw = i % n;                    // rows past n (n % R != 0) are not stored
+    const int idn = iw + 1 == n ? 0 : iw + 1;
+    const double2 dn = ld2(src, idn, n, j);
+    double lf, rt;
+    hnbrs(src, iw, n, j, cur, lane, lf, rt);
+    double2 o;
+    o.x = heat_point(cur.x, up.x, dn.x, lf, cur.y, alpha);
+    o.y = heat_point(cur.y, up.y, dn.y, cur.x, rt, alpha);
+    if (col_ok && i < n) {
+      *reinterpret_cast<double2*>(dst + (int64_t)i * n + j) = o;
+      if (copy_dst) *reinterpret_cast<double2*>(copy_dst + (int64_t)i * n + j) = cur;
+      if (loss_part) lsum += __dadd_rn(__dmul_rn(o.x, o.x), __dmul_rn(o.y, o.y));
+    }
+    up = cur;
+    cur = dn;
+  }
+  if (loss_part) {
+    lsum = block_sum(lsum, red);
+    if (threadIdx.x == 0) loss_part[blockIdx.y * gridDim.x + blockIdx.x] = lsum;
+  }
+}
+
+// ub_{t-1} = gather of unb_t through the stencil; alphab partial
+// += sum (lap u_{t-1}) unb_t. The five contributions to a cell are added in
+// the generated reverse loop's interior order: from the cell below, the cell
+// to the right, the cell itself (+g, then 4 * -(alpha g)), the cell to the
+// left, the cell above.
+__device__ __forceinline__ double gather_point(double gc, double g_above, double g_below,
+                                               double g_left, double g_right, double alpha) {
+  double acc = __dadd_rn(__dmul_rn(alpha, g_below), __dmul_rn(alpha, g_right));
+  acc = __dadd_rn(acc, gc);
+  acc = __dadd_rn(acc, __dmul_rn(4.0, -__dmul_rn(alpha, gc)));
+  acc = __dadd_rn(acc, __dmul_rn(alpha, g_left));
+  acc = __dadd_rn(acc, __dmul_rn(alpha, g_above));
+  return acc;
+}
+
+__device__ __forceinline__ double lap_point(double c, double up, double dn, double lf, double rt) {
+  double s = __dadd_rn(__dadd_rn(__dadd_rn(up, dn), lf), rt);
+  return __dadd_rn(s, -__dmul_rn(4.0, c));
+}
+
+template <int R>
+__global__ void __launch_bounds__(kThreads)
+heat_bwd_kernel(const double* __restrict__ g, const double* __restrict__ u,
+                double* __restrict__ gdst, double alpha, int n,
+                double* __restrict__ alpha_part, int first) {
+  __shared__ double red[kThreads / 32];
+  const int lane = threadIdx.x & 31;
+  const int j_raw = blockIdx.x * kColsPerBlock + threadIdx.x * 2;
+  const bool col_ok = j_raw < n;
+  const int j = col_ok ? j_raw : n - 2;
+  const int i0 = blockIdx.y * R;
+  const int row_up = i0 == 0 ? n - 1 : i0 - 1;
+  double2 gu = ld2(g, row_up, n, j), gc = ld2(g, i0 % n, n, j);
+  double2 uu = ld2(u, row_up, n, j), uc = ld2(u, i0 % n, n, j);
+  double asum = 0.0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = i0 + r;
+    const int iw = i % n;
+    const int idn = iw + 1 == n ? 0 : iw + 1;
+    const double2 gd = ld2(g, idn, n, j);
+    const double2 ud = ld2(u, idn, n, j);
+    double g_lf, g_rt, u_lf, u_rt;
+    hnbrs(g, iw, n, j, gc, lane, g_lf, g_rt);
+    hnbrs(u, iw, n, j, uc, lane, u_lf, u_rt);
+    double2 o;
+    o.x = gather_point(gc.x, gu.x, gd.x, g_lf, gc.y, alpha);
+    o.y = gather_point(gc.y, gu.y, gd.y, gc.x, g_rt, alpha);
+    if (col_ok && i < n) {
+      *reinterpret_cast<double2*>(gdst + (int64_t)i * n + j) = o;
+      asum = fma(lap_point(uc.x, uu.x, ud.x, u_lf, uc.y), gc.x, asum);
+      asum = fma(lap_point(uc.y, uu.y, ud.y, uc.x, u_rt), gc.y, asum);
+    }
+    gu = gc; gc = gd;
+    uu = uc; uc = ud;
+  }
+  asum = block_sum(asum, red);
+  if (threadIdx.x == 0) {
+    const int b = blockIdx.y * gridDim.x + blockIdx.x;
+    alpha_part[b] = first ? asum : alpha_part[b] + asum;
+  }
+}
+
+// g = unb + (ub + (2 u_final) lossb), written into `dst` (one of ub / unb).
+__global__ void heat_bwd_init_kernel(const double* __restrict__ ub, const double* __restrict__ unb,
+                                     const double* __restrict__ ufin,
+                                     const double* __restrict__ lossb,
+                                     double* __restrict__ dst, int64_t nn2) {
+  const double lb = lossb[0];
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nn2;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const double2 a = reinterpret_cast<const double2*>(ub)[e];
+    const double2 b = reinterpret_cast<const double2*>(unb)[e];
+    const double2 c = reinterpret_cast<const double2*>(ufin)[e];
+    double2 o;
+    o.x = __dadd_rn(b.x, __dadd_rn(a.x, __dmul_rn(__dmul_rn(2.0, c.x), lb)));
+    o.y = __dadd_rn(b.y, __dadd_rn(a.y, __dmul_rn(__dmul_rn(2.0, c.y), lb)));
+    reinterpret_cast<double2*>(dst)[e] = o;
+  }
+}
+
+// n_step == 0: loss += sum u^2, ub += 2 u lossb.
+__global__ void heat_nostep_kernel(const double* __restrict__ u, double* __restrict__ ub,
+                                   const double* __restrict__ lossb, int64_t nn,
+                                   double* __restrict__ part) {
+  __shared__ double red[32];
+  const double lb = lossb[0];
+  double s = 0.0;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nn;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const double v = u[e];
+    s += __dmul_rn(v, v);
+    ub[e] = __dadd_rn(ub[e], __dmul_rn(__dmul_rn(2.0, v), lb));
+  }
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+
+struct Grid {
+  dim3 fwd, bwd;
+  int nfwd, nbwd;
+};
+Grid grid_of(int64_t n) {
+  Grid g;
+  g.fwd = dim3(ceil_div_u(n, kColsPerBlock), ceil_div_u(n, kRowsFwd));
+  g.bwd = dim3(ceil_div_u(n, kColsPerBlock), ceil_div_u(n, kRowsBwd));
+  g.nfwd = (int)(g.fwd.x * g.fwd.y);
+  g.nbwd = (int)(g.bwd.x * g.bwd.y);
+  return g;
+}
+
+constexpr int kNoStepBlocks = 1184;  // 8 per SM
+
+}  // namespace
+}  // namespace stade
+
+using namespace stade;
+
+extern "C" int64_t stade_initstacks_heat2d_b(int64_t n, int64_t n_step) {
+  // max(0, div(n_step - 1, 1) + 1) * max(0, div(n * n - 1, 1) + 1), as initstacks_* sizes it
+  if (n <= 0 || n_step <= 0) return 0;
+  return n_step * n * n;
+}
+
+extern "C" size_t stade_heat2d_b_f64_workspace(int64_t n, int64_t n_step) {
+  if (n <= 0) return 0;
+  const Grid g = grid_of(n);
+  Sizer z;
+  z.take<double>((size_t)g.nfwd);                         // loss partials
+  z.take<double>((size_t)(g.nbwd > kNoStepBlocks ? g.nbwd : kNoStepBlocks));  // alphab partials
+  z.take<double>(2);                                      // host-scalar staging
+  (void)n_step;
+  return z.bytes();
+}
+
+extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, double* u,
+                                           double* ub, double* un, double* unb, double alpha,
+                                           double* alphab, int64_t n, int64_t n_step,
+                                           double* u_stack, const stade_opts* opts) {
+  STADE_REQUIRE(n >= 0 && n_step >= 0, "heat2d_b: negative size");
+  STADE_REQUIRE(alphab != nullptr, "heat2d_b: alphab is null");
+  if (n == 0) return STADE_OK;
+  STADE_REQUIRE(n % 2 == 0 && n >= 4, "heat2d_b: n must be even and >= 4 (got %lld)", (long long)n);
+  STADE_REQUIRE(n <= 65536, "heat2d_b: n = %lld exceeds 65536", (long long)n);
+  STADE_REQUIRE(loss && lossb && u && ub && un && unb, "heat2d_b: null array argument");
+  STADE_REQUIRE(n_step == 0 || u_stack, "heat2d_b: u_stack is null");
+  for (const void* p : {(const void*)u, (const void*)ub, (const void*)un, (const void*)unb,
+                        (const void*)u_stack})
+    STADE_REQUIRE(p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0,
+                  "heat2d_b: arrays must be 16-byte aligned");
+  const bool host_scalar = (flags_of(opts) & STADE_HOST_SCALARS) != 0;
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(opts, stade_heat2d_b_f64_workspace(n, n_step), &wsp);
+  if (st != STADE_OK) return st;
+  const Grid g = grid_of(n);
+  Carver c(wsp);
+  double* loss_part = c.take<double>((size_t)g.nfwd);
+  double* alpha_part = c.take<double>((size_t)(g.nbwd > kNoStepBlocks ? g.nbwd : kNoStepBlocks));
+  double* stage = c.take<double>(2);
+  double* alphab_dev = alphab;
+  if (host_scalar) {
+    STADE_CUDA(cudaMemcpyAsync(stage, alphab, sizeof(double), cudaMemcpyHostToDevice, s));
+    alphab_dev = stage;
+  }
+  const int ni = (int)n;
+  const int64_t nn = n * n;
+
+  if (n_step == 0) {
+    heat_nostep_kernel<<<kNoStepBlocks, 256, 0, s>>>(u, ub, lossb, nn, loss_part);
+    STADE_CHECK_LAUNCH();
+    st = launch_sum_to_scalar(loss_part, kNoStepBlocks, loss, true, s);
+    if (st != STADE_OK) return st;
+  } else {
+    // forward sweep: tape[t] = state before step t+1
+    for (int64_t t = 1; t <= n_step; ++t) {
+      const double* src = t == 1 ? u : u_stack + (t - 1) * nn;
+      double* dst = t == n_step ? un : u_stack + t * nn;
+      double* copy = t == 1 ? u_stack : nullptr;
+      PhaseScope ph("fwd_step", s);
+      heat_fwd_kernel<kRowsFwd><<<g.fwd, kThreads, 0, s>>>(src, dst, copy, alpha, ni,
+                                                           t == n_step ? loss_part : nullptr);
+      STADE_CHECK_LAUNCH();
+    }
+    st = launch_sum_to_scalar(loss_part, g.nfwd, loss, true, s);
+    if (st != STADE_OK) return st;
+    // backward sweep; the first step reads the seed from `a`, steps alternate
+    // a -> b -> a ... and the last one lands in ub
+    double* a = (n_step % 2 == 0) ? ub : unb;
+    double* b = (n_step % 2 == 0) ? unb : ub;
+    {
+      PhaseScope ph("bwd_init", s);
+      heat_bwd_init_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, a, nn / 2);
+      STADE_CHECK_LAUNCH();
+    }
+    for (int64_t t = n_step; t >= 1; --t) {
+      PhaseScope ph("bwd_step", s);
+      heat_bwd_kernel<kRowsBwd><<<g.bwd, kThreads, 0, s>>>(a, u_stack + (t - 1) * nn, b, alpha, ni,
+                                                           alpha_part, t == n_step ? 1 : 0);
+      STADE_CHECK_LAUNCH();
+      double* tmp = a; a = b; b = tmp;
+    }
+    // the result is in ub (== a now); the other buffer is unb, consumed to zero
+    {
+      PhaseScope ph("zero_unb", s);
+      STADE_CUDA(cudaMemsetAsync(unb, 0, (size_t)nn * sizeof(double), s));
+    }
+    st = launch_sum_to_scalar(alpha_part, g.nbwd, alphab_dev, true, s);
+    if (st != STADE_OK) return st;
+  }
+  if (host_scalar) {
+    STADE_CUDA(cudaMemcpyAsync(alphab, stage, sizeof(double), cudaMemcpyDeviceToHost, s));
+    STADE_CUDA(cudaStreamSynchronize(s));
+  }
+  return STADE_OK;
+}

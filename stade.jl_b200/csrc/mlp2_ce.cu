@@ -1,0 +1,914 @@
+// C2 mlp2_ce_b (Float32 adjoint) and C5 mlp2_ce_hv (Float64 HVP).
+//
+// Generated sweeps being replaced (restated in oracle.cc): the adjoint of a
+// batch-loop kernel h = tanh(x W1 + b1), z = h W2 + b2, softmax
+// cross-entropy, in the pattern of test/val-corpus/mlp1d_b.jl:5-78 (hidden
+// and output layers) and transformer_b.jl:615-667 (softmax reverse), and its
+// forward-over-reverse HVP as test/val-corpus/mlp1d_hv.jl.
+//
+// B200 mapping, per sweep:
+//   1. s1 = x W1 (GEMM), epilogue h = tanh(s1 + b1)     [HVP: + s1d, hd]
+//   2. per-sample head, one warp per sample: z, softmax, the whole reverse of
+//      the loss and softmax, then hb = W2 g and s1b = (1 - h^2) hb, all in
+//      registers; the generated code's tape of the row-max chain lives in
+//      registers too.
+//   3. W2b = h^T g, b2b = sum g: per-chunk partials, fixed-order sum.
+//   4. W1b = x^T s1b (GEMM, split over samples, fixed-order slice sum) with
+//      b1b = sum s1b fused as an extra row of ones in x^T.
+//   5. xb += s1b W1^T (GEMM).
+// The generated CUDA.jl port does 2-4 with atomics on every weight
+// (cgen_device_assign, src/STADE.jl:11941); here nothing is atomic.
+#include "common.cuh"
+#include "gemm_simt.cuh"
+#include "tc_gemm.cuh"
+
+namespace stade {
+namespace {
+
+constexpr int kHeadWarps = 8;   // samples in flight per block
+constexpr int kW2Chunk = 256;   // samples per W2b partial
+
+template <class T> __device__ __forceinline__ T dtanh(T x);
+template <> __device__ __forceinline__ float dtanh(float x) { return tanhf(x); }
+template <> __device__ __forceinline__ double dtanh(double x) { return tanh(x); }
+template <class T> __device__ __forceinline__ T dexp(T x);
+template <> __device__ __forceinline__ float dexp(float x) { return expf(x); }
+template <> __device__ __forceinline__ double dexp(double x) { return exp(x); }
+template <class T> __device__ __forceinline__ T dlog(T x);
+template <> __device__ __forceinline__ float dlog(float x) { return logf(x); }
+template <> __device__ __forceinline__ double dlog(double x) { return log(x); }
+template <class T> __device__ __forceinline__ T dsign(T x) {
+  return x > T(0) ? T(1) : (x < T(0) ? T(-1) : x);
+}
+// Julia's max: NaN wins, then the larger, +0.0 over -0.0
+template <class T> __device__ __forceinline__ T jmax(T a, T b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a > b) return a;
+  if (b > a) return b;
+  return signbit(a) ? b : a;
+}
+template <class T> __device__ __forceinline__ T radd(T a, T b);
+template <> __device__ __forceinline__ float radd(float a, float b) { return __fadd_rn(a, b); }
+template <> __device__ __forceinline__ double radd(double a, double b) { return __dadd_rn(a, b); }
+template <class T> __device__ __forceinline__ T rmul(T a, T b);
+template <> __device__ __forceinline__ float rmul(float a, float b) { return __fmul_rn(a, b); }
+template <> __device__ __forceinline__ double rmul(double a, double b) { return __dmul_rn(a, b); }
+
+// ---------------------------------------------------------------------------
+// Per-sample head of the adjoint (Float32 or Float64), one warp per sample.
+// NO = class capacity (>= n_o). Writes z, p (forward values), adds into yb,
+// consumes zb, pb, hb to zero, and writes g = total zb (gbuf, n_s x n_o) and
+// s1b = (1 - h^2) hb (s1b, n_s x n_h).
+template <class T, int NO>
+__global__ void __launch_bounds__(kHeadWarps * 32)
+mlp_head_b_kernel(const T* __restrict__ lossb, const T* __restrict__ y, T* __restrict__ yb,
+                  const T* __restrict__ w2, const T* __restrict__ b2, const T* __restrict__ h,
+                  T* __restrict__ hb, T* __restrict__ z, T* __restrict__ zb, T* __restrict__ p,
+                  T* __restrict__ pb, T* __restrict__ gbuf, T* __restrict__ s1b, int n_s,
+                  int n_h, int n_o, T* __restrict__ loss_part) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  T* w2t = reinterpret_cast<T*>(smraw);  // [n_o][n_h], transposed for conflict-free reads
+  __shared__ T red[kHeadWarps];
+  for (int e = threadIdx.x; e < n_h * n_o; e += blockDim.x) {
+    const int k = e / n_o, c = e % n_o;
+    w2t[c * n_h + k] = w2[e];
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int s = blockIdx.x * kHeadWarps + warp;
+  const T lb = lossb[0];
+  T loss_acc = T(0);
+  if (s < n_s) {
+    const T* hr = h + (int64_t)s * n_h;
+    T zp[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) zp[c] = T(0);
+    for (int k = lane; k < n_h; k += 32) {
+      const T hv = hr[k];
+#pragma unroll
+      for (int c = 0; c < NO; ++c)
+        if (c < n_o) zp[c] = fma(hv, w2t[c * n_h + k], zp[c]);
+    }
+    T zv[NO], yv[NO], pbin[NO], zbin[NO], ybin[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      T v = c < n_o ? warp_sum(zp[c]) : T(0);
+      zv[c] = c < n_o ? v + b2[c] : T(0);
+    }
+    const int64_t row = (int64_t)s * n_o;
+    {
+      // lane c loads the per-class inputs, then every lane gets all of them
+      const T yl = lane < n_o ? y[row + lane] : T(0);
+      const T pbl = lane < n_o ? pb[row + lane] : T(0);
+      const T zbl = lane < n_o ? zb[row + lane] : T(0);
+      const T ybl = lane < n_o ? yb[row + lane] : T(0);
+#pragma unroll
+      for (int c = 0; c < NO; ++c) {
+        yv[c] = __shfl_sync(0xffffffffu, yl, c);
+        pbin[c] = __shfl_sync(0xffffffffu, pbl, c);
+        zbin[c] = __shfl_sync(0xffffffffu, zbl, c);
+        ybin[c] = __shfl_sync(0xffffffffu, ybl, c);
+      }
+    }
+    // forward softmax cross-entropy, in the generated statement order
+    T mprev[NO];
+    T m = zv[0];
+#pragma unroll
+    for (int c = 1; c < NO; ++c)
+      if (c < n_o) { mprev[c] = m; m = jmax(m, zv[c]); }
+    T pv[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) pv[c] = c < n_o ? dexp(radd(zv[c], -m)) : T(0);
+    T rs = T(0);
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) rs = radd(rs, pv[c]);
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) loss_acc = radd(loss_acc, -rmul(yv[c], dlog(pv[c] / rs)));
+    // reverse: loss statement, i_c = n_o:-1:1
+    T ybout[NO], pbv[NO];
+    T rsb = T(0);
+#pragma unroll
+    for (int c = NO - 1; c >= 0; --c) {
+      if (c < n_o) {
+        const T q = pv[c] / rs;
+        ybout[c] = radd(ybin[c], rmul(-(dlog(q)), lb));
+        const T qb = rmul(T(1) / q, rmul(-(yv[c]), lb));
+        pbv[c] = radd(pbin[c], rmul(T(1) / rs, qb));
+        rsb = radd(rsb, rmul(-(pv[c] / rmul(rs, rs)), qb));
+      }
+    }
+    // row_sum loop, then the exp loop
+    T g[NO];
+    T mb = T(0);
+#pragma unroll
+    for (int c = NO - 1; c >= 0; --c) {
+      if (c < n_o) {
+        const T oldb = radd(pbv[c], rsb);
+        const T cse = rmul(pv[c], oldb);
+        g[c] = radd(zbin[c], cse);
+        mb = radd(mb, -cse);
+      }
+    }
+    // row-max chain, i_c = n_o:-1:2, then row_max = z[1]
+#pragma unroll
+    for (int c = NO - 1; c >= 1; --c) {
+      if (c < n_o) {
+        const T oldb = mb;
+        mb = rmul(T(0.5) * (T(1) + dsign(radd(mprev[c], -zv[c]))), oldb);
+        g[c] = radd(g[c], rmul(T(0.5) * (T(1) + dsign(radd(zv[c], -mprev[c]))), oldb));
+      }
+    }
+    g[0] = radd(g[0], mb);
+    // outputs of the per-class part; lane c stores class c
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o && lane == c) {
+        z[row + c] = zv[c];
+        p[row + c] = pv[c];
+        yb[row + c] = ybout[c];
+        zb[row + c] = T(0);
+        pb[row + c] = T(0);
+        gbuf[row + c] = g[c];
+      }
+    }
+    // hidden adjoint: hb[s,k] += w2[k,c] g_c for c = n_o:-1:1, then consumed
+    T* hbr = hb + (int64_t)s * n_h;
+    T* s1br = s1b + (int64_t)s * n_h;
+    for (int k = lane; k < n_h; k += 32) {
+      T acc = hbr[k];
+#pragma unroll
+      for (int c = NO - 1; c >= 0; --c)
+        if (c < n_o) acc = radd(acc, rmul(w2t[c * n_h + k], g[c]));
+      const T th = hr[k];
+      s1br[k] = rmul(radd(T(1), -rmul(th, th)), acc);
+      hbr[k] = T(0);
+    }
+  }
+  // fixed-order block sum of the per-warp loss terms
+  if (lane == 0) red[warp] = loss_acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    T acc = T(0);
+    for (int w = 0; w < kHeadWarps; ++w) acc += red[w];
+    loss_part[blockIdx.x] = acc;
+  }
+}
+
+// W2b[k, c] partial = sum over the chunk's samples of h[s,k] g[s,c]; b2b[c]
+// partial = sum g[s,c]. One thread per k; partial layout [chunk][n_h*n_o + n_o].
+template <class T, int NO>
+__global__ void __launch_bounds__(256)
+mlp_w2b_partial_kernel(const T* __restrict__ h, const T* __restrict__ gbuf, int n_s, int n_h,
+                       int n_o, int chunk, T* __restrict__ part) {
+  const int s0 = blockIdx.x * chunk;
+  const int s1 = min(n_s, s0 + chunk);
+  T* my = part + (int64_t)blockIdx.x * (n_h * n_o + n_o);
+  for (int k = threadIdx.x; k < n_h; k += blockDim.x) {
+    T acc[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) acc[c] = T(0);
+    for (int s = s0; s < s1; ++s) {
+      const T hv = h[(int64_t)s * n_h + k];
+      const T* gr = gbuf + (int64_t)s * n_o;
+#pragma unroll
+      for (int c = 0; c < NO; ++c)
+        if (c < n_o) acc[c] = fma(hv, gr[c], acc[c]);
+    }
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) my[k * n_o + c] = acc[c];
+  }
+  if (threadIdx.x < n_o) {
+    const int c = threadIdx.x;
+    T acc = T(0);
+    for (int s = s0; s < s1; ++s) acc += gbuf[(int64_t)s * n_o + c];
+    my[n_h * n_o + c] = acc;
+  }
+}
+
+// Sum partial vectors of length len1 + len2 in chunk order into two arrays.
+template <class T>
+__global__ void finish_two_kernel(const T* __restrict__ part, int count, int64_t len1,
+                                  T* __restrict__ dst1, int64_t len2, T* __restrict__ dst2) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t len = len1 + len2;
+  if (e >= len) return;
+  T acc = T(0);
+  for (int p = 0; p < count; ++p) acc += part[(int64_t)p * len + e];
+  if (e < len1) dst1[e] += acc;
+  else dst2[e - len1] += acc;
+}
+
+// ---- epilogues ---------------------------------------------------------------
+template <class T>
+struct EpiTanh : EpiBase {  // h[m, n] = tanh(acc + b1[n])
+  const T* b1;
+  T* h;
+  int ld;
+  __device__ __forceinline__ void operator()(int m, int n, T acc) const {
+    h[(int64_t)m * ld + n] = dtanh(acc + b1[n]);
+  }
+};
+template <class T>
+struct EpiAddTo : EpiBase {  // dst[m, n] += acc
+  T* dst;
+  int ld;
+  __device__ __forceinline__ void operator()(int m, int n, T acc) const {
+    T* q = dst + (int64_t)m * ld + n;
+    *q = *q + acc;
+  }
+};
+template <class T>
+struct EpiWeightBias : EpiBase {  // rows < n_w: w[m, n] += acc; row n_w: bias[n] += acc
+  T* w;
+  T* bias;
+  int n_w, ld;
+  __device__ __forceinline__ void operator()(int m, int n, T acc) const {
+    if (m < n_w) {
+      T* q = w + (int64_t)m * ld + n;
+      *q = *q + acc;
+    } else {
+      bias[n] = bias[n] + acc;
+    }
+  }
+};
+
+// ---- loaders -------------------------------------------------------------------
+template <class T>
+struct LdRow {  // A(m, k) = a[m * ld + k]
+  const T* a;
+  int ld;
+  __device__ __forceinline__ T operator()(int m, int k) const { return a[(int64_t)m * ld + k]; }
+};
+template <class T>
+struct LdB {  // B(k, n) = b[k * ld + n]
+  const T* b;
+  int ld;
+  __device__ __forceinline__ T operator()(int k, int n) const { return b[(int64_t)k * ld + n]; }
+};
+template <class T>
+struct LdBT {  // B(k, n) = b[n * ld + k]
+  const T* b;
+  int ld;
+  __device__ __forceinline__ T operator()(int k, int n) const { return b[(int64_t)n * ld + k]; }
+};
+template <class T>
+struct LdXtOnes {  // A(m, k) = x[k * ld + m] for m < n_m, 1 for m == n_m
+  const T* x;
+  int ld, n_m;
+  __device__ __forceinline__ T operator()(int m, int k) const {
+    return m < n_m ? x[(int64_t)k * ld + m] : T(1);
+  }
+};
+
+constexpr int kF32RM = 2, kF32RN = 2, kF32BK = 16;
+constexpr int kF64RM = 2, kF64RN = 2, kF64BK = 8;
+
+template <class T, int RM, int RN, int BK>
+int splits_for(int M, int N, int K) {
+  const int tiles = ((M + 64 * RM - 1) / (64 * RM)) * ((N + 64 * RN - 1) / (64 * RN));
+  return split_plan(tiles, K, BK, 64).splits;
+}
+
+
+// ---------------------------------------------------------------------------
+// Per-sample head of the Float64 HVP: every statement of the head with its
+// tangent twin (oracle.cc mlp2_ce_hv; hvp_double_stmt, src/STADE.jl:6904).
+template <int NO>
+__global__ void __launch_bounds__(kHeadWarps * 32)
+mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ lossbd,
+                   const double* __restrict__ y, double* __restrict__ yb,
+                   const double* __restrict__ yd, double* __restrict__ ybd,
+                   const double* __restrict__ w2, const double* __restrict__ b2,
+                   const double* __restrict__ w2d, const double* __restrict__ b2d,
+                   const double* __restrict__ h, double* __restrict__ hb,
+                   const double* __restrict__ hd, double* __restrict__ hbd,
+                   double* __restrict__ z, double* __restrict__ zb, double* __restrict__ zd,
+                   double* __restrict__ zbd, double* __restrict__ p, double* __restrict__ pb,
+                   double* __restrict__ pd, double* __restrict__ pbd,
+                   double* __restrict__ gbuf, double* __restrict__ gdbuf,
+                   double* __restrict__ s1b, double* __restrict__ s1bd, int n_s, int n_h, int n_o,
+                   double* __restrict__ loss_part, double* __restrict__ lossd_part) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  double* w2t = reinterpret_cast<double*>(smraw);  // [n_o][n_h]
+  double* w2dt = w2t + (size_t)n_o * n_h;
+  __shared__ double red[2][kHeadWarps];
+  for (int e = threadIdx.x; e < n_h * n_o; e += blockDim.x) {
+    const int k = e / n_o, c = e % n_o;
+    w2t[c * n_h + k] = w2[e];
+    w2dt[c * n_h + k] = w2d[e];
+  }
+  __syncthreads();
+  const unsigned F = 0xffffffffu;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int s = blockIdx.x * kHeadWarps + warp;
+  const double lb = lossb[0], lbd = lossbd[0];
+  double loss_acc = 0.0, lossd_acc = 0.0;
+  if (s < n_s) {
+    const double* hr = h + (int64_t)s * n_h;
+    const double* hdr = hd + (int64_t)s * n_h;
+    double zp[NO], zdp[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) { zp[c] = 0.0; zdp[c] = 0.0; }
+    for (int k = lane; k < n_h; k += 32) {
+      const double hv = hr[k], hdv = hdr[k];
+#pragma unroll
+      for (int c = 0; c < NO; ++c) {
+        if (c < n_o) {
+          const double wv = w2t[c * n_h + k];
+          zdp[c] += hv * w2dt[c * n_h + k] + wv * hdv;
+          zp[c] = fma(wv, hv, zp[c]);
+        }
+      }
+    }
+    double zv[NO], zdv[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      zv[c] = c < n_o ? warp_sum(zp[c]) + b2[c] : 0.0;
+      zdv[c] = c < n_o ? warp_sum(zdp[c]) + b2d[c] : 0.0;
+    }
+    const int64_t row = (int64_t)s * n_o;
+    double yv[NO], ydv[NO], pbin[NO], pbdin[NO], zbin[NO], zbdin[NO], ybin[NO], ybdin[NO];
+    {
+      const bool ok = lane < n_o;
+      const double a0 = ok ? y[row + lane] : 0.0, a1 = ok ? yd[row + lane] : 0.0;
+      const double a2 = ok ? pb[row + lane] : 0.0, a3 = ok ? pbd[row + lane] : 0.0;
+      const double a4 = ok ? zb[row + lane] : 0.0, a5 = ok ? zbd[row + lane] : 0.0;
+      const double a6 = ok ? yb[row + lane] : 0.0, a7 = ok ? ybd[row + lane] : 0.0;
+#pragma unroll
+      for (int c = 0; c < NO; ++c) {
+        yv[c] = __shfl_sync(F, a0, c); ydv[c] = __shfl_sync(F, a1, c);
+        pbin[c] = __shfl_sync(F, a2, c); pbdin[c] = __shfl_sync(F, a3, c);
+        zbin[c] = __shfl_sync(F, a4, c); zbdin[c] = __shfl_sync(F, a5, c);
+        ybin[c] = __shfl_sync(F, a6, c); ybdin[c] = __shfl_sync(F, a7, c);
+      }
+    }
+    // forward with tangents
+    double mprev[NO];
+    double m = zv[0], md = zdv[0];
+#pragma unroll
+    for (int c = 1; c < NO; ++c) {
+      if (c < n_o) {
+        mprev[c] = m;
+        const double g1 = 0.5 * (1.0 + dsign(m - zv[c]));
+        const double g2 = 0.5 * (1.0 + dsign(zv[c] - m));
+        md = g1 * md + g2 * zdv[c];
+        m = jmax(m, zv[c]);
+      }
+    }
+    double pv[NO], pdv[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        const double e = exp(zv[c] - m);
+        pdv[c] = e * (zdv[c] - md);
+        pv[c] = e;
+      } else {
+        pv[c] = 0.0; pdv[c] = 0.0;
+      }
+    }
+    double rs = 0.0, rsd = 0.0;
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) { rsd = rsd + pdv[c]; rs = rs + pv[c]; }
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        const double q = pv[c] / rs;
+        const double qd = pdv[c] / rs - (pv[c] / (rs * rs)) * rsd;
+        lossd_acc = lossd_acc - (ydv[c] * log(q) + yv[c] * (qd / q));
+        loss_acc = loss_acc - yv[c] * log(q);
+      }
+    }
+    // reverse of the loss statement with tangents
+    double ybo[NO], ybdo[NO], pbv[NO], pbdv[NO];
+    double rsb = 0.0, rsbd = 0.0;
+#pragma unroll
+    for (int c = NO - 1; c >= 0; --c) {
+      if (c < n_o) {
+        const double q = pv[c] / rs;
+        const double qd = pdv[c] / rs - (pv[c] / (rs * rs)) * rsd;
+        const double lq = log(q), lqd = qd / q;
+        ybdo[c] = ybdin[c] + -(lqd * lb + lq * lbd);
+        ybo[c] = ybin[c] + -(lq) * lb;
+        const double inv_q = 1.0 / q, inv_qd = -(qd / (q * q));
+        const double ny = -(yv[c]) * lb, nyd = -(ydv[c] * lb + yv[c] * lbd);
+        const double qbd = inv_qd * ny + inv_q * nyd;
+        const double qb = inv_q * ny;
+        const double inv_rs = 1.0 / rs, inv_rsd = -(rsd / (rs * rs));
+        pbdv[c] = pbdin[c] + (inv_rsd * qb + inv_rs * qbd);
+        pbv[c] = pbin[c] + inv_rs * qb;
+        const double pr2 = pv[c] / (rs * rs);
+        const double pr2d = pdv[c] / (rs * rs) - (pv[c] / (rs * rs)) * ((2.0 * rs * rsd) / (rs * rs));
+        rsbd = rsbd + -(pr2d * qb + pr2 * qbd);
+        rsb = rsb + -(pr2) * qb;
+      }
+    }
+    double g[NO], gd[NO];
+    double mb = 0.0, mbd = 0.0;
+#pragma unroll
+    for (int c = NO - 1; c >= 0; --c) {
+      if (c < n_o) {
+        const double oldbd = pbdv[c] + rsbd, oldb = pbv[c] + rsb;
+        const double e = pv[c];
+        const double ed = e * (zdv[c] - md);
+        const double csed = ed * oldb + e * oldbd;
+        const double cse = e * oldb;
+        gd[c] = zbdin[c] + csed;
+        g[c] = zbin[c] + cse;
+        mbd = mbd + -csed;
+        mb = mb + -cse;
+      }
+    }
+#pragma unroll
+    for (int c = NO - 1; c >= 1; --c) {
+      if (c < n_o) {
+        const double oldbd = mbd, oldb = mb;
+        const double g1 = 0.5 * (1.0 + dsign(mprev[c] - zv[c]));
+        const double g2 = 0.5 * (1.0 + dsign(zv[c] - mprev[c]));
+        mbd = 0.0 + g1 * oldbd;
+        mb = 0.0 + g1 * oldb;
+        gd[c] = gd[c] + g2 * oldbd;
+        g[c] = g[c] + g2 * oldb;
+      }
+    }
+    gd[0] = gd[0] + mbd;
+    g[0] = g[0] + mb;
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o && lane == c) {
+        z[row + c] = zv[c]; zd[row + c] = zdv[c];
+        p[row + c] = pv[c]; pd[row + c] = pdv[c];
+        yb[row + c] = ybo[c]; ybd[row + c] = ybdo[c];
+        zb[row + c] = 0.0; zbd[row + c] = 0.0;
+        pb[row + c] = 0.0; pbd[row + c] = 0.0;
+        gbuf[row + c] = g[c]; gdbuf[row + c] = gd[c];
+      }
+    }
+    double* hbr = hb + (int64_t)s * n_h;
+    double* hbdr = hbd + (int64_t)s * n_h;
+    double* s1br = s1b + (int64_t)s * n_h;
+    double* s1bdr = s1bd + (int64_t)s * n_h;
+    for (int k = lane; k < n_h; k += 32) {
+      double acc = hbr[k], accd = hbdr[k];
+#pragma unroll
+      for (int c = NO - 1; c >= 0; --c) {
+        if (c < n_o) {
+          const double wv = w2t[c * n_h + k];
+          accd = accd + (g[c] * w2dt[c * n_h + k] + wv * gd[c]);
+          acc = acc + wv * g[c];
+        }
+      }
+      const double th = hr[k];
+      const double gg = 1.0 - th * th;
+      s1bdr[k] = acc * -((2.0 * th) * hdr[k]) + gg * accd;
+      s1br[k] = gg * acc;
+      hbr[k] = 0.0;
+      hbdr[k] = 0.0;
+    }
+  }
+  if (lane == 0) { red[0][warp] = loss_acc; red[1][warp] = lossd_acc; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, b = 0.0;
+    for (int w = 0; w < kHeadWarps; ++w) { a += red[0][w]; b += red[1][w]; }
+    loss_part[blockIdx.x] = a;
+    lossd_part[blockIdx.x] = b;
+  }
+}
+
+// W2b, W2bd, b2b, b2bd partials of one chunk of samples; layout
+// [chunk][n_h*n_o (W2b) + n_h*n_o (W2bd) + n_o (b2b) + n_o (b2bd)].
+template <int NO>
+__global__ void __launch_bounds__(256)
+mlp_w2b_hv_partial_kernel(const double* __restrict__ h, const double* __restrict__ hd,
+                          const double* __restrict__ gbuf, const double* __restrict__ gdbuf,
+                          int n_s, int n_h, int n_o, int chunk, double* __restrict__ part) {
+  const int s0 = blockIdx.x * chunk;
+  const int s1 = min(n_s, s0 + chunk);
+  const int64_t nw = (int64_t)n_h * n_o;
+  double* my = part + (int64_t)blockIdx.x * (2 * nw + 2 * n_o);
+  for (int k = threadIdx.x; k < n_h; k += blockDim.x) {
+    double acc[NO], accd[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) { acc[c] = 0.0; accd[c] = 0.0; }
+    for (int s = s0; s < s1; ++s) {
+      const double hv = h[(int64_t)s * n_h + k], hdv = hd[(int64_t)s * n_h + k];
+      const double* gr = gbuf + (int64_t)s * n_o;
+      const double* gdr = gdbuf + (int64_t)s * n_o;
+#pragma unroll
+      for (int c = 0; c < NO; ++c) {
+        if (c < n_o) {
+          accd[c] += gr[c] * hdv + hv * gdr[c];
+          acc[c] = fma(hv, gr[c], acc[c]);
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        my[k * n_o + c] = acc[c];
+        my[nw + k * n_o + c] = accd[c];
+      }
+    }
+  }
+  if (threadIdx.x < 2 * n_o) {
+    const int c = threadIdx.x % n_o;
+    const double* src = threadIdx.x < n_o ? gbuf : gdbuf;
+    double acc = 0.0;
+    for (int s = s0; s < s1; ++s) acc += src[(int64_t)s * n_o + c];
+    my[2 * nw + threadIdx.x] = acc;
+  }
+}
+
+// Sums [chunk][4 segments] partials in chunk order into four arrays.
+__global__ void finish_four_kernel(const double* __restrict__ part, int count, int64_t nw,
+                                   int n_o, double* __restrict__ w2b, double* __restrict__ w2bd,
+                                   double* __restrict__ b2b, double* __restrict__ b2bd) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t len = 2 * nw + 2 * n_o;
+  if (e >= len) return;
+  double acc = 0.0;
+  for (int q = 0; q < count; ++q) acc += part[(int64_t)q * len + e];
+  if (e < nw) w2b[e] += acc;
+  else if (e < 2 * nw) w2bd[e - nw] += acc;
+  else if (e < 2 * nw + n_o) b2b[e - 2 * nw] += acc;
+  else b2bd[e - 2 * nw - n_o] += acc;
+}
+
+struct EpiStore : EpiBase {  // dst[m, n] = acc
+  double* dst;
+  int ld;
+  __device__ __forceinline__ void operator()(int m, int n, double acc) const {
+    dst[(int64_t)m * ld + n] = acc;
+  }
+};
+// s1d = acc + b1d; s1 = S1 + b1; h = tanh(s1); hd = (1 - h^2) s1d
+struct EpiTanhTangent : EpiBase {
+  const double *s1, *b1, *b1d;
+  double *h, *hd;
+  int ld;
+  __device__ __forceinline__ void operator()(int m, int n, double acc) const {
+    const int64_t i = (int64_t)m * ld + n;
+    const double s1d = acc + b1d[n];
+    const double th = tanh(s1[i] + b1[n]);
+    hd[i] = (1.0 - th * th) * s1d;
+    h[i] = th;
+  }
+};
+// A(m, k) over two K segments: [a0 | a1], each row-major with leading dim ld
+struct LdRow2 {
+  const double *a0, *a1;
+  int ld, k0;
+  __device__ __forceinline__ double operator()(int m, int k) const {
+    return k < k0 ? a0[(int64_t)m * ld + k] : a1[(int64_t)m * ld + (k - k0)];
+  }
+};
+// B(k, n) over two K segments: [b0 ; b1], each row-major with leading dim ld
+struct LdB2 {
+  const double *b0, *b1;
+  int ld, k0;
+  __device__ __forceinline__ double operator()(int k, int n) const {
+    return k < k0 ? b0[(int64_t)k * ld + n] : b1[(int64_t)(k - k0) * ld + n];
+  }
+};
+// B(k, n) = [b0^T ; b1^T](k, n): b0[n * ld + k] for k < k0, b1[n * ld + k - k0] after
+struct LdBT2 {
+  const double *b0, *b1;
+  int ld, k0;
+  __device__ __forceinline__ double operator()(int k, int n) const {
+    return k < k0 ? b0[(int64_t)n * ld + k] : b1[(int64_t)n * ld + (k - k0)];
+  }
+};
+// A(m, k) = [x0^T | x1^T](m, k) with a row of ones (segment 0) / zeros (segment 1) at m == n_m
+struct LdXtOnes2 {
+  const double *x0, *x1;
+  int ld, n_m, k0;
+  __device__ __forceinline__ double operator()(int m, int k) const {
+    if (k < k0) return m < n_m ? x0[(int64_t)k * ld + m] : 1.0;
+    return m < n_m ? x1[(int64_t)(k - k0) * ld + m] : 0.0;
+  }
+};
+
+struct MlpF64HvWs {
+  double *s1, *s1b, *s1bd, *gbuf, *gdbuf, *loss_part, *lossd_part, *w2_part, *w1_part;
+  int head_blocks, w2_chunks, w1_splits, w1d_splits;
+};
+template <class Alloc>
+void mlp_hv_layout(Alloc& a, MlpF64HvWs* w, int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o) {
+  const int head_blocks = (int)((n_s + kHeadWarps - 1) / kHeadWarps);
+  const int w2_chunks = (int)((n_s + kW2Chunk - 1) / kW2Chunk);
+  const int w1_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, (int)n_s);
+  const int w1d_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, 2 * (int)n_s);
+  const int maxs = w1_splits > w1d_splits ? w1_splits : w1d_splits;
+  auto p0 = a.template take<double>((size_t)(n_s * n_h));
+  auto p1 = a.template take<double>((size_t)(n_s * n_h));
+  auto p2 = a.template take<double>((size_t)(n_s * n_h));
+  auto p3 = a.template take<double>((size_t)(n_s * n_o));
+  auto p4 = a.template take<double>((size_t)(n_s * n_o));
+  auto p5 = a.template take<double>((size_t)head_blocks);
+  auto p6 = a.template take<double>((size_t)head_blocks);
+  auto p7 = a.template take<double>((size_t)w2_chunks * (size_t)(2 * n_h * n_o + 2 * n_o));
+  auto p8 = a.template take<double>(maxs > 1 ? (size_t)maxs * (size_t)((n_i + 1) * n_h) : 1);
+  if (w) {
+    w->s1 = (double*)p0; w->s1b = (double*)p1; w->s1bd = (double*)p2; w->gbuf = (double*)p3;
+    w->gdbuf = (double*)p4; w->loss_part = (double*)p5; w->lossd_part = (double*)p6;
+    w->w2_part = (double*)p7; w->w1_part = (double*)p8;
+    w->head_blocks = head_blocks; w->w2_chunks = w2_chunks;
+    w->w1_splits = w1_splits; w->w1d_splits = w1d_splits;
+  }
+}
+
+}  // namespace
+
+// ============================================================================
+// Float32 adjoint
+// ============================================================================
+namespace {
+struct MlpF32Ws {
+  float *s1b, *gbuf, *loss_part, *w2_part, *w1_part;
+  int head_blocks, w2_chunks, w1_splits;
+};
+template <class Alloc>
+void mlp_f32_layout(Alloc& a, MlpF32Ws* w, int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o) {
+  const int head_blocks = (int)((n_s + kHeadWarps - 1) / kHeadWarps);
+  const int w2_chunks = (int)((n_s + kW2Chunk - 1) / kW2Chunk);
+  const int w1_splits = splits_for<float, kF32RM, kF32RN, kF32BK>((int)n_i + 1, (int)n_h, (int)n_s);
+  if (w) {
+    w->head_blocks = head_blocks;
+    w->w2_chunks = w2_chunks;
+    w->w1_splits = w1_splits;
+  }
+  auto s1b = a.template take<float>((size_t)(n_s * n_h));
+  auto gb = a.template take<float>((size_t)(n_s * n_o));
+  auto lp = a.template take<float>((size_t)head_blocks);
+  auto w2p = a.template take<float>((size_t)w2_chunks * (size_t)(n_h * n_o + n_o));
+  auto w1p = a.template take<float>(w1_splits > 1 ? (size_t)w1_splits * (size_t)((n_i + 1) * n_h) : 1);
+  if (w) {
+    w->s1b = (float*)s1b; w->gbuf = (float*)gb; w->loss_part = (float*)lp;
+    w->w2_part = (float*)w2p; w->w1_part = (float*)w1p;
+  }
+}
+struct SizerAlloc {
+  Sizer z;
+  template <class T> void* take(size_t n) { z.take<T>(n); return nullptr; }
+};
+struct CarverAlloc {
+  Carver c;
+  explicit CarverAlloc(void* b) : c(b) {}
+  template <class T> T* take(size_t n) { return c.take<T>(n); }
+};
+}  // namespace
+
+}  // namespace stade
+
+using namespace stade;
+
+extern "C" size_t stade_mlp2_ce_b_f32_workspace(int64_t n_s, int64_t n_i, int64_t n_h,
+                                                int64_t n_o) {
+  if (n_s <= 0 || n_h <= 0 || n_o <= 0 || n_i < 0) return 256;
+  SizerAlloc a;
+  mlp_f32_layout(a, nullptr, n_s, n_i, n_h, n_o);
+  return a.z.bytes() + tc_mlp_workspace(n_s, n_i, n_h);
+}
+
+extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, const float* x,
+                                            float* xb, const float* y, float* yb, const float* w1,
+                                            float* w1b, const float* b1, float* b1b,
+                                            const float* w2, float* w2b, const float* b2,
+                                            float* b2b, float* h, float* hb, float* z, float* zb,
+                                            float* p, float* pb, int64_t n_s, int64_t n_i,
+                                            int64_t n_h, int64_t n_o, const stade_opts* opts) {
+  STADE_REQUIRE(n_s >= 0 && n_i >= 0 && n_h >= 0 && n_o >= 0, "mlp2_ce_b: negative size");
+  if (n_s == 0) return STADE_OK;
+  if (n_o == 0) {
+    // no classes: the logits and loss loops are empty; only the hidden layer runs
+    STADE_REQUIRE(n_o > 0, "mlp2_ce_b: n_o = 0 is not supported");
+  }
+  STADE_REQUIRE(n_o <= 32, "mlp2_ce_b: n_o = %lld > 32 classes", (long long)n_o);
+  STADE_REQUIRE(n_h > 0, "mlp2_ce_b: n_h = 0 is not supported");
+  STADE_REQUIRE(n_s <= (1 << 30) && n_i < (1 << 20) && n_h < (1 << 16) &&
+                    n_s * n_i < (int64_t(1) << 40),
+                "mlp2_ce_b: sizes out of range");
+  STADE_REQUIRE(loss && lossb && x && xb && y && yb && w1 && w1b && b1 && b1b && w2 && w2b && b2 &&
+                    b2b && h && hb && z && zb && p && pb,
+                "mlp2_ce_b: null array argument");
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(opts, stade_mlp2_ce_b_f32_workspace(n_s, n_i, n_h, n_o), &wsp);
+  if (st != STADE_OK) return st;
+  CarverAlloc ca(wsp);
+  MlpF32Ws w;
+  mlp_f32_layout(ca, &w, n_s, n_i, n_h, n_o);
+  void* tcws = ca.c.take<char>(tc_mlp_workspace(n_s, n_i, n_h));
+  const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
+  const bool use_tc = tc_mlp_supported(n_s, n_i, n_h);
+
+  // 1. h = tanh(x W1 + b1)
+  {
+    PhaseScope ph("fwd_gemm", s);
+    if (use_tc)
+      st = tc_forward_tanh(x, w1, b1, h, S, I, H, tcws, s);
+    else
+      st = gemm_simt<float, kF32RM, kF32RN, kF32BK, true, true>(
+          S, H, I, LdRow<float>{x, I}, LdB<float>{w1, H}, EpiTanh<float>{{}, b1, h, H}, nullptr,
+          1, s);
+  }
+  if (st != STADE_OK) return st;
+  // 2. per-sample head
+  {
+    PhaseScope ph("head", s);
+    const size_t head_smem = sizeof(float) * (size_t)(n_h * n_o);
+    STADE_REQUIRE(head_smem <= 200 * 1024, "mlp2_ce_b: n_h * n_o too large");
+    auto kern = O <= 16 ? mlp_head_b_kernel<float, 16> : mlp_head_b_kernel<float, 32>;
+    if (head_smem > 48 * 1024)
+      STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)head_smem));
+    kern<<<w.head_blocks, kHeadWarps * 32, head_smem, s>>>(lossb, y, yb, w2, b2, h, hb, z, zb, p,
+                                                           pb, w.gbuf, w.s1b, S, H, O, w.loss_part);
+    STADE_CHECK_LAUNCH();
+    st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
+  }
+  if (st != STADE_OK) return st;
+  // 3. W2b, b2b
+  {
+    PhaseScope ph("w2b", s);
+    auto kern = O <= 16 ? mlp_w2b_partial_kernel<float, 16> : mlp_w2b_partial_kernel<float, 32>;
+    kern<<<w.w2_chunks, 256, 0, s>>>(h, w.gbuf, S, H, O, kW2Chunk, w.w2_part);
+    STADE_CHECK_LAUNCH();
+    finish_two_kernel<float><<<ceil_div_u(n_h * n_o + n_o, 256), 256, 0, s>>>(
+        w.w2_part, w.w2_chunks, n_h * n_o, w2b, n_o, b2b);
+    STADE_CHECK_LAUNCH();
+  }
+  // 4. W1b = x^T s1b (+ b1b as the row of ones), 5. xb += s1b W1^T
+  {
+    PhaseScope ph("w1b_gemm", s);
+    if (use_tc)
+      st = tc_weight_grad(x, w.s1b, w1b, b1b, S, I, H, tcws, s);
+    else
+      st = gemm_simt<float, kF32RM, kF32RN, kF32BK, false, true>(
+          I + 1, H, S, LdXtOnes<float>{x, I, I}, LdB<float>{w.s1b, H},
+          EpiWeightBias<float>{{}, w1b, b1b, I, H}, w.w1_part, w.w1_splits, s);
+  }
+  if (st != STADE_OK) return st;
+  {
+    PhaseScope ph("xb_gemm", s);
+    if (use_tc)
+      st = tc_input_grad(w.s1b, w1, xb, S, I, H, tcws, s);
+    else
+      st = gemm_simt<float, kF32RM, kF32RN, kF32BK, true, false>(
+          S, I, H, LdRow<float>{w.s1b, H}, LdBT<float>{w1, H}, EpiAddTo<float>{{}, xb, I},
+          nullptr, 1, s);
+  }
+  return st;
+}
+
+// ============================================================================
+// Float64 HVP
+// ============================================================================
+extern "C" size_t stade_mlp2_ce_hv_f64_workspace(int64_t n_s, int64_t n_i, int64_t n_h,
+                                                 int64_t n_o) {
+  if (n_s <= 0 || n_h <= 0 || n_o <= 0 || n_i < 0) return 256;
+  SizerAlloc a;
+  mlp_hv_layout(a, nullptr, n_s, n_i, n_h, n_o);
+  return a.z.bytes();
+}
+
+extern "C" stade_status stade_mlp2_ce_hv_f64(
+    double* loss, const double* lossb, const double* x, double* xb, const double* y, double* yb,
+    const double* w1, double* w1b, const double* b1, double* b1b, const double* w2, double* w2b,
+    const double* b2, double* b2b, double* h, double* hb, double* z, double* zb, double* p,
+    double* pb, int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o, double* lossd,
+    const double* lossbd, const double* xd, double* xbd, const double* yd, double* ybd,
+    const double* w1d, double* w1bd, const double* b1d, double* b1bd, const double* w2d,
+    double* w2bd, const double* b2d, double* b2bd, double* hd, double* hbd, double* zd,
+    double* zbd, double* pd, double* pbd, const stade_opts* opts) {
+  STADE_REQUIRE(n_s >= 0 && n_i >= 0 && n_h >= 0 && n_o >= 0, "mlp2_ce_hv: negative size");
+  if (n_s == 0) return STADE_OK;
+  STADE_REQUIRE(n_o >= 1 && n_o <= 32, "mlp2_ce_hv: n_o = %lld outside 1..32", (long long)n_o);
+  STADE_REQUIRE(n_h > 0, "mlp2_ce_hv: n_h = 0 is not supported");
+  STADE_REQUIRE(n_s <= (1 << 29) && n_i < (1 << 20) && n_h < (1 << 16),
+                "mlp2_ce_hv: sizes out of range");
+  STADE_REQUIRE(loss && lossb && x && xb && y && yb && w1 && w1b && b1 && b1b && w2 && w2b && b2 &&
+                    b2b && h && hb && z && zb && p && pb && lossd && lossbd && xd && xbd && yd &&
+                    ybd && w1d && w1bd && b1d && b1bd && w2d && w2bd && b2d && b2bd && hd && hbd &&
+                    zd && zbd && pd && pbd,
+                "mlp2_ce_hv: null array argument");
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(opts, stade_mlp2_ce_hv_f64_workspace(n_s, n_i, n_h, n_o), &wsp);
+  if (st != STADE_OK) return st;
+  CarverAlloc ca(wsp);
+  MlpF64HvWs w;
+  mlp_hv_layout(ca, &w, n_s, n_i, n_h, n_o);
+  const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
+  constexpr int RM = kF64RM, RN = kF64RN, BK = kF64BK;
+
+  // forward: S1 = x W1; s1d = x W1d + xd W1, h, hd
+  {
+    PhaseScope ph("hv_fwd_gemms", s);
+    st = gemm_simt<double, RM, RN, BK, true, true>(S, H, I, LdRow<double>{x, I},
+                                                    LdB<double>{w1, H}, EpiStore{{}, w.s1, H},
+                                                    nullptr, 1, s);
+    if (st == STADE_OK)
+      st = gemm_simt<double, RM, RN, BK, true, true>(
+          S, H, 2 * I, LdRow2{x, xd, I, I}, LdB2{w1d, w1, H, I},
+          EpiTanhTangent{{}, w.s1, b1, b1d, h, hd, H}, nullptr, 1, s);
+  }
+  if (st != STADE_OK) return st;
+  // head
+  const size_t smem = 2 * sizeof(double) * (size_t)(n_h * n_o);
+  STADE_REQUIRE(smem <= 200 * 1024, "mlp2_ce_hv: n_h * n_o too large");
+  if (O <= 16) {
+    if (smem > 48 * 1024)
+      STADE_CUDA(cudaFuncSetAttribute(mlp_head_hv_kernel<16>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    mlp_head_hv_kernel<16><<<w.head_blocks, kHeadWarps * 32, smem, s>>>(
+        lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
+        pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part);
+  } else {
+    if (smem > 48 * 1024)
+      STADE_CUDA(cudaFuncSetAttribute(mlp_head_hv_kernel<32>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    mlp_head_hv_kernel<32><<<w.head_blocks, kHeadWarps * 32, smem, s>>>(
+        lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
+        pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part);
+  }
+  STADE_CHECK_LAUNCH();
+  st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
+  if (st != STADE_OK) return st;
+  st = launch_sum_to_scalar(w.lossd_part, w.head_blocks, lossd, true, s);
+  if (st != STADE_OK) return st;
+  // W2b, W2bd, b2b, b2bd
+  if (O <= 16)
+    mlp_w2b_hv_partial_kernel<16><<<w.w2_chunks, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O,
+                                                              kW2Chunk, w.w2_part);
+  else
+    mlp_w2b_hv_partial_kernel<32><<<w.w2_chunks, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O,
+                                                              kW2Chunk, w.w2_part);
+  STADE_CHECK_LAUNCH();
+  finish_four_kernel<<<ceil_div_u(2 * n_h * n_o + 2 * n_o, 256), 256, 0, s>>>(
+      w.w2_part, w.w2_chunks, n_h * n_o, O, w2b, w2bd, b2b, b2bd);
+  STADE_CHECK_LAUNCH();
+  // W1b (+ b1b); W1bd = x^T s1bd + xd^T s1b (+ b1bd)
+  st = gemm_simt<double, RM, RN, BK, false, true>(
+      I + 1, H, S, LdXtOnes<double>{x, I, I}, LdB<double>{w.s1b, H},
+      EpiWeightBias<double>{{}, w1b, b1b, I, H}, w.w1_part, w.w1_splits, s);
+  if (st != STADE_OK) return st;
+  st = gemm_simt<double, RM, RN, BK, false, true>(
+      I + 1, H, 2 * S, LdXtOnes2{x, xd, I, I, S}, LdB2{w.s1bd, w.s1b, H, S},
+      EpiWeightBias<double>{{}, w1bd, b1bd, I, H}, w.w1_part, w.w1d_splits, s);
+  if (st != STADE_OK) return st;
+  // xb += s1b W1^T; xbd += s1bd W1^T + s1b W1d^T
+  st = gemm_simt<double, RM, RN, BK, true, false>(S, I, H, LdRow<double>{w.s1b, H},
+                                                   LdBT<double>{w1, H}, EpiAddTo<double>{{}, xb, I},
+                                                   nullptr, 1, s);
+  if (st != STADE_OK) return st;
+  st = gemm_simt<double, RM, RN, BK, true, false>(
+      S, I, 2 * H, LdRow2{w.s1bd, w.s1b, H, H}, LdBT2{w1, w1d, H, H},
+      EpiAddTo<double>{{}, xbd, I}, nullptr, 1, s);
+  return st;
+}

@@ -1,0 +1,294 @@
+"""Data-parallel epilogue: role table, sample sharding and the generated
+epilogue functions, over NCCL through libstade_b200.
+
+Restates `ddpgen_roles` (src/STADE.jl:17404-17440): every float argument gets
+a class from two facts the caller states (`per_sample`, `reduced`) and two the
+kernel shows (which arrays it writes, which outputs are reductions), and
+every buffer of the generated layout gets a role:
+
+    class         input buffer     adjoint-valued buffer
+    :shared       :shared          :accum
+    :reduced      :reduced         :seed
+    :per_sample   :per_sample      :local
+    :scratch      :scratch         :local
+
+(a scalar float argument's adjoint is :returned). The epilogue zeroes :accum
+and :reduced once per step, :local before each sample, sums :accum (with the
+sample count) and :reduced across ranks, and checks :shared / :seed for
+agreement (src/STADE.jl:17595-17696). Here the sums are one NCCL collective
+per call over one bucket instead of one MPI.Allreduce! per buffer.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import STADE_F32, STADE_F64, check, lib, make_opts
+
+
+@dataclass(frozen=True)
+class KernelSig:
+    """What ddpgen_ reads from a parsed primal: argument order, kinds
+    (:array_float, :scalar_float, :array_int, :scalar_int), the arrays the body
+    writes, and the outputs every write of which adds to the array itself."""
+    name: str
+    args: tuple
+    kinds: dict
+    written: frozenset
+    reduced_outputs: frozenset
+
+
+def adjoint_layout(sig: KernelSig) -> list:
+    """agen_signature_args (src/STADE.jl:3455-3465): each float argument
+    followed by its adjoint."""
+    out = []
+    for a in sig.args:
+        out.append(a)
+        if sig.kinds[a] in ("array_float", "scalar_float"):
+            out.append(a + "b")
+    return out
+
+
+def hvp_layout(sig: KernelSig) -> list:
+    """ddpgen_hvp_signature_args (src/STADE.jl:17475-17484): the adjoint
+    layout, then (tangent, adjoint-of-tangent) per float argument."""
+    out = adjoint_layout(sig)
+    for a in sig.args:
+        if sig.kinds[a] in ("array_float", "scalar_float"):
+            out += [a + "d", a + "bd"]
+    return out
+
+
+def derive_roles(sig: KernelSig, per_sample, mode: str, reduced=()) -> dict:
+    """Role of every buffer of the mode's layout (ddpgen_roles)."""
+    per_sample, reduced = list(per_sample), list(reduced)
+    for kw, names in (("per_sample", per_sample), ("reduced", reduced)):
+        for p in names:
+            if p not in sig.args:
+                raise ValueError(f"{kw} names `{p}`, which is not an argument of {sig.name}")
+            if sig.kinds[p] != "array_float":
+                raise ValueError(f"{kw} names `{p}`, which is not a float array argument")
+        dups = sorted({p for p in names if names.count(p) > 1})
+        if dups:
+            raise ValueError(f"{kw} names `{'`, `'.join(dups)}` more than once")
+    both = [p for p in per_sample if p in reduced]
+    if both:
+        raise ValueError(f"`{'`, `'.join(both)}` named in both per_sample and reduced")
+    all_reduced = set(sig.reduced_outputs) | set(reduced)
+    roles = {}
+    for a in sig.args:
+        kind = sig.kinds[a]
+        if kind not in ("array_float", "scalar_float"):
+            continue
+        readonly = kind == "array_float" and a not in sig.written
+        if a in per_sample and a not in sig.written:
+            cls = "per_sample"
+        elif a in per_sample:
+            cls = "scratch"
+        elif a in all_reduced:
+            cls = "reduced"
+        elif readonly:
+            cls = "shared"
+        else:
+            cls = "scratch"
+        out_role = ("returned" if kind == "scalar_float" else
+                    "accum" if cls == "shared" else "seed" if cls == "reduced" else "local")
+        roles[a] = cls
+        if mode in ("tangent", "hvp"):
+            roles[a + "d"] = cls
+        if mode in ("adjoint", "hvp"):
+            roles[a + "b"] = out_role
+        if mode == "hvp":
+            roles[a + "bd"] = out_role
+    return roles
+
+
+def role_args(sig: KernelSig, roles: dict, mode: str, want: str) -> list:
+    """Buffers with one role, in layout order, arrays only (ddpgen_role_args)."""
+    layout = adjoint_layout(sig) if mode == "adjoint" else hvp_layout(sig)
+    scalars = set()
+    for a in sig.args:
+        if sig.kinds[a] == "scalar_float":
+            scalars |= {a, a + "b", a + "d", a + "bd"}
+    return [b for b in layout if roles.get(b) == want and b not in scalars]
+
+
+# The primal mlp2_ce (oracle/primals.jl): h, z, p and loss are written; every
+# write of loss adds to loss itself.
+MLP2_CE = KernelSig(
+    name="mlp2_ce",
+    args=("loss", "x", "y", "w1", "b1", "w2", "b2", "h", "z", "p", "n_s", "n_i", "n_h", "n_o"),
+    kinds={**{a: "array_float" for a in ("loss", "x", "y", "w1", "b1", "w2", "b2", "h", "z", "p")},
+           **{a: "scalar_int" for a in ("n_s", "n_i", "n_h", "n_o")}},
+    written=frozenset({"h", "z", "p", "loss"}),
+    reduced_outputs=frozenset({"loss"}),
+)
+
+
+def shard(n_samples: int, rank: int, nranks: int, mode: str = "block") -> range | list:
+    """Samples of one rank. "mod": sample s (1-based) on rank mod(s - 1, P),
+    as test/validate_ddp.jl:52-53; "block": contiguous blocks, which keeps
+    each rank's batch one strided array (the layout a batch-loop kernel
+    takes)."""
+    if mode == "mod":
+        return list(range(rank, n_samples, nranks))
+    lo = n_samples * rank // nranks
+    hi = n_samples * (rank + 1) // nranks
+    return range(lo, hi)
+
+
+# ---------------------------------------------------------------------------
+class NcclComm:
+    """One NCCL communicator per process / GPU (stade_comm_init). The 128-byte
+    id is made on rank 0 and broadcast with whatever the caller has: here a
+    torch.distributed group (any backend), as a Julia caller would use MPI."""
+
+    def __init__(self, rank: int, nranks: int, group=None, timeout_ms: int = 60000,
+                 unique_id: bytes | None = None):
+        if unique_id is None:
+            import torch.distributed as dist
+            buf = [None]
+            if rank == 0:
+                raw = C.create_string_buffer(128)
+                check(lib().stade_comm_unique_id(raw))
+                buf[0] = bytes(raw.raw)
+            dist.broadcast_object_list(buf, src=0, group=group)
+            unique_id = buf[0]
+        self.rank, self.size = rank, nranks
+        handle = C.c_void_p()
+        check(lib().stade_comm_init(unique_id, nranks, rank, timeout_ms, C.byref(handle)))
+        self.handle = handle
+
+    def close(self) -> None:
+        if self.handle:
+            lib().stade_comm_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _dtype_code(ts) -> int:
+    dt = ts[0].dtype
+    if any(t.dtype != dt for t in ts):
+        raise TypeError("all buffers of one epilogue call must share a dtype")
+    if dt == torch.float32:
+        return STADE_F32
+    if dt == torch.float64:
+        return STADE_F64
+    raise TypeError(f"unsupported dtype {dt}")
+
+
+def _bufs(ts):
+    for t in ts:
+        if not (t.is_cuda and t.is_contiguous()):
+            raise ValueError("epilogue buffers must be contiguous CUDA tensors")
+    n = len(ts)
+    ptrs = (C.c_void_p * n)(*[t.data_ptr() for t in ts])
+    counts = (C.c_int64 * n)(*[t.numel() for t in ts])
+    return ptrs, counts, n
+
+
+def _opts(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return make_opts(s.cuda_stream)
+
+
+def zero_(*bufs, stream=None) -> None:
+    """fill!(b, 0.0) for each buffer (ddpgen_fill_fn)."""
+    if not bufs:
+        return
+    ptrs, counts, n = _bufs(bufs)
+    o = _opts(stream)
+    check(lib().stade_ddp_zero(ptrs, counts, n, _dtype_code(bufs), C.byref(o)))
+
+
+def allreduce_sum_(comm: NcclComm, *bufs, n_local=None, stream=None):
+    """Sums the buffers across ranks in one collective. With n_local given,
+    also sums the sample counts and returns the global count (the value
+    allreduce_accum! returns; reading it waits for the stream). With
+    n_local=None nothing is counted and the call stays asynchronous."""
+    if not bufs:
+        return n_local
+    ptrs, counts, n = _bufs(bufs)
+    o = _opts(stream)
+    ng = C.c_int64(0)
+    check(lib().stade_ddp_allreduce_sum(comm.handle, ptrs, counts, n, _dtype_code(bufs),
+                                        0 if n_local is None else int(n_local),
+                                        None if n_local is None else C.byref(ng), C.byref(o)))
+    return None if n_local is None else ng.value
+
+
+def check_replicas(comm: NcclComm, *bufs, names=None, stream=None) -> None:
+    """Raises when a :shared / :seed buffer differs across ranks."""
+    if not bufs:
+        return
+    ptrs, counts, n = _bufs(bufs)
+    o = _opts(stream)
+    mask = C.c_uint64(0)
+    code = lib().stade_ddp_check_replicas(comm.handle, ptrs, counts, n, _dtype_code(bufs),
+                                          C.byref(mask), C.byref(o))
+    if code != 0 and mask.value:
+        names = names or [f"buffer {i}" for i in range(n)]
+        bad = [names[i] for i in range(n) if mask.value >> i & 1]
+        raise RuntimeError(f"`{'`, `'.join(bad)}` differ across ranks. A :shared or :seed buffer "
+                           "must hold identical values on every rank. The usual cause is a "
+                           "per-sample array left out of per_sample")
+    check(code)
+
+
+# ---- generated names of the mlp2_ce epilogue (adjoint mode) ------------------
+_ROLES_B = derive_roles(MLP2_CE, ["x", "y"], "adjoint")
+
+
+def mlp2_ce_b_reset_accum_(w1b, b1b, w2b, b2b, stream=None):
+    zero_(w1b, b1b, w2b, b2b, stream=stream)
+
+
+def mlp2_ce_b_reset_reduced_(loss, stream=None):
+    zero_(loss, stream=stream)
+
+
+def mlp2_ce_b_reset_local_(xb, yb, hb, zb, pb, stream=None):
+    zero_(xb, yb, hb, zb, pb, stream=stream)
+
+
+def mlp2_ce_b_allreduce_accum_(w1b, b1b, w2b, b2b, n_local, comm, stream=None) -> int:
+    return allreduce_sum_(comm, w1b, b1b, w2b, b2b, n_local=n_local, stream=stream)
+
+
+def mlp2_ce_b_allreduce_reduced_(loss, comm, stream=None) -> None:
+    allreduce_sum_(comm, loss, stream=stream)
+
+
+def mlp2_ce_b_check_replicas(w1, b1, w2, b2, lossb, comm, stream=None) -> None:
+    check_replicas(comm, w1, b1, w2, b2, lossb, names=["w1", "b1", "w2", "b2", "lossb"],
+                   stream=stream)
+
+
+# ---- generated names of the mlp2_ce epilogue (hvp mode) ----------------------
+def mlp2_ce_hv_reset_accum_(w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd, stream=None):
+    zero_(w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd, stream=stream)
+
+
+def mlp2_ce_hv_reset_reduced_(loss, lossd, stream=None):
+    zero_(loss, lossd, stream=stream)
+
+
+def mlp2_ce_hv_reset_local_(xb, yb, hb, zb, pb, xbd, ybd, hbd, zbd, pbd, stream=None):
+    zero_(xb, yb, hb, zb, pb, xbd, ybd, hbd, zbd, pbd, stream=stream)
+
+
+def mlp2_ce_hv_allreduce_accum_(w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd, n_local, comm,
+                                stream=None) -> int:
+    return allreduce_sum_(comm, w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd, n_local=n_local,
+                          stream=stream)
+
+
+def mlp2_ce_hv_allreduce_reduced_(loss, lossd, comm, stream=None) -> None:
+    allreduce_sum_(comm, loss, lossd, stream=stream)

@@ -1,0 +1,119 @@
+"""GPU parity: libstade_b200 (through its C ABI) against the CPU oracle on the
+same seeded inputs, at sizes the oracle finishes in seconds, plus edge cases
+(odd sizes, partial tiles, zero-trip loops, non-zero seeds in every adjoint).
+
+Tolerances (normwise relative error max|gpu - ref| / max|ref| per array,
+the metric `rel_err`): Float64 1e-12, Float32 1e-5, as the north star
+states; integer-valued and tape data bit-exact. Results that the kernels
+compute in the generated statement order with separate roundings are
+checked bit for bit.
+"""
+import numpy as np
+import pytest
+
+import cases
+from refmath import rel_err
+
+pytestmark = pytest.mark.gpu
+
+F64_TOL = 1e-12
+F32_TOL = 1e-5
+
+
+def _run_both(make, oracle, gpu):
+    st, ints = make()
+    ref = cases.copy_state(st)
+    out = cases.copy_state(st)
+    r1 = oracle(ref, ints)
+    r2 = gpu(out, ints)
+    return ref, out, ints, r1, r2
+
+
+@pytest.mark.parametrize("sizes,seeded", [((1024, 64, 32), False), ((37, 9, 5), True),
+                                          ((16, 1, 1), True), ((3, 70, 40), True)])
+def test_affine_ls(sizes, seeded):
+    ref, out, ints, _, _ = _run_both(lambda: cases.affine_state(*sizes, seeded=seeded),
+                                     cases.oracle_affine, cases.gpu_affine)
+    for k in ("y", "tb", "xb", "yb"):
+        assert np.array_equal(out[k], ref[k]), k          # same op order, same roundings
+    for k in ("wb", "bb", "loss"):
+        assert rel_err(out[k], ref[k]) <= F64_TOL, k
+
+
+@pytest.mark.parametrize("sizes,seeded", [((256, 784, 512, 10), False),
+                                          ((77, 33, 45, 7), True),
+                                          ((40, 20, 30, 1), True),
+                                          ((64, 16, 64, 32), True),
+                                          ((300, 129, 200, 10), False)])
+def test_mlp2_ce_b(sizes, seeded):
+    ref, out, ints, _, _ = _run_both(lambda: cases.mlp_state(*sizes, seeded=seeded),
+                                     cases.oracle_mlp, cases.gpu_mlp)
+    for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
+        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+    for k in ("hb", "zb", "pb"):
+        assert np.all(out[k] == 0.0), k
+
+
+def test_mlp2_ce_b_deterministic():
+    st, ints = cases.mlp_state(500, 100, 64, 10, seeded=True)
+    a, b = cases.copy_state(st), cases.copy_state(st)
+    cases.gpu_mlp(a, ints)
+    cases.gpu_mlp(b, ints)
+    for k in a:
+        assert np.array_equal(a[k], b[k]), k
+
+
+@pytest.mark.parametrize("n,n_step,seeded", [(64, 4, False), (34, 3, True), (6, 2, True),
+                                             (258, 5, False), (4, 1, True), (10, 0, True)])
+def test_heat2d_b(n, n_step, seeded):
+    ref, out, ints, ab_ref, ab_gpu = _run_both(lambda: cases.heat_state(n, n_step, seeded=seeded),
+                                               cases.oracle_heat, cases.gpu_heat)
+    for k in ("u", "un", "u_stack"):
+        assert np.array_equal(out[k], ref[k]), k          # forward is bit-exact
+    assert np.all(out["unb"] == ref["unb"])
+    assert rel_err(out["ub"], ref["ub"]) <= F64_TOL
+    assert rel_err(out["loss"], ref["loss"]) <= F64_TOL
+    assert abs(ab_gpu - ab_ref) <= F64_TOL * max(1.0, abs(ab_ref))
+
+
+def test_heat2d_b_interior_bit_exact():
+    """Interior cells add their five contributions in the generated order."""
+    n = 32
+    ref, out, ints, _, _ = _run_both(lambda: cases.heat_state(n, 1), cases.oracle_heat,
+                                     cases.gpu_heat)
+    a = out["ub"].reshape(n, n)[1:-1, 1:-1]
+    b = ref["ub"].reshape(n, n)[1:-1, 1:-1]
+    assert np.array_equal(a, b)
+
+
+def test_heat2d_b_homogeneity_medium():
+    """Size-independent property at 2048^2 x 16: <ub, u0> = 2 loss."""
+    st, ints = cases.heat_state(2048, 16)
+    u0 = st["u"].copy()
+    cases.gpu_heat(st, ints)
+    assert abs(np.dot(st["ub"], u0) - 2 * st["loss"][0]) <= 1e-11 * st["loss"][0]
+
+
+@pytest.mark.parametrize("sizes,seeded", [((2, 3, 30, 4, 5), True), ((4, 16, 200, 32, 9), False),
+                                          ((1, 1, 9, 1, 9), True), ((3, 64, 140, 128, 9), False)])
+def test_conv1d_relu_mse_b(sizes, seeded):
+    ref, out, ints, _, _ = _run_both(lambda: cases.conv_state(*sizes, seeded=seeded),
+                                     cases.oracle_conv, cases.gpu_conv)
+    for k in ("z", "r", "tb", "wb", "xb", "loss"):
+        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+    for k in ("zb", "rb"):
+        assert np.all(out[k] == 0.0), k
+
+
+@pytest.mark.parametrize("sizes,seeded,xd", [((64, 30, 40, 10), False, False),
+                                             ((33, 17, 19, 3), True, True),
+                                             ((130, 70, 129, 10), True, False)])
+def test_mlp2_ce_hv(sizes, seeded, xd):
+    ref, out, ints, _, _ = _run_both(lambda: cases.mlp_hv_state(*sizes, seeded=seeded,
+                                                                xd_nonzero=xd),
+                                     cases.oracle_mlp_hv, cases.gpu_mlp_hv)
+    for k in ("h", "hd", "z", "zd", "p", "pd", "loss", "lossd", "yb", "ybd", "xb", "xbd", "w1b",
+              "w1bd", "b1b", "b1bd", "w2b", "w2bd", "b2b", "b2bd"):
+        assert rel_err(out[k], ref[k]) <= F64_TOL, (k, rel_err(out[k], ref[k]))
+    for k in ("hb", "hbd", "zb", "zbd", "pb", "pbd"):
+        assert np.all(out[k] == 0.0), k

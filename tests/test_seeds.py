@@ -1,0 +1,44 @@
+"""The input generator: FNV-1a seeds pinned by the reference's own golden
+values (test/validate_seed_stable.jl:37-38), Box-Muller normals with the
+statistics the reference checks (validate_seed_stable.jl:60-62), and
+chunked generation that does not depend on the host thread count."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+import stadeb200
+from stadeb200 import synth
+
+
+def test_fnv1a_goldens_of_the_reference():
+    L = stadeb200.lib()
+    assert L.stade_fnv1a64(b"abc") == 0xE71FA2190541574B
+    assert L.stade_fnv1a64(b"unet") == 0x64C1DFE4857EB8BB
+
+
+def test_normals_mean_and_variance():
+    x = synth.normal(10 ** 6, 11, np.float64)
+    assert abs(x.mean()) < 5e-3 and abs((x * x).mean() - 1) < 5e-3
+
+
+def test_uniform_range_and_onehot():
+    u = synth.uniform(100000, 3, np.float32, -0.5, 0.25)
+    assert u.min() >= -0.5 and u.max() < 0.25
+    y = synth.onehot(1000, 10, 9, np.float64).reshape(1000, 10)
+    assert np.all(y.sum(1) == 1.0)
+    counts = y.sum(0)
+    assert counts.min() > 60
+
+
+def test_generation_independent_of_thread_count():
+    code = ("import sys; sys.path.insert(0, %r); import numpy as np; from stadeb200 import synth;"
+            "a = synth.normal(3 * 2**20 + 5, 77, np.float32); print(float(a.sum()), a[123456])")
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "stade.jl_b200")
+    outs = []
+    for nt in ("1", "4"):
+        env = dict(os.environ, OMP_NUM_THREADS=nt)
+        outs.append(subprocess.run([sys.executable, "-c", code % root], env=env, check=True,
+                                   capture_output=True, text=True).stdout)
+    assert outs[0] == outs[1]
