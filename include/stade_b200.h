@@ -75,6 +75,10 @@ void        stade_reset_kernel_launches(void);
  * with CUDA events on their stream; stade_profile_read waits for them and
  * sums device milliseconds per phase name (names: max entries of name_len
  * bytes each). Returns the number of distinct phases recorded. */
+/* Sticky device-side error word of the kernels with bounded waits (the
+ * tensor-core pipeline): 0 = none; nonzero = a wait ran out and the results of
+ * that call are invalid. Reading it waits for the device and clears it. */
+int         stade_device_error(void);
 void        stade_profile_enable(int on);
 int         stade_profile_read(char* names, int name_len, double* ms, int* counts, int max);
 

@@ -164,3 +164,4 @@ extern "C" stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }
+
