@@ -99,6 +99,31 @@ stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
                                    int64_t n_s, int64_t n_o, int64_t n_i,
                                    const stade_opts* opts);
 
+/* Allocation-free variant of stade_affine_ls_b_f64. It has no counterpart in
+ * the reference. For callers that cannot allocate device memory where they
+ * run the sweep (all device memory handed to their own pool, a fixed memory
+ * plan, a thread that must not block on cudaMalloc) and cannot size and pass
+ * a workspace: the per-block partial sums live in a fixed 2 MiB array in the
+ * library's own device memory, held by every GPU that loads the library until
+ * the process exits. The call makes no cudaMalloc, cudaFree or other
+ * allocating call; opts->workspace is ignored. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make that first call before any stream capture. Sizes whose
+ * partial sums exceed the array (stade_affine_ls_b_f64_noalloc_max_scratch()
+ * bytes; the full 1024 x 64 x 32 configuration needs 1.03 MiB) return
+ * STADE_EINVAL. All calls share the one array: calls that overlap on the GPU
+ * (different streams, no ordering between them) race on it. Results equal
+ * those of stade_affine_ls_b_f64. */
+size_t stade_affine_ls_b_f64_noalloc_max_scratch(void);
+stade_status stade_affine_ls_b_f64_noalloc(double* loss, const double* lossb,
+                                           const double* w, double* wb,
+                                           const double* b, double* bb,
+                                           const double* x, double* xb,
+                                           const double* t, double* tb,
+                                           double* y, double* yb,
+                                           int64_t n_s, int64_t n_o, int64_t n_i,
+                                           const stade_opts* opts);
+
 /* ---------------------------------------------------------------------------
  * C2  mlp2_ce: h = tanh(x W1 + b1), z = h W2 + b2, softmax cross-entropy
  * against y, one sample per row. Float32 (STADE's precision conversion,

@@ -15,6 +15,8 @@
 //
 // y, tb and xb follow the oracle's statement order with separate multiply and
 // add roundings (no FMA contraction), so they match it bit for bit.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace stade {
@@ -165,3 +167,90 @@ extern "C" stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
   return STADE_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of stade_affine_ls_b_f64.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// sweep: an application that has handed all device memory to its own pool, a
+// real-time loop with a fixed memory plan, or a host thread that must not
+// block (cudaMalloc may synchronize the device). They also may not be able to
+// size and pass a workspace. This entry point takes its scratch (the per-block
+// partial sums) from a fixed array that lives in the library's own device
+// memory instead, so it calls no cudaMalloc, cudaFree or allocating library
+// routine. The array is created when the library is loaded on a device and
+// is held until the process exits.
+namespace stade {
+namespace {
+
+// 2 MiB: enough for the full configuration (1024 x 64 x 32 needs 1.03 MiB).
+constexpr size_t kNoAllocScratchDoubles = (size_t(2) << 20) / sizeof(double);
+static __device__ __align__(256) double g_affine_noalloc_scratch[kNoAllocScratchDoubles];
+
+constexpr int kMaxDevices = 64;
+double* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mutex;
+
+// Device address of the scratch array on the current device. The name of a
+// __device__ array in host code is only a host-side stand-in, never a device
+// address, so it is looked up once per device with that device current.
+stade_status noalloc_scratch(double** out) {
+  int dev = 0;
+  STADE_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(STADE_ENOTSUP, "device ordinal %d too large", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_affine_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress", __FILE__, __LINE__);
+    g_noalloc_ptr[dev] = static_cast<double*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return STADE_OK;
+}
+
+}  // namespace
+}  // namespace stade
+
+extern "C" size_t stade_affine_ls_b_f64_noalloc_max_scratch(void) {
+  return stade::kNoAllocScratchDoubles * sizeof(double);
+}
+
+extern "C" stade_status stade_affine_ls_b_f64_noalloc(double* loss, const double* lossb,
+                                                      const double* w, double* wb, const double* b,
+                                                      double* bb, const double* x, double* xb,
+                                                      const double* t, double* tb, double* y,
+                                                      double* yb, int64_t n_s, int64_t n_o,
+                                                      int64_t n_i, const stade_opts* opts) {
+  STADE_REQUIRE(n_s >= 0 && n_o >= 0 && n_i >= 0, "affine_ls_b_noalloc: negative size");
+  if (n_s == 0 || n_o == 0) return STADE_OK;
+  STADE_REQUIRE(loss && lossb && w && wb && b && bb && x && xb && t && tb && y && yb,
+                "affine_ls_b_noalloc: null array argument");
+  const Plan p = plan(n_s, n_o, n_i);
+  STADE_REQUIRE(p.smem <= 200 * 1024, "affine_ls_b_noalloc: n_o * n_i = %lld too large for one block",
+                (long long)(n_o * n_i));
+  STADE_REQUIRE(n_s < (int64_t(1) << 31) / 2 && n_o * n_i < (int64_t(1) << 30),
+                "affine_ls_b_noalloc: size overflow");
+  const size_t need = (size_t)p.nblk * (size_t)(n_o * n_i + n_o + 1);
+  if (need > kNoAllocScratchDoubles)
+    return fail(STADE_EINVAL,
+                "affine_ls_b_noalloc: %zu bytes of scratch needed, the fixed array holds %zu "
+                "(n_s = %lld, n_o = %lld, n_i = %lld); use stade_affine_ls_b_f64",
+                need * sizeof(double), kNoAllocScratchDoubles * sizeof(double), (long long)n_s,
+                (long long)n_o, (long long)n_i);
+  double* part = nullptr;
+  stade_status st = noalloc_scratch(&part);
+  if (st != STADE_OK) return st;
+  cudaStream_t s = stream_of(opts);
+  if (p.smem > 48 * 1024)
+    STADE_CUDA(cudaFuncSetAttribute(affine_ls_chunk_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+  // every block writes all of its partial slots, so nothing needs clearing
+  affine_ls_chunk_kernel<<<p.nblk, kThreads, p.smem, s>>>(lossb, w, b, x, xb, t, tb, y, yb, n_s,
+                                                          (int)n_o, (int)n_i, p.chunk, part);
+  STADE_CHECK_LAUNCH();
+  const int len = (int)(n_o * n_i + n_o + 1);
+  affine_ls_finish_kernel<<<ceil_div_u(len, 256), 256, 0, s>>>(part, p.nblk, (int)n_o, (int)n_i,
+                                                                wb, bb, loss);
+  STADE_CHECK_LAUNCH();
+  return STADE_OK;
+}

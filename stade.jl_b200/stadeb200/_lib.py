@@ -58,6 +58,8 @@ SIGNATURES = {
                                      C.c_int]),
     "stade_affine_ls_b_f64_workspace": (C.c_size_t, [I64, I64, I64]),
     "stade_affine_ls_b_f64": (ST, [P] * 12 + [I64] * 3 + [OPTS]),
+    "stade_affine_ls_b_f64_noalloc_max_scratch": (C.c_size_t, []),
+    "stade_affine_ls_b_f64_noalloc": (ST, [P] * 12 + [I64] * 3 + [OPTS]),
     "stade_mlp2_ce_b_f32_workspace": (C.c_size_t, [I64] * 4),
     "stade_mlp2_ce_b_f32": (ST, [P] * 20 + [I64] * 4 + [OPTS]),
     "stade_initstacks_heat2d_b": (I64, [I64, I64]),
