@@ -337,6 +337,8 @@ tc_gemm_kernel(int M, int N, int K, int k_slice, LA la, LB lb, EPI epi) {
     // ---- epilogue: TMEM -> registers -> global --------------------------------
     if (ok) ok = mbar_wait(accb, 0);
     tc_fence_after();
+    // tcgen05.ld is warp-collective: the whole warp takes the same branch
+    ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       const int quad = warp & 3, half = warp >> 2;
       const int m = m0 + quad * 32 + lane;
@@ -430,10 +432,10 @@ int w1b_splits(int S, int I, int H) {
 }  // namespace tc
 
 bool tc_mlp_supported(int64_t n_s, int64_t n_i, int64_t n_h) {
-  // STADE_MLP_GEMM selects the contraction path: "tc" (tcgen05 3xTF32) or
-  // "simt" (CUDA-core FMA); unset = simt until the tensor-core path is the default
+  // STADE_MLP_GEMM selects the contraction path: "tc" (tcgen05 3xTF32, the
+  // default) or "simt" (CUDA-core FMA, kept as a cross-check)
   const char* sel = std::getenv("STADE_MLP_GEMM");
-  if (!sel || std::strcmp(sel, "tc") != 0) return false;
+  if (sel && std::strcmp(sel, "simt") == 0) return false;
   return n_s >= 1 && n_i >= 1 && n_h >= 1 && n_i % 4 == 0 && n_h % 4 == 0 &&
          n_s < (int64_t(1) << 30) && n_i < (1 << 20) && n_h < (1 << 20);
 }

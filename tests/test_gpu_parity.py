@@ -54,6 +54,16 @@ def test_mlp2_ce_b(sizes, seeded):
         assert np.all(out[k] == 0.0), k
 
 
+@pytest.mark.parametrize("sizes", [(256, 784, 512, 10), (300, 132, 200, 10)])
+def test_mlp2_ce_b_simt_path(sizes, monkeypatch):
+    """The CUDA-core contraction path (STADE_MLP_GEMM=simt) stays correct."""
+    monkeypatch.setenv("STADE_MLP_GEMM", "simt")
+    ref, out, ints, _, _ = _run_both(lambda: cases.mlp_state(*sizes, seeded=True),
+                                     cases.oracle_mlp, cases.gpu_mlp)
+    for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
+        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+
+
 def test_mlp2_ce_b_deterministic():
     st, ints = cases.mlp_state(500, 100, 64, 10, seeded=True)
     a, b = cases.copy_state(st), cases.copy_state(st)
@@ -116,4 +126,22 @@ def test_mlp2_ce_hv(sizes, seeded, xd):
               "w1bd", "b1b", "b1bd", "w2b", "w2bd", "b2b", "b2bd"):
         assert rel_err(out[k], ref[k]) <= F64_TOL, (k, rel_err(out[k], ref[k]))
     for k in ("hb", "hbd", "zb", "zbd", "pb", "pbd"):
+        assert np.all(out[k] == 0.0), k
+
+
+@pytest.mark.parametrize("sizes,seeded", [((256, 784, 512, 10), False),
+                                          ((300, 132, 200, 10), True),
+                                          ((1000, 784, 512, 10), True),
+                                          ((129, 4, 8, 3), True)])
+def test_mlp2_ce_b_tensor_core_path(sizes, seeded, monkeypatch):
+    """The tcgen05 3xTF32 contractions (M, N and K tails included) against the
+    oracle, and no bounded wait ran out."""
+    from stadeb200 import _lib
+    monkeypatch.setenv("STADE_MLP_GEMM", "tc")
+    ref, out, ints, _, _ = _run_both(lambda: cases.mlp_state(*sizes, seeded=seeded),
+                                     cases.oracle_mlp, cases.gpu_mlp)
+    assert _lib.lib().stade_device_error() == 0
+    for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
+        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+    for k in ("hb", "zb", "pb"):
         assert np.all(out[k] == 0.0), k
