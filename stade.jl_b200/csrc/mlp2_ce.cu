@@ -18,6 +18,9 @@
 //   5. xb += s1b W1^T (GEMM).
 // The generated CUDA.jl port does 2-4 with atomics on every weight
 // (cgen_device_assign, src/STADE.jl:11941); here nothing is atomic.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "gemm_simt.cuh"
 #include "tc_gemm.cuh"
@@ -197,6 +200,192 @@ mlp_head_b_kernel(const T* __restrict__ lossb, const T* __restrict__ y, T* __res
   }
 }
 
+// Per-sample softmax cross-entropy, forward and reverse, one thread per
+// sample (the tensor-core path): the logits come from the partial sums the
+// forward GEMM's epilogue wrote (zpart[chunk][s][c], summed in chunk order).
+// Statement order as mlp_head_b_kernel.
+template <class T, int NO>
+__global__ void __launch_bounds__(256)
+mlp_head_small_kernel(const T* __restrict__ zpart, int nchunks, const T* __restrict__ lossb,
+                      const T* __restrict__ y, T* __restrict__ yb, const T* __restrict__ b2,
+                      T* __restrict__ z, T* __restrict__ zb, T* __restrict__ p,
+                      T* __restrict__ pb, T* __restrict__ gbuf, int n_s, int n_o,
+                      T* __restrict__ loss_part) {
+  __shared__ T red[8];
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  const T lb = lossb[0];
+  T loss_acc = T(0);
+  if (s < n_s) {
+    const int64_t row = (int64_t)s * n_o;
+    T zv[NO], yv[NO], pv[NO], g[NO], mprev[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        T acc = T(0);
+        for (int ch = 0; ch < nchunks; ++ch) acc += zpart[((int64_t)ch * n_s + s) * n_o + c];
+        zv[c] = acc + b2[c];
+        yv[c] = y[row + c];
+      }
+    }
+    T m = zv[0];
+#pragma unroll
+    for (int c = 1; c < NO; ++c)
+      if (c < n_o) { mprev[c] = m; m = jmax(m, zv[c]); }
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) pv[c] = dexp(radd(zv[c], -m));
+    T rs = T(0);
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) rs = radd(rs, pv[c]);
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) loss_acc = radd(loss_acc, -rmul(yv[c], dlog(pv[c] / rs)));
+    T rsb = T(0);
+    T pbv[NO];
+#pragma unroll
+    for (int c = NO - 1; c >= 0; --c) {
+      if (c < n_o) {
+        const T q = pv[c] / rs;
+        yb[row + c] = radd(yb[row + c], rmul(-(dlog(q)), lb));
+        const T qb = rmul(T(1) / q, rmul(-(yv[c]), lb));
+        pbv[c] = radd(pb[row + c], rmul(T(1) / rs, qb));
+        rsb = radd(rsb, rmul(-(pv[c] / rmul(rs, rs)), qb));
+      }
+    }
+    T mb = T(0);
+#pragma unroll
+    for (int c = NO - 1; c >= 0; --c) {
+      if (c < n_o) {
+        const T oldb = radd(pbv[c], rsb);
+        const T cse = rmul(pv[c], oldb);
+        g[c] = radd(zb[row + c], cse);
+        mb = radd(mb, -cse);
+      }
+    }
+#pragma unroll
+    for (int c = NO - 1; c >= 1; --c) {
+      if (c < n_o) {
+        const T oldb = mb;
+        mb = rmul(T(0.5) * (T(1) + dsign(radd(mprev[c], -zv[c]))), oldb);
+        g[c] = radd(g[c], rmul(T(0.5) * (T(1) + dsign(radd(zv[c], -mprev[c]))), oldb));
+      }
+    }
+    g[0] = radd(g[0], mb);
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        z[row + c] = zv[c];
+        p[row + c] = pv[c];
+        zb[row + c] = T(0);
+        pb[row + c] = T(0);
+        gbuf[row + c] = g[c];
+      }
+    }
+  }
+  loss_acc = block_sum(loss_acc, red);
+  if (threadIdx.x == 0) loss_part[blockIdx.x] = loss_acc;
+}
+
+// One pass over h and hb (tensor-core path): s1b = (1 - h^2) (hb + sum_c
+// w2[k, c] g[s, c]) with c descending (the generated order), hb consumed to
+// zero, and the W2b / b2b partials of the chunk (sum_s h[s,k] g[s,c],
+// sum_s g[s,c]). Block (x = chunk of samples, y = 512 hidden units), two
+// adjacent units per thread. Partial layout as mlp_w2b_partial_kernel.
+// PLANES: write s1b as TF32 hi / lo planes (s1b = hi plane, s1b_lo = lo
+// plane) and add the chunk's b1b partial (sum_s s1b[s,k]) after the b2b
+// entries of the partial record.
+template <int NO, bool PLANES>
+__global__ void __launch_bounds__(256)
+mlp_s1b_w2b_kernel(const float* __restrict__ h, float* __restrict__ hb,
+                   const float* __restrict__ gbuf, const float* __restrict__ w2,
+                   float* __restrict__ s1b, float* __restrict__ s1b_lo, int n_s, int n_h, int n_o,
+                   int chunk, float* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  float* gs = reinterpret_cast<float*>(smraw);  // chunk x n_o
+  const int s0 = blockIdx.x * chunk;
+  const int s1 = min(n_s, s0 + chunk);
+  const int ns = s1 - s0;
+  for (int e = threadIdx.x; e < ns * n_o; e += blockDim.x) gs[e] = gbuf[(int64_t)s0 * n_o + e];
+  __syncthreads();
+  float* my = part + (int64_t)blockIdx.x * (n_h * n_o + n_o + (PLANES ? n_h : 0));
+  const int k = blockIdx.y * 512 + 2 * threadIdx.x;
+  if (k < n_h) {
+    float wr0[NO], wr1[NO], a0[NO], a1[NO];
+    float2 bsum = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      wr0[c] = c < n_o ? w2[(int64_t)k * n_o + c] : 0.f;
+      wr1[c] = c < n_o ? w2[(int64_t)(k + 1) * n_o + c] : 0.f;
+      a0[c] = 0.f;
+      a1[c] = 0.f;
+    }
+    // four samples per iteration: eight independent 8-byte loads in flight
+    auto one = [&](int i, float2 hv, float2 acc) {
+      const int64_t off = (int64_t)(s0 + i) * n_h + k;
+      const float* g = gs + i * n_o;
+#pragma unroll
+      for (int c = NO - 1; c >= 0; --c) {
+        if (c < n_o) {
+          const float gc = g[c];
+          acc.x = __fadd_rn(acc.x, __fmul_rn(wr0[c], gc));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(wr1[c], gc));
+          a0[c] = fmaf(hv.x, gc, a0[c]);
+          a1[c] = fmaf(hv.y, gc, a1[c]);
+        }
+      }
+      float2 o;
+      o.x = __fmul_rn(__fadd_rn(1.f, -__fmul_rn(hv.x, hv.x)), acc.x);
+      o.y = __fmul_rn(__fadd_rn(1.f, -__fmul_rn(hv.y, hv.y)), acc.y);
+      if constexpr (PLANES) {
+        bsum.x += o.x;
+        bsum.y += o.y;
+        float2 hi;
+        hi.x = __uint_as_float(__float_as_uint(o.x) & 0xFFFFE000u);
+        hi.y = __uint_as_float(__float_as_uint(o.y) & 0xFFFFE000u);
+        *reinterpret_cast<float2*>(s1b + off) = hi;
+        *reinterpret_cast<float2*>(s1b_lo + off) = make_float2(o.x - hi.x, o.y - hi.y);
+      } else {
+        *reinterpret_cast<float2*>(s1b + off) = o;
+      }
+      *reinterpret_cast<float2*>(hb + off) = make_float2(0.f, 0.f);
+    };
+    int i = 0;
+    for (; i + 4 <= ns; i += 4) {
+      float2 hv[4], hbv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t off = (int64_t)(s0 + i + u) * n_h + k;
+        hv[u] = *reinterpret_cast<const float2*>(h + off);
+        hbv[u] = *reinterpret_cast<const float2*>(hb + off);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) one(i + u, hv[u], hbv[u]);
+    }
+    for (; i < ns; ++i) {
+      const int64_t off = (int64_t)(s0 + i) * n_h + k;
+      one(i, *reinterpret_cast<const float2*>(h + off), *reinterpret_cast<const float2*>(hb + off));
+    }
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        my[(int64_t)k * n_o + c] = a0[c];
+        my[(int64_t)(k + 1) * n_o + c] = a1[c];
+      }
+    }
+    if constexpr (PLANES) {
+      my[(int64_t)n_h * n_o + n_o + k] = bsum.x;
+      my[(int64_t)n_h * n_o + n_o + k + 1] = bsum.y;
+    }
+  }
+  if (blockIdx.y == 0 && threadIdx.x < n_o) {
+    const int c = threadIdx.x;
+    float acc = 0.f;
+    for (int i = 0; i < ns; ++i) acc += gs[i * n_o + c];
+    my[n_h * n_o + c] = acc;
+  }
+}
+
 // W2b[k, c] partial = sum over the chunk's samples of h[s,k] g[s,c]; b2b[c]
 // partial = sum g[s,c]. One thread per k; partial layout [chunk][n_h*n_o + n_o].
 template <class T, int NO>
@@ -240,6 +429,21 @@ __global__ void finish_two_kernel(const T* __restrict__ part, int count, int64_t
   for (int p = 0; p < count; ++p) acc += part[(int64_t)p * len + e];
   if (e < len1) dst1[e] += acc;
   else dst2[e - len1] += acc;
+}
+
+// Sums partial records [chunk][len1 + len2 + len3] in chunk order into three arrays.
+__global__ void finish_three_kernel(const float* __restrict__ part, int count, int64_t len1,
+                                    float* __restrict__ dst1, int64_t len2,
+                                    float* __restrict__ dst2, int64_t len3,
+                                    float* __restrict__ dst3) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t len = len1 + len2 + len3;
+  if (e >= len) return;
+  float acc = 0.f;
+  for (int p = 0; p < count; ++p) acc += part[(int64_t)p * len + e];
+  if (e < len1) dst1[e] += acc;
+  else if (e < len1 + len2) dst2[e - len1] += acc;
+  else dst3[e - len1 - len2] += acc;
 }
 
 // ---- epilogues ---------------------------------------------------------------
@@ -668,10 +872,24 @@ void mlp_hv_layout(Alloc& a, MlpF64HvWs* w, int64_t n_s, int64_t n_i, int64_t n_
 // Float32 adjoint
 // ============================================================================
 namespace {
+constexpr int kW2ChunkTc = 128;  // samples per W2b partial on the tensor-core path
+
 struct MlpF32Ws {
-  float *s1b, *gbuf, *loss_part, *w2_part, *w1_part;
+  float *s1b, *gbuf, *loss_part, *w2_part, *w1_part, *zpart;
+  float *x_hi, *x_lo, *w1_hi, *w1_lo, *s1b_hi, *s1b_lo, *w1b_part;
   int head_blocks, w2_chunks, w1_splits;
 };
+
+// Contraction path of the Float32 adjoint: TMA-fed tcgen05 (default),
+// transform-fed tcgen05, or CUDA-core SIMT. STADE_MLP_GEMM = tma | tc | simt.
+enum class MlpPath { Tma, Tc, Simt };
+MlpPath mlp_path(int64_t n_s, int64_t n_i, int64_t n_h) {
+  if (!tc_mlp_supported(n_s, n_i, n_h)) return MlpPath::Simt;
+  const char* sel = std::getenv("STADE_MLP_GEMM");
+  if (sel && std::strcmp(sel, "simt") == 0) return MlpPath::Simt;
+  if (sel && std::strcmp(sel, "tc") == 0) return MlpPath::Tc;
+  return MlpPath::Tma;
+}
 template <class Alloc>
 void mlp_f32_layout(Alloc& a, MlpF32Ws* w, int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o) {
   const int head_blocks = (int)((n_s + kHeadWarps - 1) / kHeadWarps);
@@ -682,14 +900,28 @@ void mlp_f32_layout(Alloc& a, MlpF32Ws* w, int64_t n_s, int64_t n_i, int64_t n_h
     w->w2_chunks = w2_chunks;
     w->w1_splits = w1_splits;
   }
+  const int tc_chunks = (int)((n_s + kW2ChunkTc - 1) / kW2ChunkTc);
+  const int w2_parts = w2_chunks > tc_chunks ? w2_chunks : tc_chunks;
+  const int head_parts = head_blocks > (int)((n_s + 255) / 256) ? head_blocks : (int)((n_s + 255) / 256);
   auto s1b = a.template take<float>((size_t)(n_s * n_h));
   auto gb = a.template take<float>((size_t)(n_s * n_o));
-  auto lp = a.template take<float>((size_t)head_blocks);
-  auto w2p = a.template take<float>((size_t)w2_chunks * (size_t)(n_h * n_o + n_o));
+  auto lp = a.template take<float>((size_t)head_parts);
+  auto w2p = a.template take<float>((size_t)w2_parts * (size_t)(n_h * n_o + n_o + n_h));
   auto w1p = a.template take<float>(w1_splits > 1 ? (size_t)w1_splits * (size_t)((n_i + 1) * n_h) : 1);
+  auto zp = a.template take<float>((size_t)tc_logit_parts(n_h) * (size_t)(n_s * n_o));
+  const bool planes = tc_mlp_supported(n_s, n_i, n_h);
+  auto xh = a.template take<float>(planes ? (size_t)(n_s * n_i) : 1);
+  auto xl = a.template take<float>(planes ? (size_t)(n_s * n_i) : 1);
+  auto wh = a.template take<float>(planes ? (size_t)(n_i * n_h) : 1);
+  auto wl = a.template take<float>(planes ? (size_t)(n_i * n_h) : 1);
+  auto sh = a.template take<float>(planes ? (size_t)(n_s * n_h) : 1);
+  auto sl = a.template take<float>(planes ? (size_t)(n_s * n_h) : 1);
+  auto wp = a.template take<float>(planes ? tma_w1b_part_floats(n_s, n_i, n_h) : 1);
   if (w) {
     w->s1b = (float*)s1b; w->gbuf = (float*)gb; w->loss_part = (float*)lp;
-    w->w2_part = (float*)w2p; w->w1_part = (float*)w1p;
+    w->w2_part = (float*)w2p; w->w1_part = (float*)w1p; w->zpart = (float*)zp;
+    w->x_hi = (float*)xh; w->x_lo = (float*)xl; w->w1_hi = (float*)wh; w->w1_lo = (float*)wl;
+    w->s1b_hi = (float*)sh; w->s1b_lo = (float*)sl; w->w1b_part = (float*)wp;
   }
 }
 struct SizerAlloc {
@@ -745,43 +977,127 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
   mlp_f32_layout(ca, &w, n_s, n_i, n_h, n_o);
   void* tcws = ca.c.take<char>(tc_mlp_workspace(n_s, n_i, n_h));
   const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
-  const bool use_tc = tc_mlp_supported(n_s, n_i, n_h);
+  const MlpPath path = mlp_path(n_s, n_i, n_h);
+  const bool use_tc = path == MlpPath::Tc;
 
-  // 1. h = tanh(x W1 + b1)
-  {
-    PhaseScope ph("fwd_gemm", s);
-    if (use_tc)
-      st = tc_forward_tanh(x, w1, b1, h, S, I, H, tcws, s);
-    else
+  if (path == MlpPath::Tma) {
+    // 0. TF32 hi / lo planes of x and W1
+    {
+      PhaseScope ph("split", s);
+      st = tma_split(x, w.x_hi, w.x_lo, n_s * n_i, s);
+      if (st == STADE_OK) st = tma_split(w1, w.w1_hi, w.w1_lo, n_i * n_h, s);
+    }
+    if (st != STADE_OK) return st;
+    // 1. h = tanh(x W1 + b1) and the logits' partial sums, TMA-fed tensor cores
+    {
+      PhaseScope ph("fwd_gemm", s);
+      st = tma_forward_tanh_logits(w.x_hi, w.x_lo, w.w1_hi, w.w1_lo, b1, w2, h, w.zpart, S, I, H,
+                                   O, s);
+    }
+    if (st != STADE_OK) return st;
+    // 2. softmax cross-entropy and its reverse, one thread per sample
+    {
+      PhaseScope ph("head", s);
+      const int blocks = (S + 255) / 256;
+      auto kern = O <= 16 ? mlp_head_small_kernel<float, 16> : mlp_head_small_kernel<float, 32>;
+      kern<<<blocks, 256, 0, s>>>(w.zpart, tc_logit_parts(n_h), lossb, y, yb, b2, z, zb, p, pb,
+                                  w.gbuf, S, O, w.loss_part);
+      STADE_CHECK_LAUNCH();
+      st = launch_sum_to_scalar(w.loss_part, blocks, loss, true, s);
+    }
+    if (st != STADE_OK) return st;
+    // 3. s1b as hi / lo planes, hb consumed, W2b / b2b / b1b partials
+    {
+      PhaseScope ph("w2b", s);
+      const int chunks = (S + kW2ChunkTc - 1) / kW2ChunkTc;
+      const size_t smem = sizeof(float) * (size_t)kW2ChunkTc * O;
+      auto kern = O <= 16 ? mlp_s1b_w2b_kernel<16, true> : mlp_s1b_w2b_kernel<32, true>;
+      kern<<<dim3(chunks, (H + 511) / 512), 256, smem, s>>>(h, hb, w.gbuf, w2, w.s1b_hi,
+                                                            w.s1b_lo, S, H, O, kW2ChunkTc,
+                                                            w.w2_part);
+      STADE_CHECK_LAUNCH();
+      finish_three_kernel<<<ceil_div_u(n_h * n_o + n_o + n_h, 256), 256, 0, s>>>(
+          w.w2_part, chunks, n_h * n_o, w2b, n_o, b2b, n_h, b1b);
+      STADE_CHECK_LAUNCH();
+    }
+    // 4. W1b = x^T s1b, 5. xb += s1b W1^T
+    {
+      PhaseScope ph("w1b_gemm", s);
+      st = tma_weight_grad(w.x_hi, w.x_lo, w.s1b_hi, w.s1b_lo, w1b, w.w1b_part, S, I, H, s);
+    }
+    if (st != STADE_OK) return st;
+    {
+      PhaseScope ph("xb_gemm", s);
+      st = tma_input_grad(w.s1b_hi, w.s1b_lo, w.w1_hi, w.w1_lo, xb, S, I, H, s);
+    }
+    return st;
+  }
+
+  if (use_tc) {
+    // 1. h = tanh(x W1 + b1) and the logits' partial sums, on tensor cores
+    {
+      PhaseScope ph("fwd_gemm", s);
+      st = tc_forward_tanh_logits(x, w1, b1, w2, h, w.zpart, S, I, H, O, s);
+    }
+    if (st != STADE_OK) return st;
+    // 2. softmax cross-entropy and its reverse, one thread per sample
+    {
+      PhaseScope ph("head", s);
+      const int blocks = (S + 255) / 256;
+      auto kern = O <= 16 ? mlp_head_small_kernel<float, 16> : mlp_head_small_kernel<float, 32>;
+      kern<<<blocks, 256, 0, s>>>(w.zpart, tc_logit_parts(n_h), lossb, y, yb, b2, z, zb, p, pb,
+                                  w.gbuf, S, O, w.loss_part);
+      STADE_CHECK_LAUNCH();
+      st = launch_sum_to_scalar(w.loss_part, blocks, loss, true, s);
+    }
+    if (st != STADE_OK) return st;
+    // 3. s1b, hb consumed, W2b / b2b partials in one pass over h and hb
+    {
+      PhaseScope ph("w2b", s);
+      const int chunks = (S + kW2ChunkTc - 1) / kW2ChunkTc;
+      const size_t smem = sizeof(float) * (size_t)kW2ChunkTc * O;
+      auto kern = O <= 16 ? mlp_s1b_w2b_kernel<16, false> : mlp_s1b_w2b_kernel<32, false>;
+      kern<<<dim3(chunks, (H + 511) / 512), 256, smem, s>>>(h, hb, w.gbuf, w2, w.s1b, nullptr, S,
+                                                            H, O, kW2ChunkTc, w.w2_part);
+      STADE_CHECK_LAUNCH();
+      finish_two_kernel<float><<<ceil_div_u(n_h * n_o + n_o, 256), 256, 0, s>>>(
+          w.w2_part, chunks, n_h * n_o, w2b, n_o, b2b);
+      STADE_CHECK_LAUNCH();
+    }
+  } else {
+    // 1. h = tanh(x W1 + b1)
+    {
+      PhaseScope ph("fwd_gemm", s);
       st = gemm_simt<float, kF32RM, kF32RN, kF32BK, true, true>(
           S, H, I, LdRow<float>{x, I}, LdB<float>{w1, H}, EpiTanh<float>{{}, b1, h, H}, nullptr,
           1, s);
-  }
-  if (st != STADE_OK) return st;
-  // 2. per-sample head
-  {
-    PhaseScope ph("head", s);
-    const size_t head_smem = sizeof(float) * (size_t)(n_h * n_o);
-    STADE_REQUIRE(head_smem <= 200 * 1024, "mlp2_ce_b: n_h * n_o too large");
-    auto kern = O <= 16 ? mlp_head_b_kernel<float, 16> : mlp_head_b_kernel<float, 32>;
-    if (head_smem > 48 * 1024)
-      STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)head_smem));
-    kern<<<w.head_blocks, kHeadWarps * 32, head_smem, s>>>(lossb, y, yb, w2, b2, h, hb, z, zb, p,
-                                                           pb, w.gbuf, w.s1b, S, H, O, w.loss_part);
-    STADE_CHECK_LAUNCH();
-    st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
-  }
-  if (st != STADE_OK) return st;
-  // 3. W2b, b2b
-  {
-    PhaseScope ph("w2b", s);
-    auto kern = O <= 16 ? mlp_w2b_partial_kernel<float, 16> : mlp_w2b_partial_kernel<float, 32>;
-    kern<<<w.w2_chunks, 256, 0, s>>>(h, w.gbuf, S, H, O, kW2Chunk, w.w2_part);
-    STADE_CHECK_LAUNCH();
-    finish_two_kernel<float><<<ceil_div_u(n_h * n_o + n_o, 256), 256, 0, s>>>(
-        w.w2_part, w.w2_chunks, n_h * n_o, w2b, n_o, b2b);
-    STADE_CHECK_LAUNCH();
+    }
+    if (st != STADE_OK) return st;
+    // 2. per-sample head
+    {
+      PhaseScope ph("head", s);
+      const size_t head_smem = sizeof(float) * (size_t)(n_h * n_o);
+      STADE_REQUIRE(head_smem <= 200 * 1024, "mlp2_ce_b: n_h * n_o too large");
+      auto kern = O <= 16 ? mlp_head_b_kernel<float, 16> : mlp_head_b_kernel<float, 32>;
+      if (head_smem > 48 * 1024)
+        STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)head_smem));
+      kern<<<w.head_blocks, kHeadWarps * 32, head_smem, s>>>(lossb, y, yb, w2, b2, h, hb, z, zb, p,
+                                                             pb, w.gbuf, w.s1b, S, H, O, w.loss_part);
+      STADE_CHECK_LAUNCH();
+      st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
+    }
+    if (st != STADE_OK) return st;
+    // 3. W2b, b2b
+    {
+      PhaseScope ph("w2b", s);
+      auto kern = O <= 16 ? mlp_w2b_partial_kernel<float, 16> : mlp_w2b_partial_kernel<float, 32>;
+      kern<<<w.w2_chunks, 256, 0, s>>>(h, w.gbuf, S, H, O, kW2Chunk, w.w2_part);
+      STADE_CHECK_LAUNCH();
+      finish_two_kernel<float><<<ceil_div_u(n_h * n_o + n_o, 256), 256, 0, s>>>(
+          w.w2_part, w.w2_chunks, n_h * n_o, w2b, n_o, b2b);
+      STADE_CHECK_LAUNCH();
+    }
   }
   // 4. W1b = x^T s1b (+ b1b as the row of ones), 5. xb += s1b W1^T
   {

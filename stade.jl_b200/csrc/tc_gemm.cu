@@ -162,7 +162,8 @@ __device__ __forceinline__ void st_split(uint8_t* hi, uint8_t* lo, uint32_t off,
   *reinterpret_cast<float4*>(lo + off) = l;
 }
 
-// ---- operand loaders (one 128 x 32 tile, 256 threads) -------------------------
+// ---- operand loaders (one tile of up to 128 rows x 32 k, 256 threads) -----------
+// `tile_rows` (<= 128) is the tile height: 128 for A, BN for B.
 // K-contiguous source: element (r, k) = p[r * ld + k]. Thread t takes 4
 // float4, idx = t + 256 i: row idx / 8, chunk idx % 8 (eight threads read one
 // 128-byte row segment; their swizzled stores hit eight different banks).
@@ -170,12 +171,15 @@ struct LoadK {
   const float* p;
   int ld, rows, K;
   int ones_row;  // unused for K-contiguous sources
-  __device__ __forceinline__ void load(int r0, int k0, int t, float4 (&v)[4]) const {
+  __device__ __forceinline__ void load(int r0, int k0, int t, int tile_rows, float4 (&v)[4]) const {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int idx = t + 256 * i;
-      const int r = r0 + (idx >> 3), k = k0 + 4 * (idx & 7);
-      if (r < rows && k + 3 < K) {
+      const int rr = idx >> 3;
+      const int r = r0 + rr, k = k0 + 4 * (idx & 7);
+      if (rr >= tile_rows) {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else if (r < rows && k + 3 < K) {
         v[i] = __ldg(reinterpret_cast<const float4*>(p + (int64_t)r * ld + k));
       } else {
         float e[4];
@@ -185,12 +189,12 @@ struct LoadK {
       }
     }
   }
-  __device__ __forceinline__ void store(uint8_t* hi, uint8_t* lo, int t,
+  __device__ __forceinline__ void store(uint8_t* hi, uint8_t* lo, int t, int tile_rows,
                                         const float4 (&v)[4]) const {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int idx = t + 256 * i;
-      st_split(hi, lo, tile_off(idx >> 3, idx & 7), v[i]);
+      if ((idx >> 3) < tile_rows) st_split(hi, lo, tile_off(idx >> 3, idx & 7), v[i]);
     }
   }
 };
@@ -210,22 +214,26 @@ struct LoadMN {
     if (r == ones_row) return 1.f;
     return r < rows ? p[(int64_t)k * ld + r] : 0.f;
   }
-  __device__ __forceinline__ void load(int r0, int k0, int t, float4 (&v)[4]) const {
+  __device__ __forceinline__ void load(int r0, int k0, int t, int tile_rows, float4 (&v)[4]) const {
     const int w = t >> 5, l = t & 31;
     const int r = r0 + 4 * l;
+    const bool in_tile = 4 * l < tile_rows;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int k = k0 + 4 * w + q;
-      if (k < K && r + 3 < rows && (ones_row < r || ones_row > r + 3)) {
+      if (!in_tile) {
+        v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else if (k < K && r + 3 < rows && (ones_row < r || ones_row > r + 3)) {
         v[q] = __ldg(reinterpret_cast<const float4*>(p + (int64_t)k * ld + r));
       } else {
         v[q] = make_float4(elem(r, k), elem(r + 1, k), elem(r + 2, k), elem(r + 3, k));
       }
     }
   }
-  __device__ __forceinline__ void store(uint8_t* hi, uint8_t* lo, int t,
+  __device__ __forceinline__ void store(uint8_t* hi, uint8_t* lo, int t, int tile_rows,
                                         const float4 (&v)[4]) const {
     const int w = t >> 5, l = t & 31;
+    if (4 * l >= tile_rows) return;
     // column j of the 4 x 4 block (row 4l + j) holds k = 4w .. 4w+3
     float4 col[4];
     col[0] = make_float4(v[0].x, v[1].x, v[2].x, v[3].x);
@@ -242,45 +250,112 @@ struct LoadMN {
   }
 };
 
-// ---- epilogues: a thread owns 32 consecutive columns of one row ----------------
+// ---- epilogues ----------------------------------------------------------------
+// A thread owns one accumulator row m and receives it in chunks of 16
+// consecutive columns: begin(m), chunk(m, n0, v) for each of its chunks,
+// end(m, key) (key = a per-thread index unique within the CTA tile).
 struct EpiTanhBias {  // out[m, n] = tanh(acc + bias[n])
   float* out;
   const float* bias;
   int ld, M, N;
-  __device__ __forceinline__ void apply(int m, int n0, const float (&v)[32]) const {
+  __device__ __forceinline__ void begin(int) {}
+  __device__ __forceinline__ void chunk(int m, int n0, const float (&v)[16]) {
     if (m >= M) return;
     float* o = out + (int64_t)m * ld;
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < 16; ++i)
       if (n0 + i < N) o[n0 + i] = tanhf(v[i] + bias[n0 + i]);
   }
+  __device__ __forceinline__ void end(int, int) {}
 };
-struct EpiAccumulate {  // out[m, n] += acc
+
+// h[m, n] = tanh(acc + b1[n]), plus the logits' partial sums over the
+// thread's hidden units: zpart[part, m, c] = sum_n h[m, n] w2[n, c]
+// (c < n_o <= NO), part = n_tile * 2 + key.
+template <int NO>
+struct EpiTanhLogits {
   float* out;
-  int ld, M, N;
-  __device__ __forceinline__ void apply(int m, int n0, const float (&v)[32]) const {
+  const float* bias;
+  const float* w2;
+  float* zpart;
+  int ld, M, N, n_o;
+  float zp[NO];
+  __device__ __forceinline__ void begin(int) {
+#pragma unroll
+    for (int c = 0; c < NO; ++c) zp[c] = 0.f;
+  }
+  __device__ __forceinline__ void chunk(int m, int n0, const float (&v)[16]) {
     if (m >= M) return;
     float* o = out + (int64_t)m * ld;
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (n0 + i < N) o[n0 + i] = o[n0 + i] + v[i];
-  }
-};
-struct EpiPartial {  // part[slice, m, n] = acc (split-K slice of the contraction)
-  float* part;
-  int M, N;
-  __device__ __forceinline__ void apply(int m, int n0, const float (&v)[32]) const {
-    if (m >= M) return;
-    float* o = part + ((int64_t)blockIdx.z * M + m) * N;
+    for (int i = 0; i < 16; ++i) {
+      if (n0 + i < N) {
+        const float hv = tanhf(v[i] + bias[n0 + i]);
+        o[n0 + i] = hv;
+        const float* wr = w2 + (int64_t)(n0 + i) * n_o;  // same address across the warp
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (n0 + i < N) o[n0 + i] = v[i];
+        for (int c = 0; c < NO; ++c)
+          if (c < n_o) zp[c] = fmaf(hv, __ldg(wr + c), zp[c]);
+      }
+    }
+  }
+  __device__ __forceinline__ void end(int m, int key) {
+    if (m >= M) return;
+    float* zr = zpart + ((int64_t)(blockIdx.x * 2 + key) * M + m) * n_o;
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) zr[c] = zp[c];
   }
 };
 
-template <class LA, class LB, class EPI>
+struct EpiAccumulate {  // out[m, n] += acc
+  float* out;
+  int ld, M, N;
+  __device__ __forceinline__ void begin(int) {}
+  __device__ __forceinline__ void chunk(int m, int n0, const float (&v)[16]) {
+    if (m >= M) return;
+    float* o = out + (int64_t)m * ld;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < N) o[n0 + i] = o[n0 + i] + v[i];
+  }
+  __device__ __forceinline__ void end(int, int) {}
+};
+
+struct EpiPartial {  // part[slice, m, n] = acc (split-K slice of the contraction)
+  float* part;
+  int M, N;
+  __device__ __forceinline__ void begin(int) {}
+  __device__ __forceinline__ void chunk(int m, int n0, const float (&v)[16]) {
+    if (m >= M) return;
+    float* o = part + ((int64_t)blockIdx.z * M + m) * N;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < N) o[n0 + i] = v[i];
+  }
+  __device__ __forceinline__ void end(int, int) {}
+};
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// One CTA = one BM x BN output tile over one K slice. BN is a multiple of 16
+// (<= 128); the B tile has BN rows.
+template <int BN_, class LA, class LB, class EPI>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(int M, int N, int K, int k_slice, LA la, LB lb, EPI epi) {
+  static_assert(BN_ % 16 == 0 && BN_ >= 16 && BN_ <= 128, "tile width");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
@@ -291,7 +366,7 @@ tc_gemm_kernel(int M, int N, int K, int k_slice, LA la, LB lb, EPI epi) {
   const uint32_t accb = smem_u32(bars + 2 * STAGES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN_;
   const int kbeg = blockIdx.z * k_slice;
   const int kend = min(K, kbeg + k_slice);
   const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
@@ -312,27 +387,36 @@ tc_gemm_kernel(int M, int N, int K, int k_slice, LA la, LB lb, EPI epi) {
   bool ok = true;
 
   if (warp < kXWarps) {
-    // ---- transform producers --------------------------------------------------
+    // ---- transform producers: loads run two K blocks ahead of the stores --------
     const int t = threadIdx.x;
-    float4 va[4], vb[4];
+    float4 va[2][4], vb[2][4];
     if (nkb > 0) {
-      la.load(m0, kbeg, t, va);
-      lb.load(n0, kbeg, t, vb);
+      la.load(m0, kbeg, t, BM, va[0]);
+      lb.load(n0, kbeg, t, BN_, vb[0]);
     }
-    for (int kb = 0; kb < nkb && ok; ++kb) {
+    if (nkb > 1) {
+      la.load(m0, kbeg + BK, t, BM, va[1]);
+      lb.load(n0, kbeg + BK, t, BN_, vb[1]);
+    }
+    auto stage_out = [&](int kb, float4 (&a)[4], float4 (&b)[4]) -> bool {
       const int s = kb % STAGES;
       const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) { ok = false; break; }
+      if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) return false;
       uint8_t* st = tiles + s * kStageBytes;
-      la.store(st, st + kTileBytes, t, va);
-      lb.store(st + 2 * kTileBytes, st + 3 * kTileBytes, t, vb);
+      la.store(st, st + kTileBytes, t, BM, a);
+      lb.store(st + 2 * kTileBytes, st + 3 * kTileBytes, t, BN_, b);
       fence_proxy_async();
       mbar_arrive(full0 + 8 * s);
-      if (kb + 1 < nkb) {
-        const int k0 = kbeg + (kb + 1) * BK;
-        la.load(m0, k0, t, va);
-        lb.load(n0, k0, t, vb);
+      if (kb + 2 < nkb) {
+        const int k0 = kbeg + (kb + 2) * BK;
+        la.load(m0, k0, t, BM, a);
+        lb.load(n0, k0, t, BN_, b);
       }
+      return true;
+    };
+    for (int kb = 0; kb < nkb && ok; kb += 2) {
+      ok = stage_out(kb, va[0], vb[0]);
+      if (ok && kb + 1 < nkb) ok = stage_out(kb + 1, va[1], vb[1]);
     }
     // ---- epilogue: TMEM -> registers -> global --------------------------------
     if (ok) ok = mbar_wait(accb, 0);
@@ -342,21 +426,21 @@ tc_gemm_kernel(int M, int N, int K, int k_slice, LA la, LB lb, EPI epi) {
     if (ok) {
       const int quad = warp & 3, half = warp >> 2;
       const int m = m0 + quad * 32 + lane;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int col = half * 64 + c * 32;
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)col, v);
+      epi.begin(m);
+      for (int c = half; c < BN_ / 16; c += 2) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 16), v);
         if (nkb == 0) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
         }
-        epi.apply(m, n0 + col, v);
+        epi.chunk(m, n0 + c * 16, v);
       }
+      epi.end(m, half);
     }
   } else if (lane == 0) {
     // ---- MMA issuer -------------------------------------------------------------
-    constexpr uint32_t idesc = idesc_tf32(BM, BN);
+    constexpr uint32_t idesc = idesc_tf32(BM, BN_);
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % STAGES;
       const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
@@ -404,47 +488,71 @@ __global__ void tc_splitk_finish_kernel(const float* __restrict__ part, int spli
   else bias[n] += acc;
 }
 
-template <class LA, class LB, class EPI>
-stade_status launch(int M, int N, int K, int splits, const LA& la, const LB& lb, const EPI& epi,
-                    cudaStream_t s) {
-  STADE_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<LA, LB, EPI>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+struct Slices {
+  int k_slice, count;
+};
+// K slices of at least 16 K blocks, the count chosen so that tiles x slices
+// fills whole waves of one CTA per SM as nearly as possible.
+inline Slices slices_for(int tiles, int K, int max_slices) {
   const int kblocks = (K + BK - 1) / BK;
-  const int per = splits > 1 ? (kblocks + splits - 1) / splits : kblocks;
-  const int k_slice = (per > 0 ? per : 1) * BK;
-  const int nsl = splits > 1 ? (K + k_slice - 1) / k_slice : 1;
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, nsl);
-  tc_gemm_kernel<LA, LB, EPI><<<grid, kThreads, kSmemBytes, s>>>(M, N, K, k_slice, la, lb, epi);
+  int best = 1;
+  double best_eff = 0.0;
+  for (int sl = 1; sl <= max_slices; ++sl) {
+    if (sl > 1 && kblocks / sl < 16) break;
+    const int ctas = tiles * sl;
+    const int waves = (ctas + 147) / 148;
+    const double eff = (double)ctas / (waves * 148.0);
+    if (eff > best_eff + 1e-9 || (waves < 3 && sl > best)) {
+      best_eff = eff;
+      best = sl;
+    }
+    if (eff > 0.97 && waves >= 3) break;
+  }
+  const int per = (kblocks + best - 1) / best;
+  Slices r;
+  r.k_slice = (per > 0 ? per : 1) * BK;
+  r.count = K > 0 ? (K + r.k_slice - 1) / r.k_slice : 1;
+  return r;
+}
+
+template <int BN_, class LA, class LB, class EPI>
+stade_status launch(int M, int N, int K, Slices sl, const LA& la, const LB& lb, const EPI& epi,
+                    cudaStream_t s) {
+  STADE_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<BN_, LA, LB, EPI>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  dim3 grid((N + BN_ - 1) / BN_, (M + BM - 1) / BM, sl.count);
+  tc_gemm_kernel<BN_, LA, LB, EPI><<<grid, kThreads, kSmemBytes, s>>>(M, N, K, sl.k_slice, la, lb,
+                                                                     epi);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }
 
-int w1b_splits(int S, int I, int H) {
+inline Slices whole_k(int K) {
+  Slices r;
+  r.k_slice = (K > 0 ? (K + BK - 1) / BK : 1) * BK;
+  r.count = 1;
+  return r;
+}
+
+inline Slices w1b_slices(int S, int I, int H) {
   const int tiles = ((I + 1 + BM - 1) / BM) * ((H + BN - 1) / BN);
-  int want = (2 * 148 + tiles - 1) / tiles;
-  const int kblocks = (S + BK - 1) / BK;
-  while (want > 1 && kblocks / want < 8) --want;
-  if (want < 1) want = 1;
-  const int per = (kblocks + want - 1) / want;
-  return (S + per * BK - 1) / (per * BK);
+  return slices_for(tiles, S, 64);
 }
 
 }  // namespace tc
 
 bool tc_mlp_supported(int64_t n_s, int64_t n_i, int64_t n_h) {
-  // STADE_MLP_GEMM selects the contraction path: "tc" (tcgen05 3xTF32, the
-  // default) or "simt" (CUDA-core FMA, kept as a cross-check)
-  const char* sel = std::getenv("STADE_MLP_GEMM");
-  if (sel && std::strcmp(sel, "simt") == 0) return false;
   return n_s >= 1 && n_i >= 1 && n_h >= 1 && n_i % 4 == 0 && n_h % 4 == 0 &&
          n_s < (int64_t(1) << 30) && n_i < (1 << 20) && n_h < (1 << 20);
 }
 
 size_t tc_mlp_workspace(int64_t n_s, int64_t n_i, int64_t n_h) {
   if (!tc_mlp_supported(n_s, n_i, n_h)) return 0;
-  const int sp = tc::w1b_splits((int)n_s, (int)n_i, (int)n_h);
+  const int sp = tc::w1b_slices((int)n_s, (int)n_i, (int)n_h).count;
   return align_up((size_t)sp * (size_t)(n_i + 1) * (size_t)n_h * sizeof(float), 256);
 }
+
+int tc_logit_parts(int64_t n_h) { return 2 * (int)((n_h + tc::BN - 1) / tc::BN); }
 
 stade_status tc_forward_tanh(const float* x, const float* w1, const float* b1, float* h, int S,
                              int I, int H, void*, cudaStream_t s) {
@@ -452,39 +560,58 @@ stade_status tc_forward_tanh(const float* x, const float* w1, const float* b1, f
   tc::LoadK la{x, I, S, I, -1};
   tc::LoadMN lb{w1, H, H, I, -1};
   tc::EpiTanhBias epi{h, b1, H, S, H};
-  return tc::launch(S, H, I, 1, la, lb, epi, s);
+  return tc::launch<tc::BN>(S, H, I, tc::whole_k(I), la, lb, epi, s);
+}
+
+stade_status tc_forward_tanh_logits(const float* x, const float* w1, const float* b1,
+                                    const float* w2, float* h, float* zpart, int S, int I, int H,
+                                    int O, cudaStream_t s) {
+  tc::LoadK la{x, I, S, I, -1};
+  tc::LoadMN lb{w1, H, H, I, -1};
+  if (O <= 16)
+    return tc::launch<tc::BN>(S, H, I, tc::whole_k(I), la, lb,
+                              tc::EpiTanhLogits<16>{h, b1, w2, zpart, H, S, H, O, {}}, s);
+  return tc::launch<tc::BN>(S, H, I, tc::whole_k(I), la, lb,
+                            tc::EpiTanhLogits<32>{h, b1, w2, zpart, H, S, H, O, {}}, s);
 }
 
 stade_status tc_weight_grad(const float* x, const float* s1b, float* w1b, float* b1b, int S, int I,
                             int H, void* ws, cudaStream_t s) {
   // A[m = input (+ row of ones), k = sample] = x[k, m]; B[n = hidden, k = sample] = s1b[k, n]
   const int M = I + 1;
-  const int sp = tc::w1b_splits(S, I, H);
+  const tc::Slices sl = tc::w1b_slices(S, I, H);
   float* part = static_cast<float*>(ws);
   tc::LoadMN la{x, I, I, S, I};
   tc::LoadMN lb{s1b, H, H, S, -1};
   tc::EpiPartial epi{part, M, H};
-  stade_status st = tc::launch(M, H, S, sp, la, lb, epi, s);
+  stade_status st = tc::launch<tc::BN>(M, H, S, sl, la, lb, epi, s);
   if (st != STADE_OK) return st;
-  const int kblocks = (S + tc::BK - 1) / tc::BK;
-  const int per = (kblocks + sp - 1) / sp;
-  const int nsl = (S + per * tc::BK - 1) / (per * tc::BK);
   const int64_t MN = (int64_t)M * H;
-  tc::tc_splitk_finish_kernel<<<ceil_div_u(MN, 256), 256, 0, s>>>(part, nsl, M, H, I, w1b, b1b);
+  tc::tc_splitk_finish_kernel<<<ceil_div_u(MN, 256), 256, 0, s>>>(part, sl.count, M, H, I, w1b,
+                                                                   b1b);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }
 
 stade_status tc_input_grad(const float* s1b, const float* w1, float* xb, int S, int I, int H, void*,
                            cudaStream_t s) {
-  // A[m = sample, k = hidden] = s1b (K-contiguous); B[n = input, k = hidden] = w1[n, k]
+  // A[m = sample, k = hidden] = s1b (K-contiguous); B[n = input, k = hidden] = w1[n, k].
+  // The tile width divides the input width when it can (784 = 7 x 112).
   tc::LoadK la{s1b, H, S, H, -1};
   tc::LoadK lb{w1, H, I, H, -1};
   tc::EpiAccumulate epi{xb, I, S, I};
-  return tc::launch(S, I, H, 1, la, lb, epi, s);
+  if (I % 128 != 0 && I % 112 == 0)
+    return tc::launch<112>(S, I, H, tc::whole_k(H), la, lb, epi, s);
+  if (I % 128 != 0 && I % 96 == 0)
+    return tc::launch<96>(S, I, H, tc::whole_k(H), la, lb, epi, s);
+  return tc::launch<tc::BN>(S, I, H, tc::whole_k(H), la, lb, epi, s);
 }
 
 }  // namespace stade
+
+namespace stade {
+int tma_take_error();
+}
 
 extern "C" int stade_device_error(void) {
   int v = 0;
@@ -493,5 +620,7 @@ extern "C" int stade_device_error(void) {
     const int zero = 0;
     cudaMemcpyToSymbol(stade::tc::g_tc_error, &zero, sizeof(int));
   }
-  return v;
+  const int t = stade::tma_take_error();
+  if (t < 0) return -1;
+  return v | t;
 }

@@ -1,0 +1,671 @@
+// TMA-fed tensor-core (tcgen05 / TMEM) Float32 contractions with 3xTF32
+// splitting: the mlp2_ce adjoint's three GEMMs.
+//
+// Every Float32 operand is held in memory as two planes, hi (low 13 mantissa
+// bits cleared: exactly representable in TF32) and lo = value - hi (exact):
+// x is split by one pass per call, W1 by a tiny pass, and s1b is written as
+// planes directly by the pass that produces it. D = A B^T then needs
+// hi*hi + hi*lo + lo*hi (lo*lo is below Float32 rounding), three
+// tcgen05.mma.kind::tf32 per K step into one TMEM accumulator.
+//
+// Persistent kernel, one CTA per SM, warp-specialised:
+//   warp 0  one thread issues TMA loads (cp.async.bulk.tensor, no multicast)
+//           of the four 128 x 32 operand tiles of a K block into a 3-stage
+//           ring of 128-byte-swizzled shared memory, signalled by
+//           mbarrier complete_tx;
+//   warp 1  owns TMEM (2 accumulators x 128 columns) and one thread issues
+//           the MMAs, releasing each stage with tcgen05.commit;
+//   warps 2-9 drain an accumulator with tcgen05.ld while the MMAs fill the
+//           other one, and apply the fused epilogue.
+// An operand is K-major (K contiguous in memory: one 128 x 32 box) or
+// MN-major (M or N contiguous: four 32 x 32 boxes), described to the MMA by
+// its shared-memory descriptor, so no operand is ever transposed.
+// Every wait is bounded (~2 s of clock); on timeout the kernel sets
+// g_tma_error, stops issuing work, waits (bounded) for its own copies and
+// tensor-core operations, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "tc_gemm.cuh"
+
+namespace stade {
+namespace tma {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (2 + kEpiWarps) * 32;  // 320
+constexpr int kTileBytes = 128 * BK * 4;        // 16 KiB
+constexpr int kStageBytes = 4 * kTileBytes;     // A hi, A lo, B hi, B lo
+constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 512;
+constexpr uint32_t kTmemCols = 256;             // two 128-column accumulators
+constexpr long long kWaitCycles = 4000000000LL; // ~2 s at 1.9 GHz
+// K blocks per TMEM accumulation chain. The tensor core's Float32
+// accumulation is not round-to-nearest: its error grows linearly with the
+// number of accumulations into one TMEM accumulator (measured: 1.4e-5
+// relative after 1000 K). Chains of 4 K blocks (128 K, 48 MMAs) are drained
+// into round-to-nearest Float32 sums in registers by the epilogue warps,
+// while the other TMEM buffer takes the next chain.
+constexpr int kChainBlocks = 4;
+
+__device__ int g_tma_error = 0;
+
+// ---- PTX wrappers ---------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicExch(&g_tma_error, 1);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (version 1).
+//  K-major, 128-byte swizzle of 16-byte chunks (layout type 2): rows of 128
+//           bytes (32 tf32 of K), 8-row groups 1024 B apart; K step j starts
+//           32 j bytes into the row.
+//  MN-major, 128-byte swizzle of 32-byte chunks (layout type 1, the only
+//           shared-memory layout tf32 takes MN-major): rows of 128 bytes (32
+//           tf32 of M or N) per k, 4-row K groups 512 B apart, 32-wide M/N
+//           groups 4096 B apart; K step j (8 rows) starts at 1024 j bytes.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                               uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- epilogues: a thread owns one accumulator row and gets 16 columns at a time
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+struct EpiTanhLogits {  // h = tanh(acc + b1); zpart[part][m][c] = sum h w2 over the thread's columns
+  float* h;
+  const float* b1;
+  const float* w2;
+  float* zpart;
+  int ld, M, N, n_o, parts_per_tile;
+};
+struct EpiAccumulate {  // out[m, n] += acc
+  float* out;
+  int ld, M, N;
+};
+struct EpiPartial {  // part[slice][m][n] = acc
+  float* part;
+  int M, N;
+};
+
+__device__ __forceinline__ void epi_acc_chunk(const EpiAccumulate& e, int m, int n0,
+                                              const float (&v)[16]) {
+  if (m >= e.M) return;
+  float* o = e.out + (int64_t)m * e.ld + n0;
+  if (n0 + 16 <= e.N && aligned16(o)) {
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      float4 q = *reinterpret_cast<float4*>(o + i);
+      q.x += v[i]; q.y += v[i + 1]; q.z += v[i + 2]; q.w += v[i + 3];
+      *reinterpret_cast<float4*>(o + i) = q;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < e.N) o[i] = o[i] + v[i];
+  }
+}
+
+__device__ __forceinline__ void epi_part_chunk(const EpiPartial& e, int m, int n0, int slice,
+                                               const float (&v)[16]) {
+  if (m >= e.M) return;
+  float* o = e.part + ((int64_t)slice * e.M + m) * e.N + n0;
+  if (n0 + 16 <= e.N && aligned16(o)) {
+#pragma unroll
+    for (int i = 0; i < 16; i += 4)
+      *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (n0 + i < e.N) o[i] = v[i];
+  }
+}
+
+struct Geometry {
+  int M, N, K;
+  int m_tiles, n_tiles, slices, k_slice;
+  bool a_mn, b_mn;
+};
+
+// EPI_KIND: 0 logits (NO classes), 1 accumulate, 2 split-K partial
+template <int EPI_KIND, int NO>
+__global__ void __launch_bounds__(kThreads, 1)
+tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
+                const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo,
+                Geometry g, EpiTanhLogits el, EpiAccumulate ea, EpiPartial ep) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+  uint8_t* tiles = smem_raw + pad;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + STAGES * kStageBytes);
+  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
+  const uint32_t done = smem_u32(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_per_slice = g.m_tiles * g.n_tiles;
+  const int total = tiles_per_slice * g.slices;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, kEpiWarps);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ---------------------------------------------------------
+      int kb_all = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int slice = t / tiles_per_slice, r = t % tiles_per_slice;
+        const int m0 = (r / g.n_tiles) * BM, n0 = (r % g.n_tiles) * BN;
+        const int kbeg = slice * g.k_slice;
+        const int kend = min(g.K, kbeg + g.k_slice);
+        const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+        for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
+          const int s = kb_all % STAGES;
+          const uint32_t ph = (uint32_t)(kb_all / STAGES) & 1u;
+          if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) { ok = false; break; }
+          const uint32_t st = smem_u32(tiles + s * kStageBytes);
+          const uint32_t fb = full0 + 8 * s;
+          mbar_arrive_tx(fb, kStageBytes);
+          const int k0 = kbeg + kb * BK;
+          if (!g.a_mn) {
+            tma_load_2d(st, &a_hi, k0, m0, fb);
+            tma_load_2d(st + kTileBytes, &a_lo, k0, m0, fb);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              tma_load_2d(st + q * 4096, &a_hi, m0 + 32 * q, k0, fb);
+              tma_load_2d(st + kTileBytes + q * 4096, &a_lo, m0 + 32 * q, k0, fb);
+            }
+          }
+          if (!g.b_mn) {
+            tma_load_2d(st + 2 * kTileBytes, &b_hi, k0, n0, fb);
+            tma_load_2d(st + 3 * kTileBytes, &b_lo, k0, n0, fb);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              tma_load_2d(st + 2 * kTileBytes + q * 4096, &b_hi, n0 + 32 * q, k0, fb);
+              tma_load_2d(st + 3 * kTileBytes + q * 4096, &b_lo, n0 + 32 * q, k0, fb);
+            }
+          }
+        }
+      }
+      // copies still in flight land before the CTA exits: wait for the last
+      // phase armed on every stage (bounded)
+      for (int i = 0; i < STAGES && i < kb_all; ++i) {
+        const int last = kb_all - 1 - i;
+        mbar_wait(full0 + 8 * (last % STAGES), (uint32_t)(last / STAGES) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer -------------------------------------------------------------
+      const uint32_t idesc = idesc_tf32(BM, BN, g.a_mn, g.b_mn);
+      const uint32_t a_lbo = g.a_mn ? 4096u : 16u, a_sbo = g.a_mn ? 512u : 1024u;
+      const uint32_t b_lbo = g.b_mn ? 4096u : 16u, b_sbo = g.b_mn ? 512u : 1024u;
+      const uint32_t a_lay = g.a_mn ? 1u : 2u, b_lay = g.b_mn ? 1u : 2u;
+      const uint32_t a_step = g.a_mn ? 1024u : 32u, b_step = g.b_mn ? 1024u : 32u;
+      int kb_all = 0, chain = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int slice = t / tiles_per_slice;
+        const int kbeg = slice * g.k_slice;
+        const int kend = min(g.K, kbeg + g.k_slice);
+        const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+        const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+        for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
+          const int b = chain & 1;
+          const uint32_t acc = tmem + (uint32_t)(b * BN);
+          if (!mbar_wait(tempty0 + 8 * b, ((uint32_t)(chain >> 1) & 1u) ^ 1u)) { ok = false; break; }
+          tc_fence_after();
+          const int kb0 = ch * kChainBlocks, kb1 = min(nkb, kb0 + kChainBlocks);
+          for (int kb = kb0; kb < kb1; ++kb, ++kb_all) {
+            const int s = kb_all % STAGES;
+            const uint32_t ph = (uint32_t)(kb_all / STAGES) & 1u;
+            if (!mbar_wait(full0 + 8 * s, ph)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t st = smem_u32(tiles + s * kStageBytes);
+#pragma unroll
+            for (int j = 0; j < BK / 8; ++j) {
+              const uint64_t ahi = desc_sw128(st + a_step * j, a_lbo, a_sbo, a_lay);
+              const uint64_t alo = desc_sw128(st + kTileBytes + a_step * j, a_lbo, a_sbo, a_lay);
+              const uint64_t bhi = desc_sw128(st + 2 * kTileBytes + b_step * j, b_lbo, b_sbo, b_lay);
+              const uint64_t blo = desc_sw128(st + 3 * kTileBytes + b_step * j, b_lbo, b_sbo, b_lay);
+              mma_tf32(acc, ahi, blo, idesc, (kb != kb0 || j != 0) ? 1u : 0u);
+              mma_tf32(acc, alo, bhi, idesc, 1u);
+              mma_tf32(acc, ahi, bhi, idesc, 1u);
+            }
+            mma_commit(empty0 + 8 * s);
+          }
+          // an empty chain (K = 0) still hands a buffer over; the epilogue ignores it
+          mma_commit(tfull0 + 8 * b);
+        }
+      }
+      // every MMA issued above completes before TMEM is freed
+      mma_commit(done);
+      mbar_wait(done, 0);
+    }
+  } else {
+    // ---- epilogue warps -------------------------------------------------------------
+    const int e = warp - 2;
+    const int quad = warp & 3;       // TMEM lanes 32 quad .. 32 quad + 31
+    const int half = e >> 2;         // column half of the tile
+    int chain = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      const int slice = t / tiles_per_slice, r = t % tiles_per_slice;
+      const int m0 = (r / g.n_tiles) * BM, n0 = (r % g.n_tiles) * BN;
+      const int kbeg = slice * g.k_slice;
+      const int kend = min(g.K, kbeg + g.k_slice);
+      const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+      const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+      const int m = m0 + quad * 32 + lane;
+      // the thread's 64 columns: 16-wide groups half, half + 2, half + 4, half + 6
+      float sum[BN / 32][16];
+#pragma unroll
+      for (int q = 0; q < BN / 32; ++q)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sum[q][i] = 0.f;
+      for (int ch = 0; ch < nch; ++ch, ++chain) {
+        const int b = chain & 1;
+        ok = mbar_wait(tfull0 + 8 * b, (uint32_t)(chain >> 1) & 1u);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        if (nkb > 0) {
+          const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN);
+#pragma unroll
+          for (int q = 0; q < BN / 32; ++q) {
+            float v[16];
+            tmem_ld16(base + (uint32_t)((half + 2 * q) * 16), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[q][i] += v[i];
+          }
+        }
+        // this warp is done with accumulator b
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty0 + 8 * b);
+      }
+      if (!ok) break;
+      if constexpr (EPI_KIND == 0) {
+        float zp[NO];
+#pragma unroll
+        for (int c = 0; c < NO; ++c) zp[c] = 0.f;
+#pragma unroll
+        for (int q = 0; q < BN / 32; ++q) {
+          const int nn = n0 + (half + 2 * q) * 16;
+          if (m < el.M) {
+            float* o = el.h + (int64_t)m * el.ld + nn;
+            float hv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              hv[i] = (nn + i < el.N) ? tanhf(sum[q][i] + __ldg(el.b1 + nn + i)) : 0.f;
+            if (nn + 16 <= el.N && aligned16(o)) {
+#pragma unroll
+              for (int i = 0; i < 16; i += 4)
+                *reinterpret_cast<float4*>(o + i) =
+                    make_float4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (nn + i < el.N) o[i] = hv[i];
+            }
+            // logits partial; w2 rows are the same for the whole warp (L1 broadcast)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              if (nn + i < el.N) {
+                const float* wr = el.w2 + (int64_t)(nn + i) * el.n_o;
+#pragma unroll
+                for (int cc = 0; cc < NO; ++cc)
+                  if (cc < el.n_o) zp[cc] = fmaf(hv[i], __ldg(wr + cc), zp[cc]);
+              }
+            }
+          }
+        }
+        if (m < el.M) {
+          const int part = (n0 / BN) * 2 + half;
+          float* zr = el.zpart + ((int64_t)part * el.M + m) * el.n_o;
+#pragma unroll
+          for (int cc = 0; cc < NO; ++cc)
+            if (cc < el.n_o) zr[cc] = zp[cc];
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < BN / 32; ++q) {
+          if constexpr (EPI_KIND == 1) epi_acc_chunk(ea, m, n0 + (half + 2 * q) * 16, sum[q]);
+          else epi_part_chunk(ep, m, n0 + (half + 2 * q) * 16, slice, sum[q]);
+        }
+      }
+    }
+  }
+
+  // ---- teardown -----------------------------------------------------------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- host: tensor maps ---------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Row-major Float32 plane of rows x cols (row pitch `ld` elements), box of
+// box_c (inner, along cols) x box_r, 128-byte swizzle with 16-byte chunks
+// (K-major operands) or 32-byte chunks (MN-major operands), zero fill outside.
+stade_status make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld,
+                      uint32_t box_c, uint32_t box_r, bool chunk32) {
+  auto fn = encode_fn();
+  if (!fn) return fail(STADE_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (ld * 4) % 16)
+    return fail(STADE_EINVAL, "TMA operand must be 16-byte aligned with a 16-byte row pitch");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  const cuuint32_t box[2] = {box_c, box_r};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  chunk32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(STADE_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return STADE_OK;
+}
+
+// An operand of the contraction held as hi / lo planes. mn = false: rows are
+// M (or N), columns are K (K contiguous). mn = true: rows are K, columns are
+// M (or N).
+struct Operand {
+  const float *hi, *lo;
+  int64_t rows, cols, ld;
+  bool mn;
+};
+
+stade_status operand_maps(const Operand& o, CUtensorMap* hi, CUtensorMap* lo) {
+  const uint32_t bc = 32, br = o.mn ? 32u : 128u;
+  stade_status st = make_map(hi, o.hi, o.rows, o.cols, o.ld, bc, br, o.mn);
+  if (st != STADE_OK) return st;
+  return make_map(lo, o.lo, o.rows, o.cols, o.ld, bc, br, o.mn);
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int EPI_KIND, int NO>
+stade_status run(const Operand& A, const Operand& B, Geometry g, const EpiTanhLogits& el,
+                 const EpiAccumulate& ea, const EpiPartial& ep, cudaStream_t s) {
+  CUtensorMap ah, al, bh, bl;
+  stade_status st = operand_maps(A, &ah, &al);
+  if (st != STADE_OK) return st;
+  st = operand_maps(B, &bh, &bl);
+  if (st != STADE_OK) return st;
+  STADE_CUDA(cudaFuncSetAttribute(tma_gemm_kernel<EPI_KIND, NO>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  const int total = g.m_tiles * g.n_tiles * g.slices;
+  const int grid = total < sm_count() ? total : sm_count();
+  tma_gemm_kernel<EPI_KIND, NO><<<grid, kThreads, kSmemBytes, s>>>(ah, al, bh, bl, g, el, ea, ep);
+  STADE_CHECK_LAUNCH();
+  return STADE_OK;
+}
+
+Geometry geometry(int M, int N, int K, int slices, bool a_mn, bool b_mn) {
+  Geometry g;
+  g.M = M; g.N = N; g.K = K;
+  g.m_tiles = (M + BM - 1) / BM;
+  g.n_tiles = (N + BN - 1) / BN;
+  const int kblocks = (K + BK - 1) / BK;
+  const int per = slices > 1 ? (kblocks + slices - 1) / slices : kblocks;
+  g.k_slice = (per > 0 ? per : 1) * BK;
+  g.slices = K > 0 ? (K + g.k_slice - 1) / g.k_slice : 1;
+  g.a_mn = a_mn; g.b_mn = b_mn;
+  return g;
+}
+
+// Slices of the W1b contraction (K = samples): enough tiles for ~4 per SM,
+// at least 32 K blocks per slice.
+int w1b_slices(int S, int I, int H) {
+  const int tiles = ((I + BM - 1) / BM) * ((H + BN - 1) / BN);
+  const int kblocks = (S + BK - 1) / BK;
+  int sl = (4 * 148 + tiles - 1) / tiles;
+  while (sl > 1 && kblocks / sl < 32) --sl;
+  return sl < 1 ? 1 : sl;
+}
+
+// hi / lo split of a Float32 array (n % 4 == 0 handled by the vector path).
+__global__ void split_kernel(const float* __restrict__ a, float* __restrict__ hi,
+                             float* __restrict__ lo, int64_t n) {
+  const int64_t n4 = n / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(a)[i];
+    float4 h, l;
+    h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u); l.x = v.x - h.x;
+    h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u); l.y = v.y - h.y;
+    h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u); l.z = v.z - h.z;
+    h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u); l.w = v.w - h.w;
+    reinterpret_cast<float4*>(hi)[i] = h;
+    reinterpret_cast<float4*>(lo)[i] = l;
+  }
+  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = a[i];
+    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+
+__global__ void w1b_finish_kernel(const float* __restrict__ part, int slices, int64_t MN,
+                                  float* __restrict__ w1b) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= MN) return;
+  float acc = 0.f;
+  for (int z = 0; z < slices; ++z) acc += part[(int64_t)z * MN + e];
+  w1b[e] += acc;
+}
+
+}  // namespace tma
+
+// ---- entry points used by mlp2_ce -------------------------------------------------------
+stade_status tma_split(const float* a, float* hi, float* lo, int64_t n, cudaStream_t s) {
+  if (n <= 0) return STADE_OK;
+  const int64_t threads = 256;
+  int64_t blocks = (n / 4 + threads - 1) / threads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  tma::split_kernel<<<(unsigned)blocks, (unsigned)threads, 0, s>>>(a, hi, lo, n);
+  STADE_CHECK_LAUNCH();
+  return STADE_OK;
+}
+
+size_t tma_w1b_part_floats(int64_t n_s, int64_t n_i, int64_t n_h) {
+  return (size_t)tma::w1b_slices((int)n_s, (int)n_i, (int)n_h) * (size_t)n_i * (size_t)n_h;
+}
+
+stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const float* w1_hi,
+                                     const float* w1_lo, const float* b1, const float* w2,
+                                     float* h, float* zpart, int S, int I, int H, int O,
+                                     cudaStream_t s) {
+  // A[m = sample, k = input]: x, K-major. B[n = hidden, k = input] = w1[k, n]: MN-major.
+  tma::Operand A{x_hi, x_lo, S, I, I, false};
+  tma::Operand B{w1_hi, w1_lo, I, H, H, true};
+  tma::Geometry g = tma::geometry(S, H, I, 1, false, true);
+  tma::EpiTanhLogits el{h, b1, w2, zpart, H, S, H, O, 2};
+  if (O <= 16) return tma::run<0, 16>(A, B, g, el, {}, {}, s);
+  return tma::run<0, 32>(A, B, g, el, {}, {}, s);
+}
+
+stade_status tma_weight_grad(const float* x_hi, const float* x_lo, const float* s1b_hi,
+                             const float* s1b_lo, float* w1b, float* part, int S, int I, int H,
+                             cudaStream_t s) {
+  // A[m = input, k = sample] = x[k, m]: MN-major. B[n = hidden, k = sample] = s1b[k, n]: MN-major.
+  tma::Operand A{x_hi, x_lo, S, I, I, true};
+  tma::Operand B{s1b_hi, s1b_lo, S, H, H, true};
+  tma::Geometry g = tma::geometry(I, H, S, tma::w1b_slices(S, I, H), true, true);
+  tma::EpiPartial ep{part, I, H};
+  stade_status st = tma::run<2, 1>(A, B, g, {}, {}, ep, s);
+  if (st != STADE_OK) return st;
+  const int64_t MN = (int64_t)I * H;
+  tma::w1b_finish_kernel<<<ceil_div_u(MN, 256), 256, 0, s>>>(part, g.slices, MN, w1b);
+  STADE_CHECK_LAUNCH();
+  return STADE_OK;
+}
+
+stade_status tma_input_grad(const float* s1b_hi, const float* s1b_lo, const float* w1_hi,
+                            const float* w1_lo, float* xb, int S, int I, int H, cudaStream_t s) {
+  // A[m = sample, k = hidden] = s1b: K-major. B[n = input, k = hidden] = w1[n, k]: K-major.
+  tma::Operand A{s1b_hi, s1b_lo, S, H, H, false};
+  tma::Operand B{w1_hi, w1_lo, I, H, H, false};
+  tma::Geometry g = tma::geometry(S, I, H, 1, false, false);
+  tma::EpiAccumulate ea{xb, I, S, I};
+  return tma::run<1, 1>(A, B, g, {}, ea, {}, s);
+}
+
+}  // namespace stade
+
+namespace stade {
+// Reads and clears the TMA kernel's error word (-1 when it cannot be read).
+int tma_take_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tma::g_tma_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(tma::g_tma_error, &zero, sizeof(int));
+  }
+  return v;
+}
+}  // namespace stade

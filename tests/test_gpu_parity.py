@@ -20,6 +20,34 @@ F64_TOL = 1e-12
 F32_TOL = 1e-5
 
 
+def f32_verdict(gpu, ref32, truth):
+    """Float32 parity, the shape of the reference's GPU verdict
+    (val_truth_verdict_lines, src/STADE.jl:18925-18937): the GPU result is
+    within 1e-5 of the Float32 oracle, or at least as close to the exact
+    result (the same sweep in Float64) as the Float32 oracle itself is. At
+    large reduction lengths the oracle's own sequential Float32 sums are
+    ~1e-5 off, so the first test alone would fail an exact GPU result."""
+    e_ref = rel_err(gpu, ref32)
+    e_truth = rel_err(gpu, truth)
+    e_oracle = rel_err(ref32, truth)
+    return (e_ref <= F32_TOL or e_truth <= max(F32_TOL, e_oracle)), (e_ref, e_truth, e_oracle)
+
+
+def _truth(st, ints, oracle):
+    t = cases.OrderedDict((k, v.astype(np.float64)) for k, v in st.items())
+    oracle(t, ints)
+    return t
+
+
+def _run_f32(make, oracle, gpu):
+    st, ints = make()
+    ref, out = cases.copy_state(st), cases.copy_state(st)
+    truth = _truth(st, ints, oracle)
+    oracle(ref, ints)
+    gpu(out, ints)
+    return ref, out, truth, ints
+
+
 def _run_both(make, oracle, gpu):
     st, ints = make()
     ref = cases.copy_state(st)
@@ -46,10 +74,11 @@ def test_affine_ls(sizes, seeded):
                                           ((64, 16, 64, 32), True),
                                           ((300, 129, 200, 10), False)])
 def test_mlp2_ce_b(sizes, seeded):
-    ref, out, ints, _, _ = _run_both(lambda: cases.mlp_state(*sizes, seeded=seeded),
+    ref, out, truth, ints = _run_f32(lambda: cases.mlp_state(*sizes, seeded=seeded),
                                      cases.oracle_mlp, cases.gpu_mlp)
     for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
-        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+        ok, errs = f32_verdict(out[k], ref[k], truth[k])
+        assert ok, (k, errs)
     for k in ("hb", "zb", "pb"):
         assert np.all(out[k] == 0.0), k
 
@@ -58,10 +87,11 @@ def test_mlp2_ce_b(sizes, seeded):
 def test_mlp2_ce_b_simt_path(sizes, monkeypatch):
     """The CUDA-core contraction path (STADE_MLP_GEMM=simt) stays correct."""
     monkeypatch.setenv("STADE_MLP_GEMM", "simt")
-    ref, out, ints, _, _ = _run_both(lambda: cases.mlp_state(*sizes, seeded=True),
+    ref, out, truth, ints = _run_f32(lambda: cases.mlp_state(*sizes, seeded=True),
                                      cases.oracle_mlp, cases.gpu_mlp)
     for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
-        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+        ok, errs = f32_verdict(out[k], ref[k], truth[k])
+        assert ok, (k, errs)
 
 
 def test_mlp2_ce_b_deterministic():
@@ -107,10 +137,11 @@ def test_heat2d_b_homogeneity_medium():
 @pytest.mark.parametrize("sizes,seeded", [((2, 3, 30, 4, 5), True), ((4, 16, 200, 32, 9), False),
                                           ((1, 1, 9, 1, 9), True), ((3, 64, 140, 128, 9), False)])
 def test_conv1d_relu_mse_b(sizes, seeded):
-    ref, out, ints, _, _ = _run_both(lambda: cases.conv_state(*sizes, seeded=seeded),
+    ref, out, truth, ints = _run_f32(lambda: cases.conv_state(*sizes, seeded=seeded),
                                      cases.oracle_conv, cases.gpu_conv)
     for k in ("z", "r", "tb", "wb", "xb", "loss"):
-        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+        ok, errs = f32_verdict(out[k], ref[k], truth[k])
+        assert ok, (k, errs)
     for k in ("zb", "rb"):
         assert np.all(out[k] == 0.0), k
 
@@ -129,19 +160,33 @@ def test_mlp2_ce_hv(sizes, seeded, xd):
         assert np.all(out[k] == 0.0), k
 
 
+@pytest.mark.parametrize("path", ["tma", "tc"])
 @pytest.mark.parametrize("sizes,seeded", [((256, 784, 512, 10), False),
                                           ((300, 132, 200, 10), True),
                                           ((1000, 784, 512, 10), True),
-                                          ((129, 4, 8, 3), True)])
-def test_mlp2_ce_b_tensor_core_path(sizes, seeded, monkeypatch):
-    """The tcgen05 3xTF32 contractions (M, N and K tails included) against the
-    oracle, and no bounded wait ran out."""
+                                          ((129, 4, 8, 3), True),
+                                          ((2000, 68, 260, 10), True)])
+def test_mlp2_ce_b_tensor_core_path(sizes, seeded, path, monkeypatch):
+    """The tcgen05 3xTF32 contractions, TMA-fed (default) and transform-fed,
+    against the oracle (M, N and K tails included), and no bounded wait ran
+    out."""
     from stadeb200 import _lib
-    monkeypatch.setenv("STADE_MLP_GEMM", "tc")
-    ref, out, ints, _, _ = _run_both(lambda: cases.mlp_state(*sizes, seeded=seeded),
+    monkeypatch.setenv("STADE_MLP_GEMM", path)
+    ref, out, truth, ints = _run_f32(lambda: cases.mlp_state(*sizes, seeded=seeded),
                                      cases.oracle_mlp, cases.gpu_mlp)
     assert _lib.lib().stade_device_error() == 0
     for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
-        assert rel_err(out[k], ref[k]) <= F32_TOL, (k, rel_err(out[k], ref[k]))
+        ok, errs = f32_verdict(out[k], ref[k], truth[k])
+        assert ok, (k, errs)
     for k in ("hb", "zb", "pb"):
         assert np.all(out[k] == 0.0), k
+
+
+def test_mlp2_ce_b_large_batch_vs_truth():
+    """4096 samples at the full widths: every output within 1e-5 of the exact
+    result (the sweep in Float64) or at least as close as the Float32 oracle."""
+    ref, out, truth, ints = _run_f32(lambda: cases.mlp_state(4096, 784, 512, 10, seeded=True),
+                                     cases.oracle_mlp, cases.gpu_mlp)
+    for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
+        ok, errs = f32_verdict(out[k], ref[k], truth[k])
+        assert ok, (k, errs)
