@@ -386,6 +386,100 @@ mlp_s1b_w2b_kernel(const float* __restrict__ h, float* __restrict__ hb,
   }
 }
 
+// The s1b pass of the TMA path, four adjacent hidden units per thread
+// (16-byte loads and stores): s1b = (1 - h^2) (hb + sum_c w2[k, c] g[s, c]),
+// c descending (the generated order), written as TF32 hi / lo planes; hb
+// consumed to zero; the chunk's W2b (sum_s h g), b2b (sum_s g) and b1b
+// (sum_s s1b) partials. NO = the class count rounded to a template (exact
+// for 10 classes). Block = 128 threads x 4 units = 512 units of a chunk of
+// samples; partial record [chunk][n_h*n_o (W2b) + n_o (b2b) + n_h (b1b)].
+template <int NO>
+__global__ void __launch_bounds__(128)
+mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
+                      const float* __restrict__ gbuf, const float* __restrict__ w2,
+                      float* __restrict__ s1b_hi, float* __restrict__ s1b_lo, int n_s, int n_h,
+                      int n_o, int chunk, float* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  float* gs = reinterpret_cast<float*>(smraw);  // chunk x NO (zero padded)
+  const int s0 = blockIdx.x * chunk;
+  const int ns = min(n_s, s0 + chunk) - s0;
+  for (int e = threadIdx.x; e < ns * NO; e += blockDim.x) {
+    const int i = e / NO, c = e % NO;
+    gs[e] = c < n_o ? gbuf[(int64_t)(s0 + i) * n_o + c] : 0.f;
+  }
+  __syncthreads();
+  float* my = part + (int64_t)blockIdx.x * (n_h * n_o + n_o + n_h);
+  const int k = blockIdx.y * 512 + 4 * threadIdx.x;
+  if (k < n_h) {
+    float w[4][NO], a[4][NO];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int c = 0; c < NO; ++c) {
+        w[j][c] = c < n_o ? w2[(int64_t)(k + j) * n_o + c] : 0.f;
+        a[j][c] = 0.f;
+      }
+    float4 bsum = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto one = [&](int i, float4 hv, float4 acc4) {
+      const int64_t off = (int64_t)(s0 + i) * n_h + k;
+      const float* g = gs + i * NO;
+      float hh[4] = {hv.x, hv.y, hv.z, hv.w};
+      float ac[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+#pragma unroll
+      for (int c = NO - 1; c >= 0; --c) {
+        if (c < n_o) {
+          const float gc = g[c];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            ac[j] = __fadd_rn(ac[j], __fmul_rn(w[j][c], gc));
+            a[j][c] = fmaf(hh[j], gc, a[j][c]);
+          }
+        }
+      }
+      float o[4], hi[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[j] = __fmul_rn(__fadd_rn(1.f, -__fmul_rn(hh[j], hh[j])), ac[j]);
+        hi[j] = __uint_as_float(__float_as_uint(o[j]) & 0xFFFFE000u);
+      }
+      bsum.x += o[0]; bsum.y += o[1]; bsum.z += o[2]; bsum.w += o[3];
+      *reinterpret_cast<float4*>(s1b_hi + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<float4*>(s1b_lo + off) =
+          make_float4(o[0] - hi[0], o[1] - hi[1], o[2] - hi[2], o[3] - hi[3]);
+      *reinterpret_cast<float4*>(hb + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    int i = 0;
+    for (; i + 4 <= ns; i += 4) {
+      float4 hv[4], hbv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t off = (int64_t)(s0 + i + u) * n_h + k;
+        hv[u] = *reinterpret_cast<const float4*>(h + off);
+        hbv[u] = *reinterpret_cast<const float4*>(hb + off);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) one(i + u, hv[u], hbv[u]);
+    }
+    for (; i < ns; ++i) {
+      const int64_t off = (int64_t)(s0 + i) * n_h + k;
+      one(i, *reinterpret_cast<const float4*>(h + off), *reinterpret_cast<const float4*>(hb + off));
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int c = 0; c < NO; ++c)
+        if (c < n_o) my[(int64_t)(k + j) * n_o + c] = a[j][c];
+    float* bb = my + (int64_t)n_h * n_o + n_o;
+    bb[k] = bsum.x; bb[k + 1] = bsum.y; bb[k + 2] = bsum.z; bb[k + 3] = bsum.w;
+  }
+  if (blockIdx.y == 0 && threadIdx.x < n_o) {
+    const int c = threadIdx.x;
+    float acc = 0.f;
+    for (int i = 0; i < ns; ++i) acc += gs[i * NO + c];
+    my[(int64_t)n_h * n_o + c] = acc;
+  }
+}
+
 // W2b[k, c] partial = sum over the chunk's samples of h[s,k] g[s,c]; b2b[c]
 // partial = sum g[s,c]. One thread per k; partial layout [chunk][n_h*n_o + n_o].
 template <class T, int NO>
@@ -872,7 +966,7 @@ void mlp_hv_layout(Alloc& a, MlpF64HvWs* w, int64_t n_s, int64_t n_i, int64_t n_
 // Float32 adjoint
 // ============================================================================
 namespace {
-constexpr int kW2ChunkTc = 128;  // samples per W2b partial on the tensor-core path
+constexpr int kW2ChunkTc = 64;  // samples per W2b partial on the tensor-core paths
 
 struct MlpF32Ws {
   float *s1b, *gbuf, *loss_part, *w2_part, *w1_part, *zpart;
@@ -1010,11 +1104,12 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
     {
       PhaseScope ph("w2b", s);
       const int chunks = (S + kW2ChunkTc - 1) / kW2ChunkTc;
-      const size_t smem = sizeof(float) * (size_t)kW2ChunkTc * O;
-      auto kern = O <= 16 ? mlp_s1b_w2b_kernel<16, true> : mlp_s1b_w2b_kernel<32, true>;
-      kern<<<dim3(chunks, (H + 511) / 512), 256, smem, s>>>(h, hb, w.gbuf, w2, w.s1b_hi,
-                                                            w.s1b_lo, S, H, O, kW2ChunkTc,
-                                                            w.w2_part);
+      const int no = O == 10 ? 10 : O <= 16 ? 16 : 32;
+      const size_t smem = sizeof(float) * (size_t)kW2ChunkTc * no;
+      auto kern = O == 10 ? mlp_s1b_planes_kernel<10>
+                          : O <= 16 ? mlp_s1b_planes_kernel<16> : mlp_s1b_planes_kernel<32>;
+      kern<<<dim3(chunks, (H + 511) / 512), 128, smem, s>>>(h, hb, w.gbuf, w2, w.s1b_hi, w.s1b_lo,
+                                                            S, H, O, kW2ChunkTc, w.w2_part);
       STADE_CHECK_LAUNCH();
       finish_three_kernel<<<ceil_div_u(n_h * n_o + n_o + n_h, 256), 256, 0, s>>>(
           w.w2_part, chunks, n_h * n_o, w2b, n_o, b2b, n_h, b1b);

@@ -41,7 +41,10 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;  // 320
 constexpr int kTileBytes = 128 * BK * 4;        // 16 KiB
 constexpr int kStageBytes = 4 * kTileBytes;     // A hi, A lo, B hi, B lo
-constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 512;
+// stages + alignment slack + barrier block (256 B); the logits epilogue adds
+// kW2SmemBytes right after the barrier block
+constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 256;
+static_assert((2 * STAGES + 5) * 8 + 4 <= 256, "barrier block must fit in 256 bytes");
 constexpr uint32_t kTmemCols = 256;             // two 128-column accumulators
 constexpr long long kWaitCycles = 4000000000LL; // ~2 s at 1.9 GHz
 // K blocks per TMEM accumulation chain. The tensor core's Float32
@@ -166,7 +169,9 @@ struct EpiTanhLogits {  // h = tanh(acc + b1); zpart[part][m][c] = sum h w2 over
   const float* w2;
   float* zpart;
   int ld, M, N, n_o, parts_per_tile;
+  int w2_stride;  // > 0: w2 staged in shared memory with this row stride (multiple of 4)
 };
+constexpr int kW2SmemBytes = 32768;
 struct EpiAccumulate {  // out[m, n] += acc
   float* out;
   int ld, M, N;
@@ -361,6 +366,18 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
     const int e = warp - 2;
     const int quad = warp & 3;       // TMEM lanes 32 quad .. 32 quad + 31
     const int half = e >> 2;         // column half of the tile
+    // logits epilogue: all of w2 in shared memory, rows padded to w2_stride
+    // (16-byte aligned: the barrier block is 1024-aligned and uses < 256 bytes)
+    float* w2s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
+    if constexpr (EPI_KIND == 0) {
+      if (el.w2_stride > 0) {
+        for (int i = threadIdx.x - 64; i < el.N * el.w2_stride; i += kEpiWarps * 32) {
+          const int kk = i / el.w2_stride, c = i % el.w2_stride;
+          w2s[i] = c < el.n_o ? el.w2[(int64_t)kk * el.n_o + c] : 0.f;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      }
+    }
     int chain = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -422,14 +439,33 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
               for (int i = 0; i < 16; ++i)
                 if (nn + i < el.N) o[i] = hv[i];
             }
-            // logits partial; w2 rows are the same for the whole warp (L1 broadcast)
+            // logits partial; w2 rows are the same for the whole warp (broadcast)
+            if (el.w2_stride > 0) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              if (nn + i < el.N) {
-                const float* wr = el.w2 + (int64_t)(nn + i) * el.n_o;
+              for (int i = 0; i < 16; ++i) {
+                if (nn + i < el.N) {
+                  const float4* wr = reinterpret_cast<const float4*>(w2s + (nn + i) * el.w2_stride);
 #pragma unroll
-                for (int cc = 0; cc < NO; ++cc)
-                  if (cc < el.n_o) zp[cc] = fmaf(hv[i], __ldg(wr + cc), zp[cc]);
+                  for (int c4 = 0; c4 < NO / 4; ++c4) {
+                    if (4 * c4 < el.n_o) {
+                      const float4 wv = wr[c4];
+                      zp[4 * c4] = fmaf(hv[i], wv.x, zp[4 * c4]);
+                      zp[4 * c4 + 1] = fmaf(hv[i], wv.y, zp[4 * c4 + 1]);
+                      zp[4 * c4 + 2] = fmaf(hv[i], wv.z, zp[4 * c4 + 2]);
+                      zp[4 * c4 + 3] = fmaf(hv[i], wv.w, zp[4 * c4 + 3]);
+                    }
+                  }
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                if (nn + i < el.N) {
+                  const float* wr = el.w2 + (int64_t)(nn + i) * el.n_o;
+#pragma unroll
+                  for (int cc = 0; cc < NO; ++cc)
+                    if (cc < el.n_o) zp[cc] = fmaf(hv[i], __ldg(wr + cc), zp[cc]);
+                }
               }
             }
           }
@@ -533,11 +569,12 @@ stade_status run(const Operand& A, const Operand& B, Geometry g, const EpiTanhLo
   if (st != STADE_OK) return st;
   st = operand_maps(B, &bh, &bl);
   if (st != STADE_OK) return st;
+  const int smem = kSmemBytes + (EPI_KIND == 0 && el.w2_stride > 0 ? kW2SmemBytes : 0);
   STADE_CUDA(cudaFuncSetAttribute(tma_gemm_kernel<EPI_KIND, NO>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int total = g.m_tiles * g.n_tiles * g.slices;
   const int grid = total < sm_count() ? total : sm_count();
-  tma_gemm_kernel<EPI_KIND, NO><<<grid, kThreads, kSmemBytes, s>>>(ah, al, bh, bl, g, el, ea, ep);
+  tma_gemm_kernel<EPI_KIND, NO><<<grid, kThreads, smem, s>>>(ah, al, bh, bl, g, el, ea, ep);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }
@@ -624,7 +661,9 @@ stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const
   tma::Operand A{x_hi, x_lo, S, I, I, false};
   tma::Operand B{w1_hi, w1_lo, I, H, H, true};
   tma::Geometry g = tma::geometry(S, H, I, 1, false, true);
-  tma::EpiTanhLogits el{h, b1, w2, zpart, H, S, H, O, 2};
+  const int stride = (O + 3) / 4 * 4;
+  const bool smem_w2 = (int64_t)H * stride * 4 <= tma::kW2SmemBytes;
+  tma::EpiTanhLogits el{h, b1, w2, zpart, H, S, H, O, 2, smem_w2 ? stride : 0};
   if (O <= 16) return tma::run<0, 16>(A, B, g, el, {}, {}, s);
   return tma::run<0, 32>(A, B, g, el, {}, {}, s);
 }
