@@ -195,12 +195,20 @@ def roofline(phases, phase_work, steps, peaks, peak_src, traffic):
         achieved = work / avg_s / 1e9
         peak = peaks["hbm_gbs"]
         unit = "GB/s"
+    elif kind == "fp64":
+        # no measured FP64 peak exists in MEASURED_PEAKS.json: the nominal B200
+        # FP64 (vector and tensor) rate, 148 SMs x 64 DFMA/clk x 2 x 1.965 GHz
+        achieved = work / avg_s / 1e12
+        peak = 37.2
+        unit = "TFLOP/s"
+        peak_src = "nominal fp64 (no measured figure)"
     else:
         achieved = work / avg_s / 1e12
         peak = peaks["bf16_tflops"]
         unit = "TFLOP/s"
     total_ms = sum(v[0] for v in phases.values())
-    return {"bound": "hbm" if kind == "hbm" else "tensor", "kernel": name, "achieved": achieved,
+    return {"bound": "hbm" if kind == "hbm" else "tensor", "pipe": kind, "kernel": name,
+            "achieved": achieved,
             "peak": peak, "unit": unit, "frac": achieved / peak, "peak_source": peak_src,
             "traffic": traffic.get(name) if traffic else None,
             "launch_ms": ms / cnt, "share_of_step": ms / total_ms if total_ms else None,
@@ -473,7 +481,164 @@ class AffineLs:
                 "sample": f"{reps} full evaluations (oracle.cc, serial), {t:.2f} s"}
 
 
-WORKLOADS = {"mlp2_ce": Mlp2Ce, "heat2d": Heat2d, "affine_ls": AffineLs}
+class Conv1dReluMse:
+    name = "conv1d_relu_mse"
+    dtype = "f32"
+    scaling = "weak"
+
+    def __init__(self, torch, rank, world, comm_factory):
+        import numpy as np
+        from stadeb200 import synth, kernels
+        self.torch, self.np, self.kernels = torch, np, kernels
+        c = synth.FULL["conv1d_relu_mse"]
+        self.B, self.C, self.L, self.O, self.K = c["n_b"], c["n_c"], c["n_l"], c["n_o"], c["n_k"]
+        self.world = world
+        B, C, L, O, K = self.B, self.C, self.L, self.O, self.K
+        self.nt = B * O * (L - K + 1)
+        d = synth.conv1d_relu_mse_inputs(B, C, L, O, K)
+        f32 = torch.float32
+        self.pinned = {k: torch.from_numpy(v).pin_memory() for k, v in d.items()}
+        t = {k: v.to("cuda") for k, v in self.pinned.items()}
+        z = lambda m: torch.zeros(m, dtype=f32, device="cuda")
+        t.update(loss=z(1), xb=z(B * C * L), wb=z(O * C * K), tb=z(self.nt), z=z(self.nt),
+                 zb=z(self.nt), r=z(self.nt), rb=z(self.nt))
+        self.t = t
+        self.ws = torch.empty(kernels.conv1d_relu_mse_b_workspace(B, C, L, O, K), dtype=torch.uint8,
+                              device="cuda")
+        self.grad_host = {k: torch.empty(t[k].numel(), dtype=f32).pin_memory()
+                          for k in ("wb", "loss")}
+
+    def step(self):
+        t = self.t
+        for k in ("wb", "xb", "tb", "loss"):
+            t[k].zero_()
+        self.kernels.conv1d_relu_mse_b_cuda(t["loss"], t["lossb"], t["x"], t["xb"], t["w"], t["wb"],
+                                            t["t"], t["tb"], t["z"], t["zb"], t["r"], t["rb"],
+                                            self.B, self.C, self.L, self.O, self.K,
+                                            workspace=self.ws)
+
+    def e2e_step(self):
+        t, p = self.t, self.pinned
+        for k in ("x", "w", "t"):
+            t[k].copy_(p[k], non_blocking=True)
+        self.step()
+        for k, v in self.grad_host.items():
+            v.copy_(t[k], non_blocking=True)
+
+    def e2e_bytes(self):
+        h2d = sum(self.pinned[k].numel() * 4 for k in ("x", "w", "t"))
+        return h2d, sum(v.numel() * 4 for v in self.grad_host.values())
+
+    def phase_work(self):
+        fl = 2.0 * self.B * self.O * (self.L - self.K + 1) * self.C * self.K
+        return {"conv_fwd": ("tensor", fl, "implicit GEMM 2 B O Lo C K flops + elementwise"),
+                "conv_wgrad": ("tensor", fl, "weight gradient 2 B O Lo C K flops"),
+                "conv_xgrad": ("tensor", fl, "input gradient 2 B O Lo C K flops")}
+
+    def config(self):
+        return {"workload": "C4 conv1d_relu_mse_b: 1-D conv 128x64x9 + ReLU + MSE adjoint, batch "
+                            "4096 x 64 x 2048, Float32", "n_b": self.B, "n_c": self.C,
+                "n_l": self.L, "n_o": self.O, "n_k": self.K,
+                "parallelism": f"replicas{self.world}", "l2": "inputs larger than L2"}
+
+    def cpu_baseline(self, seconds):
+        np = self.np
+        from oracle import oracle as orc
+        from stadeb200 import synth
+        b = 12
+        C, L, O, K = self.C, self.L, self.O, self.K
+        d = synth.conv1d_relu_mse_inputs(b, C, L, O, K)
+        nt = b * O * (L - K + 1)
+        z = lambda m: np.zeros(m, np.float32)
+        t0 = time.perf_counter()
+        orc.conv1d_relu_mse_b(z(1), d["lossb"], d["x"], z(b * C * L), d["w"], z(O * C * K), d["t"],
+                              z(nt), z(nt), z(nt), z(nt), z(nt), b, C, L, O, K)
+        t = time.perf_counter() - t0
+        return {"value": b / (t * self.B), "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"{b} of {self.B} samples (oracle.cc, serial), {t:.2f} s, scaled"}
+
+
+class Mlp2CeHv:
+    name = "mlp2_ce_hv"
+    dtype = "f64"
+    scaling = "weak"
+
+    def __init__(self, torch, rank, world, comm_factory):
+        import numpy as np
+        from stadeb200 import synth, kernels
+        self.torch, self.np, self.kernels = torch, np, kernels
+        c = synth.FULL["mlp2_ce_hv"]
+        self.S, self.I, self.H, self.O = c["n_s"], c["n_i"], c["n_h"], c["n_o"]
+        self.world = world
+        d = synth.mlp2_ce_hv_inputs(self.S, self.I, self.H, self.O)
+        self.pinned = {k: torch.from_numpy(v).pin_memory() for k, v in d.items()}
+        t = {k: v.to("cuda") for k, v in self.pinned.items()}
+        S, I, H, O = self.S, self.I, self.H, self.O
+        for name in kernels.MLP_HV_ARGS + kernels.MLP_HV_TAN:
+            if name not in t:
+                t[name] = torch.zeros(kernels._mlp_len(name, S, I, H, O), dtype=torch.float64,
+                                      device="cuda")
+        self.t = t
+        self.ws = torch.empty(kernels.mlp2_ce_hv_workspace(S, I, H, O), dtype=torch.uint8,
+                              device="cuda")
+        self.out_names = ("w1bd", "b1bd", "w2bd", "b2bd", "lossd")
+        self.grad_host = {k: torch.empty(t[k].numel(), dtype=torch.float64).pin_memory()
+                          for k in self.out_names}
+
+    def step(self):
+        t = self.t
+        for k in ("w1b", "b1b", "w2b", "b2b", "w1bd", "b1bd", "w2bd", "b2bd", "xb", "xbd", "yb",
+                  "ybd", "loss", "lossd"):
+            t[k].zero_()
+        self.kernels.mlp2_ce_hv_cuda(*[t[a] for a in self.kernels.MLP_HV_ARGS], self.S, self.I,
+                                     self.H, self.O, *[t[a] for a in self.kernels.MLP_HV_TAN],
+                                     workspace=self.ws)
+
+    def e2e_step(self):
+        t, p = self.t, self.pinned
+        for k in ("x", "y", "w1", "b1", "w2", "b2", "w1d", "b1d", "w2d", "b2d"):
+            t[k].copy_(p[k], non_blocking=True)
+        self.step()
+        for k, v in self.grad_host.items():
+            v.copy_(t[k], non_blocking=True)
+
+    def e2e_bytes(self):
+        h2d = sum(self.pinned[k].numel() * 8 for k in ("x", "y", "w1", "b1", "w2", "b2", "w1d",
+                                                         "b1d", "w2d", "b2d"))
+        return h2d, sum(v.numel() * 8 for v in self.grad_host.values())
+
+    def phase_work(self):
+        u = 2.0 * self.S * self.I * self.H
+        return {"hv_fwd_gemms": ("fp64", 3 * u, "x W1, x W1d + xd W1 (3 units of 2 S I H flops)"),
+                "hv_w1b_gemms": ("fp64", 3 * u, "x^T s1b, x^T s1bd + xd^T s1b (3 units)"),
+                "hv_xb_gemms": ("fp64", 3 * u, "s1b W1^T, s1bd W1^T + s1b W1d^T (3 units)")}
+
+    def config(self):
+        return {"workload": "C5 mlp2_ce_hv: HVP of the C2 loss, batch 16384, Float64, direction "
+                            "over all 407,050 parameters", "n_s": self.S, "n_i": self.I,
+                "n_h": self.H, "n_o": self.O, "parallelism": f"replicas{self.world}",
+                "l2": "inputs larger than L2 and L2 flushed between steps"}
+
+    def cpu_baseline(self, seconds):
+        np = self.np
+        from oracle import oracle as orc
+        from stadeb200 import synth, kernels
+        m = 256
+        S, I, H, O = m, self.I, self.H, self.O
+        d = synth.mlp2_ce_hv_inputs(S, I, H, O)
+        arrs = {}
+        for name in kernels.MLP_HV_ARGS + kernels.MLP_HV_TAN:
+            arrs[name] = d[name].copy() if name in d else np.zeros(kernels._mlp_len(name, S, I, H, O))
+        t0 = time.perf_counter()
+        orc.mlp2_ce_hv(*[arrs[a] for a in kernels.MLP_HV_ARGS], S, I, H, O,
+                       *[arrs[a] for a in kernels.MLP_HV_TAN])
+        t = time.perf_counter() - t0
+        return {"value": m / (t * self.S), "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"{m} of {self.S} samples (oracle.cc, serial), {t:.2f} s, scaled"}
+
+
+WORKLOADS = {"mlp2_ce": Mlp2Ce, "heat2d": Heat2d, "affine_ls": AffineLs,
+             "conv1d_relu_mse": Conv1dReluMse, "mlp2_ce_hv": Mlp2CeHv}
 
 
 # ---------------------------------------------------------------------------

@@ -52,9 +52,11 @@ struct PhaseScope {
   PhaseScope(const char* name, cudaStream_t st) : on(profile_on()), s(st) {
     if (on) phase_begin(name, s);
   }
-  ~PhaseScope() {
+  void end() {
     if (on) phase_end(s);
+    on = false;
   }
+  ~PhaseScope() { end(); }
 };
 
 // ---- options --------------------------------------------------------------

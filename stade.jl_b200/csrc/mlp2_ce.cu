@@ -1271,6 +1271,7 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   }
   if (st != STADE_OK) return st;
   // head
+  PhaseScope ph_head("hv_head", s);
   const size_t smem = 2 * sizeof(double) * (size_t)(n_h * n_o);
   STADE_REQUIRE(smem <= 200 * 1024, "mlp2_ce_hv: n_h * n_o too large");
   if (O <= 16) {
@@ -1304,22 +1305,29 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   finish_four_kernel<<<ceil_div_u(2 * n_h * n_o + 2 * n_o, 256), 256, 0, s>>>(
       w.w2_part, w.w2_chunks, n_h * n_o, O, w2b, w2bd, b2b, b2bd);
   STADE_CHECK_LAUNCH();
+  ph_head.end();
   // W1b (+ b1b); W1bd = x^T s1bd + xd^T s1b (+ b1bd)
-  st = gemm_simt<double, RM, RN, BK, false, true>(
-      I + 1, H, S, LdXtOnes<double>{x, I, I}, LdB<double>{w.s1b, H},
-      EpiWeightBias<double>{{}, w1b, b1b, I, H}, w.w1_part, w.w1_splits, s);
-  if (st != STADE_OK) return st;
-  st = gemm_simt<double, RM, RN, BK, false, true>(
-      I + 1, H, 2 * S, LdXtOnes2{x, xd, I, I, S}, LdB2{w.s1bd, w.s1b, H, S},
-      EpiWeightBias<double>{{}, w1bd, b1bd, I, H}, w.w1_part, w.w1d_splits, s);
+  {
+    PhaseScope ph("hv_w1b_gemms", s);
+    st = gemm_simt<double, RM, RN, BK, false, true>(
+        I + 1, H, S, LdXtOnes<double>{x, I, I}, LdB<double>{w.s1b, H},
+        EpiWeightBias<double>{{}, w1b, b1b, I, H}, w.w1_part, w.w1_splits, s);
+    if (st == STADE_OK)
+      st = gemm_simt<double, RM, RN, BK, false, true>(
+          I + 1, H, 2 * S, LdXtOnes2{x, xd, I, I, S}, LdB2{w.s1bd, w.s1b, H, S},
+          EpiWeightBias<double>{{}, w1bd, b1bd, I, H}, w.w1_part, w.w1d_splits, s);
+  }
   if (st != STADE_OK) return st;
   // xb += s1b W1^T; xbd += s1bd W1^T + s1b W1d^T
-  st = gemm_simt<double, RM, RN, BK, true, false>(S, I, H, LdRow<double>{w.s1b, H},
-                                                   LdBT<double>{w1, H}, EpiAddTo<double>{{}, xb, I},
-                                                   nullptr, 1, s);
-  if (st != STADE_OK) return st;
-  st = gemm_simt<double, RM, RN, BK, true, false>(
-      S, I, 2 * H, LdRow2{w.s1bd, w.s1b, H, H}, LdBT2{w1, w1d, H, H},
-      EpiAddTo<double>{{}, xbd, I}, nullptr, 1, s);
+  {
+    PhaseScope ph("hv_xb_gemms", s);
+    st = gemm_simt<double, RM, RN, BK, true, false>(S, I, H, LdRow<double>{w.s1b, H},
+                                                     LdBT<double>{w1, H},
+                                                     EpiAddTo<double>{{}, xb, I}, nullptr, 1, s);
+    if (st == STADE_OK)
+      st = gemm_simt<double, RM, RN, BK, true, false>(
+          S, I, 2 * H, LdRow2{w.s1bd, w.s1b, H, H}, LdBT2{w1, w1d, H, H},
+          EpiAddTo<double>{{}, xbd, I}, nullptr, 1, s);
+  }
   return st;
 }

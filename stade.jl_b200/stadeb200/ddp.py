@@ -38,6 +38,10 @@ class KernelSig:
     kinds: dict
     written: frozenset
     reduced_outputs: frozenset
+    # arrays whose writes all add the array to itself at an index that varies
+    # with an enclosing loop: a per-sample result or a cross-sample sum, which
+    # the caller must resolve (ddpgen_reduced_outputs, src/STADE.jl:17282)
+    ambiguous: frozenset = frozenset()
 
 
 def adjoint_layout(sig: KernelSig) -> list:
@@ -61,21 +65,55 @@ def hvp_layout(sig: KernelSig) -> list:
     return out
 
 
-def derive_roles(sig: KernelSig, per_sample, mode: str, reduced=()) -> dict:
-    """Role of every buffer of the mode's layout (ddpgen_roles)."""
+def check_declaration(sig: KernelSig, per_sample, reduced=()) -> None:
+    """The refusals of ddpgen_check_declaration (src/STADE.jl:17218-17270):
+    names that are not float array arguments, duplicates, an array in both
+    lists, a per_sample array the kernel overwrites, a `reduced` array whose
+    role is already derived, and an ambiguous array left unresolved. Raises
+    ValueError with the reference's wording."""
     per_sample, reduced = list(per_sample), list(reduced)
     for kw, names in (("per_sample", per_sample), ("reduced", reduced)):
-        for p in names:
-            if p not in sig.args:
-                raise ValueError(f"{kw} names `{p}`, which is not an argument of {sig.name}")
-            if sig.kinds[p] != "array_float":
-                raise ValueError(f"{kw} names `{p}`, which is not a float array argument")
+        not_args = [p for p in names if p not in sig.args]
+        if not_args:
+            verb = "is" if len(not_args) == 1 else "are"
+            raise ValueError(f"{kw} names `{'`, `'.join(not_args)}`, which {verb} not an "
+                             f"argument of {sig.name}")
+        not_fa = [p for p in names if sig.kinds[p] != "array_float"]
+        if not_fa:
+            raise ValueError(f"{kw} names `{'`, `'.join(not_fa)}`, which is not a float array "
+                             "argument")
         dups = sorted({p for p in names if names.count(p) > 1})
         if dups:
             raise ValueError(f"{kw} names `{'`, `'.join(dups)}` more than once")
     both = [p for p in per_sample if p in reduced]
     if both:
-        raise ValueError(f"`{'`, `'.join(both)}` named in both per_sample and reduced")
+        raise ValueError(f"`{'`, `'.join(both)}` appears in per_sample and in reduced. An array "
+                         "is one or the other")
+    bad_ps = [p for p in per_sample if p in sig.written and p not in sig.ambiguous]
+    if bad_ps:
+        raise ValueError(f"per_sample names `{'`, `'.join(bad_ps)}`, which the kernel writes by "
+                         "plain overwrite. That array already takes a derived role, so naming it "
+                         "here would give it two")
+    bad_rd = [p for p in reduced if p not in sig.ambiguous]
+    if bad_rd:
+        raise ValueError(f"reduced names `{'`, `'.join(bad_rd)}`, whose role is already derived. "
+                         "`reduced` resolves an array whose writes are all additive at an index "
+                         "that varies with an enclosing loop, and no other")
+    unresolved = [a for a in sorted(sig.ambiguous) if a not in per_sample and a not in reduced]
+    if unresolved:
+        raise ValueError(f"`{'`, `'.join(unresolved)}` takes only additive writes at an index "
+                         "that varies with an enclosing loop. Two readings fit that shape and the "
+                         "kernel does not say which. Name it in `per_sample` if it holds one "
+                         "sample's own result, which needs no communication. Name it in `reduced` "
+                         "if it accumulates across samples, which is summed across ranks")
+
+
+def derive_roles(sig: KernelSig, per_sample, mode: str, reduced=()) -> dict:
+    """Role of every buffer of the mode's layout (ddpgen_roles)."""
+    if mode not in ("tangent", "adjoint", "hvp"):
+        raise ValueError(f"mode must be tangent, adjoint or hvp, got {mode}")
+    per_sample, reduced = list(per_sample), list(reduced)
+    check_declaration(sig, per_sample, reduced)
     all_reduced = set(sig.reduced_outputs) | set(reduced)
     roles = {}
     for a in sig.args:
@@ -123,6 +161,18 @@ MLP2_CE = KernelSig(
     kinds={**{a: "array_float" for a in ("loss", "x", "y", "w1", "b1", "w2", "b2", "h", "z", "p")},
            **{a: "scalar_int" for a in ("n_s", "n_i", "n_h", "n_o")}},
     written=frozenset({"h", "z", "p", "loss"}),
+    reduced_outputs=frozenset({"loss"}),
+)
+
+
+# The primal affine_ls (oracle/primals.jl): y is overwritten, every write of
+# loss adds to loss itself.
+AFFINE_LS = KernelSig(
+    name="affine_ls",
+    args=("loss", "w", "b", "x", "t", "y", "n_s", "n_o", "n_i"),
+    kinds={**{a: "array_float" for a in ("loss", "w", "b", "x", "t", "y")},
+           **{a: "scalar_int" for a in ("n_s", "n_o", "n_i")}},
+    written=frozenset({"y", "loss"}),
     reduced_outputs=frozenset({"loss"}),
 )
 
@@ -240,6 +290,62 @@ def check_replicas(comm: NcclComm, *bufs, names=None, stream=None) -> None:
                            "must hold identical values on every rank. The usual cause is a "
                            "per-sample array left out of per_sample")
     check(code)
+
+
+class NcclBackend:
+    """Epilogue operations on CUDA tensors through libstade_b200 (one bucketed
+    NCCL collective per call)."""
+
+    def __init__(self, comm: NcclComm, stream=None):
+        self.comm, self.stream = comm, stream
+
+    def zero(self, bufs):
+        zero_(*bufs, stream=self.stream)
+
+    def allreduce_sum(self, bufs, n_local=None):
+        return allreduce_sum_(self.comm, *bufs, n_local=n_local, stream=self.stream)
+
+    def check(self, bufs, names):
+        check_replicas(self.comm, *bufs, names=names, stream=self.stream)
+
+
+class Epilogue:
+    """The five functions the reference's `stade_ddp_file` writes for one
+    kernel and mode (ddpgen_emit, src/STADE.jl:17578-17696), driven by the
+    role table: reset_accum / reset_reduced / reset_local zero the :accum,
+    :reduced and :local buffers, allreduce_accum sums :accum across ranks with
+    the sample count and returns the global count, allreduce_reduced sums
+    :reduced, check_replicas checks :shared and :seed buffers for agreement.
+    `bank` maps buffer names to the caller's arrays; the backend does the
+    work (NcclBackend on CUDA tensors)."""
+
+    def __init__(self, sig: KernelSig, per_sample, mode: str, backend, reduced=()):
+        if mode not in ("adjoint", "hvp"):
+            raise ValueError("an epilogue exists for the adjoint and hvp modes")
+        self.sig, self.mode, self.backend = sig, mode, backend
+        self.roles = derive_roles(sig, per_sample, mode, reduced)
+        r = lambda want: role_args(sig, self.roles, mode, want)
+        self.accum, self.reduced, self.local = r("accum"), r("reduced"), r("local")
+        self.checked = r("shared") + r("seed")
+        self.returned = [b for b, v in self.roles.items() if v == "returned"]
+
+    def reset_accum(self, bank):
+        self.backend.zero([bank[b] for b in self.accum])
+
+    def reset_reduced(self, bank):
+        self.backend.zero([bank[b] for b in self.reduced])
+
+    def reset_local(self, bank):
+        self.backend.zero([bank[b] for b in self.local])
+
+    def allreduce_accum(self, bank, n_local: int) -> int:
+        return self.backend.allreduce_sum([bank[b] for b in self.accum], n_local=n_local)
+
+    def allreduce_reduced(self, bank):
+        self.backend.allreduce_sum([bank[b] for b in self.reduced])
+
+    def check_replicas(self, bank):
+        self.backend.check([bank[b] for b in self.checked], self.checked)
 
 
 # ---- generated names of the mlp2_ce epilogue (adjoint mode) ------------------

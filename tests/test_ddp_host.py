@@ -1,0 +1,317 @@
+"""Host logic of the data-parallel epilogue, on the CPU.
+
+Role tables and refusals restate test/validate_ddp_roles.jl (hand-written
+tables for the val-corpus subjects, the refusal list with its message
+fragments). The rank-invariance tests restate test/validate_ddp.jl
+(batch_run, :97 and :160-179): each of two `gloo` ranks runs the oracle sweep
+on its own samples between the epilogue's resets and sums, and the summed
+:accum / :reduced buffers must match one run over all samples within
+rtol 1e-12; the global sample count comes back from allreduce_accum. The
+epilogue here runs through ddp.Epilogue, the class the CUDA path drives with
+the NCCL backend, with a gloo backend over numpy arrays standing in for it.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from stadeb200 import ddp
+
+A = "array_float"
+I = "scalar_int"
+
+
+def sig(name, args, floats, written, reduced_outputs, ambiguous=()):
+    kinds = {a: (A if a in floats else I) for a in args}
+    return ddp.KernelSig(name, tuple(args), kinds, frozenset(written),
+                         frozenset(reduced_outputs), frozenset(ambiguous))
+
+
+# the val-corpus subjects of validate_ddp_roles.jl, with the write facts their
+# bodies show (test/val-corpus/<name>.jl)
+SUBJECTS = {
+    "ddp_affine": sig("ddp_affine", ["loss", "u", "a", "b", "v", "i_n"],
+                      {"loss", "u", "a", "b", "v"}, {"v", "loss"}, {"loss"}),
+    "ddp_twoparam": sig("ddp_twoparam", ["loss", "u", "w", "b", "h", "o", "i_n", "i_m"],
+                        {"loss", "u", "w", "b", "h", "o"}, {"h", "o", "loss"}, {"loss"}),
+    "ddp_ragged": sig("ddp_ragged", ["loss", "u", "a", "v", "i_n", "m0"],
+                      {"loss", "u", "a", "v"}, {"v", "loss"}, {"loss"}),
+    "ddp_branch": sig("ddp_branch", ["loss", "u", "a", "b", "v", "i_n"],
+                      {"loss", "u", "a", "b", "v"}, {"v", "loss"}, {"loss"}),
+    "ddp_tangent_input": sig("ddp_tangent_input", ["loss", "u", "a", "v", "i_n"],
+                             {"loss", "u", "a", "v"}, {"v", "loss"}, {"loss"}),
+    "ddp_batch_hist": sig("ddp_batch_hist", ["loss", "u", "a", "hist", "v", "i_n", "i_k"],
+                          {"loss", "u", "a", "hist", "v"}, {"v", "hist", "loss"}, {"loss"},
+                          {"hist"}),
+    "affine_loss": sig("affine_loss", ["loss", "u", "a", "b", "v", "i_n"],
+                       {"loss", "u", "a", "b", "v"}, {"v", "loss"}, {"loss"}),
+    "matvec_loss": sig("matvec_loss", ["loss", "a", "u", "v", "i_m", "i_n"],
+                       {"loss", "a", "u", "v"}, {"v", "loss"}, {"loss"}, {"v"}),
+    "ddp_written_per_sample": sig("ddp_written_per_sample", ["loss", "u", "a", "v", "i_n"],
+                                  {"loss", "u", "a", "v"}, {"v", "loss"}, {"loss"}),
+    "ddp_ambiguous_reduce": sig("ddp_ambiguous_reduce", ["loss", "u", "a", "v", "i_n"],
+                                {"loss", "u", "a", "v"}, {"v", "loss"}, {"loss"}, {"v"}),
+}
+
+EXPECTED = {
+    "ddp_affine": (["u"], {}, dict(loss="reduced", lossb="seed", u="per_sample", ub="local",
+                                   a="shared", ab="accum", b="shared", bb="accum", v="scratch",
+                                   vb="local")),
+    "ddp_twoparam": (["u"], {}, dict(loss="reduced", lossb="seed", u="per_sample", ub="local",
+                                     w="shared", wb="accum", b="shared", bb="accum",
+                                     h="scratch", hb="local", o="scratch", ob="local")),
+    "ddp_ragged": (["u"], {}, dict(loss="reduced", lossb="seed", u="per_sample", ub="local",
+                                   a="shared", ab="accum", v="scratch", vb="local")),
+    "ddp_branch": (["u"], {}, dict(loss="reduced", lossb="seed", u="per_sample", ub="local",
+                                   a="shared", ab="accum", b="shared", bb="accum", v="scratch",
+                                   vb="local")),
+    "ddp_tangent_input": (["u"], {}, dict(loss="reduced", lossb="seed", u="per_sample",
+                                          ub="local", a="shared", ab="accum", v="scratch",
+                                          vb="local")),
+    "ddp_batch_hist": (["u"], {"reduced": ["hist"]},
+                       dict(loss="reduced", lossb="seed", u="per_sample", ub="local",
+                            a="shared", ab="accum", hist="reduced", histb="seed", v="scratch",
+                            vb="local")),
+    "affine_loss": (["u"], {}, dict(loss="reduced", lossb="seed", u="per_sample", ub="local",
+                                    a="shared", ab="accum", b="shared", bb="accum", v="scratch",
+                                    vb="local")),
+}
+
+
+@pytest.mark.parametrize("name", sorted(EXPECTED))
+def test_role_table(name):
+    per_sample, kw, table = EXPECTED[name]
+    roles = ddp.derive_roles(SUBJECTS[name], per_sample, "adjoint", **kw)
+    assert roles == table
+
+
+def test_role_table_hvp_and_tangent():
+    roles = ddp.derive_roles(SUBJECTS["ddp_affine"], ["u"], "hvp")
+    assert roles["ad"] == "shared" and roles["abd"] == "accum" and roles["ab"] == "accum"
+    assert roles["lossd"] == "reduced" and roles["lossbd"] == "seed"
+    assert roles["vd"] == "scratch" and roles["vbd"] == "local"
+    t = ddp.derive_roles(SUBJECTS["ddp_affine"], ["u"], "tangent")
+    assert "ab" not in t and t["ad"] == "shared"
+
+
+@pytest.mark.parametrize("name,per_sample,reduced,fragment", [
+    ("ddp_written_per_sample", ["v"], [], "plain overwrite"),
+    ("ddp_ambiguous_reduce", ["u"], [], "does not say which"),
+    ("matvec_loss", ["u"], [], "does not say which"),
+    ("ddp_batch_hist", ["u"], [], "does not say which"),
+    ("ddp_affine", ["nosuch"], [], "not an argument"),
+    ("ddp_affine", ["i_n"], [], "not a float array argument"),
+    ("ddp_affine", ["u"], ["loss"], "already derived"),
+    ("ddp_batch_hist", ["hist"], ["hist"], "per_sample and in reduced"),
+    ("ddp_affine", ["u", "u"], [], "more than once"),
+])
+def test_refusals(name, per_sample, reduced, fragment):
+    with pytest.raises(ValueError, match=fragment):
+        ddp.derive_roles(SUBJECTS[name], per_sample, "adjoint", reduced)
+
+
+@pytest.mark.parametrize("name,per_sample,reduced,arr,cls", [
+    ("matvec_loss", ["u", "v"], [], "v", "scratch"),
+    ("ddp_batch_hist", ["u"], ["hist"], "hist", "reduced"),
+])
+def test_ambiguity_resolutions(name, per_sample, reduced, arr, cls):
+    assert ddp.derive_roles(SUBJECTS[name], per_sample, "adjoint", reduced)[arr] == cls
+
+
+def test_benchmark_kernels_roles():
+    r = ddp.derive_roles(ddp.MLP2_CE, ["x", "y"], "adjoint")
+    assert ddp.role_args(ddp.MLP2_CE, r, "adjoint", "accum") == ["w1b", "b1b", "w2b", "b2b"]
+    assert ddp.role_args(ddp.MLP2_CE, r, "adjoint", "reduced") == ["loss"]
+    assert ddp.role_args(ddp.MLP2_CE, r, "adjoint", "local") == ["xb", "yb", "hb", "zb", "pb"]
+    assert ddp.role_args(ddp.MLP2_CE, r, "adjoint", "shared") == ["w1", "b1", "w2", "b2"]
+    assert ddp.role_args(ddp.MLP2_CE, r, "adjoint", "seed") == ["lossb"]
+    h = ddp.derive_roles(ddp.MLP2_CE, ["x", "y"], "hvp")
+    assert ddp.role_args(ddp.MLP2_CE, h, "hvp", "accum") == [
+        "w1b", "b1b", "w2b", "b2b", "w1bd", "b1bd", "w2bd", "b2bd"]
+    a = ddp.derive_roles(ddp.AFFINE_LS, ["x", "t"], "adjoint")
+    assert ddp.role_args(ddp.AFFINE_LS, a, "adjoint", "accum") == ["wb", "bb"]
+    assert ddp.role_args(ddp.AFFINE_LS, a, "adjoint", "local") == ["xb", "tb", "yb"]
+
+
+@pytest.mark.parametrize("mode", ["block", "mod"])
+@pytest.mark.parametrize("n,p", [(6, 2), (7, 2), (5, 4), (65536, 8), (3, 4)])
+def test_shard_partition(mode, n, p):
+    seen = []
+    for r in range(p):
+        seen += list(ddp.shard(n, r, p, mode))
+    assert sorted(seen) == list(range(n))
+
+
+# ---------------------------------------------------------------------------
+class GlooBackend:
+    """The epilogue's three operations on numpy arrays over a gloo group."""
+
+    def __init__(self):
+        import torch.distributed as dist
+        self.dist = dist
+
+    def zero(self, bufs):
+        for b in bufs:
+            b[...] = 0
+
+    def allreduce_sum(self, bufs, n_local=None):
+        import torch
+        flat = torch.from_numpy(np.concatenate([b.ravel() for b in bufs]).astype(np.float64))
+        self.dist.all_reduce(flat)
+        off = 0
+        for b in bufs:
+            b[...] = flat[off:off + b.size].numpy().reshape(b.shape).astype(b.dtype)
+            off += b.size
+        if n_local is None:
+            return None
+        c = torch.tensor([n_local], dtype=torch.int64)
+        self.dist.all_reduce(c)
+        return int(c.item())
+
+    def check(self, bufs, names):
+        import torch
+        s = torch.tensor([[float(np.sum(b)), float(np.sum(np.abs(b)))] for b in bufs],
+                         dtype=torch.float64)
+        lo, hi = s.clone(), s.clone()
+        self.dist.all_reduce(lo, op=self.dist.ReduceOp.MIN)
+        self.dist.all_reduce(hi, op=self.dist.ReduceOp.MAX)
+        bad = [names[i] for i in range(len(bufs)) if not torch.equal(lo[i], hi[i])]
+        if bad:
+            raise RuntimeError(f"`{'`, `'.join(bad)}` differ across ranks")
+
+
+def _affine_bank(rows, n_o, n_i, full):
+    f = np.float64
+    m = len(rows)
+    bank = dict(loss=np.zeros(1, f), lossb=full["lossb"].copy(), w=full["w"].copy(),
+                wb=np.zeros(n_o * n_i, f), b=full["b"].copy(), bb=np.zeros(n_o, f),
+                x=full["x"].reshape(-1, n_i)[rows].ravel().copy(), xb=np.full(m * n_i, 7.0),
+                t=full["t"].reshape(-1, n_o)[rows].ravel().copy(), tb=np.full(m * n_o, 7.0),
+                y=np.zeros(m * n_o, f), yb=np.full(m * n_o, 7.0))
+    return bank
+
+
+def _affine_sweep(bank, m, n_o, n_i):
+    from oracle import oracle as orc
+    orc.affine_ls_b(bank["loss"], bank["lossb"], bank["w"], bank["wb"], bank["b"], bank["bb"],
+                    bank["x"], bank["xb"], bank["t"], bank["tb"], bank["y"], bank["yb"], m, n_o,
+                    n_i)
+
+
+def _mlp_bank(rows, n_i, n_h, n_o, full):
+    f = np.float64
+    m = len(rows)
+    z = lambda n: np.zeros(n, f)
+    return dict(loss=z(1), lossb=full["lossb"].copy(),
+                x=full["x"].reshape(-1, n_i)[rows].ravel().copy(), xb=np.full(m * n_i, 3.0),
+                y=full["y"].reshape(-1, n_o)[rows].ravel().copy(), yb=np.full(m * n_o, 3.0),
+                w1=full["w1"].copy(), w1b=np.full(n_i * n_h, 5.0), b1=full["b1"].copy(),
+                b1b=z(n_h), w2=full["w2"].copy(), w2b=z(n_h * n_o), b2=full["b2"].copy(),
+                b2b=z(n_o), h=z(m * n_h), hb=np.full(m * n_h, 2.0), z=z(m * n_o),
+                zb=np.full(m * n_o, 2.0), p=z(m * n_o), pb=np.full(m * n_o, 2.0))
+
+
+def _mlp_sweep(bank, m, n_i, n_h, n_o):
+    from oracle import oracle as orc
+    orc.mlp2_ce_b(*[bank[k] for k in ("loss", "lossb", "x", "xb", "y", "yb", "w1", "w1b", "b1",
+                                       "b1b", "w2", "w2b", "b2", "b2b", "h", "hb", "z", "zb", "p",
+                                       "pb")], m, n_i, n_h, n_o)
+
+
+def _rank_main(rank, world, port, case, mode, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from stadeb200 import synth
+        if case == "affine_ls":
+            n_s, n_o, n_i = 37, 6, 5
+            full = synth.affine_ls_inputs(n_s, n_o, n_i)
+            rows = list(ddp.shard(n_s, rank, world, mode))
+            bank = _affine_bank(rows, n_o, n_i, full)
+            epi = ddp.Epilogue(ddp.AFFINE_LS, ["x", "t"], "adjoint", GlooBackend())
+            sweep = lambda: _affine_sweep(bank, len(rows), n_o, n_i)
+        else:
+            n_s, n_i, n_h, n_o = 29, 11, 7, 4
+            full = synth.mlp2_ce_inputs(n_s, n_i, n_h, n_o, dtype=np.float64)
+            rows = list(ddp.shard(n_s, rank, world, mode))
+            bank = _mlp_bank(rows, n_i, n_h, n_o, full)
+            epi = ddp.Epilogue(ddp.MLP2_CE, ["x", "y"], "adjoint", GlooBackend())
+            sweep = lambda: _mlp_sweep(bank, len(rows), n_i, n_h, n_o)
+        epi.check_replicas(bank)
+        epi.reset_accum(bank)
+        epi.reset_reduced(bank)
+        epi.reset_local(bank)
+        sweep()
+        n_global = epi.allreduce_accum(bank, len(rows))
+        epi.allreduce_reduced(bank)
+        out = {b: bank[b].copy() for b in epi.accum + epi.reduced}
+        # a :shared buffer that differs on one rank is caught
+        if rank == 1:
+            bank[epi.checked[0]][0] += 1e-9
+        try:
+            epi.check_replicas(bank)
+            caught = None
+        except RuntimeError as e:
+            caught = str(e)
+        q.put((rank, n_global, out, caught))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _single_rank(case):
+    from stadeb200 import synth
+    if case == "affine_ls":
+        n_s, n_o, n_i = 37, 6, 5
+        full = synth.affine_ls_inputs(n_s, n_o, n_i)
+        bank = _affine_bank(list(range(n_s)), n_o, n_i, full)
+        epi = ddp.Epilogue(ddp.AFFINE_LS, ["x", "t"], "adjoint", GlooBackend())
+        epi.backend.zero([bank[b] for b in epi.accum + epi.reduced + epi.local])
+        _affine_sweep(bank, n_s, n_o, n_i)
+    else:
+        n_s, n_i, n_h, n_o = 29, 11, 7, 4
+        full = synth.mlp2_ce_inputs(n_s, n_i, n_h, n_o, dtype=np.float64)
+        bank = _mlp_bank(list(range(n_s)), n_i, n_h, n_o, full)
+        epi = ddp.Epilogue(ddp.MLP2_CE, ["x", "y"], "adjoint", GlooBackend())
+        epi.backend.zero([bank[b] for b in epi.accum + epi.reduced + epi.local])
+        _mlp_sweep(bank, n_s, n_i, n_h, n_o)
+    return n_s, {b: bank[b] for b in epi.accum + epi.reduced}
+
+
+@pytest.mark.parametrize("case", ["affine_ls", "mlp2_ce"])
+@pytest.mark.parametrize("mode", ["mod", "block"])
+def test_rank_invariance_gloo(case, mode):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, case, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        rank, n_global, out, caught = q.get(timeout=120)
+        res[rank] = (n_global, out, caught)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    n_s, ref = _single_rank(case)
+    for rank in (0, 1):
+        n_global, out, caught = res[rank]
+        assert n_global == n_s
+        assert caught is not None and "differ across ranks" in caught
+        for b, v in ref.items():
+            err = np.max(np.abs(out[b] - v)) / max(np.max(np.abs(v)), 1e-300)
+            assert err <= 1e-12, (b, err)
+    # both ranks hold the same sums
+    for b in ref:
+        assert np.array_equal(res[0][1][b], res[1][1][b])
