@@ -207,12 +207,18 @@ def roofline(phases, phase_work, steps, peaks, peak_src, traffic):
         peak = peaks["bf16_tflops"]
         unit = "TFLOP/s"
     total_ms = sum(v[0] for v in phases.values())
-    return {"bound": "hbm" if kind == "hbm" else "tensor", "pipe": kind, "kernel": name,
+    extra = {}
+    if kind == "tensor":
+        # 3xTF32: three TF32 MMAs per product, TF32 at half the bf16 rate
+        ceil = peak / 6.0
+        extra = {"ceiling_3xtf32": ceil, "frac_of_3xtf32_ceiling": achieved / ceil}
+    t = traffic.get(name) if traffic else None
+    return {**{"bound": "hbm" if kind == "hbm" else "tensor", "pipe": kind, "kernel": name,
             "achieved": achieved,
             "peak": peak, "unit": unit, "frac": achieved / peak, "peak_source": peak_src,
-            "traffic": traffic.get(name) if traffic else None,
+            "traffic": t,
             "launch_ms": ms / cnt, "share_of_step": ms / total_ms if total_ms else None,
-            "note": note}
+            "note": note}, **extra}
 
 
 def load_traffic(config):
