@@ -341,9 +341,13 @@ class Mlp2Ce:
 
 
 class Heat2d:
+    """C3. At N = 1 the generated signature (stade_heat2d_b_f64) on the whole
+    grid; at N > 1 the grid's rows split into one slab per rank
+    (stade_heat2d_b_f64_slab, a halo row to each neighbour per step over
+    NCCL): the grad-eval is fixed and its work split (strong scaling)."""
     name = "heat2d"
     dtype = "f64"
-    scaling = "weak"
+    scaling = "strong"
 
     def __init__(self, torch, rank, world, comm_factory):
         import numpy as np
@@ -353,17 +357,24 @@ class Heat2d:
         self.n, self.n_step, self.alpha = c["n"], c["n_step"], c["alpha"]
         self.world = world
         n = self.n
+        lo, hi = n * rank // world, n * (rank + 1) // world
+        self.rows = hi - lo
+        m = self.rows * n
         d = synth.heat2d_inputs(n)
         f64 = torch.float64
-        self.pinned = {"u": torch.from_numpy(d["u"]).pin_memory()}
-        z = lambda m: torch.zeros(m, dtype=f64, device="cuda")
+        self.pinned = {"u": torch.from_numpy(d["u"][lo * n:hi * n].copy()).pin_memory()}
+        z = lambda k: torch.zeros(k, dtype=f64, device="cuda")
         self.t = dict(loss=z(1), lossb=torch.ones(1, dtype=f64, device="cuda"),
-                      u=self.pinned["u"].to("cuda"), ub=z(n * n), un=z(n * n), unb=z(n * n),
-                      alphab=z(1))
-        self.stack = kernels.initstacks_heat2d_b_cuda(n, self.n_step)
-        self.ws = torch.empty(kernels.heat2d_b_workspace(n, self.n_step), dtype=torch.uint8,
-                              device="cuda")
-        self.out_host = torch.empty(n * n, dtype=f64).pin_memory()
+                      u=self.pinned["u"].to("cuda"), ub=z(m), un=z(m), unb=z(m), alphab=z(1))
+        self.comm = comm_factory() if world > 1 else None
+        if world > 1:
+            self.stack = kernels.initstacks_heat2d_b_slab_cuda(n, self.n_step, self.rows)
+            ws = kernels.heat2d_b_slab_workspace(n, self.n_step, self.rows)
+        else:
+            self.stack = kernels.initstacks_heat2d_b_cuda(n, self.n_step)
+            ws = kernels.heat2d_b_workspace(n, self.n_step)
+        self.ws = torch.empty(ws, dtype=torch.uint8, device="cuda")
+        self.out_host = torch.empty(m, dtype=f64).pin_memory()
         self.ab_host = torch.empty(1, dtype=f64).pin_memory()
 
     def step(self):
@@ -371,9 +382,15 @@ class Heat2d:
         t["ub"].zero_()
         t["loss"].zero_()
         t["alphab"].zero_()
-        self.kernels.heat2d_b_cuda_device(t["loss"], t["lossb"], t["u"], t["ub"], t["un"],
-                                          t["unb"], self.alpha, t["alphab"], self.n, self.n_step,
-                                          self.stack, workspace=self.ws)
+        if self.comm is None:
+            self.kernels.heat2d_b_cuda_device(t["loss"], t["lossb"], t["u"], t["ub"], t["un"],
+                                              t["unb"], self.alpha, t["alphab"], self.n,
+                                              self.n_step, self.stack, workspace=self.ws)
+        else:
+            self.kernels.heat2d_b_slab_cuda(t["loss"], t["lossb"], t["u"], t["ub"], t["un"],
+                                            t["unb"], self.alpha, t["alphab"], self.n,
+                                            self.n_step, self.stack, self.rows, self.comm,
+                                            workspace=self.ws)
 
     def e2e_step(self):
         self.t["u"].copy_(self.pinned["u"], non_blocking=True)
@@ -382,10 +399,11 @@ class Heat2d:
         self.ab_host.copy_(self.t["alphab"], non_blocking=True)
 
     def e2e_bytes(self):
-        return self.n * self.n * 8, self.n * self.n * 8 + 8
+        # per rank; the caller multiplies by the rank count for strong scaling
+        return self.rows * self.n * 8, self.rows * self.n * 8 + 8
 
     def phase_work(self):
-        N = float(self.n) * self.n
+        N = float(self.rows) * self.n
         return {"fwd_step": ("hbm", 16.0 * N, "read u_k, write u_k+1 (tape)"),
                 "bwd_step": ("hbm", 24.0 * N, "read unb_k, read tape u_k-1, write ub_k-1"),
                 "bwd_init": ("hbm", 32.0 * N, "read ub, unb, u_final; write seed")}
@@ -393,7 +411,8 @@ class Heat2d:
     def config(self):
         return {"workload": "C3 heat2d_b: periodic 5-point heat adjoint, 8192^2 Float64, 16 taped "
                             "steps, alpha 0.2", "n": self.n, "n_step": self.n_step,
-                "parallelism": f"replicas{self.world}",
+                "rows_per_rank": self.rows,
+                "parallelism": f"slabs{self.world}" if self.world > 1 else "single",
                 "l2": "inputs larger than L2 (512 MiB fields) and L2 flushed between steps"}
 
     def cpu_baseline(self, seconds):
@@ -564,19 +583,35 @@ class Conv1dReluMse:
                 "sample": f"{b} of {self.B} samples (oracle.cc, serial), {t:.2f} s, scaled"}
 
 
+class _LocalZero:
+    """The epilogue's zeroing at N = 1 (no communicator)."""
+
+    def zero(self, bufs):
+        from stadeb200 import ddp
+        ddp.zero_(*bufs)
+
+
 class Mlp2CeHv:
+    """C5. At N > 1 each rank takes a block of the 16,384 samples and the hvp
+    epilogue (ddp.Epilogue over NCCL) sums the 8 :accum shadows (b and bd of
+    w1, b1, w2, b2) in one bucket and the :reduced loss / lossd."""
     name = "mlp2_ce_hv"
     dtype = "f64"
-    scaling = "weak"
+    scaling = "strong"
 
     def __init__(self, torch, rank, world, comm_factory):
         import numpy as np
-        from stadeb200 import synth, kernels
+        from stadeb200 import synth, kernels, ddp
         self.torch, self.np, self.kernels = torch, np, kernels
         c = synth.FULL["mlp2_ce_hv"]
-        self.S, self.I, self.H, self.O = c["n_s"], c["n_i"], c["n_h"], c["n_o"]
+        self.G, self.I, self.H, self.O = c["n_s"], c["n_i"], c["n_h"], c["n_o"]
         self.world = world
-        d = synth.mlp2_ce_hv_inputs(self.S, self.I, self.H, self.O)
+        rng = ddp.shard(self.G, rank, world)
+        lo, hi = rng.start, rng.stop
+        self.S = hi - lo
+        d = synth.mlp2_ce_hv_inputs(self.G, self.I, self.H, self.O)
+        for k, w in (("x", self.I), ("y", self.O), ("xd", self.I), ("yd", self.O)):
+            d[k] = d[k][lo * w:hi * w].copy()
         self.pinned = {k: torch.from_numpy(v).pin_memory() for k, v in d.items()}
         t = {k: v.to("cuda") for k, v in self.pinned.items()}
         S, I, H, O = self.S, self.I, self.H, self.O
@@ -587,18 +622,24 @@ class Mlp2CeHv:
         self.t = t
         self.ws = torch.empty(kernels.mlp2_ce_hv_workspace(S, I, H, O), dtype=torch.uint8,
                               device="cuda")
+        self.comm = comm_factory() if world > 1 else None
+        backend = ddp.NcclBackend(self.comm) if self.comm is not None else _LocalZero()
+        self.epi = ddp.Epilogue(ddp.MLP2_CE, ["x", "y"], "hvp", backend)
         self.out_names = ("w1bd", "b1bd", "w2bd", "b2bd", "lossd")
         self.grad_host = {k: torch.empty(t[k].numel(), dtype=torch.float64).pin_memory()
                           for k in self.out_names}
 
     def step(self):
-        t = self.t
-        for k in ("w1b", "b1b", "w2b", "b2b", "w1bd", "b1bd", "w2bd", "b2bd", "xb", "xbd", "yb",
-                  "ybd", "loss", "lossd"):
-            t[k].zero_()
+        t, e = self.t, self.epi
+        e.reset_accum(t)
+        e.reset_reduced(t)
+        e.reset_local(t)
         self.kernels.mlp2_ce_hv_cuda(*[t[a] for a in self.kernels.MLP_HV_ARGS], self.S, self.I,
                                      self.H, self.O, *[t[a] for a in self.kernels.MLP_HV_TAN],
                                      workspace=self.ws)
+        if self.comm is not None:
+            e.backend.allreduce_sum([t[b] for b in e.accum])
+            e.allreduce_reduced(t)
 
     def e2e_step(self):
         t, p = self.t, self.pinned
@@ -621,8 +662,9 @@ class Mlp2CeHv:
 
     def config(self):
         return {"workload": "C5 mlp2_ce_hv: HVP of the C2 loss, batch 16384, Float64, direction "
-                            "over all 407,050 parameters", "n_s": self.S, "n_i": self.I,
-                "n_h": self.H, "n_o": self.O, "parallelism": f"replicas{self.world}",
+                            "over all 407,050 parameters", "global_batch": self.G,
+                "per_rank_batch": self.S, "n_i": self.I, "n_h": self.H, "n_o": self.O,
+                "parallelism": f"dp{self.world}",
                 "l2": "inputs larger than L2 and L2 flushed between steps"}
 
     def cpu_baseline(self, seconds):
@@ -639,8 +681,8 @@ class Mlp2CeHv:
         orc.mlp2_ce_hv(*[arrs[a] for a in kernels.MLP_HV_ARGS], S, I, H, O,
                        *[arrs[a] for a in kernels.MLP_HV_TAN])
         t = time.perf_counter() - t0
-        return {"value": m / (t * self.S), "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"{m} of {self.S} samples (oracle.cc, serial), {t:.2f} s, scaled"}
+        return {"value": m / (t * self.G), "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"{m} of {self.G} samples (oracle.cc, serial), {t:.2f} s, scaled"}
 
 
 WORKLOADS = {"mlp2_ce": Mlp2Ce, "heat2d": Heat2d, "affine_ls": AffineLs,
@@ -768,7 +810,7 @@ def main():
                                           "BASELINE config)",
                 "config": W.config(),
                 "roofline": roofline(phases, W.phase_work(), args.steps, peaks, peak_src,
-                                     load_traffic(args.config)),
+                                     load_traffic(args.config) if world == 1 else None),
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
                 "gpu_launches": launches,
                 "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},

@@ -285,6 +285,33 @@ stade_status stade_mlp2_ce_b_check_replicas_f32(const float* w1, const float* b1
                                                 const stade_opts* opts);
 
 /* ---------------------------------------------------------------------------
+ * C3 over several GPUs: heat2d_b on row slabs. No reference counterpart (the
+ * reference parallelises only over samples, ddpgen_); this is the domain
+ * decomposition the configuration's grid needs across GPUs. Rank r of the
+ * communicator owns `rows` consecutive grid rows directly below rank r-1's
+ * (rank 0's top neighbour is the last rank: the grid is periodic); the
+ * slabs' rows add up to n. u, ub, un, unb are this rank's rows (rows x n,
+ * row-major, 16-byte aligned) with the meaning they have in
+ * stade_heat2d_b_f64; *loss and *alphab receive the sums over ALL slabs on
+ * every rank. u_stack holds stade_initstacks_heat2d_b_slab(n, n_step, rows)
+ * values: per step one state with a halo row above and below. Per step and
+ * per sweep direction one 8 n-byte row goes to each neighbour over NCCL,
+ * overlapped with the slab's interior rows. comm == NULL is allowed when
+ * rows == n (one slab holds the grid). With STADE_HOST_SCALARS the call
+ * waits for the stream, bounded by the communicator's timeout; otherwise it
+ * returns with the work queued.
+ * ------------------------------------------------------------------------- */
+int64_t stade_initstacks_heat2d_b_slab(int64_t n, int64_t n_step, int64_t rows);
+size_t  stade_heat2d_b_f64_slab_workspace(int64_t n, int64_t n_step, int64_t rows);
+stade_status stade_heat2d_b_f64_slab(double* loss, const double* lossb,
+                                     double* u, double* ub,
+                                     double* un, double* unb,
+                                     double alpha, double* alphab,
+                                     int64_t n, int64_t n_step,
+                                     double* u_stack, int64_t rows,
+                                     stade_comm* comm, const stade_opts* opts);
+
+/* ---------------------------------------------------------------------------
  * Synthetic inputs (host side). Seed = FNV-1a-64 of a name, the scheme of
  * `val_stable_seed` (src/STADE.jl:16619-16626); draws from xoshiro256**
  * split into independent 2^20-element chunks; normals by the Box-Muller

@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "halo.cuh"
 
 struct stade_comm {
   ncclComm_t nccl = nullptr;
@@ -36,6 +37,9 @@ struct stade_comm {
   double* host_sums = nullptr;  // pinned
   int64_t* host_count = nullptr;
   bool broken = false;
+  // halo exchanges run on a side stream so the owner's interior work overlaps
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_ready = nullptr, ev_halo = nullptr;
 };
 
 namespace stade {
@@ -167,6 +171,76 @@ stade_status ensure_bucket(stade_comm* c, size_t bytes) {
 }
 
 }  // namespace
+
+stade_status halo_begin(stade_comm* c, const double* first_row, const double* last_row,
+                        double* top_halo, double* bottom_halo, int64_t count, cudaStream_t s) {
+  if (c == nullptr || c->size == 1) {
+    // one slab holds the whole periodic grid: its halos are its own edge rows
+    STADE_CUDA(cudaMemcpyAsync(top_halo, last_row, count * sizeof(double),
+                               cudaMemcpyDeviceToDevice, s));
+    STADE_CUDA(cudaMemcpyAsync(bottom_halo, first_row, count * sizeof(double),
+                               cudaMemcpyDeviceToDevice, s));
+    return STADE_OK;
+  }
+  STADE_REQUIRE(c->nccl, "halo exchange: communicator is aborted");
+  if (!c->side) {
+    STADE_CUDA(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+    STADE_CUDA(cudaEventCreateWithFlags(&c->ev_ready, cudaEventDisableTiming));
+    STADE_CUDA(cudaEventCreateWithFlags(&c->ev_halo, cudaEventDisableTiming));
+  }
+  STADE_CUDA(cudaEventRecord(c->ev_ready, s));
+  STADE_CUDA(cudaStreamWaitEvent(c->side, c->ev_ready, 0));
+  const int prev = (c->rank + c->size - 1) % c->size;
+  const int next = (c->rank + 1) % c->size;
+  const auto deadline = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+  // With two ranks both neighbours are the same peer and NCCL pairs the
+  // sends and receives between two ranks in issue order: the last row goes
+  // out first and the top halo is received first, so each receive meets the
+  // row it stands for.
+  ncclResult_t r = ncclGroupStart();
+  if (r == ncclSuccess) r = ncclSend(last_row, (size_t)count, ncclFloat64, next, c->nccl, c->side);
+  if (r == ncclSuccess || r == ncclInProgress)
+    r = ncclSend(first_row, (size_t)count, ncclFloat64, prev, c->nccl, c->side);
+  if (r == ncclSuccess || r == ncclInProgress)
+    r = ncclRecv(top_halo, (size_t)count, ncclFloat64, prev, c->nccl, c->side);
+  if (r == ncclSuccess || r == ncclInProgress)
+    r = ncclRecv(bottom_halo, (size_t)count, ncclFloat64, next, c->nccl, c->side);
+  ncclResult_t r2 = ncclGroupEnd();
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclSend/ncclRecv (halo)");
+  if (r2 != ncclSuccess && r2 != ncclInProgress) return nccl_fail(r2, "ncclGroupEnd (halo)");
+  stade_status st = wait_issue(c, deadline, "halo exchange");
+  if (st != STADE_OK) return st;
+  STADE_CUDA(cudaEventRecord(c->ev_halo, c->side));
+  return STADE_OK;
+}
+
+stade_status halo_end(stade_comm* c, cudaStream_t s) {
+  if (c == nullptr || c->size == 1) return STADE_OK;
+  STADE_CUDA(cudaStreamWaitEvent(s, c->ev_halo, 0));
+  return STADE_OK;
+}
+
+stade_status comm_allreduce_f64(stade_comm* c, double* buf, int64_t count, cudaStream_t s) {
+  if (c == nullptr || c->size == 1) return STADE_OK;
+  STADE_REQUIRE(c->nccl, "allreduce: communicator is aborted");
+  const auto deadline = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+  ncclResult_t r = ncclAllReduce(buf, buf, (size_t)count, ncclFloat64, ncclSum, c->nccl, s);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclAllReduce");
+  return wait_issue(c, deadline, "ncclAllReduce");
+}
+
+stade_status comm_wait_stream(stade_comm* c, cudaStream_t s) {
+  if (c == nullptr || c->size == 1) {
+    STADE_CUDA(cudaStreamSynchronize(s));
+    return STADE_OK;
+  }
+  STADE_REQUIRE(c->nccl, "wait: communicator is aborted");
+  const auto deadline = Clock::now() + std::chrono::milliseconds(c->timeout_ms);
+  return wait_stream(c, s, deadline, "stream wait");
+}
+
+int comm_size(const stade_comm* c) { return c ? c->size : 1; }
+
 }  // namespace stade
 
 using namespace stade;
@@ -225,6 +299,12 @@ stade_status stade_comm_destroy(stade_comm* c) {
     if (c->broken) ncclCommAbort(c->nccl);
     else ncclCommDestroy(c->nccl);
   }
+  if (c->side) {
+    cudaStreamSynchronize(c->side);
+    cudaStreamDestroy(c->side);
+  }
+  if (c->ev_ready) cudaEventDestroy(c->ev_ready);
+  if (c->ev_halo) cudaEventDestroy(c->ev_halo);
   if (c->bucket) cudaFree(c->bucket);
   if (c->sums) cudaFree(c->sums);
   if (c->count) cudaFree(c->count);

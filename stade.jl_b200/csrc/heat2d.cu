@@ -22,6 +22,7 @@
 // from the neighbouring lanes by warp shuffle. alphab and loss are summed per
 // block, then over blocks in a fixed order.
 #include "common.cuh"
+#include "halo.cuh"
 
 namespace stade {
 namespace {
@@ -56,33 +57,50 @@ __device__ __forceinline__ double heat_point(double c, double up, double dn, dou
 
 // One forward step: dst = step(src); optionally copy_dst = src (tape slot 0)
 // and a per-block partial of sum(dst^2) (the loss, last step only).
-template <int R>
+// Rows handled by one launch: block row y starts at row_lo + y * row_step and
+// covers R rows, stopping at row_hi. kWrap: the whole periodic grid (row_lo 0,
+// row_hi n, row indices wrap). !kWrap: a slab with one halo row above (row -1)
+// and below (row `rows`) already filled, rows addressed without wrapping; the
+// loads of a strip's tail past row_hi are clamped to row_hi so they stay inside
+// the halo-padded slab.
+template <bool kWrap>
+__device__ __forceinline__ void strip_rows(int i, int n, int row_hi, int& iw, int& idn) {
+  if (kWrap) {
+    iw = i % n;                    // rows past n (n % R != 0) are not stored
+    idn = iw + 1 == n ? 0 : iw + 1;
+  } else {
+    iw = i < row_hi ? i : row_hi;
+    idn = i + 1 < row_hi ? i + 1 : row_hi;
+  }
+}
+
+template <int R, bool kWrap>
 __global__ void __launch_bounds__(kThreads)
 heat_fwd_kernel(const double* __restrict__ src, double* __restrict__ dst,
-                double* __restrict__ copy_dst, double alpha, int n,
-                double* __restrict__ loss_part) {
+                double* __restrict__ copy_dst, double alpha, int n, int row_lo, int row_step,
+                int row_hi, double* __restrict__ loss_part) {
   __shared__ double red[kThreads / 32];
   const int lane = threadIdx.x & 31;
   const int j_raw = blockIdx.x * kColsPerBlock + threadIdx.x * 2;
   const bool col_ok = j_raw < n;
   const int j = col_ok ? j_raw : n - 2;
-  const int i0 = blockIdx.y * R;
-  int row_up = i0 == 0 ? n - 1 : i0 - 1;
+  const int i0 = row_lo + blockIdx.y * row_step;
+  const int row_up = kWrap ? (i0 == 0 ? n - 1 : i0 - 1) : i0 - 1;
   double2 up = ld2(src, row_up, n, j);
-  double2 cur = ld2(src, i0 % n, n, j);
+  double2 cur = ld2(src, kWrap ? i0 % n : i0, n, j);
   double lsum = 0.0;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = i0 + r;
-    const int iw = i % n;                    // rows past n (n % R != 0) are not stored
-    const int idn = iw + 1 == n ? 0 : iw + 1;
+    int iw, idn;
+    strip_rows<kWrap>(i, n, row_hi, iw, idn);
     const double2 dn = ld2(src, idn, n, j);
     double lf, rt;
     hnbrs(src, iw, n, j, cur, lane, lf, rt);
     double2 o;
     o.x = heat_point(cur.x, up.x, dn.x, lf, cur.y, alpha);
     o.y = heat_point(cur.y, up.y, dn.y, cur.x, rt, alpha);
-    if (col_ok && i < n) {
+    if (col_ok && i < row_hi) {
       *reinterpret_cast<double2*>(dst + (int64_t)i * n + j) = o;
       if (copy_dst) *reinterpret_cast<double2*>(copy_dst + (int64_t)i * n + j) = cur;
       if (loss_part) lsum += __dadd_rn(__dmul_rn(o.x, o.x), __dmul_rn(o.y, o.y));
@@ -116,26 +134,27 @@ __device__ __forceinline__ double lap_point(double c, double up, double dn, doub
   return __dadd_rn(s, -__dmul_rn(4.0, c));
 }
 
-template <int R>
+template <int R, bool kWrap>
 __global__ void __launch_bounds__(kThreads)
 heat_bwd_kernel(const double* __restrict__ g, const double* __restrict__ u,
-                double* __restrict__ gdst, double alpha, int n,
-                double* __restrict__ alpha_part, int first) {
+                double* __restrict__ gdst, double alpha, int n, int row_lo, int row_step,
+                int row_hi, double* __restrict__ alpha_part, int first) {
   __shared__ double red[kThreads / 32];
   const int lane = threadIdx.x & 31;
   const int j_raw = blockIdx.x * kColsPerBlock + threadIdx.x * 2;
   const bool col_ok = j_raw < n;
   const int j = col_ok ? j_raw : n - 2;
-  const int i0 = blockIdx.y * R;
-  const int row_up = i0 == 0 ? n - 1 : i0 - 1;
-  double2 gu = ld2(g, row_up, n, j), gc = ld2(g, i0 % n, n, j);
-  double2 uu = ld2(u, row_up, n, j), uc = ld2(u, i0 % n, n, j);
+  const int i0 = row_lo + blockIdx.y * row_step;
+  const int row_up = kWrap ? (i0 == 0 ? n - 1 : i0 - 1) : i0 - 1;
+  const int row_c = kWrap ? i0 % n : i0;
+  double2 gu = ld2(g, row_up, n, j), gc = ld2(g, row_c, n, j);
+  double2 uu = ld2(u, row_up, n, j), uc = ld2(u, row_c, n, j);
   double asum = 0.0;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = i0 + r;
-    const int iw = i % n;
-    const int idn = iw + 1 == n ? 0 : iw + 1;
+    int iw, idn;
+    strip_rows<kWrap>(i, n, row_hi, iw, idn);
     const double2 gd = ld2(g, idn, n, j);
     const double2 ud = ld2(u, idn, n, j);
     double g_lf, g_rt, u_lf, u_rt;
@@ -144,7 +163,7 @@ heat_bwd_kernel(const double* __restrict__ g, const double* __restrict__ u,
     double2 o;
     o.x = gather_point(gc.x, gu.x, gd.x, g_lf, gc.y, alpha);
     o.y = gather_point(gc.y, gu.y, gd.y, gc.x, g_rt, alpha);
-    if (col_ok && i < n) {
+    if (col_ok && i < row_hi) {
       *reinterpret_cast<double2*>(gdst + (int64_t)i * n + j) = o;
       asum = fma(lap_point(uc.x, uu.x, ud.x, u_lf, uc.y), gc.x, asum);
       asum = fma(lap_point(uc.y, uu.y, ud.y, uc.x, u_rt), gc.y, asum);
@@ -208,6 +227,34 @@ Grid grid_of(int64_t n) {
 }
 
 constexpr int kNoStepBlocks = 1184;  // 8 per SM
+
+// x = x + y for the two scalars (loss, alphab) after the cross-slab sum.
+__global__ void add_two_kernel(double* __restrict__ loss, double* __restrict__ alphab,
+                               const double* __restrict__ stage) {
+  if (threadIdx.x == 0) {
+    loss[0] = __dadd_rn(loss[0], stage[0]);
+    alphab[0] = __dadd_rn(alphab[0], stage[1]);
+  }
+}
+
+// Launch shapes of the slab path: interior rows 1 .. rows-2 in strips, and
+// the two edge rows (0 and rows-1, which read the halos) one row per block.
+struct SlabGrid {
+  dim3 fwd_in, bwd_in, edge;
+  int nfwd_in, nbwd_in, nedge;
+};
+SlabGrid slab_grid_of(int64_t n, int64_t rows) {
+  SlabGrid g;
+  const unsigned cx = ceil_div_u(n, kColsPerBlock);
+  const int64_t inner = rows - 2;
+  g.fwd_in = dim3(cx, inner > 0 ? ceil_div_u(inner, kRowsFwd) : 0);
+  g.bwd_in = dim3(cx, inner > 0 ? ceil_div_u(inner, kRowsBwd) : 0);
+  g.edge = dim3(cx, 2);
+  g.nfwd_in = (int)(g.fwd_in.x * g.fwd_in.y);
+  g.nbwd_in = (int)(g.bwd_in.x * g.bwd_in.y);
+  g.nedge = (int)(g.edge.x * g.edge.y);
+  return g;
+}
 
 }  // namespace
 }  // namespace stade
@@ -276,8 +323,8 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
       double* dst = t == n_step ? un : u_stack + t * nn;
       double* copy = t == 1 ? u_stack : nullptr;
       PhaseScope ph("fwd_step", s);
-      heat_fwd_kernel<kRowsFwd><<<g.fwd, kThreads, 0, s>>>(src, dst, copy, alpha, ni,
-                                                           t == n_step ? loss_part : nullptr);
+      heat_fwd_kernel<kRowsFwd, true><<<g.fwd, kThreads, 0, s>>>(
+          src, dst, copy, alpha, ni, 0, kRowsFwd, ni, t == n_step ? loss_part : nullptr);
       STADE_CHECK_LAUNCH();
     }
     st = launch_sum_to_scalar(loss_part, g.nfwd, loss, true, s);
@@ -293,8 +340,9 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
     }
     for (int64_t t = n_step; t >= 1; --t) {
       PhaseScope ph("bwd_step", s);
-      heat_bwd_kernel<kRowsBwd><<<g.bwd, kThreads, 0, s>>>(a, u_stack + (t - 1) * nn, b, alpha, ni,
-                                                           alpha_part, t == n_step ? 1 : 0);
+      heat_bwd_kernel<kRowsBwd, true><<<g.bwd, kThreads, 0, s>>>(
+          a, u_stack + (t - 1) * nn, b, alpha, ni, 0, kRowsBwd, ni, alpha_part,
+          t == n_step ? 1 : 0);
       STADE_CHECK_LAUNCH();
       double* tmp = a; a = b; b = tmp;
     }
@@ -309,6 +357,156 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
   if (host_scalar) {
     STADE_CUDA(cudaMemcpyAsync(alphab, stage, sizeof(double), cudaMemcpyDeviceToHost, s));
     STADE_CUDA(cudaStreamSynchronize(s));
+  }
+  return STADE_OK;
+}
+
+
+// ---------------------------------------------------------------------------
+// Slab-sharded heat2d_b: the grid's rows split into one contiguous slab per
+// rank, one halo row exchanged with each neighbouring slab per step.
+extern "C" int64_t stade_initstacks_heat2d_b_slab(int64_t n, int64_t n_step, int64_t rows) {
+  if (n <= 0 || n_step <= 0 || rows <= 0) return 0;
+  return n_step * (rows + 2) * n;
+}
+
+extern "C" size_t stade_heat2d_b_f64_slab_workspace(int64_t n, int64_t n_step, int64_t rows) {
+  if (n <= 0 || rows <= 0) return 0;
+  const SlabGrid g = slab_grid_of(n, rows);
+  Sizer z;
+  z.take<double>((size_t)(g.nfwd_in > kNoStepBlocks ? g.nfwd_in : kNoStepBlocks));  // loss, inner
+  z.take<double>((size_t)g.nedge);                          // loss partials, edge rows
+  z.take<double>((size_t)(g.nbwd_in > 0 ? g.nbwd_in : 1));  // alphab partials, interior
+  z.take<double>((size_t)g.nedge);                          // alphab partials, edge rows
+  z.take<double>(4);                                        // (loss, alphab) stage + host
+  z.take<double>((size_t)((rows + 2) * n));                 // adjoint state, halo-padded
+  z.take<double>((size_t)((rows + 2) * n));                 // second adjoint state
+  (void)n_step;
+  return z.bytes();
+}
+
+extern "C" stade_status stade_heat2d_b_f64_slab(double* loss, const double* lossb, double* u,
+                                                double* ub, double* un, double* unb,
+                                                double alpha, double* alphab, int64_t n,
+                                                int64_t n_step, double* u_stack, int64_t rows,
+                                                stade_comm* comm, const stade_opts* opts) {
+  STADE_REQUIRE(n >= 0 && n_step >= 0 && rows >= 0, "heat2d_b_slab: negative size");
+  STADE_REQUIRE(alphab != nullptr, "heat2d_b_slab: alphab is null");
+  if (n == 0 || rows == 0) return STADE_OK;
+  STADE_REQUIRE(n % 2 == 0 && n >= 4, "heat2d_b_slab: n must be even and >= 4 (got %lld)",
+                (long long)n);
+  STADE_REQUIRE(n <= 65536 && rows <= n, "heat2d_b_slab: n = %lld, rows = %lld out of range",
+                (long long)n, (long long)rows);
+  STADE_REQUIRE(rows >= 2, "heat2d_b_slab: a slab needs at least 2 rows (got %lld)",
+                (long long)rows);
+  STADE_REQUIRE(comm != nullptr || rows == n,
+                "heat2d_b_slab: without a communicator the slab must be the whole grid");
+  STADE_REQUIRE(loss && lossb && u && ub && un && unb, "heat2d_b_slab: null array argument");
+  STADE_REQUIRE(n_step == 0 || u_stack, "heat2d_b_slab: u_stack is null");
+  for (const void* p : {(const void*)u, (const void*)ub, (const void*)un, (const void*)unb,
+                        (const void*)u_stack})
+    STADE_REQUIRE(p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0,
+                  "heat2d_b_slab: arrays must be 16-byte aligned");
+  const bool host_scalar = (flags_of(opts) & STADE_HOST_SCALARS) != 0;
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(opts, stade_heat2d_b_f64_slab_workspace(n, n_step, rows), &wsp);
+  if (st != STADE_OK) return st;
+  const SlabGrid g = slab_grid_of(n, rows);
+  Carver c(wsp);
+  double* lp_in = c.take<double>((size_t)(g.nfwd_in > kNoStepBlocks ? g.nfwd_in : kNoStepBlocks));
+  double* lp_edge = c.take<double>((size_t)g.nedge);
+  double* ap_in = c.take<double>((size_t)(g.nbwd_in > 0 ? g.nbwd_in : 1));
+  double* ap_edge = c.take<double>((size_t)g.nedge);
+  double* stage = c.take<double>(4);
+  double* ga = c.take<double>((size_t)((rows + 2) * n));
+  double* gb = c.take<double>((size_t)((rows + 2) * n));
+  double* alphab_dev = alphab;
+  if (host_scalar) {
+    STADE_CUDA(cudaMemcpyAsync(stage + 2, alphab, sizeof(double), cudaMemcpyHostToDevice, s));
+    alphab_dev = stage + 2;
+  }
+  const int ni = (int)n, ri = (int)rows;
+  const int64_t nn = rows * n;            // owned cells
+  const int64_t pad = (rows + 2) * n;     // one tape slot / one padded state
+  const bool inner = rows > 2;
+  auto slot = [&](int64_t k) { return u_stack + k * pad + n; };  // row 0 of slot k
+
+  if (n_step == 0) {
+    heat_nostep_kernel<<<kNoStepBlocks, 256, 0, s>>>(u, ub, lossb, nn, lp_in);
+    STADE_CHECK_LAUNCH();
+    st = launch_sum_to_scalar(lp_in, kNoStepBlocks, stage, false, s);
+    if (st != STADE_OK) return st;
+    STADE_CUDA(cudaMemsetAsync(stage + 1, 0, sizeof(double), s));
+  } else {
+    {
+      PhaseScope ph("fwd_step", s);
+      STADE_CUDA(cudaMemcpyAsync(slot(0), u, (size_t)nn * sizeof(double),
+                                 cudaMemcpyDeviceToDevice, s));
+    }
+    for (int64_t t = 1; t <= n_step; ++t) {
+      PhaseScope ph("fwd_step", s);
+      double* src = slot(t - 1);
+      double* dst = t == n_step ? un : slot(t);
+      const bool last = t == n_step;
+      st = halo_begin(comm, src, src + (rows - 1) * n, src - n, src + rows * n, n, s);
+      if (st != STADE_OK) return st;
+      if (inner) {
+        heat_fwd_kernel<kRowsFwd, false><<<g.fwd_in, kThreads, 0, s>>>(
+            src, dst, nullptr, alpha, ni, 1, kRowsFwd, ri - 1, last ? lp_in : nullptr);
+        STADE_CHECK_LAUNCH();
+      }
+      st = halo_end(comm, s);
+      if (st != STADE_OK) return st;
+      heat_fwd_kernel<1, false><<<g.edge, kThreads, 0, s>>>(src, dst, nullptr, alpha, ni, 0,
+                                                            ri - 1, ri, last ? lp_edge : nullptr);
+      STADE_CHECK_LAUNCH();
+    }
+    st = launch_sum_to_scalar(lp_edge, g.nedge, stage, false, s);
+    if (st == STADE_OK && inner) st = launch_sum_to_scalar(lp_in, g.nfwd_in, stage, true, s);
+    if (st != STADE_OK) return st;
+    {
+      PhaseScope ph("bwd_init", s);
+      heat_bwd_init_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, ga + n, nn / 2);
+      STADE_CHECK_LAUNCH();
+    }
+    double* a = ga + n;
+    double* b = gb + n;
+    for (int64_t t = n_step; t >= 1; --t) {
+      PhaseScope ph("bwd_step", s);
+      double* dst = t == 1 ? ub : b;
+      const double* ut = slot(t - 1);
+      const int first = t == n_step ? 1 : 0;
+      st = halo_begin(comm, a, a + (rows - 1) * n, a - n, a + rows * n, n, s);
+      if (st != STADE_OK) return st;
+      if (inner) {
+        heat_bwd_kernel<kRowsBwd, false><<<g.bwd_in, kThreads, 0, s>>>(
+            a, ut, dst, alpha, ni, 1, kRowsBwd, ri - 1, ap_in, first);
+        STADE_CHECK_LAUNCH();
+      }
+      st = halo_end(comm, s);
+      if (st != STADE_OK) return st;
+      heat_bwd_kernel<1, false><<<g.edge, kThreads, 0, s>>>(a, ut, dst, alpha, ni, 0, ri - 1,
+                                                            ri, ap_edge, first);
+      STADE_CHECK_LAUNCH();
+      double* tmp = a; a = b; b = tmp;
+    }
+    {
+      PhaseScope ph("zero_unb", s);
+      STADE_CUDA(cudaMemsetAsync(unb, 0, (size_t)nn * sizeof(double), s));
+    }
+    st = launch_sum_to_scalar(ap_edge, g.nedge, stage + 1, false, s);
+    if (st == STADE_OK && inner) st = launch_sum_to_scalar(ap_in, g.nbwd_in, stage + 1, true, s);
+    if (st != STADE_OK) return st;
+  }
+  // (loss, alphab) of this slab -> sums over all slabs -> added to the outputs
+  st = comm_allreduce_f64(comm, stage, 2, s);
+  if (st != STADE_OK) return st;
+  add_two_kernel<<<1, 32, 0, s>>>(loss, alphab_dev, stage);
+  STADE_CHECK_LAUNCH();
+  if (host_scalar) {
+    STADE_CUDA(cudaMemcpyAsync(alphab, alphab_dev, sizeof(double), cudaMemcpyDeviceToHost, s));
+    return comm_wait_stream(comm, s);
   }
   return STADE_OK;
 }

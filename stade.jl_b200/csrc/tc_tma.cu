@@ -9,7 +9,7 @@
 // tcgen05.mma.kind::tf32 per K step into one TMEM accumulator.
 //
 // Persistent kernel, one CTA per SM, warp-specialised:
-//   warp 0  one thread issues TMA loads (cp.async.bulk.tensor, no multicast)
+//   warp 0  one thread issues TMA loads (cp.async.bulk.tensor, each copy into its own CTA)
 //           of the four 128 x 32 operand tiles of a K block into a 3-stage
 //           ring of 128-byte-swizzled shared memory, signalled by
 //           mbarrier complete_tx;

@@ -6,5 +6,6 @@ from ._lib import StadeError, lib, LIB_PATH  # noqa: F401
 from .kernels import (  # noqa: F401
     affine_ls_b_cuda, mlp2_ce_b_cuda, heat2d_b_cuda, heat2d_b_cuda_device,
     initstacks_heat2d_b_cuda, conv1d_relu_mse_b_cuda, mlp2_ce_hv_cuda,
+    heat2d_b_slab_cuda, initstacks_heat2d_b_slab_cuda,
     kernel_launches, reset_kernel_launches,
 )

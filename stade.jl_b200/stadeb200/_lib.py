@@ -65,6 +65,9 @@ SIGNATURES = {
     "stade_initstacks_heat2d_b": (I64, [I64, I64]),
     "stade_heat2d_b_f64_workspace": (C.c_size_t, [I64, I64]),
     "stade_heat2d_b_f64": (ST, [P] * 6 + [D, P, I64, I64, P, OPTS]),
+    "stade_initstacks_heat2d_b_slab": (I64, [I64, I64, I64]),
+    "stade_heat2d_b_f64_slab_workspace": (C.c_size_t, [I64, I64, I64]),
+    "stade_heat2d_b_f64_slab": (ST, [P] * 6 + [D, P, I64, I64, P, I64, P, OPTS]),
     "stade_conv1d_relu_mse_b_f32_workspace": (C.c_size_t, [I64] * 5),
     "stade_conv1d_relu_mse_b_f32": (ST, [P] * 12 + [I64] * 5 + [OPTS]),
     "stade_mlp2_ce_hv_f64_workspace": (C.c_size_t, [I64] * 4),

@@ -132,6 +132,34 @@ def heat2d_b_workspace(n, n_step) -> int:
     return lib().stade_heat2d_b_f64_workspace(n, n_step)
 
 
+def initstacks_heat2d_b_slab_cuda(n, n_step, rows, device=None):
+    """Tape of one slab: n_step states of (rows + 2) x n values (halo rows)."""
+    m = lib().stade_initstacks_heat2d_b_slab(n, n_step, rows)
+    return torch.empty(max(m, 1), dtype=torch.float64, device=device or "cuda")
+
+
+def heat2d_b_slab_cuda(loss, lossb, u, ub, un, unb, alpha, alphab_dev, n, n_step, u_stack, rows,
+                       comm=None, *, stream=None, workspace=None):
+    """heat2d_b on this rank's slab of `rows` grid rows (rank order = slab
+    order, periodic); loss and alphab_dev (1-element device tensors) receive
+    the sums over all slabs. comm: a ddp.NcclComm, or None when the slab is
+    the whole grid."""
+    f = torch.float64
+    nn = rows * n
+    ptrs = [_arr(loss, f, 1, "loss"), _arr(lossb, f, 1, "lossb"), _arr(u, f, nn, "u"),
+            _arr(ub, f, nn, "ub"), _arr(un, f, nn, "un"), _arr(unb, f, nn, "unb")]
+    stack = _arr(u_stack, f, lib().stade_initstacks_heat2d_b_slab(n, n_step, rows), "u_stack")
+    ab = _arr(alphab_dev, f, 1, "alphab")
+    o = _opts(stream, workspace)
+    handle = comm.handle if comm is not None else None
+    check(lib().stade_heat2d_b_f64_slab(*ptrs, float(alpha), ab, n, n_step, stack, rows, handle,
+                                        C.byref(o)))
+
+
+def heat2d_b_slab_workspace(n, n_step, rows) -> int:
+    return lib().stade_heat2d_b_f64_slab_workspace(n, n_step, rows)
+
+
 # ---------------------------------------------------------------------------
 def conv1d_relu_mse_b_cuda(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb,
                            n_b, n_c, n_l, n_o, n_k, *, stream=None, workspace=None):
