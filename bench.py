@@ -44,6 +44,7 @@ METRIC = "adjoint grad-evals/sec at 1/2/4/8 B200; % of HBM or tensor-pipe roofli
 UNIT = "grad-evals/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
+L2_BYTES = 126 * 1000 * 1000  # B200 L2; a rank whose step inputs are smaller gets its L2 flushed
 
 
 def parse_args():
@@ -147,29 +148,44 @@ def dist_setup(args):
 
 
 def timed_loop(torch, step, steps, warmup, world, dist, flush, stream):
-    """W warm-up steps, barrier + sync, K steps each between CUDA events on the
-    launching stream with an L2 flush between steps (outside the events),
-    barrier + sync. Returns (max-over-ranks total ms, per-step ms list)."""
+    """W warm-up steps, barrier + sync, K steps, barrier + sync. With `flush`
+    (workloads whose inputs fit in L2) each step sits between CUDA events on
+    the launching stream and the L2 is flushed between steps, outside the
+    events; without it (inputs larger than L2) one event pair brackets all K
+    steps back to back, gaps included. Returns (max-over-ranks total ms,
+    per-step ms list)."""
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(steps)]
-    for i in range(steps):
-        if flush is not None:
+    if flush is None:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        total = t0.elapsed_time(t1)
+        per = [total / steps] * steps
+    else:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)]
+        for i in range(steps):
             flush.add_(1)
-        evs[i][0].record(stream)
-        step()
-        evs[i][1].record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    per = [a.elapsed_time(b) for a, b in evs]
-    total = sum(per)
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        per = [a.elapsed_time(b) for a, b in evs]
+        total = sum(per)
     if world > 1:
         t = torch.tensor([total], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -265,6 +281,7 @@ class Mlp2Ce:
         self.comm = comm_factory() if world > 1 else None
         self.grad_host = {k: torch.empty(t[k].numel(), dtype=f32).pin_memory()
                           for k in ("w1b", "b1b", "w2b", "b2b", "loss")}
+        self.flush_l2 = sum(v.numel() * 4 for v in self.host.values()) < L2_BYTES
 
     def step(self):
         t, d = self.t, self.ddp
@@ -308,7 +325,8 @@ class Mlp2Ce:
                             "adjoint, Float32, per-sample shadow-weight accumulation",
                 "global_batch": self.G, "per_rank_batch": self.n_s, "n_i": self.n_i,
                 "n_h": self.n_h, "n_o": self.n_o, "parallelism": f"dp{self.world}",
-                "l2": "flushed between timed steps (256 MiB write outside the events)"}
+                "l2": ("L2 flushed between timed steps (256 MiB write outside the events)"
+                       if self.flush_l2 else "inputs larger than L2, steps timed back to back")}
 
     def cpu_baseline(self, seconds):
         """Oracle (the restated generated sweep), OpenMP over samples, on a
@@ -376,6 +394,7 @@ class Heat2d:
         self.ws = torch.empty(ws, dtype=torch.uint8, device="cuda")
         self.out_host = torch.empty(m, dtype=f64).pin_memory()
         self.ab_host = torch.empty(1, dtype=f64).pin_memory()
+        self.flush_l2 = m * 8 < L2_BYTES
 
     def step(self):
         t = self.t
@@ -413,7 +432,8 @@ class Heat2d:
                             "steps, alpha 0.2", "n": self.n, "n_step": self.n_step,
                 "rows_per_rank": self.rows,
                 "parallelism": f"slabs{self.world}" if self.world > 1 else "single",
-                "l2": "inputs larger than L2 (512 MiB fields) and L2 flushed between steps"}
+                "l2": ("L2 flushed between timed steps" if self.flush_l2 else
+                       "inputs larger than L2 (the slab's fields), steps timed back to back")}
 
     def cpu_baseline(self, seconds):
         np = self.np
@@ -435,6 +455,7 @@ class AffineLs:
     name = "affine_ls"
     dtype = "f64"
     scaling = "weak"
+    flush_l2 = True
 
     def __init__(self, torch, rank, world, comm_factory):
         import numpy as np
@@ -487,7 +508,7 @@ class AffineLs:
         return {"workload": "C1 affine_ls_b: y = W x + b, 0.5 sum (y - t)^2 adjoint, W 64x32, "
                             "batch 1024, Float64", "n_s": self.n_s, "n_o": self.n_o,
                 "n_i": self.n_i, "parallelism": f"replicas{self.world}",
-                "l2": "working set 1.6 MB stays in L2; L2 flushed between steps"}
+                "l2": "working set 1.6 MB fits in L2; L2 flushed between timed steps"}
 
     def cpu_baseline(self, seconds):
         np = self.np
@@ -510,6 +531,7 @@ class Conv1dReluMse:
     name = "conv1d_relu_mse"
     dtype = "f32"
     scaling = "weak"
+    flush_l2 = False  # x alone is 2.1 GB
 
     def __init__(self, torch, rank, world, comm_factory):
         import numpy as np
@@ -556,7 +578,9 @@ class Conv1dReluMse:
 
     def phase_work(self):
         fl = 2.0 * self.B * self.O * (self.L - self.K + 1) * self.C * self.K
-        return {"conv_fwd": ("tensor", fl, "implicit GEMM 2 B O Lo C K flops + elementwise"),
+        nx = float(self.B) * self.C * self.L
+        return {"conv_split": ("hbm", 12.0 * nx, "x read, x^T hi / lo planes written"),
+                "conv_fwd": ("tensor", fl, "implicit GEMM 2 B O Lo C K flops + elementwise"),
                 "conv_wgrad": ("tensor", fl, "weight gradient 2 B O Lo C K flops"),
                 "conv_xgrad": ("tensor", fl, "input gradient 2 B O Lo C K flops")}
 
@@ -625,6 +649,7 @@ class Mlp2CeHv:
         self.comm = comm_factory() if world > 1 else None
         backend = ddp.NcclBackend(self.comm) if self.comm is not None else _LocalZero()
         self.epi = ddp.Epilogue(ddp.MLP2_CE, ["x", "y"], "hvp", backend)
+        self.flush_l2 = sum(v.numel() * 8 for v in self.pinned.values()) < L2_BYTES
         self.out_names = ("w1bd", "b1bd", "w2bd", "b2bd", "lossd")
         self.grad_host = {k: torch.empty(t[k].numel(), dtype=torch.float64).pin_memory()
                           for k in self.out_names}
@@ -665,7 +690,8 @@ class Mlp2CeHv:
                             "over all 407,050 parameters", "global_batch": self.G,
                 "per_rank_batch": self.S, "n_i": self.I, "n_h": self.H, "n_o": self.O,
                 "parallelism": f"dp{self.world}",
-                "l2": "inputs larger than L2 and L2 flushed between steps"}
+                "l2": ("L2 flushed between timed steps" if self.flush_l2 else
+                       "inputs (x, xd) larger than L2, steps timed back to back")}
 
     def cpu_baseline(self, seconds):
         np = self.np
@@ -778,7 +804,8 @@ def main():
     _lib.profile_enable(True)
     launches0 = _lib.lib().stade_kernel_launches()
     clocks.start()
-    total_ms, per = timed_loop(torch, W.step, args.steps, 0, world, dist, flush, stream)
+    total_ms, per = timed_loop(torch, W.step, args.steps, 0, world, dist,
+                               flush if W.flush_l2 else None, stream)
     clocks.stop()
     launches = _lib.lib().stade_kernel_launches() - launches0
     _lib.profile_enable(False)

@@ -15,7 +15,11 @@
 // whole elementwise epilogue fused, the weight gradient split over
 // (sample, position) with a fixed-order slice sum, and the input gradient
 // as a gather (each output element owned by one thread, no atomics).
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
+#include "conv_tc.cuh"
 #include "gemm_simt.cuh"
 
 namespace stade {
@@ -166,6 +170,13 @@ struct CarverA {
   template <class T> T* take(size_t n) { return c.take<T>(n); }
 };
 
+// The tcgen05 path runs unless the sizes do not suit it or STADE_CONV_GEMM=simt.
+bool use_tc(const ConvShape& sh) {
+  const char* e = std::getenv("STADE_CONV_GEMM");
+  if (e && std::strcmp(e, "simt") == 0) return false;
+  return conv_tc_supported(sh);
+}
+
 }  // namespace
 }  // namespace stade
 
@@ -174,6 +185,8 @@ using namespace stade;
 extern "C" size_t stade_conv1d_relu_mse_b_f32_workspace(int64_t n_b, int64_t n_c, int64_t n_l,
                                                         int64_t n_o, int64_t n_k) {
   if (n_b <= 0 || n_c <= 0 || n_o <= 0 || n_k <= 0 || n_l < n_k) return 256;
+  const ConvShape sh{n_b, n_c, n_l, n_o, n_k};
+  if (use_tc(sh)) return conv_tc_workspace(sh);
   ConvDims d{(int)n_b, (int)n_c, (int)n_l, (int)n_o, (int)n_k, (int)(n_l - n_k + 1)};
   SizerA a;
   conv_layout(a, nullptr, d);
@@ -201,6 +214,13 @@ extern "C" stade_status stade_conv1d_relu_mse_b_f32(float* loss, const float* lo
   stade_status st = get_workspace(
       opts, stade_conv1d_relu_mse_b_f32_workspace(n_b, n_c, n_l, n_o, n_k), &wsp);
   if (st != STADE_OK) return st;
+  const ConvShape sh{n_b, n_c, n_l, n_o, n_k};
+  if (use_tc(sh)) {
+    for (const void* p : {(const void*)x, (const void*)w})
+      STADE_REQUIRE((reinterpret_cast<uintptr_t>(p) & 15u) == 0,
+                    "conv1d_relu_mse_b: x and w must be 16-byte aligned");
+    return conv_tc_run(sh, loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, wsp, s);
+  }
   const ConvDims d{(int)n_b, (int)n_c, (int)n_l, (int)n_o, (int)n_k, (int)n_lo};
   CarverA ca(wsp);
   ConvWs cw;

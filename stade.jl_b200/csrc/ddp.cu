@@ -53,9 +53,18 @@ stade_status nccl_fail(ncclResult_t r, const char* what) {
 
 using Clock = std::chrono::steady_clock;
 
+// Poll pacing: the first polls spin (issuing usually completes within a few
+// microseconds and a sleep would hold the host thread, and with it the
+// launches queued behind the call, for the sleep's whole length), later ones
+// sleep.
+inline void poll_pause(int& polls) {
+  if (++polls > 2000) std::this_thread::sleep_for(std::chrono::microseconds(20));
+}
+
 // Waits until the non-blocking communicator has finished issuing the last
 // call (ncclInProgress -> ncclSuccess), bounded by the deadline.
 stade_status wait_issue(stade_comm* c, Clock::time_point deadline, const char* what) {
+  int polls = 0;
   for (;;) {
     ncclResult_t st = ncclSuccess;
     ncclResult_t r = ncclCommGetAsyncError(c->nccl, &st);
@@ -73,13 +82,14 @@ stade_status wait_issue(stade_comm* c, Clock::time_point deadline, const char* w
       c->nccl = nullptr;
       return fail(STADE_ETIMEDOUT, "%s: peers did not respond within the timeout", what);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    poll_pause(polls);
   }
 }
 
 // Waits for the stream to drain while watching the communicator for errors.
 stade_status wait_stream(stade_comm* c, cudaStream_t s, Clock::time_point deadline,
                          const char* what) {
+  int polls = 0;
   for (;;) {
     cudaError_t q = cudaStreamQuery(s);
     if (q == cudaSuccess) return STADE_OK;
@@ -98,7 +108,7 @@ stade_status wait_stream(stade_comm* c, cudaStream_t s, Clock::time_point deadli
       c->nccl = nullptr;
       return fail(STADE_ETIMEDOUT, "%s: collective did not complete within the timeout", what);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+    poll_pause(polls);
   }
 }
 

@@ -611,6 +611,7 @@ stade_status tc_input_grad(const float* s1b, const float* w1, float* xb, int S, 
 
 namespace stade {
 int tma_take_error();
+int conv_tc_take_error();
 }
 
 extern "C" int stade_device_error(void) {
@@ -621,6 +622,7 @@ extern "C" int stade_device_error(void) {
     cudaMemcpyToSymbol(stade::tc::g_tc_error, &zero, sizeof(int));
   }
   const int t = stade::tma_take_error();
-  if (t < 0) return -1;
-  return v | t;
+  const int c = stade::conv_tc_take_error();
+  if (t < 0 || c < 0) return -1;
+  return v | t | c;
 }

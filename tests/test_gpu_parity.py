@@ -146,6 +146,30 @@ def test_conv1d_relu_mse_b(sizes, seeded):
         assert np.all(out[k] == 0.0), k
 
 
+@pytest.mark.parametrize("path", ["tc", "simt"])
+@pytest.mark.parametrize("sizes,seeded", [((4, 16, 200, 32, 9), True),
+                                          ((3, 68, 300, 36, 9), True),
+                                          ((2, 64, 2048, 128, 9), False),
+                                          ((5, 4, 40, 4, 3), True),
+                                          ((2, 32, 130, 132, 1), True)])
+def test_conv1d_relu_mse_b_paths(sizes, seeded, path, monkeypatch):
+    """The tcgen05 3xTF32 implicit GEMMs (default where n_c and n_o are
+    multiples of 4) and the CUDA-core path, against the oracle: channel
+    counts off the 32-wide tiles, output-channel tiles past n_o, one tap,
+    and no bounded wait ran out."""
+    from stadeb200 import _lib
+    if path == "simt":
+        monkeypatch.setenv("STADE_CONV_GEMM", "simt")
+    ref, out, truth, ints = _run_f32(lambda: cases.conv_state(*sizes, seeded=seeded),
+                                     cases.oracle_conv, cases.gpu_conv)
+    assert _lib.lib().stade_device_error() == 0
+    for k in ("z", "r", "tb", "wb", "xb", "loss"):
+        ok, errs = f32_verdict(out[k], ref[k], truth[k])
+        assert ok, (k, errs)
+    for k in ("zb", "rb"):
+        assert np.all(out[k] == 0.0), k
+
+
 @pytest.mark.parametrize("sizes,seeded,xd", [((64, 30, 40, 10), False, False),
                                              ((33, 17, 19, 3), True, True),
                                              ((130, 70, 129, 10), True, False)])
