@@ -23,15 +23,12 @@
 // Every wait is bounded (~2 s of clock); on timeout the kernel sets
 // g_tma_error, stops issuing work, waits (bounded) for its own copies and
 // tensor-core operations, frees TMEM and returns.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
-#include <mutex>
 
 #include "tc_gemm.cuh"
+#include "tcgen05.cuh"
 
 namespace stade {
 namespace tma {
@@ -46,7 +43,6 @@ constexpr int kStageBytes = 4 * kTileBytes;     // A hi, A lo, B hi, B lo
 constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 256;
 static_assert((2 * STAGES + 5) * 8 + 4 <= 256, "barrier block must fit in 256 bytes");
 constexpr uint32_t kTmemCols = 256;             // two 128-column accumulators
-constexpr long long kWaitCycles = 4000000000LL; // ~2 s at 1.9 GHz
 // K blocks per TMEM accumulation chain. The tensor core's Float32
 // accumulation is not round-to-nearest: its error grows linearly with the
 // number of accumulations into one TMEM accumulator (measured: 1.4e-5
@@ -57,106 +53,22 @@ constexpr int kChainBlocks = 4;
 
 __device__ int g_tma_error = 0;
 
-// ---- PTX wrappers ---------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
+// ---- PTX building blocks (tcgen05.cuh) -------------------------------------------
+using tc5::smem_u32;
+using tc5::mbar_init;
+using tc5::mbar_arrive;
+using tc5::mbar_arrive_tx;
+using tc5::tma_load_2d;
+using tc5::mma_tf32;
+using tc5::mma_commit;
+using tc5::tmem_ld16;
+using tc5::desc_sw128;
+using tc5::idesc_tf32;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  if (mbar_try(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
-      atomicExch(&g_tma_error, 1);
-      return false;
-    }
-  }
-  return true;
+  return tc5::mbar_wait(bar, parity, &g_tma_error);
 }
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor (version 1).
-//  K-major, 128-byte swizzle of 16-byte chunks (layout type 2): rows of 128
-//           bytes (32 tf32 of K), 8-row groups 1024 B apart; K step j starts
-//           32 j bytes into the row.
-//  MN-major, 128-byte swizzle of 32-byte chunks (layout type 1, the only
-//           shared-memory layout tf32 takes MN-major): rows of 128 bytes (32
-//           tf32 of M or N) per k, 4-row K groups 512 B apart, 32-wide M/N
-//           groups 4096 B apart; K step j (8 rows) starts at 1024 j bytes.
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo,
-                                               uint32_t layout) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1u << 46;
-  d |= (uint64_t)layout << 61;
-  return d;
-}
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
+__device__ __forceinline__ void tc_fence_before() { tc5::fence_before(); }
+__device__ __forceinline__ void tc_fence_after() { tc5::fence_after(); }
 
 // ---- epilogues: a thread owns one accumulator row and gets 16 columns at a time
 __device__ __forceinline__ bool aligned16(const void* p) {
@@ -499,39 +411,14 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
 }
 
 // ---- host: tensor maps ---------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // Row-major Float32 plane of rows x cols (row pitch `ld` elements), box of
 // box_c (inner, along cols) x box_r, 128-byte swizzle with 16-byte chunks
 // (K-major operands) or 32-byte chunks (MN-major operands), zero fill outside.
 stade_status make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld,
                       uint32_t box_c, uint32_t box_r, bool chunk32) {
-  auto fn = encode_fn();
-  if (!fn) return fail(STADE_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (ld * 4) % 16)
-    return fail(STADE_EINVAL, "TMA operand must be 16-byte aligned with a 16-byte row pitch");
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
-  const cuuint32_t box[2] = {box_c, box_r};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  chunk32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(STADE_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return STADE_OK;
+  const int64_t dims[2] = {cols, rows}, pitch[1] = {ld};
+  const uint32_t box[2] = {box_c, box_r};
+  return tc5::make_map_f32(map, base, 2, dims, pitch, box, chunk32);
 }
 
 // An operand of the contraction held as hi / lo planes. mn = false: rows are
@@ -550,16 +437,7 @@ stade_status operand_maps(const Operand& o, CUtensorMap* hi, CUtensorMap* lo) {
   return make_map(lo, o.lo, o.rows, o.cols, o.ld, bc, br, o.mn);
 }
 
-int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+using tc5::sm_count;
 
 template <int EPI_KIND, int NO>
 stade_status run(const Operand& A, const Operand& B, Geometry g, const EpiTanhLogits& el,

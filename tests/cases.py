@@ -208,3 +208,38 @@ def gpu_conv(st, ints):
     stadeb200.conv1d_relu_mse_b_cuda(*[dev[a] for a in CONV_ARGS], ints["n_b"], ints["n_c"],
                                      ints["n_l"], ints["n_o"], ints["n_k"])
     _back(dev, st)
+
+
+def conv_kink_adjust(st0, truth, out, ints, band=1e-5):
+    """The exact adjoint of the ReLU branch the GPU took, where it took the
+    other one at a kink. max(z, 0)' = 0.5 (1 + sign z) jumps at z = 0; where
+    the exact pre-activation |z| is within `band` * max|z| (the contraction's
+    Float32 rounding) and the GPU's z has the other sign, the GPU's g = dz
+    differs from the exact one by (d_gpu - d_exact) * rb_total. Returns a copy
+    of `truth` with wb and xb moved by exactly that, and the number of such
+    elements. Everything else (z, r, tb, loss) is continuous at the kink."""
+    n_b, n_c, n_l, n_o, n_k = (ints[k] for k in ("n_b", "n_c", "n_l", "n_o", "n_k"))
+    n_lo = n_l - n_k + 1
+    zt = truth["z"].reshape(n_b, n_o, n_lo)
+    zg = out["z"].astype(np.float64).reshape(n_b, n_o, n_lo)
+    flip = (np.sign(zt) != np.sign(zg)) & (np.abs(zt) <= band * np.abs(zt).max())
+    adj = OrderedDict((k, v.copy()) for k, v in truth.items())
+    idx = np.argwhere(flip)
+    if len(idx) == 0:
+        return adj, 0
+    inv_n = 1.0 / (n_b * n_o * n_lo)
+    tt = st0["t"].astype(np.float64).reshape(n_b, n_o, n_lo)
+    rb0 = st0["rb"].astype(np.float64).reshape(n_b, n_o, n_lo)
+    lb = float(st0["lossb"][0])
+    x = st0["x"].astype(np.float64).reshape(n_b, n_c, n_l)
+    w = st0["w"].astype(np.float64).reshape(n_o, n_c, n_k)
+    wb = adj["wb"].reshape(n_o, n_c, n_k)
+    xb = adj["xb"].reshape(n_b, n_c, n_l)
+    for b, o, t in idx:
+        rt = max(zt[b, o, t], 0.0)
+        rbt = rb0[b, o, t] + inv_n * 2.0 * (rt - tt[b, o, t]) * lb
+        dg = (0.5 * (1.0 + np.sign(zg[b, o, t])) - 0.5 * (1.0 + np.sign(zt[b, o, t]))) * rbt
+        wb[o, :, :] += dg * np.stack([x[b, :, t + k] for k in range(n_k)], axis=1)
+        for k in range(n_k):
+            xb[b, :, t + k] += dg * w[o, :, k]
+    return adj, len(idx)

@@ -137,13 +137,7 @@ def test_heat2d_b_homogeneity_medium():
 @pytest.mark.parametrize("sizes,seeded", [((2, 3, 30, 4, 5), True), ((4, 16, 200, 32, 9), False),
                                           ((1, 1, 9, 1, 9), True), ((3, 64, 140, 128, 9), False)])
 def test_conv1d_relu_mse_b(sizes, seeded):
-    ref, out, truth, ints = _run_f32(lambda: cases.conv_state(*sizes, seeded=seeded),
-                                     cases.oracle_conv, cases.gpu_conv)
-    for k in ("z", "r", "tb", "wb", "xb", "loss"):
-        ok, errs = f32_verdict(out[k], ref[k], truth[k])
-        assert ok, (k, errs)
-    for k in ("zb", "rb"):
-        assert np.all(out[k] == 0.0), k
+    _check_conv(sizes, seeded)
 
 
 @pytest.mark.parametrize("path", ["tc", "simt"])
@@ -160,12 +154,31 @@ def test_conv1d_relu_mse_b_paths(sizes, seeded, path, monkeypatch):
     from stadeb200 import _lib
     if path == "simt":
         monkeypatch.setenv("STADE_CONV_GEMM", "simt")
-    ref, out, truth, ints = _run_f32(lambda: cases.conv_state(*sizes, seeded=seeded),
-                                     cases.oracle_conv, cases.gpu_conv)
+    _check_conv(sizes, seeded)
     assert _lib.lib().stade_device_error() == 0
+
+
+def _check_conv(sizes, seeded):
+    """Float32 verdict per output; at a ReLU kink (exact |z| within 1e-5 of
+    max|z|) where the GPU's z took the other sign, wb and xb are checked
+    against the exact adjoint of the branch the GPU took (cases.conv_kink_adjust)
+    — such elements must be rare."""
+    st, ints = cases.conv_state(*sizes, seeded=seeded)
+    ref, out = cases.copy_state(st), cases.copy_state(st)
+    truth = _truth(st, ints, cases.oracle_conv)
+    cases.oracle_conv(ref, ints)
+    cases.gpu_conv(out, ints)
+    adj, flips = cases.conv_kink_adjust(st, truth, out, ints)
+    assert flips <= max(2, out["z"].size // 10000), flips
     for k in ("z", "r", "tb", "wb", "xb", "loss"):
-        ok, errs = f32_verdict(out[k], ref[k], truth[k])
-        assert ok, (k, errs)
+        if flips and k in ("wb", "xb"):
+            # the oracle took the exact branch: its own error is measured
+            # against the exact result, the GPU's against the adjusted one
+            e_gpu, e_oracle = rel_err(out[k], adj[k]), rel_err(ref[k], truth[k])
+            assert e_gpu <= max(F32_TOL, e_oracle), (k, e_gpu, e_oracle, flips)
+        else:
+            ok, errs = f32_verdict(out[k], ref[k], truth[k])
+            assert ok, (k, errs, flips)
     for k in ("zb", "rb"):
         assert np.all(out[k] == 0.0), k
 
