@@ -56,6 +56,8 @@ def parse_args():
     ap.add_argument("--config", default="mlp2_ce",
                     choices=["mlp2_ce", "heat2d", "affine_ls", "mlp2_ce_hv", "conv1d_relu_mse"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time eager launches instead of a replayed CUDA graph of one step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target length of the CPU-baseline sample")
@@ -502,7 +504,10 @@ class AffineLs:
         return h2d, sum(v.numel() * 8 for v in self.grad_host.values())
 
     def phase_work(self):
-        return {}
+        S, O, I = self.n_s, self.n_o, self.n_i
+        byts = 8.0 * (S * I + S * O + O * I + O + O * I + O + S * I + S * O)
+        return {"affine": ("hbm", byts, "read X, T, W, b; write Wb, bb, Xb, Tb (1,606,656 B); "
+                                        "two launches, latency-bound")}
 
     def config(self):
         return {"workload": "C1 affine_ls_b: y = W x + b, 0.5 sum (y - t)^2 adjoint, W 64x32, "
@@ -794,24 +799,52 @@ def main():
     flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     peaks, peak_src = load_peaks()
 
-    # device-resident timed run, with the phase profiler on
-    clocks = ClockSampler(local)
-    _lib.lib().stade_reset_kernel_launches()
+    # device-resident timed run: one step captured in a CUDA graph and
+    # replayed (N = 1; eager at N > 1, where the step holds NCCL calls on a
+    # non-blocking communicator), phase profiler off
     for _ in range(args.warmup):
         W.step()
     torch.cuda.synchronize()
+    step_fn, graph = W.step, None
+    if world == 1 and not args.no_graph:
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                W.step()                     # workspace / attributes settled outside capture
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                W.step()
+            torch.cuda.synchronize()
+            step_fn = graph.replay
+            for _ in range(2):
+                step_fn()
+            torch.cuda.synchronize()
+        except Exception as e:  # fall back to eager launches, and say so
+            graph = None
+            step_fn = W.step
+            print(f"# graph capture failed, timing eager launches: {e!r}", file=sys.stderr)
+    clocks = ClockSampler(local)
+    clocks.start()
+    total_ms, per = timed_loop(torch, step_fn, args.steps, 0, world, dist,
+                               flush if W.flush_l2 else None, stream)
+    clocks.stop()
+    ms_per_step = total_ms / args.steps
+    value = 1000.0 / ms_per_step if W.scaling == "strong" else world * 1000.0 / ms_per_step
+
+    # the same steps eagerly with the phase profiler on: per-phase device time
+    # for the roofline, and the launch count (a replayed graph holds the same
+    # kernels)
     _lib.profile_read()
     _lib.profile_enable(True)
     launches0 = _lib.lib().stade_kernel_launches()
-    clocks.start()
-    total_ms, per = timed_loop(torch, W.step, args.steps, 0, world, dist,
-                               flush if W.flush_l2 else None, stream)
-    clocks.stop()
+    p_ms, _ = timed_loop(torch, W.step, args.steps, 0, world, dist,
+                         flush if W.flush_l2 else None, stream)
     launches = _lib.lib().stade_kernel_launches() - launches0
     _lib.profile_enable(False)
     phases = _lib.profile_read()
-    ms_per_step = total_ms / args.steps
-    value = 1000.0 / ms_per_step if W.scaling == "strong" else world * 1000.0 / ms_per_step
 
     # end to end through the public entry points with host buffers
     e2e = None
@@ -840,6 +873,9 @@ def main():
                                      load_traffic(args.config) if world == 1 else None),
                 "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
                 "gpu_launches": launches,
+                "timing": ("CUDA graph of one step, replayed" if graph is not None
+                           else "eager launches"),
+                "eager_profiled_ms_per_step": p_ms / args.steps,
                 "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
                 "step_ms_min_max": [min(per), max(per)]}
         print(json.dumps(line), flush=True)

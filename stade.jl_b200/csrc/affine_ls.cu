@@ -157,6 +157,7 @@ extern "C" stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
   if (p.smem > 48 * 1024)
     STADE_CUDA(cudaFuncSetAttribute(affine_ls_chunk_kernel,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+  PhaseScope ph("affine", s);
   affine_ls_chunk_kernel<<<p.nblk, kThreads, p.smem, s>>>(lossb, w, b, x, xb, t, tb, y, yb, n_s,
                                                           (int)n_o, (int)n_i, p.chunk, part);
   STADE_CHECK_LAUNCH();

@@ -288,28 +288,41 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
 #pragma unroll
           for (int q = 0; q < BN / 32; ++q) {
             const int o0 = tl.n0 + (half + 2 * q) * 16;
+            const int64_t idx0 = ((int64_t)tl.b * g.O + o0) * g.Lo + m;
             float gv[16];
+            // 8 columns at a time: their loads first (nothing here aliases
+            // another thread's elements), then the arithmetic and the stores
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int o = o0 + i;
-              gv[i] = 0.f;
-              if (o < g.O) {
-                const float a = sum[q][i];
-                const int64_t idx = ((int64_t)tl.b * g.O + o) * g.Lo + m;
-                fo.z[idx] = a;
-                const float rv = a > 0.0f ? a : (a < 0.0f ? 0.0f : (a == 0.0f ? 0.0f : a));
-                fo.r[idx] = rv;
-                const float dlt = __fadd_rn(rv, -__ldg(fo.t + idx));
-                lsum = __fadd_rn(lsum, __fmul_rn(fo.inv_n, __fmul_rn(dlt, dlt)));
-                const float cse1 = __fmul_rn(__fmul_rn(fo.inv_n, __fmul_rn(2.0f, dlt)), lb);
-                const float rb_in = fo.rb[idx];
-                const float rbt = __fadd_rn(rb_in, cse1);
-                fo.tb[idx] = __fadd_rn(fo.tb[idx], -cse1);
-                const float sg = a > 0.0f ? 1.0f : (a < 0.0f ? -1.0f : a);
-                const float zb_in = fo.zb[idx];
-                gv[i] = __fadd_rn(__fmul_rn(0.5f * (1.0f + sg), rbt), zb_in);
-                if (rb_in != 0.0f) fo.rb[idx] = 0.0f;
-                if (zb_in != 0.0f) fo.zb[idx] = 0.0f;
+            for (int h8 = 0; h8 < 16; h8 += 8) {
+              float tv[8], rbv[8], zbv[8], tbv[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int64_t idx = idx0 + (int64_t)(h8 + i) * g.Lo;
+                const bool in = o0 + h8 + i < g.O;
+                tv[i] = in ? __ldg(fo.t + idx) : 0.f;
+                rbv[i] = in ? fo.rb[idx] : 0.f;
+                zbv[i] = in ? fo.zb[idx] : 0.f;
+                tbv[i] = in ? fo.tb[idx] : 0.f;
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                gv[h8 + i] = 0.f;
+                if (o0 + h8 + i < g.O) {
+                  const int64_t idx = idx0 + (int64_t)(h8 + i) * g.Lo;
+                  const float a = sum[q][h8 + i];
+                  const float rv = a > 0.0f ? a : (a < 0.0f ? 0.0f : (a == 0.0f ? 0.0f : a));
+                  const float dlt = __fadd_rn(rv, -tv[i]);
+                  lsum = __fadd_rn(lsum, __fmul_rn(fo.inv_n, __fmul_rn(dlt, dlt)));
+                  const float cse1 = __fmul_rn(__fmul_rn(fo.inv_n, __fmul_rn(2.0f, dlt)), lb);
+                  const float rbt = __fadd_rn(rbv[i], cse1);
+                  const float sg = a > 0.0f ? 1.0f : (a < 0.0f ? -1.0f : a);
+                  gv[h8 + i] = __fadd_rn(__fmul_rn(0.5f * (1.0f + sg), rbt), zbv[i]);
+                  fo.z[idx] = a;
+                  fo.r[idx] = rv;
+                  fo.tb[idx] = __fadd_rn(tbv[i], -cse1);
+                  if (rbv[i] != 0.0f) fo.rb[idx] = 0.0f;
+                  if (zbv[i] != 0.0f) fo.zb[idx] = 0.0f;
+                }
               }
             }
             const int64_t gi = ((int64_t)tl.b * g.Lo + m) * g.O + o0;
@@ -357,14 +370,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
 #pragma unroll
           for (int q = 0; q < BN / 32; ++q) {
             const int c0 = tl.n0 + (half + 2 * q) * 16;
+            float* p0 = xb + ((int64_t)tl.b * g.C + c0) * g.L + m;
+            float old[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int c = c0 + i;
-              if (c < g.C) {
-                float* p = xb + ((int64_t)tl.b * g.C + c) * g.L + m;
-                *p = *p + sum[q][i];
-              }
-            }
+            for (int i = 0; i < 16; ++i) old[i] = c0 + i < g.C ? p0[(int64_t)i * g.L] : 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c0 + i < g.C) p0[(int64_t)i * g.L] = old[i] + sum[q][i];
           }
         }
       }
