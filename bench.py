@@ -81,7 +81,8 @@ class ClockSampler:
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,"
+              "timestamp")
 
     def __init__(self, device_index: int):
         self.proc = None
@@ -96,12 +97,22 @@ class ClockSampler:
                     "--format=csv,noheader,nounits", "-lms", "200"]
 
     def start(self):
+        """Starts sampling; call well before the timed region (nvidia-smi's
+        start-up must not overlap the timing) and bracket that region with
+        mark_begin / mark_end."""
+        self.window = None
+        self._t0 = None
         try:
             self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
-        time.sleep(0.3)
+
+    def mark_begin(self):
+        self._t0 = time.time()
+
+    def mark_end(self):
+        self.window = (self._t0, time.time())
 
     def stop(self):
         if not self.proc:
@@ -116,10 +127,17 @@ class ClockSampler:
         self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
+        import datetime
         rows = []
         for l in self.lines:
             parts = [p.strip() for p in l.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(parts[9], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                ts = None
+            if self.window and ts is not None and not (self.window[0] - 0.25 <= ts <= self.window[1] + 0.25):
                 continue
             try:
                 rows.append(dict(sm=float(parts[1]), smax=float(parts[2]),
@@ -802,6 +820,9 @@ def main():
     # device-resident timed run: one step captured in a CUDA graph and
     # replayed (N = 1; eager at N > 1, where the step holds NCCL calls on a
     # non-blocking communicator), phase profiler off
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_setup = time.time()
     for _ in range(args.warmup):
         W.step()
     torch.cuda.synchronize()
@@ -826,11 +847,11 @@ def main():
             graph = None
             step_fn = W.step
             print(f"# graph capture failed, timing eager launches: {e!r}", file=sys.stderr)
-    clocks = ClockSampler(local)
-    clocks.start()
+    time.sleep(max(0.0, 1.5 - (time.time() - t_setup)))  # nvidia-smi is up and sampling
+    clocks.mark_begin()
     total_ms, per = timed_loop(torch, step_fn, args.steps, 0, world, dist,
                                flush if W.flush_l2 else None, stream)
-    clocks.stop()
+    clocks.mark_end()
     ms_per_step = total_ms / args.steps
     value = 1000.0 / ms_per_step if W.scaling == "strong" else world * 1000.0 / ms_per_step
 
@@ -858,6 +879,7 @@ def main():
                "d2h_bytes_per_step": d2h * (world if W.scaling == "strong" else 1),
                "ms_per_step": e_ms / args.steps}
 
+    clocks.stop()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = W.cpu_baseline(args.cpu_seconds)

@@ -224,6 +224,57 @@ stade_status stade_mlp2_ce_hv_f64(double* loss, const double* lossb,
                                   const stade_opts* opts);
 
 /* ---------------------------------------------------------------------------
+ * Tangent (forward-mode) sweeps `<k>_d`. Replace the functions
+ * `stade_tangent_file` writes (tgen_emit, src/STADE.jl:3271-3279): one sweep
+ * in primal order, every active statement preceded by its tangent line.
+ * Arguments in tgen_signature_args order (src/STADE.jl:3306-3316): each float
+ * argument followed by its `d` shadow, integer sizes once. Scratch arrays and
+ * their shadows are overwritten; loss and lossd accumulate. No scalar argument
+ * of these primals is reassigned, so nothing is returned (a scalar's tangent,
+ * alphad, is passed by value).
+ * ------------------------------------------------------------------------- */
+size_t stade_affine_ls_d_f64_workspace(int64_t n_s, int64_t n_o, int64_t n_i);
+stade_status stade_affine_ls_d_f64(double* loss, double* lossd,
+                                   const double* w, const double* wd,
+                                   const double* b, const double* bd,
+                                   const double* x, const double* xd,
+                                   const double* t, const double* td,
+                                   double* y, double* yd,
+                                   int64_t n_s, int64_t n_o, int64_t n_i,
+                                   const stade_opts* opts);
+size_t stade_mlp2_ce_d_f32_workspace(int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o);
+size_t stade_mlp2_ce_d_f64_workspace(int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o);
+stade_status stade_mlp2_ce_d_f32(float* loss, float* lossd, const float* x, const float* xd,
+                                 const float* y, const float* yd, const float* w1,
+                                 const float* w1d, const float* b1, const float* b1d,
+                                 const float* w2, const float* w2d, const float* b2,
+                                 const float* b2d, float* h, float* hd, float* z, float* zd,
+                                 float* p, float* pd, int64_t n_s, int64_t n_i, int64_t n_h,
+                                 int64_t n_o, const stade_opts* opts);
+stade_status stade_mlp2_ce_d_f64(double* loss, double* lossd, const double* x, const double* xd,
+                                 const double* y, const double* yd, const double* w1,
+                                 const double* w1d, const double* b1, const double* b1d,
+                                 const double* w2, const double* w2d, const double* b2,
+                                 const double* b2d, double* h, double* hd, double* z,
+                                 double* zd, double* p, double* pd, int64_t n_s, int64_t n_i,
+                                 int64_t n_h, int64_t n_o, const stade_opts* opts);
+size_t stade_heat2d_d_f64_workspace(int64_t n, int64_t n_step);
+/* On exit u == un and ud == und hold the final state and its tangent, as the
+ * generated copy loop leaves them. */
+stade_status stade_heat2d_d_f64(double* loss, double* lossd, double* u, double* ud,
+                                double* un, double* und, double alpha, double alphad,
+                                int64_t n, int64_t n_step, const stade_opts* opts);
+size_t stade_conv1d_relu_mse_d_f32_workspace(int64_t n_b, int64_t n_c, int64_t n_l,
+                                             int64_t n_o, int64_t n_k);
+stade_status stade_conv1d_relu_mse_d_f32(float* loss, float* lossd,
+                                         const float* x, const float* xd,
+                                         const float* w, const float* wd,
+                                         const float* t, const float* td,
+                                         float* z, float* zd, float* r, float* rd,
+                                         int64_t n_b, int64_t n_c, int64_t n_l,
+                                         int64_t n_o, int64_t n_k, const stade_opts* opts);
+
+/* ---------------------------------------------------------------------------
  * Data-parallel epilogue (replaces the MPI functions `ddpgen_` emits,
  * src/STADE.jl:17595-17696). One communicator per GPU, one process per GPU.
  * ------------------------------------------------------------------------- */

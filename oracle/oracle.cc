@@ -535,6 +535,149 @@ void conv1d_relu_mse_b(T* loss, const T* lossb, const T* x, T* xb, const T* w, T
 }
 
 // ---------------------------------------------------------------------------
+// Tangent (forward-mode) sweeps `<k>_d`, tgen_emit (src/STADE.jl:3271-3279):
+// one sweep in primal order; every active statement is preceded by its
+// shadow line computed from the pre-statement values, `vd = sum_i partial_i
+// * argd_i` (tgen_tangent_expr, src/STADE.jl:3350-3356, der_tangent_generic);
+// arguments in tgen_signature_args order (src/STADE.jl:3306-3316): each float
+// argument followed by its `d` shadow. No scalar argument is reassigned in
+// these primals, so nothing is returned.
+
+// C1 affine_ls_d
+template <class T>
+void affine_ls_d(T* loss, T* lossd, const T* w, const T* wd, const T* b, const T* bd,
+                 const T* x, const T* xd, const T* t, const T* td, T* y, T* yd,
+                 i64 n_s, i64 n_o, i64 n_i) {
+  for (i64 idx = 0; idx < n_s * n_o; ++idx) {
+    const i64 i_s = idx / n_o, i_o = idx % n_o;
+    T sd = bd[i_o], s = b[i_o];
+    for (i64 k = 0; k < n_i; ++k) {
+      const T wv = w[i_o * n_i + k], xv = x[i_s * n_i + k];
+      sd = sd + (wd[i_o * n_i + k] * xv + wv * xd[i_s * n_i + k]);
+      s = s + wv * xv;
+    }
+    yd[idx] = sd;
+    y[idx] = s;
+  }
+  for (i64 idx2 = 0; idx2 < n_s * n_o; ++idx2) {
+    const T d = y[idx2] - t[idx2];
+    lossd[0] = lossd[0] + T(0.5) * ((T(2) * d) * (yd[idx2] - td[idx2]));
+    loss[0] = loss[0] + T(0.5) * (d * d);
+  }
+}
+
+// C2 mlp2_ce_d (the forward half of mlp2_ce_hv: the same tangent lines)
+template <class T>
+void mlp2_ce_d(T* loss, T* lossd, const T* x, const T* xd, const T* y, const T* yd,
+               const T* w1, const T* w1d, const T* b1, const T* b1d, const T* w2, const T* w2d,
+               const T* b2, const T* b2d, T* h, T* hd, T* z, T* zd, T* p, T* pd,
+               i64 n_s, i64 n_i, i64 n_h, i64 n_o) {
+  for (i64 idx = 0; idx < n_s * n_h; ++idx) {
+    const i64 i_s = idx / n_h, j = idx % n_h;
+    T s1d = b1d[j], s1 = b1[j];
+    for (i64 k = 0; k < n_i; ++k) {
+      const T xv = x[i_s * n_i + k], wv = w1[k * n_h + j];
+      s1d = s1d + (xv * w1d[k * n_h + j] + wv * xd[i_s * n_i + k]);
+      s1 = s1 + xv * wv;
+    }
+    const T th = jl_tanh(s1);
+    hd[idx] = (T(1) - th * th) * s1d;
+    h[idx] = th;
+  }
+  for (i64 idx2 = 0; idx2 < n_s * n_o; ++idx2) {
+    const i64 i_s = idx2 / n_o, c = idx2 % n_o;
+    T s2d = b2d[c], s2 = b2[c];
+    for (i64 k = 0; k < n_h; ++k) {
+      const T hv = h[i_s * n_h + k], wv = w2[k * n_o + c];
+      s2d = s2d + (hv * w2d[k * n_o + c] + wv * hd[i_s * n_h + k]);
+      s2 = s2 + wv * hv;
+    }
+    zd[idx2] = s2d;
+    z[idx2] = s2;
+  }
+  for (i64 i_s = 0; i_s < n_s; ++i_s) {
+    const T* zr = z + i_s * n_o; const T* zdr = zd + i_s * n_o;
+    T* pr = p + i_s * n_o; T* pdr = pd + i_s * n_o;
+    T m = zr[0], md = zdr[0];
+    for (i64 c = 1; c < n_o; ++c) {
+      const T g1 = T(0.5) * (T(1) + jl_sign(m - zr[c]));
+      const T g2 = T(0.5) * (T(1) + jl_sign(zr[c] - m));
+      md = g1 * md + g2 * zdr[c];
+      m = jl_max(m, zr[c]);
+    }
+    for (i64 c = 0; c < n_o; ++c) {
+      const T e = jl_exp(zr[c] - m);
+      pdr[c] = e * (zdr[c] - md);
+      pr[c] = e;
+    }
+    T rs = T(0), rsd = T(0);
+    for (i64 c = 0; c < n_o; ++c) { rsd = rsd + pdr[c]; rs = rs + pr[c]; }
+    for (i64 c = 0; c < n_o; ++c) {
+      const T q = pr[c] / rs;
+      const T qd = pdr[c] / rs - (pr[c] / (rs * rs)) * rsd;
+      lossd[0] = lossd[0] - (yd[i_s * n_o + c] * jl_log(q) + y[i_s * n_o + c] * (qd / q));
+      loss[0] = loss[0] - y[i_s * n_o + c] * jl_log(q);
+    }
+  }
+}
+
+// C3 heat2d_d: un's shadow from u's before each step, then u = un with ud = und
+template <class T>
+void heat2d_d(T* loss, T* lossd, T* u, T* ud, T* un, T* und, T alpha, T alphad, i64 n,
+              i64 n_step) {
+  const i64 nn = n * n;
+  for (i64 it = 0; it < n_step; ++it) {
+    for (i64 idx = 0; idx < nn; ++idx) {
+      const i64 i = idx / n, j = idx % n;
+      const i64 up = ((i - 1 + n) % n) * n + j, dn = ((i + 1) % n) * n + j;
+      const i64 lf = i * n + (j - 1 + n) % n, rt = i * n + (j + 1) % n;
+      const T c = u[idx], cd = ud[idx];
+      const T lap = (((u[up] + u[dn]) + u[lf]) + u[rt]) - T(4) * c;
+      const T lapd = (((ud[up] + ud[dn]) + ud[lf]) + ud[rt]) - T(4) * cd;
+      und[idx] = cd + (alphad * lap + alpha * lapd);
+      un[idx] = c + alpha * lap;
+    }
+    for (i64 idx2 = 0; idx2 < nn; ++idx2) {
+      ud[idx2] = und[idx2];
+      u[idx2] = un[idx2];
+    }
+  }
+  for (i64 idx3 = 0; idx3 < nn; ++idx3) {
+    lossd[0] = lossd[0] + (T(2) * u[idx3]) * ud[idx3];
+    loss[0] = loss[0] + u[idx3] * u[idx3];
+  }
+}
+
+// C4 conv1d_relu_mse_d: max(a, 0)'s tangent 0.5 (1 + sign(a - 0)) ad
+template <class T>
+void conv1d_relu_mse_d(T* loss, T* lossd, const T* x, const T* xd, const T* w, const T* wd,
+                       const T* t, const T* td, T* z, T* zd, T* r, T* rd,
+                       i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  const i64 n_lo = n_l - n_k + 1;
+  const i64 nt = n_b * n_o * n_lo;
+  for (i64 idx = 0; idx < nt; ++idx) {
+    const i64 i_b = idx / (n_o * n_lo), i_o = (idx / n_lo) % n_o, i_t = idx % n_lo;
+    T a = T(0), ad = T(0);
+    for (i64 c = 0; c < n_c; ++c)
+      for (i64 k = 0; k < n_k; ++k) {
+        const i64 wi = (i_o * n_c + c) * n_k + k, xi = (i_b * n_c + c) * n_l + i_t + k;
+        ad = ad + (wd[wi] * x[xi] + w[wi] * xd[xi]);
+        a = a + w[wi] * x[xi];
+      }
+    zd[idx] = ad;
+    z[idx] = a;
+    rd[idx] = (T(0.5) * (T(1) + jl_sign(a - T(0)))) * ad;
+    r[idx] = jl_max(a, T(0));
+  }
+  const T inv_n = T(1) / T(nt);
+  for (i64 idx2 = 0; idx2 < nt; ++idx2) {
+    const T d = r[idx2] - t[idx2];
+    lossd[0] = lossd[0] + inv_n * ((T(2) * d) * (rd[idx2] - td[idx2]));
+    loss[0] = loss[0] + inv_n * (d * d);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Parallel CPU variants (timed CPU baseline only): samples split across host
 // threads, each with private copies of the summed shadows, then one
 // fixed-order sum. Same arithmetic per sample as the serial sweeps above.
@@ -635,6 +778,41 @@ void oracle_conv1d_relu_mse_b_f64(double* loss, const double* lossb, const doubl
                                   double* z, double* zb, double* r, double* rb,
                                   i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
   conv1d_relu_mse_b<double>(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k);
+}
+
+void oracle_affine_ls_d_f64(double* loss, double* lossd, const double* w, const double* wd,
+                            const double* b, const double* bd, const double* x, const double* xd,
+                            const double* t, const double* td, double* y, double* yd, i64 n_s,
+                            i64 n_o, i64 n_i) {
+  affine_ls_d<double>(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i);
+}
+
+#define MLP_D_ARGS(T)                                                                      \
+  T *loss, T *lossd, const T *x, const T *xd, const T *y, const T *yd, const T *w1,        \
+      const T *w1d, const T *b1, const T *b1d, const T *w2, const T *w2d, const T *b2,     \
+      const T *b2d, T *h, T *hd, T *z, T *zd, T *p, T *pd, i64 n_s, i64 n_i, i64 n_h, i64 n_o
+#define MLP_D_PASS loss, lossd, x, xd, y, yd, w1, w1d, b1, b1d, w2, w2d, b2, b2d, h, hd, z, zd, p, pd, n_s, n_i, n_h, n_o
+void oracle_mlp2_ce_d_f32(MLP_D_ARGS(float)) { mlp2_ce_d<float>(MLP_D_PASS); }
+void oracle_mlp2_ce_d_f64(MLP_D_ARGS(double)) { mlp2_ce_d<double>(MLP_D_PASS); }
+
+void oracle_heat2d_d_f64(double* loss, double* lossd, double* u, double* ud, double* un,
+                         double* und, double alpha, double alphad, i64 n, i64 n_step) {
+  heat2d_d<double>(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step);
+}
+
+void oracle_conv1d_relu_mse_d_f32(float* loss, float* lossd, const float* x, const float* xd,
+                                  const float* w, const float* wd, const float* t,
+                                  const float* td, float* z, float* zd, float* r, float* rd,
+                                  i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  conv1d_relu_mse_d<float>(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o,
+                           n_k);
+}
+void oracle_conv1d_relu_mse_d_f64(double* loss, double* lossd, const double* x, const double* xd,
+                                  const double* w, const double* wd, const double* t,
+                                  const double* td, double* z, double* zd, double* r, double* rd,
+                                  i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  conv1d_relu_mse_d<double>(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o,
+                            n_k);
 }
 
 }  // extern "C"

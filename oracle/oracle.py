@@ -45,6 +45,12 @@ def lib() -> C.CDLL:
         L.oracle_heat2d_b_f64.restype = D
         for n in ("oracle_conv1d_relu_mse_b_f32", "oracle_conv1d_relu_mse_b_f64"):
             getattr(L, n).argtypes = [P] * 12 + [I64] * 5
+        L.oracle_affine_ls_d_f64.argtypes = [P] * 12 + [I64] * 3
+        for n in ("oracle_mlp2_ce_d_f32", "oracle_mlp2_ce_d_f64"):
+            getattr(L, n).argtypes = [P] * 20 + [I64] * 4
+        L.oracle_heat2d_d_f64.argtypes = [P] * 6 + [D, D, I64, I64]
+        for n in ("oracle_conv1d_relu_mse_d_f32", "oracle_conv1d_relu_mse_d_f64"):
+            getattr(L, n).argtypes = [P] * 12 + [I64] * 5
         for f in L.oracle_affine_ls_b_f64, L.oracle_mlp2_ce_b_f32:
             f.restype = None
         _lib = L
@@ -113,3 +119,32 @@ def conv1d_relu_mse_b(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, 
     fn = lib().oracle_conv1d_relu_mse_b_f32 if dt == np.float32 else lib().oracle_conv1d_relu_mse_b_f64
     fn(*[_p(a, dt) for a in arrs], n_b, n_c, n_l, n_o, n_k)
     return None
+
+
+# ---- tangent (forward-mode) sweeps <k>_d, tgen_signature_args order ---------
+def affine_ls_d(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i):
+    f = np.float64
+    lib().oracle_affine_ls_d_f64(*[_p(a, f) for a in (loss, lossd, w, wd, b, bd, x, xd, t, td,
+                                                      y, yd)], n_s, n_o, n_i)
+
+
+def mlp2_ce_d(*args):
+    assert len(args) == 24
+    arrs, ints = args[:20], args[20:]
+    dt = arrs[0].dtype
+    fn = lib().oracle_mlp2_ce_d_f32 if dt == np.float32 else lib().oracle_mlp2_ce_d_f64
+    fn(*[_p(a, dt) for a in arrs], *ints)
+
+
+def heat2d_d(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step):
+    f = np.float64
+    lib().oracle_heat2d_d_f64(*[_p(a, f) for a in (loss, lossd, u, ud, un, und)], float(alpha),
+                              float(alphad), n, n_step)
+
+
+def conv1d_relu_mse_d(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o, n_k):
+    arrs = (loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd)
+    dt = arrs[0].dtype
+    fn = lib().oracle_conv1d_relu_mse_d_f32 if dt == np.float32 else \
+        lib().oracle_conv1d_relu_mse_d_f64
+    fn(*[_p(a, dt) for a in arrs], n_b, n_c, n_l, n_o, n_k)

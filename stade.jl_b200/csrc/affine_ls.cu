@@ -99,8 +99,7 @@ __global__ void affine_ls_finish_kernel(const double* __restrict__ part, int nbl
   const int len = nw + n_o + 1;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= len) return;
-  double acc = 0.0;
-  for (int p = nblk - 1; p >= 0; --p) acc += part[(size_t)p * len + e];
+  const double acc = ordered_sum(part + e, nblk, len, true);
   if (e < nw) wb[e] += acc;
   else if (e < nw + n_o) bb[e - nw] += acc;
   else loss[0] += acc;
@@ -254,4 +253,84 @@ extern "C" stade_status stade_affine_ls_b_f64_noalloc(double* loss, const double
                                                                 wb, bb, loss);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Tangent sweep affine_ls_d (tgen_emit, src/STADE.jl:3271-3279; restated in
+// oracle.cc affine_ls_d): one thread per (sample, output) computes y and yd
+// in the primal's statement order; loss / lossd per-block partials.
+namespace stade {
+namespace {
+
+__global__ void __launch_bounds__(256)
+affine_ls_d_kernel(const double* __restrict__ w, const double* __restrict__ wd,
+                   const double* __restrict__ b, const double* __restrict__ bd,
+                   const double* __restrict__ x, const double* __restrict__ xd,
+                   const double* __restrict__ t, const double* __restrict__ td,
+                   double* __restrict__ y, double* __restrict__ yd, int64_t n_s, int n_o,
+                   int n_i, double* __restrict__ part) {
+  __shared__ double red[32];
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  double l = 0.0, ld = 0.0;
+  if (idx < n_s * n_o) {
+    const int64_t i_s = idx / n_o;
+    const int i_o = (int)(idx % n_o);
+    double sd = bd[i_o], s = b[i_o];
+    for (int k = 0; k < n_i; ++k) {
+      const double wv = w[(int64_t)i_o * n_i + k], xv = x[i_s * n_i + k];
+      sd = __dadd_rn(sd, __dadd_rn(__dmul_rn(wd[(int64_t)i_o * n_i + k], xv),
+                                   __dmul_rn(wv, xd[i_s * n_i + k])));
+      s = __dadd_rn(s, __dmul_rn(wv, xv));
+    }
+    yd[idx] = sd;
+    y[idx] = s;
+    const double dl = __dadd_rn(s, -t[idx]);
+    ld = __dmul_rn(0.5, __dmul_rn(__dmul_rn(2.0, dl), __dadd_rn(sd, -td[idx])));
+    l = __dmul_rn(0.5, __dmul_rn(dl, dl));
+  }
+  l = block_sum(l, red);
+  __syncthreads();
+  ld = block_sum(ld, red);
+  if (threadIdx.x == 0) {
+    part[blockIdx.x] = l;
+    part[gridDim.x + blockIdx.x] = ld;
+  }
+}
+
+}  // namespace
+}  // namespace stade
+
+extern "C" size_t stade_affine_ls_d_f64_workspace(int64_t n_s, int64_t n_o, int64_t n_i) {
+  (void)n_i;
+  if (n_s <= 0 || n_o <= 0) return 256;
+  Sizer z;
+  z.take<double>(2 * (size_t)ceil_div_u(n_s * n_o, 256));
+  return z.bytes();
+}
+
+extern "C" stade_status stade_affine_ls_d_f64(double* loss, double* lossd, const double* w,
+                                              const double* wd, const double* b,
+                                              const double* bd, const double* x,
+                                              const double* xd, const double* t,
+                                              const double* td, double* y, double* yd,
+                                              int64_t n_s, int64_t n_o, int64_t n_i,
+                                              const stade_opts* opts) {
+  STADE_REQUIRE(n_s >= 0 && n_o >= 0 && n_i >= 0, "affine_ls_d: negative size");
+  if (n_s == 0 || n_o == 0) return STADE_OK;
+  STADE_REQUIRE(loss && lossd && w && wd && b && bd && x && xd && t && td && y && yd,
+                "affine_ls_d: null array argument");
+  STADE_REQUIRE(n_s * n_o < (int64_t(1) << 40) && n_i < (1 << 30), "affine_ls_d: size overflow");
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(opts, stade_affine_ls_d_f64_workspace(n_s, n_o, n_i), &wsp);
+  if (st != STADE_OK) return st;
+  const unsigned blocks = ceil_div_u(n_s * n_o, 256);
+  Carver c(wsp);
+  double* part = c.take<double>(2 * (size_t)blocks);
+  affine_ls_d_kernel<<<blocks, 256, 0, s>>>(w, wd, b, bd, x, xd, t, td, y, yd, n_s, (int)n_o,
+                                            (int)n_i, part);
+  STADE_CHECK_LAUNCH();
+  st = launch_sum_to_scalar(part, blocks, loss, true, s);
+  if (st == STADE_OK) st = launch_sum_to_scalar(part + blocks, (int64_t)blocks, lossd, true, s);
+  return st;
 }

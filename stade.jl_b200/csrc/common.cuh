@@ -133,6 +133,31 @@ __device__ __forceinline__ T block_sum(T v, T* red) {
 // Sums `count` partial vectors of length `len` (partials[p * len + e]) in the
 // fixed order p = 0, 1, ..., and adds the result into dst[e] (or stores it
 // when `accumulate` is false). One thread per element: deterministic.
+
+// sum over q of v[q * stride] added in the order q = 0, 1, ..., count - 1
+// (reverse: count - 1 down to 0); the loads are issued 8 at a time so their
+// latencies overlap, the additions stay in that order.
+template <class T>
+__device__ __forceinline__ T ordered_sum(const T* __restrict__ v, int count, int64_t stride,
+                                         bool reverse = false) {
+  T acc = T(0);
+  int p = 0;
+  for (; p + 8 <= count; p += 8) {
+    T r[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = reverse ? count - 1 - (p + u) : p + u;
+      r[u] = v[(int64_t)q * stride];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = acc + r[u];
+  }
+  for (; p < count; ++p) {
+    const int q = reverse ? count - 1 - p : p;
+    acc = acc + v[(int64_t)q * stride];
+  }
+  return acc;
+}
 template <class T>
 __global__ void reduce_partials_kernel(const T* __restrict__ partials, int64_t len, int count,
                                        T* __restrict__ dst, bool accumulate) {

@@ -251,3 +251,129 @@ extern "C" stade_status stade_conv1d_relu_mse_b_f32(float* loss, const float* lo
   }
   return st;
 }
+
+// ---------------------------------------------------------------------------
+// Tangent sweep conv1d_relu_mse_d (tgen_emit, src/STADE.jl:3271-3279;
+// restated in oracle.cc conv1d_relu_mse_d): z = conv(x, w) and
+// zd = conv(xd, w) + conv(x, wd) as two implicit GEMMs (the second over a
+// doubled K: [w | wd] against [Xcol(xd) ; Xcol(x)]), the elementwise tail
+// and the loss partials in the second one's epilogue.
+namespace stade {
+namespace {
+
+struct EpiConvZ : EpiBase {  // z[b, o, t] = acc
+  float* z;
+  ConvDims d;
+  __device__ __forceinline__ void operator()(int o, int n, float a) const {
+    const int b = n / d.n_lo, tt = n - b * d.n_lo;
+    z[((int64_t)b * d.n_o + o) * d.n_lo + tt] = a;
+  }
+};
+struct LdW2 {  // A(o, kk2) = [w | wd](o, kk2)
+  const float *w, *wd;
+  int ck;
+  __device__ __forceinline__ float operator()(int m, int k) const {
+    return k < ck ? w[(int64_t)m * ck + k] : wd[(int64_t)m * ck + (k - ck)];
+  }
+};
+struct LdXcol2 {  // B(kk2, n) = [Xcol(xd) ; Xcol(x)](kk2, n)
+  const float *xd, *x;
+  ConvDims d;
+  __device__ __forceinline__ float operator()(int kk2, int n) const {
+    const int ck = d.n_c * d.n_k;
+    const float* src = kk2 < ck ? xd : x;
+    const int kk = kk2 < ck ? kk2 : kk2 - ck;
+    const int b = n / d.n_lo, t = n - b * d.n_lo;
+    const int c = kk / d.n_k, k = kk - c * d.n_k;
+    return src[((int64_t)b * d.n_c + c) * d.n_l + t + k];
+  }
+};
+struct EpiConvTan {
+  const float *z, *t, *td;
+  float *zd, *r, *rd;
+  float inv_n;
+  ConvDims d;
+  float* part;  // [2][blocks]: loss, lossd
+  int64_t nblk;
+  mutable float lsum, ldsum;
+  __device__ __forceinline__ void operator()(int o, int n, float ad) const {
+    const int b = n / d.n_lo, tt = n - b * d.n_lo;
+    const int64_t idx = ((int64_t)b * d.n_o + o) * d.n_lo + tt;
+    const float a = z[idx];
+    zd[idx] = ad;
+    const float sg = a > 0.0f ? 1.0f : (a < 0.0f ? -1.0f : a);
+    const float rdv = __fmul_rn(0.5f * (1.0f + sg), ad);
+    rd[idx] = rdv;
+    const float rv = a > 0.0f ? a : (a < 0.0f ? 0.0f : (a == 0.0f ? 0.0f : a));
+    r[idx] = rv;
+    const float dlt = __fadd_rn(rv, -t[idx]);
+    ldsum = __fadd_rn(ldsum, __fmul_rn(inv_n, __fmul_rn(__fmul_rn(2.0f, dlt),
+                                                         __fadd_rn(rdv, -td[idx]))));
+    lsum = __fadd_rn(lsum, __fmul_rn(inv_n, __fmul_rn(dlt, dlt)));
+  }
+  __device__ __forceinline__ void finish(int64_t blk) const {
+    __shared__ float red[32];
+    const float v = block_sum(lsum, red);
+    __syncthreads();
+    const float w = block_sum(ldsum, red);
+    if (threadIdx.x == 0) {
+      part[blk] = v;
+      part[nblk + blk] = w;
+    }
+  }
+};
+
+}  // namespace
+}  // namespace stade
+
+extern "C" size_t stade_conv1d_relu_mse_d_f32_workspace(int64_t n_b, int64_t n_c, int64_t n_l,
+                                                        int64_t n_o, int64_t n_k) {
+  if (n_b <= 0 || n_c <= 0 || n_o <= 0 || n_k <= 0 || n_l < n_k) return 256;
+  const int64_t ncol = n_b * (n_l - n_k + 1);
+  const int64_t blocks = ((n_o + 127) / 128) * ((ncol + 127) / 128);
+  Sizer z;
+  z.take<float>((size_t)(2 * blocks));
+  return z.bytes();
+}
+
+extern "C" stade_status stade_conv1d_relu_mse_d_f32(float* loss, float* lossd, const float* x,
+                                                    const float* xd, const float* w,
+                                                    const float* wd, const float* t,
+                                                    const float* td, float* z, float* zd,
+                                                    float* r, float* rd, int64_t n_b,
+                                                    int64_t n_c, int64_t n_l, int64_t n_o,
+                                                    int64_t n_k, const stade_opts* opts) {
+  STADE_REQUIRE(n_b >= 0 && n_c >= 0 && n_l >= 0 && n_o >= 0 && n_k >= 0,
+                "conv1d_relu_mse_d: negative size");
+  const int64_t n_lo = n_l - n_k + 1;
+  if (n_b == 0 || n_o == 0 || n_lo <= 0) return STADE_OK;
+  STADE_REQUIRE(n_c > 0 && n_k > 0, "conv1d_relu_mse_d: n_c and n_k must be positive");
+  STADE_REQUIRE(n_b * n_lo < (int64_t(1) << 31) && n_c * n_k < (1 << 19),
+                "conv1d_relu_mse_d: sizes out of range");
+  STADE_REQUIRE(loss && lossd && x && xd && w && wd && t && td && z && zd && r && rd,
+                "conv1d_relu_mse_d: null array argument");
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(
+      opts, stade_conv1d_relu_mse_d_f32_workspace(n_b, n_c, n_l, n_o, n_k), &wsp);
+  if (st != STADE_OK) return st;
+  const ConvDims d{(int)n_b, (int)n_c, (int)n_l, (int)n_o, (int)n_k, (int)n_lo};
+  const int ncol = (int)(n_b * n_lo), ck = (int)(n_c * n_k);
+  const int64_t blocks = ((n_o + 127) / 128) * ((ncol + 127) / 128);
+  Carver c(wsp);
+  float* part = c.take<float>((size_t)(2 * blocks));
+  const float inv_n = 1.0f / (float)(n_b * n_o * n_lo);
+  {
+    PhaseScope ph("d_conv", s);
+    st = gemm_simt<float, RM, RN, BK, true, true>((int)n_o, ncol, ck, LdW{w, ck}, LdXcol{x, d},
+                                                  EpiConvZ{{}, z, d}, nullptr, 1, s);
+    if (st == STADE_OK)
+      st = gemm_simt<float, RM, RN, BK, true, true>(
+          (int)n_o, ncol, 2 * ck, LdW2{w, wd, ck}, LdXcol2{xd, x, d},
+          EpiConvTan{z, t, td, zd, r, rd, inv_n, d, part, blocks, 0.0f, 0.0f}, nullptr, 1, s);
+  }
+  if (st != STADE_OK) return st;
+  st = launch_sum_to_scalar(part, blocks, loss, true, s);
+  if (st == STADE_OK) st = launch_sum_to_scalar(part + blocks, blocks, lossd, true, s);
+  return st;
+}

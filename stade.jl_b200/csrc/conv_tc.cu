@@ -459,8 +459,7 @@ __global__ void wgrad_finish_kernel(const float* __restrict__ part, int slices, 
   const int c = (int)(r % g.C), o = (int)(r / g.C);
   const int64_t col = (int64_t)o * g.nw + (int64_t)k * g.cpad + c;
   const int64_t stride = (int64_t)g.O * g.nw;
-  float acc = 0.f;
-  for (int s = 0; s < slices; ++s) acc += part[(int64_t)s * stride + col];
+  const float acc = ordered_sum(part + col, slices, stride);
   wb[e] += acc;
 }
 

@@ -165,7 +165,7 @@ __global__ void gemm_splitk_finish_kernel(const T* __restrict__ partial, int spl
   const int64_t MN = (int64_t)M * N;
   if (e < MN) {
     T acc = T(0);
-    for (int z = 0; z < splits; ++z) acc += partial[(int64_t)z * MN + e];
+    acc = ordered_sum(partial + e, splits, MN);
     epi((int)(e / N), (int)(e % N), acc);
   }
   epi.finish((int64_t)blockIdx.x);

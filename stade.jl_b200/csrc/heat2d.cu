@@ -21,6 +21,8 @@
 // keeping the rows above and below in registers; horizontal neighbours come
 // from the neighbouring lanes by warp shuffle. alphab and loss are summed per
 // block, then over blocks in a fixed order.
+#include <utility>
+
 #include "common.cuh"
 #include "halo.cuh"
 
@@ -509,4 +511,102 @@ extern "C" stade_status stade_heat2d_b_f64_slab(double* loss, const double* loss
     return comm_wait_stream(comm, s);
   }
   return STADE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Tangent sweep heat2d_d (tgen_emit, src/STADE.jl:3271-3279; restated in
+// oracle.cc heat2d_d): per step und from ud and alphad before un, then
+// u = un, ud = und; loss and lossd accumulate at the end. The two state
+// buffers alternate between u and un, and after the last step both hold the
+// final state (the generated copy loop leaves u == un).
+namespace stade {
+namespace {
+
+__global__ void __launch_bounds__(256)
+heat_tan_step_kernel(const double* __restrict__ u, const double* __restrict__ ud,
+                     double* __restrict__ un, double* __restrict__ und, double alpha,
+                     double alphad, int n) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int i = blockIdx.y;
+  if (j >= n) return;
+  const int iu = i == 0 ? n - 1 : i - 1, id = i + 1 == n ? 0 : i + 1;
+  const int jl = j == 0 ? n - 1 : j - 1, jr = j + 1 == n ? 0 : j + 1;
+  const int64_t r = (int64_t)i * n;
+  const double c = u[r + j], cd = ud[r + j];
+  const double lap = __dadd_rn(__dadd_rn(__dadd_rn(__dadd_rn(u[(int64_t)iu * n + j],
+                                                              u[(int64_t)id * n + j]),
+                                                     u[r + jl]),
+                                            u[r + jr]),
+                               -__dmul_rn(4.0, c));
+  const double lapd = __dadd_rn(__dadd_rn(__dadd_rn(__dadd_rn(ud[(int64_t)iu * n + j],
+                                                               ud[(int64_t)id * n + j]),
+                                                      ud[r + jl]),
+                                             ud[r + jr]),
+                                -__dmul_rn(4.0, cd));
+  und[r + j] = __dadd_rn(cd, __dadd_rn(__dmul_rn(alphad, lap), __dmul_rn(alpha, lapd)));
+  un[r + j] = __dadd_rn(c, __dmul_rn(alpha, lap));
+}
+
+// loss += sum u^2, lossd += sum 2 u ud: per-block partials.
+__global__ void heat_tan_loss_kernel(const double* __restrict__ u, const double* __restrict__ ud,
+                                     int64_t nn, double* __restrict__ part) {
+  __shared__ double red[32];
+  double a = 0.0, b = 0.0;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nn;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const double v = u[e];
+    a += __dmul_rn(v, v);
+    b += __dmul_rn(__dmul_rn(2.0, v), ud[e]);
+  }
+  a = block_sum(a, red);
+  b = block_sum(b, red);
+  if (threadIdx.x == 0) {
+    part[blockIdx.x] = a;
+    part[gridDim.x + blockIdx.x] = b;
+  }
+}
+
+}  // namespace
+}  // namespace stade
+
+extern "C" size_t stade_heat2d_d_f64_workspace(int64_t n, int64_t n_step) {
+  (void)n; (void)n_step;
+  Sizer z;
+  z.take<double>(2 * (size_t)kNoStepBlocks);
+  return z.bytes();
+}
+
+extern "C" stade_status stade_heat2d_d_f64(double* loss, double* lossd, double* u, double* ud,
+                                           double* un, double* und, double alpha, double alphad,
+                                           int64_t n, int64_t n_step, const stade_opts* opts) {
+  STADE_REQUIRE(n >= 0 && n_step >= 0, "heat2d_d: negative size");
+  if (n == 0) return STADE_OK;
+  STADE_REQUIRE(n >= 3 && n <= 65536, "heat2d_d: n = %lld outside 3..65536", (long long)n);
+  STADE_REQUIRE(loss && lossd && u && ud && un && und, "heat2d_d: null array argument");
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(opts, stade_heat2d_d_f64_workspace(n, n_step), &wsp);
+  if (st != STADE_OK) return st;
+  Carver c(wsp);
+  double* part = c.take<double>(2 * (size_t)kNoStepBlocks);
+  const int64_t nn = n * n;
+  const dim3 grid(ceil_div_u(n, 256), (unsigned)n);
+  double *a = u, *ad = ud, *b = un, *bd = und;
+  for (int64_t t = 0; t < n_step; ++t) {
+    PhaseScope ph("d_step", s);
+    heat_tan_step_kernel<<<grid, 256, 0, s>>>(a, ad, b, bd, alpha, alphad, (int)n);
+    STADE_CHECK_LAUNCH();
+    std::swap(a, b);
+    std::swap(ad, bd);
+  }
+  if (n_step > 0) {
+    // the final state is in (a, ad); the generated copy leaves it in both pairs
+    STADE_CUDA(cudaMemcpyAsync(b, a, (size_t)nn * sizeof(double), cudaMemcpyDeviceToDevice, s));
+    STADE_CUDA(cudaMemcpyAsync(bd, ad, (size_t)nn * sizeof(double), cudaMemcpyDeviceToDevice, s));
+  }
+  heat_tan_loss_kernel<<<kNoStepBlocks, 256, 0, s>>>(a, ad, nn, part);
+  STADE_CHECK_LAUNCH();
+  st = launch_sum_to_scalar(part, kNoStepBlocks, loss, true, s);
+  if (st == STADE_OK) st = launch_sum_to_scalar(part + kNoStepBlocks, kNoStepBlocks, lossd, true, s);
+  return st;
 }

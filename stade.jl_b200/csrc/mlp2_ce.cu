@@ -446,7 +446,9 @@ mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
       *reinterpret_cast<float4*>(s1b_hi + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
       *reinterpret_cast<float4*>(s1b_lo + off) =
           make_float4(o[0] - hi[0], o[1] - hi[1], o[2] - hi[2], o[3] - hi[3]);
-      *reinterpret_cast<float4*>(hb + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+      // hb is consumed: zero it (only where it held a seed; a zero stays zero)
+      if (acc4.x != 0.f || acc4.y != 0.f || acc4.z != 0.f || acc4.w != 0.f)
+        *reinterpret_cast<float4*>(hb + off) = make_float4(0.f, 0.f, 0.f, 0.f);
     };
     int i = 0;
     for (; i + 4 <= ns; i += 4) {
@@ -519,10 +521,21 @@ __global__ void finish_two_kernel(const T* __restrict__ part, int count, int64_t
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t len = len1 + len2;
   if (e >= len) return;
-  T acc = T(0);
-  for (int p = 0; p < count; ++p) acc += part[(int64_t)p * len + e];
+  const T acc = ordered_sum(part + e, count, len);
   if (e < len1) dst1[e] += acc;
   else dst2[e - len1] += acc;
+}
+
+// First level of a fixed-order sum of `count` partial records of length len:
+// group g (blockIdx.y) adds records [g per, (g + 1) per) in order into
+// out[g][len]. finish_three_kernel then adds the groups in order.
+__global__ void sum_groups_kernel(const float* __restrict__ part, int count, int per, int64_t len,
+                                  float* __restrict__ out) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= len) return;
+  const int p0 = blockIdx.y * per, p1 = min(count, p0 + per);
+  const float acc = ordered_sum(part + (int64_t)p0 * len + e, p1 - p0, len);
+  out[(int64_t)blockIdx.y * len + e] = acc;
 }
 
 // Sums partial records [chunk][len1 + len2 + len3] in chunk order into three arrays.
@@ -533,8 +546,7 @@ __global__ void finish_three_kernel(const float* __restrict__ part, int count, i
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t len = len1 + len2 + len3;
   if (e >= len) return;
-  float acc = 0.f;
-  for (int p = 0; p < count; ++p) acc += part[(int64_t)p * len + e];
+  const float acc = ordered_sum(part + e, count, len);
   if (e < len1) dst1[e] += acc;
   else if (e < len1 + len2) dst2[e - len1] += acc;
   else dst3[e - len1 - len2] += acc;
@@ -642,10 +654,10 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
   __syncthreads();
   const unsigned F = 0xffffffffu;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int s = blockIdx.x * kHeadWarps + warp;
   const double lb = lossb[0], lbd = lossbd[0];
   double loss_acc = 0.0, lossd_acc = 0.0;
-  if (s < n_s) {
+  // the block stages W2 / W2d once and its warps take samples block-strided
+  for (int s = blockIdx.x * kHeadWarps + warp; s < n_s; s += gridDim.x * kHeadWarps) {
     const double* hr = h + (int64_t)s * n_h;
     const double* hdr = hd + (int64_t)s * n_h;
     double zp[NO], zdp[NO];
@@ -869,8 +881,7 @@ __global__ void finish_four_kernel(const double* __restrict__ part, int count, i
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t len = 2 * nw + 2 * n_o;
   if (e >= len) return;
-  double acc = 0.0;
-  for (int q = 0; q < count; ++q) acc += part[(int64_t)q * len + e];
+  const double acc = ordered_sum(part + e, count, len);
   if (e < nw) w2b[e] += acc;
   else if (e < 2 * nw) w2bd[e - nw] += acc;
   else if (e < 2 * nw + n_o) b2b[e - 2 * nw] += acc;
@@ -937,7 +948,9 @@ struct MlpF64HvWs {
 };
 template <class Alloc>
 void mlp_hv_layout(Alloc& a, MlpF64HvWs* w, int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o) {
-  const int head_blocks = (int)((n_s + kHeadWarps - 1) / kHeadWarps);
+  // two blocks per SM (W2 and W2d staged in shared memory), samples strided
+  const int head_need = (int)((n_s + kHeadWarps - 1) / kHeadWarps);
+  const int head_blocks = head_need < 2 * 148 ? head_need : 2 * 148;
   const int w2_chunks = (int)((n_s + kW2Chunk - 1) / kW2Chunk);
   const int w1_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, (int)n_s);
   const int w1d_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, 2 * (int)n_s);
@@ -968,8 +981,10 @@ void mlp_hv_layout(Alloc& a, MlpF64HvWs* w, int64_t n_s, int64_t n_i, int64_t n_
 namespace {
 constexpr int kW2ChunkTc = 64;  // samples per W2b partial on the tensor-core paths
 
+constexpr int kFinGroups = 16;  // first-level groups of the W2b / b2b / b1b partial sum
+
 struct MlpF32Ws {
-  float *s1b, *gbuf, *loss_part, *w2_part, *w1_part, *zpart;
+  float *s1b, *gbuf, *loss_part, *w2_part, *w1_part, *zpart, *fin;
   float *x_hi, *x_lo, *w1_hi, *w1_lo, *s1b_hi, *s1b_lo, *w1b_part;
   int head_blocks, w2_chunks, w1_splits;
 };
@@ -1011,7 +1026,9 @@ void mlp_f32_layout(Alloc& a, MlpF32Ws* w, int64_t n_s, int64_t n_i, int64_t n_h
   auto sh = a.template take<float>(planes ? (size_t)(n_s * n_h) : 1);
   auto sl = a.template take<float>(planes ? (size_t)(n_s * n_h) : 1);
   auto wp = a.template take<float>(planes ? tma_w1b_part_floats(n_s, n_i, n_h) : 1);
+  auto fin = a.template take<float>((size_t)kFinGroups * (size_t)(n_h * n_o + n_o + n_h));
   if (w) {
+    w->fin = (float*)fin;
     w->s1b = (float*)s1b; w->gbuf = (float*)gb; w->loss_part = (float*)lp;
     w->w2_part = (float*)w2p; w->w1_part = (float*)w1p; w->zpart = (float*)zp;
     w->x_hi = (float*)xh; w->x_lo = (float*)xl; w->w1_hi = (float*)wh; w->w1_lo = (float*)wl;
@@ -1111,8 +1128,15 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
       kern<<<dim3(chunks, (H + 511) / 512), 128, smem, s>>>(h, hb, w.gbuf, w2, w.s1b_hi, w.s1b_lo,
                                                             S, H, O, kW2ChunkTc, w.w2_part);
       STADE_CHECK_LAUNCH();
-      finish_three_kernel<<<ceil_div_u(n_h * n_o + n_o + n_h, 256), 256, 0, s>>>(
-          w.w2_part, chunks, n_h * n_o, w2b, n_o, b2b, n_h, b1b);
+      // chunk partials -> kFinGroups group sums -> the three outputs, fixed order
+      const int64_t len = n_h * n_o + n_o + n_h;
+      const int per = (chunks + kFinGroups - 1) / kFinGroups;
+      const int groups = (chunks + per - 1) / per;
+      sum_groups_kernel<<<dim3(ceil_div_u(len, 256), groups), 256, 0, s>>>(w.w2_part, chunks, per,
+                                                                          len, w.fin);
+      STADE_CHECK_LAUNCH();
+      finish_three_kernel<<<ceil_div_u(len, 256), 256, 0, s>>>(w.fin, groups, n_h * n_o, w2b, n_o,
+                                                               b2b, n_h, b1b);
       STADE_CHECK_LAUNCH();
     }
     // 4. W1b = x^T s1b, 5. xb += s1b W1^T
@@ -1330,4 +1354,230 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
           EpiAddTo<double>{{}, xbd, I}, nullptr, 1, s);
   }
   return st;
+}
+
+// ============================================================================
+// Tangent sweep mlp2_ce_d (tgen_emit, src/STADE.jl:3271-3279): the primal in
+// order with every active statement preceded by its tangent line, arguments
+// in tgen_signature_args order (src/STADE.jl:3306-3316). Restated in
+// oracle.cc mlp2_ce_d (the forward half of the HVP sweep).
+// ============================================================================
+namespace stade {
+namespace {
+
+template <class T>
+struct EpiStoreT : EpiBase {  // dst[m, n] = acc
+  T* dst;
+  int ld;
+  __device__ __forceinline__ void operator()(int m, int n, T acc) const {
+    dst[(int64_t)m * ld + n] = acc;
+  }
+};
+// s1d = acc + b1d (acc = sum x w1d + xd w1); h = tanh(S1 + b1); hd = (1 - h^2) s1d
+template <class T>
+struct EpiTanhTangentT : EpiBase {
+  const T *s1, *b1, *b1d;
+  T *h, *hd;
+  int ld;
+  __device__ __forceinline__ void operator()(int m, int n, T acc) const {
+    const int64_t i = (int64_t)m * ld + n;
+    const T s1d = acc + b1d[n];
+    const T th = dtanh(s1[i] + b1[n]);
+    hd[i] = (T(1) - th * th) * s1d;
+    h[i] = th;
+  }
+};
+template <class T>
+struct LdRow2T {  // A(m, k) over two K segments [a0 | a1]
+  const T *a0, *a1;
+  int ld, k0;
+  __device__ __forceinline__ T operator()(int m, int k) const {
+    return k < k0 ? a0[(int64_t)m * ld + k] : a1[(int64_t)m * ld + (k - k0)];
+  }
+};
+template <class T>
+struct LdB2T {  // B(k, n) over two K segments [b0 ; b1]
+  const T *b0, *b1;
+  int ld, k0;
+  __device__ __forceinline__ T operator()(int k, int n) const {
+    return k < k0 ? b0[(int64_t)k * ld + n] : b1[(int64_t)(k - k0) * ld + n];
+  }
+};
+
+// Per-sample head of the tangent sweep: logits and their tangents, the
+// running max through max's partials, exp, the row sum and the loss with its
+// tangent. One warp per sample, blocks strided over the samples.
+template <class T, int NO>
+__global__ void __launch_bounds__(kHeadWarps * 32)
+mlp_head_d_kernel(const T* __restrict__ y, const T* __restrict__ yd, const T* __restrict__ w2,
+                  const T* __restrict__ b2, const T* __restrict__ w2d,
+                  const T* __restrict__ b2d, const T* __restrict__ h,
+                  const T* __restrict__ hd, T* __restrict__ z, T* __restrict__ zd,
+                  T* __restrict__ p, T* __restrict__ pd, int n_s, int n_h, int n_o,
+                  T* __restrict__ loss_part, T* __restrict__ lossd_part) {
+  __shared__ T red[2][kHeadWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  T loss_acc = T(0), lossd_acc = T(0);
+  for (int s = blockIdx.x * kHeadWarps + warp; s < n_s; s += gridDim.x * kHeadWarps) {
+    const T* hr = h + (int64_t)s * n_h;
+    const T* hdr = hd + (int64_t)s * n_h;
+    T zp[NO], zdp[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) { zp[c] = T(0); zdp[c] = T(0); }
+    for (int k = lane; k < n_h; k += 32) {
+      const T hv = hr[k], hdv = hdr[k];
+#pragma unroll
+      for (int c = 0; c < NO; ++c) {
+        if (c < n_o) {
+          const T wv = __ldg(w2 + (int64_t)k * n_o + c);
+          zdp[c] += hv * __ldg(w2d + (int64_t)k * n_o + c) + wv * hdv;
+          zp[c] += wv * hv;
+        }
+      }
+    }
+    T zv[NO], zdv[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      zv[c] = c < n_o ? warp_sum(zp[c]) + b2[c] : T(0);
+      zdv[c] = c < n_o ? warp_sum(zdp[c]) + b2d[c] : T(0);
+    }
+    T m = zv[0], md = zdv[0];
+#pragma unroll
+    for (int c = 1; c < NO; ++c) {
+      if (c < n_o) {
+        const T g1 = T(0.5) * (T(1) + dsign(m - zv[c]));
+        const T g2 = T(0.5) * (T(1) + dsign(zv[c] - m));
+        md = g1 * md + g2 * zdv[c];
+        m = jmax(m, zv[c]);
+      }
+    }
+    T pv[NO], pdv[NO];
+    T rs = T(0), rsd = T(0);
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      pv[c] = T(0);
+      pdv[c] = T(0);
+      if (c < n_o) {
+        const T e = dexp(zv[c] - m);
+        pdv[c] = e * (zdv[c] - md);
+        pv[c] = e;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < NO; ++c)
+      if (c < n_o) { rsd = rsd + pdv[c]; rs = rs + pv[c]; }
+    const int64_t row = (int64_t)s * n_o;
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        const T yv = __ldg(y + row + c), ydv = __ldg(yd + row + c);
+        const T q = pv[c] / rs;
+        const T qd = pdv[c] / rs - (pv[c] / (rs * rs)) * rsd;
+        lossd_acc = lossd_acc - (ydv * dlog(q) + yv * (qd / q));
+        loss_acc = loss_acc - yv * dlog(q);
+        if (lane == c) {
+          z[row + c] = zv[c]; zd[row + c] = zdv[c];
+          p[row + c] = pv[c]; pd[row + c] = pdv[c];
+        }
+      }
+    }
+  }
+  if (lane == 0) { red[0][warp] = loss_acc; red[1][warp] = lossd_acc; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    T a = T(0), b = T(0);
+    for (int w = 0; w < kHeadWarps; ++w) { a += red[0][w]; b += red[1][w]; }
+    loss_part[blockIdx.x] = a;
+    lossd_part[blockIdx.x] = b;
+  }
+}
+
+constexpr int kHeadDBlocks = 4 * 148;
+
+template <class T>
+size_t mlp_d_workspace(int64_t n_s, int64_t n_h) {
+  Sizer z;
+  z.take<T>((size_t)(n_s * n_h));   // s1 = x W1
+  z.take<T>(kHeadDBlocks);          // loss partials
+  z.take<T>(kHeadDBlocks);          // lossd partials
+  return z.bytes();
+}
+
+template <class T, int RM, int RN, int BK>
+stade_status mlp2_ce_d_impl(T* loss, T* lossd, const T* x, const T* xd, const T* y, const T* yd,
+                            const T* w1, const T* w1d, const T* b1, const T* b1d, const T* w2,
+                            const T* w2d, const T* b2, const T* b2d, T* h, T* hd, T* z, T* zd,
+                            T* p, T* pd, int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o,
+                            const stade_opts* opts, const char* name) {
+  STADE_REQUIRE(n_s >= 0 && n_i >= 0 && n_h >= 0 && n_o >= 0, "%s: negative size", name);
+  if (n_s == 0) return STADE_OK;
+  STADE_REQUIRE(n_o >= 1 && n_o <= 32, "%s: n_o = %lld outside 1..32", name, (long long)n_o);
+  STADE_REQUIRE(n_h > 0, "%s: n_h = 0 is not supported", name);
+  STADE_REQUIRE(n_s <= (1 << 29) && n_i < (1 << 20) && n_h < (1 << 16), "%s: sizes out of range",
+                name);
+  STADE_REQUIRE(loss && lossd && x && xd && y && yd && w1 && w1d && b1 && b1d && w2 && w2d && b2 &&
+                    b2d && h && hd && z && zd && p && pd,
+                "%s: null array argument", name);
+  cudaStream_t s = stream_of(opts);
+  void* wsp = nullptr;
+  stade_status st = get_workspace(opts, mlp_d_workspace<T>(n_s, n_h), &wsp);
+  if (st != STADE_OK) return st;
+  Carver c(wsp);
+  T* s1 = c.take<T>((size_t)(n_s * n_h));
+  T* lp = c.take<T>(kHeadDBlocks);
+  T* ldp = c.take<T>(kHeadDBlocks);
+  const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
+  {
+    PhaseScope ph("d_gemms", s);
+    st = gemm_simt<T, RM, RN, BK, true, true>(S, H, I, LdRow<T>{x, I}, LdB<T>{w1, H},
+                                              EpiStoreT<T>{{}, s1, H}, nullptr, 1, s);
+    if (st == STADE_OK)
+      st = gemm_simt<T, RM, RN, BK, true, true>(
+          S, H, 2 * I, LdRow2T<T>{x, xd, I, I}, LdB2T<T>{w1d, w1, H, I},
+          EpiTanhTangentT<T>{{}, s1, b1, b1d, h, hd, H}, nullptr, 1, s);
+  }
+  if (st != STADE_OK) return st;
+  PhaseScope ph("d_head", s);
+  const int need = (S + kHeadWarps - 1) / kHeadWarps;
+  const int blocks = need < kHeadDBlocks ? need : kHeadDBlocks;
+  if (O <= 16)
+    mlp_head_d_kernel<T, 16><<<blocks, kHeadWarps * 32, 0, s>>>(
+        y, yd, w2, b2, w2d, b2d, h, hd, z, zd, p, pd, S, H, O, lp, ldp);
+  else
+    mlp_head_d_kernel<T, 32><<<blocks, kHeadWarps * 32, 0, s>>>(
+        y, yd, w2, b2, w2d, b2d, h, hd, z, zd, p, pd, S, H, O, lp, ldp);
+  STADE_CHECK_LAUNCH();
+  st = launch_sum_to_scalar(lp, blocks, loss, true, s);
+  if (st == STADE_OK) st = launch_sum_to_scalar(ldp, blocks, lossd, true, s);
+  return st;
+}
+
+}  // namespace
+}  // namespace stade
+
+#define MLP_D_SIG(T)                                                                          \
+  T *loss, T *lossd, const T *x, const T *xd, const T *y, const T *yd, const T *w1,           \
+      const T *w1d, const T *b1, const T *b1d, const T *w2, const T *w2d, const T *b2,        \
+      const T *b2d, T *h, T *hd, T *z, T *zd, T *p, T *pd, int64_t n_s, int64_t n_i,          \
+      int64_t n_h, int64_t n_o, const stade_opts *opts
+#define MLP_D_FWD loss, lossd, x, xd, y, yd, w1, w1d, b1, b1d, w2, w2d, b2, b2d, h, hd, z, zd, p, \
+      pd, n_s, n_i, n_h, n_o, opts
+
+extern "C" size_t stade_mlp2_ce_d_f32_workspace(int64_t n_s, int64_t n_i, int64_t n_h,
+                                                int64_t n_o) {
+  (void)n_i; (void)n_o;
+  return n_s > 0 && n_h > 0 ? stade::mlp_d_workspace<float>(n_s, n_h) : 256;
+}
+extern "C" size_t stade_mlp2_ce_d_f64_workspace(int64_t n_s, int64_t n_i, int64_t n_h,
+                                                int64_t n_o) {
+  (void)n_i; (void)n_o;
+  return n_s > 0 && n_h > 0 ? stade::mlp_d_workspace<double>(n_s, n_h) : 256;
+}
+extern "C" stade_status stade_mlp2_ce_d_f32(MLP_D_SIG(float)) {
+  return stade::mlp2_ce_d_impl<float, stade::kF32RM, stade::kF32RN, stade::kF32BK>(
+      MLP_D_FWD, "mlp2_ce_d");
+}
+extern "C" stade_status stade_mlp2_ce_d_f64(MLP_D_SIG(double)) {
+  return stade::mlp2_ce_d_impl<double, stade::kF64RM, stade::kF64RN, stade::kF64BK>(
+      MLP_D_FWD, "mlp2_ce_d");
 }

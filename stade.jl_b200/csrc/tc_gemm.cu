@@ -482,7 +482,7 @@ __global__ void tc_splitk_finish_kernel(const float* __restrict__ part, int spli
   const int64_t MN = (int64_t)M * N;
   if (e >= MN) return;
   float acc = 0.f;
-  for (int z = 0; z < splits; ++z) acc += part[(int64_t)z * MN + e];
+  acc = ordered_sum(part + e, splits, MN);
   const int m = (int)(e / N), n = (int)(e % N);
   if (m < n_w) w[(int64_t)m * N + n] += acc;
   else bias[n] += acc;

@@ -509,7 +509,7 @@ __global__ void w1b_finish_kernel(const float* __restrict__ part, int slices, in
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= MN) return;
   float acc = 0.f;
-  for (int z = 0; z < slices; ++z) acc += part[(int64_t)z * MN + e];
+  acc = ordered_sum(part + e, slices, MN);
   w1b[e] += acc;
 }
 

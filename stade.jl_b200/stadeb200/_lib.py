@@ -65,6 +65,16 @@ SIGNATURES = {
     "stade_initstacks_heat2d_b": (I64, [I64, I64]),
     "stade_heat2d_b_f64_workspace": (C.c_size_t, [I64, I64]),
     "stade_heat2d_b_f64": (ST, [P] * 6 + [D, P, I64, I64, P, OPTS]),
+    "stade_affine_ls_d_f64_workspace": (C.c_size_t, [I64] * 3),
+    "stade_affine_ls_d_f64": (ST, [P] * 12 + [I64] * 3 + [OPTS]),
+    "stade_mlp2_ce_d_f32_workspace": (C.c_size_t, [I64] * 4),
+    "stade_mlp2_ce_d_f64_workspace": (C.c_size_t, [I64] * 4),
+    "stade_mlp2_ce_d_f32": (ST, [P] * 20 + [I64] * 4 + [OPTS]),
+    "stade_mlp2_ce_d_f64": (ST, [P] * 20 + [I64] * 4 + [OPTS]),
+    "stade_heat2d_d_f64_workspace": (C.c_size_t, [I64] * 2),
+    "stade_heat2d_d_f64": (ST, [P] * 6 + [D, D, I64, I64, OPTS]),
+    "stade_conv1d_relu_mse_d_f32_workspace": (C.c_size_t, [I64] * 5),
+    "stade_conv1d_relu_mse_d_f32": (ST, [P] * 12 + [I64] * 5 + [OPTS]),
     "stade_initstacks_heat2d_b_slab": (I64, [I64, I64, I64]),
     "stade_heat2d_b_f64_slab_workspace": (C.c_size_t, [I64, I64, I64]),
     "stade_heat2d_b_f64_slab": (ST, [P] * 6 + [D, P, I64, I64, P, I64, P, OPTS]),

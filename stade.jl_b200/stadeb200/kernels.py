@@ -225,3 +225,61 @@ def kernel_launches() -> int:
 
 def reset_kernel_launches() -> None:
     lib().stade_reset_kernel_launches()
+
+
+# ---- tangent (forward-mode) sweeps <k>_d, tgen_signature_args order ----------
+def affine_ls_d_cuda(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i, *,
+                     stream=None, workspace=None):
+    """Tangent of affine_ls (C1), Float64: lossd += directional derivative."""
+    f = torch.float64
+    sz = dict(loss=1, lossd=1, w=n_o * n_i, wd=n_o * n_i, b=n_o, bd=n_o, x=n_s * n_i,
+              xd=n_s * n_i, t=n_s * n_o, td=n_s * n_o, y=n_s * n_o, yd=n_s * n_o)
+    arrs = dict(loss=loss, lossd=lossd, w=w, wd=wd, b=b, bd=bd, x=x, xd=xd, t=t, td=td, y=y, yd=yd)
+    ptrs = [_arr(arrs[k], f, sz[k], k) for k in sz]
+    o = _opts(stream, workspace)
+    check(lib().stade_affine_ls_d_f64(*ptrs, n_s, n_o, n_i, C.byref(o)))
+
+
+MLP_D_ARGS = ["loss", "lossd", "x", "xd", "y", "yd", "w1", "w1d", "b1", "b1d", "w2", "w2d",
+              "b2", "b2d", "h", "hd", "z", "zd", "p", "pd"]
+
+
+def mlp2_ce_d_cuda(*args, stream=None, workspace=None):
+    """Tangent of mlp2_ce: the 20 arrays of tgen_signature_args, then n_s,
+    n_i, n_h, n_o. Float32 or Float64 by the arrays' dtype."""
+    if len(args) != 24:
+        raise TypeError(f"mlp2_ce_d_cuda takes 24 positional arguments, got {len(args)}")
+    arrs, (n_s, n_i, n_h, n_o) = args[:20], args[20:]
+    dt = arrs[0].dtype
+    if dt not in (torch.float32, torch.float64):
+        raise TypeError(f"mlp2_ce_d_cuda: unsupported dtype {dt}")
+    ptrs = [_arr(t, dt, _mlp_len(nm, n_s, n_i, n_h, n_o), nm) for nm, t in zip(MLP_D_ARGS, arrs)]
+    o = _opts(stream, workspace)
+    fn = lib().stade_mlp2_ce_d_f32 if dt == torch.float32 else lib().stade_mlp2_ce_d_f64
+    check(fn(*ptrs, n_s, n_i, n_h, n_o, C.byref(o)))
+
+
+def heat2d_d_cuda(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step, *, stream=None,
+                  workspace=None):
+    """Tangent of heat2d (C3), Float64."""
+    f = torch.float64
+    nn = n * n
+    ptrs = [_arr(loss, f, 1, "loss"), _arr(lossd, f, 1, "lossd"), _arr(u, f, nn, "u"),
+            _arr(ud, f, nn, "ud"), _arr(un, f, nn, "un"), _arr(und, f, nn, "und")]
+    o = _opts(stream, workspace)
+    check(lib().stade_heat2d_d_f64(*ptrs, float(alpha), float(alphad), n, n_step, C.byref(o)))
+
+
+def conv1d_relu_mse_d_cuda(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o,
+                           n_k, *, stream=None, workspace=None):
+    """Tangent of conv1d_relu_mse (C4), Float32."""
+    f = torch.float32
+    n_lo = n_l - n_k + 1
+    nt = n_b * n_o * max(n_lo, 0)
+    nx, nw = n_b * n_c * n_l, n_o * n_c * n_k
+    sz = [("loss", 1), ("lossd", 1), ("x", nx), ("xd", nx), ("w", nw), ("wd", nw), ("t", nt),
+          ("td", nt), ("z", nt), ("zd", nt), ("r", nt), ("rd", nt)]
+    arrs = (loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd)
+    ptrs = [_arr(a, f, n, nm) for a, (nm, n) in zip(arrs, sz)]
+    o = _opts(stream, workspace)
+    check(lib().stade_conv1d_relu_mse_d_f32(*ptrs, n_b, n_c, n_l, n_o, n_k, C.byref(o)))
