@@ -627,7 +627,12 @@ int splits_for(int M, int N, int K) {
 // ---------------------------------------------------------------------------
 // Per-sample head of the Float64 HVP: every statement of the head with its
 // tangent twin (oracle.cc mlp2_ce_hv; hvp_double_stmt, src/STADE.jl:6904).
-template <int NO>
+// One warp per sample, lane c owns class c (n_o <= 32): its logit and
+// tangent as the sequential sums over hidden units, its softmax terms and
+// their reverse. The class-to-class scans (the running max and its reverse)
+// run in every lane over values passed by shuffle; sums over classes are
+// warp sums. Lanes then own hidden units for s1b = (1 - h^2)(hb + W2 g) and
+// its tangent, with g and gd broadcast class by class.
 __global__ void __launch_bounds__(kHeadWarps * 32)
 mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ lossbd,
                    const double* __restrict__ y, double* __restrict__ yb,
@@ -642,182 +647,138 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
                    double* __restrict__ gbuf, double* __restrict__ gdbuf,
                    double* __restrict__ s1b, double* __restrict__ s1bd, int n_s, int n_h, int n_o,
                    double* __restrict__ loss_part, double* __restrict__ lossd_part) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  double* w2t = reinterpret_cast<double*>(smraw);  // [n_o][n_h]
-  double* w2dt = w2t + (size_t)n_o * n_h;
   __shared__ double red[2][kHeadWarps];
-  for (int e = threadIdx.x; e < n_h * n_o; e += blockDim.x) {
-    const int k = e / n_o, c = e % n_o;
-    w2t[c * n_h + k] = w2[e];
-    w2dt[c * n_h + k] = w2d[e];
-  }
-  __syncthreads();
   const unsigned F = 0xffffffffu;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool cl = lane < n_o;          // this lane owns class `lane`
+  const int c = cl ? lane : 0;
   const double lb = lossb[0], lbd = lossbd[0];
   double loss_acc = 0.0, lossd_acc = 0.0;
-  // the block stages W2 / W2d once and its warps take samples block-strided
   for (int s = blockIdx.x * kHeadWarps + warp; s < n_s; s += gridDim.x * kHeadWarps) {
     const double* hr = h + (int64_t)s * n_h;
     const double* hdr = hd + (int64_t)s * n_h;
-    double zp[NO], zdp[NO];
-#pragma unroll
-    for (int c = 0; c < NO; ++c) { zp[c] = 0.0; zdp[c] = 0.0; }
-    for (int k = lane; k < n_h; k += 32) {
-      const double hv = hr[k], hdv = hdr[k];
-#pragma unroll
-      for (int c = 0; c < NO; ++c) {
-        if (c < n_o) {
-          const double wv = w2t[c * n_h + k];
-          zdp[c] += hv * w2dt[c * n_h + k] + wv * hdv;
-          zp[c] = fma(wv, hv, zp[c]);
-        }
-      }
-    }
-    double zv[NO], zdv[NO];
-#pragma unroll
-    for (int c = 0; c < NO; ++c) {
-      zv[c] = c < n_o ? warp_sum(zp[c]) + b2[c] : 0.0;
-      zdv[c] = c < n_o ? warp_sum(zdp[c]) + b2d[c] : 0.0;
-    }
     const int64_t row = (int64_t)s * n_o;
-    double yv[NO], ydv[NO], pbin[NO], pbdin[NO], zbin[NO], zbdin[NO], ybin[NO], ybdin[NO];
-    {
-      const bool ok = lane < n_o;
-      const double a0 = ok ? y[row + lane] : 0.0, a1 = ok ? yd[row + lane] : 0.0;
-      const double a2 = ok ? pb[row + lane] : 0.0, a3 = ok ? pbd[row + lane] : 0.0;
-      const double a4 = ok ? zb[row + lane] : 0.0, a5 = ok ? zbd[row + lane] : 0.0;
-      const double a6 = ok ? yb[row + lane] : 0.0, a7 = ok ? ybd[row + lane] : 0.0;
-#pragma unroll
-      for (int c = 0; c < NO; ++c) {
-        yv[c] = __shfl_sync(F, a0, c); ydv[c] = __shfl_sync(F, a1, c);
-        pbin[c] = __shfl_sync(F, a2, c); pbdin[c] = __shfl_sync(F, a3, c);
-        zbin[c] = __shfl_sync(F, a4, c); zbdin[c] = __shfl_sync(F, a5, c);
-        ybin[c] = __shfl_sync(F, a6, c); ybdin[c] = __shfl_sync(F, a7, c);
-      }
+    // logits and tangents, hidden units in order (the primal's sequential sum)
+    double zv = b2[c], zdv = b2d[c];
+    for (int k = 0; k < n_h; ++k) {
+      const double hv = hr[k], hdv = hdr[k];
+      const double wv = w2[(int64_t)k * n_o + c];
+      zdv = zdv + (hv * w2d[(int64_t)k * n_o + c] + wv * hdv);
+      zv = zv + wv * hv;
     }
-    // forward with tangents
-    double mprev[NO];
-    double m = zv[0], md = zdv[0];
-#pragma unroll
-    for (int c = 1; c < NO; ++c) {
-      if (c < n_o) {
-        mprev[c] = m;
-        const double g1 = 0.5 * (1.0 + dsign(m - zv[c]));
-        const double g2 = 0.5 * (1.0 + dsign(zv[c] - m));
-        md = g1 * md + g2 * zdv[c];
-        m = jmax(m, zv[c]);
-      }
+    // running max over classes with its tangent
+    double m = __shfl_sync(F, zv, 0), md = __shfl_sync(F, zdv, 0);
+    double mprev = 0.0;
+    for (int cc = 1; cc < n_o; ++cc) {
+      const double zc = __shfl_sync(F, zv, cc), zdc = __shfl_sync(F, zdv, cc);
+      if (lane == cc) mprev = m;
+      const double g1 = 0.5 * (1.0 + dsign(m - zc));
+      const double g2 = 0.5 * (1.0 + dsign(zc - m));
+      md = g1 * md + g2 * zdc;
+      m = jmax(m, zc);
     }
-    double pv[NO], pdv[NO];
-#pragma unroll
-    for (int c = 0; c < NO; ++c) {
-      if (c < n_o) {
-        const double e = exp(zv[c] - m);
-        pdv[c] = e * (zdv[c] - md);
-        pv[c] = e;
-      } else {
-        pv[c] = 0.0; pdv[c] = 0.0;
-      }
-    }
-    double rs = 0.0, rsd = 0.0;
-#pragma unroll
-    for (int c = 0; c < NO; ++c)
-      if (c < n_o) { rsd = rsd + pdv[c]; rs = rs + pv[c]; }
-#pragma unroll
-    for (int c = 0; c < NO; ++c) {
-      if (c < n_o) {
-        const double q = pv[c] / rs;
-        const double qd = pdv[c] / rs - (pv[c] / (rs * rs)) * rsd;
-        lossd_acc = lossd_acc - (ydv[c] * log(q) + yv[c] * (qd / q));
-        loss_acc = loss_acc - yv[c] * log(q);
-      }
+    const double e = cl ? exp(zv - m) : 0.0;
+    const double ed = cl ? e * (zdv - md) : 0.0;
+    const double rs = warp_sum(e), rsd = warp_sum(ed);
+    double yv = 0.0, ydv = 0.0;
+    double lq = 0.0, lqd = 0.0, q = 1.0, qd = 0.0;
+    if (cl) {
+      yv = y[row + c];
+      ydv = yd[row + c];
+      q = e / rs;
+      qd = ed / rs - (e / (rs * rs)) * rsd;
+      lq = log(q);
+      lqd = qd / q;
+      lossd_acc = lossd_acc - (ydv * lq + yv * lqd);
+      loss_acc = loss_acc - yv * lq;
     }
     // reverse of the loss statement with tangents
-    double ybo[NO], ybdo[NO], pbv[NO], pbdv[NO];
-    double rsb = 0.0, rsbd = 0.0;
-#pragma unroll
-    for (int c = NO - 1; c >= 0; --c) {
-      if (c < n_o) {
-        const double q = pv[c] / rs;
-        const double qd = pdv[c] / rs - (pv[c] / (rs * rs)) * rsd;
-        const double lq = log(q), lqd = qd / q;
-        ybdo[c] = ybdin[c] + -(lqd * lb + lq * lbd);
-        ybo[c] = ybin[c] + -(lq) * lb;
-        const double inv_q = 1.0 / q, inv_qd = -(qd / (q * q));
-        const double ny = -(yv[c]) * lb, nyd = -(ydv[c] * lb + yv[c] * lbd);
-        const double qbd = inv_qd * ny + inv_q * nyd;
-        const double qb = inv_q * ny;
-        const double inv_rs = 1.0 / rs, inv_rsd = -(rsd / (rs * rs));
-        pbdv[c] = pbdin[c] + (inv_rsd * qb + inv_rs * qbd);
-        pbv[c] = pbin[c] + inv_rs * qb;
-        const double pr2 = pv[c] / (rs * rs);
-        const double pr2d = pdv[c] / (rs * rs) - (pv[c] / (rs * rs)) * ((2.0 * rs * rsd) / (rs * rs));
-        rsbd = rsbd + -(pr2d * qb + pr2 * qbd);
-        rsb = rsb + -(pr2) * qb;
-      }
+    double pbv = 0.0, pbdv = 0.0, rsb_c = 0.0, rsbd_c = 0.0;
+    if (cl) {
+      ybd[row + c] = ybd[row + c] + -(lqd * lb + lq * lbd);
+      yb[row + c] = yb[row + c] + -(lq) * lb;
+      const double inv_q = 1.0 / q, inv_qd = -(qd / (q * q));
+      const double ny = -(yv) * lb, nyd = -(ydv * lb + yv * lbd);
+      const double qbd = inv_qd * ny + inv_q * nyd;
+      const double qb = inv_q * ny;
+      const double inv_rs = 1.0 / rs, inv_rsd = -(rsd / (rs * rs));
+      pbdv = pbd[row + c] + (inv_rsd * qb + inv_rs * qbd);
+      pbv = pb[row + c] + inv_rs * qb;
+      const double pr2 = e / (rs * rs);
+      const double pr2d = ed / (rs * rs) - (e / (rs * rs)) * ((2.0 * rs * rsd) / (rs * rs));
+      rsbd_c = -(pr2d * qb + pr2 * qbd);
+      rsb_c = -(pr2)*qb;
     }
-    double g[NO], gd[NO];
-    double mb = 0.0, mbd = 0.0;
-#pragma unroll
-    for (int c = NO - 1; c >= 0; --c) {
-      if (c < n_o) {
-        const double oldbd = pbdv[c] + rsbd, oldb = pbv[c] + rsb;
-        const double e = pv[c];
-        const double ed = e * (zdv[c] - md);
-        const double csed = ed * oldb + e * oldbd;
-        const double cse = e * oldb;
-        gd[c] = zbdin[c] + csed;
-        g[c] = zbin[c] + cse;
-        mbd = mbd + -csed;
-        mb = mb + -cse;
-      }
+    const double rsb = warp_sum(rsb_c), rsbd = warp_sum(rsbd_c);
+    double g = 0.0, gd = 0.0, cse = 0.0, csed = 0.0;
+    if (cl) {
+      const double oldbd = pbdv + rsbd, oldb = pbv + rsb;
+      csed = ed * oldb + e * oldbd;
+      cse = e * oldb;
+      gd = zbd[row + c] + csed;
+      g = zb[row + c] + cse;
     }
-#pragma unroll
-    for (int c = NO - 1; c >= 1; --c) {
-      if (c < n_o) {
-        const double oldbd = mbd, oldb = mb;
-        const double g1 = 0.5 * (1.0 + dsign(mprev[c] - zv[c]));
-        const double g2 = 0.5 * (1.0 + dsign(zv[c] - mprev[c]));
-        mbd = 0.0 + g1 * oldbd;
-        mb = 0.0 + g1 * oldb;
-        gd[c] = gd[c] + g2 * oldbd;
-        g[c] = g[c] + g2 * oldb;
+    double mb = warp_sum(-cse), mbd = warp_sum(-csed);
+    // reverse of the running max, classes n_o - 1 .. 1
+    for (int cc = n_o - 1; cc >= 1; --cc) {
+      const double mp = __shfl_sync(F, mprev, cc), zc = __shfl_sync(F, zv, cc);
+      const double g1 = 0.5 * (1.0 + dsign(mp - zc));
+      const double g2 = 0.5 * (1.0 + dsign(zc - mp));
+      if (lane == cc) {
+        gd = gd + g2 * mbd;
+        g = g + g2 * mb;
       }
+      mbd = 0.0 + g1 * mbd;
+      mb = 0.0 + g1 * mb;
     }
-    gd[0] = gd[0] + mbd;
-    g[0] = g[0] + mb;
-#pragma unroll
-    for (int c = 0; c < NO; ++c) {
-      if (c < n_o && lane == c) {
-        z[row + c] = zv[c]; zd[row + c] = zdv[c];
-        p[row + c] = pv[c]; pd[row + c] = pdv[c];
-        yb[row + c] = ybo[c]; ybd[row + c] = ybdo[c];
-        zb[row + c] = 0.0; zbd[row + c] = 0.0;
-        pb[row + c] = 0.0; pbd[row + c] = 0.0;
-        gbuf[row + c] = g[c]; gdbuf[row + c] = gd[c];
-      }
+    if (lane == 0) {
+      gd = gd + mbd;
+      g = g + mb;
     }
+    if (cl) {
+      z[row + c] = zv; zd[row + c] = zdv;
+      p[row + c] = e; pd[row + c] = ed;
+      zb[row + c] = 0.0; zbd[row + c] = 0.0;
+      pb[row + c] = 0.0; pbd[row + c] = 0.0;
+      gbuf[row + c] = g; gdbuf[row + c] = gd;
+    }
+    // s1b, s1bd: lanes own hidden units, g and gd broadcast class by class
     double* hbr = hb + (int64_t)s * n_h;
     double* hbdr = hbd + (int64_t)s * n_h;
     double* s1br = s1b + (int64_t)s * n_h;
     double* s1bdr = s1bd + (int64_t)s * n_h;
-    for (int k = lane; k < n_h; k += 32) {
-      double acc = hbr[k], accd = hbdr[k];
+    for (int k0 = 0; k0 < n_h; k0 += 32 * 8) {
+      double acc[8], accd[8];
 #pragma unroll
-      for (int c = NO - 1; c >= 0; --c) {
-        if (c < n_o) {
-          const double wv = w2t[c * n_h + k];
-          accd = accd + (g[c] * w2dt[c * n_h + k] + wv * gd[c]);
-          acc = acc + wv * g[c];
+      for (int j = 0; j < 8; ++j) {
+        const int k = k0 + 32 * j + lane;
+        acc[j] = k < n_h ? hbr[k] : 0.0;
+        accd[j] = k < n_h ? hbdr[k] : 0.0;
+      }
+      for (int cc = n_o - 1; cc >= 0; --cc) {
+        const double gc = __shfl_sync(F, g, cc), gdc = __shfl_sync(F, gd, cc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = k0 + 32 * j + lane;
+          if (k < n_h) {
+            const double wv = w2[(int64_t)k * n_o + cc];
+            accd[j] = accd[j] + (gc * w2d[(int64_t)k * n_o + cc] + wv * gdc);
+            acc[j] = acc[j] + wv * gc;
+          }
         }
       }
-      const double th = hr[k];
-      const double gg = 1.0 - th * th;
-      s1bdr[k] = acc * -((2.0 * th) * hdr[k]) + gg * accd;
-      s1br[k] = gg * acc;
-      hbr[k] = 0.0;
-      hbdr[k] = 0.0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int k = k0 + 32 * j + lane;
+        if (k < n_h) {
+          const double th = hr[k];
+          const double gg = 1.0 - th * th;
+          s1bdr[k] = acc[j] * -((2.0 * th) * hdr[k]) + gg * accd[j];
+          s1br[k] = gg * acc[j];
+          hbr[k] = 0.0;
+          hbdr[k] = 0.0;
+        }
+      }
     }
   }
   if (lane == 0) { red[0][warp] = loss_acc; red[1][warp] = lossd_acc; }
@@ -948,9 +909,9 @@ struct MlpF64HvWs {
 };
 template <class Alloc>
 void mlp_hv_layout(Alloc& a, MlpF64HvWs* w, int64_t n_s, int64_t n_i, int64_t n_h, int64_t n_o) {
-  // two blocks per SM (W2 and W2d staged in shared memory), samples strided
+  // warps stride over the samples; eight blocks of eight warps per SM
   const int head_need = (int)((n_s + kHeadWarps - 1) / kHeadWarps);
-  const int head_blocks = head_need < 2 * 148 ? head_need : 2 * 148;
+  const int head_blocks = head_need < 8 * 148 ? head_need : 8 * 148;
   const int w2_chunks = (int)((n_s + kW2Chunk - 1) / kW2Chunk);
   const int w1_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, (int)n_s);
   const int w1d_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, 2 * (int)n_s);
@@ -1296,23 +1257,9 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   if (st != STADE_OK) return st;
   // head
   PhaseScope ph_head("hv_head", s);
-  const size_t smem = 2 * sizeof(double) * (size_t)(n_h * n_o);
-  STADE_REQUIRE(smem <= 200 * 1024, "mlp2_ce_hv: n_h * n_o too large");
-  if (O <= 16) {
-    if (smem > 48 * 1024)
-      STADE_CUDA(cudaFuncSetAttribute(mlp_head_hv_kernel<16>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    mlp_head_hv_kernel<16><<<w.head_blocks, kHeadWarps * 32, smem, s>>>(
-        lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
-        pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part);
-  } else {
-    if (smem > 48 * 1024)
-      STADE_CUDA(cudaFuncSetAttribute(mlp_head_hv_kernel<32>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    mlp_head_hv_kernel<32><<<w.head_blocks, kHeadWarps * 32, smem, s>>>(
-        lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
-        pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part);
-  }
+  mlp_head_hv_kernel<<<w.head_blocks, kHeadWarps * 32, 0, s>>>(
+      lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
+      pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part);
   STADE_CHECK_LAUNCH();
   st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
   if (st != STADE_OK) return st;
