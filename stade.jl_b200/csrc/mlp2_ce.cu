@@ -781,6 +781,9 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
       }
     }
   }
+  // each lane holds its classes' terms
+  loss_acc = warp_sum(loss_acc);
+  lossd_acc = warp_sum(lossd_acc);
   if (lane == 0) { red[0][warp] = loss_acc; red[1][warp] = lossd_acc; }
   __syncthreads();
   if (threadIdx.x == 0) {
