@@ -78,6 +78,41 @@ function conv1d_relu_mse_b_cuda(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb,
     return nothing
 end
 
+# Tangent sweeps -- replace the `<k>_d` functions stade_tangent_file writes
+# (tgen_signature_args: each float argument followed by its `d` shadow)
+function affine_ls_d_cuda(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i)
+    check(ccall((:stade_affine_ls_d_f64, libstade), Cint,
+        (ntuple(_ -> CuPtr{Float64}, 12)..., Int64, Int64, Int64, Ref{StadeOpts}),
+        loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i, opts()))
+    return nothing
+end
+
+function mlp2_ce_d_cuda(loss, lossd, x, xd, y, yd, w1, w1d, b1, b1d, w2, w2d, b2, b2d,
+                        h, hd, z, zd, p, pd, n_s, n_i, n_h, n_o)
+    T = eltype(loss)
+    sym = T == Float32 ? :stade_mlp2_ce_d_f32 : :stade_mlp2_ce_d_f64
+    check(ccall((sym, libstade), Cint,
+        (ntuple(_ -> CuPtr{T}, 20)..., Int64, Int64, Int64, Int64, Ref{StadeOpts}),
+        loss, lossd, x, xd, y, yd, w1, w1d, b1, b1d, w2, w2d, b2, b2d, h, hd, z, zd, p, pd,
+        n_s, n_i, n_h, n_o, opts()))
+    return nothing
+end
+
+function heat2d_d_cuda(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step)
+    check(ccall((:stade_heat2d_d_f64, libstade), Cint,
+        (ntuple(_ -> CuPtr{Float64}, 6)..., Float64, Float64, Int64, Int64, Ref{StadeOpts}),
+        loss, lossd, u, ud, un, und, alpha, alphad, n, n_step, opts()))
+    return nothing
+end
+
+function conv1d_relu_mse_d_cuda(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd,
+                                n_b, n_c, n_l, n_o, n_k)
+    check(ccall((:stade_conv1d_relu_mse_d_f32, libstade), Cint,
+        (ntuple(_ -> CuPtr{Float32}, 12)..., Int64, Int64, Int64, Int64, Int64, Ref{StadeOpts}),
+        loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o, n_k, opts()))
+    return nothing
+end
+
 # C5 -- replaces mlp2_ce_hv_cuda (hvp_emit layout: adjoint args, then pairs)
 function mlp2_ce_hv_cuda(loss, lossb, x, xb, y, yb, w1, w1b, b1, b1b, w2, w2b, b2, b2b,
                          h, hb, z, zb, p, pb, n_s, n_i, n_h, n_o,
