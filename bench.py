@@ -848,8 +848,10 @@ def main():
             step_fn = W.step
             print(f"# graph capture failed, timing eager launches: {e!r}", file=sys.stderr)
     time.sleep(max(0.0, 1.5 - (time.time() - t_setup)))  # nvidia-smi is up and sampling
+    # the warm-up steps again right before timing: the GPU idled during the
+    # wait above and its clocks are back at speed only after some work
     clocks.mark_begin()
-    total_ms, per = timed_loop(torch, step_fn, args.steps, 0, world, dist,
+    total_ms, per = timed_loop(torch, step_fn, args.steps, args.warmup, world, dist,
                                flush if W.flush_l2 else None, stream)
     clocks.mark_end()
     ms_per_step = total_ms / args.steps

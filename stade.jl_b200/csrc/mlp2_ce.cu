@@ -20,8 +20,10 @@
 // (cgen_device_assign, src/STADE.jl:11941); here nothing is atomic.
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
+#include "gemm_dmma.cuh"
 #include "gemm_simt.cuh"
 #include "tc_gemm.cuh"
 
@@ -617,12 +619,30 @@ struct LdXtOnes {  // A(m, k) = x[k * ld + m] for m < n_m, 1 for m == n_m
 constexpr int kF32RM = 2, kF32RN = 2, kF32BK = 16;
 constexpr int kF64RM = 2, kF64RN = 2, kF64BK = 8;
 
+// Float64 contractions run on the FP64 tensor cores (DMMA) unless
+// STADE_F64_GEMM=simt selects the CUDA-core kernel.
+inline bool f64_dmma() {
+  const char* e = std::getenv("STADE_F64_GEMM");
+  return !(e && std::strcmp(e, "simt") == 0);
+}
+template <bool A_KC, bool B_NC, class LA, class LB, class Epi>
+stade_status gemm_f64(int M, int N, int K, LA la, LB lb, Epi epi, double* partial, int splits,
+                      cudaStream_t s);
+
 template <class T, int RM, int RN, int BK>
 int splits_for(int M, int N, int K) {
   const int tiles = ((M + 64 * RM - 1) / (64 * RM)) * ((N + 64 * RN - 1) / (64 * RN));
   return split_plan(tiles, K, BK, 64).splits;
 }
 
+
+template <bool A_KC, bool B_NC, class LA, class LB, class Epi>
+stade_status gemm_f64(int M, int N, int K, LA la, LB lb, Epi epi, double* partial, int splits,
+                      cudaStream_t s) {
+  if (f64_dmma()) return gemm_dmma<A_KC, B_NC>(M, N, K, la, lb, epi, partial, splits, s);
+  return gemm_simt<double, kF64RM, kF64RN, kF64BK, A_KC, B_NC>(M, N, K, la, lb, epi, partial,
+                                                                 splits, s);
+}
 
 // ---------------------------------------------------------------------------
 // Per-sample head of the Float64 HVP: every statement of the head with its
@@ -1249,11 +1269,11 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   // forward: S1 = x W1; s1d = x W1d + xd W1, h, hd
   {
     PhaseScope ph("hv_fwd_gemms", s);
-    st = gemm_simt<double, RM, RN, BK, true, true>(S, H, I, LdRow<double>{x, I},
+    st = gemm_f64<true, true>(S, H, I, LdRow<double>{x, I},
                                                     LdB<double>{w1, H}, EpiStore{{}, w.s1, H},
                                                     nullptr, 1, s);
     if (st == STADE_OK)
-      st = gemm_simt<double, RM, RN, BK, true, true>(
+      st = gemm_f64<true, true>(
           S, H, 2 * I, LdRow2{x, xd, I, I}, LdB2{w1d, w1, H, I},
           EpiTanhTangent{{}, w.s1, b1, b1d, h, hd, H}, nullptr, 1, s);
   }
@@ -1283,11 +1303,11 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   // W1b (+ b1b); W1bd = x^T s1bd + xd^T s1b (+ b1bd)
   {
     PhaseScope ph("hv_w1b_gemms", s);
-    st = gemm_simt<double, RM, RN, BK, false, true>(
+    st = gemm_f64<false, true>(
         I + 1, H, S, LdXtOnes<double>{x, I, I}, LdB<double>{w.s1b, H},
         EpiWeightBias<double>{{}, w1b, b1b, I, H}, w.w1_part, w.w1_splits, s);
     if (st == STADE_OK)
-      st = gemm_simt<double, RM, RN, BK, false, true>(
+      st = gemm_f64<false, true>(
           I + 1, H, 2 * S, LdXtOnes2{x, xd, I, I, S}, LdB2{w.s1bd, w.s1b, H, S},
           EpiWeightBias<double>{{}, w1bd, b1bd, I, H}, w.w1_part, w.w1d_splits, s);
   }
@@ -1295,11 +1315,11 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   // xb += s1b W1^T; xbd += s1bd W1^T + s1b W1d^T
   {
     PhaseScope ph("hv_xb_gemms", s);
-    st = gemm_simt<double, RM, RN, BK, true, false>(S, I, H, LdRow<double>{w.s1b, H},
+    st = gemm_f64<true, false>(S, I, H, LdRow<double>{w.s1b, H},
                                                      LdBT<double>{w1, H},
                                                      EpiAddTo<double>{{}, xb, I}, nullptr, 1, s);
     if (st == STADE_OK)
-      st = gemm_simt<double, RM, RN, BK, true, false>(
+      st = gemm_f64<true, false>(
           S, I, 2 * H, LdRow2{w.s1bd, w.s1b, H, H}, LdBT2{w1, w1d, H, H},
           EpiAddTo<double>{{}, xbd, I}, nullptr, 1, s);
   }
@@ -1479,12 +1499,20 @@ stade_status mlp2_ce_d_impl(T* loss, T* lossd, const T* x, const T* xd, const T*
   const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
   {
     PhaseScope ph("d_gemms", s);
-    st = gemm_simt<T, RM, RN, BK, true, true>(S, H, I, LdRow<T>{x, I}, LdB<T>{w1, H},
-                                              EpiStoreT<T>{{}, s1, H}, nullptr, 1, s);
-    if (st == STADE_OK)
-      st = gemm_simt<T, RM, RN, BK, true, true>(
-          S, H, 2 * I, LdRow2T<T>{x, xd, I, I}, LdB2T<T>{w1d, w1, H, I},
-          EpiTanhTangentT<T>{{}, s1, b1, b1d, h, hd, H}, nullptr, 1, s);
+    if constexpr (std::is_same<T, double>::value) {
+      st = gemm_f64<true, true>(S, H, I, LdRow<T>{x, I}, LdB<T>{w1, H}, EpiStoreT<T>{{}, s1, H},
+                                nullptr, 1, s);
+      if (st == STADE_OK)
+        st = gemm_f64<true, true>(S, H, 2 * I, LdRow2T<T>{x, xd, I, I}, LdB2T<T>{w1d, w1, H, I},
+                                  EpiTanhTangentT<T>{{}, s1, b1, b1d, h, hd, H}, nullptr, 1, s);
+    } else {
+      st = gemm_simt<T, RM, RN, BK, true, true>(S, H, I, LdRow<T>{x, I}, LdB<T>{w1, H},
+                                                EpiStoreT<T>{{}, s1, H}, nullptr, 1, s);
+      if (st == STADE_OK)
+        st = gemm_simt<T, RM, RN, BK, true, true>(
+            S, H, 2 * I, LdRow2T<T>{x, xd, I, I}, LdB2T<T>{w1d, w1, H, I},
+            EpiTanhTangentT<T>{{}, s1, b1, b1d, h, hd, H}, nullptr, 1, s);
+    }
   }
   if (st != STADE_OK) return st;
   PhaseScope ph("d_head", s);

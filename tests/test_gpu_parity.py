@@ -183,10 +183,15 @@ def _check_conv(sizes, seeded):
         assert np.all(out[k] == 0.0), k
 
 
+@pytest.mark.parametrize("f64_gemm", ["dmma", "simt"])
 @pytest.mark.parametrize("sizes,seeded,xd", [((64, 30, 40, 10), False, False),
                                              ((33, 17, 19, 3), True, True),
-                                             ((130, 70, 129, 10), True, False)])
-def test_mlp2_ce_hv(sizes, seeded, xd):
+                                             ((130, 70, 129, 10), True, False),
+                                             ((300, 784, 512, 10), True, True)])
+def test_mlp2_ce_hv(sizes, seeded, xd, f64_gemm, monkeypatch):
+    """Float64 contractions on the FP64 tensor cores (DMMA, default) and on
+    the CUDA cores (STADE_F64_GEMM=simt)."""
+    monkeypatch.setenv("STADE_F64_GEMM", f64_gemm)
     ref, out, ints, _, _ = _run_both(lambda: cases.mlp_hv_state(*sizes, seeded=seeded,
                                                                 xd_nonzero=xd),
                                      cases.oracle_mlp_hv, cases.gpu_mlp_hv)
