@@ -27,6 +27,7 @@ copied back, inside the timed region.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -174,18 +175,27 @@ def timed_loop(torch, step, steps, warmup, world, dist, flush, stream):
     events; without it (inputs larger than L2) one event pair brackets all K
     steps back to back, gaps included. Returns (max-over-ranks total ms,
     per-step ms list)."""
-    for _ in range(warmup):
+    for _ in range(max(warmup, 1)):
+        if flush is not None:
+            flush.add_(1)   # the flush kernel's first launch (module load) happens here
         step()
     torch.cuda.synchronize()
+    # the interpreter's cycle collector pauses for ~10 ms at a time; a pause
+    # on one rank inside the timed steps holds every rank at the next
+    # all-reduce, so it is run before the timing and held off during it
+    gc.collect()
+    gc.disable()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    h0 = time.perf_counter()
     if flush is None:
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for _ in range(steps):
             step()
         t1.record(stream)
+        host = time.perf_counter() - h0
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -200,16 +210,19 @@ def timed_loop(torch, step, steps, warmup, world, dist, flush, stream):
             evs[i][0].record(stream)
             step()
             evs[i][1].record(stream)
+        host = time.perf_counter() - h0
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         per = [a.elapsed_time(b) for a, b in evs]
         total = sum(per)
+    gc.enable()
+    timed_loop.host_ms = host * 1e3   # host time to enqueue the K steps (this rank)
     if world > 1:
-        t = torch.tensor([total], dtype=torch.float64, device="cuda")
+        t = torch.tensor([total, timed_loop.host_ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total = float(t.item())
+        total, timed_loop.host_ms = float(t[0].item()), float(t[1].item())
     return total, per
 
 
@@ -854,6 +867,7 @@ def main():
     total_ms, per = timed_loop(torch, step_fn, args.steps, args.warmup, world, dist,
                                flush if W.flush_l2 else None, stream)
     clocks.mark_end()
+    host_ms = timed_loop.host_ms / args.steps
     ms_per_step = total_ms / args.steps
     value = 1000.0 / ms_per_step if W.scaling == "strong" else world * 1000.0 / ms_per_step
 
@@ -900,6 +914,7 @@ def main():
                 "timing": ("CUDA graph of one step, replayed" if graph is not None
                            else "eager launches"),
                 "eager_profiled_ms_per_step": p_ms / args.steps,
+                "host_enqueue_ms_per_step": host_ms,
                 "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
                 "step_ms_min_max": [min(per), max(per)]}
         print(json.dumps(line), flush=True)

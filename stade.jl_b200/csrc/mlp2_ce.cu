@@ -388,12 +388,13 @@ mlp_s1b_w2b_kernel(const float* __restrict__ h, float* __restrict__ hb,
   }
 }
 
-// The s1b pass of the TMA path, four adjacent hidden units per thread
-// (16-byte loads and stores): s1b = (1 - h^2) (hb + sum_c w2[k, c] g[s, c]),
-// c descending (the generated order), written as TF32 hi / lo planes; hb
-// consumed to zero; the chunk's W2b (sum_s h g), b2b (sum_s g) and b1b
-// (sum_s s1b) partials. NO = the class count rounded to a template (exact
-// for 10 classes). Block = 128 threads x 4 units = 512 units of a chunk of
+// The s1b pass of the TMA path, two adjacent hidden units per thread (8-byte
+// loads and stores, few registers, many blocks in flight):
+// s1b = (1 - h^2) (hb + sum_c w2[k, c] g[s, c]), c descending (the generated
+// order), written as TF32 hi / lo planes; hb consumed to zero (stored only
+// where it held a seed); the chunk's W2b (sum_s h g), b2b (sum_s g) and b1b
+// (sum_s s1b) partials. NO = the class count rounded to a template (exact for
+// 10 classes). Block = 128 threads x 2 units = 256 units of a chunk of
 // samples; partial record [chunk][n_h*n_o (W2b) + n_o (b2b) + n_h (b1b)].
 template <int NO>
 __global__ void __launch_bounds__(128)
@@ -411,70 +412,69 @@ mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
   }
   __syncthreads();
   float* my = part + (int64_t)blockIdx.x * (n_h * n_o + n_o + n_h);
-  const int k = blockIdx.y * 512 + 4 * threadIdx.x;
+  const int k = blockIdx.y * 256 + 2 * threadIdx.x;
   if (k < n_h) {
-    float w[4][NO], a[4][NO];
+    float w[2][NO], a[2][NO];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int c = 0; c < NO; ++c) {
         w[j][c] = c < n_o ? w2[(int64_t)(k + j) * n_o + c] : 0.f;
         a[j][c] = 0.f;
       }
-    float4 bsum = make_float4(0.f, 0.f, 0.f, 0.f);
-    auto one = [&](int i, float4 hv, float4 acc4) {
+    float2 bsum = make_float2(0.f, 0.f);
+    auto one = [&](int i, float2 hv, float2 acc2) {
       const int64_t off = (int64_t)(s0 + i) * n_h + k;
       const float* g = gs + i * NO;
-      float hh[4] = {hv.x, hv.y, hv.z, hv.w};
-      float ac[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+      float hh[2] = {hv.x, hv.y};
+      float ac[2] = {acc2.x, acc2.y};
 #pragma unroll
       for (int c = NO - 1; c >= 0; --c) {
         if (c < n_o) {
           const float gc = g[c];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 2; ++j) {
             ac[j] = __fadd_rn(ac[j], __fmul_rn(w[j][c], gc));
             a[j][c] = fmaf(hh[j], gc, a[j][c]);
           }
         }
       }
-      float o[4], hi[4];
+      float o[2], hi[2];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 2; ++j) {
         o[j] = __fmul_rn(__fadd_rn(1.f, -__fmul_rn(hh[j], hh[j])), ac[j]);
         hi[j] = __uint_as_float(__float_as_uint(o[j]) & 0xFFFFE000u);
       }
-      bsum.x += o[0]; bsum.y += o[1]; bsum.z += o[2]; bsum.w += o[3];
-      *reinterpret_cast<float4*>(s1b_hi + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<float4*>(s1b_lo + off) =
-          make_float4(o[0] - hi[0], o[1] - hi[1], o[2] - hi[2], o[3] - hi[3]);
+      bsum.x += o[0]; bsum.y += o[1];
+      *reinterpret_cast<float2*>(s1b_hi + off) = make_float2(hi[0], hi[1]);
+      *reinterpret_cast<float2*>(s1b_lo + off) = make_float2(o[0] - hi[0], o[1] - hi[1]);
       // hb is consumed: zero it (only where it held a seed; a zero stays zero)
-      if (acc4.x != 0.f || acc4.y != 0.f || acc4.z != 0.f || acc4.w != 0.f)
-        *reinterpret_cast<float4*>(hb + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (acc2.x != 0.f || acc2.y != 0.f)
+        *reinterpret_cast<float2*>(hb + off) = make_float2(0.f, 0.f);
     };
     int i = 0;
     for (; i + 4 <= ns; i += 4) {
-      float4 hv[4], hbv[4];
+      float2 hv[4], hbv[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int64_t off = (int64_t)(s0 + i + u) * n_h + k;
-        hv[u] = *reinterpret_cast<const float4*>(h + off);
-        hbv[u] = *reinterpret_cast<const float4*>(hb + off);
+        hv[u] = *reinterpret_cast<const float2*>(h + off);
+        hbv[u] = *reinterpret_cast<const float2*>(hb + off);
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) one(i + u, hv[u], hbv[u]);
     }
     for (; i < ns; ++i) {
       const int64_t off = (int64_t)(s0 + i) * n_h + k;
-      one(i, *reinterpret_cast<const float4*>(h + off), *reinterpret_cast<const float4*>(hb + off));
+      one(i, *reinterpret_cast<const float2*>(h + off), *reinterpret_cast<const float2*>(hb + off));
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int c = 0; c < NO; ++c)
         if (c < n_o) my[(int64_t)(k + j) * n_o + c] = a[j][c];
     float* bb = my + (int64_t)n_h * n_o + n_o;
-    bb[k] = bsum.x; bb[k + 1] = bsum.y; bb[k + 2] = bsum.z; bb[k + 3] = bsum.w;
+    bb[k] = bsum.x; bb[k + 1] = bsum.y;
   }
   if (blockIdx.y == 0 && threadIdx.x < n_o) {
     const int c = threadIdx.x;
@@ -969,7 +969,7 @@ constexpr int kFinGroups = 16;  // first-level groups of the W2b / b2b / b1b par
 
 struct MlpF32Ws {
   float *s1b, *gbuf, *loss_part, *w2_part, *w1_part, *zpart, *fin;
-  float *x_hi, *x_lo, *w1_hi, *w1_lo, *s1b_hi, *s1b_lo, *w1b_part;
+  float *x_lo, *w1_lo, *s1b_hi, *s1b_lo, *w1b_part;
   int head_blocks, w2_chunks, w1_splits;
 };
 
@@ -1003,9 +1003,8 @@ void mlp_f32_layout(Alloc& a, MlpF32Ws* w, int64_t n_s, int64_t n_i, int64_t n_h
   auto w1p = a.template take<float>(w1_splits > 1 ? (size_t)w1_splits * (size_t)((n_i + 1) * n_h) : 1);
   auto zp = a.template take<float>((size_t)tc_logit_parts(n_h) * (size_t)(n_s * n_o));
   const bool planes = tc_mlp_supported(n_s, n_i, n_h);
-  auto xh = a.template take<float>(planes ? (size_t)(n_s * n_i) : 1);
+  // lo planes of x and W1 (each array is its own hi plane)
   auto xl = a.template take<float>(planes ? (size_t)(n_s * n_i) : 1);
-  auto wh = a.template take<float>(planes ? (size_t)(n_i * n_h) : 1);
   auto wl = a.template take<float>(planes ? (size_t)(n_i * n_h) : 1);
   auto sh = a.template take<float>(planes ? (size_t)(n_s * n_h) : 1);
   auto sl = a.template take<float>(planes ? (size_t)(n_s * n_h) : 1);
@@ -1015,7 +1014,7 @@ void mlp_f32_layout(Alloc& a, MlpF32Ws* w, int64_t n_s, int64_t n_i, int64_t n_h
     w->fin = (float*)fin;
     w->s1b = (float*)s1b; w->gbuf = (float*)gb; w->loss_part = (float*)lp;
     w->w2_part = (float*)w2p; w->w1_part = (float*)w1p; w->zpart = (float*)zp;
-    w->x_hi = (float*)xh; w->x_lo = (float*)xl; w->w1_hi = (float*)wh; w->w1_lo = (float*)wl;
+    w->x_lo = (float*)xl; w->w1_lo = (float*)wl;
     w->s1b_hi = (float*)sh; w->s1b_lo = (float*)sl; w->w1b_part = (float*)wp;
   }
 }
@@ -1072,21 +1071,27 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
   mlp_f32_layout(ca, &w, n_s, n_i, n_h, n_o);
   void* tcws = ca.c.take<char>(tc_mlp_workspace(n_s, n_i, n_h));
   const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
-  const MlpPath path = mlp_path(n_s, n_i, n_h);
+  MlpPath path = mlp_path(n_s, n_i, n_h);
+  // the TMA path reads x and W1 in place: their base addresses must be 16-byte aligned
+  if (path == MlpPath::Tma &&
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w1)) & 15u))
+    path = MlpPath::Simt;
   const bool use_tc = path == MlpPath::Tc;
 
   if (path == MlpPath::Tma) {
-    // 0. TF32 hi / lo planes of x and W1
+    // 0. TF32 lo planes of x and W1
     {
       PhaseScope ph("split", s);
-      st = tma_split(x, w.x_hi, w.x_lo, n_s * n_i, s);
-      if (st == STADE_OK) st = tma_split(w1, w.w1_hi, w.w1_lo, n_i * n_h, s);
+      // x and W1 serve as their own hi planes (kind::tf32 reads the top 19
+      // bits); only their lo planes are written
+      st = tma_split_lo(x, w.x_lo, n_s * n_i, s);
+      if (st == STADE_OK) st = tma_split_lo(w1, w.w1_lo, n_i * n_h, s);
     }
     if (st != STADE_OK) return st;
     // 1. h = tanh(x W1 + b1) and the logits' partial sums, TMA-fed tensor cores
     {
       PhaseScope ph("fwd_gemm", s);
-      st = tma_forward_tanh_logits(w.x_hi, w.x_lo, w.w1_hi, w.w1_lo, b1, w2, h, w.zpart, S, I, H,
+      st = tma_forward_tanh_logits(x, w.x_lo, w1, w.w1_lo, b1, w2, h, w.zpart, S, I, H,
                                    O, s);
     }
     if (st != STADE_OK) return st;
@@ -1109,7 +1114,7 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
       const size_t smem = sizeof(float) * (size_t)kW2ChunkTc * no;
       auto kern = O == 10 ? mlp_s1b_planes_kernel<10>
                           : O <= 16 ? mlp_s1b_planes_kernel<16> : mlp_s1b_planes_kernel<32>;
-      kern<<<dim3(chunks, (H + 511) / 512), 128, smem, s>>>(h, hb, w.gbuf, w2, w.s1b_hi, w.s1b_lo,
+      kern<<<dim3(chunks, (H + 255) / 256), 128, smem, s>>>(h, hb, w.gbuf, w2, w.s1b_hi, w.s1b_lo,
                                                             S, H, O, kW2ChunkTc, w.w2_part);
       STADE_CHECK_LAUNCH();
       // chunk partials -> kFinGroups group sums -> the three outputs, fixed order
@@ -1126,12 +1131,12 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
     // 4. W1b = x^T s1b, 5. xb += s1b W1^T
     {
       PhaseScope ph("w1b_gemm", s);
-      st = tma_weight_grad(w.x_hi, w.x_lo, w.s1b_hi, w.s1b_lo, w1b, w.w1b_part, S, I, H, s);
+      st = tma_weight_grad(x, w.x_lo, w.s1b_hi, w.s1b_lo, w1b, w.w1b_part, S, I, H, s);
     }
     if (st != STADE_OK) return st;
     {
       PhaseScope ph("xb_gemm", s);
-      st = tma_input_grad(w.s1b_hi, w.s1b_lo, w.w1_hi, w.w1_lo, xb, S, I, H, s);
+      st = tma_input_grad(w.s1b_hi, w.s1b_lo, w1, w.w1_lo, xb, S, I, H, s);
     }
     return st;
   }

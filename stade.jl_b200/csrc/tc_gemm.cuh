@@ -28,6 +28,8 @@ stade_status tc_input_grad(const float* s1b, const float* w1, float* xb, int S, 
 
 // ---- TMA-fed path (tc_tma.cu): operands as TF32 hi / lo planes --------------
 stade_status tma_split(const float* a, float* hi, float* lo, int64_t n, cudaStream_t s);
+// lo plane only (the array is its own hi plane for kind::tf32)
+stade_status tma_split_lo(const float* a, float* lo, int64_t n, cudaStream_t s);
 size_t tma_w1b_part_floats(int64_t n_s, int64_t n_i, int64_t n_h);
 stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const float* w1_hi,
                                      const float* w1_lo, const float* b1, const float* w2,

@@ -2,9 +2,11 @@
 // splitting: the mlp2_ce adjoint's three GEMMs.
 //
 // Every Float32 operand is held in memory as two planes, hi (low 13 mantissa
-// bits cleared: exactly representable in TF32) and lo = value - hi (exact):
-// x is split by one pass per call, W1 by a tiny pass, and s1b is written as
-// planes directly by the pass that produces it. D = A B^T then needs
+// bits cleared: exactly representable in TF32) and lo = value - hi (exact).
+// kind::tf32 reads only the top 19 bits of each 32-bit operand (measured on
+// the B200: products with the raw value and with hi agree bit for bit), so a
+// caller's array serves as its own hi plane and one pass writes its lo plane
+// (x, W1); s1b is written as planes directly by the pass that produces it. D = A B^T then needs
 // hi*hi + hi*lo + lo*hi (lo*lo is below Float32 rounding), three
 // tcgen05.mma.kind::tf32 per K step into one TMEM accumulator.
 //
@@ -504,6 +506,27 @@ __global__ void split_kernel(const float* __restrict__ a, float* __restrict__ hi
   }
 }
 
+// lo = a - hi(a) only: the tensor core reads just the top 19 bits of a
+// Float32 operand (kind::tf32), so the array itself serves as its hi plane.
+__global__ void split_lo_kernel(const float* __restrict__ a, float* __restrict__ lo, int64_t n) {
+  const int64_t n4 = n / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(a)[i];
+    float4 l;
+    l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    reinterpret_cast<float4*>(lo)[i] = l;
+  }
+  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = a[i];
+    lo[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+  }
+}
+
 __global__ void w1b_finish_kernel(const float* __restrict__ part, int slices, int64_t MN,
                                   float* __restrict__ w1b) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -523,6 +546,17 @@ stade_status tma_split(const float* a, float* hi, float* lo, int64_t n, cudaStre
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
   tma::split_kernel<<<(unsigned)blocks, (unsigned)threads, 0, s>>>(a, hi, lo, n);
+  STADE_CHECK_LAUNCH();
+  return STADE_OK;
+}
+
+stade_status tma_split_lo(const float* a, float* lo, int64_t n, cudaStream_t s) {
+  if (n <= 0) return STADE_OK;
+  const int64_t threads = 256;
+  int64_t blocks = (n / 4 + threads - 1) / threads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  tma::split_lo_kernel<<<(unsigned)blocks, (unsigned)threads, 0, s>>>(a, lo, n);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }

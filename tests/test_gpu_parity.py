@@ -232,3 +232,25 @@ def test_mlp2_ce_b_large_batch_vs_truth():
     for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
         ok, errs = f32_verdict(out[k], ref[k], truth[k])
         assert ok, (k, errs)
+
+
+def test_mlp2_ce_b_unaligned_inputs():
+    """x and W1 at addresses that are not 16-byte aligned: the tensor-core path
+    reads them in place through TMA, which needs 16-byte alignment, so the
+    sweep takes the CUDA-core contractions instead and stays correct."""
+    import torch
+    import stadeb200
+    st, ints = cases.mlp_state(300, 132, 200, 10, seeded=True)
+    ref, truth = cases.copy_state(st), _truth(st, ints, cases.oracle_mlp)
+    cases.oracle_mlp(ref, ints)
+    dev = {k: torch.from_numpy(v).cuda() for k, v in st.items()}
+    for k in ("x", "w1"):
+        big = torch.zeros(dev[k].numel() + 1, dtype=torch.float32, device="cuda")
+        big[1:] = dev[k]
+        dev[k] = big[1:]          # 4-byte offset
+        assert dev[k].data_ptr() % 16 != 0
+    stadeb200.mlp2_ce_b_cuda(*[dev[a] for a in cases.MLP_ARGS], ints["n_s"], ints["n_i"],
+                             ints["n_h"], ints["n_o"])
+    for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
+        ok, errs = f32_verdict(dev[k].cpu().numpy(), ref[k], truth[k])
+        assert ok, (k, errs)
