@@ -43,8 +43,12 @@ constexpr int kStageBytes = 4 * kTileBytes;     // A hi, A lo, B hi, B lo
 // stages + alignment slack + barrier block (256 B); the logits epilogue adds
 // kW2SmemBytes right after the barrier block
 constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 256;
-static_assert((2 * STAGES + 5) * 8 + 4 <= 256, "barrier block must fit in 256 bytes");
-constexpr uint32_t kTmemCols = 256;             // two 128-column accumulators
+// TMEM accumulators the MMAs rotate through: the MMA thread may run up to
+// kAccBufs - 1 accumulation chains ahead of the epilogue warps draining them
+constexpr int kAccBufs = 4;
+constexpr uint32_t kTmemCols = kAccBufs * 128;  // all 512 columns of the SM's TMEM
+constexpr int kBarWords = 2 * STAGES + 2 * kAccBufs + 1;  // full, empty, tfull, tempty, done
+static_assert(kBarWords * 8 + 4 <= 256, "barrier block must fit in 256 bytes");
 // K blocks per TMEM accumulation chain. The tensor core's Float32
 // accumulation is not round-to-nearest: its error grows linearly with the
 // number of accumulations into one TMEM accumulator (measured: 1.4e-5
@@ -128,6 +132,84 @@ __device__ __forceinline__ void epi_part_chunk(const EpiPartial& e, int m, int n
   }
 }
 
+// The fused epilogue of one tile, from the thread's register sums of its 64
+// columns (16-wide groups half, half + 2, half + 4, half + 6) of row m.
+template <int EPI_KIND, int NO>
+__device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m, int n0, int half,
+                                         int slice, const EpiTanhLogits& el,
+                                         const EpiAccumulate& ea, const EpiPartial& ep,
+                                         const float* w2s) {
+  if constexpr (EPI_KIND == 0) {
+    float zp[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) zp[c] = 0.f;
+#pragma unroll
+    for (int q = 0; q < BN / 32; ++q) {
+      const int nn = n0 + (half + 2 * q) * 16;
+      if (m < el.M) {
+        float* o = el.h + (int64_t)m * el.ld + nn;
+        float hv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          hv[i] = (nn + i < el.N) ? tanhf(sum[q][i] + __ldg(el.b1 + nn + i)) : 0.f;
+        if (nn + 16 <= el.N && aligned16(o)) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(o + i) =
+                make_float4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (nn + i < el.N) o[i] = hv[i];
+        }
+        // logits partial; w2 rows are the same for the whole warp (broadcast)
+        if (el.w2_stride > 0) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (nn + i < el.N) {
+              const float4* wr = reinterpret_cast<const float4*>(w2s + (nn + i) * el.w2_stride);
+#pragma unroll
+              for (int c4 = 0; c4 < NO / 4; ++c4) {
+                if (4 * c4 < el.n_o) {
+                  const float4 wv = wr[c4];
+                  zp[4 * c4] = fmaf(hv[i], wv.x, zp[4 * c4]);
+                  zp[4 * c4 + 1] = fmaf(hv[i], wv.y, zp[4 * c4 + 1]);
+                  zp[4 * c4 + 2] = fmaf(hv[i], wv.z, zp[4 * c4 + 2]);
+                  zp[4 * c4 + 3] = fmaf(hv[i], wv.w, zp[4 * c4 + 3]);
+                }
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (nn + i < el.N) {
+              const float* wr = el.w2 + (int64_t)(nn + i) * el.n_o;
+#pragma unroll
+              for (int cc = 0; cc < NO; ++cc)
+                if (cc < el.n_o) zp[cc] = fmaf(hv[i], __ldg(wr + cc), zp[cc]);
+            }
+          }
+        }
+      }
+    }
+    if (m < el.M) {
+      const int part = (n0 / BN) * 2 + half;
+      float* zr = el.zpart + ((int64_t)part * el.M + m) * el.n_o;
+#pragma unroll
+      for (int cc = 0; cc < NO; ++cc)
+        if (cc < el.n_o) zr[cc] = zp[cc];
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < BN / 32; ++q) {
+      if constexpr (EPI_KIND == 1) epi_acc_chunk(ea, m, n0 + (half + 2 * q) * 16, sum[q]);
+      else epi_part_chunk(ep, m, n0 + (half + 2 * q) * 16, slice, sum[q]);
+    }
+  }
+
+}
+
 struct Geometry {
   int M, N, K;
   int m_tiles, n_tiles, slices, k_slice;
@@ -146,10 +228,11 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
   uint8_t* tiles = smem_raw + pad;
   uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + STAGES * kStageBytes);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarWords);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
-  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
-  const uint32_t done = smem_u32(bars + 2 * STAGES + 4);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES);
+  const uint32_t tempty0 = smem_u32(bars + 2 * STAGES + kAccBufs);
+  const uint32_t done = smem_u32(bars + 2 * STAGES + 2 * kAccBufs);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_per_slice = g.m_tiles * g.n_tiles;
@@ -160,7 +243,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tempty0 + 8 * b, kEpiWarps);
     }
@@ -244,9 +327,9 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
         const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
         const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
         for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
-          const int b = chain & 1;
+          const int b = chain % kAccBufs;
           const uint32_t acc = tmem + (uint32_t)(b * BN);
-          if (!mbar_wait(tempty0 + 8 * b, ((uint32_t)(chain >> 1) & 1u) ^ 1u)) { ok = false; break; }
+          if (!mbar_wait(tempty0 + 8 * b, ((uint32_t)(chain / kAccBufs) & 1u) ^ 1u)) { ok = false; break; }
           tc_fence_after();
           const int kb0 = ch * kChainBlocks, kb1 = min(nkb, kb0 + kChainBlocks);
           for (int kb = kb0; kb < kb1; ++kb, ++kb_all) {
@@ -309,8 +392,8 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
 #pragma unroll
         for (int i = 0; i < 16; ++i) sum[q][i] = 0.f;
       for (int ch = 0; ch < nch; ++ch, ++chain) {
-        const int b = chain & 1;
-        ok = mbar_wait(tfull0 + 8 * b, (uint32_t)(chain >> 1) & 1u);
+        const int b = chain % kAccBufs;
+        ok = mbar_wait(tfull0 + 8 * b, (uint32_t)(chain / kAccBufs) & 1u);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -330,74 +413,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
         if (lane == 0) mbar_arrive(tempty0 + 8 * b);
       }
       if (!ok) break;
-      if constexpr (EPI_KIND == 0) {
-        float zp[NO];
-#pragma unroll
-        for (int c = 0; c < NO; ++c) zp[c] = 0.f;
-#pragma unroll
-        for (int q = 0; q < BN / 32; ++q) {
-          const int nn = n0 + (half + 2 * q) * 16;
-          if (m < el.M) {
-            float* o = el.h + (int64_t)m * el.ld + nn;
-            float hv[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              hv[i] = (nn + i < el.N) ? tanhf(sum[q][i] + __ldg(el.b1 + nn + i)) : 0.f;
-            if (nn + 16 <= el.N && aligned16(o)) {
-#pragma unroll
-              for (int i = 0; i < 16; i += 4)
-                *reinterpret_cast<float4*>(o + i) =
-                    make_float4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (nn + i < el.N) o[i] = hv[i];
-            }
-            // logits partial; w2 rows are the same for the whole warp (broadcast)
-            if (el.w2_stride > 0) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                if (nn + i < el.N) {
-                  const float4* wr = reinterpret_cast<const float4*>(w2s + (nn + i) * el.w2_stride);
-#pragma unroll
-                  for (int c4 = 0; c4 < NO / 4; ++c4) {
-                    if (4 * c4 < el.n_o) {
-                      const float4 wv = wr[c4];
-                      zp[4 * c4] = fmaf(hv[i], wv.x, zp[4 * c4]);
-                      zp[4 * c4 + 1] = fmaf(hv[i], wv.y, zp[4 * c4 + 1]);
-                      zp[4 * c4 + 2] = fmaf(hv[i], wv.z, zp[4 * c4 + 2]);
-                      zp[4 * c4 + 3] = fmaf(hv[i], wv.w, zp[4 * c4 + 3]);
-                    }
-                  }
-                }
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                if (nn + i < el.N) {
-                  const float* wr = el.w2 + (int64_t)(nn + i) * el.n_o;
-#pragma unroll
-                  for (int cc = 0; cc < NO; ++cc)
-                    if (cc < el.n_o) zp[cc] = fmaf(hv[i], __ldg(wr + cc), zp[cc]);
-                }
-              }
-            }
-          }
-        }
-        if (m < el.M) {
-          const int part = (n0 / BN) * 2 + half;
-          float* zr = el.zpart + ((int64_t)part * el.M + m) * el.n_o;
-#pragma unroll
-          for (int cc = 0; cc < NO; ++cc)
-            if (cc < el.n_o) zr[cc] = zp[cc];
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < BN / 32; ++q) {
-          if constexpr (EPI_KIND == 1) epi_acc_chunk(ea, m, n0 + (half + 2 * q) * 16, sum[q]);
-          else epi_part_chunk(ep, m, n0 + (half + 2 * q) * 16, slice, sum[q]);
-        }
-      }
+      epi_tile<EPI_KIND, NO>(sum, m, n0, half, slice, el, ea, ep, w2s);
     }
   }
 
@@ -409,6 +425,240 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
                  : "memory");
+  }
+}
+
+// ---- CTA pairs ---------------------------------------------------------------------
+// The same contraction with a 2-SM MMA (tcgen05.mma.cta_group::2, M = 256 per
+// pair): the two CTAs of a cluster each load their own 128 rows of A and one
+// half (64 rows or columns) of the tile's B into their shared memory, and the
+// leader CTA's single MMA thread computes the 256 x 128 tile from both; each
+// CTA's TMEM holds its own 128 rows. Per SM and K block that is 48 KB of
+// operand planes instead of 64 KB, so four stages fit. Completion of both
+// CTAs' loads counts on the leader's `full` barrier; the leader's commits
+// arrive on `empty`, `tfull` and `done` in both CTAs; the epilogue warps of
+// both CTAs arrive on the leader's `tempty`. Every wait is bounded.
+constexpr int kPairStages = 4;
+constexpr int kPairBPlane = (BN / 2) * BK * 4;               // 8 KB: half of a B plane
+constexpr int kPairStageBytes = 2 * kTileBytes + 2 * kPairBPlane;  // 48 KB
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256;
+static_assert((2 * kPairStages + 2 * kAccBufs + 1) * 8 + 4 <= 256, "barrier block must fit");
+static_assert(kPairSmemBytes + kW2SmemBytes <= 232448, "shared memory of a CTA");
+
+template <int EPI_KIND, int NO>
+__global__ void __launch_bounds__(kThreads, 1)
+tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
+                     const __grid_constant__ CUtensorMap a_lo,
+                     const __grid_constant__ CUtensorMap b_hi,
+                     const __grid_constant__ CUtensorMap b_lo, Geometry g, EpiTanhLogits el,
+                     EpiAccumulate ea, EpiPartial ep) {
+  constexpr int ST = kPairStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+  uint8_t* tiles = smem_raw + pad;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + ST * kPairStageBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 2 * kAccBufs + 1);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + ST);
+  const uint32_t tfull0 = smem_u32(bars + 2 * ST);
+  const uint32_t tempty0 = smem_u32(bars + 2 * ST + kAccBufs);
+  const uint32_t done = smem_u32(bars + 2 * ST + 2 * kAccBufs);
+  const uint32_t rank = tc5::cluster_rank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_per_slice = g.m_tiles * g.n_tiles;   // m_tiles counts 256-row tiles
+  const int total = tiles_per_slice * g.slices;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 2 * kEpiWarps);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tc5::tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+  tc_fence_before();
+  tc5::cluster_sync();   // both CTAs' barriers exist before anything signals them
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs) ---------------------------------------------------
+      int kb_all = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += npairs) {
+        const int slice = t / tiles_per_slice, r = t % tiles_per_slice;
+        const int m0 = (r / g.n_tiles) * (2 * BM) + (int)rank * BM;
+        const int nb = (r % g.n_tiles) * BN + (int)rank * (BN / 2);   // this CTA's half of B
+        const int kbeg = slice * g.k_slice;
+        const int kend = min(g.K, kbeg + g.k_slice);
+        const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+        for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
+          const int s = kb_all % ST;
+          const uint32_t ph = (uint32_t)(kb_all / ST) & 1u;
+          if (!tc5::mbar_wait_cluster(empty0 + 8 * s, ph ^ 1u, &g_tma_error)) { ok = false; break; }
+          const uint32_t st = smem_u32(tiles + s * kPairStageBytes);
+          const uint32_t fb = full0 + 8 * s;
+          if (leader) mbar_arrive_tx(fb, 2 * kPairStageBytes);
+          const int k0 = kbeg + kb * BK;
+          if (!g.a_mn) {
+            tc5::tma_load_2d_pair(st, &a_hi, k0, m0, fb);
+            tc5::tma_load_2d_pair(st + kTileBytes, &a_lo, k0, m0, fb);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              tc5::tma_load_2d_pair(st + q * 4096, &a_hi, m0 + 32 * q, k0, fb);
+              tc5::tma_load_2d_pair(st + kTileBytes + q * 4096, &a_lo, m0 + 32 * q, k0, fb);
+            }
+          }
+          const uint32_t sb = st + 2 * kTileBytes;
+          if (!g.b_mn) {
+            tc5::tma_load_2d_pair(sb, &b_hi, k0, nb, fb);
+            tc5::tma_load_2d_pair(sb + kPairBPlane, &b_lo, k0, nb, fb);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              tc5::tma_load_2d_pair(sb + q * 4096, &b_hi, nb + 32 * q, k0, fb);
+              tc5::tma_load_2d_pair(sb + kPairBPlane + q * 4096, &b_lo, nb + 32 * q, k0, fb);
+            }
+          }
+        }
+      }
+      // this CTA's copies in flight land before it exits (bounded): the last
+      // phase of every stage completes on the leader's barriers, so the peer
+      // waits for the leader's commits on its own `empty` instead
+      for (int i = 0; i < ST && i < kb_all; ++i) {
+        const int last = kb_all - 1 - i;
+        if (leader)
+          tc5::mbar_wait_cluster(full0 + 8 * (last % ST), (uint32_t)(last / ST) & 1u,
+                                 &g_tma_error);
+        else
+          tc5::mbar_wait_cluster(empty0 + 8 * (last % ST), (uint32_t)(last / ST) & 1u,
+                                 &g_tma_error);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (leader CTA) ------------------------------------------------------
+      const uint32_t idesc = idesc_tf32(2 * BM, BN, g.a_mn, g.b_mn);
+      const uint32_t a_lbo = g.a_mn ? 4096u : 16u, a_sbo = g.a_mn ? 512u : 1024u;
+      const uint32_t b_lbo = g.b_mn ? 4096u : 16u, b_sbo = g.b_mn ? 512u : 1024u;
+      const uint32_t a_lay = g.a_mn ? 1u : 2u, b_lay = g.b_mn ? 1u : 2u;
+      const uint32_t a_step = g.a_mn ? 1024u : 32u, b_step = g.b_mn ? 1024u : 32u;
+      int kb_all = 0, chain = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += npairs) {
+        const int slice = t / tiles_per_slice;
+        const int kbeg = slice * g.k_slice;
+        const int kend = min(g.K, kbeg + g.k_slice);
+        const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+        const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+        for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
+          const int b = chain % kAccBufs;
+          const uint32_t acc = tmem + (uint32_t)(b * BN);
+          if (!tc5::mbar_wait_cluster(tempty0 + 8 * b, ((uint32_t)(chain / kAccBufs) & 1u) ^ 1u,
+                                      &g_tma_error)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int kb0 = ch * kChainBlocks, kb1 = min(nkb, kb0 + kChainBlocks);
+          for (int kb = kb0; kb < kb1; ++kb, ++kb_all) {
+            const int s = kb_all % ST;
+            const uint32_t ph = (uint32_t)(kb_all / ST) & 1u;
+            if (!tc5::mbar_wait_cluster(full0 + 8 * s, ph, &g_tma_error)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t st = smem_u32(tiles + s * kPairStageBytes);
+            const uint32_t sb = st + 2 * kTileBytes;
+#pragma unroll
+            for (int j = 0; j < BK / 8; ++j) {
+              const uint64_t ahi = desc_sw128(st + a_step * j, a_lbo, a_sbo, a_lay);
+              const uint64_t alo = desc_sw128(st + kTileBytes + a_step * j, a_lbo, a_sbo, a_lay);
+              const uint64_t bhi = desc_sw128(sb + b_step * j, b_lbo, b_sbo, b_lay);
+              const uint64_t blo = desc_sw128(sb + kPairBPlane + b_step * j, b_lbo, b_sbo, b_lay);
+              tc5::mma_tf32_pair(acc, ahi, blo, idesc, (kb != kb0 || j != 0) ? 1u : 0u);
+              tc5::mma_tf32_pair(acc, alo, bhi, idesc, 1u);
+              tc5::mma_tf32_pair(acc, ahi, bhi, idesc, 1u);
+            }
+            tc5::mma_commit_pair(empty0 + 8 * s);
+          }
+          tc5::mma_commit_pair(tfull0 + 8 * b);
+        }
+      }
+      tc5::mma_commit_pair(done);
+    }
+    if (lane == 0) tc5::mbar_wait_cluster(done, 0, &g_tma_error);
+    __syncwarp();
+  } else {
+    // ---- epilogue warps (both CTAs) -----------------------------------------------------
+    const int e = warp - 2;
+    const int quad = warp & 3;
+    const int half = e >> 2;
+    float* w2s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
+    if constexpr (EPI_KIND == 0) {
+      if (el.w2_stride > 0) {
+        for (int i = threadIdx.x - 64; i < el.N * el.w2_stride; i += kEpiWarps * 32) {
+          const int kk = i / el.w2_stride, c = i % el.w2_stride;
+          w2s[i] = c < el.n_o ? el.w2[(int64_t)kk * el.n_o + c] : 0.f;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      }
+    }
+    const uint32_t tempty_leader = tc5::mapa(tempty0, 0);
+    int chain = 0;
+    bool ok = true;
+    for (int t = pair; t < total && ok; t += npairs) {
+      const int slice = t / tiles_per_slice, r = t % tiles_per_slice;
+      const int m0 = (r / g.n_tiles) * (2 * BM) + (int)rank * BM, n0 = (r % g.n_tiles) * BN;
+      const int kbeg = slice * g.k_slice;
+      const int kend = min(g.K, kbeg + g.k_slice);
+      const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+      const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+      const int m = m0 + quad * 32 + lane;
+      float sum[BN / 32][16];
+#pragma unroll
+      for (int q = 0; q < BN / 32; ++q)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sum[q][i] = 0.f;
+      for (int ch = 0; ch < nch; ++ch, ++chain) {
+        const int b = chain % kAccBufs;
+        ok = tc5::mbar_wait_cluster(tfull0 + 8 * b, (uint32_t)(chain / kAccBufs) & 1u, &g_tma_error);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        if (nkb > 0) {
+          const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN);
+#pragma unroll
+          for (int q = 0; q < BN / 32; ++q) {
+            float v[16];
+            tmem_ld16(base + (uint32_t)((half + 2 * q) * 16), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[q][i] += v[i];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc5::mbar_arrive_remote(tempty_leader + 8 * b);
+      }
+      if (!ok) break;
+      epi_tile<EPI_KIND, NO>(sum, m, n0, half, slice, el, ea, ep, w2s);
+    }
+  }
+
+  // ---- teardown: neither CTA leaves (or frees TMEM) while the pair still works ----------
+  tc_fence_before();
+  __syncthreads();
+  tc5::cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tc5::tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -456,6 +706,53 @@ stade_status run(const Operand& A, const Operand& B, Geometry g, const EpiTanhLo
   const int grid = total < sm_count() ? total : sm_count();
   tma_gemm_kernel<EPI_KIND, NO><<<grid, kThreads, smem, s>>>(ah, al, bh, bl, g, el, ea, ep);
   STADE_CHECK_LAUNCH();
+  return STADE_OK;
+}
+
+// The pair kernel for the same contraction: 256-row tiles, each CTA of a
+// 2-CTA cluster loading its rows of A and half of B (K-major B boxes of 64
+// rows). Opt-in (STADE_TMA_PAIR=1): it moves 25 % fewer operand bytes per MMA
+// but measured slower on the B200 than the one-CTA kernel with four TMEM
+// accumulators (C2 forward 0.41 vs 0.39 ms, input gradient 0.34 vs 0.31 ms),
+// so operand bandwidth is not what bounds these GEMMs.
+bool pair_enabled() {
+  const char* e = std::getenv("STADE_TMA_PAIR");
+  return e && std::strcmp(e, "1") == 0;
+}
+
+template <int EPI_KIND, int NO>
+stade_status run_pair(const Operand& A, const Operand& B, Geometry g, const EpiTanhLogits& el,
+                      const EpiAccumulate& ea, const EpiPartial& ep, cudaStream_t s) {
+  CUtensorMap ah, al, bh, bl;
+  stade_status st = operand_maps(A, &ah, &al);
+  if (st != STADE_OK) return st;
+  if (B.mn) {
+    st = operand_maps(B, &bh, &bl);
+  } else {
+    st = make_map(&bh, B.hi, B.rows, B.cols, B.ld, 32, BN / 2, false);
+    if (st == STADE_OK) st = make_map(&bl, B.lo, B.rows, B.cols, B.ld, 32, BN / 2, false);
+  }
+  if (st != STADE_OK) return st;
+  g.m_tiles = (g.M + 2 * BM - 1) / (2 * BM);
+  const int smem = kPairSmemBytes + (EPI_KIND == 0 && el.w2_stride > 0 ? kW2SmemBytes : 0);
+  auto kern = tma_gemm_pair_kernel<EPI_KIND, NO>;
+  STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int total = g.m_tiles * g.n_tiles * g.slices;
+  const int pairs = total < sm_count() / 2 ? total : sm_count() / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  STADE_CUDA(cudaLaunchKernelEx(&cfg, kern, ah, al, bh, bl, g, el, ea, ep));
+  count_launch();
   return STADE_OK;
 }
 
@@ -576,6 +873,10 @@ stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const
   const int stride = (O + 3) / 4 * 4;
   const bool smem_w2 = (int64_t)H * stride * 4 <= tma::kW2SmemBytes;
   tma::EpiTanhLogits el{h, b1, w2, zpart, H, S, H, O, 2, smem_w2 ? stride : 0};
+  if (tma::pair_enabled()) {
+    if (O <= 16) return tma::run_pair<0, 16>(A, B, g, el, {}, {}, s);
+    return tma::run_pair<0, 32>(A, B, g, el, {}, {}, s);
+  }
   if (O <= 16) return tma::run<0, 16>(A, B, g, el, {}, {}, s);
   return tma::run<0, 32>(A, B, g, el, {}, {}, s);
 }
@@ -603,6 +904,7 @@ stade_status tma_input_grad(const float* s1b_hi, const float* s1b_lo, const floa
   tma::Operand B{w1_hi, w1_lo, I, H, H, false};
   tma::Geometry g = tma::geometry(S, I, H, 1, false, false);
   tma::EpiAccumulate ea{xb, I, S, I};
+  if (tma::pair_enabled()) return tma::run_pair<1, 1>(A, B, g, {}, ea, {}, s);
   return tma::run<1, 1>(A, B, g, {}, ea, {}, s);
 }
 
