@@ -175,9 +175,9 @@ def timed_loop(torch, step, steps, warmup, world, dist, flush, stream):
     events; without it (inputs larger than L2) one event pair brackets all K
     steps back to back, gaps included. Returns (max-over-ranks total ms,
     per-step ms list)."""
-    for _ in range(max(warmup, 1)):
-        if flush is not None:
-            flush.add_(1)   # the flush kernel's first launch (module load) happens here
+    if flush is not None:
+        flush.add_(1)   # the flush kernel's first launch (module load) happens here
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     # the interpreter's cycle collector pauses for ~10 ms at a time; a pause

@@ -20,7 +20,7 @@
 //   xgrad    D[l][c] = sum_k sum_o gT[b][l-k][o] Wf[k][o][c]     xb += D
 //
 // Persistent kernel, one CTA per SM, warp-specialised as the mlp2_ce GEMMs:
-// warp 0 issues the TMA loads into a 3-stage ring, warp 1 owns TMEM (two
+// warp 0 issues the TMA loads into a 3-stage ring, warp 1 owns TMEM (four
 // accumulators) and issues the MMAs, warps 2-9 drain the accumulators in
 // chains of 4 K blocks into round-to-nearest register sums (the tensor core's
 // Float32 accumulation error grows with chain length) and run the epilogue.
@@ -41,7 +41,11 @@ constexpr int kPlane = BM * BK * 4;  // 16 KiB: one 128 x 32 plane tile
 constexpr int kStageBytes = 4 * kPlane;
 constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 256;
 constexpr int kChainBlocks = 4;
-static_assert((2 * STAGES + 5) * 8 + 4 + 4 * kEpiWarps <= 256, "barrier block overflow");
+// TMEM accumulators the MMAs rotate through (up to kAccBufs - 1 chains ahead
+// of the epilogue warps)
+constexpr int kAccBufs = 4;
+constexpr int kBarWords = 2 * STAGES + 2 * kAccBufs + 1;  // full, empty, tfull, tempty, done
+static_assert(kBarWords * 8 + 4 + 4 * kEpiWarps <= 256, "barrier block overflow");
 
 __device__ int g_conv_error = 0;
 
@@ -113,17 +117,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
   constexpr bool A_MN = Cfg<MODE>::a_mn, B_MN = Cfg<MODE>::b_mn;
   constexpr int kBPlane = BN * BK * 4;
   constexpr uint32_t kTx = 2 * kPlane + 2 * kBPlane;
-  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kTmemCols = kAccBufs * BN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
   uint8_t* tiles = smem_raw + pad;
   uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + STAGES * kStageBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarWords);
   float* red = reinterpret_cast<float*>(tmem_slot + 1);  // kEpiWarps floats
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
-  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
-  const uint32_t done = smem_u32(bars + 2 * STAGES + 4);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES);
+  const uint32_t tempty0 = smem_u32(bars + 2 * STAGES + kAccBufs);
+  const uint32_t done = smem_u32(bars + 2 * STAGES + 2 * kAccBufs);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = g.m_tiles * g.n_tiles * g.slices;
 
@@ -132,7 +137,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tempty0 + 8 * b, kEpiWarps);
     }
@@ -211,9 +216,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
         const Tile tl = decode<MODE>(g, t);
         const int nch = tl.nkb > 0 ? (tl.nkb + kChainBlocks - 1) / kChainBlocks : 1;
         for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
-          const int b = chain & 1;
+          const int b = chain % kAccBufs;
           const uint32_t acc = tmem + (uint32_t)(b * BN);
-          if (!mbar_wait(tempty0 + 8 * b, ((uint32_t)(chain >> 1) & 1u) ^ 1u, &g_conv_error)) {
+          if (!mbar_wait(tempty0 + 8 * b, ((uint32_t)(chain / kAccBufs) & 1u) ^ 1u, &g_conv_error)) {
             ok = false;
             break;
           }
@@ -260,8 +265,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
 #pragma unroll
         for (int i = 0; i < 16; ++i) sum[q][i] = 0.f;
       for (int ch = 0; ch < nch; ++ch, ++chain) {
-        const int b = chain & 1;
-        ok = mbar_wait(tfull0 + 8 * b, (uint32_t)(chain >> 1) & 1u, &g_conv_error);
+        const int b = chain % kAccBufs;
+        ok = mbar_wait(tfull0 + 8 * b, (uint32_t)(chain / kAccBufs) & 1u, &g_conv_error);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         fence_after();
