@@ -840,7 +840,7 @@ def main():
         W.step()
     torch.cuda.synchronize()
     step_fn, graph = W.step, None
-    if world == 1 and not args.no_graph:
+    if not args.no_graph:
         try:
             side = torch.cuda.Stream()
             side.wait_stream(torch.cuda.current_stream())
@@ -860,6 +860,13 @@ def main():
             graph = None
             step_fn = W.step
             print(f"# graph capture failed, timing eager launches: {e!r}", file=sys.stderr)
+        if world > 1:
+            # every rank replays its graph or none does (the steps hold collectives)
+            ok = torch.tensor([1.0 if graph is not None else 0.0], device="cuda")
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if float(ok.item()) < 1.0:
+                graph = None
+                step_fn = W.step
     time.sleep(max(0.0, 1.5 - (time.time() - t_setup)))  # nvidia-smi is up and sampling
     # the warm-up steps again right before timing: the GPU idled during the
     # wait above and its clocks are back at speed only after some work
@@ -913,11 +920,17 @@ def main():
                 "gpu_launches": launches,
                 "timing": ("CUDA graph of one step, replayed" if graph is not None
                            else "eager launches"),
+                "graph_note": ("the step's NCCL calls are captured in the graph"
+                               if graph is not None and world > 1 else None),
                 "eager_profiled_ms_per_step": p_ms / args.steps,
                 "host_enqueue_ms_per_step": host_ms,
                 "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
                 "step_ms_min_max": [min(per), max(per)]}
         print(json.dumps(line), flush=True)
+    # a graph that holds NCCL calls goes before the communicators
+    step_fn = None
+    del graph
+    torch.cuda.synchronize()
     if world > 1:
         if getattr(W, "comm", None) is not None:
             W.comm.close()
