@@ -330,11 +330,44 @@ class Mlp2Ce:
             d.allreduce_sum_(self.comm, t["w1b"], t["b1b"], t["w2b"], t["b2b"])
             d.allreduce_sum_(self.comm, t["loss"])
 
+    E2E_CHUNKS = 8
+
     def e2e_step(self):
-        t, p = self.t, self.pinned
-        for k in ("x", "y", "w1", "b1", "w2", "b2"):
+        """The grad-eval from host buffers, pipelined as a caller would: the
+        batch's rows go up in 8 chunks on a copy stream while the sweep runs on
+        the chunks already there (the sweep accumulates its weight gradients
+        and loss, so chunk calls add up to the whole-batch call)."""
+        torch, t, p, d = self.torch, self.t, self.pinned, self.ddp
+        main = torch.cuda.current_stream()
+        if not hasattr(self, "copy_stream"):
+            self.copy_stream = torch.cuda.Stream()
+            self.copied = [torch.cuda.Event() for _ in range(self.E2E_CHUNKS)]
+        for k in ("w1", "b1", "w2", "b2"):
             t[k].copy_(p[k], non_blocking=True)
-        self.step()
+        d.mlp2_ce_b_reset_accum_(t["w1b"], t["b1b"], t["w2b"], t["b2b"])
+        d.mlp2_ce_b_reset_reduced_(t["loss"])
+        d.mlp2_ce_b_reset_local_(t["xb"], t["yb"], t["hb"], t["zb"], t["pb"])
+        S, I, H, O = self.n_s, self.n_i, self.n_h, self.n_o
+        bounds = [S * c // self.E2E_CHUNKS for c in range(self.E2E_CHUNKS + 1)]
+        self.copy_stream.wait_stream(main)   # the previous step's use of x and y is done
+        with torch.cuda.stream(self.copy_stream):
+            for c in range(self.E2E_CHUNKS):
+                lo, hi = bounds[c], bounds[c + 1]
+                t["x"][lo * I:hi * I].copy_(p["x"][lo * I:hi * I], non_blocking=True)
+                t["y"][lo * O:hi * O].copy_(p["y"][lo * O:hi * O], non_blocking=True)
+                self.copied[c].record(self.copy_stream)
+        for c in range(self.E2E_CHUNKS):
+            lo, hi = bounds[c], bounds[c + 1]
+            main.wait_event(self.copied[c])
+            sl = lambda k, w: t[k][lo * w:hi * w]
+            self.kernels.mlp2_ce_b_cuda(t["loss"], t["lossb"], sl("x", I), sl("xb", I), sl("y", O),
+                                        sl("yb", O), t["w1"], t["w1b"], t["b1"], t["b1b"], t["w2"],
+                                        t["w2b"], t["b2"], t["b2b"], sl("h", H), sl("hb", H),
+                                        sl("zz", O), sl("zb", O), sl("p", O), sl("pb", O),
+                                        hi - lo, I, H, O, workspace=self.ws)
+        if self.comm is not None:
+            d.allreduce_sum_(self.comm, t["w1b"], t["b1b"], t["w2b"], t["b2b"])
+            d.allreduce_sum_(self.comm, t["loss"])
         for k, v in self.grad_host.items():
             v.copy_(t[k], non_blocking=True)
 
