@@ -489,11 +489,7 @@ class Heat2d:
 
     def phase_work(self):
         N = float(self.rows) * self.n
-        return {"fwd_2step": ("hbm", 32.0 * N, "two steps' algorithmic bytes (2 x 16 N); "
-                                              "one pass moves 24 N"),
-                "bwd_2step": ("hbm", 48.0 * N, "two steps' algorithmic bytes (2 x 24 N); "
-                                              "one pass moves 32 N"),
-                "fwd_step": ("hbm", 16.0 * N, "read u_k, write u_k+1 (tape)"),
+        return {"fwd_step": ("hbm", 16.0 * N, "read u_k, write u_k+1 (tape)"),
                 "bwd_step": ("hbm", 24.0 * N, "read unb_k, read tape u_k-1, write ub_k-1"),
                 "bwd_init": ("hbm", 32.0 * N, "read ub, unb, u_final; write seed")}
 

@@ -21,8 +21,6 @@
 // keeping the rows above and below in registers; horizontal neighbours come
 // from the neighbouring lanes by warp shuffle. alphab and loss are summed per
 // block, then over blocks in a fixed order.
-#include <cstdlib>
-#include <cstring>
 #include <utility>
 
 #include "common.cuh"
@@ -217,140 +215,6 @@ __global__ void heat_nostep_kernel(const double* __restrict__ u, double* __restr
   if (threadIdx.x == 0) part[blockIdx.x] = s;
 }
 
-// ---- two steps per pass (temporal blocking) -------------------------------------------
-// A block stages a (TR + 4) x (TW + 4) tile of the input state with a 2-cell
-// periodic halo in shared memory, computes the intermediate state on the
-// (TR + 2) x (TW + 2) cells the second step needs, then the second step on its
-// TR x TW cells. Every cell goes through heat_point / gather_point, so the
-// fields match the one-step kernels bit for bit; the intermediate state never
-// makes a round trip through HBM (forward: read u_k, write the tape state
-// u_k+1 and u_k+2: 24 B per cell per two steps instead of 32; backward: read
-// g_k+2 and the taped u_k+1, u_k, write g_k: 32 B instead of 48).
-constexpr int kTR = 16, kTW = 128, kPairThreads = 256;
-constexpr int kHW = kTW + 4;   // row pitch of a halo-2 tile
-constexpr int kH1 = kTW + 2;   // row pitch of a halo-1 tile
-constexpr size_t kBwd2Smem = sizeof(double) * ((kTR + 4) * kHW + 2 * (kTR + 2) * kH1);
-
-// Periodic index; a tile can reach past the grid by more than one period
-// when n is smaller than the tile.
-__device__ __forceinline__ int wrapi(int i, int n) {
-  while (i < 0) i += n;
-  while (i >= n) i -= n;
-  return i;
-}
-
-// Loads rows [i0 - h, i0 + TR + h) x cols [j0 - h, j0 + TW + h) of a periodic
-// n x n field into a tile of pitch TW + 2h.
-template <int H>
-__device__ __forceinline__ void load_tile(const double* __restrict__ src, double* tile, int i0,
-                                          int j0, int n) {
-  constexpr int rows = kTR + 2 * H, cols = kTW + 2 * H;
-  for (int e = threadIdx.x; e < rows * cols; e += kPairThreads) {
-    const int r = e / cols, c = e % cols;
-    const int i = wrapi(i0 - H + r, n), j = wrapi(j0 - H + c, n);
-    tile[e] = __ldg(src + (int64_t)i * n + j);
-  }
-}
-
-__global__ void __launch_bounds__(kPairThreads)
-heat_fwd2_kernel(const double* __restrict__ src, double* __restrict__ mid,
-                 double* __restrict__ dst, double* __restrict__ copy_dst, double alpha, int n,
-                 double* __restrict__ loss_part) {
-  __shared__ double t0[(kTR + 4) * kHW];   // u_k with halo 2
-  __shared__ double t1[(kTR + 2) * kH1];   // u_k+1 with halo 1
-  __shared__ double red[kPairThreads / 32];
-  const int i0 = blockIdx.y * kTR, j0 = blockIdx.x * kTW;
-  load_tile<2>(src, t0, i0, j0, n);
-  __syncthreads();
-  // u_k+1 on the halo-1 region; its own cells go to the tape
-  for (int e = threadIdx.x; e < (kTR + 2) * kH1; e += kPairThreads) {
-    const int r = e / kH1, c = e % kH1;             // tile-1 coordinates
-    const int R = r + 1, C = c + 1;                 // the same cell in tile 0
-    const double cc = t0[R * kHW + C];
-    const double v = heat_point(cc, t0[(R - 1) * kHW + C], t0[(R + 1) * kHW + C],
-                                t0[R * kHW + C - 1], t0[R * kHW + C + 1], alpha);
-    t1[e] = v;
-    const int i = i0 + r - 1, j = j0 + c - 1;
-    if (r >= 1 && r <= kTR && c >= 1 && c <= kTW && i < n && j < n) {
-      mid[(int64_t)i * n + j] = v;
-      if (copy_dst) copy_dst[(int64_t)i * n + j] = cc;
-    }
-  }
-  __syncthreads();
-  // u_k+2 on the block's own cells
-  double lsum = 0.0;
-  for (int e = threadIdx.x; e < kTR * kTW; e += kPairThreads) {
-    const int r = e / kTW, c = e % kTW;
-    const int R = r + 1, C = c + 1;                 // in tile 1
-    const int i = i0 + r, j = j0 + c;
-    if (i < n && j < n) {
-      const double v = heat_point(t1[R * kH1 + C], t1[(R - 1) * kH1 + C], t1[(R + 1) * kH1 + C],
-                                  t1[R * kH1 + C - 1], t1[R * kH1 + C + 1], alpha);
-      dst[(int64_t)i * n + j] = v;
-      if (loss_part) lsum = __dadd_rn(lsum, __dmul_rn(v, v));
-    }
-  }
-  if (loss_part) {
-    lsum = block_sum(lsum, red);
-    if (threadIdx.x == 0) loss_part[blockIdx.y * gridDim.x + blockIdx.x] = lsum;
-  }
-}
-
-__global__ void __launch_bounds__(kPairThreads)
-heat_bwd2_kernel(const double* __restrict__ g2, const double* __restrict__ u1,
-                 const double* __restrict__ u0, double* __restrict__ gdst, double alpha, int n,
-                 double* __restrict__ alpha_part, int first) {
-  extern __shared__ double bwd2_smem[];
-  double* tg2 = bwd2_smem;                       // g_k+2 with halo 2
-  double* tg1 = tg2 + (kTR + 4) * kHW;           // g_k+1 with halo 1
-  double* tu = tg1 + (kTR + 2) * kH1;            // u_k+1, then u_k, with halo 1
-  __shared__ double red[kPairThreads / 32];
-  const int i0 = blockIdx.y * kTR, j0 = blockIdx.x * kTW;
-  load_tile<2>(g2, tg2, i0, j0, n);
-  load_tile<1>(u1, tu, i0, j0, n);
-  __syncthreads();
-  // g_k+1 on the halo-1 region
-  for (int e = threadIdx.x; e < (kTR + 2) * kH1; e += kPairThreads) {
-    const int r = e / kH1, c = e % kH1;
-    const int R = r + 1, C = c + 1;
-    tg1[e] = gather_point(tg2[R * kHW + C], tg2[(R - 1) * kHW + C], tg2[(R + 1) * kHW + C],
-                          tg2[R * kHW + C - 1], tg2[R * kHW + C + 1], alpha);
-  }
-  // alphab of step k+2 over the block's own cells: lap(u_k+1) g_k+2
-  double asum = 0.0;
-  for (int e = threadIdx.x; e < kTR * kTW; e += kPairThreads) {
-    const int r = e / kTW, c = e % kTW;
-    if (i0 + r < n && j0 + c < n) {
-      const int R = r + 1, C = c + 1;                // in a halo-1 tile
-      const double lap = lap_point(tu[R * kH1 + C], tu[(R - 1) * kH1 + C], tu[(R + 1) * kH1 + C],
-                                   tu[R * kH1 + C - 1], tu[R * kH1 + C + 1]);
-      asum = fma(lap, tg2[(R + 1) * kHW + C + 1], asum);
-    }
-  }
-  __syncthreads();
-  load_tile<1>(u0, tu, i0, j0, n);
-  __syncthreads();
-  // g_k and the alphab of step k+1 (lap(u_k) g_k+1) on the block's own cells
-  for (int e = threadIdx.x; e < kTR * kTW; e += kPairThreads) {
-    const int r = e / kTW, c = e % kTW;
-    const int i = i0 + r, j = j0 + c;
-    if (i < n && j < n) {
-      const int R = r + 1, C = c + 1;                // in a halo-1 tile
-      gdst[(int64_t)i * n + j] =
-          gather_point(tg1[R * kH1 + C], tg1[(R - 1) * kH1 + C], tg1[(R + 1) * kH1 + C],
-                       tg1[R * kH1 + C - 1], tg1[R * kH1 + C + 1], alpha);
-      const double lap = lap_point(tu[R * kH1 + C], tu[(R - 1) * kH1 + C], tu[(R + 1) * kH1 + C],
-                                   tu[R * kH1 + C - 1], tu[R * kH1 + C + 1]);
-      asum = fma(lap, tg1[R * kH1 + C], asum);
-    }
-  }
-  asum = block_sum(asum, red);
-  if (threadIdx.x == 0) {
-    const int b = blockIdx.y * gridDim.x + blockIdx.x;
-    alpha_part[b] = first ? asum : alpha_part[b] + asum;
-  }
-}
-
 struct Grid {
   dim3 fwd, bwd;
   int nfwd, nbwd;
@@ -405,27 +269,12 @@ extern "C" int64_t stade_initstacks_heat2d_b(int64_t n, int64_t n_step) {
   return n_step * n * n;
 }
 
-namespace stade {
-namespace {
-dim3 pair_grid(int64_t n) { return dim3(ceil_div_u(n, kTW), ceil_div_u(n, kTR)); }
-// Two steps per pass unless STADE_HEAT_STEPS=1 (one-step kernels only).
-bool heat_pairs() {
-  const char* e = std::getenv("STADE_HEAT_STEPS");
-  return !(e && std::strcmp(e, "1") == 0);
-}
-}  // namespace
-}  // namespace stade
-
 extern "C" size_t stade_heat2d_b_f64_workspace(int64_t n, int64_t n_step) {
   if (n <= 0) return 0;
   const Grid g = grid_of(n);
-  const dim3 g2 = pair_grid(n);
-  const size_t n2 = (size_t)g2.x * g2.y;
-  const size_t nf = (size_t)g.nfwd > n2 ? (size_t)g.nfwd : n2;
   Sizer z;
-  z.take<double>(nf > (size_t)kNoStepBlocks ? nf : (size_t)kNoStepBlocks);  // loss partials
-  z.take<double>((size_t)(g.nbwd > kNoStepBlocks ? g.nbwd : kNoStepBlocks));  // alphab, 1-step
-  z.take<double>(n2);                                     // alphab partials, 2-step passes
+  z.take<double>((size_t)g.nfwd);                         // loss partials
+  z.take<double>((size_t)(g.nbwd > kNoStepBlocks ? g.nbwd : kNoStepBlocks));  // alphab partials
   z.take<double>(2);                                      // host-scalar staging
   (void)n_step;
   return z.bytes();
@@ -452,15 +301,10 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
   stade_status st = get_workspace(opts, stade_heat2d_b_f64_workspace(n, n_step), &wsp);
   if (st != STADE_OK) return st;
   const Grid g = grid_of(n);
-  const dim3 g2 = pair_grid(n);
-  const int n2 = (int)(g2.x * g2.y);
-  const size_t nf = (size_t)g.nfwd > (size_t)n2 ? (size_t)g.nfwd : (size_t)n2;
   Carver c(wsp);
-  double* loss_part = c.take<double>(nf > (size_t)kNoStepBlocks ? nf : (size_t)kNoStepBlocks);
+  double* loss_part = c.take<double>((size_t)g.nfwd);
   double* alpha_part = c.take<double>((size_t)(g.nbwd > kNoStepBlocks ? g.nbwd : kNoStepBlocks));
-  double* alpha_part2 = c.take<double>((size_t)n2);
   double* stage = c.take<double>(2);
-  const bool pairs = heat_pairs();
   double* alphab_dev = alphab;
   if (host_scalar) {
     STADE_CUDA(cudaMemcpyAsync(stage, alphab, sizeof(double), cudaMemcpyHostToDevice, s));
@@ -475,67 +319,33 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
     st = launch_sum_to_scalar(loss_part, kNoStepBlocks, loss, true, s);
     if (st != STADE_OK) return st;
   } else {
-    auto tape = [&](int64_t k) { return u_stack + k * nn; };  // state k (before step k+1)
-    // forward sweep: two steps per pass, a last single step when n_step is odd
-    int loss_parts = g.nfwd;
-    for (int64_t t = 1; t <= n_step;) {
-      const double* src = t == 1 ? u : tape(t - 1);
+    // forward sweep: tape[t] = state before step t+1
+    for (int64_t t = 1; t <= n_step; ++t) {
+      const double* src = t == 1 ? u : u_stack + (t - 1) * nn;
+      double* dst = t == n_step ? un : u_stack + t * nn;
       double* copy = t == 1 ? u_stack : nullptr;
-      if (pairs && t + 1 <= n_step) {
-        const bool last = t + 1 == n_step;
-        PhaseScope ph("fwd_2step", s);
-        heat_fwd2_kernel<<<g2, kPairThreads, 0, s>>>(src, tape(t), last ? un : tape(t + 1), copy,
-                                                     alpha, ni, last ? loss_part : nullptr);
-        STADE_CHECK_LAUNCH();
-        if (last) loss_parts = n2;
-        t += 2;
-      } else {
-        const bool last = t == n_step;
-        PhaseScope ph("fwd_step", s);
-        heat_fwd_kernel<kRowsFwd, true><<<g.fwd, kThreads, 0, s>>>(
-            src, last ? un : tape(t), copy, alpha, ni, 0, kRowsFwd, ni,
-            last ? loss_part : nullptr);
-        STADE_CHECK_LAUNCH();
-        if (last) loss_parts = g.nfwd;
-        t += 1;
-      }
+      PhaseScope ph("fwd_step", s);
+      heat_fwd_kernel<kRowsFwd, true><<<g.fwd, kThreads, 0, s>>>(
+          src, dst, copy, alpha, ni, 0, kRowsFwd, ni, t == n_step ? loss_part : nullptr);
+      STADE_CHECK_LAUNCH();
     }
-    st = launch_sum_to_scalar(loss_part, loss_parts, loss, true, s);
+    st = launch_sum_to_scalar(loss_part, g.nfwd, loss, true, s);
     if (st != STADE_OK) return st;
-    // backward sweep: a single step first when n_step is odd, then two steps
-    // per pass; passes alternate a -> b -> a ... and the last one lands in ub
-    const int64_t singles = pairs ? (n_step % 2) : n_step;
-    const int64_t passes = singles + (pairs ? n_step / 2 : 0);
-    double* a = (passes % 2 == 0) ? ub : unb;
-    double* b = (passes % 2 == 0) ? unb : ub;
+    // backward sweep; the first step reads the seed from `a`, steps alternate
+    // a -> b -> a ... and the last one lands in ub
+    double* a = (n_step % 2 == 0) ? ub : unb;
+    double* b = (n_step % 2 == 0) ? unb : ub;
     {
       PhaseScope ph("bwd_init", s);
       heat_bwd_init_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, a, nn / 2);
       STADE_CHECK_LAUNCH();
     }
-    if (pairs) {
-      STADE_CUDA(cudaFuncSetAttribute(heat_bwd2_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)kBwd2Smem));
-    }
-    bool first1 = true, first2 = true;
-    for (int64_t t = n_step; t >= 1;) {
-      if (pairs && t >= 2 && !(t == n_step && n_step % 2 == 1)) {
-        PhaseScope ph("bwd_2step", s);
-        heat_bwd2_kernel<<<g2, kPairThreads, kBwd2Smem, s>>>(a, tape(t - 1), tape(t - 2), b,
-                                                             alpha, ni, alpha_part2,
-                                                             first2 ? 1 : 0);
-        STADE_CHECK_LAUNCH();
-        first2 = false;
-        t -= 2;
-      } else {
-        PhaseScope ph("bwd_step", s);
-        heat_bwd_kernel<kRowsBwd, true><<<g.bwd, kThreads, 0, s>>>(
-            a, tape(t - 1), b, alpha, ni, 0, kRowsBwd, ni, alpha_part, first1 ? 1 : 0);
-        STADE_CHECK_LAUNCH();
-        first1 = false;
-        t -= 1;
-      }
+    for (int64_t t = n_step; t >= 1; --t) {
+      PhaseScope ph("bwd_step", s);
+      heat_bwd_kernel<kRowsBwd, true><<<g.bwd, kThreads, 0, s>>>(
+          a, u_stack + (t - 1) * nn, b, alpha, ni, 0, kRowsBwd, ni, alpha_part,
+          t == n_step ? 1 : 0);
+      STADE_CHECK_LAUNCH();
       double* tmp = a; a = b; b = tmp;
     }
     // the result is in ub (== a now); the other buffer is unb, consumed to zero
@@ -543,8 +353,7 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
       PhaseScope ph("zero_unb", s);
       STADE_CUDA(cudaMemsetAsync(unb, 0, (size_t)nn * sizeof(double), s));
     }
-    if (!first1) st = launch_sum_to_scalar(alpha_part, g.nbwd, alphab_dev, true, s);
-    if (st == STADE_OK && !first2) st = launch_sum_to_scalar(alpha_part2, n2, alphab_dev, true, s);
+    st = launch_sum_to_scalar(alpha_part, g.nbwd, alphab_dev, true, s);
     if (st != STADE_OK) return st;
   }
   if (host_scalar) {

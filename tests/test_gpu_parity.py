@@ -103,14 +103,9 @@ def test_mlp2_ce_b_deterministic():
         assert np.array_equal(a[k], b[k]), k
 
 
-@pytest.mark.parametrize("steps_per_pass", ["2", "1"])
 @pytest.mark.parametrize("n,n_step,seeded", [(64, 4, False), (34, 3, True), (6, 2, True),
-                                             (258, 5, False), (4, 1, True), (10, 0, True),
-                                             (300, 6, True), (130, 16, False)])
-def test_heat2d_b(n, n_step, seeded, steps_per_pass, monkeypatch):
-    """Two steps per pass (default: temporal blocking through shared memory)
-    and one step per pass (STADE_HEAT_STEPS=1)."""
-    monkeypatch.setenv("STADE_HEAT_STEPS", steps_per_pass)
+                                             (258, 5, False), (4, 1, True), (10, 0, True)])
+def test_heat2d_b(n, n_step, seeded):
     ref, out, ints, ab_ref, ab_gpu = _run_both(lambda: cases.heat_state(n, n_step, seeded=seeded),
                                                cases.oracle_heat, cases.gpu_heat)
     for k in ("u", "un", "u_stack"):
