@@ -746,6 +746,7 @@ void oracle_affine_ls_b_f128(long double* loss, const long double* lossb, const 
 
 void oracle_mlp2_ce_b_f32(MLP_B_ARGS(float)) { mlp2_ce_b<float>(MLP_B_PASS); }
 void oracle_mlp2_ce_b_f64(MLP_B_ARGS(double)) { mlp2_ce_b<double>(MLP_B_PASS); }
+void oracle_mlp2_ce_b_f128(MLP_B_ARGS(long double)) { mlp2_ce_b<long double>(MLP_B_PASS); }
 void oracle_mlp2_ce_b_f32_omp(MLP_B_ARGS(float), int nthreads) {
   mlp2_ce_b_omp<float>(MLP_B_PASS, nthreads);
 }
@@ -766,6 +767,12 @@ double oracle_heat2d_b_f64(double* loss, const double* lossb, double* u, double*
                            double* u_stack) {
   return heat2d_b<double>(loss, lossb, u, ub, un, unb, alpha, alphab, n, n_step, u_stack);
 }
+long double oracle_heat2d_b_f128(long double* loss, const long double* lossb, long double* u,
+                                 long double* ub, long double* un, long double* unb,
+                                 long double alpha, long double alphab, i64 n, i64 n_step,
+                                 long double* u_stack) {
+  return heat2d_b<long double>(loss, lossb, u, ub, un, unb, alpha, alphab, n, n_step, u_stack);
+}
 
 void oracle_conv1d_relu_mse_b_f32(float* loss, const float* lossb, const float* x, float* xb,
                                   const float* w, float* wb, const float* t, float* tb,
@@ -779,12 +786,27 @@ void oracle_conv1d_relu_mse_b_f64(double* loss, const double* lossb, const doubl
                                   i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
   conv1d_relu_mse_b<double>(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k);
 }
+void oracle_conv1d_relu_mse_b_f128(long double* loss, const long double* lossb,
+                                   const long double* x, long double* xb, const long double* w,
+                                   long double* wb, const long double* t, long double* tb,
+                                   long double* z, long double* zb, long double* r,
+                                   long double* rb, i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  conv1d_relu_mse_b<long double>(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l,
+                                 n_o, n_k);
+}
 
 void oracle_affine_ls_d_f64(double* loss, double* lossd, const double* w, const double* wd,
                             const double* b, const double* bd, const double* x, const double* xd,
                             const double* t, const double* td, double* y, double* yd, i64 n_s,
                             i64 n_o, i64 n_i) {
   affine_ls_d<double>(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i);
+}
+void oracle_affine_ls_d_f128(long double* loss, long double* lossd, const long double* w,
+                             const long double* wd, const long double* b, const long double* bd,
+                             const long double* x, const long double* xd, const long double* t,
+                             const long double* td, long double* y, long double* yd, i64 n_s,
+                             i64 n_o, i64 n_i) {
+  affine_ls_d<long double>(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i);
 }
 
 #define MLP_D_ARGS(T)                                                                      \
@@ -794,10 +816,16 @@ void oracle_affine_ls_d_f64(double* loss, double* lossd, const double* w, const 
 #define MLP_D_PASS loss, lossd, x, xd, y, yd, w1, w1d, b1, b1d, w2, w2d, b2, b2d, h, hd, z, zd, p, pd, n_s, n_i, n_h, n_o
 void oracle_mlp2_ce_d_f32(MLP_D_ARGS(float)) { mlp2_ce_d<float>(MLP_D_PASS); }
 void oracle_mlp2_ce_d_f64(MLP_D_ARGS(double)) { mlp2_ce_d<double>(MLP_D_PASS); }
+void oracle_mlp2_ce_d_f128(MLP_D_ARGS(long double)) { mlp2_ce_d<long double>(MLP_D_PASS); }
 
 void oracle_heat2d_d_f64(double* loss, double* lossd, double* u, double* ud, double* un,
                          double* und, double alpha, double alphad, i64 n, i64 n_step) {
   heat2d_d<double>(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step);
+}
+void oracle_heat2d_d_f128(long double* loss, long double* lossd, long double* u, long double* ud,
+                          long double* un, long double* und, long double alpha,
+                          long double alphad, i64 n, i64 n_step) {
+  heat2d_d<long double>(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step);
 }
 
 void oracle_conv1d_relu_mse_d_f32(float* loss, float* lossd, const float* x, const float* xd,
@@ -813,6 +841,15 @@ void oracle_conv1d_relu_mse_d_f64(double* loss, double* lossd, const double* x, 
                                   i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
   conv1d_relu_mse_d<double>(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o,
                             n_k);
+}
+void oracle_conv1d_relu_mse_d_f128(long double* loss, long double* lossd, const long double* x,
+                                   const long double* xd, const long double* w,
+                                   const long double* wd, const long double* t,
+                                   const long double* td, long double* z, long double* zd,
+                                   long double* r, long double* rd, i64 n_b, i64 n_c, i64 n_l,
+                                   i64 n_o, i64 n_k) {
+  conv1d_relu_mse_d<long double>(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l,
+                                 n_o, n_k);
 }
 
 }  // extern "C"

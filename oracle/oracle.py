@@ -36,20 +36,26 @@ def lib() -> C.CDLL:
         P, I64, D = C.c_void_p, C.c_int64, C.c_double
         L.oracle_affine_ls_b_f64.argtypes = [P] * 12 + [I64] * 3
         L.oracle_affine_ls_b_f128.argtypes = [P] * 12 + [I64] * 3
-        for n in ("oracle_mlp2_ce_b_f32", "oracle_mlp2_ce_b_f64"):
+        for n in ("oracle_mlp2_ce_b_f32", "oracle_mlp2_ce_b_f64", "oracle_mlp2_ce_b_f128"):
             getattr(L, n).argtypes = [P] * 20 + [I64] * 4
         L.oracle_mlp2_ce_b_f32_omp.argtypes = [P] * 20 + [I64] * 4 + [C.c_int]
         for n in ("oracle_mlp2_ce_hv_f64", "oracle_mlp2_ce_hv_f128"):
             getattr(L, n).argtypes = [P] * 20 + [I64] * 4 + [P] * 20
         L.oracle_heat2d_b_f64.argtypes = [P] * 6 + [D, D, I64, I64, P]
         L.oracle_heat2d_b_f64.restype = D
-        for n in ("oracle_conv1d_relu_mse_b_f32", "oracle_conv1d_relu_mse_b_f64"):
+        L.oracle_heat2d_b_f128.argtypes = [P] * 6 + [C.c_longdouble] * 2 + [I64, I64, P]
+        L.oracle_heat2d_b_f128.restype = C.c_longdouble
+        for n in ("oracle_conv1d_relu_mse_b_f32", "oracle_conv1d_relu_mse_b_f64",
+                  "oracle_conv1d_relu_mse_b_f128"):
             getattr(L, n).argtypes = [P] * 12 + [I64] * 5
-        L.oracle_affine_ls_d_f64.argtypes = [P] * 12 + [I64] * 3
-        for n in ("oracle_mlp2_ce_d_f32", "oracle_mlp2_ce_d_f64"):
+        for n in ("oracle_affine_ls_d_f64", "oracle_affine_ls_d_f128"):
+            getattr(L, n).argtypes = [P] * 12 + [I64] * 3
+        for n in ("oracle_mlp2_ce_d_f32", "oracle_mlp2_ce_d_f64", "oracle_mlp2_ce_d_f128"):
             getattr(L, n).argtypes = [P] * 20 + [I64] * 4
         L.oracle_heat2d_d_f64.argtypes = [P] * 6 + [D, D, I64, I64]
-        for n in ("oracle_conv1d_relu_mse_d_f32", "oracle_conv1d_relu_mse_d_f64"):
+        L.oracle_heat2d_d_f128.argtypes = [P] * 6 + [C.c_longdouble] * 2 + [I64, I64]
+        for n in ("oracle_conv1d_relu_mse_d_f32", "oracle_conv1d_relu_mse_d_f64",
+                  "oracle_conv1d_relu_mse_d_f128"):
             getattr(L, n).argtypes = [P] * 12 + [I64] * 5
         for f in L.oracle_affine_ls_b_f64, L.oracle_mlp2_ce_b_f32:
             f.restype = None
@@ -76,10 +82,25 @@ def affine_ls_b(loss, lossb, w, wb, b, bb, x, xb, t, tb, y, yb, n_s, n_o, n_i, t
     return None
 
 
+def _truth_run(fn, arrs, *rest):
+    """Runs the long-double (x87 80-bit) instantiation on widened copies of
+    `arrs` and writes the results back into `arrs`, whose dtype stays as it
+    was: the caller passes float64 arrays to keep the truth at full width."""
+    ld = np.longdouble
+    conv = [np.asarray(a, dtype=ld).copy() for a in arrs]
+    r = fn(*[_p(a, ld) for a in conv], *rest)
+    for dst, src in zip(arrs, conv):
+        dst[...] = src
+    return r
+
+
 def mlp2_ce_b(loss, lossb, x, xb, y, yb, w1, w1b, b1, b1b, w2, w2b, b2, b2b, h, hb, z, zb, p, pb,
-              n_s, n_i, n_h, n_o, threads=None):
+              n_s, n_i, n_h, n_o, threads=None, truth=False):
     arrs = (loss, lossb, x, xb, y, yb, w1, w1b, b1, b1b, w2, w2b, b2, b2b, h, hb, z, zb, p, pb)
     dt = arrs[0].dtype
+    if truth:
+        _truth_run(lib().oracle_mlp2_ce_b_f128, arrs, n_s, n_i, n_h, n_o)
+        return None
     if dt == np.float32:
         if threads is not None:
             lib().oracle_mlp2_ce_b_f32_omp(*[_p(a, dt) for a in arrs], n_s, n_i, n_h, n_o, threads)
@@ -106,45 +127,68 @@ def mlp2_ce_hv(*args, truth=False):
     return None
 
 
-def heat2d_b(loss, lossb, u, ub, un, unb, alpha, alphab, n, n_step, u_stack):
+def heat2d_b(loss, lossb, u, ub, un, unb, alpha, alphab, n, n_step, u_stack, truth=False):
     f = np.float64
+    if truth:
+        return float(_truth_run(
+            lambda *a: lib().oracle_heat2d_b_f128(*a[:6], alpha, alphab, n, n_step, a[6]),
+            (loss, lossb, u, ub, un, unb, u_stack)))
     return lib().oracle_heat2d_b_f64(_p(loss, f), _p(lossb, f), _p(u, f), _p(ub, f), _p(un, f),
                                      _p(unb, f), float(alpha), float(alphab), n, n_step,
                                      _p(u_stack, f))
 
 
-def conv1d_relu_mse_b(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k):
+def conv1d_relu_mse_b(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k,
+                      truth=False):
     arrs = (loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb)
     dt = arrs[0].dtype
+    if truth:
+        _truth_run(lib().oracle_conv1d_relu_mse_b_f128, arrs, n_b, n_c, n_l, n_o, n_k)
+        return None
     fn = lib().oracle_conv1d_relu_mse_b_f32 if dt == np.float32 else lib().oracle_conv1d_relu_mse_b_f64
     fn(*[_p(a, dt) for a in arrs], n_b, n_c, n_l, n_o, n_k)
     return None
 
 
 # ---- tangent (forward-mode) sweeps <k>_d, tgen_signature_args order ---------
-def affine_ls_d(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i):
+def affine_ls_d(loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd, n_s, n_o, n_i, truth=False):
     f = np.float64
+    if truth:
+        _truth_run(lib().oracle_affine_ls_d_f128, (loss, lossd, w, wd, b, bd, x, xd, t, td, y, yd),
+                   n_s, n_o, n_i)
+        return
     lib().oracle_affine_ls_d_f64(*[_p(a, f) for a in (loss, lossd, w, wd, b, bd, x, xd, t, td,
                                                       y, yd)], n_s, n_o, n_i)
 
 
-def mlp2_ce_d(*args):
+def mlp2_ce_d(*args, truth=False):
     assert len(args) == 24
     arrs, ints = args[:20], args[20:]
     dt = arrs[0].dtype
+    if truth:
+        _truth_run(lib().oracle_mlp2_ce_d_f128, arrs, *ints)
+        return
     fn = lib().oracle_mlp2_ce_d_f32 if dt == np.float32 else lib().oracle_mlp2_ce_d_f64
     fn(*[_p(a, dt) for a in arrs], *ints)
 
 
-def heat2d_d(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step):
+def heat2d_d(loss, lossd, u, ud, un, und, alpha, alphad, n, n_step, truth=False):
     f = np.float64
+    if truth:
+        _truth_run(lambda *a: lib().oracle_heat2d_d_f128(*a, alpha, alphad, n, n_step),
+                   (loss, lossd, u, ud, un, und))
+        return
     lib().oracle_heat2d_d_f64(*[_p(a, f) for a in (loss, lossd, u, ud, un, und)], float(alpha),
                               float(alphad), n, n_step)
 
 
-def conv1d_relu_mse_d(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o, n_k):
+def conv1d_relu_mse_d(loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd, n_b, n_c, n_l, n_o, n_k,
+                      truth=False):
     arrs = (loss, lossd, x, xd, w, wd, t, td, z, zd, r, rd)
     dt = arrs[0].dtype
+    if truth:
+        _truth_run(lib().oracle_conv1d_relu_mse_d_f128, arrs, n_b, n_c, n_l, n_o, n_k)
+        return
     fn = lib().oracle_conv1d_relu_mse_d_f32 if dt == np.float32 else \
         lib().oracle_conv1d_relu_mse_d_f64
     fn(*[_p(a, dt) for a in arrs], n_b, n_c, n_l, n_o, n_k)
