@@ -15,6 +15,7 @@ Also selectable with --config: heat2d (C3), affine_ls (C1), mlp2_ce_hv (C5),
 conv1d_relu_mse (C4); each is a single-GPU line (replicas at N > 1).
 
     python bench.py [--gpus N --steps K --warmup W] [--config NAME] [--impl reference]
+    python bench.py --config affine_ls|heat2d --impl emitted
 
 Rank 0 prints one JSON line. Timing: W untimed warm-up steps, then exactly K
 steps between a barrier + synchronize on both sides; each step is bracketed by
@@ -53,7 +54,9 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "emitted"], default="ours",
+                    help="emitted: C1 / C3 through the .cu emitter's output for the "
+                         "generated sweep text (one GPU)")
     ap.add_argument("--config", default="mlp2_ce",
                     choices=["mlp2_ce", "heat2d", "affine_ls", "mlp2_ce_hv", "conv1d_relu_mse"])
     ap.add_argument("--no-e2e", action="store_true")
@@ -596,6 +599,70 @@ class AffineLs:
                 "sample": f"{reps} full evaluations (oracle.cc, serial), {t:.2f} s"}
 
 
+class EmittedAffineLs(AffineLs):
+    """C1 through the .cu emitter: the generated affine_ls_b text
+    (julia/generated/affine_ls_b.jl) emitted, built for sm_100a and called
+    through its C ABI in place of the hand-written sweep."""
+
+    def __init__(self, torch, rank, world, comm_factory):
+        super().__init__(torch, rank, world, comm_factory)
+        from stadeb200 import emit
+        self.sweep = emit.load(emit.generated_source("affine_ls_b"))
+
+    def _eval(self):
+        t = self.t
+        for k in ("wb", "bb", "xb", "tb", "loss"):
+            t[k].zero_()
+        self.sweep(t["loss"], t["lossb"], t["w"], t["wb"], t["b"], t["bb"], t["x"], t["xb"],
+                   t["t"], t["tb"], t["y"], t["yb"], self.n_s, self.n_o, self.n_i)
+
+    def phase_work(self):
+        kind, work, note = super().phase_work()["affine"]
+        return {"emitted_sweep": (kind, work, "whole emitted call; " + note)}
+
+    def config(self):
+        c = super().config()
+        c["workload"] += " (the .cu emitter's output for the generated sweep text)"
+        return c
+
+
+class EmittedHeat2d(Heat2d):
+    """C3 through the .cu emitter's output for julia/generated/heat2d_b.jl
+    (one GPU: the emitted sweep has no slab form)."""
+
+    def __init__(self, torch, rank, world, comm_factory):
+        if world > 1:
+            raise SystemExit("--impl emitted runs on one GPU")
+        super().__init__(torch, rank, world, comm_factory)
+        from stadeb200 import emit
+        self.sweep = emit.load(emit.generated_source("heat2d_b"))
+        self.stack = None
+        self.stack = self.sweep.initstacks(self.n, self.n_step)[0]
+
+    def step(self):
+        t = self.t
+        t["ub"].zero_()
+        t["loss"].zero_()
+        ab = self.sweep(t["loss"], t["lossb"], t["u"], t["ub"], t["un"], t["unb"], self.alpha,
+                        0.0, self.n, self.n_step, self.stack)
+        self.ab_host[0] = ab
+
+    def e2e_step(self):
+        self.t["u"].copy_(self.pinned["u"], non_blocking=True)
+        self.step()
+        self.out_host.copy_(self.t["ub"], non_blocking=True)
+
+    def phase_work(self):
+        N = float(self.rows) * self.n
+        return {"emitted_sweep": ("hbm", 80.0 * 8.0 * N / 16 * self.n_step,
+                                  "whole emitted call; algorithmic 80 N x 8 B per 16 steps")}
+
+    def config(self):
+        c = super().config()
+        c["workload"] += " (the .cu emitter's output for the generated sweep text)"
+        return c
+
+
 class Conv1dReluMse:
     name = "conv1d_relu_mse"
     dtype = "f32"
@@ -782,6 +849,7 @@ class Mlp2CeHv:
 
 WORKLOADS = {"mlp2_ce": Mlp2Ce, "heat2d": Heat2d, "affine_ls": AffineLs,
              "conv1d_relu_mse": Conv1dReluMse, "mlp2_ce_hv": Mlp2CeHv}
+EMITTED = {"affine_ls": EmittedAffineLs, "heat2d": EmittedHeat2d}
 
 
 # ---------------------------------------------------------------------------
@@ -858,7 +926,12 @@ def main():
     def comm_factory():
         return ddp.NcclComm(rank, world)
 
-    W = WORKLOADS[args.config](torch, rank, world, comm_factory)
+    if args.impl == "emitted":
+        if args.config not in EMITTED:
+            raise SystemExit(f"--impl emitted: one of {sorted(EMITTED)}")
+        W = EMITTED[args.config](torch, rank, world, comm_factory)
+    else:
+        W = WORKLOADS[args.config](torch, rank, world, comm_factory)
     stream = torch.cuda.current_stream()
     flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     peaks, peak_src = load_peaks()
@@ -917,11 +990,16 @@ def main():
     _lib.profile_read()
     _lib.profile_enable(True)
     launches0 = _lib.lib().stade_kernel_launches()
+    e0 = W.sweep.launches() if args.impl == "emitted" else 0
     p_ms, _ = timed_loop(torch, W.step, args.steps, 0, world, dist,
                          flush if W.flush_l2 else None, stream)
     launches = _lib.lib().stade_kernel_launches() - launches0
     _lib.profile_enable(False)
     phases = _lib.profile_read()
+    if args.impl == "emitted":
+        # the emitted sweep's own launch counter, and the whole call as its phase
+        launches = W.sweep.launches() - e0
+        phases = {"emitted_sweep": (p_ms, args.steps)}
 
     # end to end through the public entry points with host buffers
     e2e = None
@@ -942,6 +1020,7 @@ def main():
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                **({"impl": "emitted"} if args.impl == "emitted" else {}),
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
                 "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None,
                 "dtype": W.dtype, "data": "synthetic (seeded, shapes and distributions of the "

@@ -180,6 +180,91 @@ heat_bwd_kernel(const double* __restrict__ g, const double* __restrict__ u,
   }
 }
 
+// General path (odd n, n < 4, or arrays not 16-byte aligned): the same steps
+// with one column per thread (kColsPerBlock threads, so the block grid and the
+// partials match the paired path) and the horizontal neighbours loaded, not
+// shuffled. Periodic wrap on every side, so n = 1, 2 work as the generated
+// code's modular indices do.
+template <int R>
+__global__ void __launch_bounds__(kColsPerBlock)
+heat_fwd1_kernel(const double* __restrict__ src, double* __restrict__ dst,
+                 double* __restrict__ copy_dst, double alpha, int n,
+                 double* __restrict__ loss_part) {
+  __shared__ double red[kColsPerBlock / 32];
+  const int j_raw = blockIdx.x * kColsPerBlock + threadIdx.x;
+  const bool col_ok = j_raw < n;
+  const int j = col_ok ? j_raw : n - 1;
+  const int jl = j == 0 ? n - 1 : j - 1, jr = j + 1 == n ? 0 : j + 1;
+  const int i0 = blockIdx.y * R;
+  double up = src[(int64_t)(i0 == 0 ? n - 1 : i0 - 1) * n + j];
+  double cur = src[(int64_t)i0 * n + j];
+  double lsum = 0.0;
+  for (int r = 0; r < R; ++r) {
+    const int i = i0 + r;
+    if (i >= n) break;                       // uniform over the block
+    const int64_t row = (int64_t)i * n;
+    const double dn = src[(int64_t)(i + 1 == n ? 0 : i + 1) * n + j];
+    const double o = heat_point(cur, up, dn, src[row + jl], src[row + jr], alpha);
+    if (col_ok) {
+      dst[row + j] = o;
+      if (copy_dst) copy_dst[row + j] = cur;
+      if (loss_part) lsum += __dmul_rn(o, o);
+    }
+    up = cur;
+    cur = dn;
+  }
+  if (loss_part) {
+    lsum = block_sum(lsum, red);
+    if (threadIdx.x == 0) loss_part[blockIdx.y * gridDim.x + blockIdx.x] = lsum;
+  }
+}
+
+template <int R>
+__global__ void __launch_bounds__(kColsPerBlock)
+heat_bwd1_kernel(const double* __restrict__ g, const double* __restrict__ u,
+                 double* __restrict__ gdst, double alpha, int n,
+                 double* __restrict__ alpha_part, int first) {
+  __shared__ double red[kColsPerBlock / 32];
+  const int j_raw = blockIdx.x * kColsPerBlock + threadIdx.x;
+  const bool col_ok = j_raw < n;
+  const int j = col_ok ? j_raw : n - 1;
+  const int jl = j == 0 ? n - 1 : j - 1, jr = j + 1 == n ? 0 : j + 1;
+  const int i0 = blockIdx.y * R;
+  const int64_t rup = (int64_t)(i0 == 0 ? n - 1 : i0 - 1) * n;
+  double gu = g[rup + j], gc = g[(int64_t)i0 * n + j];
+  double uu = u[rup + j], uc = u[(int64_t)i0 * n + j];
+  double asum = 0.0;
+  for (int r = 0; r < R; ++r) {
+    const int i = i0 + r;
+    if (i >= n) break;
+    const int64_t row = (int64_t)i * n, rdn = (int64_t)(i + 1 == n ? 0 : i + 1) * n;
+    const double gd = g[rdn + j], ud = u[rdn + j];
+    const double o = gather_point(gc, gu, gd, g[row + jl], g[row + jr], alpha);
+    if (col_ok) {
+      gdst[row + j] = o;
+      asum = fma(lap_point(uc, uu, ud, u[row + jl], u[row + jr]), gc, asum);
+    }
+    gu = gc; gc = gd;
+    uu = uc; uc = ud;
+  }
+  asum = block_sum(asum, red);
+  if (threadIdx.x == 0) {
+    const int b = blockIdx.y * gridDim.x + blockIdx.x;
+    alpha_part[b] = first ? asum : alpha_part[b] + asum;
+  }
+}
+
+__global__ void heat_bwd_init1_kernel(const double* __restrict__ ub,
+                                      const double* __restrict__ unb,
+                                      const double* __restrict__ ufin,
+                                      const double* __restrict__ lossb,
+                                      double* __restrict__ dst, int64_t nn) {
+  const double lb = lossb[0];
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nn;
+       e += (int64_t)gridDim.x * blockDim.x)
+    dst[e] = __dadd_rn(unb[e], __dadd_rn(ub[e], __dmul_rn(__dmul_rn(2.0, ufin[e]), lb)));
+}
+
 // g = unb + (ub + (2 u_final) lossb), written into `dst` (one of ub / unb).
 __global__ void heat_bwd_init_kernel(const double* __restrict__ ub, const double* __restrict__ unb,
                                      const double* __restrict__ ufin,
@@ -287,14 +372,15 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
   STADE_REQUIRE(n >= 0 && n_step >= 0, "heat2d_b: negative size");
   STADE_REQUIRE(alphab != nullptr, "heat2d_b: alphab is null");
   if (n == 0) return STADE_OK;
-  STADE_REQUIRE(n % 2 == 0 && n >= 4, "heat2d_b: n must be even and >= 4 (got %lld)", (long long)n);
   STADE_REQUIRE(n <= 65536, "heat2d_b: n = %lld exceeds 65536", (long long)n);
   STADE_REQUIRE(loss && lossb && u && ub && un && unb, "heat2d_b: null array argument");
   STADE_REQUIRE(n_step == 0 || u_stack, "heat2d_b: u_stack is null");
+  // Paired columns (16-byte loads, shuffled neighbours) need even n >= 4 and
+  // 16-byte aligned arrays; anything else takes the one-column path.
+  bool paired = n % 2 == 0 && n >= 4;
   for (const void* p : {(const void*)u, (const void*)ub, (const void*)un, (const void*)unb,
                         (const void*)u_stack})
-    STADE_REQUIRE(p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0,
-                  "heat2d_b: arrays must be 16-byte aligned");
+    if (p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15u) != 0) paired = false;
   const bool host_scalar = (flags_of(opts) & STADE_HOST_SCALARS) != 0;
   cudaStream_t s = stream_of(opts);
   void* wsp = nullptr;
@@ -325,8 +411,12 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
       double* dst = t == n_step ? un : u_stack + t * nn;
       double* copy = t == 1 ? u_stack : nullptr;
       PhaseScope ph("fwd_step", s);
-      heat_fwd_kernel<kRowsFwd, true><<<g.fwd, kThreads, 0, s>>>(
-          src, dst, copy, alpha, ni, 0, kRowsFwd, ni, t == n_step ? loss_part : nullptr);
+      double* lp = t == n_step ? loss_part : nullptr;
+      if (paired)
+        heat_fwd_kernel<kRowsFwd, true><<<g.fwd, kThreads, 0, s>>>(src, dst, copy, alpha, ni, 0,
+                                                                   kRowsFwd, ni, lp);
+      else
+        heat_fwd1_kernel<kRowsFwd><<<g.fwd, kColsPerBlock, 0, s>>>(src, dst, copy, alpha, ni, lp);
       STADE_CHECK_LAUNCH();
     }
     st = launch_sum_to_scalar(loss_part, g.nfwd, loss, true, s);
@@ -337,14 +427,22 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
     double* b = (n_step % 2 == 0) ? unb : ub;
     {
       PhaseScope ph("bwd_init", s);
-      heat_bwd_init_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, a, nn / 2);
+      if (paired)
+        heat_bwd_init_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, a, nn / 2);
+      else
+        heat_bwd_init1_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, a, nn);
       STADE_CHECK_LAUNCH();
     }
     for (int64_t t = n_step; t >= 1; --t) {
       PhaseScope ph("bwd_step", s);
-      heat_bwd_kernel<kRowsBwd, true><<<g.bwd, kThreads, 0, s>>>(
-          a, u_stack + (t - 1) * nn, b, alpha, ni, 0, kRowsBwd, ni, alpha_part,
-          t == n_step ? 1 : 0);
+      const double* ut = u_stack + (t - 1) * nn;
+      const int first = t == n_step ? 1 : 0;
+      if (paired)
+        heat_bwd_kernel<kRowsBwd, true><<<g.bwd, kThreads, 0, s>>>(
+            a, ut, b, alpha, ni, 0, kRowsBwd, ni, alpha_part, first);
+      else
+        heat_bwd1_kernel<kRowsBwd><<<g.bwd, kColsPerBlock, 0, s>>>(a, ut, b, alpha, ni,
+                                                                    alpha_part, first);
       STADE_CHECK_LAUNCH();
       double* tmp = a; a = b; b = tmp;
     }
@@ -581,7 +679,7 @@ extern "C" stade_status stade_heat2d_d_f64(double* loss, double* lossd, double* 
                                            int64_t n, int64_t n_step, const stade_opts* opts) {
   STADE_REQUIRE(n >= 0 && n_step >= 0, "heat2d_d: negative size");
   if (n == 0) return STADE_OK;
-  STADE_REQUIRE(n >= 3 && n <= 65536, "heat2d_d: n = %lld outside 3..65536", (long long)n);
+  STADE_REQUIRE(n <= 65536, "heat2d_d: n = %lld exceeds 65536", (long long)n);
   STADE_REQUIRE(loss && lossd && u && ud && un && und, "heat2d_d: null array argument");
   cudaStream_t s = stream_of(opts);
   void* wsp = nullptr;

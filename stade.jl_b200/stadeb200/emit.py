@@ -1,0 +1,239 @@
+"""The .cu emitter (include/stade_emit.h) from Python: STADE-generated Julia
+sweep text in, a CUDA source, a built library and a callable out.
+
+    cu, manifest = emit(open("foo_b.jl").read())            # C++ emitter, via ctypes
+    so = build(cu)                                          # nvcc, sm_100a
+    sweep = Sweep(so, manifest)
+    stacks = sweep.initstacks(n, n_step)                   # the tape, on the device
+    ret = sweep(*args, *stacks)                             # the generated call
+
+`cuda_file(in_path, out_path)` is the file-to-file form of STADE.jl's
+stade_cuda_file (src/STADE.jl:12062-12111): it writes the .cu and, beside it,
+the manifest (.json) with the loop decisions. `build(..., host=True)` compiles
+the same source for the CPU (kernels as loops over their threads), which the
+tests use to check the translation without a GPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import hashlib
+import json
+import os
+import subprocess
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(_HERE)
+EMIT_LIB = os.path.join(PKG, "libstade_emit.so")
+GEN_DIR = os.path.join(PKG, "_gen")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+GENERATED = os.path.join(PKG, "julia", "generated")
+
+_lib = None
+
+
+def generated_source(name: str) -> str:
+    """The text of a generated sweep shipped with the package
+    (julia/generated/<name>.jl: the C1 and C3 adjoints in STADE's output
+    style)."""
+    with open(os.path.join(GENERATED, name + ".jl")) as f:
+        return f.read()
+
+
+class EmitError(RuntimeError):
+    pass
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(EMIT_LIB):
+            raise EmitError(f"{EMIT_LIB} is missing: run `make -C {PKG}`")
+        L = C.CDLL(EMIT_LIB)
+        L.stade_emit_cuda.restype = C.c_int
+        L.stade_emit_cuda.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.c_char_p, C.c_char_p,
+                                      C.c_size_t, C.POINTER(C.c_size_t), C.c_char_p, C.c_size_t,
+                                      C.POINTER(C.c_size_t)]
+        L.stade_emit_last_error.restype = C.c_char_p
+        _lib = L
+    return _lib
+
+
+def _dims_spec(dims) -> str:
+    if not dims:
+        return ""
+    if isinstance(dims, str):
+        return dims
+    return ";".join(f"{k}=" + ",".join(str(x) for x in v) for k, v in dims.items())
+
+
+def emit(source: str, function: str | None = None, precision: int = 64, dims=None):
+    """(CUDA source, manifest dict). dims: {"a": ["i_m"]} or "a=i_m"."""
+    L = lib()
+    src = source.encode()
+    fn = function.encode() if function else None
+    ds = _dims_spec(dims).encode()
+    n_cu, n_m = C.c_size_t(0), C.c_size_t(0)
+    if L.stade_emit_cuda(src, fn, precision, ds, None, 0, C.byref(n_cu), None, 0, C.byref(n_m)):
+        raise EmitError(L.stade_emit_last_error().decode())
+    cu = C.create_string_buffer(n_cu.value + 1)
+    man = C.create_string_buffer(n_m.value + 1)
+    if L.stade_emit_cuda(src, fn, precision, ds, cu, n_cu.value + 1, C.byref(n_cu), man,
+                         n_m.value + 1, C.byref(n_m)):
+        raise EmitError(L.stade_emit_last_error().decode())
+    return cu.value.decode(), json.loads(man.value.decode())
+
+
+def cuda_file(in_path: str, out_path: str, function: str | None = None, precision: int = 64,
+              dims=None) -> dict:
+    """stade_cuda_file: reads a generated .jl, writes the .cu and its manifest
+    (out_path with .json). Returns the manifest."""
+    with open(in_path) as f:
+        cu, man = emit(f.read(), function, precision, dims)
+    with open(out_path, "w") as f:
+        f.write(cu)
+    with open(os.path.splitext(out_path)[0] + ".json", "w") as f:
+        json.dump(man, f, indent=1)
+    return man
+
+
+def build(cu: str, out_dir: str | None = None, host: bool = False) -> str:
+    """Compiles the source into a shared library (cached by content) and
+    returns its path. GPU: nvcc for sm_100a with -fmad=false (each a * b + c
+    rounded twice, as the generated Julia evaluates it). host: g++ with the
+    same rounding."""
+    out_dir = out_dir or GEN_DIR
+    os.makedirs(out_dir, exist_ok=True)
+    h = hashlib.sha256((cu + ("host" if host else "sm_100a")).encode()).hexdigest()[:16]
+    so = os.path.join(out_dir, f"gen_{h}{'_host' if host else ''}.so")
+    if os.path.exists(so):
+        return so
+    src = os.path.join(out_dir, f"gen_{h}.cu")
+    with open(src, "w") as f:
+        f.write(cu)
+    tmp = so + f".{os.getpid()}.tmp"
+    if host:
+        cmd = ["/usr/bin/g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
+               "-DSTADE_EMIT_HOST", "-x", "c++", src, "-o", tmp]
+    else:
+        cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-fmad=false", "-std=c++17", "-shared",
+               "-Xcompiler", "-fPIC", "-diag-suppress", "177", src, "-o", tmp]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise EmitError(f"compiling {src} failed:\n{r.stderr[-4000:]}")
+    os.replace(tmp, so)
+    return so
+
+
+_DT = {"f64": ("float64", C.c_double), "f32": ("float32", C.c_float)}
+
+
+class Sweep:
+    """A built sweep. Call it with the generated positional arguments: device
+    arrays (torch CUDA tensors; numpy arrays for a host build), Python ints
+    and floats. Returns what the generated Julia returns: None, the one
+    returned scalar, or the tuple of them."""
+
+    def __init__(self, so_path: str, manifest: dict, host: bool = False):
+        self.m = manifest
+        self.host = host
+        self.lib = C.CDLL(so_path)
+        self.fdt, self.cf = _DT[manifest["precision"]]
+        args = []
+        for a in manifest["args"]:
+            k = a["kind"]
+            if k in ("array_float", "array_int"):
+                args.append(C.c_void_p)
+            elif k == "scalar_int":
+                args.append(C.c_int64)
+            elif k == "scalar_float":
+                args.append(self.cf)
+            else:
+                args.append(C.POINTER(self.cf))
+        self.fn = getattr(self.lib, manifest["symbol"])
+        self.fn.restype = C.c_int
+        self.fn.argtypes = args + [C.c_void_p]
+        ini = manifest["initstacks"]
+        self.init = None
+        if ini["symbol"]:
+            self.init = getattr(self.lib, ini["symbol"])
+            self.init.restype = C.c_int64
+            self.init.argtypes = [C.c_int64] * len(ini["args"]) + [C.POINTER(C.c_int64),
+                                                                  C.POINTER(C.c_int)]
+
+    def launches(self) -> int:
+        """Kernels this library has launched so far (all calls)."""
+        f = getattr(self.lib, self.m["symbol"] + "_launches")
+        f.restype = C.c_int64
+        return int(f())
+
+    def stack_sizes(self, *ints):
+        ini = self.m["initstacks"]
+        if not self.init:
+            return []
+        n = len(ini["stacks"])
+        sizes = (C.c_int64 * max(n, 1))()
+        dts = (C.c_int * max(n, 1))()
+        got = self.init(*[int(i) for i in ints], sizes, dts)
+        return [(int(sizes[i]), ("float64", "float32", "int64")[dts[i]]) for i in range(got)]
+
+    def initstacks(self, *ints, device="cuda"):
+        """The stacks initstacks_<k> allocates, zero-filled."""
+        out = []
+        for n, dt in self.stack_sizes(*ints):
+            if self.host:
+                import numpy as np
+                out.append(np.zeros(n, dt))
+            else:
+                import torch
+                out.append(torch.zeros(n, dtype=getattr(torch, dt), device=device))
+        return tuple(out)
+
+    def _ptr(self, a, spec):
+        want = "int64" if spec["kind"] == "array_int" else self.fdt
+        if self.host:
+            import numpy as np
+            if not isinstance(a, np.ndarray) or a.dtype != np.dtype(want) or not a.flags.c_contiguous:
+                raise TypeError(f"{spec['name']}: expected a contiguous numpy {want} array")
+            return a.ctypes.data
+        import torch
+        if not (isinstance(a, torch.Tensor) and a.is_cuda and a.is_contiguous()
+                and str(a.dtype) == f"torch.{want}"):
+            raise TypeError(f"{spec['name']}: expected a contiguous CUDA {want} tensor")
+        return a.data_ptr()
+
+    def __call__(self, *args, stream=None):
+        specs = self.m["args"]
+        if len(args) != len(specs):
+            raise TypeError(f"{self.m['function']} takes {len(specs)} arguments, got {len(args)}")
+        cargs, boxes = [], {}
+        for a, s in zip(args, specs):
+            k = s["kind"]
+            if k in ("array_float", "array_int"):
+                cargs.append(self._ptr(a, s))
+            elif k == "scalar_int":
+                cargs.append(int(a))
+            elif k == "scalar_float":
+                cargs.append(float(a))
+            else:
+                b = self.cf(float(a))
+                boxes[s["name"]] = b
+                cargs.append(C.pointer(b))
+        if stream is None and not self.host:
+            import torch
+            stream = torch.cuda.current_stream().cuda_stream
+        rc = self.fn(*cargs, stream or None)
+        if rc != 0:
+            raise EmitError(f"{self.m['symbol']} returned {rc}")
+        ret = [boxes[r].value for r in self.m["returns"]]
+        if not ret:
+            return None
+        return ret[0] if len(ret) == 1 else tuple(ret)
+
+
+def load(source: str, function: str | None = None, precision: int = 64, dims=None,
+         host: bool = False) -> Sweep:
+    """emit + build + Sweep in one call."""
+    cu, man = emit(source, function, precision, dims)
+    return Sweep(build(cu, host=host), man, host=host)

@@ -1,0 +1,233 @@
+"""The .cu emitter on the CPU: its checker (the Julia-subset interpreter) pinned
+to the C++ oracle, the loop decisions it records, the emitted program built
+for the host and compared bit for bit with the interpreter, the sm_100a build,
+the corpus adjoints checked against finite differences of their primals, and
+the refusals."""
+import json
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import cases
+import emit_cases as ec
+import jlsub
+from oracle import oracle as orc
+from stadeb200 import emit
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _interp_run(name, args, precision=64):
+    I = jlsub.Interp(ec.source(name), precision, ec.CASES[name][2])
+    fn = name
+    stacks = ()
+    if f"initstacks_{fn}" in I.funcs:
+        stacks = I.initstacks(f"initstacks_{fn}", *ec.stack_ints(name, args))
+    ret = I.call(fn, *args.values(), *stacks)
+    return ret, stacks
+
+
+# ---- the checker, pinned to the oracle ----------------------------------------------
+@pytest.mark.parametrize("sizes", [(37, 9, 5), (1, 1, 1), (0, 3, 2), (64, 32, 16)])
+def test_interp_matches_oracle_affine(sizes):
+    st, _ = cases.affine_state(*sizes, seeded=True)
+    a, b = cases.copy_state(st), cases.copy_state(st)
+    orc.affine_ls_b(*[a[k] for k in cases.AFFINE_ARGS], *sizes)
+    jlsub.Interp(ec.source("affine_ls_b")).call("affine_ls_b",
+                                                *[b[k] for k in cases.AFFINE_ARGS], *sizes)
+    for k in a:
+        assert np.array_equal(a[k], b[k]), k
+
+
+@pytest.mark.parametrize("n,n_step", [(7, 3), (1, 2), (4, 0), (12, 5)])
+def test_interp_matches_oracle_heat(n, n_step):
+    st, ints = cases.heat_state(n, n_step, seeded=True)
+    a, b = cases.copy_state(st), cases.copy_state(st)
+    r1 = orc.heat2d_b(*[a[k] for k in cases.HEAT_ARGS], 0.2, 0.75, n, n_step, a["u_stack"])
+    I = jlsub.Interp(ec.source("heat2d_b"))
+    (stack,) = I.initstacks("initstacks_heat2d_b", n, n_step)
+    assert stack.size == max(n_step * n * n, 0) or (n_step == 0 and stack.size == 0)
+    r2 = I.call("heat2d_b", *[b[k] for k in cases.HEAT_ARGS], 0.2, 0.75, n, n_step,
+                b["u_stack"][:stack.size])
+    assert r1 == r2
+    for k in cases.HEAT_ARGS + ["u_stack"]:
+        assert np.array_equal(a[k], b[k]), k
+
+
+# ---- loop decisions -----------------------------------------------------------------------
+def _loops(name):
+    _, man = emit.emit(ec.source(name), dims=ec.CASES[name][2])
+    return man, [(l["line"], l["mode"], set(l["atomics"]), set(l["reductions"]),
+                  set(l["private"])) for l in man["loops"]]
+
+
+def test_decisions_affine():
+    man, L = _loops("affine_ls_b")
+    assert [m for _, m, *_ in L] == ["parallel"] * 4
+    assert L[1][2] == {"loss"}                           # the loss sum: atomics
+    assert L[2][2] == set()                              # yb, tb at the thread's own index
+    assert L[3][2] == {"wb", "xb", "bb"} and "sb=0.0" in L[3][4]   # convergent constant
+    assert man["returns"] == [] and man["initstacks"]["stacks"] == []
+
+
+def test_decisions_heat():
+    man, L = _loops("heat2d_b")
+    modes = [m for _, m, *_ in L]
+    assert modes == ["host", "parallel", "parallel", "parallel", "parallel", "host", "parallel",
+                     "parallel"]
+    assert L[7][2] == {"ub"} and L[7][3] == {"alphab"}   # gather as scatter: atomics
+    assert L[6][2] == set()                               # tape restore: own index
+    assert man["returns"] == ["alphab"]
+    kinds = {a["name"]: a["kind"] for a in man["args"]}
+    assert kinds["alpha"] == "scalar_float" and kinds["alphab"] == "scalar_float_inout"
+    assert kinds["n"] == "scalar_int" and man["initstacks"]["stacks"] == [
+        {"name": "u_stack", "dtype": "f64"}]
+
+
+def test_decisions_generic():
+    _, L = _loops("decay_b")
+    assert [m for _, m, *_ in L] == ["host", "parallel", "host", "parallel"]
+    assert L[3][3] == {"kb", "dtb"}
+    _, L = _loops("edge_relu_b")
+    assert [m for _, m, *_ in L] == ["parallel", "parallel"]
+    assert L[1][2] == {"xb"} and "db=0.0" in L[1][4]       # scatter through the table
+    _, L = _loops("bilin_b")
+    assert L[1][2] == {"xb", "zb"}                        # ab[i_i, i_j]: the decode is injective
+    _, L = _loops("cumsum_sq_b")
+    assert [m for _, m, *_ in L] == ["sequential", "parallel", "parallel", "sequential"]
+    _, L = _loops("window_b")
+    assert L[3][2] == {"wb", "xb"}
+    man, L = _loops("halving_b")
+    assert [m for _, m, *_ in L] == ["sequential", "parallel"]
+
+
+# ---- the emitted program, host build, against the interpreter -----------------------------
+@pytest.mark.parametrize("name", sorted(ec.CASES))
+def test_host_build_matches_interpreter(name):
+    sw = emit.load(ec.source(name), dims=ec.CASES[name][2], host=True)
+    for size in ec.CASES[name][4][:3]:
+        args = ec.make(name, size)
+        ref = ec.copy_args(args)
+        r_ref, st_ref = _interp_run(name, ref)
+        out = ec.copy_args(args)
+        stacks = sw.initstacks(*ec.stack_ints(name, out))
+        assert [s.size for s in stacks] == [s.size for s in st_ref]
+        r_out = sw(*out.values(), *stacks)
+        assert r_out == r_ref, (name, size)
+        for k, v in out.items():
+            if isinstance(v, np.ndarray):
+                assert np.array_equal(v, ref[k]), (name, size, k)
+        for s1, s2 in zip(stacks, st_ref):
+            assert np.array_equal(s1, s2), (name, size, "stack")
+
+
+@pytest.mark.parametrize("name", ["affine_ls_b", "window_b"])
+def test_host_build_float32(name):
+    sw = emit.load(ec.source(name), precision=32, dims=ec.CASES[name][2], host=True)
+    args = ec.make(name, ec.CASES[name][4][0])
+    a32 = ec.copy_args(args)
+    for k, v in a32.items():
+        if isinstance(v, np.ndarray) and v.dtype == np.float64:
+            a32[k] = v.astype(np.float32)
+    ref = ec.copy_args(a32)
+    _interp_run(name, ref, precision=32)
+    sw(*a32.values())
+    for k, v in a32.items():
+        if isinstance(v, np.ndarray):
+            assert v.dtype == np.float32
+            err = np.abs(v - ref[k]).max() / max(np.abs(ref[k]).max(), 1e-30)
+            assert err <= 1e-6, (k, err)
+
+
+# ---- the corpus adjoints are the derivatives of their primals ---------------------------
+def _primal_loss(I, name, args, wseed):
+    """<seed, outputs> of the primal: loss-style primals report loss[1];
+    decay reports <w, u_final>."""
+    a = ec.copy_args(args)
+    prim = name[:-2]
+    params = I.funcs[prim][0]
+    I.call(prim, *[a[p] for p in params])
+    if "loss" in a:
+        return float(a["loss"][0])
+    return float(np.dot(wseed, a["u"]))
+
+
+@pytest.mark.parametrize("name", ["decay_b", "edge_relu_b", "bilin_b", "cumsum_sq_b",
+                                  "window_b"])
+def test_corpus_adjoint_is_the_derivative(name):
+    size = ec.CASES[name][4][0]
+    args = ec.make(name, size, "fd")
+    I = jlsub.Interp(ec.source(name), 64, ec.CASES[name][2])
+    prim_params = I.funcs[name[:-2]][0]
+    floats = [p for p in prim_params if isinstance(args.get(p), (np.ndarray, float))
+              and not (isinstance(args.get(p), np.ndarray) and args[p].dtype == np.int64)
+              and p != "loss" and p not in ("c", "z")]
+    r = np.random.default_rng(7)
+    v = {p: (r.standard_normal(args[p].shape) if isinstance(args[p], np.ndarray)
+             else float(r.standard_normal())) for p in floats}
+    wseed = r.standard_normal(args["u"].shape) if name == "decay_b" else None
+    # adjoint: zero shadows, seed lossb = 1 (or ub = w for decay)
+    adj = ec.copy_args(args)
+    for p in list(adj):
+        if p.endswith("b") and p[:-1] in adj and p not in ("b",):
+            adj[p] = np.zeros_like(adj[p]) if isinstance(adj[p], np.ndarray) else 0.0
+    if "lossb" in adj:
+        adj["lossb"][:] = 1.0
+    if name == "decay_b":
+        adj["ub"] = wseed.copy()
+    stacks = I.initstacks(f"initstacks_{name}", *ec.stack_ints(name, adj))
+    ret = I.call(name, *adj.values(), *stacks)
+    rets = dict(zip([p + "b" for p in prim_params if not isinstance(args.get(p), np.ndarray)
+                     and p not in ec.CASES[name][3] and not p.startswith("i_")],
+                    ret if isinstance(ret, tuple) else ([ret] if ret is not None else [])))
+    grad_dot = 0.0
+    for p in floats:
+        g = rets[p + "b"] if not isinstance(args[p], np.ndarray) else adj[p + "b"]
+        grad_dot += float(np.sum(np.asarray(g) * v[p]))
+    eps = 1e-6
+
+    def at(s):
+        a = ec.copy_args(args)
+        for p in floats:
+            a[p] = a[p] + s * v[p]
+        return _primal_loss(I, name, a, wseed)
+    fd = (at(eps) - at(-eps)) / (2 * eps)
+    assert abs(fd - grad_dot) <= 1e-6 * max(1.0, abs(fd)), (fd, grad_dot)
+
+
+# ---- builds and refusals --------------------------------------------------------------------
+@pytest.mark.parametrize("name", sorted(ec.CASES))
+def test_builds_for_sm100a(name):
+    cu, _ = emit.emit(ec.source(name), dims=ec.CASES[name][2])
+    assert os.path.exists(emit.build(cu))
+
+
+@pytest.mark.parametrize("src,msg", [
+    ("function f_b(x, i_n)\n for i = 1:i_n\n x[i] = gamma(x[i])\n end\nend\n",
+     "function gamma is not supported"),
+    ("function f_b(a, i_n)\n for k = 1:i_n\n a[div(k, 2), k] = 1.0\n end\nend\n",
+     "cannot infer dimension 1 of a"),
+    ("function f_b(x, i_n)\n for i = 1:i_n\n if x[i] > 0.0\n return nothing\n end\n end\nend\n",
+     "return inside a loop or branch"),
+    ("function f_b(x, i_n)\n for i = 1:i_n\n x[i] = 1.0\n", "missing 'end'"),
+])
+def test_refusals(src, msg):
+    with pytest.raises(emit.EmitError, match=msg):
+        emit.emit(src)
+
+
+def test_cli_and_cuda_file(tmp_path):
+    src = os.path.join(ROOT, "tests", ec.CORPUS, "bilin_b.jl")
+    exe = os.path.join(ROOT, "stade.jl_b200", "stade_emit")
+    out = tmp_path / "bilin_b.cu"
+    man = tmp_path / "bilin_b.json"
+    subprocess.run([exe, src, str(out), "--dims", "a=i_m;ab=i_m", "--manifest", str(man)],
+                   check=True)
+    m = json.loads(man.read_text())
+    assert m["symbol"] == "stade_bilin_b" and "extern \"C\" int stade_bilin_b(" in out.read_text()
+    m2 = emit.cuda_file(src, str(tmp_path / "b2.cu"), dims={"a": ["i_m"], "ab": ["i_m"]})
+    assert m2 == m and (tmp_path / "b2.json").exists()
+    bad = subprocess.run([exe, src, str(out)], capture_output=True, text=True)
+    assert bad.returncode == 1 and "cannot infer dimension" in bad.stderr

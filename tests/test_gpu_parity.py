@@ -104,7 +104,9 @@ def test_mlp2_ce_b_deterministic():
 
 
 @pytest.mark.parametrize("n,n_step,seeded", [(64, 4, False), (34, 3, True), (6, 2, True),
-                                             (258, 5, False), (4, 1, True), (10, 0, True)])
+                                             (258, 5, False), (4, 1, True), (10, 0, True),
+                                             (5, 3, True), (1, 2, True), (2, 3, True),
+                                             (3, 1, False), (257, 4, True)])
 def test_heat2d_b(n, n_step, seeded):
     ref, out, ints, ab_ref, ab_gpu = _run_both(lambda: cases.heat_state(n, n_step, seeded=seeded),
                                                cases.oracle_heat, cases.gpu_heat)

@@ -100,7 +100,8 @@ def test_mlp2_ce_d_parity(sizes, dtype):
             assert e <= max(1e-5, rel_err(ref[k], truth[k])), (k, e)
 
 
-@pytest.mark.parametrize("n,n_step", [(34, 3), (64, 4), (7, 2), (10, 0), (258, 5)])
+@pytest.mark.parametrize("n,n_step", [(34, 3), (64, 4), (7, 2), (10, 0), (258, 5), (1, 3),
+                                      (2, 2)])
 def test_heat2d_d_parity(n, n_step):
     u0 = synth.heat2d_inputs(n)["u"]
     r = _rng(f"heat{n}")
