@@ -630,6 +630,8 @@ class EmittedHeat2d(Heat2d):
     """C3 through the .cu emitter's output for julia/generated/heat2d_b.jl
     (one GPU: the emitted sweep has no slab form)."""
 
+    graphable = False   # returns alphab to the host: synchronises, cannot be captured
+
     def __init__(self, torch, rank, world, comm_factory):
         if world > 1:
             raise SystemExit("--impl emitted runs on one GPU")
@@ -946,7 +948,7 @@ def main():
         W.step()
     torch.cuda.synchronize()
     step_fn, graph = W.step, None
-    if not args.no_graph:
+    if not args.no_graph and getattr(W, "graphable", True):
         try:
             side = torch.cuda.Stream()
             side.wait_stream(torch.cuda.current_stream())

@@ -1660,7 +1660,7 @@ class Emitter {
           const std::string& v = s.lhs->s;
           if (u.par && u.plan.reductions.count(v)) {
             EP term = accum_term(s);
-            o << pad << "atomicAdd(&" << scalar_ref(v, {}) << ", (" << T_ << ")"
+            o << pad << "jl_atomic_add(&" << scalar_ref(v, {}) << ", (" << T_ << ")"
               << cx(term, locals, s.line) << ");\n";
             return;
           }
@@ -1678,8 +1678,8 @@ class Emitter {
             o << pad << "atomicAdd((unsigned long long*)&p_" << a << "[" << offset(s.lhs, locals, s.line)
               << "], (unsigned long long)(" << cx(term, locals, s.line) << "));\n";
           else
-            o << pad << "atomicAdd(&p_" << a << "[" << offset(s.lhs, locals, s.line) << "], (" << T_
-              << ")" << cx(term, locals, s.line) << ");\n";
+            o << pad << "jl_atomic_add(&p_" << a << "[" << offset(s.lhs, locals, s.line) << "], ("
+              << T_ << ")" << cx(term, locals, s.line) << ");\n";
           (void)ty;
           return;
         }
@@ -1915,6 +1915,7 @@ class Emitter {
     for (size_t i = 0; i < decl.size(); ++i) o << decl[i] << ", ";
     o << "void* stream) {\n";
     o << "  cudaStream_t s_ = (cudaStream_t)stream;\n  (void)s_;\n";
+    o << "  STADE_CLEAR_ERROR();   // a failure before this call is not this call's\n";
     for (auto& h : host_ints_)
       if (!params_.count(h)) o << "  int64_t " << cname(h) << " = 0;\n";
     o << "  STADE_LAUNCH(stade_k_init, 1, 1, s_";
@@ -2037,6 +2038,7 @@ template <class T, class U> static T atomicAdd(T* p, U v) { T o = *p; *p = (T)(o
   for (unsigned b_ = 0; b_ < (unsigned)(nb); ++b_) for (unsigned t_ = 0; t_ < (unsigned)(nt); ++t_) { \
     blockIdx.x = b_; threadIdx.x = t_; k(__VA_ARGS__); } } while (0)
 #define STADE_GEN_CHECK() do { } while (0)
+#define STADE_CLEAR_ERROR() do { } while (0)
 static int stade_box_read(void* dst, const void* box, size_t n, cudaStream_t) { memcpy(dst, box, n); return 0; }
 #define JL_FN(name) static inline double jl_##name(double x) { return name(x); } \
                     static inline float jl_##name(float x) { return name##f(x); }
@@ -2044,6 +2046,7 @@ static int stade_box_read(void* dst, const void* box, size_t n, cudaStream_t) { 
 #include <cuda_runtime.h>
 #define STADE_LAUNCH(k, nb, nt, s, ...) do { k<<<(nb), (nt), 0, (s)>>>(__VA_ARGS__); ++stade_launches_; } while (0)
 #define STADE_GEN_CHECK() do { if (cudaGetLastError() != cudaSuccess) return 2; } while (0)
+#define STADE_CLEAR_ERROR() do { (void)cudaGetLastError(); } while (0)
 template <class B>
 static int stade_box_read(void* dst, const B& box, size_t n, cudaStream_t s) {
   if (cudaMemcpyFromSymbolAsync(dst, box, n, 0, cudaMemcpyDeviceToHost, s) != cudaSuccess) return 1;
@@ -2051,6 +2054,25 @@ static int stade_box_read(void* dst, const B& box, size_t n, cudaStream_t s) {
 }
 #define JL_FN(name) __device__ __forceinline__ double jl_##name(double x) { return name(x); } \
                     __device__ __forceinline__ float jl_##name(float x) { return name##f(x); }
+// Atomic add aggregated over the lanes of a warp that hit the same address
+// (one atomic per address per warp, as the generated __stade_wa_add! does).
+template <class T>
+__device__ __forceinline__ void jl_atomic_add(T* p, T v) {
+  const unsigned mask = __activemask();
+  const unsigned lane = threadIdx.x & 31u;
+  const unsigned peers = __match_any_sync(mask, (unsigned long long)p);
+  if (!__any_sync(mask, __popc(peers) > 1)) {
+    atomicAdd(p, v);
+    return;
+  }
+  // every lane of a peer group walks the group's lanes in the same order
+  T sum = (T)0;
+  for (unsigned m = peers; m; m &= m - 1u) sum += __shfl_sync(peers, v, __ffs(m) - 1);
+  if ((unsigned)(__ffs(peers) - 1) == lane) atomicAdd(p, sum);
+}
+#endif
+#ifdef STADE_EMIT_HOST
+template <class T> static inline void jl_atomic_add(T* p, T v) { *p = (T)(*p + v); }
 #endif
 #ifdef STADE_EMIT_HOST
 #define JL_HD static inline
@@ -2061,11 +2083,25 @@ JL_FN(sqrt) JL_FN(exp) JL_FN(log) JL_FN(tanh) JL_FN(sin) JL_FN(cos) JL_FN(tan) J
 JL_FN(cosh) JL_FN(asin) JL_FN(acos) JL_FN(atan) JL_FN(log2) JL_FN(log10) JL_FN(exp2)
 JL_FN(expm1) JL_FN(log1p) JL_FN(cbrt)
 // Julia's integer division family (div truncates, fld floors, mod takes the divisor's sign)
-JL_HD int64_t jl_div(int64_t a, int64_t b) { return a / b; }
-JL_HD int64_t jl_rem(int64_t a, int64_t b) { return a % b; }
+// 64-bit division is a long instruction sequence on the GPU; index arithmetic
+// is almost always non-negative and below 2^31, where 32-bit division gives
+// the same quotient.
+JL_HD bool jl_small(int64_t a, int64_t b) {
+  return (uint64_t)a <= 0x7fffffffull && (uint64_t)(b - 1) < 0x7fffffffull;
+}
+JL_HD int64_t jl_div(int64_t a, int64_t b) {
+  return jl_small(a, b) ? (int64_t)((uint32_t)a / (uint32_t)b) : a / b;
+}
+JL_HD int64_t jl_rem(int64_t a, int64_t b) {
+  return jl_small(a, b) ? (int64_t)((uint32_t)a % (uint32_t)b) : a % b;
+}
 JL_HD int64_t jl_fld(int64_t a, int64_t b) { int64_t q = a / b; return (q * b != a && ((a < 0) != (b < 0))) ? q - 1 : q; }
 JL_HD int64_t jl_cld(int64_t a, int64_t b) { int64_t q = a / b; return (q * b != a && ((a < 0) == (b < 0))) ? q + 1 : q; }
-JL_HD int64_t jl_mod(int64_t a, int64_t b) { int64_t r = a % b; return (r != 0 && ((r < 0) != (b < 0))) ? r + b : r; }
+JL_HD int64_t jl_mod(int64_t a, int64_t b) {
+  if (jl_small(a, b)) return (int64_t)((uint32_t)a % (uint32_t)b);
+  int64_t r = a % b;
+  return (r != 0 && ((r < 0) != (b < 0))) ? r + b : r;
+}
 JL_HD int64_t jl_mod1(int64_t a, int64_t b) { int64_t r = jl_mod(a, b); return r == 0 ? b : r; }
 JL_HD int64_t jl_imax(int64_t a, int64_t b) { return a > b ? a : b; }
 JL_HD int64_t jl_imin(int64_t a, int64_t b) { return a < b ? a : b; }
