@@ -26,6 +26,7 @@
 #include "gemm_dmma.cuh"
 #include "gemm_simt.cuh"
 #include "tc_gemm.cuh"
+#include "tcgen05.cuh"
 
 namespace stade {
 namespace {
@@ -202,10 +203,73 @@ mlp_head_b_kernel(const T* __restrict__ lossb, const T* __restrict__ y, T* __res
   }
 }
 
+// Logits without bias for the TMA path, z0[s][c] = sum_k h[s, k] w2[k, c]
+// (the GEMM epilogue then only computes h, which takes the logits off its
+// critical path: forward GEMM 374 -> 270 us, this pass ~90 us, at 65,536 x
+// 512). One warp per sample row, n_h % 4 == 0: lane l takes the float4 groups
+// l, l + 32, ... of the row (coalesced), all loaded before any arithmetic; w2
+// is staged in shared memory class-major, so the lanes' float4 reads are
+// consecutive; then one warp sum per class. (Measured slower: one thread per
+// sample, with w2 read as broadcasts, and the same fused into the head.)
+template <int NO>
+__global__ void __launch_bounds__(256)
+mlp_logits_kernel(const float* __restrict__ h, const float* __restrict__ w2,
+                  float* __restrict__ z0, int n_s, int n_h, int n_o) {
+  extern __shared__ __align__(16) float w2t[];   // NO x n_h
+  for (int e = threadIdx.x; e < n_h * NO; e += blockDim.x) {
+    const int c = e / n_h, k = e % n_h;
+    w2t[e] = c < n_o ? w2[(int64_t)k * n_o + c] : 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int n4 = n_h >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w2t);
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < n_s; s += warps) {
+    const float4* hr = reinterpret_cast<const float4*>(h + (int64_t)s * n_h);
+    float acc[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) acc[c] = 0.f;
+    for (int base = 0; base < n4; base += 128) {
+      float4 hv[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int k4 = base + lane + 32 * t;
+        hv[t] = k4 < n4 ? hr[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int k4 = base + lane + 32 * t;
+        if (k4 < n4) {
+#pragma unroll
+          for (int c = 0; c < NO; ++c) {
+            if (c < n_o) {
+              const float4 w = w4[c * n4 + k4];
+              acc[c] = fmaf(hv[t].x, w.x, acc[c]);
+              acc[c] = fmaf(hv[t].y, w.y, acc[c]);
+              acc[c] = fmaf(hv[t].z, w.z, acc[c]);
+              acc[c] = fmaf(hv[t].w, w.w, acc[c]);
+            }
+          }
+        }
+      }
+    }
+    float mine = 0.f;
+#pragma unroll
+    for (int c = 0; c < NO; ++c) {
+      if (c < n_o) {
+        const float v = warp_sum(acc[c]);
+        if (lane == c) mine = v;
+      }
+    }
+    if (lane < n_o) z0[(int64_t)s * n_o + lane] = mine;
+  }
+}
+
 // Per-sample softmax cross-entropy, forward and reverse, one thread per
-// sample (the tensor-core path): the logits come from the partial sums the
-// forward GEMM's epilogue wrote (zpart[chunk][s][c], summed in chunk order).
-// Statement order as mlp_head_b_kernel.
+// sample (the tensor-core path): the logits come from the partial sums
+// zpart[chunk][s][c] (the forward GEMM's epilogue, or mlp_logits_kernel with
+// one chunk), summed in chunk order. Statement order as mlp_head_b_kernel.
 template <class T, int NO>
 __global__ void __launch_bounds__(256)
 mlp_head_small_kernel(const T* __restrict__ zpart, int nchunks, const T* __restrict__ lossb,
@@ -452,17 +516,19 @@ mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
       if (acc2.x != 0.f || acc2.y != 0.f)
         *reinterpret_cast<float2*>(hb + off) = make_float2(0.f, 0.f);
     };
+    // eight samples' loads in flight per thread (measured: 175 -> 136 us at
+    // 65,536 x 512; h and hb are read once, so they stream past the caches)
     int i = 0;
-    for (; i + 4 <= ns; i += 4) {
-      float2 hv[4], hbv[4];
+    for (; i + 8 <= ns; i += 8) {
+      float2 hv[8], hbv[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const int64_t off = (int64_t)(s0 + i + u) * n_h + k;
-        hv[u] = *reinterpret_cast<const float2*>(h + off);
-        hbv[u] = *reinterpret_cast<const float2*>(hb + off);
+        hv[u] = __ldcs(reinterpret_cast<const float2*>(h + off));
+        hbv[u] = __ldcs(reinterpret_cast<const float2*>(hb + off));
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) one(i + u, hv[u], hbv[u]);
+      for (int u = 0; u < 8; ++u) one(i + u, hv[u], hbv[u]);
     }
     for (; i < ns; ++i) {
       const int64_t off = (int64_t)(s0 + i) * n_h + k;
@@ -1088,11 +1154,14 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
       if (st == STADE_OK) st = tma_split_lo(w1, w.w1_lo, n_i * n_h, s);
     }
     if (st != STADE_OK) return st;
-    // 1. h = tanh(x W1 + b1) and the logits' partial sums, TMA-fed tensor cores
+    // 1. h = tanh(x W1 + b1), TMA-fed tensor cores (the logits in a pass of
+    // their own when w2 fits in shared memory, else in the GEMM's epilogue)
+    const size_t lsm = sizeof(float) * (size_t)H * (O <= 16 ? 16 : 32);
+    const bool own_logits = lsm <= 160 * 1024 && H % 4 == 0;
     {
       PhaseScope ph("fwd_gemm", s);
-      st = tma_forward_tanh_logits(x, w.x_lo, w1, w.w1_lo, b1, w2, h, w.zpart, S, I, H,
-                                   O, s);
+      st = tma_forward_tanh_logits(x, w.x_lo, w1, w.w1_lo, b1, w2, h,
+                                   own_logits ? nullptr : w.zpart, S, I, H, O, s);
     }
     if (st != STADE_OK) return st;
     // 2. softmax cross-entropy and its reverse, one thread per sample
@@ -1100,8 +1169,16 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
       PhaseScope ph("head", s);
       const int blocks = (S + 255) / 256;
       auto kern = O <= 16 ? mlp_head_small_kernel<float, 16> : mlp_head_small_kernel<float, 32>;
-      kern<<<blocks, 256, 0, s>>>(w.zpart, tc_logit_parts(n_h), lossb, y, yb, b2, z, zb, p, pb,
-                                  w.gbuf, S, O, w.loss_part);
+      if (own_logits) {
+        auto lk = O <= 16 ? mlp_logits_kernel<16> : mlp_logits_kernel<32>;
+        if (lsm > 48 * 1024)
+          STADE_CUDA(cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)lsm));
+        lk<<<6 * tc5::sm_count(), 256, lsm, s>>>(h, w2, w.zpart, S, H, O);
+        STADE_CHECK_LAUNCH();
+      }
+      kern<<<blocks, 256, 0, s>>>(w.zpart, own_logits ? 1 : tc_logit_parts(n_h), lossb, y, yb,
+                                  b2, z, zb, p, pb, w.gbuf, S, O, w.loss_part);
       STADE_CHECK_LAUNCH();
       st = launch_sum_to_scalar(w.loss_part, blocks, loss, true, s);
     }

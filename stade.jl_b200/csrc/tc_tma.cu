@@ -162,8 +162,10 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m,
           for (int i = 0; i < 16; ++i)
             if (nn + i < el.N) o[i] = hv[i];
         }
-        // logits partial; w2 rows are the same for the whole warp (broadcast)
-        if (el.w2_stride > 0) {
+        // logits partial (when asked for); w2 rows are the same for the whole
+        // warp (broadcast)
+        if (el.zpart == nullptr) {
+        } else if (el.w2_stride > 0) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             if (nn + i < el.N) {
@@ -193,7 +195,7 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m,
         }
       }
     }
-    if (m < el.M) {
+    if (m < el.M && el.zpart != nullptr) {
       const int part = (n0 / BN) * 2 + half;
       float* zr = el.zpart + ((int64_t)part * el.M + m) * el.n_o;
 #pragma unroll
@@ -871,7 +873,7 @@ stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const
   tma::Operand B{w1_hi, w1_lo, I, H, H, true};
   tma::Geometry g = tma::geometry(S, H, I, 1, false, true);
   const int stride = (O + 3) / 4 * 4;
-  const bool smem_w2 = (int64_t)H * stride * 4 <= tma::kW2SmemBytes;
+  const bool smem_w2 = zpart != nullptr && (int64_t)H * stride * 4 <= tma::kW2SmemBytes;
   tma::EpiTanhLogits el{h, b1, w2, zpart, H, S, H, O, 2, smem_w2 ? stride : 0};
   if (tma::pair_enabled()) {
     if (O <= 16) return tma::run_pair<0, 16>(A, B, g, el, {}, {}, s);
