@@ -315,7 +315,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
   } else if (warp == 1) {
     if (lane == 0) {
       // ---- MMA issuer -------------------------------------------------------------
-      const uint32_t idesc = idesc_tf32(BM, BN, g.a_mn, g.b_mn);
+      const uint32_t idesc_full = idesc_tf32(BM, BN, g.a_mn, g.b_mn);
       const uint32_t a_lbo = g.a_mn ? 4096u : 16u, a_sbo = g.a_mn ? 512u : 1024u;
       const uint32_t b_lbo = g.b_mn ? 4096u : 16u, b_sbo = g.b_mn ? 512u : 1024u;
       const uint32_t a_lay = g.a_mn ? 1u : 2u, b_lay = g.b_mn ? 1u : 2u;
@@ -328,6 +328,16 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
         const int kend = min(g.K, kbeg + g.k_slice);
         const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
         const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+        // A ragged last N tile of a K-major B runs MMAs only as wide as its
+        // columns (rounded up to 16; the rest of the box is zero-filled and
+        // the epilogue stores only columns < N): 784 = 6 x 128 + 16 spends
+        // 1/8 of a tile there instead of a whole one.
+        uint32_t idesc = idesc_full;
+        if (!g.b_mn) {
+          const int n0 = ((t % tiles_per_slice) % g.n_tiles) * BN;
+          const int n_eff = min(BN, (g.N - n0 + 15) / 16 * 16);
+          if (n_eff < BN) idesc = idesc_tf32(BM, n_eff, g.a_mn, g.b_mn);
+        }
         for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
           const int b = chain % kAccBufs;
           const uint32_t acc = tmem + (uint32_t)(b * BN);
