@@ -40,6 +40,7 @@
 #include <algorithm>
 #include <cctype>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -612,8 +613,29 @@ struct LoopPlan {
 
 enum Storage { S_HOSTINT, S_LOCAL, S_FBOX, S_IBOX };
 
+// The iteration v whose accumulation lands on target index j, for one
+// accumulation statement (the scatter -> gather rewrite, as cgen_gather_loop
+// and cgen_gather_periodic_inverse, src/STADE.jl:7343-7532).
+struct Inverse {
+  enum Kind { IDENT, OFFSET, PERIODIC2 } kind = IDENT;
+  long off = 0;        // OFFSET: the index is v + off
+  EP n;                // PERIODIC2: v = (i - 1) n + j decoded on an n x n grid
+  long sr = 0, sc = 0; // PERIODIC2: periodic row / column shift of the target
+};
+struct GatherPart {
+  Stmt* st;
+  EP term;
+  Inverse inv;
+};
+struct Gather {
+  std::string array;
+  std::vector<GatherPart> parts;
+};
+
 struct Unit {
   bool par = false;
+  bool gather = false;        // a gather kernel (stmts = {the original loop})
+  std::vector<Gather> gathers;
   std::vector<SP> stmts;      // SEQ: statements in order; PAR: the one For
   LoopPlan plan;
   std::set<std::string> scalars, arrays;  // referenced
@@ -656,6 +678,8 @@ class Emitter {
   Func& f_;
   const Func* init_;
   bool f32_;
+  // scatter -> gather rewrite of invertible accumulations (STADE_EMIT_GATHER=0: atomics)
+  bool gather_ = !(std::getenv("STADE_EMIT_GATHER") && std::string(std::getenv("STADE_EMIT_GATHER")) == "0");
   std::string T_;
   std::set<std::string> params_, arrays_, ints_, int_arrays_, host_ints_, returned_;
   std::map<std::string, std::vector<EP>> dims_;
@@ -666,6 +690,7 @@ class Emitter {
   std::set<std::string> stacks_;
   std::map<std::string, std::string> stack_type_;  // name -> "f" / "i"
   std::vector<std::string> decisions_;
+  std::map<const Stmt*, std::string> red_sites_;   // accumulation -> block sum register
 
   // ---- kinds: array / scalar, integer / float (the evidence shape_infer uses,
   // src/STADE.jl:936-958: loop variables, range bounds, div / mod arguments,
@@ -1129,6 +1154,202 @@ class Emitter {
     return reads_array(e, lhs->s);
   }
 
+  // Private integer scalars of loop L assigned one expression (however often)
+  // that does not read them: their definitions, to see through decoded indices.
+  std::map<std::string, EP> int_defs(Stmt& L, const LoopPlan& p) {
+    std::map<std::string, EP> defs;
+    std::map<std::string, std::vector<EP>> rhs_of;
+    walk_stmts(L.body, [&](Stmt& x) {
+      if (x.kind == Stmt::Assign && x.lhs->kind == Expr::Var) rhs_of[x.lhs->s].push_back(x.rhs);
+    });
+    for (auto& [v, rs] : rhs_of) {
+      auto pv = p.privates.find(v);
+      if (pv == p.privates.end() || !pv->second.empty() || !ints_.count(v)) continue;
+      bool same = true;
+      for (auto& r : rs)
+        if (text(r) != text(rs[0]) || reads_scalar(r, v)) same = false;
+      if (same) defs[v] = rs[0];
+    }
+    return defs;
+  }
+
+  // ---- scatter -> gather ---------------------------------------------------------
+  EP subst(const EP& e, const std::map<std::string, EP>& defs, int depth = 0) {
+    if (!e) return e;
+    if (e->kind == Expr::Var) {
+      auto d = defs.find(e->s);
+      if (d != defs.end() && depth < 32) return subst(d->second, defs, depth + 1);
+      return e;
+    }
+    if (e->a.empty()) return e;
+    auto c = std::make_shared<Expr>(*e);
+    for (auto& x : c->a) x = subst(x, defs, depth + 1);
+    return c;
+  }
+  static bool is_lit(const EP& e, long* v) {
+    if (!e || e->kind != Expr::Num || !e->int_lit) return false;
+    *v = std::stol(e->s);
+    return true;
+  }
+  static bool is_var(const EP& e, const std::string& v) {
+    return e->kind == Expr::Var && e->s == v;
+  }
+  static bool plus_one(const EP& e) {
+    long one;
+    return e->kind == Expr::Bin && e->s == "+" && is_lit(e->a[1], &one) && one == 1;
+  }
+
+  struct Coord {
+    int axis;
+    EP n;
+    long shift;
+  };
+  // div(v - 1, n) + 1 (axis 0, the row) or mod(v - 1, n) + 1 (axis 1, the column)
+  bool decode(const EP& e, const std::string& v, Coord& c) {
+    if (!plus_one(e)) return false;
+    const EP& f = e->a[0];
+    if (f->kind != Expr::Call || (f->s != "div" && f->s != "mod") || f->a.size() != 2) return false;
+    const EP& x = f->a[0];
+    long k;
+    if (!(x->kind == Expr::Bin && x->s == "-" && is_var(x->a[0], v) && is_lit(x->a[1], &k) &&
+          k == 1))
+      return false;
+    c.axis = f->s == "div" ? 0 : 1;
+    c.n = f->a[1];
+    c.shift = 0;
+    return true;
+  }
+  // a decoded coordinate, or its periodic shift mod(x + k, n) + 1 (by k + 1)
+  bool coord(const EP& e, const std::string& v, Coord& c) {
+    if (decode(e, v, c)) return true;
+    if (!plus_one(e)) return false;
+    const EP& f = e->a[0];
+    if (f->kind != Expr::Call || f->s != "mod" || f->a.size() != 2) return false;
+    EP base = f->a[0];
+    long k = 0;
+    Coord b;
+    if (!decode(base, v, b)) {   // mod(x + k, n): strip the literal k
+      if (!(base->kind == Expr::Bin && (base->s == "+" || base->s == "-") &&
+            is_lit(base->a[1], &k)))
+        return false;
+      if (base->s == "-") k = -k;
+      base = base->a[0];
+      if (!decode(base, v, b)) return false;
+    }
+    if (text(b.n) != text(f->a[1])) return false;
+    c = b;
+    c.shift = k + 1;
+    return true;
+  }
+  // the inverse of a target index: the identity, a constant offset, or a
+  // periodic shift on the n x n grid that v = (i - 1) n + j flattens
+  bool inverse_of(const EP& idx, const std::string& v, Inverse& inv) {
+    long k;
+    if (is_var(idx, v)) {
+      inv.kind = Inverse::IDENT;
+      return true;
+    }
+    if (idx->kind == Expr::Bin && (idx->s == "+" || idx->s == "-")) {
+      if (is_var(idx->a[0], v) && is_lit(idx->a[1], &k)) {
+        inv.kind = Inverse::OFFSET;
+        inv.off = idx->s == "+" ? k : -k;
+        return true;
+      }
+      if (idx->s == "+" && is_var(idx->a[1], v) && is_lit(idx->a[0], &k)) {
+        inv.kind = Inverse::OFFSET;
+        inv.off = k;
+        return true;
+      }
+    }
+    if (idx->kind == Expr::Bin && idx->s == "+") {
+      for (int o = 0; o < 2; ++o) {
+        const EP& prod = idx->a[o];
+        const EP& cexp = idx->a[1 - o];
+        if (prod->kind != Expr::Bin || prod->s != "*") continue;
+        for (int q = 0; q < 2; ++q) {
+          const EP& rm1 = prod->a[q];
+          const EP& nn = prod->a[1 - q];
+          long one;
+          if (rm1->kind != Expr::Bin || rm1->s != "-" || !is_lit(rm1->a[1], &one) || one != 1)
+            continue;
+          Coord R, Cc;
+          if (!coord(rm1->a[0], v, R) || !coord(cexp, v, Cc)) continue;
+          if (R.axis != 0 || Cc.axis != 1 || text(R.n) != text(Cc.n) || text(R.n) != text(nn))
+            continue;
+          if (R.shift == 0 && Cc.shift == 0) {
+            inv.kind = Inverse::IDENT;
+            return true;
+          }
+          inv.kind = Inverse::PERIODIC2;
+          inv.n = R.n;
+          inv.sr = R.shift;
+          inv.sc = Cc.shift;
+          return true;
+        }
+      }
+    }
+    return false;
+  }
+
+  // Arrays that parallel loop L only accumulates into through invertible
+  // indices: each becomes a gather (a thread per target element replays the
+  // iterations that land on it, no atomics). The loop body must be
+  // straight-line, and no array the loop writes may be read after its write,
+  // so that a replay sees the values from before the loop.
+  std::vector<Gather> plan_gather(Stmt& L, const LoopPlan& p) {
+    std::vector<Gather> out;
+    if (p.atomic_arrays.empty()) return out;
+    for (auto& st : L.body)
+      if (st->kind != Stmt::Assign) return out;
+    long stepv = 1;
+    if (L.step && !is_lit(L.step, &stepv)) return out;
+    if (stepv != 1 && stepv != -1) return out;
+    std::set<std::string> written;
+    for (auto& st : L.body) {
+      bool bad = false;
+      auto chk = [&](const EP& e) {
+        walk_expr(e, [&](const EP& y) {
+          if (y->kind == Expr::Ref && written.count(y->s)) bad = true;
+        });
+      };
+      chk(st->rhs);
+      if (st->lhs->kind == Expr::Ref)
+        for (auto& i : st->lhs->a) chk(i);
+      if (bad) return out;
+      if (st->lhs->kind == Expr::Ref && !accum_term(*st)) written.insert(st->lhs->s);
+    }
+    const std::map<std::string, EP> defs = int_defs(L, p);
+    for (auto& a : p.atomic_arrays) {
+      if (int_arrays_.count(a)) continue;
+      Gather g;
+      g.array = a;
+      bool ok = true;
+      for (auto& st : L.body) {
+        if (st->lhs->kind != Expr::Ref || st->lhs->s != a) continue;
+        EP term = accum_term(*st);
+        Inverse inv;
+        if (!term || st->lhs->a.size() != 1 ||
+            !inverse_of(subst(st->lhs->a[0], defs), L.var, inv)) {
+          ok = false;
+          break;
+        }
+        if (inv.kind == Inverse::PERIODIC2) {   // the loop covers the whole grid
+          const EP& lo = stepv == 1 ? L.lo : L.hi;
+          const EP& hi = stepv == 1 ? L.hi : L.lo;
+          long one;
+          const std::string cn = canon(inv.n, {});
+          if (!is_lit(lo, &one) || one != 1 || canon(hi, {}) != "*(" + cn + "," + cn + ",)") {
+            ok = false;
+            break;
+          }
+        }
+        g.parts.push_back({st.get(), term, inv});
+      }
+      if (ok && !g.parts.empty()) out.push_back(g);
+    }
+    return out;
+  }
+
   LoopPlan plan_loop(Stmt& L) {
     LoopPlan p;
     std::set<std::string> assigned, inner_vars{L.var}, written;
@@ -1196,20 +1417,7 @@ class Emitter {
       return p;
     }
     // private integer definitions used to see through decoded indices
-    std::map<std::string, EP> defs;
-    {
-      std::map<std::string, std::vector<EP>> rhs_of;
-      walk_stmts(L.body, [&](Stmt& x) {
-        if (x.kind == Stmt::Assign && x.lhs->kind == Expr::Var) rhs_of[x.lhs->s].push_back(x.rhs);
-      });
-      for (auto& [v, rs] : rhs_of) {
-        if (!p.privates.count(v) || !p.privates[v].empty() || !ints_.count(v)) continue;
-        bool same = true;
-        for (auto& r : rs)
-          if (text(r) != text(rs[0]) || reads_scalar(r, v)) same = false;
-        if (same) defs[v] = rs[0];
-      }
-    }
+    std::map<std::string, EP> defs = int_defs(L, p);
     // arrays
     std::map<std::string, std::vector<Site>> sites;
     walk_stmts(L.body, [&](Stmt& s) {
@@ -1340,6 +1548,52 @@ class Emitter {
           LoopPlan p = plan_loop(*s);
           if (p.parallel) {
             flush();
+            std::vector<Gather> gs = gather_ ? plan_gather(*s, p) : std::vector<Gather>{};
+            SP rest;
+            LoopPlan prest;
+            if (!gs.empty()) {
+              // the loop without the gathered accumulations
+              rest = std::make_shared<Stmt>(*s);
+              rest->body.clear();
+              for (auto& st : s->body) {
+                bool part = false;
+                for (auto& g : gs)
+                  for (auto& q : g.parts) part = part || q.st == st.get();
+                if (!part) rest->body.push_back(st);
+              }
+              prest = plan_loop(*rest);
+              if (!prest.parallel) gs.clear();
+            }
+            if (!gs.empty()) {
+              Unit ug;
+              ug.par = ug.gather = true;
+              ug.gathers = gs;
+              ug.stmts = {s};
+              ug.plan = p;
+              ug.id = (int)units_.size();
+              units_.push_back(ug);
+              Item ig;
+              ig.kind = Item::Kernel;
+              ig.unit = ug.id;
+              items.push_back(ig);
+              std::vector<std::string> names;
+              for (auto& g : gs) names.push_back(g.array);
+              decisions_.push_back(json_decision(*s, "gather", "", {}, {}, {}, names));
+              if (!rest->body.empty()) {
+                Unit u;
+                u.par = true;
+                u.stmts = {rest};
+                u.plan = prest;
+                u.id = (int)units_.size();
+                units_.push_back(u);
+                Item it;
+                it.kind = Item::Kernel;
+                it.unit = u.id;
+                items.push_back(it);
+                record_par(*rest, prest);
+              }
+              break;
+            }
             Unit u;
             u.par = true;
             u.stmts = {s};
@@ -1443,13 +1697,14 @@ class Emitter {
   std::string json_decision(Stmt& s, const std::string& mode, const std::string& why,
                             const std::vector<std::string>& priv,
                             const std::vector<std::string>& red,
-                            const std::vector<std::string>& atom) {
+                            const std::vector<std::string>& atom,
+                            const std::vector<std::string>& gathered = {}) {
     std::string loop = "for " + s.var + " = " + text(s.lo) + ":" +
                        (s.step ? text(s.step) + ":" : "") + text(s.hi);
     return "{\"line\": " + std::to_string(s.line) + ", \"loop\": " + jstr(loop) +
            ", \"mode\": " + jstr(mode) + ", \"why\": " + jstr(why) +
            ", \"private\": " + jlist(priv) + ", \"reductions\": " + jlist(red) +
-           ", \"atomics\": " + jlist(atom) + "}";
+           ", \"atomics\": " + jlist(atom) + ", \"gathered\": " + jlist(gathered) + "}";
   }
 
   // ---- storage -----------------------------------------------------------------
@@ -1658,6 +1913,11 @@ class Emitter {
       case Stmt::Assign: {
         if (s.lhs->kind == Expr::Var) {
           const std::string& v = s.lhs->s;
+          if (red_sites_.count(&s)) {
+            o << pad << red_sites_[&s] << " += (" << T_ << ")" << cx(accum_term(s), locals, s.line)
+              << ";\n";
+            return;
+          }
           if (u.par && u.plan.reductions.count(v)) {
             EP term = accum_term(s);
             o << pad << "jl_atomic_add(&" << scalar_ref(v, {}) << ", (" << T_ << ")"
@@ -1671,6 +1931,11 @@ class Emitter {
           return;
         }
         const std::string& a = s.lhs->s;
+        if (red_sites_.count(&s)) {
+          o << pad << red_sites_[&s] << " += (" << T_ << ")" << cx(accum_term(s), locals, s.line)
+            << ";\n";
+          return;
+        }
         if (u.par && u.plan.atomic_arrays.count(a)) {
           EP term = accum_term(s);
           std::string ty = int_arrays_.count(a) ? "unsigned long long" : T_;
@@ -1754,7 +2019,99 @@ class Emitter {
     return k;
   }
 
+  // v_ = the iteration whose accumulation lands on jt_
+  std::string inverse_src(const Inverse& inv, const std::set<std::string>& locals, int line) {
+    switch (inv.kind) {
+      case Inverse::IDENT:
+        return "v_ = jt_;";
+      case Inverse::OFFSET:
+        return "v_ = jt_ - (" + std::to_string(inv.off) + ");";
+      case Inverse::PERIODIC2: {
+        const std::string n = "(int64_t)(" + cx(inv.n, locals, line) + ")";
+        return "{ const int64_t nn_ = " + n +
+               "; const int64_t r_ = jl_mod(jl_div(jt_ - 1, nn_) - (" + std::to_string(inv.sr) +
+               "), nn_), c_ = jl_mod(jl_mod(jt_ - 1, nn_) - (" + std::to_string(inv.sc) +
+               "), nn_); v_ = r_ * nn_ + c_ + 1; }";
+      }
+    }
+    return "v_ = jt_;";
+  }
+  static std::string inv_key(const Inverse& v) {
+    return std::to_string((int)v.kind) + ":" + std::to_string(v.off) + ":" +
+           std::to_string(v.sr) + ":" + std::to_string(v.sc);
+  }
+
+  std::string gather_src(const Unit& u) {
+    std::ostringstream o;
+    KArgs k = kernel_args(u);
+    Stmt& L = *u.stmts[0];
+    o << "// " << text_loop(L) << "  (line " << L.line
+      << "): gather, a thread per target element replays the iterations that land on it\n";
+    o << "__global__ void stade_k" << u.id << "(int64_t jlo_, int64_t n_, int64_t vlo_, int64_t vhi_";
+    for (auto& d : k.decl) o << ", " << d;
+    o << ") {\n";
+    o << "  const int64_t tid_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;\n";
+    o << "  if (tid_ >= n_) return;\n";
+    o << "  const int64_t jt_ = jlo_ + tid_;\n";
+    std::set<std::string> base;
+    for (auto& sc : u.scalars) {
+      if (u.plan.privates.count(sc) || u.plan.reductions.count(sc) || sc == L.var) continue;
+      auto it = store_.find(sc);
+      if (it == store_.end()) fail(L.line, "scalar " + sc + " is read but never set");
+      if (it->second == S_FBOX || it->second == S_IBOX) {
+        o << "  const " << ctype(sc) << " " << cname(sc) << " = " << scalar_ref(sc, {}) << ";\n";
+        base.insert(sc);
+      }
+    }
+    for (auto& g : u.gathers) {
+      o << "  {\n    " << T_ << " acc_ = p_" << g.array << "[jt_ - 1];\n    bool any_ = false;\n";
+      // parts grouped by inverse, each group one replay of the body up to its last part
+      std::vector<std::string> keys;
+      for (auto& q : g.parts)
+        if (std::find(keys.begin(), keys.end(), inv_key(q.inv)) == keys.end())
+          keys.push_back(inv_key(q.inv));
+      for (auto& key : keys) {
+        const GatherPart* first = nullptr;
+        std::set<const Stmt*> mine;
+        for (auto& q : g.parts)
+          if (inv_key(q.inv) == key) {
+            if (!first) first = &q;
+            mine.insert(q.st);
+          }
+        std::set<std::string> locals = base;
+        locals.insert(L.var);
+        o << "    {\n      int64_t v_;\n      " << inverse_src(first->inv, locals, L.line) << "\n";
+        o << "      if (v_ >= vlo_ && v_ <= vhi_) {\n        any_ = true;\n";
+        o << "        const int64_t " << cname(L.var) << " = v_;\n";
+        for (auto& [v, init] : u.plan.privates) {
+          const std::string iv = init.empty() ? "0" : (ints_.count(v) ? init : flit(init));
+          o << "        " << ctype(v) << " " << cname(v) << " = " << cast_to(v, iv) << ";\n";
+          locals.insert(v);
+        }
+        size_t left = mine.size();
+        for (auto& st : L.body) {
+          if (!left) break;
+          if (mine.count(st.get())) {
+            const GatherPart* q = nullptr;
+            for (auto& x : g.parts)
+              if (x.st == st.get()) q = &x;
+            o << "        acc_ += (" << T_ << ")" << cx(q->term, locals, st->line) << ";\n";
+            --left;
+          } else if (st->lhs->kind == Expr::Var && u.plan.privates.count(st->lhs->s)) {
+            o << "        " << cname(st->lhs->s) << " = "
+              << cast_to(st->lhs->s, cx(st->rhs, locals, st->line)) << ";\n";
+          }
+        }
+        o << "      }\n    }\n";
+      }
+      o << "    if (any_) p_" << g.array << "[jt_ - 1] = acc_;\n  }\n";
+    }
+    o << "}\n";
+    return o.str();
+  }
+
   std::string kernel_src(const Unit& u) {
+    if (u.gather) return gather_src(u);
     std::ostringstream o;
     KArgs k = kernel_args(u);
     std::string name = "stade_k" + std::to_string(u.id);
@@ -1764,9 +2121,49 @@ class Emitter {
       o << "__global__ void " << name << "(int64_t lo_, int64_t st_, int64_t n_";
       for (auto& d : k.decl) o << ", " << d;
       o << ") {\n";
+      // accumulations into one loop-invariant target from one site: a block
+      // sum and one atomic per block (the generated loss and scalar-adjoint sums)
+      std::vector<std::pair<std::string, std::string>> blk;   // register, target
+      red_sites_.clear();
+      {
+        std::set<std::string> varying{L.var}, written;
+        walk_stmts(L.body, [&](Stmt& x) {
+          if (x.kind == Stmt::Assign && x.lhs->kind == Expr::Var) varying.insert(x.lhs->s);
+          if (x.kind == Stmt::Assign && x.lhs->kind == Expr::Ref) written.insert(x.lhs->s);
+          if (x.kind == Stmt::For) varying.insert(x.var);
+        });
+        std::map<std::string, std::vector<Stmt*>> sites;
+        walk_stmts(L.body, [&](Stmt& x) {
+          if (x.kind != Stmt::Assign || !accum_term(x)) return;
+          const std::string& nm = x.lhs->s;
+          if (x.lhs->kind == Expr::Var ? u.plan.reductions.count(nm) > 0
+                                       : u.plan.atomic_arrays.count(nm) > 0)
+            sites[nm].push_back(&x);
+          else if (x.lhs->kind == Expr::Ref && u.plan.atomic_arrays.count(nm))
+            sites[nm].push_back(&x);
+        });
+        for (auto& [nm, ss] : sites) {
+          if (ss.size() != 1) continue;
+          Stmt* x = ss[0];
+          if (x->lhs->kind == Expr::Ref) {
+            if (int_arrays_.count(nm)) continue;
+            bool inv = true;
+            for (auto& i : x->lhs->a)
+              if (classify(i, L.var, varying, written, {}, 0).k != Cls::INV) inv = false;
+            if (!inv) continue;
+          }
+          const std::string reg = "red" + std::to_string(blk.size()) + "_";
+          red_sites_[x] = reg;
+          blk.push_back({reg, x->lhs->kind == Expr::Var
+                                  ? "&" + scalar_ref(nm, {})
+                                  : "&p_" + nm + "[" + offset(x->lhs, {}, x->line) + "]"});
+        }
+      }
       o << "  const int64_t tid_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;\n";
-      o << "  if (tid_ >= n_) return;\n";
-      o << "  const int64_t " << cname(L.var) << " = lo_ + tid_ * st_;\n";
+      if (blk.empty()) o << "  if (tid_ >= n_) return;\n";
+      o << "  const int64_t " << cname(L.var)
+        << " = lo_ + (STADE_ASC && st_ < 0 ? n_ - 1 - tid_ : tid_) * st_;\n";
+      for (auto& [reg, tgt] : blk) o << "  " << T_ << " " << reg << " = 0;\n";
       std::set<std::string> locals{L.var};
       for (auto& [v, init] : u.plan.privates) {
         std::string iv = init.empty() ? "0" : (ints_.count(v) ? init : flit(init));
@@ -1787,7 +2184,15 @@ class Emitter {
       locals.erase(L.var);
       locals.insert(L.var);
       std::set<std::string> body_locals = locals;
-      stmts(o, L.body, body_locals, u, 2);
+      if (blk.empty()) {
+        stmts(o, L.body, body_locals, u, 2);
+      } else {
+        o << "  if (tid_ < n_) {\n";
+        stmts(o, L.body, body_locals, u, 4);
+        o << "  }\n";
+        for (auto& [reg, tgt] : blk) o << "  jl_block_add(" << tgt << ", " << reg << ");\n";
+      }
+      red_sites_.clear();
       o << "}\n";
     } else {
       o << "// statements at line " << u.stmts[0]->line << ": one thread, in order\n";
@@ -1842,6 +2247,29 @@ class Emitter {
           const Unit& u = units_[it.unit];
           KArgs k = kernel_args(u);
           std::string name = "stade_k" + std::to_string(u.id);
+          if (u.gather) {
+            Stmt& L = *u.stmts[0];
+            long lo_off = 0, hi_off = 0;
+            for (auto& g : u.gathers)
+              for (auto& q : g.parts)
+                if (q.inv.kind == Inverse::OFFSET) {
+                  lo_off = std::min(lo_off, q.inv.off);
+                  hi_off = std::max(hi_off, q.inv.off);
+                }
+            o << pad << "{\n" << pad << "  const int64_t a_ = " << cx(L.lo, {}, L.line)
+              << ", b_ = " << cx(L.hi, {}, L.line) << ";\n";
+            o << pad << "  const int64_t vlo_ = a_ < b_ ? a_ : b_, vhi_ = a_ < b_ ? b_ : a_;\n";
+            o << pad << "  const int64_t jlo_ = vlo_ + (" << lo_off << "), jhi_ = vhi_ + (" << hi_off
+              << ");\n";
+            o << pad << "  if (jhi_ >= jlo_ && jl_trip(a_, " << (L.step ? cx(L.step, {}, L.line) : "((int64_t)1)")
+              << ", b_) > 0) {\n";
+            o << pad << "    const int64_t n_ = jhi_ - jlo_ + 1;\n";
+            o << pad << "    STADE_LAUNCH(" << name
+              << ", (unsigned)((n_ + 255) / 256), 256, s_, jlo_, n_, vlo_, vhi_";
+            for (auto& p : k.pass) o << ", " << p;
+            o << ");\n" << pad << "    STADE_GEN_CHECK();\n" << pad << "  }\n" << pad << "}\n";
+            break;
+          }
           if (u.par) {
             Stmt& L = *u.stmts[0];
             o << pad << "{\n" << pad << "  const int64_t lo_ = " << cx(L.lo, {}, L.line)
@@ -2073,6 +2501,26 @@ __device__ __forceinline__ void jl_atomic_add(T* p, T v) {
 #endif
 #ifdef STADE_EMIT_HOST
 template <class T> static inline void jl_atomic_add(T* p, T v) { *p = (T)(*p + v); }
+template <class T> static inline void jl_block_add(T* p, T v) { *p = (T)(*p + v); }
+#define STADE_ASC 0
+#else
+// Sum over the block, then one atomic add: every thread of the block calls it.
+template <class T>
+__device__ __forceinline__ void jl_block_add(T* p, T v) {
+  __shared__ T part_[32];
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) part_[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    T t = l < (int)(blockDim.x >> 5) ? part_[l] : (T)0;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (l == 0) atomicAdd(p, t);
+  }
+}
+// threads of a reversed parallel loop take its iterations in ascending address order
+#define STADE_ASC 1
 #endif
 #ifdef STADE_EMIT_HOST
 #define JL_HD static inline

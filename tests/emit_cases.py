@@ -93,6 +93,16 @@ def window(size, r):
     return a
 
 
+def smooth(size, r):
+    (n,) = size
+    a = OrderedDict()
+    a["loss"], a["lossb"] = np.full(1, 0.0), np.full(1, 0.75)
+    a["u"], a["ub"] = _n(r, n), _n(r, n, 0.1)
+    a["v"], a["vb"] = _n(r, n), _n(r, n, 0.1)
+    a["i_n"] = n
+    return a
+
+
 def halving(size, r):
     (n,) = size
     a = OrderedDict()
@@ -117,6 +127,7 @@ CASES = {
     "window_b": ("window_b.jl", window, None, ("i_n", "i_k"),
                  [(40, 5), (1, 1), (0, 3), (5000, 17)]),
     "halving_b": ("halving_b.jl", halving, None, None, [(16,), (13,), (1,), (4096,)]),
+    "smooth_b": ("smooth_b.jl", smooth, None, ("i_n",), [(12,), (3,), (2,), (100000,)]),
 }
 
 
