@@ -732,8 +732,28 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
                    double* __restrict__ pd, double* __restrict__ pbd,
                    double* __restrict__ gbuf, double* __restrict__ gdbuf,
                    double* __restrict__ s1b, double* __restrict__ s1bd, int n_s, int n_h, int n_o,
-                   double* __restrict__ loss_part, double* __restrict__ lossd_part) {
+                   double* __restrict__ loss_part, double* __restrict__ lossd_part, int w2_smem) {
   __shared__ double red[2][kHeadWarps];
+  // w2 and w2d staged class-major with an odd row stride: the class lanes of
+  // the logits loop and the hidden-unit lanes of the s1b loop both read
+  // distinct banks (read from global memory instead, [k][c], when they do
+  // not fit)
+  extern __shared__ double w2sm[];
+  const int LD = n_h + 1;
+  if (w2_smem) {
+    for (int e = threadIdx.x; e < n_o * n_h; e += blockDim.x) {
+      const int cc = e / n_h, k = e % n_h;
+      w2sm[cc * LD + k] = w2[(int64_t)k * n_o + cc];
+      w2sm[n_o * LD + cc * LD + k] = w2d[(int64_t)k * n_o + cc];
+    }
+    __syncthreads();
+  }
+  auto W = [&](int k, int cc) {
+    return w2_smem ? w2sm[cc * LD + k] : w2[(int64_t)k * n_o + cc];
+  };
+  auto WD = [&](int k, int cc) {
+    return w2_smem ? w2sm[n_o * LD + cc * LD + k] : w2d[(int64_t)k * n_o + cc];
+  };
   const unsigned F = 0xffffffffu;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool cl = lane < n_o;          // this lane owns class `lane`
@@ -746,10 +766,11 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
     const int64_t row = (int64_t)s * n_o;
     // logits and tangents, hidden units in order (the primal's sequential sum)
     double zv = b2[c], zdv = b2d[c];
+#pragma unroll 8
     for (int k = 0; k < n_h; ++k) {
       const double hv = hr[k], hdv = hdr[k];
-      const double wv = w2[(int64_t)k * n_o + c];
-      zdv = zdv + (hv * w2d[(int64_t)k * n_o + c] + wv * hdv);
+      const double wv = W(k, c);
+      zdv = zdv + (hv * WD(k, c) + wv * hdv);
       zv = zv + wv * hv;
     }
     // running max over classes with its tangent
@@ -847,8 +868,8 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
         for (int j = 0; j < 8; ++j) {
           const int k = k0 + 32 * j + lane;
           if (k < n_h) {
-            const double wv = w2[(int64_t)k * n_o + cc];
-            accd[j] = accd[j] + (gc * w2d[(int64_t)k * n_o + cc] + wv * gdc);
+            const double wv = W(k, cc);
+            accd[j] = accd[j] + (gc * WD(k, cc) + wv * gdc);
             acc[j] = acc[j] + wv * gc;
           }
         }
@@ -891,11 +912,16 @@ mlp_w2b_hv_partial_kernel(const double* __restrict__ h, const double* __restrict
   const int s1 = min(n_s, s0 + chunk);
   const int64_t nw = (int64_t)n_h * n_o;
   double* my = part + (int64_t)blockIdx.x * (2 * nw + 2 * n_o);
-  for (int k = threadIdx.x; k < n_h; k += blockDim.x) {
-    double acc[NO], accd[NO];
+  // block (chunk, 32 hidden units); a warp holds 4 units x 8 sample lanes,
+  // the sample lanes summed by shuffles in a fixed order
+  const int lane = threadIdx.x & 31, sl = lane & 7;
+  const int k = blockIdx.y * 32 + (threadIdx.x >> 5) * 4 + (lane >> 3);
+  double acc[NO], accd[NO];
 #pragma unroll
-    for (int c = 0; c < NO; ++c) { acc[c] = 0.0; accd[c] = 0.0; }
-    for (int s = s0; s < s1; ++s) {
+  for (int c = 0; c < NO; ++c) { acc[c] = 0.0; accd[c] = 0.0; }
+  if (k < n_h) {
+#pragma unroll 4
+    for (int s = s0 + sl; s < s1; s += 8) {
       const double hv = h[(int64_t)s * n_h + k], hdv = hd[(int64_t)s * n_h + k];
       const double* gr = gbuf + (int64_t)s * n_o;
       const double* gdr = gdbuf + (int64_t)s * n_o;
@@ -907,6 +933,18 @@ mlp_w2b_hv_partial_kernel(const double* __restrict__ h, const double* __restrict
         }
       }
     }
+  }
+#pragma unroll
+  for (int c = 0; c < NO; ++c) {
+    if (c < n_o) {
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], o);
+        accd[c] += __shfl_xor_sync(0xffffffffu, accd[c], o);
+      }
+    }
+  }
+  if (k < n_h && sl == 0) {
 #pragma unroll
     for (int c = 0; c < NO; ++c) {
       if (c < n_o) {
@@ -915,12 +953,12 @@ mlp_w2b_hv_partial_kernel(const double* __restrict__ h, const double* __restrict
       }
     }
   }
-  if (threadIdx.x < 2 * n_o) {
+  if (blockIdx.y == 0 && threadIdx.x < 2 * n_o) {
     const int c = threadIdx.x % n_o;
     const double* src = threadIdx.x < n_o ? gbuf : gdbuf;
-    double acc = 0.0;
-    for (int s = s0; s < s1; ++s) acc += src[(int64_t)s * n_o + c];
-    my[2 * nw + threadIdx.x] = acc;
+    double a = 0.0;
+    for (int s = s0; s < s1; ++s) a += src[(int64_t)s * n_o + c];
+    my[2 * nw + threadIdx.x] = a;
   }
 }
 
@@ -1362,21 +1400,29 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   if (st != STADE_OK) return st;
   // head
   PhaseScope ph_head("hv_head", s);
-  mlp_head_hv_kernel<<<w.head_blocks, kHeadWarps * 32, 0, s>>>(
+  const size_t hsm = sizeof(double) * 2 * (size_t)O * (size_t)(H + 1);
+  const int w2_smem = hsm <= 160 * 1024;
+  if (w2_smem && hsm > 48 * 1024)
+    STADE_CUDA(cudaFuncSetAttribute(mlp_head_hv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)hsm));
+  // with w2 in shared memory, one wave of blocks (each stages w2 once)
+  const int hgrid = w2_smem ? std::min(w.head_blocks, 2 * tc5::sm_count()) : w.head_blocks;
+  mlp_head_hv_kernel<<<hgrid, kHeadWarps * 32, w2_smem ? hsm : 0, s>>>(
       lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
-      pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part);
+      pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part, w2_smem);
   STADE_CHECK_LAUNCH();
-  st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
+  st = launch_sum_to_scalar(w.loss_part, hgrid, loss, true, s);
   if (st != STADE_OK) return st;
-  st = launch_sum_to_scalar(w.lossd_part, w.head_blocks, lossd, true, s);
+  st = launch_sum_to_scalar(w.lossd_part, hgrid, lossd, true, s);
   if (st != STADE_OK) return st;
   // W2b, W2bd, b2b, b2bd
+  const dim3 w2g(w.w2_chunks, (H + 31) / 32);
   if (O <= 16)
-    mlp_w2b_hv_partial_kernel<16><<<w.w2_chunks, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O,
-                                                              kW2Chunk, w.w2_part);
+    mlp_w2b_hv_partial_kernel<16><<<w2g, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O, kW2Chunk,
+                                                      w.w2_part);
   else
-    mlp_w2b_hv_partial_kernel<32><<<w.w2_chunks, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O,
-                                                              kW2Chunk, w.w2_part);
+    mlp_w2b_hv_partial_kernel<32><<<w2g, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O, kW2Chunk,
+                                                      w.w2_part);
   STADE_CHECK_LAUNCH();
   finish_four_kernel<<<ceil_div_u(2 * n_h * n_o + 2 * n_o, 256), 256, 0, s>>>(
       w.w2_part, w.w2_chunks, n_h * n_o, O, w2b, w2bd, b2b, b2bd);
