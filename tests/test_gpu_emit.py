@@ -87,3 +87,28 @@ def test_emitted_c1_matches_hand_written_sweep():
     for a, b in zip(d1, d2):
         if isinstance(a, torch.Tensor):
             assert rel_err(a.cpu().numpy(), b.cpu().numpy()) <= 1e-12
+
+
+@pytest.mark.parametrize("name", ["affine_ls_b", "window_b", "smooth_b"])
+def test_emitted_float32_on_gpu(name):
+    """The Float32 build (cgen_convert_precision) against the interpreter in
+    Float32, 1e-5 normwise (the north star's Float32 bound)."""
+    sw = emit.load(ec.source(name), precision=32, dims=ec.CASES[name][2])
+    args = ec.make(name, ec.CASES[name][4][0], "f32")
+    for k, v in args.items():
+        if isinstance(v, np.ndarray) and v.dtype == np.float64:
+            args[k] = v.astype(np.float32)
+    ref = ec.copy_args(args)
+    I = jlsub.Interp(ec.source(name), 32, ec.CASES[name][2])
+    stacks = ()
+    if f"initstacks_{name}" in I.funcs:
+        stacks = I.initstacks(f"initstacks_{name}", *ec.stack_ints(name, ref))
+    I.call(name, *ref.values(), *stacks)
+    dev = _dev(args)
+    sw(*dev, *sw.initstacks(*ec.stack_ints(name, args)))
+    torch.cuda.synchronize()
+    for (k, v), d in zip(args.items(), dev):
+        if isinstance(v, np.ndarray):
+            got = d.cpu().numpy()
+            assert got.dtype == np.float32
+            assert rel_err(got, ref[k]) <= 1e-5, (name, k, rel_err(got, ref[k]))
