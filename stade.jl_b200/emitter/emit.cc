@@ -1767,6 +1767,7 @@ class Emitter {
 
   // ---- C++ expression printing -------------------------------------------------
   std::string cname(const std::string& v) { return "j_" + v; }
+  size_t fstride() const { return f32_ ? 32 : 16; }   // elements per 128-byte line
 
   std::string scalar_ref(const std::string& v, const std::set<std::string>& locals) {
     if (locals.count(v)) return cname(v);
@@ -1777,9 +1778,9 @@ class Emitter {
       case S_LOCAL:
         return cname(v);
       case S_FBOX:
-        return "g_fbox[" + std::to_string(fslot_.at(v)) + "]";
+        return "g_fbox[" + std::to_string(fslot_.at(v) * fstride()) + "]";
       case S_IBOX:
-        return "g_ibox[" + std::to_string(islot_.at(v)) + "]";
+        return "g_ibox[" + std::to_string(islot_.at(v) * 16) + "]";
     }
     return cname(v);
   }
@@ -2359,8 +2360,11 @@ class Emitter {
       << "// Loop decisions are listed in the manifest.\n";
     o << prelude();
     o << "namespace {\n";
-    o << "__device__ " << T_ << " g_fbox[" << std::max<size_t>(1, fslot_.size()) << "];\n";
-    o << "__device__ int64_t g_ibox[" << std::max<size_t>(1, islot_.size()) << "];\n";
+    // one 128-byte line per boxed scalar: a scalar every thread reads (alpha)
+    // must not share a line with one the blocks add into (alphab)
+    o << "__device__ " << T_ << " g_fbox[" << std::max<size_t>(1, fslot_.size()) * fstride()
+      << "];\n";
+    o << "__device__ int64_t g_ibox[" << std::max<size_t>(1, islot_.size()) * 16 << "];\n";
     // box initialisation kernel: the float scalar arguments
     std::vector<std::string> fparams;
     for (auto& p : f_.params)
@@ -2370,7 +2374,7 @@ class Emitter {
     if (fparams.empty()) o << "int unused_";
     o << ") {\n";
     for (size_t i = 0; i < fparams.size(); ++i)
-      o << "  g_fbox[" << fslot_.at(fparams[i]) << "] = v" << i << ";\n";
+      o << "  g_fbox[" << fslot_.at(fparams[i]) * fstride() << "] = v" << i << ";\n";
     if (fparams.empty()) o << "  (void)unused_;\n";
     o << "}\n";
     for (auto& u : units_) o << kernel_src(u);
@@ -2411,9 +2415,10 @@ class Emitter {
     o << ");\n  STADE_GEN_CHECK();\n";
     host_items(o, items_, 2);
     if (!returned_.empty()) {
-      o << "  " << T_ << " box_[" << fslot_.size() << "];\n";
+      o << "  " << T_ << " box_[" << fslot_.size() * fstride() << "];\n";
       o << "  if (stade_box_read(box_, g_fbox, sizeof(box_), s_) != 0) return 3;\n";
-      for (auto& r : returned_) o << "  *h_" << r << " = box_[" << fslot_.at(r) << "];\n";
+      for (auto& r : returned_)
+        o << "  *h_" << r << " = box_[" << fslot_.at(r) * fstride() << "];\n";
     }
     o << "  return 0;\n}\n\n";
     o << "extern \"C\" int64_t stade_" << f_.name << "_launches(void) { return stade_launches_; }\n\n";
