@@ -27,7 +27,9 @@
 //     allowscalar).
 // Scalars live in registers when one kernel uses them, else in a device box
 // (`g_fbox` / `g_ibox`); integer scalars computed on the host from the integer
-// arguments are kernel arguments. No host synchronisation happens before the
+// arguments, and float arguments the sweep never assigns, are kernel
+// arguments. A parallel loop holding block sums strides over its iterations
+// with the grid the device holds at once. No host synchronisation happens before the
 // end, where returned scalar adjoints are copied back.
 //
 // Index injectivity: an index is injective in the thread variable v when one
@@ -611,7 +613,7 @@ struct LoopPlan {
   std::set<std::string> atomic_arrays;
 };
 
-enum Storage { S_HOSTINT, S_LOCAL, S_FBOX, S_IBOX };
+enum Storage { S_HOSTINT, S_LOCAL, S_FBOX, S_IBOX, S_FPARAM };
 
 // The iteration v whose accumulation lands on target index j, for one
 // accumulation statement (the scatter -> gather rewrite, as cgen_gather_loop
@@ -691,6 +693,7 @@ class Emitter {
   std::map<std::string, std::string> stack_type_;  // name -> "f" / "i"
   std::vector<std::string> decisions_;
   std::map<const Stmt*, std::string> red_sites_;   // accumulation -> block sum register
+  std::set<int> blk_units_;                         // units whose kernel has block sums
 
   // ---- kinds: array / scalar, integer / float (the evidence shape_infer uses,
   // src/STADE.jl:936-958: loop variables, range bounds, div / mod arguments,
@@ -1743,9 +1746,16 @@ class Emitter {
       unit_refs(u);
       for (auto& s : u.scalars) ++n_units[s];
     }
+    // float arguments the sweep never assigns (alpha) go to the kernels by value
+    std::set<std::string> assigned;
+    walk_stmts(f_.body, [&](Stmt& s) {
+      if (s.kind == Stmt::Assign && s.lhs->kind == Expr::Var) assigned.insert(s.lhs->s);
+      if (s.kind == Stmt::For) assigned.insert(s.var);
+    });
     for (auto& p : f_.params) {
       if (arrays_.count(p)) continue;
       if (ints_.count(p)) store_[p] = S_HOSTINT;
+      else if (!assigned.count(p) && !returned_.count(p)) store_[p] = S_FPARAM;
       else store_[p] = S_FBOX;
     }
     for (auto& h : host_ints_) store_[h] = S_HOSTINT;
@@ -1767,6 +1777,11 @@ class Emitter {
 
   // ---- C++ expression printing -------------------------------------------------
   std::string cname(const std::string& v) { return "j_" + v; }
+  std::set<std::string> fd_avail_;   // divisors with a jl_fd argument in the kernel being printed
+  std::string fast_divisor(const EP& d, const std::set<std::string>& locals) {
+    if (!d || d->kind != Expr::Var || locals.count(d->s) || !fd_avail_.count(d->s)) return "";
+    return "fd_" + d->s;
+  }
   size_t fstride() const { return f32_ ? 32 : 16; }   // elements per 128-byte line
 
   std::string scalar_ref(const std::string& v, const std::set<std::string>& locals) {
@@ -1776,6 +1791,7 @@ class Emitter {
     switch (it->second) {
       case S_HOSTINT:
       case S_LOCAL:
+      case S_FPARAM:
         return cname(v);
       case S_FBOX:
         return "g_fbox[" + std::to_string(fslot_.at(v) * fstride()) + "]";
@@ -1824,8 +1840,11 @@ class Emitter {
         const std::string& op = e->s;
         std::string l = cx(e->a[0], locals, line), r = cx(e->a[1], locals, line);
         if (op == "/") return "((" + T_ + ")" + l + " / (" + T_ + ")" + r + ")";
-        if (op == "÷") return "jl_div(" + l + ", " + r + ")";
-        if (op == "%") return is_int_expr(e) ? "jl_rem(" + l + ", " + r + ")" : "fmod(" + l + ", " + r + ")";
+        const std::string fd = fast_divisor(e->a[1], locals);
+        if (op == "÷") return fd.empty() ? "jl_div(" + l + ", " + r + ")" : "jl_divf(" + l + ", " + r + ", " + fd + ")";
+        if (op == "%" && is_int_expr(e))
+          return fd.empty() ? "jl_rem(" + l + ", " + r + ")" : "jl_remf(" + l + ", " + r + ", " + fd + ")";
+        if (op == "%") return "fmod(" + l + ", " + r + ")";
         if (op == "^") {
           const EP& x = e->a[1];
           bool ib = is_int_expr(e->a[0]);
@@ -1854,6 +1873,9 @@ class Emitter {
           need(2);
           if (!is_int_expr(e->a[0]) || !is_int_expr(e->a[1]))
             fail(line, n + " of a float is not supported");
+          const std::string fd = fast_divisor(e->a[1], locals);
+          if (!fd.empty() && (n == "div" || n == "mod" || n == "rem"))
+            return "jl_" + n + "f(" + a[0] + ", " + a[1] + ", " + fd + ")";
           return "jl_" + n + "(" + a[0] + ", " + a[1] + ")";
         }
         if (n == "max" || n == "min") {
@@ -1913,11 +1935,18 @@ class Emitter {
   // stores (the arrays are distinct __restrict__ arguments). Measured on a
   // tape-restore loop (u = tape; ub read then zeroed; unb += ...): 745 us in
   // statement order, 120 us with the stores deferred.
+  // A store whose value does not come from the load of the same address
+  // (the generated `__oldb = xb[i]; xb[i] = 0.0`) still issues at once and,
+  // with that load in flight, held a stencil adjoint loop at 2980 us instead
+  // of 650 us: its value is given a dependence on the loaded register
+  // (jl_after with the kernel argument z_, which is 0), so it issues after the
+  // load returns and stores the same bits.
   struct Pending {
     std::string array, off, val;
   };
   std::vector<Pending>* pending_ = nullptr;
   int pending_n_ = 0;
+  std::map<std::string, std::string> loaded_;   // "A[offset]" -> register loaded from it
 
   void flush_pending(std::ostringstream& o, const std::string& pad, const std::set<std::string>& arrays,
                      bool all) {
@@ -1954,12 +1983,24 @@ class Emitter {
         const std::string& a = s.lhs->s;
         const std::string n = std::to_string(pending_n_++);
         const std::string ty = int_arrays_.count(a) ? "int64_t" : T_;
-        o << pad << "const int64_t so" << n << "_ = " << offset(s.lhs, locals, s.line) << ";\n";
-        o << pad << "const " << ty << " sv" << n << "_ = (" << ty << ")" << cx(s.rhs, locals, s.line)
-          << ";\n";
+        const std::string off = offset(s.lhs, locals, s.line);
+        std::string val = "(" + ty + ")" + cx(s.rhs, locals, s.line);
+        auto ld = loaded_.find(a + "[" + off + "]");
+        if (ld != loaded_.end() && reads.empty()) {
+          bool uses = false;
+          walk_expr(s.rhs, [&](const EP& y) {
+            if (y->kind == Expr::Var && cname(y->s) == ld->second) uses = true;
+          });
+          if (!uses) val = "jl_after(" + val + ", jl_bits(" + ld->second + ") & z_)";
+        }
+        o << pad << "const int64_t so" << n << "_ = " << off << ";\n";
+        o << pad << "const " << ty << " sv" << n << "_ = " << val << ";\n";
         pending_->push_back({a, "so" + n + "_", "sv" + n + "_"});
         return;
       }
+      if (s.lhs->kind == Expr::Var && s.rhs->kind == Expr::Ref && locals.count(s.lhs->s) &&
+          arrays_.count(s.rhs->s))
+        loaded_[s.rhs->s + "[" + offset(s.rhs, locals, s.line) + "]"] = cname(s.lhs->s);
     }
     switch (s.kind) {
       case Stmt::Assign: {
@@ -2067,8 +2108,43 @@ class Emitter {
         k.decl.push_back("int64_t " + cname(s));
         k.pass.push_back(cname(s));
       }
+      if (it != store_.end() && it->second == S_FPARAM) {
+        k.decl.push_back(T_ + " " + cname(s));
+        k.pass.push_back(cname(s));
+      }
+    }
+    for (auto& d : divisors(u)) {
+      k.decl.push_back("jl_fd fd_" + d);
+      k.pass.push_back("jl_fd_make(" + cname(d) + ")");
     }
     return k;
+  }
+
+  // host-integer scalars a unit divides by (div / mod / rem, ÷, %, and the
+  // periodic inverses of its gathers)
+  std::set<std::string> divisors(const Unit& u) {
+    std::set<std::string> d;
+    auto host_int = [&](const EP& e) {
+      if (!e || e->kind != Expr::Var) return;
+      auto it = store_.find(e->s);
+      if (it != store_.end() && it->second == S_HOSTINT && u.scalars.count(e->s)) d.insert(e->s);
+    };
+    auto visit = [&](const EP& e) {
+      walk_expr(e, [&](const EP& x) {
+        if (x->kind == Expr::Call && (x->s == "div" || x->s == "mod" || x->s == "rem") &&
+            x->a.size() == 2)
+          host_int(x->a[1]);
+        if (x->kind == Expr::Bin && (x->s == "÷" || x->s == "%") && is_int_expr(x)) host_int(x->a[1]);
+      });
+    };
+    walk_stmts(u.stmts, [&](Stmt& s) {
+      for (const EP* e : {&s.lhs, &s.rhs, &s.cond, &s.lo, &s.hi, &s.step, &s.ret})
+        if (*e) visit(*e);
+    });
+    for (auto& g : u.gathers)
+      for (auto& q : g.parts)
+        if (q.inv.kind == Inverse::PERIODIC2) host_int(q.inv.n);
+    return d;
   }
 
   // v_ = the iteration whose accumulation lands on jt_
@@ -2080,10 +2156,14 @@ class Emitter {
         return "v_ = jt_ - (" + std::to_string(inv.off) + ");";
       case Inverse::PERIODIC2: {
         const std::string n = "(int64_t)(" + cx(inv.n, locals, line) + ")";
-        return "{ const int64_t nn_ = " + n +
-               "; const int64_t r_ = jl_mod(jl_div(jt_ - 1, nn_) - (" + std::to_string(inv.sr) +
-               "), nn_), c_ = jl_mod(jl_mod(jt_ - 1, nn_) - (" + std::to_string(inv.sc) +
-               "), nn_); v_ = r_ * nn_ + c_ + 1; }";
+        const std::string fd = fast_divisor(inv.n, locals);
+        const std::string dv = fd.empty() ? "jl_div(jt_ - 1, nn_)" : "jl_divf(jt_ - 1, nn_, " + fd + ")";
+        const std::string md = fd.empty() ? "jl_mod" : "jl_modf";
+        const std::string fa = fd.empty() ? "" : ", " + fd;
+        return "{ const int64_t nn_ = " + n + "; const int64_t q_ = " + dv +
+               "; const int64_t r_ = " + md + "(q_ - (" + std::to_string(inv.sr) + "), nn_" + fa +
+               "), c_ = " + md + "((jt_ - 1 - q_ * nn_) - (" + std::to_string(inv.sc) + "), nn_" + fa +
+               "); v_ = r_ * nn_ + c_ + 1; }";
       }
     }
     return "v_ = jt_;";
@@ -2163,14 +2243,20 @@ class Emitter {
   }
 
   std::string kernel_src(const Unit& u) {
-    if (u.gather) return gather_src(u);
+    fd_avail_ = divisors(u);
+    std::string r = u.gather ? gather_src(u) : kernel_body_src(u);
+    fd_avail_.clear();
+    return r;
+  }
+
+  std::string kernel_body_src(const Unit& u) {
     std::ostringstream o;
     KArgs k = kernel_args(u);
     std::string name = "stade_k" + std::to_string(u.id);
     if (u.par) {
       Stmt& L = *u.stmts[0];
       o << "// " << text_loop(L) << "  (line " << L.line << "): thread per iteration\n";
-      o << "__global__ void " << name << "(int64_t lo_, int64_t st_, int64_t n_";
+      o << "__global__ void " << name << "(int64_t lo_, int64_t st_, int64_t n_, int64_t z_";
       for (auto& d : k.decl) o << ", " << d;
       o << ") {\n";
       // accumulations into one loop-invariant target from one site: a block
@@ -2211,15 +2297,14 @@ class Emitter {
                                   : "&p_" + nm + "[" + offset(x->lhs, {}, x->line) + "]"});
         }
       }
-      o << "  const int64_t tid_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;\n";
-      if (blk.empty()) o << "  if (tid_ >= n_) return;\n";
-      o << "  const int64_t " << cname(L.var)
-        << " = lo_ + (STADE_ASC && st_ < 0 ? n_ - 1 - tid_ : tid_) * st_;\n";
-      for (auto& [reg, tgt] : blk) o << "  " << T_ << " " << reg << " = 0;\n";
+      // a kernel with block sums strides over the iterations with a grid the
+      // SMs hold at once, so that one atomic per resident block remains
+      const std::string ind = blk.empty() ? "  " : "    ";
+      std::ostringstream pv, rd;
       std::set<std::string> locals{L.var};
       for (auto& [v, init] : u.plan.privates) {
         std::string iv = init.empty() ? "0" : (ints_.count(v) ? init : flit(init));
-        o << "  " << ctype(v) << " " << cname(v) << " = " << cast_to(v, iv) << ";\n";
+        pv << ind << ctype(v) << " " << cname(v) << " = " << cast_to(v, iv) << ";\n";
         locals.insert(v);
       }
       // scalars only read: from their box (or by value), once
@@ -2228,9 +2313,25 @@ class Emitter {
         auto it = store_.find(s);
         if (it == store_.end()) fail(L.line, "scalar " + s + " is read but never set");
         if (it->second == S_FBOX || it->second == S_IBOX) {
-          o << "  const " << ctype(s) << " " << cname(s) << " = " << scalar_ref(s, {}) << ";\n";
+          rd << "  const " << ctype(s) << " " << cname(s) << " = " << scalar_ref(s, {}) << ";\n";
           locals.insert(s);
         }
+      }
+      if (blk.empty()) {
+        o << "  const int64_t tid_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;\n";
+        o << "  if (tid_ >= n_) return;\n";
+        o << "  const int64_t " << cname(L.var)
+          << " = lo_ + (STADE_ASC && st_ < 0 ? n_ - 1 - tid_ : tid_) * st_;\n";
+        o << pv.str() << rd.str();
+      } else {
+        blk_units_.insert(u.id);
+        for (auto& [reg, tgt] : blk) o << "  " << T_ << " " << reg << " = 0;\n";
+        o << rd.str();
+        o << "  for (int64_t tid_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tid_ < n_;\n"
+          << "       tid_ += (int64_t)gridDim.x * blockDim.x) {\n";
+        o << "    const int64_t " << cname(L.var)
+          << " = lo_ + (STADE_ASC && st_ < 0 ? n_ - 1 - tid_ : tid_) * st_;\n";
+        o << pv.str();
       }
       for (auto& v : u.inner_vars) locals.insert(v);
       locals.erase(L.var);
@@ -2241,11 +2342,11 @@ class Emitter {
         if (st->kind != Stmt::Assign) straight = false;
       std::vector<Pending> pend;
       if (straight) pending_ = &pend;
+      loaded_.clear();
       if (blk.empty()) {
         stmts(o, L.body, body_locals, u, 2);
         flush_pending(o, "  ", {}, true);
       } else {
-        o << "  if (tid_ < n_) {\n";
         stmts(o, L.body, body_locals, u, 4);
         flush_pending(o, "    ", {}, true);
         o << "  }\n";
@@ -2337,7 +2438,13 @@ class Emitter {
               << ", st_ = " << (L.step ? cx(L.step, {}, L.line) : "((int64_t)1)") << ";\n";
             o << pad << "  const int64_t n_ = jl_trip(lo_, st_, hi_);\n";
             o << pad << "  if (n_ > 0) {\n";
-            o << pad << "    STADE_LAUNCH(" << name << ", (unsigned)((n_ + 255) / 256), 256, s_, lo_, st_, n_";
+            std::string grid = "(unsigned)((n_ + 255) / 256)";
+            if (blk_units_.count(u.id)) {
+              o << pad << "    static int cap_ = 0;\n" << pad
+                << "    if (cap_ == 0) cap_ = stade_resident_blocks((const void*)" << name << ");\n";
+              grid = "(unsigned)((n_ + 255) / 256 < cap_ ? (n_ + 255) / 256 : cap_)";
+            }
+            o << pad << "    STADE_LAUNCH(" << name << ", " << grid << ", 256, s_, lo_, st_, n_, (int64_t)0";
             for (auto& p : k.pass) o << ", " << p;
             o << ");\n" << pad << "    STADE_GEN_CHECK();\n" << pad << "  }\n" << pad << "}\n";
           } else {
@@ -2368,7 +2475,7 @@ class Emitter {
     // box initialisation kernel: the float scalar arguments
     std::vector<std::string> fparams;
     for (auto& p : f_.params)
-      if (!arrays_.count(p) && !ints_.count(p)) fparams.push_back(p);
+      if (!arrays_.count(p) && store_.at(p) == S_FBOX) fparams.push_back(p);
     o << "__global__ void stade_k_init(";
     for (size_t i = 0; i < fparams.size(); ++i) o << (i ? ", " : "") << T_ << " v" << i;
     if (fparams.empty()) o << "int unused_";
@@ -2520,18 +2627,20 @@ static int64_t stade_launches_ = 0;   // kernels this module has launched
 // Host build of the same program (tests): kernels run as loops over their
 // threads, in thread order; atomics are plain adds.
 struct stade_dim3_ { unsigned x = 0; };
-static stade_dim3_ blockIdx, threadIdx, blockDim;
+static stade_dim3_ blockIdx, threadIdx, blockDim, gridDim;
 #define __global__ static
 #define __device__ static
 #define __restrict__
 typedef void* cudaStream_t;
 template <class T, class U> static T atomicAdd(T* p, U v) { T o = *p; *p = (T)(o + (T)v); return o; }
-#define STADE_LAUNCH(k, nb, nt, s, ...) do { blockDim.x = (nt); ++stade_launches_; \
+#define STADE_LAUNCH(k, nb, nt, s, ...) do { blockDim.x = (nt); gridDim.x = (nb); ++stade_launches_; \
   for (unsigned b_ = 0; b_ < (unsigned)(nb); ++b_) for (unsigned t_ = 0; t_ < (unsigned)(nt); ++t_) { \
     blockIdx.x = b_; threadIdx.x = t_; k(__VA_ARGS__); } } while (0)
 #define STADE_GEN_CHECK() do { } while (0)
 #define STADE_CLEAR_ERROR() do { } while (0)
 static int stade_box_read(void* dst, const void* box, size_t n, cudaStream_t) { memcpy(dst, box, n); return 0; }
+// a thread per iteration, in order, as the sequential loop adds
+static int stade_resident_blocks(const void*) { return 1 << 30; }
 #define JL_FN(name) static inline double jl_##name(double x) { return name(x); } \
                     static inline float jl_##name(float x) { return name##f(x); }
 #else
@@ -2539,6 +2648,18 @@ static int stade_box_read(void* dst, const void* box, size_t n, cudaStream_t) { 
 #define STADE_LAUNCH(k, nb, nt, s, ...) do { k<<<(nb), (nt), 0, (s)>>>(__VA_ARGS__); ++stade_launches_; } while (0)
 #define STADE_GEN_CHECK() do { if (cudaGetLastError() != cudaSuccess) return 2; } while (0)
 #define STADE_CLEAR_ERROR() do { (void)cudaGetLastError(); } while (0)
+// blocks of 256 threads the device holds at once for kernel k (a grid-stride
+// kernel launched with that many blocks makes one pass)
+static int stade_resident_blocks(const void* k) {
+  int d = 0, sms = 0, per = 0;
+  if (cudaGetDevice(&d) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, 256, 0) != cudaSuccess || per < 1) {
+    (void)cudaGetLastError();
+    return 1 << 30;
+  }
+  return sms * per;
+}
 template <class B>
 static int stade_box_read(void* dst, const B& box, size_t n, cudaStream_t s) {
   if (cudaMemcpyFromSymbolAsync(dst, box, n, 0, cudaMemcpyDeviceToHost, s) != cudaSuccess) return 1;
@@ -2566,6 +2687,8 @@ __device__ __forceinline__ void jl_atomic_add(T* p, T v) {
 #ifdef STADE_EMIT_HOST
 template <class T> static inline void jl_atomic_add(T* p, T v) { *p = (T)(*p + v); }
 template <class T> static inline void jl_block_add(T* p, T v) { *p = (T)(*p + v); }
+template <class T> static inline int64_t jl_bits(T) { return 0; }
+template <class T> static inline T jl_after(T v, int64_t) { return v; }
 #define STADE_ASC 0
 #else
 // Sum over the block, then one atomic add: every thread of the block calls it.
@@ -2583,6 +2706,17 @@ __device__ __forceinline__ void jl_block_add(T* p, T v) {
     if (l == 0) atomicAdd(p, t);
   }
 }
+// the bits of a loaded value, and v made to depend on them (d is 0 at run time)
+__device__ __forceinline__ int64_t jl_bits(double x) { return __double_as_longlong(x); }
+__device__ __forceinline__ int64_t jl_bits(float x) { return (int64_t)__float_as_int(x); }
+__device__ __forceinline__ int64_t jl_bits(int64_t x) { return x; }
+__device__ __forceinline__ double jl_after(double v, int64_t d) {
+  return __longlong_as_double(__double_as_longlong(v) | d);
+}
+__device__ __forceinline__ float jl_after(float v, int64_t d) {
+  return __int_as_float(__float_as_int(v) | (int)d);
+}
+__device__ __forceinline__ int64_t jl_after(int64_t v, int64_t d) { return v | d; }
 // threads of a reversed parallel loop take its iterations in ascending address order
 #define STADE_ASC 1
 #endif
@@ -2615,6 +2749,36 @@ JL_HD int64_t jl_mod(int64_t a, int64_t b) {
   return (r != 0 && ((r < 0) != (b < 0))) ? r + b : r;
 }
 JL_HD int64_t jl_mod1(int64_t a, int64_t b) { int64_t r = jl_mod(a, b); return r == 0 ? b : r; }
+// Division by a divisor d fixed for a kernel (a host integer argument): with
+// l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1, the quotient of
+// x < 2^31 is (umulhi(x, m) + x) >> l (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994). m and l are made on
+// the host once per launch; outside jl_small's range the plain division runs.
+struct jl_fd { uint32_t m, l; };
+static inline jl_fd jl_fd_make(int64_t d) {
+  jl_fd f{1u, 0u};
+  if (d < 1 || d > 0x80000000ll) return f;
+  while (((uint64_t)1 << f.l) < (uint64_t)d) ++f.l;
+  f.m = (uint32_t)(((((uint64_t)1 << f.l) - (uint64_t)d) << 32) / (uint64_t)d + 1);
+  return f;
+}
+JL_HD uint32_t jl_fd_q(uint32_t x, jl_fd f) {
+#ifdef __CUDA_ARCH__
+  const uint32_t t = __umulhi(x, f.m);
+#else
+  const uint32_t t = (uint32_t)(((uint64_t)x * f.m) >> 32);
+#endif
+  return (t + x) >> f.l;
+}
+JL_HD int64_t jl_divf(int64_t a, int64_t b, jl_fd f) {
+  return jl_small(a, b) ? (int64_t)jl_fd_q((uint32_t)a, f) : a / b;
+}
+JL_HD int64_t jl_remf(int64_t a, int64_t b, jl_fd f) {
+  return jl_small(a, b) ? (int64_t)((uint32_t)a - jl_fd_q((uint32_t)a, f) * (uint32_t)b) : a % b;
+}
+JL_HD int64_t jl_modf(int64_t a, int64_t b, jl_fd f) {
+  return jl_small(a, b) ? jl_remf(a, b, f) : jl_mod(a, b);
+}
 JL_HD int64_t jl_imax(int64_t a, int64_t b) { return a > b ? a : b; }
 JL_HD int64_t jl_imin(int64_t a, int64_t b) { return a < b ? a : b; }
 JL_HD int64_t jl_iabs(int64_t a) { return a < 0 ? -a : a; }

@@ -111,6 +111,14 @@ def halving(size, r):
     return a
 
 
+def divmod(size, r):
+    n, d = size
+    a = OrderedDict()
+    a["x"], a["xb"] = _n(r, n), _n(r, n, 0.1)
+    a["i_n"], a["i_d"] = n, d
+    return a
+
+
 # name -> (file, builder, dims, initstacks argument names, sizes: small, odd, zero-trip, large)
 CASES = {
     "affine_ls_b": ("affine_ls_b.jl", affine, None, ("n_s", "n_o", "n_i"),
@@ -128,6 +136,9 @@ CASES = {
                  [(40, 5), (1, 1), (0, 3), (5000, 17)]),
     "halving_b": ("halving_b.jl", halving, None, None, [(16,), (13,), (1,), (4096,)]),
     "smooth_b": ("smooth_b.jl", smooth, None, ("i_n",), [(12,), (3,), (2,), (100000,)]),
+    "divmod_b": ("divmod_b.jl", divmod, None, None,
+                 [(50, 7), (777, 1), (0, 3), (500, 3), (1000, 64), (3000, 2147483647),
+                  (3000, 2147483648), (20000, 97)]),
 }
 
 
