@@ -89,6 +89,21 @@ def test_decisions_heat():
         {"name": "u_stack", "dtype": "f64"}]
 
 
+def test_heat_kernel_rewrites():
+    """The emitted C3 kernels carry the rewrites their speed rests on: alpha
+    (never assigned) goes by value, the block-sum kernels stride over a
+    resident grid, the consumed adjoints' zero stores wait for their loads,
+    and the divisions by n multiply by a per-launch magic number."""
+    cu, _ = emit.emit(ec.source("heat2d_b"))
+    assert "g_fbox[0] = v0" in cu and "double j_alpha" in cu   # alphab boxed, alpha by value
+    assert cu.count("stade_resident_blocks((const void*)") == 2   # loss and the stencil rest
+    assert "tid_ += (int64_t)gridDim.x * blockDim.x" in cu
+    assert "jl_after((double)(0.0), jl_bits(j___oldb_1) & z_)" in cu   # unb[idx] = 0.0
+    assert "jl_after((double)(0.0), jl_bits(j___oldb_0) & z_)" in cu   # ub[idx2] = 0.0
+    assert "jl_divf((j_idx - ((int64_t)1)), j_n, fd_n)" in cu and "jl_fd_make(j_n)" in cu
+    assert "jl_div((j_idx" not in cu
+
+
 def test_decisions_generic():
     _, L = _loops("decay_b")
     assert [m for _, m, *_ in L] == ["host", "parallel", "host", "parallel"]
