@@ -11,8 +11,10 @@ the adjoint sweep on this rank's block of samples, and (N > 1) the NCCL sum of
 the :accum bucket and of the loss. With N GPUs each rank owns 65,536 / N
 samples (strong scaling: the grad-eval is fixed, its work is split).
 
-Also selectable with --config: heat2d (C3), affine_ls (C1), mlp2_ce_hv (C5),
-conv1d_relu_mse (C4); each is a single-GPU line (replicas at N > 1).
+Also selectable with --config: heat2d (C3; row slabs with a halo exchange per
+step at N > 1), affine_ls (C1; replicas at N > 1), mlp2_ce_hv (C5; sample
+blocks), conv1d_relu_mse (C4; sample blocks, the mean loss's seed and sum
+scaled by 1/N).
 
     python bench.py [--gpus N --steps K --warmup W] [--config NAME] [--impl reference]
     python bench.py --config affine_ls|heat2d --impl emitted
@@ -666,23 +668,35 @@ class EmittedHeat2d(Heat2d):
 
 
 class Conv1dReluMse:
+    """C4. At N > 1 (a power of two) each rank takes a block of the 4,096
+    samples; the loss is a mean, so the loss seed goes in scaled by 1/N and
+    the summed loss comes out scaled by 1/N (ddp.mean_loss_factor), and the
+    :accum wb and the loss are summed in one bucket."""
     name = "conv1d_relu_mse"
     dtype = "f32"
-    scaling = "weak"
     flush_l2 = False  # x alone is 2.1 GB
 
     def __init__(self, torch, rank, world, comm_factory):
         import numpy as np
-        from stadeb200 import synth, kernels
-        self.torch, self.np, self.kernels = torch, np, kernels
+        from stadeb200 import synth, kernels, ddp
+        self.torch, self.np, self.kernels, self.ddp = torch, np, kernels, ddp
         c = synth.FULL["conv1d_relu_mse"]
-        self.B, self.C, self.L, self.O, self.K = c["n_b"], c["n_c"], c["n_l"], c["n_o"], c["n_k"]
+        self.G, self.C, self.L, self.O, self.K = c["n_b"], c["n_c"], c["n_l"], c["n_o"], c["n_k"]
         self.world = world
+        self.factor = ddp.mean_loss_factor(self.G, world) if world > 1 else 1.0
+        self.scaling = "strong"
+        rng = ddp.shard(self.G, rank, world)
+        self.B = len(rng)
         B, C, L, O, K = self.B, self.C, self.L, self.O, self.K
-        self.nt = B * O * (L - K + 1)
-        d = synth.conv1d_relu_mse_inputs(B, C, L, O, K)
+        lo_ = L - K + 1
+        self.nt = B * O * lo_
+        d = synth.conv1d_relu_mse_inputs(self.G, C, L, O, K)
+        d["x"] = d["x"][rng.start * C * L:rng.stop * C * L]
+        d["t"] = d["t"][rng.start * O * lo_:rng.stop * O * lo_]
+        d["lossb"] = (d["lossb"] * np.float32(self.factor)).astype(np.float32)
         f32 = torch.float32
-        self.pinned = {k: torch.from_numpy(v).pin_memory() for k, v in d.items()}
+        self.pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory()
+                       for k, v in d.items()}
         t = {k: v.to("cuda") for k, v in self.pinned.items()}
         z = lambda m: torch.zeros(m, dtype=f32, device="cuda")
         t.update(loss=z(1), xb=z(B * C * L), wb=z(O * C * K), tb=z(self.nt), z=z(self.nt),
@@ -692,6 +706,7 @@ class Conv1dReluMse:
                               device="cuda")
         self.grad_host = {k: torch.empty(t[k].numel(), dtype=f32).pin_memory()
                           for k in ("wb", "loss")}
+        self.comm = comm_factory() if world > 1 else None
 
     def step(self):
         t = self.t
@@ -701,6 +716,9 @@ class Conv1dReluMse:
                                             t["t"], t["tb"], t["z"], t["zb"], t["r"], t["rb"],
                                             self.B, self.C, self.L, self.O, self.K,
                                             workspace=self.ws)
+        if self.comm is not None:
+            self.ddp.allreduce_sum_(self.comm, t["wb"], t["loss"])
+            t["loss"].mul_(self.factor)
 
     def e2e_step(self):
         t, p = self.t, self.pinned
@@ -724,9 +742,10 @@ class Conv1dReluMse:
 
     def config(self):
         return {"workload": "C4 conv1d_relu_mse_b: 1-D conv 128x64x9 + ReLU + MSE adjoint, batch "
-                            "4096 x 64 x 2048, Float32", "n_b": self.B, "n_c": self.C,
+                            "4096 x 64 x 2048, Float32", "global_batch": self.G,
+                "per_rank_batch": self.B, "n_c": self.C,
                 "n_l": self.L, "n_o": self.O, "n_k": self.K,
-                "parallelism": f"replicas{self.world}", "l2": "inputs larger than L2"}
+                "parallelism": f"dp{self.world}", "l2": "inputs larger than L2"}
 
     def cpu_baseline(self, seconds):
         np = self.np

@@ -177,6 +177,34 @@ AFFINE_LS = KernelSig(
 )
 
 
+# The primal conv1d_relu_mse (oracle/primals.jl): z, r are overwritten, every
+# write of loss adds to loss itself; its loss is a mean over all outputs
+# (inv_n = 1 / (n_b n_o n_lo) inside the sweep).
+CONV1D_RELU_MSE = KernelSig(
+    name="conv1d_relu_mse",
+    args=("loss", "x", "w", "t", "z", "r", "n_b", "n_c", "n_l", "n_o", "n_k"),
+    kinds={**{a: "array_float" for a in ("loss", "x", "w", "t", "z", "r")},
+           **{a: "scalar_int" for a in ("n_b", "n_c", "n_l", "n_o", "n_k")}},
+    written=frozenset({"z", "r", "loss"}),
+    reduced_outputs=frozenset({"loss"}),
+)
+
+
+def mean_loss_factor(n_samples: int, nranks: int) -> float:
+    """For a primal whose loss is a mean over its samples (C4's inv_n), a
+    rank of a sample-sharded run computes inv_n over its own block, nranks
+    times the whole batch's. Multiplying the loss seed by the returned factor
+    before the sweep and the summed :reduced loss by it after the sum makes
+    the sharded run the whole-batch function. The factor is 1 / nranks and is
+    required to be a power of two with equal blocks: then every product that
+    carries it is exact, the per-sample adjoints equal the whole-batch ones
+    bit for bit, and the :accum sums differ only in summation order."""
+    if nranks < 1 or nranks & (nranks - 1) or n_samples % nranks:
+        raise ValueError(f"a mean loss shards exactly over a power-of-two rank count that "
+                         f"divides the samples; got {n_samples} samples on {nranks} ranks")
+    return 1.0 / nranks
+
+
 def shard(n_samples: int, rank: int, nranks: int, mode: str = "block") -> range | list:
     """Samples of one rank. "mod": sample s (1-based) on rank mod(s - 1, P),
     as test/validate_ddp.jl:52-53; "block": contiguous blocks, which keeps

@@ -315,3 +315,97 @@ def test_rank_invariance_gloo(case, mode):
     # both ranks hold the same sums
     for b in ref:
         assert np.array_equal(res[0][1][b], res[1][1][b])
+
+
+# ---- C4: a mean loss over sample blocks ---------------------------------------------
+CONV_SIZES = (8, 3, 12, 4, 3)   # n_b, n_c, n_l, n_o, n_k
+
+
+def _conv_bank(rows, dtype, factor):
+    from stadeb200 import synth
+    n_b, n_c, n_l, n_o, n_k = CONV_SIZES
+    n_lo = n_l - n_k + 1
+    full = synth.conv1d_relu_mse_inputs(*CONV_SIZES)
+    rng = np.random.default_rng(5)          # the same non-zero local seeds on every rank
+    seeds = {k: rng.standard_normal(n_b * n) for k, n in
+             (("xb", n_c * n_l), ("tb", n_o * n_lo), ("zb", n_o * n_lo), ("rb", n_o * n_lo))}
+    per = dict(x=n_c * n_l, xb=n_c * n_l, t=n_o * n_lo, tb=n_o * n_lo, zb=n_o * n_lo,
+               rb=n_o * n_lo)
+    lo, hi = rows.start, rows.stop
+    sl = lambda a, k: np.ascontiguousarray(a[lo * per[k]:hi * per[k]]).astype(dtype)
+    m = hi - lo
+    return dict(loss=np.zeros(1, dtype), lossb=(full["lossb"] * factor).astype(dtype),
+                x=sl(full["x"], "x"), xb=sl(seeds["xb"], "xb"), w=full["w"].astype(dtype),
+                wb=np.zeros(n_o * n_c * n_k, dtype), t=sl(full["t"], "t"),
+                tb=sl(seeds["tb"], "tb"), z=np.zeros(m * n_o * n_lo, dtype),
+                zb=sl(seeds["zb"], "zb"), r=np.zeros(m * n_o * n_lo, dtype),
+                rb=sl(seeds["rb"], "rb"))
+
+
+def _conv_sweep(bank, m):
+    from oracle import oracle as orc
+    n_b, n_c, n_l, n_o, n_k = CONV_SIZES
+    orc.conv1d_relu_mse_b(*[bank[k] for k in ("loss", "lossb", "x", "xb", "w", "wb", "t", "tb",
+                                              "z", "zb", "r", "rb")], m, n_c, n_l, n_o, n_k)
+
+
+def _conv_rank_main(rank, world, port, dtype, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        factor = ddp.mean_loss_factor(CONV_SIZES[0], world)
+        rows = ddp.shard(CONV_SIZES[0], rank, world)
+        bank = _conv_bank(rows, dtype, factor)
+        epi = ddp.Epilogue(ddp.CONV1D_RELU_MSE, ["x", "t"], "adjoint", GlooBackend())
+        assert epi.accum == ["wb"] and epi.reduced == ["loss"]
+        epi.reset_accum(bank)
+        epi.reset_reduced(bank)
+        _conv_sweep(bank, len(rows))
+        n_global = epi.allreduce_accum(bank, len(rows))
+        epi.allreduce_reduced(bank)
+        bank["loss"] *= bank["loss"].dtype.type(factor)
+        q.put((rank, rows.start, rows.stop, n_global, bank))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_conv_mean_loss_shards_exactly(dtype):
+    """C4 on two gloo ranks, each on its block of samples with the loss seed
+    and the summed loss scaled by 1/2: every per-sample array (z, r and the
+    adjoints xb, tb, zb, rb) equals the whole-batch run's rows bit for bit;
+    wb and loss agree to summation order."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_conv_rank_main, args=(r, 2, port, dtype, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    n_b, n_c, n_l, n_o, n_k = CONV_SIZES
+    n_lo = n_l - n_k + 1
+    ref = _conv_bank(range(0, n_b), dtype, 1.0)
+    _conv_sweep(ref, n_b)
+    per = dict(xb=n_c * n_l, tb=n_o * n_lo, z=n_o * n_lo, zb=n_o * n_lo, r=n_o * n_lo,
+               rb=n_o * n_lo)
+    tol = 1e-5 if dtype == np.float32 else 1e-12
+    for rank, lo, hi, n_global, bank in res:
+        assert n_global == n_b
+        for k, n in per.items():
+            assert np.array_equal(bank[k], ref[k][lo * n:hi * n]), (rank, k)
+        for k in ("wb", "loss"):
+            err = np.max(np.abs(bank[k] - ref[k])) / np.max(np.abs(ref[k]))
+            assert err <= tol, (rank, k, err)
+    assert np.array_equal(res[0][4]["wb"], res[1][4]["wb"])
+
+
+def test_mean_loss_factor_refusals():
+    assert ddp.mean_loss_factor(4096, 8) == 0.125
+    for n, p in ((4096, 3), (6, 4), (10, 0)):
+        with pytest.raises(ValueError):
+            ddp.mean_loss_factor(n, p)
