@@ -147,7 +147,22 @@ function Comm(id::Vector{UInt8}, nranks::Integer, rank::Integer; timeout_ms::Int
     return Comm(h[])
 end
 
-mlp2_ce_b_reset_accum!(w1b, b1b, w2b, b2b) = (foreach(b -> fill!(b, 0f0), (w1b, b1b, w2b, b2b)); nothing)
+"""Sum the buffers (all Float32 or all Float64) across ranks in one
+collective; with `n_local` given, also the sample counts, returning the
+global count (the generic form of `<k>_b_allreduce_accum!`)."""
+function ddp_allreduce_sum!(comm::Comm, bufs::CuArray{T}...; n_local = nothing) where {T}
+    dt = T === Float32 ? Cint(0) : T === Float64 ? Cint(1) : error("Float32 or Float64 buffers")
+    ptrs = [reinterpret(Ptr{Cvoid}, pointer(b)) for b in bufs]
+    counts = Int64[length(b) for b in bufs]
+    ng = Ref{Int64}(0)
+    check(ccall((:stade_ddp_allreduce_sum, libstade), Cint,
+        (Ptr{Cvoid}, Ptr{Ptr{Cvoid}}, Ptr{Int64}, Cint, Cint, Int64, Ptr{Int64}, Ref{StadeOpts}),
+        comm.handle, ptrs, counts, length(bufs), dt, n_local === nothing ? 0 : n_local,
+        n_local === nothing ? C_NULL : ng, opts()))
+    return n_local === nothing ? nothing : ng[]
+end
+
+mlp2_ce_b_reset_accum!(w1b, b1b, w2b, b2b) =(foreach(b -> fill!(b, 0f0), (w1b, b1b, w2b, b2b)); nothing)
 mlp2_ce_b_reset_reduced!(loss) = (fill!(loss, 0f0); nothing)
 mlp2_ce_b_reset_local!(xb, yb, hb, zb, pb) = (foreach(b -> fill!(b, 0f0), (xb, yb, hb, zb, pb)); nothing)
 
