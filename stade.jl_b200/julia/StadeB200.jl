@@ -152,7 +152,7 @@ collective; with `n_local` given, also the sample counts, returning the
 global count (the generic form of `<k>_b_allreduce_accum!`)."""
 function ddp_allreduce_sum!(comm::Comm, bufs::CuArray{T}...; n_local = nothing) where {T}
     dt = T === Float32 ? Cint(0) : T === Float64 ? Cint(1) : error("Float32 or Float64 buffers")
-    ptrs = [reinterpret(Ptr{Cvoid}, pointer(b)) for b in bufs]
+    ptrs = [Ptr{Cvoid}(UInt(pointer(b))) for b in bufs]   # device addresses
     counts = Int64[length(b) for b in bufs]
     ng = Ref{Int64}(0)
     check(ccall((:stade_ddp_allreduce_sum, libstade), Cint,
