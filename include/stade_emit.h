@@ -7,17 +7,27 @@
  * and writes one CUDA source that defines
  *
  *   int     stade_<k>_b(<generated argument order>, void* stream);
- *   int64_t stade_initstacks_<k>_b(<int arguments>, int64_t* sizes, int* dtypes);
+ *   int64_t stade_initstacks_<k>_b(<int arguments>, int64_t* sizes, int* dtypes,
+ *                                  void* const* fill);
  *
  * Arguments keep the generated order. Float arrays are T* (T = double, or
  * float with precision 32, as cgen_convert_precision), integer arrays and
  * stacks int64_t*, integer scalars int64_t by value, float scalars by value
  * unless the sweep returns them (their adjoints), in which case they are T*
  * host pointers updated in place (the generated code returns them by value,
- * emit_return_scalars src/STADE.jl:2072). stade_initstacks_<k>_b evaluates the
- * stack sizes initstacks_<k>_b allocates (the tape layout of
- * agen_indexed_layout, src/STADE.jl:4917) and returns the number of stacks;
- * the caller allocates them (the library never allocates).
+ * emit_return_scalars src/STADE.jl:2072). stade_initstacks_<k>_b runs
+ * initstacks_<k>_b's statements on the host (the closed-form tape layout of
+ * agen_indexed_layout, src/STADE.jl:4917, or the Tier-B sizing loop of
+ * agen_tier_b_block_stmts, src/STADE.jl:5338-5380) and returns the number
+ * of items it returns; per item i, sizes[i] and dtypes[i]:
+ *   0 / 1 / 2  a stack (Float64 / Float32 / Int64) of sizes[i] elements the
+ *              caller allocates and zero-fills (the library never allocates);
+ *   3          an integer (a running total, a length): its value in sizes[i];
+ *   4 / 5      a table initstacks fills (Int64 / the sweep's float type) of
+ *              sizes[i] elements: with fill non-NULL and fill[i] a host buffer
+ *              of that size, its contents are written there.
+ * An argument initstacks reads only through length(a) is passed as that
+ * length (the manifest lists these as "length_args").
  *
  * The manifest (JSON) lists the arguments with their kinds, the stacks, the
  * returned scalars and one record per loop: parallel kernel (thread per

@@ -127,6 +127,9 @@ std::vector<Tok> lex(const std::string& src) {
                                  ? ".0" : "")
                       : t);
       i = j;
+      // a numeric literal coefficient (`0.5__oldb_0`, `2(x + 1)`): multiplication
+      if (i < n && (std::isalpha((unsigned char)src[i]) || src[i] == '_' || src[i] == '('))
+        push(T_OP, "jux");
       continue;
     }
     static const char* two[] = {"==", "!=", "<=", ">=", "&&", "||", "+=", "-=", "*=", "/="};
@@ -453,6 +456,12 @@ class Parser {
   }
   EP power() {
     EP b = postfix();
+    if (b->kind == Expr::Num && is_op("jux")) {
+      // Julia: a literal coefficient binds tighter than * and / (1/2x is
+      // 1/(2x)) and takes the power after it (2x^3 is 2(x^3))
+      next();
+      return mk(Expr::Bin, "*", {b, power()});
+    }
     if (is_op("^")) {
       next();
       return mk(Expr::Bin, "^", {b, unary()});
@@ -690,6 +699,9 @@ class Emitter {
   std::map<std::string, Storage> store_;
   std::map<std::string, int> fslot_, islot_;
   std::set<std::string> stacks_;
+  std::set<std::string> tier_b_tables_;   // prefix_<stack>_<id> tables initstacks fills
+  bool init_printing_ = false;          // printing initstacks: length(p) is the argument p
+  std::string init_len_args_ = "[]";    // initstacks arguments passed as an array's length
   std::map<std::string, std::string> stack_type_;  // name -> "f" / "i"
   std::vector<std::string> decisions_;
   std::map<const Stmt*, std::string> red_sites_;   // accumulation -> block sum register
@@ -825,13 +837,31 @@ class Emitter {
         returned_.insert(e->s);
       }
     });
-    // stacks: the trailing parameters initstacks returns
+    // stacks: the trailing parameters initstacks returns, allocated there
+    // (`Vector{T}(undef, n)`); a returned integer (`__len_m = length(m)`) is
+    // an integer argument of the sweep
     if (init_) {
+      std::set<std::string> allocated;
+      for (auto& s : init_->body)
+        if (s->kind == Stmt::Assign && s->lhs->kind == Expr::Var && s->rhs->kind == Expr::Curly)
+          allocated.insert(s->lhs->s);
+      // Tier-B prefix tables: filled by initstacks' sizing loop
+      walk_stmts(init_->body, [&](Stmt& s) {
+        if (s.kind == Stmt::Assign && s.lhs->kind == Expr::Ref && s.lhs->s.rfind("prefix_", 0) == 0)
+          tier_b_tables_.insert(s.lhs->s);
+      });
       for (auto& s : init_->body)
         if (s->kind == Stmt::Return && s->ret) {
           std::vector<EP> items = s->ret->kind == Expr::Tuple ? s->ret->a : std::vector<EP>{s->ret};
-          for (auto& e : items)
-            if (e->kind == Expr::Var) stacks_.insert(e->s);
+          for (auto& e : items) {
+            if (e->kind != Expr::Var) continue;
+            if (allocated.count(e->s)) {
+              stacks_.insert(e->s);
+            } else if (params_.count(e->s)) {
+              ints_.insert(e->s);
+              arrays_.erase(e->s);
+            }
+          }
         }
     }
     for (auto& p : f_.params)
@@ -1130,6 +1160,43 @@ class Emitter {
       for (auto& b : cs)
         if (a.k == Cls::DIVP && b.k == Cls::MODP && a.key == b.key) return true;
     return false;
+  }
+
+  // A Tier-B tape slot (agen_tier_b_block_stmts, src/STADE.jl:5338-5380):
+  // prefix_<stack>_<id>[f(v)] + g, the prefix table filled by initstacks and
+  // indexed injectively by the thread variable, g varying only with loops
+  // inside the iteration. The layout gives each iteration of the header loop
+  // its own span of slots, so threads write disjoint slots.
+  bool tier_b_slot(const std::vector<EP>& idx, const std::string& v,
+                   const std::set<std::string>& varying, const std::set<std::string>& written,
+                   const std::map<std::string, EP>& defs, const std::set<std::string>& inner) {
+    if (idx.size() != 1) return false;
+    std::vector<EP> terms;
+    std::function<void(const EP&)> flat = [&](const EP& x) {
+      if (x->kind == Expr::Bin && x->s == "+") {
+        flat(x->a[0]);
+        flat(x->a[1]);
+      } else {
+        terms.push_back(x);
+      }
+    };
+    flat(subst(idx[0], defs));
+    int n_prefix = 0;
+    for (auto& t : terms) {
+      if (t->kind == Expr::Ref && t->a.size() == 1 && tier_b_tables_.count(t->s) &&
+          !written.count(t->s) && classify(t->a[0], v, varying, written, defs, 0).k == Cls::INJ) {
+        ++n_prefix;
+        continue;
+      }
+      bool ok = true;
+      walk_expr(t, [&](const EP& y) {
+        if (y->kind == Expr::Ref || (y->kind == Expr::Var && y->s == v) ||
+            (y->kind == Expr::Var && varying.count(y->s) && !inner.count(y->s)))
+          ok = false;
+      });
+      if (!ok) return false;
+    }
+    return n_prefix == 1;
   }
 
   // ---- loop plan ---------------------------------------------------------------
@@ -1455,6 +1522,7 @@ class Emitter {
       }
       if (!any_write) continue;
       if (same && injective(ss[0].index, L.var, varying, written, defs)) continue;
+      if (same && tier_b_slot(ss[0].index, L.var, varying, written, defs, inner_vars)) continue;
       if (all_acc && !any_read) {
         p.atomic_arrays.insert(a);
         continue;
@@ -1863,6 +1931,8 @@ class Emitter {
       }
       case Expr::Call: {
         const std::string& n = e->s;
+        if (n == "length" && init_printing_ && e->a.size() == 1 && e->a[0]->kind == Expr::Var)
+          return cname(e->a[0]->s);   // the caller passes the array's length
         std::vector<std::string> a;
         for (auto& x : e->a) a.push_back(cx(x, locals, line));
         auto need = [&](size_t k) {
@@ -2532,61 +2602,8 @@ class Emitter {
     // initstacks
     std::string mf_stacks = "[]", init_sym = "null", init_args = "[]";
     if (init_) {
-      for (auto& p : init_->params) ints_.insert(p);
-      for (auto& s : init_->body)
-        if (s->kind == Stmt::Assign && s->lhs->kind == Expr::Var && s->rhs->kind != Expr::Curly)
-          ints_.insert(s->lhs->s);
-      std::ostringstream q;
-      std::vector<std::string> st_names, st_types;
-      std::map<std::string, EP> sizes;
-      for (auto& s : init_->body) {
-        if (s->kind == Stmt::Assign && s->lhs->kind == Expr::Var && s->rhs->kind == Expr::Curly) {
-          if (s->rhs->a.size() != 2) fail(s->line, "expected Vector{T}(undef, n)");
-          sizes[s->lhs->s] = s->rhs->a[1];
-          st_types.push_back(s->rhs->s);
-        } else if (s->kind == Stmt::Return) {
-          if (s->ret) {
-            std::vector<EP> items = s->ret->kind == Expr::Tuple ? s->ret->a : std::vector<EP>{s->ret};
-            for (auto& e : items) st_names.push_back(e->s);
-          }
-        } else if (s->kind == Stmt::Assign && s->lhs->kind == Expr::Var) {
-          sizes[s->lhs->s] = s->rhs;   // integer temporaries
-        } else {
-          fail(s->line, "unsupported statement in " + init_->name);
-        }
-      }
-      q << "extern \"C\" int64_t stade_" << init_->name << "(";
-      std::string ia;
-      for (auto& p : init_->params) {
-        q << "int64_t " << cname(p) << ", ";
-        ia += std::string(ia.empty() ? "" : ", ") + jstr(p);
-      }
-      q << "int64_t* sizes, int* dtypes) {\n";
-      // temporaries first (integer), in order
-      for (auto& s : init_->body)
-        if (s->kind == Stmt::Assign && s->rhs->kind != Expr::Curly)
-          q << "  const int64_t " << cname(s->lhs->s) << " = " << cx(s->rhs, init_locals(), s->line)
-            << ";\n";
-      std::string ms;
-      for (size_t i = 0; i < st_names.size(); ++i) {
-        const std::string& nm = st_names[i];
-        auto it = sizes.find(nm);
-        if (it == sizes.end()) fail(init_->line, "initstacks returns " + nm + " without allocating it");
-        std::string ty;
-        for (auto& s : init_->body)
-          if (s->kind == Stmt::Assign && s->lhs->s == nm && s->rhs->kind == Expr::Curly) ty = s->rhs->s;
-        int code = ty.find("Int") != std::string::npos ? 2 : (f32_ ? 1 : 0);
-        q << "  if (sizes) sizes[" << i << "] = jl_imax((int64_t)0, (int64_t)("
-          << cx(it->second, init_locals(), init_->line) << "));\n";
-        q << "  if (dtypes) dtypes[" << i << "] = " << code << ";\n";
-        ms += std::string(ms.empty() ? "" : ", ") + "{\"name\": " + jstr(nm) + ", \"dtype\": " +
-              jstr(code == 2 ? "i64" : (code == 1 ? "f32" : "f64")) + "}";
-      }
-      q << "  return " << st_names.size() << ";\n}\n";
-      o << q.str();
-      mf_stacks = "[" + ms + "]";
+      o << initstacks_src(mf_stacks, init_args);
       init_sym = jstr("stade_" + init_->name);
-      init_args = "[" + ia + "]";
     }
     cu = o.str();
     std::string ret;
@@ -2604,8 +2621,192 @@ class Emitter {
     manifest = "{\"function\": " + jstr(f_.name) + ", \"symbol\": " + jstr("stade_" + f_.name) +
                ", \"precision\": " + jstr(f32_ ? "f32" : "f64") + ", \"args\": [" + mf_args +
                "], \"returns\": " + jlist(ret_order) + ", \"initstacks\": {\"symbol\": " + init_sym +
-               ", \"args\": " + init_args + ", \"stacks\": " + mf_stacks + "}, \"kernels\": " +
+               ", \"args\": " + init_args + ", \"length_args\": " + init_len_args_ +
+               ", \"stacks\": " + mf_stacks + "}, \"kernels\": " +
                std::to_string(units_.size()) + ", \"loops\": [\n  " + dec + "]}\n";
+  }
+
+  // initstacks_<k> as a host function whose statements run in order: the
+  // closed-form stack sizes of agen_indexed_layout (src/STADE.jl:4917), or
+  // the Tier-B sizing loop of agen_tier_b_block_stmts (src/STADE.jl:5338-5380)
+  // with its prefix / value tables and running totals. Per returned item:
+  //   a stack it allocates and does not fill: its size, dtype 0 / 1 (float,
+  //   the sweep's precision) or 2 (Int64), zero-filled by the caller;
+  //   a table it fills: its size, dtype 4 (Int64) or 5 (float), and its
+  //   contents copied into fill[i] when the caller passes a buffer there;
+  //   an integer (a total, __len_m): its value in sizes[i], dtype 3.
+  std::string initstacks_src(std::string& mf_stacks, std::string& init_args) {
+    const Func& F = *init_;
+    std::map<std::string, std::string> alloc_ty;   // allocated array -> Vector{T}
+    std::set<std::string> written, scalars, loop_vars;
+    walk_stmts(F.body, [&](Stmt& s) {
+      if (s.kind == Stmt::Assign && s.lhs->kind == Expr::Var) {
+        if (s.rhs->kind == Expr::Curly) {
+          if (s.rhs->a.size() != 2) fail(s.line, "expected Vector{T}(undef, n)");
+          alloc_ty[s.lhs->s] = s.rhs->s;
+        } else {
+          scalars.insert(s.lhs->s);
+        }
+      } else if (s.kind == Stmt::Assign && s.lhs->kind == Expr::Ref) {
+        written.insert(s.lhs->s);
+      } else if (s.kind == Stmt::For) {
+        loop_vars.insert(s.var);
+      } else if (s.kind != Stmt::If && s.kind != Stmt::While && s.kind != Stmt::Return) {
+        fail(s.line, "unsupported statement in " + F.name);
+      }
+    });
+    for (auto& w : written)
+      if (!alloc_ty.count(w)) fail(F.line, F.name + " writes " + w + ", which it does not allocate");
+    // arrays of the initstacks body, as cx prints them (p_<name>)
+    for (auto& [a, ty] : alloc_ty) {
+      arrays_.insert(a);
+      if (ty.find("Int") != std::string::npos) int_arrays_.insert(a);
+      else int_arrays_.erase(a);
+    }
+    // scalar types: integer unless some assignment gives a float
+    for (auto& p : F.params) ints_.insert(p);
+    for (auto& v : loop_vars) ints_.insert(v);
+    for (auto& v : scalars) ints_.insert(v);
+    std::set<std::string> floats;
+    for (bool changed = true; changed;) {
+      changed = false;
+      walk_stmts(F.body, [&](Stmt& s) {
+        if (s.kind == Stmt::Assign && s.lhs->kind == Expr::Var && s.rhs->kind != Expr::Curly &&
+            !floats.count(s.lhs->s) && !is_int_expr(s.rhs)) {
+          floats.insert(s.lhs->s);
+          ints_.erase(s.lhs->s);
+          changed = true;
+        }
+      });
+    }
+    std::set<std::string> locals(F.params.begin(), F.params.end());
+    locals.insert(scalars.begin(), scalars.end());
+    locals.insert(loop_vars.begin(), loop_vars.end());
+
+    std::ostringstream q;
+    q << "extern \"C\" int64_t stade_" << F.name << "(";
+    std::string ia, la;
+    std::set<std::string> len_params;
+    walk_stmts(F.body, [&](Stmt& s) {
+      for (const EP* e : {&s.lhs, &s.rhs, &s.cond, &s.lo, &s.hi, &s.step})
+        if (*e)
+          walk_expr(*e, [&](const EP& x) {
+            if (x->kind == Expr::Call && x->s == "length" && x->a.size() == 1 &&
+                x->a[0]->kind == Expr::Var)
+              len_params.insert(x->a[0]->s);
+          });
+    });
+    for (auto& p : F.params) {
+      q << "int64_t " << cname(p) << ", ";
+      ia += std::string(ia.empty() ? "" : ", ") + jstr(p);
+      if (len_params.count(p)) la += std::string(la.empty() ? "" : ", ") + jstr(p);
+    }
+    init_len_args_ = "[" + la + "]";
+    init_args = "[" + ia + "]";
+    q << "int64_t* sizes, int* dtypes, void* const* fill) {\n";
+    q << "  (void)sizes; (void)dtypes; (void)fill;\n";
+    for (auto& v : scalars)
+      if (!std::count(F.params.begin(), F.params.end(), v))
+        q << "  " << (floats.count(v) ? T_ : std::string("int64_t")) << " " << cname(v) << " = 0;\n";
+    for (auto& [a, ty] : alloc_ty) {
+      q << "  int64_t n_" << a << " = 0;\n";
+      if (written.count(a)) {
+        const std::string et = int_arrays_.count(a) ? "int64_t" : T_;
+        q << "  std::vector<" << et << "> v_" << a << ";\n  " << et << "* p_" << a << " = nullptr;\n";
+      }
+    }
+    init_printing_ = true;
+    init_stmts(q, F.body, locals, alloc_ty, written, 2, mf_stacks);
+    init_printing_ = false;
+    q << "  return 0;\n}\n";
+    return q.str();
+  }
+
+  void init_stmts(std::ostringstream& q, const std::vector<SP>& body, std::set<std::string> locals,
+                  const std::map<std::string, std::string>& alloc_ty,
+                  const std::set<std::string>& written, int ind, std::string& mf_stacks) {
+    const std::string pad(ind, ' ');
+    for (auto& sp : body) {
+      Stmt& s = *sp;
+      switch (s.kind) {
+        case Stmt::Assign:
+          if (s.lhs->kind == Expr::Var && s.rhs->kind == Expr::Curly) {
+            const std::string& a = s.lhs->s;
+            q << pad << "n_" << a << " = jl_imax((int64_t)0, (int64_t)("
+              << cx(s.rhs->a[1], locals, s.line) << "));\n";
+            if (written.count(a))
+              q << pad << "v_" << a << ".assign((size_t)n_" << a << ", 0);\n" << pad << "p_" << a
+                << " = v_" << a << ".data();\n";
+          } else if (s.lhs->kind == Expr::Var) {
+            q << pad << cname(s.lhs->s) << " = " << cast_to(s.lhs->s, cx(s.rhs, locals, s.line))
+              << ";\n";
+          } else {
+            q << pad << cx(s.lhs, locals, s.line) << " = "
+              << (int_arrays_.count(s.lhs->s) ? "(int64_t)" : "(" + T_ + ")")
+              << cx(s.rhs, locals, s.line) << ";\n";
+          }
+          break;
+        case Stmt::For: {
+          const std::string v = cname(s.var);
+          q << pad << "{\n" << pad << "  const int64_t lo_ = " << cx(s.lo, locals, s.line)
+            << ", hi_ = " << cx(s.hi, locals, s.line)
+            << ", st_ = " << (s.step ? cx(s.step, locals, s.line) : "((int64_t)1)") << ";\n";
+          q << pad << "  for (int64_t " << v << " = lo_; st_ > 0 ? " << v << " <= hi_ : " << v
+            << " >= hi_; " << v << " += st_) {\n";
+          std::set<std::string> inner = locals;
+          inner.insert(s.var);
+          init_stmts(q, s.body, inner, alloc_ty, written, ind + 4, mf_stacks);
+          q << pad << "  }\n" << pad << "}\n";
+          break;
+        }
+        case Stmt::If:
+          q << pad << "if (" << cx(s.cond, locals, s.line) << ") {\n";
+          init_stmts(q, s.body, locals, alloc_ty, written, ind + 2, mf_stacks);
+          q << pad << "} else {\n";
+          init_stmts(q, s.els, locals, alloc_ty, written, ind + 2, mf_stacks);
+          q << pad << "}\n";
+          break;
+        case Stmt::While:
+          q << pad << "while (" << cx(s.cond, locals, s.line) << ") {\n";
+          init_stmts(q, s.body, locals, alloc_ty, written, ind + 2, mf_stacks);
+          q << pad << "}\n";
+          break;
+        case Stmt::Return: {
+          std::vector<EP> items;
+          if (s.ret) items = s.ret->kind == Expr::Tuple ? s.ret->a : std::vector<EP>{s.ret};
+          std::string ms;
+          for (size_t i = 0; i < items.size(); ++i) {
+            if (items[i]->kind != Expr::Var) fail(s.line, "initstacks returns " + text(items[i]));
+            const std::string& nm = items[i]->s;
+            const std::string at = "[" + std::to_string(i) + "]";
+            std::string dt;
+            auto al = alloc_ty.find(nm);
+            if (al == alloc_ty.end()) {
+              if (!locals.count(nm) || !ints_.count(nm))
+                fail(s.line, "initstacks returns " + nm + ", neither an array it allocates nor an integer");
+              q << pad << "if (sizes) sizes" << at << " = " << cname(nm) << ";\n";
+              q << pad << "if (dtypes) dtypes" << at << " = 3;\n";
+              dt = "int";
+            } else {
+              const bool is_int = al->second.find("Int") != std::string::npos;
+              int code = written.count(nm) ? (is_int ? 4 : 5) : (is_int ? 2 : (f32_ ? 1 : 0));
+              q << pad << "if (sizes) sizes" << at << " = n_" << nm << ";\n";
+              q << pad << "if (dtypes) dtypes" << at << " = " << code << ";\n";
+              if (written.count(nm))
+                q << pad << "if (fill && fill" << at << " && n_" << nm << " > 0) memcpy(fill" << at
+                  << ", p_" << nm << ", (size_t)n_" << nm << " * sizeof(*p_" << nm << "));\n";
+              static const char* names[] = {"f64", "f32", "i64", "int", "i64_table", "float_table"};
+              dt = code == 5 ? (f32_ ? "f32_table" : "f64_table") : names[code];
+            }
+            ms += std::string(ms.empty() ? "" : ", ") + "{\"name\": " + jstr(nm) +
+                  ", \"dtype\": " + jstr(dt) + "}";
+          }
+          mf_stacks = "[" + ms + "]";
+          q << pad << "return " << items.size() << ";\n";
+          break;
+        }
+      }
+    }
   }
 
   std::set<std::string> init_locals() {
@@ -2622,6 +2823,7 @@ class Emitter {
     return R"PRE(#include <stdint.h>
 #include <string.h>
 #include <math.h>
+#include <vector>
 static int64_t stade_launches_ = 0;   // kernels this module has launched
 #ifdef STADE_EMIT_HOST
 // Host build of the same program (tests): kernels run as loops over their

@@ -159,8 +159,8 @@ class Sweep:
         if ini["symbol"]:
             self.init = getattr(self.lib, ini["symbol"])
             self.init.restype = C.c_int64
-            self.init.argtypes = [C.c_int64] * len(ini["args"]) + [C.POINTER(C.c_int64),
-                                                                  C.POINTER(C.c_int)]
+            self.init.argtypes = [C.c_int64] * len(ini["args"]) + [
+                C.POINTER(C.c_int64), C.POINTER(C.c_int), C.POINTER(C.c_void_p)]
 
     def launches(self) -> int:
         """Kernels this library has launched so far (all calls)."""
@@ -168,26 +168,64 @@ class Sweep:
         f.restype = C.c_int64
         return int(f())
 
-    def stack_sizes(self, *ints):
+    def _init_args(self, args):
+        """initstacks' integer arguments; one it reads through `length(a)`
+        may be given as the array (or as its length)."""
+        import numpy as np
+        ini = self.m["initstacks"]
+        lens = set(ini.get("length_args", []))
+        vals = []
+        for name, a in zip(ini["args"], args):
+            if name in lens and not isinstance(a, int) and hasattr(a, "__len__"):
+                a = a.numel() if hasattr(a, "numel") else int(np.asarray(a).size)
+            vals.append(int(a))
+        return vals
+
+    def stack_sizes(self, *args):
+        """(size, kind) per item initstacks_<k> returns: kind "float64",
+        "float32" or "int64" for a stack the caller zero-fills, "int" for a
+        returned integer (size = its value), "int64_table" / "float_table"
+        for a table initstacks fills."""
         ini = self.m["initstacks"]
         if not self.init:
             return []
         n = len(ini["stacks"])
         sizes = (C.c_int64 * max(n, 1))()
         dts = (C.c_int * max(n, 1))()
-        got = self.init(*[int(i) for i in ints], sizes, dts)
-        return [(int(sizes[i]), ("float64", "float32", "int64")[dts[i]]) for i in range(got)]
+        got = self.init(*self._init_args(args), sizes, dts, None)
+        kinds = ("float64", "float32", "int64", "int", "int64_table", "float_table")
+        return [(int(sizes[i]), kinds[dts[i]]) for i in range(got)]
 
-    def initstacks(self, *ints, device="cuda"):
-        """The stacks initstacks_<k> allocates, zero-filled."""
+    def initstacks(self, *args, device="cuda"):
+        """What initstacks_<k> returns: its stacks zero-filled, its tables
+        with the contents it computes, its integers as ints."""
+        import numpy as np
+        items = self.stack_sizes(*args)
+        host = []
+        fill = (C.c_void_p * max(len(items), 1))()
+        for i, (n, kind) in enumerate(items):
+            if kind == "int":
+                host.append(n)
+                continue
+            dt = {"int64_table": "int64", "float_table": self.fdt}.get(kind, kind)
+            on_host = self.host or kind.endswith("_table")
+            a = np.zeros(max(n, 0) if on_host else 0, dt)
+            if kind.endswith("_table") and n > 0:
+                fill[i] = a.ctypes.data
+            host.append(a)
+        if any(k.endswith("_table") for _, k in items):
+            self.init(*self._init_args(args), None, None, fill)
+        if self.host:
+            return tuple(host)
+        import torch
         out = []
-        for n, dt in self.stack_sizes(*ints):
-            if self.host:
-                import numpy as np
-                out.append(np.zeros(n, dt))
+        for h, (n, kind) in zip(host, items):   # stacks straight on the device, tables copied up
+            if isinstance(h, int):
+                out.append(h)
+            elif kind.endswith("_table"):
+                out.append(torch.from_numpy(h).to(device))
             else:
-                import torch
-                out.append(torch.zeros(n, dtype=getattr(torch, dt), device=device))
+                out.append(torch.zeros(max(n, 0), dtype=getattr(torch, kind), device=device))
         return tuple(out)
 
     def _ptr(self, a, spec):

@@ -119,6 +119,16 @@ def divmod(size, r):
     return a
 
 
+def ragged(size, r):
+    (n,) = size
+    a = OrderedDict()
+    a["loss"], a["lossb"] = np.full(1, 0.0), np.full(1, 0.75)
+    a["x"], a["xb"] = _n(r, n), _n(r, n, 0.1)
+    a["w"], a["wb"] = _n(r, 3, 0.8), _n(r, 3, 0.1)
+    a["i_n"] = n
+    return a
+
+
 # name -> (file, builder, dims, initstacks argument names, sizes: small, odd, zero-trip, large)
 CASES = {
     "affine_ls_b": ("affine_ls_b.jl", affine, None, ("n_s", "n_o", "n_i"),
@@ -136,6 +146,7 @@ CASES = {
                  [(40, 5), (1, 1), (0, 3), (5000, 17)]),
     "halving_b": ("halving_b.jl", halving, None, None, [(16,), (13,), (1,), (4096,)]),
     "smooth_b": ("smooth_b.jl", smooth, None, ("i_n",), [(12,), (3,), (2,), (100000,)]),
+    "ragged_b": ("ragged_b.jl", ragged, None, ("i_n",), [(10,), (1,), (0,), (5000,)]),
     "divmod_b": ("divmod_b.jl", divmod, None, None,
                  [(50, 7), (777, 1), (0, 3), (500, 3), (1000, 64), (3000, 2147483647),
                   (3000, 2147483648), (20000, 97)]),

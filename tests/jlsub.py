@@ -345,24 +345,19 @@ class Interp:
             return r.value
         return None
 
-    def initstacks(self, name, *ints):
+    def initstacks(self, name, *args):
+        """Runs initstacks_<k> (closed-form sizes, or a Tier-B sizing loop
+        filling prefix tables and totals); returns what it returns, arrays
+        zero-filled where it does not write them."""
         params, body = self.funcs[name]
-        env = dict(zip(params, ints))
-        out = []
-        for st in body:
-            if st[0] == "assign" and st[2][0] == "alloc":
-                _, ty, args = st[2]
-                n = max(0, int(self.ev(args[1], env)))
-                dt = np.int64 if "Int" in ty else (np.float32 if self.f32 else np.float64)
-                env[st[1][1]] = np.zeros(n, dt)
-            elif st[0] == "assign":
-                env[st[1][1]] = self.ev(st[2], env)
-            elif st[0] == "return":
-                if st[1] is None:
-                    return ()
-                items = st[1][1] if st[1][0] == "tuple" else [st[1]]
-                return tuple(env[i[1]] for i in items)
-        return tuple(out)
+        env = dict(zip(params, args))
+        self.dims = {}
+        try:
+            self.run(body, env)
+        except _Return as r:
+            v = r.value
+            return () if v is None else (v if isinstance(v, tuple) else (v,))
+        return ()
 
     def _off(self, name, idx, env):
         ix = [int(self.ev(i, env)) for i in idx]
@@ -408,6 +403,10 @@ class Interp:
 
     def ev(self, e, env):
         k = e[0]
+        if k == "alloc":   # Vector{T}(undef, n)
+            n = max(0, int(self.ev(e[2][1], env)))
+            return np.zeros(n, np.int64 if "Int" in e[1] else
+                            (np.float32 if self.f32 else np.float64))
         if k == "num":
             return e[1] if isinstance(e[1], int) else self._flt(e[1])
         if k == "var":
@@ -458,6 +457,8 @@ class Interp:
                     ">=": a >= b}[op]
         if k == "call":
             name, args = e[1], [self.ev(x, env) for x in e[2]]
+            if name == "length":
+                return int(np.asarray(args[0]).size)
             if name == "div":
                 return _jdiv(args[0], args[1])
             if name == "mod":

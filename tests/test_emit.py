@@ -122,6 +122,14 @@ def test_decisions_generic():
     man, L = _loops("smooth_b")
     assert [m for _, m, *_ in L] == ["parallel", "parallel", "parallel", "gather", "parallel"]
     assert man["loops"][3]["gathered"] == ["ub"] and L[4][2] == set()
+    # a Tier-B tape: initstacks fills the prefix table and returns the total;
+    # the taping loop is parallel because each iteration owns its span of slots
+    man, L = _loops("ragged_b")
+    assert [m for _, m, *_ in L] == ["parallel", "parallel"]
+    assert L[0][2] == {"loss"} and L[1][2] == {"wb"}
+    assert man["initstacks"]["stacks"] == [
+        {"name": "v_stack", "dtype": "f64"}, {"name": "prefix_v_stack_1", "dtype": "i64_table"},
+        {"name": "__tot_v_stack_1", "dtype": "int"}]
 
 
 # ---- the emitted program, host build, against the interpreter -----------------------------
@@ -135,7 +143,8 @@ def test_host_build_matches_interpreter(name):
         r_ref, st_ref = _interp_run(name, ref)
         out = ec.copy_args(args)
         stacks = sw.initstacks(*ec.stack_ints(name, out))
-        assert [s.size for s in stacks] == [s.size for s in st_ref]
+        sig = lambda s: s if isinstance(s, (int, np.integer)) else ("array", s.size)
+        assert [sig(s) for s in stacks] == [sig(s) for s in st_ref]
         r_out = sw(*out.values(), *stacks)
         if gathered and r_ref is not None:   # the gathered values feed later statements
             assert np.allclose(r_out, r_ref, rtol=1e-13, atol=1e-13), (name, size)
@@ -183,7 +192,7 @@ def _primal_loss(I, name, args, wseed):
 
 
 @pytest.mark.parametrize("name", ["decay_b", "edge_relu_b", "bilin_b", "cumsum_sq_b",
-                                  "window_b", "smooth_b"])
+                                  "window_b", "smooth_b", "ragged_b"])
 def test_corpus_adjoint_is_the_derivative(name):
     size = ec.CASES[name][4][0]
     args = ec.make(name, size, "fd")
