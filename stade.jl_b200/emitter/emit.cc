@@ -672,12 +672,53 @@ class Emitter {
       : f_(f), init_(init), f32_(precision == 32) {
     T_ = f32_ ? "float" : "double";
     link(f_.body, nullptr);
+    scope_loop_vars();
     for (auto& p : f_.params) params_.insert(p);
     parse_dims(dims_spec);
     infer_kinds();
   }
 
   std::string cu, manifest;
+
+  // A Julia loop variable is local to its loop. Where a loop's variable name
+  // is also assigned outside that loop (transformer_b: `for i = 1:n` as a host
+  // loop, `i = div(...)` in a later kernel), the loop's own `i` is renamed
+  // `i__<line>` in its header and body, so that one name is one variable.
+  void scope_loop_vars() {
+    std::vector<Stmt*> loops;
+    walk_stmts(f_.body, [&](Stmt& x) {
+      if (x.kind == Stmt::For) loops.push_back(&x);
+    });
+    for (Stmt* F : loops) {
+      const std::string v = F->var;
+      bool outside = false;
+      walk_stmts(f_.body, [&](Stmt& x) {
+        if (x.kind != Stmt::Assign || x.lhs->kind != Expr::Var || x.lhs->s != v) return;
+        bool inside = false;
+        for (Stmt* o = x.owner; o; o = o->owner) inside = inside || o == F;
+        if (!inside) outside = true;
+      });
+      if (!outside) continue;
+      const std::string w = v + "__" + std::to_string(F->line);
+      F->var = w;
+      rename_in(F->body, v, w);
+    }
+  }
+  static void rename_expr(const EP& e, const std::string& v, const std::string& w) {
+    if (!e) return;
+    walk_expr(e, [&](const EP& x) {
+      if (x->kind == Expr::Var && x->s == v) x->s = w;
+    });
+  }
+  static void rename_in(std::vector<SP>& body, const std::string& v, const std::string& w) {
+    for (auto& sp : body) {
+      Stmt& x = *sp;
+      for (EP* e : {&x.lhs, &x.rhs, &x.cond, &x.lo, &x.hi, &x.step, &x.ret}) rename_expr(*e, v, w);
+      if (x.kind == Stmt::For && x.var == v) continue;   // an inner loop binds its own v
+      rename_in(x.body, v, w);
+      rename_in(x.els, v, w);
+    }
+  }
 
   void run() {
     items_ = plan_body(f_.body);

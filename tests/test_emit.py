@@ -268,3 +268,32 @@ def test_cli_and_cuda_file(tmp_path):
     assert m2 == m and (tmp_path / "b2.json").exists()
     bad = subprocess.run([exe, src, str(out)], capture_output=True, text=True)
     assert bad.returncode == 1 and "cannot infer dimension" in bad.stderr
+
+
+# ---- the reference's own generated adjoints, read as input text ----------------------------
+_REF_CORPUS = os.path.join(os.path.dirname(ROOT), "reference", "test", "val-corpus")
+
+
+@pytest.mark.skipif(not os.path.isdir(_REF_CORPUS), reason="the reference checkout is not here")
+def test_reference_corpus_emits():
+    """STADE's generated adjoints (its test corpus, read from the reference
+    checkout beside this repository): the emitter accepts all but those that
+    index a multi-dimensional argument whose leading extent no loop gives
+    (they need dims), and a sample of the emitted programs compiles."""
+    names = sorted(f for f in os.listdir(_REF_CORPUS) if f.endswith("_b.jl"))
+    accepted, refused = [], []
+    for f in names:
+        with open(os.path.join(_REF_CORPUS, f)) as fh:
+            src = fh.read()
+        try:
+            cu, _ = emit.emit(src)
+            accepted.append((f, cu))
+        except emit.EmitError as e:
+            refused.append((f, str(e)))
+    assert len(names) >= 139 and len(accepted) >= 131, refused
+    for f, msg in refused:
+        assert "cannot infer dimension" in msg, (f, msg)
+    for f, cu in accepted[::16]:
+        r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-DSTADE_EMIT_HOST", "-x", "c++",
+                            "-"], input=cu, capture_output=True, text=True)
+        assert r.returncode == 0, (f, r.stderr[-2000:])
