@@ -297,3 +297,40 @@ def test_reference_corpus_emits():
         r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-DSTADE_EMIT_HOST", "-x", "c++",
                             "-"], input=cu, capture_output=True, text=True)
         assert r.returncode == 0, (f, r.stderr[-2000:])
+
+
+@pytest.mark.skipif(not os.path.isdir(_REF_CORPUS), reason="the reference checkout is not here")
+def test_reference_tier_b_sweep():
+    """The reference's raggedind_b (a row length that grows with the row: a
+    Tier-B tape with prefix tables), emitted and built for the host: bit for
+    bit the interpreter's result and tables, and its x adjoint the central
+    difference of the primal raggedind (sizes from the primal's header: out
+    and u of length n, x of length m0 + n)."""
+    rd = lambda f: open(os.path.join(_REF_CORPUS, f)).read()
+    src = rd("raggedind_b.jl")
+    sw = emit.load(src, host=True)
+    assert [l["mode"] for l in sw.m["loops"]] == ["parallel", "parallel"]
+    n, m0 = 7, 3
+    r = np.random.default_rng(1)
+    args = dict(out=np.zeros(n), outb=r.standard_normal(n), u=r.standard_normal(n),
+                ub=np.zeros(n), x=r.standard_normal(m0 + n), xb=np.zeros(m0 + n))
+    ref = {k: v.copy() for k, v in args.items()}
+    I = jlsub.Interp(src)
+    st_ref = I.initstacks("initstacks_raggedind_b", m0, n)
+    I.call("raggedind_b", *ref.values(), n, m0, *st_ref)
+    out = {k: v.copy() for k, v in args.items()}
+    st = sw.initstacks(m0, n)
+    sw(*out.values(), n, m0, *st)
+    for k in args:
+        assert np.array_equal(out[k], ref[k]), k
+    for a, b in zip(st, st_ref):
+        assert np.array_equal(a, b)
+    P = jlsub.Interp(rd("raggedind.jl"))
+
+    def loss(x):
+        o = np.zeros(n)
+        P.call("raggedind", o, args["u"].copy(), x, n, m0)
+        return float(np.dot(o, args["outb"]))
+    v = r.standard_normal(m0 + n)
+    fd = (loss(args["x"] + 1e-6 * v) - loss(args["x"] - 1e-6 * v)) / 2e-6
+    assert abs(fd - float(np.dot(out["xb"], v))) <= 1e-6 * max(1.0, abs(fd))
