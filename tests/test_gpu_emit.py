@@ -3,7 +3,8 @@ sm_100a and called through its C ABI on device arrays, against the
 sequential interpreter (or, at the C1 / C3 sizes the interpreter is too slow
 for, the C++ oracle it is pinned to). Atomics reorder sums, so float arrays
 and returned scalars are compared with the Float64 bound 1e-12 (normwise
-relative); integer arrays and tapes bit for bit."""
+relative); integer arrays and tables bit for bit, float tapes within the same
+bound (a tape of tanh values holds the device's tanh, ulps from the host's)."""
 import numpy as np
 import pytest
 import torch
@@ -71,7 +72,11 @@ def test_emitted_sweep_on_gpu(name):
                 assert rel_err(got, ref[k]) <= 1e-12, (name, size, k, rel_err(got, ref[k]))
         for s_gpu, s_ref in zip(stacks, st_ref):
             got = s_gpu if isinstance(s_gpu, int) else s_gpu.cpu().numpy()
-            assert np.array_equal(got, s_ref), (name, size, "stack")
+            if isinstance(got, np.ndarray) and got.dtype.kind == "f" and got.size:
+                # taped values of device tanh / exp differ from the host's by ulps
+                assert rel_err(got, s_ref) <= 1e-12, (name, size, "stack")
+            else:
+                assert np.array_equal(got, s_ref), (name, size, "stack")
 
 
 def test_emitted_c1_matches_hand_written_sweep():
