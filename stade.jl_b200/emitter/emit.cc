@@ -860,6 +860,23 @@ class Emitter {
           ints_.insert(s.rhs->s);
           changed = true;
         }
+        // an integer assigned a sum / difference / product of variables and
+        // integer literals (`w = m0 + i_x`): those variables are integers too
+        if (lhs_int && s.rhs->kind == Expr::Bin) {
+          bool arith = true;
+          walk_expr(s.rhs, [&](const EP& x) {
+            if (x->kind == Expr::Bin && x->s != "+" && x->s != "-" && x->s != "*") arith = false;
+            if (x->kind == Expr::Num && !x->int_lit) arith = false;
+            if (x->kind != Expr::Bin && x->kind != Expr::Num && x->kind != Expr::Var) arith = false;
+          });
+          if (arith)
+            walk_expr(s.rhs, [&](const EP& x) {
+              if (x->kind == Expr::Var && !arrays_.count(x->s) && !ints_.count(x->s)) {
+                ints_.insert(x->s);
+                changed = true;
+              }
+            });
+        }
         if (lhs_int && s.rhs->kind == Expr::Ref && !int_arrays_.count(s.rhs->s)) {
           int_arrays_.insert(s.rhs->s);
           changed = true;
