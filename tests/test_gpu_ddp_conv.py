@@ -49,7 +49,7 @@ def _rank_main(rank, world, port, q):
         st["loss"][:] = 0
         st["wb"][:] = 0
         st["lossb"] = (st["lossb"] * np.float32(factor)).astype(np.float32)
-        for k in ("x",) + PER_SAMPLE:
+        for k in ("x", "t") + PER_SAMPLE:
             st[k] = np.ascontiguousarray(st[k][rows.start * _per(k):rows.stop * _per(k)])
         dev = {k: torch.from_numpy(v).cuda() for k, v in st.items()}
         stadeb200.conv1d_relu_mse_b_cuda(*[dev[a] for a in cases.CONV_ARGS], len(rows),
