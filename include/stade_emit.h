@@ -29,6 +29,18 @@
  * An argument initstacks reads only through length(a) is passed as that
  * length (the manifest lists these as "length_args").
  *
+ * An array the sweep allocates at its top level in Julia (an HVP sweep's
+ * tangent of a tape, `du_stack_d = Vector{Float64}(undef, length(du_stack))`)
+ * becomes a trailing argument of stade_<k>, after the generated ones; the
+ * caller allocates it. Its size comes from
+ *
+ *   int64_t stade_<k>_locals(<integer arguments>, <lengths of the arrays the
+ *                            sizes read through length()>, int64_t* sizes,
+ *                            int* dtypes);
+ *
+ * (dtype 0 / 1 / 2 as for stacks; the manifest's "locals" names them). An
+ * HVP sweep <k>_hv takes its stacks from initstacks_<k>_b.
+ *
  * The manifest (JSON) lists the arguments with their kinds, the stacks, the
  * returned scalars and one record per loop: parallel kernel (thread per
  * iteration, with the arrays and scalars it updates by atomics and the

@@ -673,6 +673,7 @@ class Emitter {
     T_ = f32_ ? "float" : "double";
     link(f_.body, nullptr);
     scope_loop_vars();
+    hoist_local_arrays();
     for (auto& p : f_.params) params_.insert(p);
     parse_dims(dims_spec);
     infer_kinds();
@@ -718,6 +719,81 @@ class Emitter {
       rename_in(x.body, v, w);
       rename_in(x.els, v, w);
     }
+  }
+
+  // An array the sweep allocates itself at its top level (an HVP sweep's
+  // tangent of a tape, `du_stack_d = Vector{Float64}(undef, length(du_stack))`)
+  // becomes a trailing argument that the caller allocates: the library never
+  // allocates. stade_<k>_locals gives the sizes.
+  struct LocalArray {
+    std::string name, type;
+    EP size;
+  };
+  std::vector<LocalArray> locals_;
+  void hoist_local_arrays() {
+    std::vector<SP> kept;
+    for (auto& sp : f_.body) {
+      Stmt& s = *sp;
+      if (s.kind == Stmt::Assign && s.lhs->kind == Expr::Var && s.rhs->kind == Expr::Curly) {
+        if (s.rhs->a.size() != 2) fail(s.line, "expected Vector{T}(undef, n)");
+        locals_.push_back({s.lhs->s, s.rhs->s, s.rhs->a[1]});
+        f_.params.push_back(s.lhs->s);
+        arrays_.insert(s.lhs->s);
+        if (s.rhs->s.find("Int") != std::string::npos) int_arrays_.insert(s.lhs->s);
+        continue;
+      }
+      kept.push_back(sp);
+    }
+    if (locals_.empty()) return;
+    f_.body = kept;
+    link(f_.body, nullptr);
+  }
+
+  // stade_<k>_locals(<integer arguments>, <lengths of the arrays the sizes
+  // read through length()>, sizes, dtypes): the sizes of the hoisted arrays
+  std::string locals_src(std::string& mf) {
+    if (locals_.empty()) {
+      mf = "null";
+      return "";
+    }
+    std::set<std::string> lens;
+    for (auto& l : locals_)
+      walk_expr(l.size, [&](const EP& x) {
+        if (x->kind == Expr::Call && x->s == "length" && x->a.size() == 1 &&
+            x->a[0]->kind == Expr::Var)
+          lens.insert(x->a[0]->s);
+      });
+    std::ostringstream q;
+    std::string ia, la;
+    q << "extern \"C\" int64_t stade_" << f_.name << "_locals(";
+    for (auto& p : f_.params)
+      if (!arrays_.count(p) && ints_.count(p)) {
+        q << "int64_t " << cname(p) << ", ";
+        ia += std::string(ia.empty() ? "" : ", ") + jstr(p);
+      }
+    for (auto& p : f_.params)
+      if (lens.count(p)) {
+        q << "int64_t " << cname(p) << ", ";
+        la += std::string(la.empty() ? "" : ", ") + jstr(p);
+      }
+    q << "int64_t* sizes, int* dtypes) {\n";
+    std::set<std::string> loc(f_.params.begin(), f_.params.end());
+    std::string ms;
+    init_printing_ = true;
+    for (size_t i = 0; i < locals_.size(); ++i) {
+      const auto& l = locals_[i];
+      const int code = l.type.find("Int") != std::string::npos ? 2 : (f32_ ? 1 : 0);
+      q << "  if (sizes) sizes[" << i << "] = jl_imax((int64_t)0, (int64_t)("
+        << cx(l.size, loc, 0) << "));\n";
+      q << "  if (dtypes) dtypes[" << i << "] = " << code << ";\n";
+      ms += std::string(ms.empty() ? "" : ", ") + "{\"name\": " + jstr(l.name) + ", \"dtype\": " +
+            jstr(code == 2 ? "i64" : (code == 1 ? "f32" : "f64")) + "}";
+    }
+    init_printing_ = false;
+    q << "  return " << locals_.size() << ";\n}\n";
+    mf = "{\"symbol\": " + jstr("stade_" + f_.name + "_locals") + ", \"args\": [" + ia +
+         "], \"length_args\": [" + la + "], \"arrays\": [" + ms + "]}";
+    return q.str();
   }
 
   void run() {
@@ -2634,9 +2710,12 @@ class Emitter {
         decl.push_back(T_ + " " + cname(p));
         kind = "scalar_float";
       }
+      bool local = false;
+      for (auto& l : locals_) local = local || l.name == p;
       mf_args += std::string(mf_args.empty() ? "" : ", ") + "{\"name\": " + jstr(p) +
                  ", \"kind\": " + jstr(kind) + ", \"stack\": " +
-                 (stacks_.count(p) ? "true" : "false") + "}";
+                 (stacks_.count(p) ? "true" : "false") + ", \"local\": " +
+                 (local ? "true" : "false") + "}";
     }
     for (size_t i = 0; i < decl.size(); ++i) o << decl[i] << ", ";
     o << "void* stream) {\n";
@@ -2657,6 +2736,8 @@ class Emitter {
     }
     o << "  return 0;\n}\n\n";
     o << "extern \"C\" int64_t stade_" << f_.name << "_launches(void) { return stade_launches_; }\n\n";
+    std::string mf_locals;
+    o << locals_src(mf_locals);
     // initstacks
     std::string mf_stacks = "[]", init_sym = "null", init_args = "[]";
     if (init_) {
@@ -2680,7 +2761,7 @@ class Emitter {
                ", \"precision\": " + jstr(f32_ ? "f32" : "f64") + ", \"args\": [" + mf_args +
                "], \"returns\": " + jlist(ret_order) + ", \"initstacks\": {\"symbol\": " + init_sym +
                ", \"args\": " + init_args + ", \"length_args\": " + init_len_args_ +
-               ", \"stacks\": " + mf_stacks + "}, \"kernels\": " +
+               ", \"stacks\": " + mf_stacks + "}, \"locals\": " + mf_locals + ", \"kernels\": " +
                std::to_string(units_.size()) + ", \"loops\": [\n  " + dec + "]}\n";
   }
 
@@ -3108,9 +3189,16 @@ static int emit_impl(const char* source, const char* function, int precision, co
         }
     if (!f) throw Error("no sweep function in the source");
   }
+  // an HVP sweep <k>_hv takes the stacks of the adjoint's initstacks_<k>_b
+  std::string base = f->name;
+  if (base.size() > 3 && base.compare(base.size() - 3, 3, "_hv") == 0)
+    base = base.substr(0, base.size() - 3) + "_b";
   const Func* init = nullptr;
   for (auto& x : fs)
     if (x.name == "initstacks_" + f->name) init = &x;
+  if (!init)
+    for (auto& x : fs)
+      if (x.name == "initstacks_" + base) init = &x;
   Emitter e(*f, init, precision, dims ? dims : "");
   e.run();
   cu = e.cu;

@@ -241,8 +241,38 @@ class Sweep:
             raise TypeError(f"{spec['name']}: expected a contiguous CUDA {want} tensor")
         return a.data_ptr()
 
+    def local_arrays(self, *args, device="cuda"):
+        """The arrays the sweep allocates for itself in Julia (hoisted to
+        trailing arguments), zero-filled, sized by stade_<k>_locals from the
+        sweep's other arguments (everything but these locals, in order)."""
+        loc = self.m.get("locals")
+        if not loc:
+            return ()
+        import numpy as np
+        by_name = dict(zip([a["name"] for a in self.m["args"]], args))
+        f = getattr(self.lib, loc["symbol"])
+        f.restype = C.c_int64
+        vals = [int(by_name[n]) for n in loc["args"]]
+        for n in loc["length_args"]:
+            a = by_name[n]
+            vals.append(a.numel() if hasattr(a, "numel") else int(np.asarray(a).size))
+        n = len(loc["arrays"])
+        sizes = (C.c_int64 * n)()
+        dts = (C.c_int * n)()
+        f.argtypes = [C.c_int64] * len(vals) + [C.POINTER(C.c_int64), C.POINTER(C.c_int)]
+        f(*vals, sizes, dts)
+        kinds = ("float64", "float32", "int64")
+        if self.host:
+            return tuple(np.zeros(sizes[i], kinds[dts[i]]) for i in range(n))
+        import torch
+        return tuple(torch.zeros(sizes[i], dtype=getattr(torch, kinds[dts[i]]), device=device)
+                     for i in range(n))
+
     def __call__(self, *args, stream=None):
         specs = self.m["args"]
+        n_local = sum(1 for a in specs if a.get("local"))
+        if n_local and len(args) == len(specs) - n_local:
+            args = tuple(args) + self.local_arrays(*args)
         if len(args) != len(specs):
             raise TypeError(f"{self.m['function']} takes {len(specs)} arguments, got {len(args)}")
         cargs, boxes = [], {}

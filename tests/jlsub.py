@@ -45,6 +45,9 @@ def tokenize(src):
             continue
         else:
             out.append((kind, text, line))
+            # a numeric literal coefficient (`0.5x`, `2(a + b)`) multiplies
+            if kind == "num" and pos < len(src) and (src[pos].isalpha() or src[pos] in "_("):
+                out.append(("op", "jux", line))
     out.append(("nl", "\n", line))
     out.append(("eof", "", line))
     return out
@@ -222,7 +225,13 @@ class _P:
             if op == "-" and e[0] == "num":
                 return ("num", -e[1])
             return ("un", op, e)
+        return self.power()
+
+    def power(self):
         b = self.postfix()
+        if b[0] == "num" and self.op("jux"):   # binds tighter than * and /, looser than ^
+            self.next()
+            return ("bin", "*", b, self.power())
         if self.op("^"):
             self.next()
             return ("bin", "^", b, self.unary())
