@@ -372,3 +372,31 @@ def test_reference_hvp_sweep():
     for k, v in a.items():
         if isinstance(v, np.ndarray):
             assert np.allclose(out[k], ref[k], rtol=1e-13, atol=1e-13), k
+
+
+@pytest.mark.skipif(not os.path.isdir(_REF_CORPUS), reason="the reference checkout is not here")
+def test_reference_tangent_sweep():
+    """The reference's advection_d (forward mode), emitted and built for the
+    host: bit for bit the interpreter, and its tangent ud the central
+    difference of the primal advection along (ud, cd, dxd, dtd)."""
+    src = open(os.path.join(_REF_CORPUS, "advection_d.jl")).read()
+    sw = emit.load(src, host=True)
+    nn, ns = 9, 4
+    r = np.random.default_rng(3)
+    u0, ud0 = r.standard_normal(nn), r.standard_normal(nn)
+    c, dx, dt, cd, dxd, dtd = 0.7, 0.5, 0.05, 0.3, -0.2, 0.4
+    out = dict(u=u0.copy(), ud=ud0.copy(), du=np.zeros(nn), dud=np.zeros(nn))
+    ref = {k: v.copy() for k, v in out.items()}
+    jlsub.Interp(src).call("advection_d", ref["u"], ref["ud"], ref["du"], ref["dud"], c, cd, dx,
+                           dxd, dt, dtd, ns, nn)
+    sw(out["u"], out["ud"], out["du"], out["dud"], c, cd, dx, dxd, dt, dtd, ns, nn)
+    for k in out:
+        assert np.array_equal(out[k], ref[k]), k
+    P = jlsub.Interp(src)
+
+    def prim(h):
+        u = u0 + h * ud0
+        P.call("advection", u, np.zeros(nn), c + h * cd, dx + h * dxd, dt + h * dtd, ns, nn)
+        return u
+    fd = (prim(1e-6) - prim(-1e-6)) / 2e-6
+    assert np.max(np.abs(fd - out["ud"])) <= 1e-6 * max(1.0, np.max(np.abs(fd)))
