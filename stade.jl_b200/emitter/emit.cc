@@ -1026,6 +1026,62 @@ class Emitter {
 
   // leading dimensions of a multi-dimensional array: given, or the upper
   // bound of a `for v = 1:hi` whose variable is that subscript
+  // The extent of a variable decoded from a flattened nest, the generators'
+  // canonical form (`for idx = 1:A * n; i = div(idx - 1, n) + 1;
+  // j = mod(idx - 1, n) + 1`): A for i, n for j. Null when v is not one.
+  EP decoded_extent(const std::string& v) {
+    std::map<std::string, std::vector<EP>> all;
+    walk_stmts(f_.body, [&](Stmt& s) {
+      if (s.kind == Stmt::Assign && s.lhs->kind == Expr::Var) all[s.lhs->s].push_back(s.rhs);
+    });
+    auto one = [&](const std::string& name) -> EP {   // a temporary assigned one text
+      auto f = all.find(name);
+      if (f == all.end()) return nullptr;
+      for (auto& e : f->second)
+        if (text(e) != text(f->second[0])) return nullptr;
+      return f->second[0];
+    };
+    // the top H of the range 1..H of loop variable idx (1:H or H:-1:1), one for all its loops
+    auto top = [&](const std::string& idx) -> EP {
+      EP h;
+      bool ok = true;
+      walk_stmts(f_.body, [&](Stmt& s) {
+        if (s.kind != Stmt::For || s.var != idx) return;
+        EP t;
+        if (!s.step && s.lo->kind == Expr::Num && s.lo->s == "1") t = s.hi;
+        else if (s.step && text(s.step) == "-1" && s.hi->kind == Expr::Num && s.hi->s == "1") t = s.lo;
+        if (!t || (h && text(h) != text(t))) ok = false;
+        if (t) h = t;
+      });
+      return ok ? h : nullptr;
+    };
+    auto extent = [&](const EP& r) -> EP {
+      if (r->kind != Expr::Bin || r->s != "+" || r->a[1]->kind != Expr::Num || r->a[1]->s != "1")
+        return nullptr;
+      const EP& c = r->a[0];
+      if (c->kind != Expr::Call || (c->s != "div" && c->s != "mod") || c->a.size() != 2)
+        return nullptr;
+      EP x = c->a[0];
+      const EP& n = c->a[1];
+      if (x->kind == Expr::Var) x = one(x->s);
+      if (!x || x->kind != Expr::Bin || x->s != "-" || x->a[0]->kind != Expr::Var ||
+          x->a[1]->kind != Expr::Num || x->a[1]->s != "1")
+        return nullptr;
+      EP h = top(x->a[0]->s);
+      if (!h || h->kind != Expr::Bin || h->s != "*" || text(h->a[1]) != text(n)) return nullptr;
+      return c->s == "div" ? h->a[0] : n;
+    };
+    auto it = all.find(v);
+    if (it == all.end()) return nullptr;
+    EP first;
+    for (auto& r : it->second) {
+      EP e = extent(r);
+      if (!e || (first && text(first) != text(e))) return nullptr;
+      first = e;
+    }
+    return first;
+  }
+
   std::vector<EP> dims_of(const std::string& a, size_t rank, int line) {
     auto it = dims_.find(a);
     if (it != dims_.end()) {
@@ -1033,11 +1089,13 @@ class Emitter {
       return it->second;
     }
     std::vector<EP> d(rank - 1);
+    std::vector<std::set<std::string>> seen(rank - 1);
     walk_stmts(f_.body, [&](Stmt& s) {
       std::function<void(const EP&)> look = [&](const EP& e) {
         walk_expr(e, [&](const EP& x) {
           if (x->kind != Expr::Ref || x->s != a || x->a.size() != rank) return;
           for (size_t k = 0; k + 1 < rank; ++k) {
+            if (x->a[k]->kind == Expr::Var) seen[k].insert(x->a[k]->s);
             if (d[k] || x->a[k]->kind != Expr::Var) continue;
             // find the enclosing loop of that variable
             for (Stmt* o = &s; o; o = o->owner)
@@ -1052,6 +1110,9 @@ class Emitter {
       for (const EP* e : {&s.lhs, &s.rhs, &s.cond})
         if (*e) look(*e);
     });
+    for (size_t k = 0; k + 1 < rank; ++k)
+      for (auto& v : seen[k])
+        if (!d[k]) d[k] = decoded_extent(v);
     for (size_t k = 0; k + 1 < rank; ++k)
       if (!d[k])
         fail(line, "cannot infer dimension " + std::to_string(k + 1) + " of " + a +

@@ -266,7 +266,15 @@ def test_cli_and_cuda_file(tmp_path):
     assert m["symbol"] == "stade_bilin_b" and "extern \"C\" int stade_bilin_b(" in out.read_text()
     m2 = emit.cuda_file(src, str(tmp_path / "b2.cu"), dims={"a": ["i_m"], "ab": ["i_m"]})
     assert m2 == m and (tmp_path / "b2.json").exists()
-    bad = subprocess.run([exe, src, str(out)], capture_output=True, text=True)
+    # without --dims the leading extent comes from the flattened nest's decode
+    inferred = tmp_path / "bilin_inferred.cu"
+    subprocess.run([exe, src, str(inferred)], check=True)
+    assert inferred.read_text() == out.read_text()
+    # an extent nothing gives is refused with a pointer to --dims
+    odd = tmp_path / "odd_b.jl"
+    odd.write_text("function odd_b(a, ab, i_r, i_c)\n    for k = 1:i_c\n"
+                   "        ab[i_r, k] = ab[i_r, k] + a[i_r, k]\n    end\nend\n")
+    bad = subprocess.run([exe, str(odd), str(out)], capture_output=True, text=True)
     assert bad.returncode == 1 and "cannot infer dimension" in bad.stderr
 
 
@@ -275,12 +283,13 @@ _REF_CORPUS = os.path.join(os.path.dirname(ROOT), "reference", "test", "val-corp
 
 
 @pytest.mark.skipif(not os.path.isdir(_REF_CORPUS), reason="the reference checkout is not here")
-@pytest.mark.parametrize("suffix,least", [("_b", 131), ("_hv", 131), ("_d", 134)])
+@pytest.mark.parametrize("suffix,least", [("_b", 133), ("_hv", 133), ("_d", 136)])
 def test_reference_corpus_emits(suffix, least):
     """STADE's generated adjoints, HVP and tangent sweeps (its test corpus,
     read from the reference checkout beside this repository): the emitter
     accepts all but those that index a multi-dimensional argument whose
-    leading extent no loop gives (they need dims) and two tangents that
+    leading extent neither a loop nor a flattened nest's decode gives (they
+    need dims) and two tangents that
     reassign an integer argument inside device loops; a sample of the
     emitted programs compiles."""
     names = sorted(f for f in os.listdir(_REF_CORPUS) if f.endswith(suffix + ".jl"))
@@ -400,3 +409,24 @@ def test_reference_tangent_sweep():
         return u
     fd = (prim(1e-6) - prim(-1e-6)) / 2e-6
     assert np.max(np.abs(fd - out["ud"])) <= 1e-6 * max(1.0, np.max(np.abs(fd)))
+
+
+@pytest.mark.skipif(not os.path.isdir(_REF_CORPUS), reason="the reference checkout is not here")
+def test_reference_flattened_nest_extent():
+    """The reference's matvec_loss_b indexes a[i_i, i_j] with i_i, i_j decoded
+    from one flattened loop over 1:i_m * i_n (div / mod by i_n): the emitter
+    takes a's leading extent i_m from that decode, and the host build agrees
+    bit for bit with the interpreter given a = i_m x i_n explicitly."""
+    src = open(os.path.join(_REF_CORPUS, "matvec_loss_b.jl")).read()
+    sw = emit.load(src, host=True)
+    m, n = 5, 3
+    r = np.random.default_rng(4)
+    a = dict(loss=np.zeros(1), lossb=np.ones(1), a=r.standard_normal(m * n), ab=np.zeros(m * n),
+             u=r.standard_normal(n), ub=np.zeros(n), v=np.zeros(m), vb=np.zeros(m))
+    ref = {k: v.copy() for k, v in a.items()}
+    jlsub.Interp(src, 64, {"a": ["i_m"], "ab": ["i_m"]}).call("matvec_loss_b", *ref.values(), m, n)
+    out = {k: v.copy() for k, v in a.items()}
+    sw(*out.values(), m, n)
+    for k in a:
+        assert np.array_equal(out[k], ref[k]), k
+    assert np.any(out["ab"] != 0)
