@@ -27,7 +27,8 @@
  *              sizes[i] elements: with fill non-NULL and fill[i] a host buffer
  *              of that size, its contents are written there.
  * An argument initstacks reads only through length(a) is passed as that
- * length (the manifest lists these as "length_args").
+ * length (the manifest lists these as "length_args"). It returns -1 when a
+ * table write falls outside the table.
  *
  * An array the sweep allocates at its top level in Julia (an HVP sweep's
  * tangent of a tape, `du_stack_d = Vector{Float64}(undef, length(du_stack))`)

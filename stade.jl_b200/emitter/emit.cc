@@ -2941,9 +2941,12 @@ class Emitter {
             q << pad << cname(s.lhs->s) << " = " << cast_to(s.lhs->s, cx(s.rhs, locals, s.line))
               << ";\n";
           } else {
-            q << pad << cx(s.lhs, locals, s.line) << " = "
-              << (int_arrays_.count(s.lhs->s) ? "(int64_t)" : "(" + T_ + ")")
-              << cx(s.rhs, locals, s.line) << ";\n";
+            // a table write outside the table's size makes the call fail (-1)
+            const std::string& a = s.lhs->s;
+            q << pad << "{\n" << pad << "  const int64_t o_ = " << offset(s.lhs, locals, s.line)
+              << ";\n" << pad << "  if (o_ < 0 || o_ >= n_" << a << ") return -1;\n" << pad
+              << "  p_" << a << "[o_] = " << (int_arrays_.count(a) ? "(int64_t)" : "(" + T_ + ")")
+              << cx(s.rhs, locals, s.line) << ";\n" << pad << "}\n";
           }
           break;
         case Stmt::For: {

@@ -193,6 +193,8 @@ class Sweep:
         sizes = (C.c_int64 * max(n, 1))()
         dts = (C.c_int * max(n, 1))()
         got = self.init(*self._init_args(args), sizes, dts, None)
+        if got < 0:
+            raise EmitError(f"{ini['symbol']}: a table write fell outside its table")
         kinds = ("float64", "float32", "int64", "int", "int64_table", "float_table")
         return [(int(sizes[i]), kinds[dts[i]]) for i in range(got)]
 
@@ -214,7 +216,8 @@ class Sweep:
                 fill[i] = a.ctypes.data
             host.append(a)
         if any(k.endswith("_table") for _, k in items):
-            self.init(*self._init_args(args), None, None, fill)
+            if self.init(*self._init_args(args), None, None, fill) < 0:
+                raise EmitError(f"{self.m['initstacks']['symbol']}: a table write fell outside its table")
         if self.host:
             return tuple(host)
         import torch
