@@ -71,6 +71,10 @@ const char* stade_last_error(void);          /* thread-local message of the last
 const char* stade_version(void);
 int         stade_kernel_launches(void);     /* kernels this thread launched since the last reset */
 void        stade_reset_kernel_launches(void);
+/* Bytes of the library-managed workspace cache on the current device (0 when
+ * no entry point has needed one there: every call so far passed its own
+ * workspace or needed none). */
+size_t      stade_workspace_cached_bytes(void);
 /* Phase profiler (tracing): when enabled, entry points bracket each phase
  * with CUDA events on their stream; stade_profile_read waits for them and
  * sums device milliseconds per phase name (names: max entries of name_len
@@ -106,9 +110,11 @@ stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
  * a workspace: the per-block partial sums live in a fixed 2 MiB array in the
  * library's own device memory, held by every GPU that loads the library until
  * the process exits. The call makes no cudaMalloc, cudaFree or other
- * allocating call; opts->workspace is ignored. The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) with that device
- * current, so make that first call before any stream capture. Sizes whose
+ * allocating call; opts->workspace is ignored. Every call looks up the
+ * array's device address on the current device (cudaGetSymbolAddress, a query
+ * that allocates nothing), so a cudaDeviceReset between calls is harmless; the
+ * first call on a device also loads the library's device code there, so make
+ * that first call before any stream capture. Sizes whose
  * partial sums exceed the array (stade_affine_ls_b_f64_noalloc_max_scratch()
  * bytes; the full 1024 x 64 x 32 configuration needs 1.03 MiB) return
  * STADE_EINVAL. All calls share the one array: calls that overlap on the GPU

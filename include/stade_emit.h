@@ -42,6 +42,13 @@
  * (dtype 0 / 1 / 2 as for stacks; the manifest's "locals" names them). An
  * HVP sweep <k>_hv takes its stacks from initstacks_<k>_b.
  *
+ * Calls of one emitted sweep share its file-scope device boxes (the boxed
+ * scalars and the returned scalar adjoints live in one __device__ array per
+ * emitted library): order the calls of one sweep on one stream, or put events
+ * between streams. Two calls that overlap on the GPU race on the boxes, and
+ * one can read back the other's returned scalars. Different emitted sweeps
+ * have separate boxes.
+ *
  * The manifest (JSON) lists the arguments with their kinds, the stacks, the
  * returned scalars and one record per loop: parallel kernel (thread per
  * iteration, with the arrays and scalars it updates by atomics and the

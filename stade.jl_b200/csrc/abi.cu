@@ -131,6 +131,13 @@ const char* stade_version(void) { return "libstade_b200 0.1 (sm_100a)"; }
 int stade_kernel_launches(void) { return stade::g_launches; }
 void stade_reset_kernel_launches(void) { stade::g_launches = 0; }
 
+size_t stade_workspace_cached_bytes(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(stade::g_ws_mutex);
+  return dev < (int)stade::g_ws.size() ? stade::g_ws[dev].bytes : 0;
+}
+
 void stade_profile_enable(int on) { stade::g_prof = on != 0; }
 
 // Sums the recorded phases by name (in first-seen order) into names / ms /

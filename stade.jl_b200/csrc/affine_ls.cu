@@ -15,7 +15,6 @@
 //
 // y, tb and xb follow the oracle's statement order with separate multiply and
 // add roundings (no FMA contraction), so they match it bit for bit.
-#include <mutex>
 
 #include "common.cuh"
 
@@ -177,8 +176,8 @@ extern "C" stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
 // size and pass a workspace. This entry point takes its scratch (the per-block
 // partial sums) from a fixed array that lives in the library's own device
 // memory instead, so it calls no cudaMalloc, cudaFree or allocating library
-// routine. The array is created when the library is loaded on a device and
-// is held until the process exits.
+// routine. The array is created when the library's device code is loaded on
+// a device and is held until the process exits.
 namespace stade {
 namespace {
 
@@ -186,25 +185,17 @@ namespace {
 constexpr size_t kNoAllocScratchDoubles = (size_t(2) << 20) / sizeof(double);
 static __device__ __align__(256) double g_affine_noalloc_scratch[kNoAllocScratchDoubles];
 
-constexpr int kMaxDevices = 64;
-double* g_noalloc_ptr[kMaxDevices] = {};
-std::mutex g_noalloc_mutex;
-
-// Device address of the scratch array on the current device. The name of a
-// __device__ array in host code is only a host-side stand-in, never a device
-// address, so it is looked up once per device with that device current.
+// Device address of the scratch array on the current device. In host code the
+// array's name is only a host-side stand-in, never a device address, so the
+// address is looked up with the device current. The lookup is a query (it
+// allocates nothing) and runs on every call, so a cudaDeviceReset between
+// calls, which reloads the library's device code at a new address, is
+// harmless; the first call on a device also loads that code there.
 stade_status noalloc_scratch(double** out) {
-  int dev = 0;
-  STADE_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices) return fail(STADE_ENOTSUP, "device ordinal %d too large", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_affine_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress", __FILE__, __LINE__);
-    g_noalloc_ptr[dev] = static_cast<double*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_affine_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress", __FILE__, __LINE__);
+  *out = static_cast<double*>(p);
   return STADE_OK;
 }
 
@@ -244,6 +235,7 @@ extern "C" stade_status stade_affine_ls_b_f64_noalloc(double* loss, const double
   if (p.smem > 48 * 1024)
     STADE_CUDA(cudaFuncSetAttribute(affine_ls_chunk_kernel,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+  PhaseScope ph("affine", s);
   // every block writes all of its partial slots, so nothing needs clearing
   affine_ls_chunk_kernel<<<p.nblk, kThreads, p.smem, s>>>(lossb, w, b, x, xb, t, tb, y, yb, n_s,
                                                           (int)n_o, (int)n_i, p.chunk, part);

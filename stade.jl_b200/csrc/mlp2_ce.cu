@@ -25,7 +25,7 @@
 #include "common.cuh"
 #include "gemm_dmma.cuh"
 #include "gemm_simt.cuh"
-#include "tc_gemm.cuh"
+#include "tc_tma.cuh"
 #include "tcgen05.cuh"
 
 namespace stade {
@@ -351,105 +351,6 @@ mlp_head_small_kernel(const T* __restrict__ zpart, int nchunks, const T* __restr
   }
   loss_acc = block_sum(loss_acc, red);
   if (threadIdx.x == 0) loss_part[blockIdx.x] = loss_acc;
-}
-
-// One pass over h and hb (tensor-core path): s1b = (1 - h^2) (hb + sum_c
-// w2[k, c] g[s, c]) with c descending (the generated order), hb consumed to
-// zero, and the W2b / b2b partials of the chunk (sum_s h[s,k] g[s,c],
-// sum_s g[s,c]). Block (x = chunk of samples, y = 512 hidden units), two
-// adjacent units per thread. Partial layout as mlp_w2b_partial_kernel.
-// PLANES: write s1b as TF32 hi / lo planes (s1b = hi plane, s1b_lo = lo
-// plane) and add the chunk's b1b partial (sum_s s1b[s,k]) after the b2b
-// entries of the partial record.
-template <int NO, bool PLANES>
-__global__ void __launch_bounds__(256)
-mlp_s1b_w2b_kernel(const float* __restrict__ h, float* __restrict__ hb,
-                   const float* __restrict__ gbuf, const float* __restrict__ w2,
-                   float* __restrict__ s1b, float* __restrict__ s1b_lo, int n_s, int n_h, int n_o,
-                   int chunk, float* __restrict__ part) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  float* gs = reinterpret_cast<float*>(smraw);  // chunk x n_o
-  const int s0 = blockIdx.x * chunk;
-  const int s1 = min(n_s, s0 + chunk);
-  const int ns = s1 - s0;
-  for (int e = threadIdx.x; e < ns * n_o; e += blockDim.x) gs[e] = gbuf[(int64_t)s0 * n_o + e];
-  __syncthreads();
-  float* my = part + (int64_t)blockIdx.x * (n_h * n_o + n_o + (PLANES ? n_h : 0));
-  const int k = blockIdx.y * 512 + 2 * threadIdx.x;
-  if (k < n_h) {
-    float wr0[NO], wr1[NO], a0[NO], a1[NO];
-    float2 bsum = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int c = 0; c < NO; ++c) {
-      wr0[c] = c < n_o ? w2[(int64_t)k * n_o + c] : 0.f;
-      wr1[c] = c < n_o ? w2[(int64_t)(k + 1) * n_o + c] : 0.f;
-      a0[c] = 0.f;
-      a1[c] = 0.f;
-    }
-    // four samples per iteration: eight independent 8-byte loads in flight
-    auto one = [&](int i, float2 hv, float2 acc) {
-      const int64_t off = (int64_t)(s0 + i) * n_h + k;
-      const float* g = gs + i * n_o;
-#pragma unroll
-      for (int c = NO - 1; c >= 0; --c) {
-        if (c < n_o) {
-          const float gc = g[c];
-          acc.x = __fadd_rn(acc.x, __fmul_rn(wr0[c], gc));
-          acc.y = __fadd_rn(acc.y, __fmul_rn(wr1[c], gc));
-          a0[c] = fmaf(hv.x, gc, a0[c]);
-          a1[c] = fmaf(hv.y, gc, a1[c]);
-        }
-      }
-      float2 o;
-      o.x = __fmul_rn(__fadd_rn(1.f, -__fmul_rn(hv.x, hv.x)), acc.x);
-      o.y = __fmul_rn(__fadd_rn(1.f, -__fmul_rn(hv.y, hv.y)), acc.y);
-      if constexpr (PLANES) {
-        bsum.x += o.x;
-        bsum.y += o.y;
-        float2 hi;
-        hi.x = __uint_as_float(__float_as_uint(o.x) & 0xFFFFE000u);
-        hi.y = __uint_as_float(__float_as_uint(o.y) & 0xFFFFE000u);
-        *reinterpret_cast<float2*>(s1b + off) = hi;
-        *reinterpret_cast<float2*>(s1b_lo + off) = make_float2(o.x - hi.x, o.y - hi.y);
-      } else {
-        *reinterpret_cast<float2*>(s1b + off) = o;
-      }
-      *reinterpret_cast<float2*>(hb + off) = make_float2(0.f, 0.f);
-    };
-    int i = 0;
-    for (; i + 4 <= ns; i += 4) {
-      float2 hv[4], hbv[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t off = (int64_t)(s0 + i + u) * n_h + k;
-        hv[u] = *reinterpret_cast<const float2*>(h + off);
-        hbv[u] = *reinterpret_cast<const float2*>(hb + off);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) one(i + u, hv[u], hbv[u]);
-    }
-    for (; i < ns; ++i) {
-      const int64_t off = (int64_t)(s0 + i) * n_h + k;
-      one(i, *reinterpret_cast<const float2*>(h + off), *reinterpret_cast<const float2*>(hb + off));
-    }
-#pragma unroll
-    for (int c = 0; c < NO; ++c) {
-      if (c < n_o) {
-        my[(int64_t)k * n_o + c] = a0[c];
-        my[(int64_t)(k + 1) * n_o + c] = a1[c];
-      }
-    }
-    if constexpr (PLANES) {
-      my[(int64_t)n_h * n_o + n_o + k] = bsum.x;
-      my[(int64_t)n_h * n_o + n_o + k + 1] = bsum.y;
-    }
-  }
-  if (blockIdx.y == 0 && threadIdx.x < n_o) {
-    const int c = threadIdx.x;
-    float acc = 0.f;
-    for (int i = 0; i < ns; ++i) acc += gs[i * n_o + c];
-    my[n_h * n_o + c] = acc;
-  }
 }
 
 // The s1b pass of the TMA path, two adjacent hidden units per thread (8-byte
@@ -1077,14 +978,13 @@ struct MlpF32Ws {
   int head_blocks, w2_chunks, w1_splits;
 };
 
-// Contraction path of the Float32 adjoint: TMA-fed tcgen05 (default),
-// transform-fed tcgen05, or CUDA-core SIMT. STADE_MLP_GEMM = tma | tc | simt.
-enum class MlpPath { Tma, Tc, Simt };
+// Contraction path of the Float32 adjoint: TMA-fed tcgen05 (default) or
+// CUDA-core SIMT (sizes TMA cannot describe; STADE_MLP_GEMM=simt forces it).
+enum class MlpPath { Tma, Simt };
 MlpPath mlp_path(int64_t n_s, int64_t n_i, int64_t n_h) {
-  if (!tc_mlp_supported(n_s, n_i, n_h)) return MlpPath::Simt;
+  if (!tma_mlp_supported(n_s, n_i, n_h)) return MlpPath::Simt;
   const char* sel = std::getenv("STADE_MLP_GEMM");
   if (sel && std::strcmp(sel, "simt") == 0) return MlpPath::Simt;
-  if (sel && std::strcmp(sel, "tc") == 0) return MlpPath::Tc;
   return MlpPath::Tma;
 }
 template <class Alloc>
@@ -1105,8 +1005,8 @@ void mlp_f32_layout(Alloc& a, MlpF32Ws* w, int64_t n_s, int64_t n_i, int64_t n_h
   auto lp = a.template take<float>((size_t)head_parts);
   auto w2p = a.template take<float>((size_t)w2_parts * (size_t)(n_h * n_o + n_o + n_h));
   auto w1p = a.template take<float>(w1_splits > 1 ? (size_t)w1_splits * (size_t)((n_i + 1) * n_h) : 1);
-  auto zp = a.template take<float>((size_t)tc_logit_parts(n_h) * (size_t)(n_s * n_o));
-  const bool planes = tc_mlp_supported(n_s, n_i, n_h);
+  auto zp = a.template take<float>((size_t)tma_logit_parts(n_h) * (size_t)(n_s * n_o));
+  const bool planes = tma_mlp_supported(n_s, n_i, n_h);
   // lo planes of x and W1 (each array is its own hi plane)
   auto xl = a.template take<float>(planes ? (size_t)(n_s * n_i) : 1);
   auto wl = a.template take<float>(planes ? (size_t)(n_i * n_h) : 1);
@@ -1142,7 +1042,7 @@ extern "C" size_t stade_mlp2_ce_b_f32_workspace(int64_t n_s, int64_t n_i, int64_
   if (n_s <= 0 || n_h <= 0 || n_o <= 0 || n_i < 0) return 256;
   SizerAlloc a;
   mlp_f32_layout(a, nullptr, n_s, n_i, n_h, n_o);
-  return a.z.bytes() + tc_mlp_workspace(n_s, n_i, n_h);
+  return a.z.bytes();
 }
 
 extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, const float* x,
@@ -1173,14 +1073,12 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
   CarverAlloc ca(wsp);
   MlpF32Ws w;
   mlp_f32_layout(ca, &w, n_s, n_i, n_h, n_o);
-  void* tcws = ca.c.take<char>(tc_mlp_workspace(n_s, n_i, n_h));
   const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
   MlpPath path = mlp_path(n_s, n_i, n_h);
   // the TMA path reads x and W1 in place: their base addresses must be 16-byte aligned
   if (path == MlpPath::Tma &&
       ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w1)) & 15u))
     path = MlpPath::Simt;
-  const bool use_tc = path == MlpPath::Tc;
 
   if (path == MlpPath::Tma) {
     // 0. TF32 lo planes of x and W1
@@ -1215,7 +1113,7 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
         lk<<<6 * tc5::sm_count(), 256, lsm, s>>>(h, w2, w.zpart, S, H, O);
         STADE_CHECK_LAUNCH();
       }
-      kern<<<blocks, 256, 0, s>>>(w.zpart, own_logits ? 1 : tc_logit_parts(n_h), lossb, y, yb,
+      kern<<<blocks, 256, 0, s>>>(w.zpart, own_logits ? 1 : tma_logit_parts(n_h), lossb, y, yb,
                                   b2, z, zb, p, pb, w.gbuf, S, O, w.loss_part);
       STADE_CHECK_LAUNCH();
       st = launch_sum_to_scalar(w.loss_part, blocks, loss, true, s);
@@ -1256,91 +1154,53 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
     return st;
   }
 
-  if (use_tc) {
-    // 1. h = tanh(x W1 + b1) and the logits' partial sums, on tensor cores
-    {
-      PhaseScope ph("fwd_gemm", s);
-      st = tc_forward_tanh_logits(x, w1, b1, w2, h, w.zpart, S, I, H, O, s);
-    }
-    if (st != STADE_OK) return st;
-    // 2. softmax cross-entropy and its reverse, one thread per sample
-    {
-      PhaseScope ph("head", s);
-      const int blocks = (S + 255) / 256;
-      auto kern = O <= 16 ? mlp_head_small_kernel<float, 16> : mlp_head_small_kernel<float, 32>;
-      kern<<<blocks, 256, 0, s>>>(w.zpart, tc_logit_parts(n_h), lossb, y, yb, b2, z, zb, p, pb,
-                                  w.gbuf, S, O, w.loss_part);
-      STADE_CHECK_LAUNCH();
-      st = launch_sum_to_scalar(w.loss_part, blocks, loss, true, s);
-    }
-    if (st != STADE_OK) return st;
-    // 3. s1b, hb consumed, W2b / b2b partials in one pass over h and hb
-    {
-      PhaseScope ph("w2b", s);
-      const int chunks = (S + kW2ChunkTc - 1) / kW2ChunkTc;
-      const size_t smem = sizeof(float) * (size_t)kW2ChunkTc * O;
-      auto kern = O <= 16 ? mlp_s1b_w2b_kernel<16, false> : mlp_s1b_w2b_kernel<32, false>;
-      kern<<<dim3(chunks, (H + 511) / 512), 256, smem, s>>>(h, hb, w.gbuf, w2, w.s1b, nullptr, S,
-                                                            H, O, kW2ChunkTc, w.w2_part);
-      STADE_CHECK_LAUNCH();
-      finish_two_kernel<float><<<ceil_div_u(n_h * n_o + n_o, 256), 256, 0, s>>>(
-          w.w2_part, chunks, n_h * n_o, w2b, n_o, b2b);
-      STADE_CHECK_LAUNCH();
-    }
-  } else {
-    // 1. h = tanh(x W1 + b1)
-    {
-      PhaseScope ph("fwd_gemm", s);
-      st = gemm_simt<float, kF32RM, kF32RN, kF32BK, true, true>(
-          S, H, I, LdRow<float>{x, I}, LdB<float>{w1, H}, EpiTanh<float>{{}, b1, h, H}, nullptr,
-          1, s);
-    }
-    if (st != STADE_OK) return st;
-    // 2. per-sample head
-    {
-      PhaseScope ph("head", s);
-      const size_t head_smem = sizeof(float) * (size_t)(n_h * n_o);
-      STADE_REQUIRE(head_smem <= 200 * 1024, "mlp2_ce_b: n_h * n_o too large");
-      auto kern = O <= 16 ? mlp_head_b_kernel<float, 16> : mlp_head_b_kernel<float, 32>;
-      if (head_smem > 48 * 1024)
-        STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)head_smem));
-      kern<<<w.head_blocks, kHeadWarps * 32, head_smem, s>>>(lossb, y, yb, w2, b2, h, hb, z, zb, p,
-                                                             pb, w.gbuf, w.s1b, S, H, O, w.loss_part);
-      STADE_CHECK_LAUNCH();
-      st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
-    }
-    if (st != STADE_OK) return st;
-    // 3. W2b, b2b
-    {
-      PhaseScope ph("w2b", s);
-      auto kern = O <= 16 ? mlp_w2b_partial_kernel<float, 16> : mlp_w2b_partial_kernel<float, 32>;
-      kern<<<w.w2_chunks, 256, 0, s>>>(h, w.gbuf, S, H, O, kW2Chunk, w.w2_part);
-      STADE_CHECK_LAUNCH();
-      finish_two_kernel<float><<<ceil_div_u(n_h * n_o + n_o, 256), 256, 0, s>>>(
-          w.w2_part, w.w2_chunks, n_h * n_o, w2b, n_o, b2b);
-      STADE_CHECK_LAUNCH();
-    }
+  // CUDA-core path
+  // 1. h = tanh(x W1 + b1)
+  {
+    PhaseScope ph("fwd_gemm", s);
+    st = gemm_simt<float, kF32RM, kF32RN, kF32BK, true, true>(
+        S, H, I, LdRow<float>{x, I}, LdB<float>{w1, H}, EpiTanh<float>{{}, b1, h, H}, nullptr,
+        1, s);
+  }
+  if (st != STADE_OK) return st;
+  // 2. per-sample head
+  {
+    PhaseScope ph("head", s);
+    const size_t head_smem = sizeof(float) * (size_t)(n_h * n_o);
+    STADE_REQUIRE(head_smem <= 200 * 1024, "mlp2_ce_b: n_h * n_o too large");
+    auto kern = O <= 16 ? mlp_head_b_kernel<float, 16> : mlp_head_b_kernel<float, 32>;
+    if (head_smem > 48 * 1024)
+      STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)head_smem));
+    kern<<<w.head_blocks, kHeadWarps * 32, head_smem, s>>>(lossb, y, yb, w2, b2, h, hb, z, zb, p,
+                                                           pb, w.gbuf, w.s1b, S, H, O, w.loss_part);
+    STADE_CHECK_LAUNCH();
+    st = launch_sum_to_scalar(w.loss_part, w.head_blocks, loss, true, s);
+  }
+  if (st != STADE_OK) return st;
+  // 3. W2b, b2b
+  {
+    PhaseScope ph("w2b", s);
+    auto kern = O <= 16 ? mlp_w2b_partial_kernel<float, 16> : mlp_w2b_partial_kernel<float, 32>;
+    kern<<<w.w2_chunks, 256, 0, s>>>(h, w.gbuf, S, H, O, kW2Chunk, w.w2_part);
+    STADE_CHECK_LAUNCH();
+    finish_two_kernel<float><<<ceil_div_u(n_h * n_o + n_o, 256), 256, 0, s>>>(
+        w.w2_part, w.w2_chunks, n_h * n_o, w2b, n_o, b2b);
+    STADE_CHECK_LAUNCH();
   }
   // 4. W1b = x^T s1b (+ b1b as the row of ones), 5. xb += s1b W1^T
   {
     PhaseScope ph("w1b_gemm", s);
-    if (use_tc)
-      st = tc_weight_grad(x, w.s1b, w1b, b1b, S, I, H, tcws, s);
-    else
-      st = gemm_simt<float, kF32RM, kF32RN, kF32BK, false, true>(
-          I + 1, H, S, LdXtOnes<float>{x, I, I}, LdB<float>{w.s1b, H},
-          EpiWeightBias<float>{{}, w1b, b1b, I, H}, w.w1_part, w.w1_splits, s);
+    st = gemm_simt<float, kF32RM, kF32RN, kF32BK, false, true>(
+        I + 1, H, S, LdXtOnes<float>{x, I, I}, LdB<float>{w.s1b, H},
+        EpiWeightBias<float>{{}, w1b, b1b, I, H}, w.w1_part, w.w1_splits, s);
   }
   if (st != STADE_OK) return st;
   {
     PhaseScope ph("xb_gemm", s);
-    if (use_tc)
-      st = tc_input_grad(w.s1b, w1, xb, S, I, H, tcws, s);
-    else
-      st = gemm_simt<float, kF32RM, kF32RN, kF32BK, true, false>(
-          S, I, H, LdRow<float>{w.s1b, H}, LdBT<float>{w1, H}, EpiAddTo<float>{{}, xb, I},
-          nullptr, 1, s);
+    st = gemm_simt<float, kF32RM, kF32RN, kF32BK, true, false>(
+        S, I, H, LdRow<float>{w.s1b, H}, LdBT<float>{w1, H}, EpiAddTo<float>{{}, xb, I},
+        nullptr, 1, s);
   }
   return st;
 }

@@ -29,7 +29,7 @@
 #include <cstdlib>
 #include <cstring>
 
-#include "tc_gemm.cuh"
+#include "tc_tma.cuh"
 #include "tcgen05.cuh"
 
 namespace stade {
@@ -923,6 +923,14 @@ stade_status tma_input_grad(const float* s1b_hi, const float* s1b_lo, const floa
 }  // namespace stade
 
 namespace stade {
+bool tma_mlp_supported(int64_t n_s, int64_t n_i, int64_t n_h) {
+  return n_s >= 1 && n_i >= 1 && n_h >= 1 && n_i % 4 == 0 && n_h % 4 == 0 &&
+         n_s < (int64_t(1) << 30) && n_i < (1 << 20) && n_h < (1 << 20);
+}
+
+// two partial sums per 128-wide tile of hidden units (one per epilogue warp group)
+int tma_logit_parts(int64_t n_h) { return 2 * (int)((n_h + tma::BN - 1) / tma::BN); }
+
 // Reads and clears the TMA kernel's error word (-1 when it cannot be read).
 int tma_take_error() {
   int v = 0;
@@ -934,3 +942,17 @@ int tma_take_error() {
   return v;
 }
 }  // namespace stade
+
+namespace stade {
+int conv_tc_take_error();
+}
+
+// The library's device error word: set when a bounded wait inside a
+// tensor-core kernel ran out (the kernel then skipped its remaining work and
+// returned). Reading clears it.
+extern "C" int stade_device_error(void) {
+  const int t = stade::tma_take_error();
+  const int c = stade::conv_tc_take_error();
+  if (t < 0 || c < 0) return -1;
+  return t | c;
+}

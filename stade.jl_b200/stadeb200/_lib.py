@@ -52,6 +52,7 @@ SIGNATURES = {
     "stade_version": (C.c_char_p, []),
     "stade_kernel_launches": (C.c_int, []),
     "stade_reset_kernel_launches": (None, []),
+    "stade_workspace_cached_bytes": (C.c_size_t, []),
     "stade_device_error": (C.c_int, []),
     "stade_profile_enable": (None, [C.c_int]),
     "stade_profile_read": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(D), C.POINTER(C.c_int),

@@ -45,6 +45,19 @@ class EmitError(RuntimeError):
     pass
 
 
+# The generated sweeps shipped in julia/generated/ and the precisions the
+# package builds them in (the bench's emitted arm and its Julia binding load
+# these).
+SHIPPED = {"affine_ls_b": (64, 32), "heat2d_b": (64,)}
+
+
+def build_shipped() -> list:
+    """Emits and builds every shipped generated sweep for sm_100a (cached by
+    content under _gen/); returns the library paths."""
+    return [build(emit(generated_source(name), precision=prec)[0])
+            for name, precs in SHIPPED.items() for prec in precs]
+
+
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:

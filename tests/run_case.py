@@ -3,21 +3,25 @@
 Meant for profiling one kernel at a controlled size (for example under ncu)
 and for quick timing; it checks nothing.
 
-    python -m stadeb200.run_case heat2d --n 4096 --n-step 4 --repeat 2
-    python -m stadeb200.run_case mlp2_ce --n-s 8192
-    python -m stadeb200.run_case mlp2_ce_hv --n-s 2048
-    python -m stadeb200.run_case conv1d_relu_mse --n-b 64
-    python -m stadeb200.run_case affine_ls
+    python tests/run_case.py heat2d --n 4096 --n-step 4 --repeat 2
+    python tests/run_case.py mlp2_ce --n-s 8192
+    python tests/run_case.py mlp2_ce_hv --n-s 2048
+    python tests/run_case.py conv1d_relu_mse --n-b 64
+    python tests/run_case.py affine_ls
 
-(run with stade.jl_b200/ on PYTHONPATH, or from that directory)
+(a profiling driver kept beside the tests; pytest does not collect it)
 """
 from __future__ import annotations
 
 import argparse
+import os
+import sys
 
 import torch
 
-from . import kernels, synth
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                "stade.jl_b200"))
+from stadeb200 import kernels, synth  # noqa: E402
 
 
 def _dev(d):

@@ -2,7 +2,7 @@
 
 The reference cannot run here (Julia) and ships no numeric gradients for
 these primals, so the oracle is pinned by what the reference's own tests
-check (SURVEY: test/validate_corpus.jl, src/STADE.jl:16334-17159):
+check (test/validate_corpus.jl, src/STADE.jl:16334-17159):
   - agreement with the textbook gradients of the same functions (refmath),
   - central finite differences (the reference's FD oracle, rtol 1e-3),
   - the dot-product identity <grad, v> = lossd of the HVP's forward tangent
