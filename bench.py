@@ -14,7 +14,13 @@ samples (strong scaling: the grad-eval is fixed, its work is split).
 Also selectable with --config: heat2d (C3; row slabs with a halo exchange per
 step at N > 1), affine_ls (C1; replicas at N > 1), mlp2_ce_hv (C5; sample
 blocks), conv1d_relu_mse (C4; sample blocks, the mean loss's seed and sum
-scaled by 1/N).
+scaled by 1/N). The default run at N = 1 also measures C1, C3, C4 and C5 the
+same way and reports them under "configs" (C2 stays the headline value).
+
+--impl reference times the reference's CPU implementation of the path: the
+oracle (the generated sweep restated in C++, OpenMP over all host threads)
+on inputs from the oracle's own generator, one whole grad-eval per step for
+C1, C2 and C5; no product library is loaded on that arm.
 
     python bench.py [--gpus N --steps K --warmup W] [--config NAME] [--impl reference]
     python bench.py --config affine_ls|heat2d --impl emitted
@@ -65,6 +71,8 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of a replayed CUDA graph of one step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="N = 1 default run: skip the C1 / C3 / C4 / C5 blocks of \"configs\"")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target length of the CPU-baseline sample")
     return ap.parse_args()
@@ -104,9 +112,9 @@ class ClockSampler:
 
     def start(self):
         """Starts sampling; call well before the timed region (nvidia-smi's
-        start-up must not overlap the timing) and bracket that region with
-        mark_begin / mark_end."""
-        self.window = None
+        start-up must not overlap the timing) and bracket each timed region
+        with mark_begin / mark_end (summary(i) covers the i-th)."""
+        self.windows = []
         self._t0 = None
         try:
             self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE,
@@ -118,7 +126,8 @@ class ClockSampler:
         self._t0 = time.time()
 
     def mark_end(self):
-        self.window = (self._t0, time.time())
+        self.windows.append((self._t0, time.time()))
+        return len(self.windows) - 1
 
     def stop(self):
         if not self.proc:
@@ -132,8 +141,9 @@ class ClockSampler:
             out, _ = self.proc.communicate()
         self.lines = [l for l in out.splitlines() if l.strip()]
 
-    def summary(self):
+    def summary(self, i=0):
         import datetime
+        window = self.windows[i] if i < len(self.windows) else None
         rows = []
         for l in self.lines:
             parts = [p.strip() for p in l.split(",")]
@@ -143,7 +153,7 @@ class ClockSampler:
                 ts = datetime.datetime.strptime(parts[9], "%Y/%m/%d %H:%M:%S.%f").timestamp()
             except ValueError:
                 ts = None
-            if self.window and ts is not None and not (self.window[0] - 0.25 <= ts <= self.window[1] + 0.25):
+            if window and ts is not None and not (window[0] - 0.25 <= ts <= window[1] + 0.25):
                 continue
             try:
                 rows.append(dict(sm=float(parts[1]), smax=float(parts[2]),
@@ -285,6 +295,135 @@ def load_traffic(config):
 
 
 # ---------------------------------------------------------------------------
+# The CPU side (the reference arm and each line's cpu_baseline): the oracle,
+# the generated sweeps restated in C++ (oracle/oracle.cc) with OpenMP over
+# samples (C3: over grid cells, bit-identical to the serial sweep), on inputs
+# from the oracle's own restatement of the generator, so this side never
+# loads the product library.
+FULL_UNITS = {"affine_ls": (1, "evaluation"), "mlp2_ce": (65536, "samples"),
+              "heat2d": (16, "time steps of the 8192^2 grid"),
+              "conv1d_relu_mse": (4096, "samples"), "mlp2_ce_hv": (16384, "samples")}
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+class CpuSweep:
+    """One configuration's oracle sweep over `units` of one grad-eval's work
+    (FULL_UNITS: samples of the batch, or time steps of the C3 grid), inputs
+    drawn once; run() times one sweep."""
+
+    def __init__(self, config, units, threads):
+        import numpy as np
+        from oracle import oracle as orc
+        self.config, self.units, self.threads = config, units, threads
+        self.orc, self.np = orc, np
+        g = orc.generator()
+        full = _synth_full()[config]
+        z = lambda n, dt: np.zeros(n, dt)
+        if config == "affine_ls":
+            S, O, I = full["n_s"], full["n_o"], full["n_i"]
+            d = g.affine_ls_inputs(S, O, I)
+            f = np.float64
+            self.args = [z(1, f), d["lossb"], d["w"], z(O * I, f), d["b"], z(O, f), d["x"],
+                         z(S * I, f), d["t"], z(S * O, f), z(S * O, f), z(S * O, f), S, O, I]
+        elif config in ("mlp2_ce", "mlp2_ce_hv"):
+            S, I, H, O = units, full["n_i"], full["n_h"], full["n_o"]
+            if config == "mlp2_ce":
+                d, f = g.mlp2_ce_inputs(S, I, H, O), np.float32
+            else:
+                d, f = g.mlp2_ce_hv_inputs(S, I, H, O, kernel="mlp2_ce_hv"), np.float64
+            lens = dict(loss=1, x=S * I, y=S * O, w1=I * H, b1=H, w2=H * O, b2=O, h=S * H, z=S * O,
+                        p=S * O)
+            names = ["loss", "lossb", "x", "xb", "y", "yb", "w1", "w1b", "b1", "b1b", "w2", "w2b",
+                     "b2", "b2b", "h", "hb", "z", "zb", "p", "pb"]
+
+            def arr(nm, tan=False):
+                key = nm + ("d" if tan else "")
+                if key in d:
+                    return d[key]
+                base = nm[:-1] if nm not in lens and nm != "lossb" else nm
+                return z(1 if nm == "lossb" else lens[base], f)
+            self.args = [arr(a) for a in names] + [S, I, H, O]
+            if config == "mlp2_ce_hv":
+                tan = [arr(a, True) for a in names]
+                tan[1] = d["lossbd"]   # lossbd
+                self.args += tan
+        elif config == "heat2d":
+            n = full["n"]
+            d = g.heat2d_inputs(n)
+            f = np.float64
+            self.args = [z(1, f), d["lossb"], d["u"], z(n * n, f), z(n * n, f), z(n * n, f),
+                         full["alpha"], 0.0, n, units, z(units * n * n, f)]
+        elif config == "conv1d_relu_mse":
+            B, C, L, O, K = units, full["n_c"], full["n_l"], full["n_o"], full["n_k"]
+            d = g.conv1d_relu_mse_inputs(B, C, L, O, K)
+            nt, f = B * O * (L - K + 1), np.float32
+            self.args = [z(1, f), d["lossb"], d["x"], z(B * C * L, f), d["w"], z(O * C * K, f),
+                         d["t"], z(nt, f), z(nt, f), z(nt, f), z(nt, f), z(nt, f), B, C, L, O, K]
+        else:
+            raise ValueError(config)
+
+    def run(self):
+        orc, c, t = self.orc, self.config, self.threads
+        t0 = time.perf_counter()
+        if c == "affine_ls":
+            orc.affine_ls_b(*self.args)
+        elif c == "mlp2_ce":
+            orc.mlp2_ce_b(*self.args, threads=t)
+        elif c == "mlp2_ce_hv":
+            orc.mlp2_ce_hv(*self.args, threads=t)
+        elif c == "heat2d":
+            orc.heat2d_b(*self.args, threads=t)
+        else:
+            orc.conv1d_relu_mse_b(*self.args, threads=t)
+        return time.perf_counter() - t0
+
+    def describe(self):
+        full, what = FULL_UNITS[self.config]
+        par = (f"OpenMP over {'grid cells' if self.config == 'heat2d' else 'samples'}, "
+               f"{self.threads} threads") if self.threads > 1 else "serial"
+        part = ("the whole grad-eval" if self.units >= full else
+                f"{self.units} of {full} {what}, scaled to the whole grad-eval")
+        return f"{part} (oracle.cc, the generated sweep restated; {par})"
+
+
+def _synth_full():
+    from stadeb200.synth import FULL
+    return FULL
+
+
+def cpu_baseline(config, seconds):
+    """The oracle timed on the host on a bounded sample of the configuration
+    (about `seconds` of work, at most the whole grad-eval); grad-evals/s."""
+    full, _ = FULL_UNITS[config]
+    threads = 1 if config == "affine_ls" else cpu_threads()
+    if config == "affine_ls":
+        sw = CpuSweep(config, 1, threads)
+        reps, t = 0, 0.0
+        while t < min(seconds, 3.0):
+            t += sw.run()
+            reps += 1
+        return {"value": reps / t, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"{reps} whole grad-evals, {t:.2f} s (oracle.cc, the generated sweep "
+                          "restated; serial: 1.6 MB of work per evaluation)"}
+    probe = {"mlp2_ce": 4 * threads, "mlp2_ce_hv": 2 * threads, "heat2d": 1,
+             "conv1d_relu_mse": threads}[config]
+    t0 = CpuSweep(config, probe, threads).run()
+    units = int(min(full, max(probe, probe * seconds / max(t0, 1e-3))))
+    if config == "heat2d":
+        units = max(1, min(full, units))
+    sw = CpuSweep(config, units, threads)
+    t = sw.run()
+    return {"value": (units / full) / t, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": sw.describe() + f", {t:.2f} s"}
+
+
+# ---------------------------------------------------------------------------
 # Workloads
 class Mlp2Ce:
     name = "mlp2_ce"
@@ -319,7 +458,7 @@ class Mlp2Ce:
         self.comm = comm_factory() if world > 1 else None
         self.grad_host = {k: torch.empty(t[k].numel(), dtype=f32).pin_memory()
                           for k in ("w1b", "b1b", "w2b", "b2b", "loss")}
-        self.flush_l2 = sum(v.numel() * 4 for v in self.host.values()) < L2_BYTES
+        self.flush_l2 = self.static_flush(world)
 
     def step(self):
         t, d = self.t, self.ddp
@@ -376,6 +515,10 @@ class Mlp2Ce:
         for k, v in self.grad_host.items():
             v.copy_(t[k], non_blocking=True)
 
+    e2e_note = ("inputs and weights up every step; the weight gradients and the loss come "
+                "back (a data-parallel caller's view); xb, which the sweep also writes, stays on "
+                "the device")
+
     def e2e_bytes(self):
         h2d = sum(self.pinned[k].numel() * 4 for k in ("x", "y", "w1", "b1", "w2", "b2"))
         d2h = sum(v.numel() * 4 for v in self.grad_host.values())
@@ -391,43 +534,26 @@ class Mlp2Ce:
                          "reads h, hb; writes s1b, hb (4 S H floats) + per-class arrays"),
                 "w2b": ("hbm", 4.0 * S * H + 4.0 * S * O, "reads h and g once")}
 
-    def config(self):
+    @staticmethod
+    def static_flush(world):
+        c = _synth_full()["mlp2_ce"]
+        S = c["n_s"] // world
+        return 4 * (S * (c["n_i"] + c["n_o"]) + c["n_i"] * c["n_h"] + c["n_h"] +
+                    c["n_h"] * c["n_o"] + c["n_o"] + 1) < L2_BYTES
+
+    @classmethod
+    def static_config(cls, world):
+        c = _synth_full()["mlp2_ce"]
         return {"workload": "C2 mlp2_ce_b: 2-layer tanh MLP 784-512-10 softmax cross-entropy "
                             "adjoint, Float32, per-sample shadow-weight accumulation",
-                "global_batch": self.G, "per_rank_batch": self.n_s, "n_i": self.n_i,
-                "n_h": self.n_h, "n_o": self.n_o, "parallelism": f"dp{self.world}",
+                "global_batch": c["n_s"], "per_rank_batch": c["n_s"] // world, "n_i": c["n_i"],
+                "n_h": c["n_h"], "n_o": c["n_o"], "parallelism": f"dp{world}",
                 "l2": ("L2 flushed between timed steps (256 MiB write outside the events)"
-                       if self.flush_l2 else "inputs larger than L2, steps timed back to back")}
+                       if cls.static_flush(world) else
+                       "inputs larger than L2, steps timed back to back")}
 
-    def cpu_baseline(self, seconds):
-        """Oracle (the restated generated sweep), OpenMP over samples, on a
-        bounded sample of the batch; scaled to grad-evals of the 65,536 batch."""
-        np = self.np
-        from oracle import oracle as orc
-        from stadeb200 import synth
-        threads = os.cpu_count() or 1
-
-        def run(m):
-            d = synth.mlp2_ce_inputs(m, self.n_i, self.n_h, self.n_o)
-            f = np.float32
-            z = lambda n: np.zeros(n, f)
-            a = dict(loss=z(1), lossb=d["lossb"], x=d["x"], xb=z(m * self.n_i), y=d["y"],
-                     yb=z(m * self.n_o), w1=d["w1"], w1b=z(self.n_i * self.n_h), b1=d["b1"],
-                     b1b=z(self.n_h), w2=d["w2"], w2b=z(self.n_h * self.n_o), b2=d["b2"],
-                     b2b=z(self.n_o), h=z(m * self.n_h), hb=z(m * self.n_h), z=z(m * self.n_o),
-                     zb=z(m * self.n_o), p=z(m * self.n_o), pb=z(m * self.n_o))
-            t0 = time.perf_counter()
-            orc.mlp2_ce_b(*a.values(), m, self.n_i, self.n_h, self.n_o, threads=threads)
-            return time.perf_counter() - t0
-
-        m0 = 64 * threads
-        t0 = run(m0)
-        m = int(min(self.G, max(m0, m0 * seconds / max(t0, 1e-3))))
-        t = run(m)
-        return {"value": (m / t) / self.G, "unit": UNIT, "cores": threads, "kind": "port",
-                "sample": f"{m} of {self.G} samples (oracle.cc OpenMP sweep, {threads} threads), "
-                          f"{t:.2f} s, scaled to the full batch"}
-
+    def config(self):
+        return self.static_config(self.world)
 
 class Heat2d:
     """C3. At N = 1 the generated signature (stade_heat2d_b_f64) on the whole
@@ -465,7 +591,7 @@ class Heat2d:
         self.ws = torch.empty(ws, dtype=torch.uint8, device="cuda")
         self.out_host = torch.empty(m, dtype=f64).pin_memory()
         self.ab_host = torch.empty(1, dtype=f64).pin_memory()
-        self.flush_l2 = m * 8 < L2_BYTES
+        self.flush_l2 = self.static_flush(world)
 
     def step(self):
         t = self.t
@@ -498,29 +624,23 @@ class Heat2d:
                 "bwd_step": ("hbm", 24.0 * N, "read unb_k, read tape u_k-1, write ub_k-1"),
                 "bwd_init": ("hbm", 32.0 * N, "read ub, unb, u_final; write seed")}
 
-    def config(self):
+    @staticmethod
+    def static_flush(world):
+        n = _synth_full()["heat2d"]["n"]
+        return (n // world) * n * 8 < L2_BYTES
+
+    @classmethod
+    def static_config(cls, world):
+        c = _synth_full()["heat2d"]
         return {"workload": "C3 heat2d_b: periodic 5-point heat adjoint, 8192^2 Float64, 16 taped "
-                            "steps, alpha 0.2", "n": self.n, "n_step": self.n_step,
-                "rows_per_rank": self.rows,
-                "parallelism": f"slabs{self.world}" if self.world > 1 else "single",
-                "l2": ("L2 flushed between timed steps" if self.flush_l2 else
+                            "steps, alpha 0.2", "n": c["n"], "n_step": c["n_step"],
+                "rows_per_rank": c["n"] // world,
+                "parallelism": f"slabs{world}" if world > 1 else "single",
+                "l2": ("L2 flushed between timed steps" if cls.static_flush(world) else
                        "inputs larger than L2 (the slab's fields), steps timed back to back")}
 
-    def cpu_baseline(self, seconds):
-        np = self.np
-        from oracle import oracle as orc
-        n = self.n
-        u = self.pinned["u"].numpy().copy()
-        z = lambda m: np.zeros(m, np.float64)
-        stack = z(n * n)
-        t0 = time.perf_counter()
-        orc.heat2d_b(z(1), np.ones(1), u, z(n * n), z(n * n), z(n * n), self.alpha, 0.0, n, 1, stack)
-        t = time.perf_counter() - t0
-        per_eval = t * self.n_step
-        return {"value": 1.0 / per_eval, "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"1 of {self.n_step} time steps on the full {n}^2 grid (oracle.cc, "
-                          f"serial), {t:.2f} s, scaled x{self.n_step}"}
-
+    def config(self):
+        return self.static_config(self.world)
 
 class AffineLs:
     name = "affine_ls"
@@ -578,28 +698,16 @@ class AffineLs:
         return {"affine": ("hbm", byts, "read X, T, W, b; write Wb, bb, Xb, Tb (1,606,656 B); "
                                         "two launches, latency-bound")}
 
-    def config(self):
+    @classmethod
+    def static_config(cls, world):
+        c = _synth_full()["affine_ls"]
         return {"workload": "C1 affine_ls_b: y = W x + b, 0.5 sum (y - t)^2 adjoint, W 64x32, "
-                            "batch 1024, Float64", "n_s": self.n_s, "n_o": self.n_o,
-                "n_i": self.n_i, "parallelism": f"replicas{self.world}",
+                            "batch 1024, Float64", "n_s": c["n_s"], "n_o": c["n_o"],
+                "n_i": c["n_i"], "parallelism": f"replicas{world}",
                 "l2": "working set 1.6 MB fits in L2; L2 flushed between timed steps"}
 
-    def cpu_baseline(self, seconds):
-        np = self.np
-        from oracle import oracle as orc
-        d = {k: v.numpy().copy() for k, v in self.pinned.items()}
-        S, O, I = self.n_s, self.n_o, self.n_i
-        z = lambda m: np.zeros(m, np.float64)
-        reps, t = 0, 0.0
-        t0 = time.perf_counter()
-        while t < min(seconds, 3.0):
-            orc.affine_ls_b(z(1), d["lossb"], d["w"], z(O * I), d["b"], z(O), d["x"], z(S * I),
-                            d["t"], z(S * O), z(S * O), z(S * O), S, O, I)
-            reps += 1
-            t = time.perf_counter() - t0
-        return {"value": reps / t, "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"{reps} full evaluations (oracle.cc, serial), {t:.2f} s"}
-
+    def config(self):
+        return self.static_config(self.world)
 
 class EmittedAffineLs(AffineLs):
     """C1 through the .cu emitter: the generated affine_ls_b text
@@ -740,29 +848,17 @@ class Conv1dReluMse:
                 "conv_wgrad": ("tensor", fl, "weight gradient 2 B O Lo C K flops"),
                 "conv_xgrad": ("tensor", fl, "input gradient 2 B O Lo C K flops")}
 
-    def config(self):
+    @classmethod
+    def static_config(cls, world):
+        c = _synth_full()["conv1d_relu_mse"]
         return {"workload": "C4 conv1d_relu_mse_b: 1-D conv 128x64x9 + ReLU + MSE adjoint, batch "
-                            "4096 x 64 x 2048, Float32", "global_batch": self.G,
-                "per_rank_batch": self.B, "n_c": self.C,
-                "n_l": self.L, "n_o": self.O, "n_k": self.K,
-                "parallelism": f"dp{self.world}", "l2": "inputs larger than L2"}
+                            "4096 x 64 x 2048, Float32", "global_batch": c["n_b"],
+                "per_rank_batch": c["n_b"] // world, "n_c": c["n_c"], "n_l": c["n_l"],
+                "n_o": c["n_o"], "n_k": c["n_k"], "parallelism": f"dp{world}",
+                "l2": "inputs larger than L2"}
 
-    def cpu_baseline(self, seconds):
-        np = self.np
-        from oracle import oracle as orc
-        from stadeb200 import synth
-        b = 12
-        C, L, O, K = self.C, self.L, self.O, self.K
-        d = synth.conv1d_relu_mse_inputs(b, C, L, O, K)
-        nt = b * O * (L - K + 1)
-        z = lambda m: np.zeros(m, np.float32)
-        t0 = time.perf_counter()
-        orc.conv1d_relu_mse_b(z(1), d["lossb"], d["x"], z(b * C * L), d["w"], z(O * C * K), d["t"],
-                              z(nt), z(nt), z(nt), z(nt), z(nt), b, C, L, O, K)
-        t = time.perf_counter() - t0
-        return {"value": b / (t * self.B), "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"{b} of {self.B} samples (oracle.cc, serial), {t:.2f} s, scaled"}
-
+    def config(self):
+        return self.static_config(self.world)
 
 class _LocalZero:
     """The epilogue's zeroing at N = 1 (no communicator)."""
@@ -806,7 +902,7 @@ class Mlp2CeHv:
         self.comm = comm_factory() if world > 1 else None
         backend = ddp.NcclBackend(self.comm) if self.comm is not None else _LocalZero()
         self.epi = ddp.Epilogue(ddp.MLP2_CE, ["x", "y"], "hvp", backend)
-        self.flush_l2 = sum(v.numel() * 8 for v in self.pinned.values()) < L2_BYTES
+        self.flush_l2 = self.static_flush(world)
         self.out_names = ("w1bd", "b1bd", "w2bd", "b2bd", "lossd")
         self.grad_host = {k: torch.empty(t[k].numel(), dtype=torch.float64).pin_memory()
                           for k in self.out_names}
@@ -842,31 +938,24 @@ class Mlp2CeHv:
                 "hv_w1b_gemms": ("fp64", 3 * u, "x^T s1b, x^T s1bd + xd^T s1b (3 units)"),
                 "hv_xb_gemms": ("fp64", 3 * u, "s1b W1^T, s1bd W1^T + s1b W1d^T (3 units)")}
 
-    def config(self):
+    @staticmethod
+    def static_flush(world):
+        c = _synth_full()["mlp2_ce_hv"]
+        S, I, H, O = c["n_s"] // world, c["n_i"], c["n_h"], c["n_o"]
+        return 8 * (2 * S * (I + O) + 2 * (I * H + H + H * O + O) + 2) < L2_BYTES
+
+    @classmethod
+    def static_config(cls, world):
+        c = _synth_full()["mlp2_ce_hv"]
         return {"workload": "C5 mlp2_ce_hv: HVP of the C2 loss, batch 16384, Float64, direction "
-                            "over all 407,050 parameters", "global_batch": self.G,
-                "per_rank_batch": self.S, "n_i": self.I, "n_h": self.H, "n_o": self.O,
-                "parallelism": f"dp{self.world}",
-                "l2": ("L2 flushed between timed steps" if self.flush_l2 else
+                            "over all 407,050 parameters", "global_batch": c["n_s"],
+                "per_rank_batch": c["n_s"] // world, "n_i": c["n_i"], "n_h": c["n_h"],
+                "n_o": c["n_o"], "parallelism": f"dp{world}",
+                "l2": ("L2 flushed between timed steps" if cls.static_flush(world) else
                        "inputs (x, xd) larger than L2, steps timed back to back")}
 
-    def cpu_baseline(self, seconds):
-        np = self.np
-        from oracle import oracle as orc
-        from stadeb200 import synth, kernels
-        m = 256
-        S, I, H, O = m, self.I, self.H, self.O
-        d = synth.mlp2_ce_hv_inputs(S, I, H, O)
-        arrs = {}
-        for name in kernels.MLP_HV_ARGS + kernels.MLP_HV_TAN:
-            arrs[name] = d[name].copy() if name in d else np.zeros(kernels._mlp_len(name, S, I, H, O))
-        t0 = time.perf_counter()
-        orc.mlp2_ce_hv(*[arrs[a] for a in kernels.MLP_HV_ARGS], S, I, H, O,
-                       *[arrs[a] for a in kernels.MLP_HV_TAN])
-        t = time.perf_counter() - t0
-        return {"value": m / (t * self.G), "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"{m} of {self.G} samples (oracle.cc, serial), {t:.2f} s, scaled"}
-
+    def config(self):
+        return self.static_config(self.world)
 
 WORKLOADS = {"mlp2_ce": Mlp2Ce, "heat2d": Heat2d, "affine_ls": AffineLs,
              "conv1d_relu_mse": Conv1dReluMse, "mlp2_ce_hv": Mlp2CeHv}
@@ -874,94 +963,63 @@ EMITTED = {"affine_ls": EmittedAffineLs, "heat2d": EmittedHeat2d}
 
 
 # ---------------------------------------------------------------------------
+REF_FULL_STEPS = ("mlp2_ce", "affine_ls", "mlp2_ce_hv")   # whole grad-evals per step
+
+
 def run_reference(args):
-    """The reference's CPU implementation of the path (the oracle restatement:
-    the reference's Julia cannot run on these machines), all host threads,
-    each step a bounded sample of the workload."""
+    """The reference's CPU implementation of the path on the host cores: the
+    oracle (the generated sweep restated in C++; the reference's Julia cannot
+    run on these machines) with OpenMP over all host threads, on the oracle's
+    own inputs, so no product library is loaded. Each step is one whole
+    grad-eval of the configuration (C3 and C4, whose whole grad-eval takes
+    minutes on the host, run a bounded sample per step, stated in the line).
+    Under torchrun only rank 0 runs it."""
     world, rank, _ = dist_setup(args)
     if rank != 0:
         return
-    import torch  # noqa: F401  (keeps library load order as in the GPU arm)
-    cls = WORKLOADS.get(args.config)
-
-    class _NoGpu:
-        pass
-    if args.config == "mlp2_ce":
-        import numpy as np
-        from oracle import oracle as orc
-        from stadeb200 import synth
-        c = synth.FULL["mlp2_ce"]
-        G, I, H, O = c["n_s"], c["n_i"], c["n_h"], c["n_o"]
-        threads = os.cpu_count() or 1
-        m = 64 * threads
-        d = synth.mlp2_ce_inputs(m, I, H, O)
-        f = np.float32
-
-        def one():
-            z = lambda n: np.zeros(n, f)
-            a = [z(1), d["lossb"], d["x"], z(m * I), d["y"], z(m * O), d["w1"], z(I * H), d["b1"],
-                 z(H), d["w2"], z(H * O), d["b2"], z(O), z(m * H), z(m * H), z(m * O), z(m * O),
-                 z(m * O), z(m * O)]
-            t0 = time.perf_counter()
-            orc.mlp2_ce_b(*a, m, I, H, O, threads=threads)
-            return time.perf_counter() - t0
-        for _ in range(args.warmup):
-            one()
-        times = [one() for _ in range(args.steps)]
-        per_sample = sum(times) / (args.steps * m)
-        value = 1.0 / (per_sample * G)
-        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": per_sample * G * 1e3, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": "C2 mlp2_ce_b (see the ours arm)", "global_batch": G,
-                           "parallelism": "cpu"},
-                "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                                 "sample": f"{m} of {G} samples per step (oracle.cc OpenMP "
-                                           "restatement of the generated sweep; the reference's "
-                                           "Julia is not runnable here)"},
-                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return
-    print(json.dumps({"impl": "reference", "unavailable":
-                      f"reference arm implemented for mlp2_ce only (asked {args.config})"}))
-
-
-def main():
-    args = parse_args()
-    if args.impl == "reference":
-        run_reference(args)
-        return
-    import torch
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    from stadeb200 import _lib, ddp
-
-    def comm_factory():
-        return ddp.NcclComm(rank, world)
-
-    if args.impl == "emitted":
-        if args.config not in EMITTED:
-            raise SystemExit(f"--impl emitted: one of {sorted(EMITTED)}")
-        W = EMITTED[args.config](torch, rank, world, comm_factory)
+    config = args.config
+    full, _ = FULL_UNITS[config]
+    threads = 1 if config == "affine_ls" else cpu_threads()
+    if config in REF_FULL_STEPS:
+        units = full
+    elif config == "heat2d":
+        units = 2
     else:
-        W = WORKLOADS[args.config](torch, rank, world, comm_factory)
-    stream = torch.cuda.current_stream()
-    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
-    peaks, peak_src = load_peaks()
+        units = 4 * threads
+    sw = CpuSweep(config, units, threads)
+    for _ in range(args.warmup):
+        sw.run()
+    h0 = time.perf_counter()
+    times = [sw.run() for _ in range(args.steps)]
+    wall = time.perf_counter() - h0
+    ms_per_step = 1e3 * sum(times) / args.steps
+    value = (units / full) * 1e3 / ms_per_step
+    cls = WORKLOADS[config]
+    cpu = {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": sw.describe()}
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": cls.scaling,
+            "vs_baseline": None, "dtype": cls.dtype, "data": "synthetic (seeded, shapes and "
+                                                            "distributions of the BASELINE config)",
+            "config": cls.static_config(world),
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "timing": "host wall clock around each step (perf_counter)",
+            "timed_region_s": wall}
+    print(json.dumps(line), flush=True)
 
-    # device-resident timed run: one step captured in a CUDA graph and
-    # replayed (N = 1; eager at N > 1, where the step holds NCCL calls on a
-    # non-blocking communicator), phase profiler off
-    clocks = ClockSampler(local)
-    clocks.start()
+
+EXTRA_CONFIGS = ("affine_ls", "heat2d", "conv1d_relu_mse", "mlp2_ce_hv")
+
+
+def measure(W, args, torch, world, rank, dist, stream, flush, clocks, peaks, peak_src):
+    """Times one workload: W warm-up steps, K timed steps of a replayed CUDA
+    graph of one step (eager where capture is not possible), then the same
+    steps eagerly with the phase profiler on (roofline, launch count), then
+    the end-to-end steps from host buffers, then the CPU baseline (rank 0,
+    N = 1). Returns the JSON-line fields of this workload."""
+    from stadeb200 import _lib
     t_setup = time.time()
     for _ in range(args.warmup):
         W.step()
@@ -1000,7 +1058,7 @@ def main():
     clocks.mark_begin()
     total_ms, per = timed_loop(torch, step_fn, args.steps, args.warmup, world, dist,
                                flush if W.flush_l2 else None, stream)
-    clocks.mark_end()
+    window = clocks.mark_end()
     host_ms = timed_loop.host_ms / args.steps
     ms_per_step = total_ms / args.steps
     value = 1000.0 / ms_per_step if W.scaling == "strong" else world * 1000.0 / ms_per_step
@@ -1030,46 +1088,108 @@ def main():
         ev = 1000.0 / (e_ms / args.steps)
         if W.scaling != "strong":
             ev *= world
-        e2e = {"value": ev, "unit": UNIT, "h2d_bytes_per_step": h2d * (world if W.scaling == "strong" else 1),
+        e2e = {"value": ev, "unit": UNIT,
+               "h2d_bytes_per_step": h2d * (world if W.scaling == "strong" else 1),
                "d2h_bytes_per_step": d2h * (world if W.scaling == "strong" else 1),
                "ms_per_step": e_ms / args.steps}
-
-    clocks.stop()
+        note = getattr(W, "e2e_note", None)
+        if note:
+            e2e["note"] = note
+    torch.cuda.synchronize()
+    timing = "CUDA graph of one step, replayed" if graph is not None else "eager launches"
+    graph_note = ("the step's NCCL calls are captured in the graph"
+                  if graph is not None and world > 1 else None)
+    # a graph that holds NCCL calls goes before the communicators
+    step_fn = graph = None
+    torch.cuda.synchronize()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = W.cpu_baseline(args.cpu_seconds)
+        cpu = cpu_baseline(W.name, args.cpu_seconds)
+    return {"value": value, "ms_per_step": ms_per_step, "scaling": W.scaling, "dtype": W.dtype,
+            "config": W.config(),
+            "roofline": roofline(phases, W.phase_work(), args.steps, peaks, peak_src,
+                                 load_traffic(W.name) if world == 1 else None),
+            "cpu_baseline": cpu, "e2e": e2e, "clocks_window": window,
+            "gpu_launches": launches,
+            "timing": timing, "graph_note": graph_note,
+            "eager_profiled_ms_per_step": p_ms / args.steps,
+            "host_enqueue_ms_per_step": host_ms,
+            "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
+            "step_ms_min_max": [min(per), max(per)]}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    from stadeb200 import ddp
+
+    def comm_factory():
+        return ddp.NcclComm(rank, world)
+
+    def make(name):
+        if args.impl == "emitted":
+            if name not in EMITTED:
+                raise SystemExit(f"--impl emitted: one of {sorted(EMITTED)}")
+            return EMITTED[name](torch, rank, world, comm_factory)
+        return WORKLOADS[name](torch, rank, world, comm_factory)
+
+    stream = torch.cuda.current_stream()
+    flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    peaks, peak_src = load_peaks()
+    clocks = ClockSampler(local)
+    clocks.start()
+
+    W = make(args.config)
+    head = measure(W, args, torch, world, rank, dist, stream, flush, clocks, peaks, peak_src)
+    comm = getattr(W, "comm", None)
+    del W
+    # the other configurations at N = 1 (the default run), each measured the
+    # same way, reported in "configs"
+    extras = {}
+    if (world == 1 and args.impl == "ours" and args.config == "mlp2_ce" and not args.no_extra):
+        for name in EXTRA_CONFIGS:
+            gc.collect()
+            torch.cuda.empty_cache()
+            Wx = make(name)
+            extras[name] = measure(Wx, args, torch, world, rank, dist, stream, flush, clocks,
+                                   peaks, peak_src)
+            del Wx
+    clocks.stop()
 
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        def finish(m):
+            m["clocks"] = clocks.summary(m.pop("clocks_window"))
+            return m
+        head = finish(head)
+        line = {"metric": METRIC, "value": head.pop("value"), "unit": UNIT, "n_gpus": world,
                 **({"impl": "emitted"} if args.impl == "emitted" else {}),
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-                "higher_is_better": True, "scaling": W.scaling, "vs_baseline": None,
-                "dtype": W.dtype, "data": "synthetic (seeded, shapes and distributions of the "
-                                          "BASELINE config)",
-                "config": W.config(),
-                "roofline": roofline(phases, W.phase_work(), args.steps, peaks, peak_src,
-                                     load_traffic(args.config) if world == 1 else None),
-                "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
-                "gpu_launches": launches,
-                "timing": ("CUDA graph of one step, replayed" if graph is not None
-                           else "eager launches"),
-                "graph_note": ("the step's NCCL calls are captured in the graph"
-                               if graph is not None and world > 1 else None),
-                "eager_profiled_ms_per_step": p_ms / args.steps,
-                "host_enqueue_ms_per_step": host_ms,
-                "phases_ms_per_step": {k: v[0] / args.steps for k, v in phases.items()},
-                "step_ms_min_max": [min(per), max(per)]}
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": head.pop("ms_per_step"), "higher_is_better": True,
+                "scaling": head.pop("scaling"), "vs_baseline": None, "dtype": head.pop("dtype"),
+                "data": "synthetic (seeded, shapes and distributions of the BASELINE config)",
+                **head}
+        if extras:
+            line["configs"] = {k: finish(v) for k, v in extras.items()}
+            line["gpu_launches_all_configs"] = line["gpu_launches"] + sum(
+                v["gpu_launches"] for v in extras.values())
         print(json.dumps(line), flush=True)
-    # a graph that holds NCCL calls goes before the communicators
-    step_fn = None
-    del graph
     torch.cuda.synchronize()
     if world > 1:
-        if getattr(W, "comm", None) is not None:
-            W.comm.close()
+        if comm is not None:
+            comm.close()
         dist.barrier()
         dist.destroy_process_group()
-
 
 if __name__ == "__main__":
     main()

@@ -37,6 +37,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <utility>
 #include <vector>
 
 #ifdef _OPENMP
@@ -482,10 +483,12 @@ T heat2d_b(T* loss, const T* lossb, T* u, T* ub, T* un, T* unb, T alpha, T alpha
 // self-overlapping index t + ci - 1), ReLU through max(a, 0.0) with the der_
 // partial 0.5 * (1 + sign(a - 0.0)) (src/STADE.jl:1489-1501), the local `a`
 // recomputed in the reverse iteration (mlp1d_b.jl:43-47).
+// inv_n is the primal's `1.0 / (n_b * n_o * n_lo)` of the whole batch: a block
+// of samples (the parallel variant below) keeps the whole batch's value.
 template <class T>
-void conv1d_relu_mse_b(T* loss, const T* lossb, const T* x, T* xb, const T* w, T* wb,
-                       const T* t, T* tb, T* z, T* zb, T* r, T* rb,
-                       i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+void conv1d_relu_mse_b_inv(T* loss, const T* lossb, const T* x, T* xb, const T* w, T* wb,
+                           const T* t, T* tb, T* z, T* zb, T* r, T* rb,
+                           i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k, T inv_n) {
   const i64 n_lo = n_l - n_k + 1;
   const i64 nt = n_b * n_o * n_lo;
   T a = T(0), ab = T(0);
@@ -502,7 +505,6 @@ void conv1d_relu_mse_b(T* loss, const T* lossb, const T* x, T* xb, const T* w, T
     z[idx] = a;
     r[idx] = jl_max(a, T(0));
   }
-  const T inv_n = T(1) / T(nt);
   for (i64 idx2 = 0; idx2 < nt; ++idx2) {
     const T d = r[idx2] - t[idx2];
     loss[0] = loss[0] + inv_n * (d * d);
@@ -532,6 +534,14 @@ void conv1d_relu_mse_b(T* loss, const T* lossb, const T* x, T* xb, const T* w, T
     }
     ab = T(0);
   }
+}
+template <class T>
+void conv1d_relu_mse_b(T* loss, const T* lossb, const T* x, T* xb, const T* w, T* wb,
+                       const T* t, T* tb, T* z, T* zb, T* r, T* rb,
+                       i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
+  const T inv_n = T(1) / T(n_b * n_o * (n_l - n_k + 1));
+  conv1d_relu_mse_b_inv(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k,
+                        inv_n);
 }
 
 // ---------------------------------------------------------------------------
@@ -678,21 +688,24 @@ void conv1d_relu_mse_d(T* loss, T* lossd, const T* x, const T* xd, const T* w, c
 }
 
 // ---------------------------------------------------------------------------
-// Parallel CPU variants (timed CPU baseline only): samples split across host
-// threads, each with private copies of the summed shadows, then one
-// fixed-order sum. Same arithmetic per sample as the serial sweeps above.
-template <class T>
-void mlp2_ce_b_omp(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
-                   const T* w1, T* w1b, const T* b1, T* b1b, const T* w2, T* w2b,
-                   const T* b2, T* b2b, T* h, T* hb, T* z, T* zb, T* p, T* pb,
-                   i64 n_s, i64 n_i, i64 n_h, i64 n_o, int nthreads) {
+// Parallel CPU variants (the timed CPU baseline and the checks at the full
+// configuration sizes): samples split across host threads, each with private
+// copies of the summed shadows, then one fixed-order sum. Same arithmetic per
+// sample as the serial sweeps above; only the order in which the per-sample
+// contributions to a summed shadow are added differs.
+
+// Threads over contiguous sample blocks; each block's summed shadows go to
+// private zeroed copies (`my`), added to the outputs afterwards in block
+// order. `run(lo, hi, my)` runs the serial sweep on samples [lo, hi).
+template <class T, class Run>
+void over_sample_blocks(i64 n_s, int nthreads, size_t private_len, Run run,
+                        const std::vector<std::pair<T*, i64>>& outs) {
 #ifdef _OPENMP
   if (nthreads <= 0) nthreads = omp_get_max_threads();
 #else
   nthreads = 1;
 #endif
-  const i64 nw1 = n_i * n_h, nw2 = n_h * n_o;
-  std::vector<T> part((size_t)nthreads * (nw1 + n_h + nw2 + n_o + 1), T(0));
+  std::vector<T> part((size_t)nthreads * private_len, T(0));
 #pragma omp parallel num_threads(nthreads)
   {
 #ifdef _OPENMP
@@ -700,24 +713,177 @@ void mlp2_ce_b_omp(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb
 #else
     const int tid = 0;
 #endif
-    T* my = part.data() + (size_t)tid * (nw1 + n_h + nw2 + n_o + 1);
     const i64 lo = n_s * tid / nthreads, hi = n_s * (tid + 1) / nthreads;
-    if (hi > lo) {
-      const i64 m = hi - lo;
-      mlp2_ce_b(my + nw1 + n_h + nw2 + n_o, lossb, x + lo * n_i, xb + lo * n_i, y + lo * n_o,
-                yb + lo * n_o, w1, my, b1, my + nw1, w2, my + nw1 + n_h, b2,
-                my + nw1 + n_h + nw2, h + lo * n_h, hb + lo * n_h, z + lo * n_o, zb + lo * n_o,
-                p + lo * n_o, pb + lo * n_o, m, n_i, n_h, n_o);
-    }
+    if (hi > lo) run(lo, hi, part.data() + (size_t)tid * private_len);
   }
   for (int tid = 0; tid < nthreads; ++tid) {
-    const T* my = part.data() + (size_t)tid * (nw1 + n_h + nw2 + n_o + 1);
-    for (i64 i = 0; i < nw1; ++i) w1b[i] += my[i];
-    for (i64 i = 0; i < n_h; ++i) b1b[i] += my[nw1 + i];
-    for (i64 i = 0; i < nw2; ++i) w2b[i] += my[nw1 + n_h + i];
-    for (i64 i = 0; i < n_o; ++i) b2b[i] += my[nw1 + n_h + nw2 + i];
-    loss[0] += my[nw1 + n_h + nw2 + n_o];
+    const T* my = part.data() + (size_t)tid * private_len;
+    for (const auto& o : outs) {
+      for (i64 i = 0; i < o.second; ++i) o.first[i] += my[i];
+      my += o.second;
+    }
   }
+}
+
+template <class T>
+void mlp2_ce_b_omp(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
+                   const T* w1, T* w1b, const T* b1, T* b1b, const T* w2, T* w2b,
+                   const T* b2, T* b2b, T* h, T* hb, T* z, T* zb, T* p, T* pb,
+                   i64 n_s, i64 n_i, i64 n_h, i64 n_o, int nthreads) {
+  const i64 nw1 = n_i * n_h, nw2 = n_h * n_o;
+  over_sample_blocks<T>(
+      n_s, nthreads, (size_t)(nw1 + n_h + nw2 + n_o + 1),
+      [&](i64 lo, i64 hi, T* my) {
+        const i64 io = lo * n_i, oo = lo * n_o, ho = lo * n_h;
+        mlp2_ce_b(my + nw1 + n_h + nw2 + n_o, lossb, x + io, xb + io, y + oo, yb + oo, w1, my,
+                  b1, my + nw1, w2, my + nw1 + n_h, b2, my + nw1 + n_h + nw2, h + ho, hb + ho,
+                  z + oo, zb + oo, p + oo, pb + oo, hi - lo, n_i, n_h, n_o);
+      },
+      {{w1b, nw1}, {b1b, n_h}, {w2b, nw2}, {b2b, n_o}, {loss, 1}});
+}
+
+// C3 heat2d_b with every per-cell loop parallel over cells and bit-identical
+// to the serial sweep above. The loss and alphab sums stay serial in the
+// generated order. The reverse stencil loop scatters into ub[up], ub[dn],
+// ub[lf], ub[rt] and ub[idx]; here each cell instead gathers, from the (at
+// most five) iterations that write it, their additions sorted the way the
+// serial loop performs them (iteration index descending, then statement
+// order), so every cell sees the same additions in the same order. ub is zero
+// when that loop starts (the restore loop above consumed it).
+template <class T>
+T heat2d_b_omp(T* loss, const T* lossb, T* u, T* ub, T* un, T* unb, T alpha, T alphab,
+               i64 n, i64 n_step, T* u_stack, int nthreads) {
+#ifdef _OPENMP
+  if (nthreads <= 0) nthreads = omp_get_max_threads();
+#else
+  nthreads = 1;
+#endif
+  const i64 nn = n * n;
+  // neighbours of cell (i, j) without division: rows and columns wrap
+  auto up_row = [n](i64 i) { return i == 0 ? n - 1 : i - 1; };
+  auto dn_row = [n](i64 i) { return i == n - 1 ? 0 : i + 1; };
+  auto lf_col = [n](i64 j) { return j == 0 ? n - 1 : j - 1; };
+  auto rt_col = [n](i64 j) { return j == n - 1 ? 0 : j + 1; };
+  auto stencil = [&](const T* v, i64 i, i64 j) {
+    const T c = v[i * n + j];
+    return ((((v[up_row(i) * n + j] + v[dn_row(i) * n + j]) + v[i * n + lf_col(j)]) +
+             v[i * n + rt_col(j)]) - T(4) * c);
+  };
+  for (i64 it = 0; it < n_step; ++it) {
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+    for (i64 i = 0; i < n; ++i)
+      for (i64 j = 0; j < n; ++j) un[i * n + j] = u[i * n + j] + alpha * stencil(u, i, j);
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+    for (i64 idx2 = 0; idx2 < nn; ++idx2) {
+      u_stack[idx2 + it * nn] = u[idx2];
+      u[idx2] = un[idx2];
+    }
+  }
+  for (i64 idx3 = 0; idx3 < nn; ++idx3) loss[0] = loss[0] + u[idx3] * u[idx3];
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+  for (i64 idx3 = 0; idx3 < nn; ++idx3) ub[idx3] = ub[idx3] + (T(2) * u[idx3]) * lossb[0];
+  for (i64 it = n_step - 1; it >= 0; --it) {
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+    for (i64 idx2 = 0; idx2 < nn; ++idx2) {
+      u[idx2] = u_stack[idx2 + it * nn];
+      const T oldb = ub[idx2];
+      ub[idx2] = T(0);
+      unb[idx2] = unb[idx2] + oldb;
+    }
+    // alphab, serial in the generated (descending) order
+    for (i64 i = n - 1; i >= 0; --i)
+      for (i64 j = n - 1; j >= 0; --j) alphab = alphab + stencil(u, i, j) * unb[i * n + j];
+    // ub from the reverse stencil loop. Iteration k of that loop adds, in
+    // order: oldb_k to ub[k]; a_k = alpha oldb_k to ub[up], ub[dn], ub[lf],
+    // ub[rt]; 4 * -a_k to ub[k]; and the loop runs k descending. Each cell
+    // collects the additions that land on it and applies them sorted by
+    // (k descending, statement ascending), as the serial loop does.
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+    for (i64 i = 0; i < n; ++i) {
+      for (i64 j = 0; j < n; ++j) {
+        const i64 cell = i * n + j;
+        i64 key_it[30];
+        int key_st[30];
+        T val[30];
+        int m = 0;
+        const i64 cand[5] = {dn_row(i) * n + j, up_row(i) * n + j, i * n + rt_col(j),
+                             i * n + lf_col(j), cell};
+        for (int a = 0; a < 5; ++a) {
+          const i64 k = cand[a];
+          bool seen = false;
+          for (int b = 0; b < a; ++b) seen = seen || cand[b] == k;
+          if (seen) continue;
+          const i64 ki = k / n, kj = k % n;
+          const T oldb = unb[k];
+          const T cse_a = alpha * oldb;
+          const i64 tgt[6] = {k, up_row(ki) * n + kj, dn_row(ki) * n + kj, ki * n + lf_col(kj),
+                              ki * n + rt_col(kj), k};
+          const T v[6] = {oldb, cse_a, cse_a, cse_a, cse_a, T(4) * -cse_a};
+          for (int st = 0; st < 6; ++st)
+            if (tgt[st] == cell) { key_it[m] = k; key_st[m] = st; val[m] = v[st]; ++m; }
+        }
+        for (int x = 1; x < m; ++x)
+          for (int y = x; y > 0; --y) {
+            const bool later = key_it[y] > key_it[y - 1] ||
+                               (key_it[y] == key_it[y - 1] && key_st[y] < key_st[y - 1]);
+            if (!later) break;
+            std::swap(key_it[y], key_it[y - 1]);
+            std::swap(key_st[y], key_st[y - 1]);
+            std::swap(val[y], val[y - 1]);
+          }
+        T acc = ub[cell];
+        for (int x = 0; x < m; ++x) acc = acc + val[x];
+        ub[cell] = acc;
+      }
+    }
+#pragma omp parallel for schedule(static) num_threads(nthreads)
+    for (i64 idx = 0; idx < nn; ++idx) unb[idx] = T(0);
+  }
+  return alphab;
+}
+
+template <class T>
+void conv1d_relu_mse_b_omp(T* loss, const T* lossb, const T* x, T* xb, const T* w, T* wb,
+                           const T* t, T* tb, T* z, T* zb, T* r, T* rb,
+                           i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k, int nthreads) {
+  const i64 n_lo = n_l - n_k + 1, nw = n_o * n_c * n_k;
+  const T inv_n = T(1) / T(n_b * n_o * n_lo);
+  over_sample_blocks<T>(
+      n_b, nthreads, (size_t)(nw + 1),
+      [&](i64 lo, i64 hi, T* my) {
+        const i64 xo = lo * n_c * n_l, to = lo * n_o * n_lo;
+        conv1d_relu_mse_b_inv(my + nw, lossb, x + xo, xb + xo, w, my, t + to, tb + to, z + to,
+                              zb + to, r + to, rb + to, hi - lo, n_c, n_l, n_o, n_k, inv_n);
+      },
+      {{wb, nw}, {loss, 1}});
+}
+
+template <class T>
+void mlp2_ce_hv_omp(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
+                    const T* w1, T* w1b, const T* b1, T* b1b, const T* w2, T* w2b,
+                    const T* b2, T* b2b, T* h, T* hb, T* z, T* zb, T* p, T* pb,
+                    i64 n_s, i64 n_i, i64 n_h, i64 n_o,
+                    T* lossd, const T* lossbd, const T* xd, T* xbd, const T* yd, T* ybd,
+                    const T* w1d, T* w1bd, const T* b1d, T* b1bd, const T* w2d, T* w2bd,
+                    const T* b2d, T* b2bd, T* hd, T* hbd, T* zd, T* zbd, T* pd, T* pbd,
+                    int nthreads) {
+  const i64 nw1 = n_i * n_h, nw2 = n_h * n_o;
+  const i64 one = nw1 + n_h + nw2 + n_o + 1;  // w1b b1b w2b b2b loss
+  over_sample_blocks<T>(
+      n_s, nthreads, (size_t)(2 * one),
+      [&](i64 lo, i64 hi, T* my) {
+        T* mb = my;          // adjoint shadows
+        T* md = my + one;    // their tangents
+        const i64 io = lo * n_i, oo = lo * n_o, ho = lo * n_h;
+        mlp2_ce_hv(mb + nw1 + n_h + nw2 + n_o, lossb, x + io, xb + io, y + oo, yb + oo, w1, mb,
+                   b1, mb + nw1, w2, mb + nw1 + n_h, b2, mb + nw1 + n_h + nw2, h + ho, hb + ho,
+                   z + oo, zb + oo, p + oo, pb + oo, hi - lo, n_i, n_h, n_o,
+                   md + nw1 + n_h + nw2 + n_o, lossbd, xd + io, xbd + io, yd + oo, ybd + oo, w1d,
+                   md, b1d, md + nw1, w2d, md + nw1 + n_h, b2d, md + nw1 + n_h + nw2, hd + ho,
+                   hbd + ho, zd + oo, zbd + oo, pd + oo, pbd + oo);
+      },
+      {{w1b, nw1}, {b1b, n_h}, {w2b, nw2}, {b2b, n_o}, {loss, 1},
+       {w1bd, nw1}, {b1bd, n_h}, {w2bd, nw2}, {b2bd, n_o}, {lossd, 1}});
 }
 
 }  // namespace
@@ -750,6 +916,9 @@ void oracle_mlp2_ce_b_f128(MLP_B_ARGS(long double)) { mlp2_ce_b<long double>(MLP
 void oracle_mlp2_ce_b_f32_omp(MLP_B_ARGS(float), int nthreads) {
   mlp2_ce_b_omp<float>(MLP_B_PASS, nthreads);
 }
+void oracle_mlp2_ce_b_f64_omp(MLP_B_ARGS(double), int nthreads) {
+  mlp2_ce_b_omp<double>(MLP_B_PASS, nthreads);
+}
 
 #define MLP_HV_ARGS(T)                                                                     \
   MLP_B_ARGS(T), T *lossd, const T *lossbd, const T *xd, T *xbd, const T *yd, T *ybd,      \
@@ -761,6 +930,12 @@ void oracle_mlp2_ce_b_f32_omp(MLP_B_ARGS(float), int nthreads) {
 
 void oracle_mlp2_ce_hv_f64(MLP_HV_ARGS(double)) { mlp2_ce_hv<double>(MLP_HV_PASS); }
 void oracle_mlp2_ce_hv_f128(MLP_HV_ARGS(long double)) { mlp2_ce_hv<long double>(MLP_HV_PASS); }
+void oracle_mlp2_ce_hv_f64_omp(MLP_HV_ARGS(double), int nthreads) {
+  mlp2_ce_hv_omp<double>(MLP_HV_PASS, nthreads);
+}
+void oracle_mlp2_ce_hv_f128_omp(MLP_HV_ARGS(long double), int nthreads) {
+  mlp2_ce_hv_omp<long double>(MLP_HV_PASS, nthreads);
+}
 
 double oracle_heat2d_b_f64(double* loss, const double* lossb, double* u, double* ub, double* un,
                            double* unb, double alpha, double alphab, i64 n, i64 n_step,
@@ -793,6 +968,23 @@ void oracle_conv1d_relu_mse_b_f128(long double* loss, const long double* lossb,
                                    long double* rb, i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k) {
   conv1d_relu_mse_b<long double>(loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l,
                                  n_o, n_k);
+}
+
+#define CONV_B_ARGS(T)                                                                     \
+  T *loss, const T *lossb, const T *x, T *xb, const T *w, T *wb, const T *t, T *tb, T *z,   \
+      T *zb, T *r, T *rb, i64 n_b, i64 n_c, i64 n_l, i64 n_o, i64 n_k
+#define CONV_B_PASS loss, lossb, x, xb, w, wb, t, tb, z, zb, r, rb, n_b, n_c, n_l, n_o, n_k
+double oracle_heat2d_b_f64_omp(double* loss, const double* lossb, double* u, double* ub,
+                               double* un, double* unb, double alpha, double alphab, i64 n,
+                               i64 n_step, double* u_stack, int nthreads) {
+  return heat2d_b_omp<double>(loss, lossb, u, ub, un, unb, alpha, alphab, n, n_step, u_stack,
+                              nthreads);
+}
+void oracle_conv1d_relu_mse_b_f32_omp(CONV_B_ARGS(float), int nthreads) {
+  conv1d_relu_mse_b_omp<float>(CONV_B_PASS, nthreads);
+}
+void oracle_conv1d_relu_mse_b_f64_omp(CONV_B_ARGS(double), int nthreads) {
+  conv1d_relu_mse_b_omp<double>(CONV_B_PASS, nthreads);
 }
 
 void oracle_affine_ls_d_f64(double* loss, double* lossd, const double* w, const double* wd,

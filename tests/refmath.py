@@ -93,3 +93,30 @@ def rel_err(a, b) -> float:
     if den == 0.0:
         return float(num)
     return float(num / den)
+
+
+def ref_rel_err(a, b) -> float:
+    """The reference's element-wise relative error, max_i |a_i - b_i| /
+    max(|a_i|, |b_i|, 1) (_relerr_arr of the generated GPU parity script,
+    src/STADE.jl:18980)."""
+    a = np.asarray(a, dtype=np.float64).ravel()
+    b = np.asarray(b, dtype=np.float64).ravel()
+    if a.size == 0:
+        return 0.0
+    return float(np.max(np.abs(a - b) / np.maximum(np.maximum(np.abs(a), np.abs(b)), 1.0)))
+
+
+def elem_rel_err(a, b, floor_frac) -> float:
+    """Element-wise relative error against b with a floor scaled to the
+    array: max_i |a_i - b_i| / max(|b_i|, floor_frac * max_j |b_j|). With
+    floor_frac = 0 every element counts relative to itself (exact zeros in b
+    must then be exact in a)."""
+    a = np.asarray(a, dtype=np.float64).ravel()
+    b = np.asarray(b, dtype=np.float64).ravel()
+    if a.size == 0:
+        return 0.0
+    d = np.abs(a - b)
+    den = np.maximum(np.abs(b), floor_frac * float(np.max(np.abs(b))))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        r = np.where(d == 0.0, 0.0, d / den)
+    return float(np.max(r))

@@ -205,3 +205,75 @@ def test_hvp_against_long_double_truth():
     cases.oracle_mlp_hv(tr, ints, truth=True)
     for k in ("w1bd", "b1bd", "w2bd", "b2bd", "xbd", "ybd", "w1b", "xb", "hd", "zd", "pd"):
         assert rel_err(st[k], tr[k]) < 1e-12, k
+
+
+# ---- the sample-parallel oracle variants (full-size checks, CPU baseline) ----
+def _omp_vs_serial(state_fn, args, ints_keys, run, summed, threads=3):
+    """Per-sample outputs bit-identical to the serial sweep; the summed
+    shadows differ only in the order the blocks' sums are added."""
+    st, ints = state_fn()
+    a, b = cases.copy_state(st), cases.copy_state(st)
+    run(a, ints, None)
+    run(b, ints, threads)
+    for k in args:
+        if k in summed:
+            scale = max(1.0, float(np.abs(a[k]).max()))
+            assert float(np.abs(a[k] - b[k]).max()) <= 1e-5 * scale, k
+        else:
+            assert np.array_equal(a[k], b[k]), k
+
+
+def test_parallel_mlp2_ce_b_matches_serial():
+    from oracle import oracle as orc
+    for dt in (np.float32, np.float64):
+        def run(st, ints, threads):
+            orc.mlp2_ce_b(*[st[a] for a in cases.MLP_ARGS], ints["n_s"], ints["n_i"], ints["n_h"],
+                          ints["n_o"], threads=threads)
+        _omp_vs_serial(lambda: cases.mlp_state(37, 12, 8, 5, dtype=dt, seeded=True),
+                       cases.MLP_ARGS, None, run, {"w1b", "b1b", "w2b", "b2b", "loss"})
+
+
+def test_parallel_conv1d_relu_mse_b_keeps_the_whole_batch_mean():
+    from oracle import oracle as orc
+    for dt in (np.float32, np.float64):
+        def run(st, ints, threads):
+            orc.conv1d_relu_mse_b(*[st[a] for a in cases.CONV_ARGS], ints["n_b"], ints["n_c"],
+                                  ints["n_l"], ints["n_o"], ints["n_k"], threads=threads)
+        _omp_vs_serial(lambda: cases.conv_state(5, 3, 20, 4, 3, dtype=dt, seeded=True),
+                       cases.CONV_ARGS, None, run, {"wb", "loss"})
+
+
+def test_parallel_mlp2_ce_hv_matches_serial():
+    from oracle import oracle as orc
+
+    def run(st, ints, threads, truth=False):
+        orc.mlp2_ce_hv(*[st[a] for a in cases.MLP_ARGS], ints["n_s"], ints["n_i"], ints["n_h"],
+                       ints["n_o"], *[st[a] for a in cases.MLP_TAN], threads=threads, truth=truth)
+    summed = {"w1b", "b1b", "w2b", "b2b", "loss", "w1bd", "b1bd", "w2bd", "b2bd", "lossd"}
+    _omp_vs_serial(lambda: cases.mlp_hv_state(23, 12, 8, 5, seeded=True),
+                   cases.MLP_ARGS + cases.MLP_TAN, None, run, summed)
+    # the long-double instantiation as well
+    st, ints = cases.mlp_hv_state(23, 12, 8, 5, seeded=True)
+    a, b = cases.copy_state(st), cases.copy_state(st)
+    run(a, ints, None, truth=True)
+    run(b, ints, 3, truth=True)
+    for k in cases.MLP_ARGS + cases.MLP_TAN:
+        scale = max(1.0, float(np.abs(a[k]).max()))
+        assert float(np.abs(a[k] - b[k]).max()) <= 1e-15 * scale, k
+
+
+@pytest.mark.parametrize("n,n_step", [(1, 3), (2, 2), (3, 4), (5, 3), (17, 5), (64, 2)])
+def test_parallel_heat2d_b_bit_identical_to_serial(n, n_step):
+    """The parallel C3 oracle gathers each cell's additions in the serial
+    scatter's order: every field, the tape, loss and alphab bit for bit
+    (wrapped neighbours, n = 1 and 2 where neighbours coincide, included)."""
+    from oracle import oracle as orc
+    st, ints = cases.heat_state(n, n_step, seeded=True)
+    a, b = cases.copy_state(st), cases.copy_state(st)
+    ra = orc.heat2d_b(*[a[k] for k in cases.HEAT_ARGS], ints["alpha"], ints["alphab"], n, n_step,
+                      a["u_stack"])
+    rb = orc.heat2d_b(*[b[k] for k in cases.HEAT_ARGS], ints["alpha"], ints["alphab"], n, n_step,
+                      b["u_stack"], threads=4)
+    assert ra == rb
+    for k in st:
+        assert np.array_equal(a[k], b[k]), k

@@ -48,3 +48,25 @@ def test_generation_independent_of_thread_count():
         outs.append(subprocess.run([sys.executable, "-c", code % root], env=env, check=True,
                                    capture_output=True, text=True).stdout)
     assert outs[0] == outs[1]
+
+
+def test_oracle_generator_matches_the_library_bit_for_bit():
+    """The oracle side's own generator (oracle/synth.cc, used by the bench's
+    reference arm so that it never loads the product library) draws the same
+    bits as the library's, for every configuration's recipe and across the
+    2^20-element chunk boundary."""
+    from oracle import oracle as orc
+    og = orc.generator()
+    cases = [("affine_ls_inputs", (37, 9, 5)),
+             ("mlp2_ce_inputs", (300, 132, 20, 10)),
+             ("mlp2_ce_hv_inputs", (64, 16, 8, 10)),
+             ("heat2d_inputs", (1100,)),                  # 1.21 M > 2^20 elements
+             ("conv1d_relu_mse_inputs", (3, 5, 40, 4, 3))]
+    for name, args in cases:
+        a, b = getattr(synth, name)(*args), getattr(og, name)(*args)
+        assert a.keys() == b.keys(), name
+        for k in a:
+            assert a[k].dtype == b[k].dtype and np.array_equal(a[k], b[k]), (name, k)
+    assert og.seed("abc", "x") == synth.seed("abc", "x")
+    for dt in (np.float32, np.float64):
+        assert np.array_equal(og.onehot(2 ** 20 + 7, 10, 5, dt), synth.onehot(2 ** 20 + 7, 10, 5, dt))
