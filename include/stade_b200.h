@@ -83,6 +83,15 @@ size_t      stade_workspace_cached_bytes(void);
  * tensor-core pipeline): 0 = none; nonzero = a wait ran out and the results of
  * that call are invalid. Reading it waits for the device and clears it. */
 int         stade_device_error(void);
+/* Check of the device-side wait guard (no counterpart in the reference, whose
+ * kernels have no bounded waits): one kernel waits on an mbarrier nothing
+ * ever arrives on, with the tensor-core kernels' own wait loop limited to
+ * wait_cycles SM clock cycles (1000 .. ~4e9, the kernels' own limit); the wait
+ * gives up, sets the device error word and the kernel returns. Synchronises
+ * the stream. Returns STADE_ETIMEDOUT when the guard worked; afterwards
+ * stade_device_error() reads nonzero (and clears it), and the context stays
+ * usable. */
+stade_status stade_check_bounded_wait(int64_t wait_cycles, const stade_opts* opts);
 void        stade_profile_enable(int on);
 int         stade_profile_read(char* names, int name_len, double* ms, int* counts, int max);
 
@@ -340,6 +349,68 @@ stade_status stade_mlp2_ce_b_check_replicas_f32(const float* w1, const float* b1
                                                 int64_t n_i, int64_t n_h, int64_t n_o,
                                                 stade_comm* comm, uint64_t* bad_mask,
                                                 const stade_opts* opts);
+
+/* The generated epilogue functions of conv1d_relu_mse in adjoint mode with
+ * per_sample = [:x, :t] (`conv1d_relu_mse_b_reset_accum!` ...
+ * `conv1d_relu_mse_b_check_replicas`, ddpgen_fname src/STADE.jl:17578-17582;
+ * roles by ddpgen_roles, src/STADE.jl:17404):
+ *   :accum  wb                    :reduced loss       :seed lossb
+ *   :local  xb tb zb rb           :shared  w
+ * The mean loss (1 / (n_b n_o n_lo) inside the primal) makes a rank's loss
+ * seed and summed loss carry its own batch's count: scale lossb by
+ * n_local / n_global before the sweep and the summed loss by the same factor
+ * after (exact for power-of-two rank counts). */
+stade_status stade_conv1d_relu_mse_b_reset_accum_f32(float* wb, int64_t n_o, int64_t n_c,
+                                                     int64_t n_k, const stade_opts* opts);
+stade_status stade_conv1d_relu_mse_b_reset_reduced_f32(float* loss, const stade_opts* opts);
+stade_status stade_conv1d_relu_mse_b_reset_local_f32(float* xb, float* tb, float* zb, float* rb,
+                                                     int64_t n_b, int64_t n_c, int64_t n_l,
+                                                     int64_t n_o, int64_t n_k,
+                                                     const stade_opts* opts);
+stade_status stade_conv1d_relu_mse_b_allreduce_accum_f32(float* wb, int64_t n_o, int64_t n_c,
+                                                         int64_t n_k, int64_t n_local,
+                                                         stade_comm* comm, int64_t* n_global,
+                                                         const stade_opts* opts);
+stade_status stade_conv1d_relu_mse_b_allreduce_reduced_f32(float* loss, stade_comm* comm,
+                                                           const stade_opts* opts);
+stade_status stade_conv1d_relu_mse_b_check_replicas_f32(const float* w, const float* lossb,
+                                                        int64_t n_o, int64_t n_c, int64_t n_k,
+                                                        stade_comm* comm, uint64_t* bad_mask,
+                                                        const stade_opts* opts);
+
+/* The generated epilogue functions of mlp2_ce in hvp mode, with the `_hv`
+ * suffix ddpgen_mode_suffix gives that mode (`mlp2_ce_hv_reset_accum!` ...,
+ * src/STADE.jl:17578-17582), per_sample = [:x, :y]:
+ *   :accum   w1b b1b w2b b2b w1bd b1bd w2bd b2bd     :reduced loss lossd
+ *   :local   xb yb hb zb pb xbd ybd hbd zbd pbd      :seed    lossb lossbd
+ *   :shared  w1 b1 w2 b2 w1d b1d w2d b2d
+ * allreduce_accum sums all eight :accum buffers in one NCCL bucket. */
+stade_status stade_mlp2_ce_hv_reset_accum_f64(double* w1b, double* b1b, double* w2b, double* b2b,
+                                              double* w1bd, double* b1bd, double* w2bd,
+                                              double* b2bd, int64_t n_i, int64_t n_h, int64_t n_o,
+                                              const stade_opts* opts);
+stade_status stade_mlp2_ce_hv_reset_reduced_f64(double* loss, double* lossd,
+                                                const stade_opts* opts);
+stade_status stade_mlp2_ce_hv_reset_local_f64(double* xb, double* yb, double* hb, double* zb,
+                                              double* pb, double* xbd, double* ybd, double* hbd,
+                                              double* zbd, double* pbd, int64_t n_s, int64_t n_i,
+                                              int64_t n_h, int64_t n_o, const stade_opts* opts);
+stade_status stade_mlp2_ce_hv_allreduce_accum_f64(double* w1b, double* b1b, double* w2b,
+                                                  double* b2b, double* w1bd, double* b1bd,
+                                                  double* w2bd, double* b2bd, int64_t n_i,
+                                                  int64_t n_h, int64_t n_o, int64_t n_local,
+                                                  stade_comm* comm, int64_t* n_global,
+                                                  const stade_opts* opts);
+stade_status stade_mlp2_ce_hv_allreduce_reduced_f64(double* loss, double* lossd, stade_comm* comm,
+                                                    const stade_opts* opts);
+stade_status stade_mlp2_ce_hv_check_replicas_f64(const double* w1, const double* b1,
+                                                 const double* w2, const double* b2,
+                                                 const double* w1d, const double* b1d,
+                                                 const double* w2d, const double* b2d,
+                                                 const double* lossb, const double* lossbd,
+                                                 int64_t n_i, int64_t n_h, int64_t n_o,
+                                                 stade_comm* comm, uint64_t* bad_mask,
+                                                 const stade_opts* opts);
 
 /* ---------------------------------------------------------------------------
  * C3 over several GPUs: heat2d_b on row slabs. No reference counterpart (the

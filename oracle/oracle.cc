@@ -57,6 +57,32 @@ template <class T> inline T jl_max(T a, T b) {
   if (b > a) return b;
   return std::signbit(a) ? b : a;
 }
+// ---- Rules of the generated code, shared by the five sweeps below and by the
+// restated reference exemplars at the end of this file (which pin them: the
+// exemplars are compared bit for bit with the reference's own generated text,
+// run by an interpreter). Each returns the expression the generator writes.
+// A consumed adjoint: `__oldb = vb; vb = 0.0` (agen_backward_assign,
+// src/STADE.jl:6605; affine_loss_b.jl:16-17).
+template <class T> inline T take(T& vb) {
+  const T o = vb;
+  vb = T(0);
+  return o;
+}
+// d(v^2)/dv = `2 * v` (der_partials_pow with a literal 2, src/STADE.jl:1369;
+// affine_loss_b.jl:13, `(2__cse_0)` in mlp1d_b.jl:32).
+template <class T> inline T d_sq(T v) { return T(2) * v; }
+// d tanh(s)/ds = `1.0 - tanh(s) ^ 2` from the recomputed tanh (der_partials_tanh,
+// src/STADE.jl:1462; mlp1d_b.jl:50); th = tanh(s), th^2 = th * th (literal_pow).
+template <class T> inline T d_tanh(T th) { return T(1) - th * th; }
+// d max(a, b)/da = `0.5 * (1 + sign(a - b))`, 0.5 at a tie (der_partials_maxmin,
+// src/STADE.jl:1489-1501).
+template <class T> inline T d_max(T a, T b);
+// The HVP twin of `sb += d_tanh(th) * oldb` (hvp_double_stmt, src/STADE.jl:6904):
+// `oldb * -((2 th) * (g * sd)) + g * oldbd`, g = d_tanh(th) (mlp1d_hv.jl:92-93).
+template <class T> inline T d_tanh_tangent(T th, T g, T sd, T oldb, T oldbd) {
+  return oldb * -((T(2) * th) * (g * sd)) + g * oldbd;
+}
+
 inline float jl_tanh(float x) { return std::tanh(x); }
 inline double jl_tanh(double x) { return std::tanh(x); }
 inline long double jl_tanh(long double x) { return tanhl(x); }
@@ -66,6 +92,7 @@ inline long double jl_exp(long double x) { return expl(x); }
 inline float jl_log(float x) { return std::log(x); }
 inline double jl_log(double x) { return std::log(x); }
 inline long double jl_log(long double x) { return logl(x); }
+template <class T> inline T d_max(T a, T b) { return T(0.5) * (T(1) + jl_sign(a - b)); }
 
 // ---------------------------------------------------------------------------
 // C1 affine_ls_b. Follows affine_loss_b.jl:5-23 (per-element adjoint with
@@ -90,21 +117,19 @@ void affine_ls_b(T* loss, const T* lossb, const T* w, T* wb, const T* b, T* bb,
   // backward sweep
   for (i64 idx2 = n_s * n_o - 1; idx2 >= 0; --idx2) {  // for idx2 = n_s * n_o:-1:1
     const T cse0 = y[idx2] - t[idx2];
-    const T cse1 = (T(0.5) * (T(2) * cse0)) * lossb[0];
+    const T cse1 = (T(0.5) * d_sq(cse0)) * lossb[0];
     yb[idx2] = yb[idx2] + cse1;
     tb[idx2] = tb[idx2] + -cse1;
   }
   for (i64 idx = n_s * n_o - 1; idx >= 0; --idx) {      // for idx = n_s * n_o:-1:1
     const i64 i_s = idx / n_o, i_o = idx % n_o;
-    T oldb = yb[idx];
-    yb[idx] = T(0);
+    T oldb = take(yb[idx]);
     sb = sb + oldb;
     for (i64 k = n_i - 1; k >= 0; --k) {                 // for i_k = n_i:-1:1
       wb[i_o * n_i + k] = wb[i_o * n_i + k] + x[i_s * n_i + k] * sb;
       xb[i_s * n_i + k] = xb[i_s * n_i + k] + w[i_o * n_i + k] * sb;
     }
-    oldb = sb;
-    sb = T(0);
+    oldb = take(sb);
     bb[i_o] = bb[i_o] + oldb;
   }
   (void)s;
@@ -178,8 +203,7 @@ void mlp2_ce_b(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
     row_sumb = T(0);
     // p[c] = exp(z[c] - row_max)
     for (i64 c = n_o - 1; c >= 0; --c) {
-      const T oldb = pbr[c];
-      pbr[c] = T(0);
+      const T oldb = take(pbr[c]);
       const T cse = jl_exp(zr[c] - row_max) * oldb;
       zbr[c] = zbr[c] + cse;
       row_maxb = row_maxb + -cse;
@@ -187,31 +211,27 @@ void mlp2_ce_b(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
     // row_max = max(row_max, z[c]), for i_c = n_o:-1:2
     for (i64 c = n_o - 1; c >= 1; --c) {
       const T m_prev = max_tape[c];
-      const T oldb = row_maxb;
-      row_maxb = T(0);
+      const T oldb = take(row_maxb);
       const T zc = zr[c];
-      row_maxb = row_maxb + (T(0.5) * (T(1) + jl_sign(m_prev - zc))) * oldb;
-      zbr[c] = zbr[c] + (T(0.5) * (T(1) + jl_sign(zc - m_prev))) * oldb;
+      row_maxb = row_maxb + d_max(m_prev, zc) * oldb;
+      zbr[c] = zbr[c] + d_max(zc, m_prev) * oldb;
     }
     // row_max = z[1]
     {
-      const T oldb = row_maxb;
-      row_maxb = T(0);
+      const T oldb = take(row_maxb);
       zbr[0] = zbr[0] + oldb;
     }
   }
   // reverse of the output-logit loop: for idx2 = n_s * n_o:-1:1
   for (i64 idx2 = n_s * n_o - 1; idx2 >= 0; --idx2) {
     const i64 i_s = idx2 / n_o, c = idx2 % n_o;
-    T oldb = zb[idx2];
-    zb[idx2] = T(0);
+    T oldb = take(zb[idx2]);
     s2b = s2b + oldb;
     for (i64 k = n_h - 1; k >= 0; --k) {
       w2b[k * n_o + c] = w2b[k * n_o + c] + h[i_s * n_h + k] * s2b;
       hb[i_s * n_h + k] = hb[i_s * n_h + k] + w2[k * n_o + c] * s2b;
     }
-    oldb = s2b;
-    s2b = T(0);
+    oldb = take(s2b);
     b2b[c] = b2b[c] + oldb;
   }
   // reverse of the hidden loop: for idx = n_s * n_h:-1:1
@@ -219,18 +239,16 @@ void mlp2_ce_b(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
     const i64 i_s = idx / n_h, j = idx % n_h;
     T s1 = b1[j];
     for (i64 k = 0; k < n_i; ++k) s1 = s1 + x[i_s * n_i + k] * w1[k * n_h + j];
-    T oldb = hb[idx];
-    hb[idx] = T(0);
+    T oldb = take(hb[idx]);
     const T th = jl_tanh(s1);
-    s1b = s1b + (T(1) - th * th) * oldb;
+    s1b = s1b + d_tanh(th) * oldb;
     for (i64 k = 0; k < n_i; ++k) {
       const T cse_w = w1[k * n_h + j];
       const T cse_x = x[i_s * n_i + k];
       w1b[k * n_h + j] = w1b[k * n_h + j] + cse_x * s1b;
       xb[i_s * n_i + k] = xb[i_s * n_i + k] + cse_w * s1b;
     }
-    oldb = s1b;
-    s1b = T(0);
+    oldb = take(s1b);
     b1b[j] = b1b[j] + oldb;
   }
 }
@@ -277,8 +295,8 @@ void mlp2_ce_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
     T* pr = p + i_s * n_o; T* pdr = pd + i_s * n_o;
     T m = zr[0], md = zdr[0];
     for (i64 c = 1; c < n_o; ++c) {
-      const T g1 = T(0.5) * (T(1) + jl_sign(m - zr[c]));
-      const T g2 = T(0.5) * (T(1) + jl_sign(zr[c] - m));
+      const T g1 = d_max(m, zr[c]);
+      const T g2 = d_max(zr[c], m);
       md = g1 * md + g2 * zdr[c];
       m = jl_max(m, zr[c]);
     }
@@ -306,8 +324,8 @@ void mlp2_ce_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
     T m = zr[0], md = zdr[0];
     for (i64 c = 1; c < n_o; ++c) {
       mt[c] = m; mdt[c] = md;
-      const T g1 = T(0.5) * (T(1) + jl_sign(m - zr[c]));
-      const T g2 = T(0.5) * (T(1) + jl_sign(zr[c] - m));
+      const T g1 = d_max(m, zr[c]);
+      const T g2 = d_max(zr[c], m);
       md = g1 * md + g2 * zdr[c];
       m = jl_max(m, zr[c]);
     }
@@ -343,8 +361,7 @@ void mlp2_ce_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
     }
     rsbd = T(0); rsb = T(0);
     for (i64 c = n_o - 1; c >= 0; --c) {
-      const T oldbd = pbdr[c], oldb = pbr[c];
-      pbdr[c] = T(0); pbr[c] = T(0);
+      const T oldbd = take(pbdr[c]), oldb = take(pbr[c]);
       const T e = jl_exp(zr[c] - m);
       const T ed = e * (zdr[c] - md);
       const T csed = ed * oldb + e * oldbd;
@@ -356,27 +373,24 @@ void mlp2_ce_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
     }
     for (i64 c = n_o - 1; c >= 1; --c) {
       const T m_prev = mt[c];
-      const T oldbd = mbd, oldb = mb;
-      mbd = T(0); mb = T(0);
+      const T oldbd = take(mbd), oldb = take(mb);
       const T zc = zr[c];
-      const T g1 = T(0.5) * (T(1) + jl_sign(m_prev - zc));
-      const T g2 = T(0.5) * (T(1) + jl_sign(zc - m_prev));
+      const T g1 = d_max(m_prev, zc);
+      const T g2 = d_max(zc, m_prev);
       mbd = mbd + g1 * oldbd;
       mb = mb + g1 * oldb;
       zbdr[c] = zbdr[c] + g2 * oldbd;
       zbr[c] = zbr[c] + g2 * oldb;
     }
     {
-      const T oldbd = mbd, oldb = mb;
-      mbd = T(0); mb = T(0);
+      const T oldbd = take(mbd), oldb = take(mb);
       zbdr[0] = zbdr[0] + oldbd;
       zbr[0] = zbr[0] + oldb;
     }
   }
   for (i64 idx2 = n_s * n_o - 1; idx2 >= 0; --idx2) {
     const i64 i_s = idx2 / n_o, c = idx2 % n_o;
-    T oldbd = zbd[idx2], oldb = zb[idx2];
-    zbd[idx2] = T(0); zb[idx2] = T(0);
+    T oldbd = take(zbd[idx2]), oldb = take(zb[idx2]);
     s2bd = s2bd + oldbd;
     s2b = s2b + oldb;
     for (i64 k = n_h - 1; k >= 0; --k) {
@@ -387,8 +401,7 @@ void mlp2_ce_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
       hbd[i_s * n_h + k] = hbd[i_s * n_h + k] + (s2b * w2d[k * n_o + c] + wv * s2bd);
       hb[i_s * n_h + k] = hb[i_s * n_h + k] + wv * s2b;
     }
-    oldbd = s2bd; oldb = s2b;
-    s2bd = T(0); s2b = T(0);
+    oldbd = take(s2bd); oldb = take(s2b);
     b2bd[c] = b2bd[c] + oldbd;
     b2b[c] = b2b[c] + oldb;
   }
@@ -400,15 +413,12 @@ void mlp2_ce_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb,
       s1d = s1d + (xv * w1d[k * n_h + j] + wv * xd[i_s * n_i + k]);
       s1 = s1 + xv * wv;
     }
-    T oldbd = hbd[idx], oldb = hb[idx];
-    hbd[idx] = T(0); hb[idx] = T(0);
+    T oldbd = take(hbd[idx]), oldb = take(hb[idx]);
     const T th = jl_tanh(s1);
-    const T g = T(1) - th * th;
-    // mlp1d_hv.jl:108-109: s2bd += __oldb * -((2 tanh) * (g * s2d)) + g * __oldb_d
-    s1bd = s1bd + (oldb * -((T(2) * th) * (g * s1d)) + g * oldbd);
+    const T g = d_tanh(th);
+    s1bd = s1bd + d_tanh_tangent(th, g, s1d, oldb, oldbd);
     s1b = s1b + g * oldb;
-    oldbd = s1bd; oldb = s1b;
-    s1bd = T(0); s1b = T(0);
+    oldbd = take(s1bd); oldb = take(s1b);
     for (i64 k = 0; k < n_i; ++k) {
       const T wdv = w1d[k * n_h + j], wv = w1[k * n_h + j];
       const T xdv = xd[i_s * n_i + k], xv = x[i_s * n_i + k];
@@ -450,19 +460,17 @@ T heat2d_b(T* loss, const T* lossb, T* u, T* ub, T* un, T* unb, T alpha, T alpha
   }
   for (i64 idx3 = 0; idx3 < nn; ++idx3) loss[0] = loss[0] + u[idx3] * u[idx3];
   // backward sweep
-  for (i64 idx3 = nn - 1; idx3 >= 0; --idx3) ub[idx3] = ub[idx3] + (T(2) * u[idx3]) * lossb[0];
+  for (i64 idx3 = nn - 1; idx3 >= 0; --idx3) ub[idx3] = ub[idx3] + d_sq(u[idx3]) * lossb[0];
   for (i64 it = n_step - 1; it >= 0; --it) {           // for i_t = n_step:-1:1
     for (i64 idx2 = nn - 1; idx2 >= 0; --idx2) {
       u[idx2] = u_stack[idx2 + it * nn];
-      const T oldb = ub[idx2];
-      ub[idx2] = T(0);
+      const T oldb = take(ub[idx2]);
       unb[idx2] = unb[idx2] + oldb;
     }
     for (i64 idx = nn - 1; idx >= 0; --idx) {
       i64 up, dn, lf, rt;
       nbrs(idx, up, dn, lf, rt);
-      const T oldb = unb[idx];
-      unb[idx] = T(0);
+      const T oldb = take(unb[idx]);
       const T c = u[idx];
       const T cse_a = alpha * oldb;
       ub[idx] = ub[idx] + oldb;
@@ -511,18 +519,16 @@ void conv1d_relu_mse_b_inv(T* loss, const T* lossb, const T* x, T* xb, const T* 
   }
   for (i64 idx2 = nt - 1; idx2 >= 0; --idx2) {
     const T cse0 = r[idx2] - t[idx2];
-    const T cse1 = (inv_n * (T(2) * cse0)) * lossb[0];
+    const T cse1 = (inv_n * d_sq(cse0)) * lossb[0];
     rb[idx2] = rb[idx2] + cse1;
     tb[idx2] = tb[idx2] + -cse1;
   }
   for (i64 idx = nt - 1; idx >= 0; --idx) {
     const i64 i_b = idx / (n_o * n_lo), i_o = (idx / n_lo) % n_o, i_t = idx % n_lo;
     a = conv_at(idx);
-    T oldb = rb[idx];
-    rb[idx] = T(0);
-    ab = ab + (T(0.5) * (T(1) + jl_sign(a - T(0)))) * oldb;
-    oldb = zb[idx];
-    zb[idx] = T(0);
+    T oldb = take(rb[idx]);
+    ab = ab + d_max(a, T(0)) * oldb;
+    oldb = take(zb[idx]);
     ab = ab + oldb;
     for (i64 c = n_c - 1; c >= 0; --c) {
       for (i64 k = n_k - 1; k >= 0; --k) {
@@ -610,8 +616,8 @@ void mlp2_ce_d(T* loss, T* lossd, const T* x, const T* xd, const T* y, const T* 
     T* pr = p + i_s * n_o; T* pdr = pd + i_s * n_o;
     T m = zr[0], md = zdr[0];
     for (i64 c = 1; c < n_o; ++c) {
-      const T g1 = T(0.5) * (T(1) + jl_sign(m - zr[c]));
-      const T g2 = T(0.5) * (T(1) + jl_sign(zr[c] - m));
+      const T g1 = d_max(m, zr[c]);
+      const T g2 = d_max(zr[c], m);
       md = g1 * md + g2 * zdr[c];
       m = jl_max(m, zr[c]);
     }
@@ -676,7 +682,7 @@ void conv1d_relu_mse_d(T* loss, T* lossd, const T* x, const T* xd, const T* w, c
       }
     zd[idx] = ad;
     z[idx] = a;
-    rd[idx] = (T(0.5) * (T(1) + jl_sign(a - T(0)))) * ad;
+    rd[idx] = d_max(a, T(0)) * ad;
     r[idx] = jl_max(a, T(0));
   }
   const T inv_n = T(1) / T(nt);
@@ -886,9 +892,362 @@ void mlp2_ce_hv_omp(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* y
        {w1bd, nw1}, {b1bd, n_h}, {w2bd, nw2}, {b2bd, n_o}, {lossd, 1}});
 }
 
+
+// ---------------------------------------------------------------------------
+// Restated reference exemplars. Seven sweeps the reference ships as generated
+// text (test/val-corpus/*.jl, written by STADE with keep_push_pop = false and
+// fuse_ii_loops = true), restated statement for statement on the rule helpers
+// above. tests/test_exemplar_pins.py runs each on seeded inputs and requires
+// the results to equal, bit for bit, the reference text itself run by the
+// interpreter tests/jlsub.py (fixtures written by
+// tests/golden/make_exemplar_golden.py). That pins the rules the five sweeps
+// use (take, d_sq, d_tanh, d_max through mlp1d's max-free form, d_tanh_tangent,
+// the tape slot formula, the recompute of locals, the HVP doubling order).
+// Loop direction: under fuse_ii_loops = true the generator emits an
+// iteration-independent loop's adjoint un-reversed (agen_emit_ii_loop,
+// src/STADE.jl:6309; mlp1d_b.jl:58, 77 run ascending), as restated here. The
+// five sweeps above target the library default, fuse_ii_loops = false, under
+// which every backward loop reverses (src/STADE.jl:6553-6557).
+
+// affine_loss_b.jl:5-23
+template <class T>
+void ex_affine_loss_b(T* loss, const T* lossb, const T* u, T* ub, const T* a, T* ab, const T* b,
+                      T* bb, T* v, T* vb, i64 n) {
+  for (i64 i = 0; i < n; ++i) v[i] = a[i] * u[i] + b[i];
+  for (i64 i = 0; i < n; ++i) loss[0] = loss[0] + v[i] * v[i];
+  for (i64 i = n - 1; i >= 0; --i) vb[i] = vb[i] + d_sq(v[i]) * lossb[0];
+  for (i64 i = n - 1; i >= 0; --i) {
+    const T oldb = take(vb[i]);
+    ab[i] = ab[i] + u[i] * oldb;
+    ub[i] = ub[i] + a[i] * oldb;
+    bb[i] = bb[i] + oldb;
+  }
+}
+
+// matvec_loss_b.jl:5-27; a is i_m x i_n, column-major (a[i, j] at j * m + i)
+template <class T>
+void ex_matvec_loss_b(T* loss, const T* lossb, const T* a, T* ab, const T* u, T* ub, T* v, T* vb,
+                      i64 m, i64 n) {
+  for (i64 idx = 0; idx < m * n; ++idx) {
+    const i64 i = idx / n, j = idx % n;
+    v[i] = v[i] + a[j * m + i] * u[j];
+  }
+  for (i64 i = 0; i < m; ++i) loss[0] = loss[0] + v[i] * v[i];
+  for (i64 i = m - 1; i >= 0; --i) vb[i] = vb[i] + d_sq(v[i]) * lossb[0];
+  for (i64 idx = m * n - 1; idx >= 0; --idx) {
+    const i64 i = idx / n, j = idx % n;
+    const T cse = vb[i];
+    ab[j * m + i] = ab[j * m + i] + u[j] * cse;
+    ub[j] = ub[j] + a[j * m + i] * cse;
+  }
+}
+
+// stencil_loss_b.jl:5-23 (the generated scatter adjoint of the 3-point stencil)
+template <class T>
+void ex_stencil_loss_b(T* loss, const T* lossb, const T* u, T* ub, T* w, T* wb, i64 n) {
+  for (i64 i = 1; i < n - 1; ++i) w[i] = (u[i - 1] - T(2) * u[i]) + u[i + 1];
+  for (i64 i = 1; i < n - 1; ++i) loss[0] = loss[0] + w[i] * w[i];
+  for (i64 i = n - 2; i >= 1; --i) wb[i] = wb[i] + d_sq(w[i]) * lossb[0];
+  for (i64 i = n - 2; i >= 1; --i) {
+    const T oldb = take(wb[i]);
+    ub[i - 1] = ub[i - 1] + oldb;
+    ub[i] = ub[i] + T(2) * -oldb;
+    ub[i + 1] = ub[i + 1] + oldb;
+  }
+}
+
+// advection_b.jl:6-37: time loop with the overwritten du taped at slot
+// ((i_x - 2) + (i_ - 1) * (nnode - 1)) + 1; the scalar arguments' adjoints
+// in / out (the generated code returns (cb, dxb, dtb))
+template <class T>
+void ex_advection_b(T* u, T* ub, T* du, T* dub, T c, T* cb, T dx, T* dxb, T dt, T* dtb,
+                    i64 nstep, i64 nnode, T* du_stack) {
+  const i64 width = nnode - 1;
+  for (i64 it = 0; it < nstep; ++it) {
+    for (i64 x = 1; x < nnode; ++x) {
+      du_stack[(x - 1) + it * width] = du[x];
+      du[x] = u[x] - u[x - 1];
+    }
+    for (i64 x = 1; x < nnode; ++x) u[x] = u[x] - (c * dt * du[x]) / dx;
+  }
+  for (i64 it = nstep - 1; it >= 0; --it) {
+    for (i64 x = nnode - 1; x >= 1; --x) {
+      const T cse0 = du[x];
+      const T cse1 = -(ub[x]);
+      const T cse2 = (T(1) / dx) * cse1;
+      *cb = *cb + (dt * cse0) * cse2;
+      *dtb = *dtb + (c * cse0) * cse2;
+      dub[x] = dub[x] + (c * dt) * cse2;
+      *dxb = *dxb + -((c * dt * cse0) / (dx * dx)) * cse1;
+    }
+    for (i64 x = nnode - 1; x >= 1; --x) {
+      du[x] = du_stack[(x - 1) + it * width];
+      const T oldb = take(dub[x]);
+      ub[x] = ub[x] + oldb;
+      ub[x - 1] = ub[x - 1] + -oldb;
+    }
+  }
+}
+
+// selfrace_conv_b.jl:5-35: valid convolution, the local `a` reset per
+// output, `loss += z * z` giving two adjoint adds, xb at the self-overlapping
+// index t + ci - 1
+template <class T>
+void ex_selfrace_conv_b(const T* x, T* xb, const T* w, T* wb, T* z, T* zb, T* loss,
+                        const T* lossb, i64 n, i64 nc) {
+  T a = T(0), ab = T(0);
+  for (i64 t = 0; t < n; ++t) {
+    a = T(0);
+    for (i64 ci = 0; ci < nc; ++ci) a = a + x[t + ci] * w[ci];
+    z[t] = a;
+  }
+  for (i64 m = 0; m < n; ++m) {
+    const T cse0 = z[m];
+    loss[0] = loss[0] + cse0 * cse0;
+  }
+  for (i64 m = n - 1; m >= 0; --m) {
+    const T cse1 = z[m] * lossb[0];
+    zb[m] = zb[m] + cse1;
+    zb[m] = zb[m] + cse1;
+  }
+  for (i64 t = n - 1; t >= 0; --t) {
+    const T oldb = take(zb[t]);
+    ab = ab + oldb;
+    for (i64 ci = nc - 1; ci >= 0; --ci) {
+      xb[t + ci] = xb[t + ci] + w[ci] * ab;
+      wb[ci] = wb[ci] + x[t + ci] * ab;
+    }
+    ab = T(0);
+  }
+}
+
+// mlp1d_b.jl:5-78: 1 -> n_h -> n_h -> 1 tanh MLP, squared error; the hidden
+// loops' adjoints recompute their local sums and run ascending (ii loops)
+template <class T>
+void ex_mlp1d_b(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb, const T* w1,
+                T* w1b, const T* b1, T* b1b, const T* w2, T* w2b, const T* b2, T* b2b,
+                const T* w3, T* w3b, const T* b3, T* b3b, T* h1, T* h1b, T* h2, T* h2b, T* o,
+                T* ob, i64 nh) {
+  T s1 = T(0), s2 = T(0), s3 = T(0), s1b = T(0), s2b = T(0), s3b = T(0);
+  for (i64 j = 0; j < nh; ++j) {
+    s1 = w1[j] * x[0] + b1[j];
+    h1[j] = jl_tanh(s1);
+  }
+  for (i64 j2 = 0; j2 < nh; ++j2) {
+    s2 = b2[j2];
+    for (i64 k = 0; k < nh; ++k) s2 = s2 + w2[j2 * nh + k] * h1[k];
+    h2[j2] = jl_tanh(s2);
+  }
+  s3 = b3[0];
+  for (i64 k2 = 0; k2 < nh; ++k2) s3 = s3 + w3[k2] * h2[k2];
+  o[0] = s3;
+  const T cse0 = o[0] - y[0];
+  loss[0] = loss[0] + cse0 * cse0;
+  const T cse1 = d_sq(cse0) * lossb[0];
+  ob[0] = ob[0] + cse1;
+  yb[0] = yb[0] + -cse1;
+  T oldb = take(ob[0]);
+  s3b = s3b + oldb;
+  for (i64 k2 = nh - 1; k2 >= 0; --k2) {
+    w3b[k2] = w3b[k2] + h2[k2] * s3b;
+    h2b[k2] = h2b[k2] + w3[k2] * s3b;
+  }
+  oldb = take(s3b);
+  b3b[0] = b3b[0] + oldb;
+  for (i64 j2 = 0; j2 < nh; ++j2) {
+    s2 = b2[j2];
+    for (i64 k = 0; k < nh; ++k) s2 = s2 + w2[j2 * nh + k] * h1[k];
+    oldb = take(h2b[j2]);
+    s2b = s2b + d_tanh(jl_tanh(s2)) * oldb;
+    for (i64 k = 0; k < nh; ++k) {
+      const T cse2 = w2[j2 * nh + k], cse3 = h1[k];
+      s2 = s2 + cse2 * cse3;
+      w2b[j2 * nh + k] = w2b[j2 * nh + k] + cse3 * s2b;
+      h1b[k] = h1b[k] + cse2 * s2b;
+    }
+    oldb = take(s2b);
+    b2b[j2] = b2b[j2] + oldb;
+  }
+  for (i64 j = 0; j < nh; ++j) {
+    const T cse4 = w1[j], cse5 = x[0];
+    const T cse6 = cse4 * cse5 + b1[j];
+    s1 = cse6;
+    oldb = take(h1b[j]);
+    s1b = s1b + d_tanh(jl_tanh(s1)) * oldb;
+    oldb = take(s1b);
+    w1b[j] = w1b[j] + cse5 * oldb;
+    xb[0] = xb[0] + cse4 * oldb;
+    b1b[j] = b1b[j] + oldb;
+  }
+}
+
+// mlp1d_hv.jl:5-150: the HVP of mlp1d; every statement's tangent twin first
+template <class T>
+void ex_mlp1d_hv(T* loss, const T* lossb, const T* x, T* xb, const T* y, T* yb, const T* w1,
+                 T* w1b, const T* b1, T* b1b, const T* w2, T* w2b, const T* b2, T* b2b,
+                 const T* w3, T* w3b, const T* b3, T* b3b, T* h1, T* h1b, T* h2, T* h2b, T* o,
+                 T* ob, i64 nh, T* lossd, const T* lossbd, const T* xd, T* xbd, const T* yd,
+                 T* ybd, const T* w1d, T* w1bd, const T* b1d, T* b1bd, const T* w2d, T* w2bd,
+                 const T* b2d, T* b2bd, const T* w3d, T* w3bd, const T* b3d, T* b3bd, T* h1d,
+                 T* h1bd, T* h2d, T* h2bd, T* od, T* obd) {
+  T s1 = 0, s2 = 0, s3 = 0, s1b = 0, s2b = 0, s3b = 0;
+  T s1d = 0, s1bd = 0, s2d = 0, s2bd = 0, s3d = 0, s3bd = 0;
+  for (i64 j = 0; j < nh; ++j) {
+    const T hx = x[0], hw = w1[j];
+    s1d = (hx * w1d[j] + hw * xd[0]) + b1d[j];
+    s1 = hw * hx + b1[j];
+    const T th = jl_tanh(s1);
+    h1d[j] = d_tanh(th) * s1d;
+    h1[j] = th;
+  }
+  for (i64 j2 = 0; j2 < nh; ++j2) {
+    s2d = b2d[j2];
+    s2 = b2[j2];
+    for (i64 k = 0; k < nh; ++k) {
+      const T hh = h1[k], hw = w2[j2 * nh + k];
+      s2d = s2d + (hh * w2d[j2 * nh + k] + hw * h1d[k]);
+      s2 = s2 + hw * hh;
+    }
+    const T th = jl_tanh(s2);
+    h2d[j2] = d_tanh(th) * s2d;
+    h2[j2] = th;
+  }
+  s3d = b3d[0];
+  s3 = b3[0];
+  for (i64 k2 = 0; k2 < nh; ++k2) {
+    const T hh = h2[k2], hw = w3[k2];
+    s3d = s3d + (hh * w3d[k2] + hw * h2d[k2]);
+    s3 = s3 + hw * hh;
+  }
+  od[0] = s3d;
+  o[0] = s3;
+  const T e = o[0] - y[0];
+  const T e2 = d_sq(e);
+  const T ed = od[0] + -(yd[0]);
+  lossd[0] = lossd[0] + e2 * ed;
+  loss[0] = loss[0] + e * e;
+  const T lb = lossb[0];
+  const T cse0d = lb * d_sq(ed) + e2 * lossbd[0];
+  const T cse0 = e2 * lb;
+  obd[0] = obd[0] + cse0d;
+  ob[0] = ob[0] + cse0;
+  ybd[0] = ybd[0] + -cse0d;
+  yb[0] = yb[0] + -cse0;
+  T oldbd = take(obd[0]), oldb = take(ob[0]);
+  s3bd = s3bd + oldbd;
+  s3b = s3b + oldb;
+  for (i64 k2 = nh - 1; k2 >= 0; --k2) {
+    const T hh = h2[k2];
+    w3bd[k2] = w3bd[k2] + (s3b * h2d[k2] + hh * s3bd);
+    w3b[k2] = w3b[k2] + hh * s3b;
+    const T hw = w3[k2];
+    h2bd[k2] = h2bd[k2] + (s3b * w3d[k2] + hw * s3bd);
+    h2b[k2] = h2b[k2] + hw * s3b;
+  }
+  oldbd = take(s3bd);
+  oldb = take(s3b);
+  b3bd[0] = b3bd[0] + oldbd;
+  b3b[0] = b3b[0] + oldb;
+  for (i64 j2 = 0; j2 < nh; ++j2) {
+    s2d = b2d[j2];
+    s2 = b2[j2];
+    for (i64 k = 0; k < nh; ++k) {
+      const T hh = h1[k], hw = w2[j2 * nh + k];
+      s2d = s2d + (hh * w2d[j2 * nh + k] + hw * h1d[k]);
+      s2 = s2 + hw * hh;
+    }
+    oldbd = take(h2bd[j2]);
+    oldb = take(h2b[j2]);
+    const T th = jl_tanh(s2);
+    const T g = d_tanh(th);
+    s2bd = s2bd + d_tanh_tangent(th, g, s2d, oldb, oldbd);
+    s2b = s2b + g * oldb;
+    for (i64 k = 0; k < nh; ++k) {
+      const T c1d = w2d[j2 * nh + k], c1 = w2[j2 * nh + k];
+      const T c2d = h1d[k], c2 = h1[k];
+      s2d = s2d + (c2 * c1d + c1 * c2d);
+      s2 = s2 + c1 * c2;
+      w2bd[j2 * nh + k] = w2bd[j2 * nh + k] + (s2b * c2d + c2 * s2bd);
+      w2b[j2 * nh + k] = w2b[j2 * nh + k] + c2 * s2b;
+      h1bd[k] = h1bd[k] + (s2b * c1d + c1 * s2bd);
+      h1b[k] = h1b[k] + c1 * s2b;
+    }
+    oldbd = take(s2bd);
+    oldb = take(s2b);
+    b2bd[j2] = b2bd[j2] + oldbd;
+    b2b[j2] = b2b[j2] + oldb;
+  }
+  for (i64 j = 0; j < nh; ++j) {
+    const T c3d = w1d[j], c3 = w1[j], c4d = xd[0], c4 = x[0];
+    const T c5d = (c4 * c3d + c3 * c4d) + b1d[j];
+    const T c5 = c3 * c4 + b1[j];
+    s1d = c5d;
+    s1 = c5;
+    oldbd = take(h1bd[j]);
+    oldb = take(h1b[j]);
+    const T th = jl_tanh(s1);
+    const T g = d_tanh(th);
+    s1bd = s1bd + d_tanh_tangent(th, g, s1d, oldb, oldbd);
+    s1b = s1b + g * oldb;
+    oldbd = take(s1bd);
+    oldb = take(s1b);
+    w1bd[j] = w1bd[j] + (oldb * c4d + c4 * oldbd);
+    w1b[j] = w1b[j] + c4 * oldb;
+    xbd[0] = xbd[0] + (oldb * c3d + c3 * oldbd);
+    xb[0] = xb[0] + c3 * oldb;
+    b1bd[j] = b1bd[j] + oldbd;
+    b1b[j] = b1b[j] + oldb;
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+// ---- restated reference exemplars, Float64 ----
+void oracle_ex_affine_loss_b_f64(double* loss, const double* lossb, const double* u, double* ub,
+                                 const double* a, double* ab, const double* b, double* bb,
+                                 double* v, double* vb, i64 n) {
+  ex_affine_loss_b(loss, lossb, u, ub, a, ab, b, bb, v, vb, n);
+}
+void oracle_ex_matvec_loss_b_f64(double* loss, const double* lossb, const double* a, double* ab,
+                                 const double* u, double* ub, double* v, double* vb, i64 m,
+                                 i64 n) {
+  ex_matvec_loss_b(loss, lossb, a, ab, u, ub, v, vb, m, n);
+}
+void oracle_ex_stencil_loss_b_f64(double* loss, const double* lossb, const double* u, double* ub,
+                                  double* w, double* wb, i64 n) {
+  ex_stencil_loss_b(loss, lossb, u, ub, w, wb, n);
+}
+void oracle_ex_advection_b_f64(double* u, double* ub, double* du, double* dub, double c,
+                               double* cb, double dx, double* dxb, double dt, double* dtb,
+                               i64 nstep, i64 nnode, double* du_stack) {
+  ex_advection_b(u, ub, du, dub, c, cb, dx, dxb, dt, dtb, nstep, nnode, du_stack);
+}
+void oracle_ex_selfrace_conv_b_f64(const double* x, double* xb, const double* w, double* wb,
+                                   double* z, double* zb, double* loss, const double* lossb,
+                                   i64 n, i64 nc) {
+  ex_selfrace_conv_b(x, xb, w, wb, z, zb, loss, lossb, n, nc);
+}
+#define MLP1D_B_ARGS(T)                                                                    \
+  T *loss, const T *lossb, const T *x, T *xb, const T *y, T *yb, const T *w1, T *w1b,     \
+      const T *b1, T *b1b, const T *w2, T *w2b, const T *b2, T *b2b, const T *w3, T *w3b,  \
+      const T *b3, T *b3b, T *h1, T *h1b, T *h2, T *h2b, T *o, T *ob, i64 nh
+#define MLP1D_B_PASS                                                                       \
+  loss, lossb, x, xb, y, yb, w1, w1b, b1, b1b, w2, w2b, b2, b2b, w3, w3b, b3, b3b, h1, h1b, \
+      h2, h2b, o, ob, nh
+void oracle_ex_mlp1d_b_f64(MLP1D_B_ARGS(double)) { ex_mlp1d_b(MLP1D_B_PASS); }
+void oracle_ex_mlp1d_hv_f64(MLP1D_B_ARGS(double), double* lossd, const double* lossbd,
+                            const double* xd, double* xbd, const double* yd, double* ybd,
+                            const double* w1d, double* w1bd, const double* b1d, double* b1bd,
+                            const double* w2d, double* w2bd, const double* b2d, double* b2bd,
+                            const double* w3d, double* w3bd, const double* b3d, double* b3bd,
+                            double* h1d, double* h1bd, double* h2d, double* h2bd, double* od,
+                            double* obd) {
+  ex_mlp1d_hv(MLP1D_B_PASS, lossd, lossbd, xd, xbd, yd, ybd, w1d, w1bd, b1d, b1bd, w2d, w2bd,
+              b2d, b2bd, w3d, w3bd, b3d, b3bd, h1d, h1bd, h2d, h2bd, od, obd);
+}
+
 
 void oracle_affine_ls_b_f64(double* loss, const double* lossb, const double* w, double* wb,
                             const double* b, double* bb, const double* x, double* xb,

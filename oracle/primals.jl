@@ -3,8 +3,9 @@
 # with div/mod-recovered indices, no allocation, length-1 arrays for scalar
 # outputs, every float argument positional). STADE.jl differentiates these;
 # oracle.cc restates, loop for loop, the adjoint / HVP sweeps it generates for
-# them (keep_push_pop = false, fuse_ii_loops = true), and libstade_b200 runs
-# the same sweeps on the GPU.
+# them with indexed tapes and STADE's default loop handling (keep_push_pop =
+# false, fuse_ii_loops = false: every backward loop runs reversed,
+# src/STADE.jl:6553-6557), and libstade_b200 runs the same sweeps on the GPU.
 #
 # This file is a specification for readers and for a Julia caller that wants to
 # regenerate the adjoints with STADE; nothing in this repository executes it.

@@ -53,6 +53,7 @@ struct Geo {
   int B, C, L, O, K, Lo;
   int cblk, oblk, tblk, cpad, nw;  // ceil(C/32), ceil(O/32), ceil(Lo/32), C rounded to 32, K cpad
   int m_tiles, n_tiles, slices, bps;
+  int chain;  // K blocks per TMEM accumulation chain
 };
 
 struct FwdOut {  // the forward epilogue's arrays
@@ -214,7 +215,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const Tile tl = decode<MODE>(g, t);
-        const int nch = tl.nkb > 0 ? (tl.nkb + kChainBlocks - 1) / kChainBlocks : 1;
+        const int nch = tl.nkb > 0 ? (tl.nkb + g.chain - 1) / g.chain : 1;
         for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
           const int b = chain % kAccBufs;
           const uint32_t acc = tmem + (uint32_t)(b * BN);
@@ -223,7 +224,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
             break;
           }
           fence_after();
-          const int kb0 = ch * kChainBlocks, kb1 = min(tl.nkb, kb0 + kChainBlocks);
+          const int kb0 = ch * g.chain, kb1 = min(tl.nkb, kb0 + g.chain);
           for (int kb = kb0; kb < kb1; ++kb, ++kb_all) {
             const int s = kb_all % STAGES;
             const uint32_t ph = (uint32_t)(kb_all / STAGES) & 1u;
@@ -258,7 +259,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const Tile tl = decode<MODE>(g, t);
-      const int nch = tl.nkb > 0 ? (tl.nkb + kChainBlocks - 1) / kChainBlocks : 1;
+      const int nch = tl.nkb > 0 ? (tl.nkb + g.chain - 1) / g.chain : 1;
       float sum[BN / 32][16];
 #pragma unroll
       for (int q = 0; q < BN / 32; ++q)
@@ -335,21 +336,17 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
 #pragma unroll
               for (int i = 0; i < 16; i += 4) {
                 float4 h, l;
-                h.x = tf32_hi(gv[i]); l.x = gv[i] - h.x;
-                h.y = tf32_hi(gv[i + 1]); l.y = gv[i + 1] - h.y;
-                h.z = tf32_hi(gv[i + 2]); l.z = gv[i + 2] - h.z;
-                h.w = tf32_hi(gv[i + 3]); l.w = gv[i + 3] - h.w;
+                tf32_split(gv[i], h.x, l.x);
+                tf32_split(gv[i + 1], h.y, l.y);
+                tf32_split(gv[i + 2], h.z, l.z);
+                tf32_split(gv[i + 3], h.w, l.w);
                 *reinterpret_cast<float4*>(fo.g_hi + gi + i) = h;
                 *reinterpret_cast<float4*>(fo.g_lo + gi + i) = l;
               }
             } else {
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                if (o0 + i < g.O) {
-                  const float h = tf32_hi(gv[i]);
-                  fo.g_hi[gi + i] = h;
-                  fo.g_lo[gi + i] = gv[i] - h;
-                }
+                if (o0 + i < g.O) tf32_split(gv[i], fo.g_hi[gi + i], fo.g_lo[gi + i]);
               }
             }
           }
@@ -429,10 +426,7 @@ xt_split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __re
   for (int j = 0; j < 32; j += 8) {
     const int l = l0 + ty + j, c = c0 + tx;
     if (l < L && c < C) {
-      const float v = tile[tx][ty + j];
-      const float h = tf32_hi(v);
-      hi[base + (int64_t)l * C + c] = h;
-      lo[base + (int64_t)l * C + c] = v - h;
+      tf32_split(tile[tx][ty + j], hi[base + (int64_t)l * C + c], lo[base + (int64_t)l * C + c]);
     }
   }
 }
@@ -446,10 +440,7 @@ __global__ void wf_split_kernel(const float* __restrict__ w, float* __restrict__
     const int c = (int)(e % C);
     const int64_t r = e / C;
     const int o = (int)(r % O), k = (int)(r / O);
-    const float v = w[((int64_t)o * C + c) * K + k];
-    const float h = tf32_hi(v);
-    hi[e] = h;
-    lo[e] = v - h;
+    tf32_split(w[((int64_t)o * C + c) * K + k], hi[e], lo[e]);
   }
 }
 
@@ -471,6 +462,7 @@ __global__ void wgrad_finish_kernel(const float* __restrict__ part, int slices, 
 // ---- host ----------------------------------------------------------------------------
 Geo base_geo(const ConvShape& sh) {
   Geo g{};
+  g.chain = tc5::tc_chain_blocks(kChainBlocks);
   g.B = (int)sh.n_b; g.C = (int)sh.n_c; g.L = (int)sh.n_l; g.O = (int)sh.n_o; g.K = (int)sh.n_k;
   g.Lo = g.L - g.K + 1;
   g.cblk = (g.C + 31) / 32;

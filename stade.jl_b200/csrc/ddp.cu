@@ -470,4 +470,107 @@ stade_status stade_mlp2_ce_b_check_replicas_f32(const float* w1, const float* b1
   return stade_ddp_check_replicas(comm, bufs, counts, 5, STADE_F32, bad_mask, opts);
 }
 
+
+// ---- conv1d_relu_mse in adjoint mode, per_sample = [:x, :t] ------------------
+// roles: :accum wb   :reduced loss   :local xb tb zb rb   :shared w   :seed lossb
+stade_status stade_conv1d_relu_mse_b_reset_accum_f32(float* wb, int64_t n_o, int64_t n_c,
+                                                     int64_t n_k, const stade_opts* opts) {
+  void* bufs[1] = {wb};
+  const int64_t counts[1] = {n_o * n_c * n_k};
+  return stade_ddp_zero(bufs, counts, 1, STADE_F32, opts);
+}
+stade_status stade_conv1d_relu_mse_b_reset_reduced_f32(float* loss, const stade_opts* opts) {
+  void* bufs[1] = {loss};
+  const int64_t counts[1] = {1};
+  return stade_ddp_zero(bufs, counts, 1, STADE_F32, opts);
+}
+stade_status stade_conv1d_relu_mse_b_reset_local_f32(float* xb, float* tb, float* zb, float* rb,
+                                                     int64_t n_b, int64_t n_c, int64_t n_l,
+                                                     int64_t n_o, int64_t n_k,
+                                                     const stade_opts* opts) {
+  const int64_t nt = n_b * n_o * (n_l - n_k + 1);
+  STADE_REQUIRE(n_l >= n_k, "conv1d_relu_mse_b_reset_local: n_l < n_k");
+  void* bufs[4] = {xb, tb, zb, rb};
+  const int64_t counts[4] = {n_b * n_c * n_l, nt, nt, nt};
+  return stade_ddp_zero(bufs, counts, 4, STADE_F32, opts);
+}
+stade_status stade_conv1d_relu_mse_b_allreduce_accum_f32(float* wb, int64_t n_o, int64_t n_c,
+                                                         int64_t n_k, int64_t n_local,
+                                                         stade_comm* comm, int64_t* n_global,
+                                                         const stade_opts* opts) {
+  void* bufs[1] = {wb};
+  const int64_t counts[1] = {n_o * n_c * n_k};
+  return stade_ddp_allreduce_sum(comm, bufs, counts, 1, STADE_F32, n_local, n_global, opts);
+}
+stade_status stade_conv1d_relu_mse_b_allreduce_reduced_f32(float* loss, stade_comm* comm,
+                                                           const stade_opts* opts) {
+  void* bufs[1] = {loss};
+  const int64_t counts[1] = {1};
+  return stade_ddp_allreduce_sum(comm, bufs, counts, 1, STADE_F32, 0, nullptr, opts);
+}
+stade_status stade_conv1d_relu_mse_b_check_replicas_f32(const float* w, const float* lossb,
+                                                        int64_t n_o, int64_t n_c, int64_t n_k,
+                                                        stade_comm* comm, uint64_t* bad_mask,
+                                                        const stade_opts* opts) {
+  const void* bufs[2] = {w, lossb};
+  const int64_t counts[2] = {n_o * n_c * n_k, 1};
+  return stade_ddp_check_replicas(comm, bufs, counts, 2, STADE_F32, bad_mask, opts);
+}
+
+// ---- mlp2_ce in hvp mode (the _hv names), per_sample = [:x, :y] --------------
+// roles: :accum w1b b1b w2b b2b w1bd b1bd w2bd b2bd   :reduced loss lossd
+//        :local xb yb hb zb pb xbd ybd hbd zbd pbd    :shared w1 b1 w2 b2 w1d b1d w2d b2d
+//        :seed lossb lossbd
+stade_status stade_mlp2_ce_hv_reset_accum_f64(double* w1b, double* b1b, double* w2b, double* b2b,
+                                              double* w1bd, double* b1bd, double* w2bd,
+                                              double* b2bd, int64_t n_i, int64_t n_h, int64_t n_o,
+                                              const stade_opts* opts) {
+  void* bufs[8] = {w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd};
+  const int64_t counts[8] = {n_i * n_h, n_h, n_h * n_o, n_o, n_i * n_h, n_h, n_h * n_o, n_o};
+  return stade_ddp_zero(bufs, counts, 8, STADE_F64, opts);
+}
+stade_status stade_mlp2_ce_hv_reset_reduced_f64(double* loss, double* lossd,
+                                                const stade_opts* opts) {
+  void* bufs[2] = {loss, lossd};
+  const int64_t counts[2] = {1, 1};
+  return stade_ddp_zero(bufs, counts, 2, STADE_F64, opts);
+}
+stade_status stade_mlp2_ce_hv_reset_local_f64(double* xb, double* yb, double* hb, double* zb,
+                                              double* pb, double* xbd, double* ybd, double* hbd,
+                                              double* zbd, double* pbd, int64_t n_s, int64_t n_i,
+                                              int64_t n_h, int64_t n_o, const stade_opts* opts) {
+  void* bufs[10] = {xb, yb, hb, zb, pb, xbd, ybd, hbd, zbd, pbd};
+  const int64_t counts[10] = {n_s * n_i, n_s * n_o, n_s * n_h, n_s * n_o, n_s * n_o,
+                              n_s * n_i, n_s * n_o, n_s * n_h, n_s * n_o, n_s * n_o};
+  return stade_ddp_zero(bufs, counts, 10, STADE_F64, opts);
+}
+stade_status stade_mlp2_ce_hv_allreduce_accum_f64(double* w1b, double* b1b, double* w2b,
+                                                  double* b2b, double* w1bd, double* b1bd,
+                                                  double* w2bd, double* b2bd, int64_t n_i,
+                                                  int64_t n_h, int64_t n_o, int64_t n_local,
+                                                  stade_comm* comm, int64_t* n_global,
+                                                  const stade_opts* opts) {
+  void* bufs[8] = {w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd};
+  const int64_t counts[8] = {n_i * n_h, n_h, n_h * n_o, n_o, n_i * n_h, n_h, n_h * n_o, n_o};
+  return stade_ddp_allreduce_sum(comm, bufs, counts, 8, STADE_F64, n_local, n_global, opts);
+}
+stade_status stade_mlp2_ce_hv_allreduce_reduced_f64(double* loss, double* lossd, stade_comm* comm,
+                                                    const stade_opts* opts) {
+  void* bufs[2] = {loss, lossd};
+  const int64_t counts[2] = {1, 1};
+  return stade_ddp_allreduce_sum(comm, bufs, counts, 2, STADE_F64, 0, nullptr, opts);
+}
+stade_status stade_mlp2_ce_hv_check_replicas_f64(const double* w1, const double* b1,
+                                                 const double* w2, const double* b2,
+                                                 const double* w1d, const double* b1d,
+                                                 const double* w2d, const double* b2d,
+                                                 const double* lossb, const double* lossbd,
+                                                 int64_t n_i, int64_t n_h, int64_t n_o,
+                                                 stade_comm* comm, uint64_t* bad_mask,
+                                                 const stade_opts* opts) {
+  const void* bufs[10] = {w1, b1, w2, b2, w1d, b1d, w2d, b2d, lossb, lossbd};
+  const int64_t counts[10] = {n_i * n_h, n_h, n_h * n_o, n_o, n_i * n_h, n_h, n_h * n_o, n_o, 1, 1};
+  return stade_ddp_check_replicas(comm, bufs, counts, 10, STADE_F64, bad_mask, opts);
+}
+
 }  // extern "C"

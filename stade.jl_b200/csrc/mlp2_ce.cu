@@ -404,15 +404,15 @@ mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
           }
         }
       }
-      float o[2], hi[2];
+      float o[2], hi[2], lo[2];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         o[j] = __fmul_rn(__fadd_rn(1.f, -__fmul_rn(hh[j], hh[j])), ac[j]);
-        hi[j] = __uint_as_float(__float_as_uint(o[j]) & 0xFFFFE000u);
+        tc5::tf32_split(o[j], hi[j], lo[j]);
       }
       bsum.x += o[0]; bsum.y += o[1];
       *reinterpret_cast<float2*>(s1b_hi + off) = make_float2(hi[0], hi[1]);
-      *reinterpret_cast<float2*>(s1b_lo + off) = make_float2(o[0] - hi[0], o[1] - hi[1]);
+      *reinterpret_cast<float2*>(s1b_lo + off) = make_float2(lo[0], lo[1]);
       // hb is consumed: zero it (only where it held a seed; a zero stays zero)
       if (acc2.x != 0.f || acc2.y != 0.f)
         *reinterpret_cast<float2*>(hb + off) = make_float2(0.f, 0.f);

@@ -49,7 +49,7 @@ constexpr int kAccBufs = 4;
 constexpr uint32_t kTmemCols = kAccBufs * 128;  // all 512 columns of the SM's TMEM
 constexpr int kBarWords = 2 * STAGES + 2 * kAccBufs + 1;  // full, empty, tfull, tempty, done
 static_assert(kBarWords * 8 + 4 <= 256, "barrier block must fit in 256 bytes");
-// K blocks per TMEM accumulation chain. The tensor core's Float32
+// Default K blocks per TMEM accumulation chain. The tensor core's Float32
 // accumulation is not round-to-nearest: its error grows linearly with the
 // number of accumulations into one TMEM accumulator (measured: 1.4e-5
 // relative after 1000 K). Chains of 4 K blocks (128 K, 48 MMAs) are drained
@@ -216,6 +216,7 @@ struct Geometry {
   int M, N, K;
   int m_tiles, n_tiles, slices, k_slice;
   bool a_mn, b_mn;
+  int chain;  // K blocks per TMEM accumulation chain
 };
 
 // EPI_KIND: 0 logits (NO classes), 1 accumulate, 2 split-K partial
@@ -327,7 +328,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
         const int kbeg = slice * g.k_slice;
         const int kend = min(g.K, kbeg + g.k_slice);
         const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
-        const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+        const int nch = nkb > 0 ? (nkb + g.chain - 1) / g.chain : 1;
         // A ragged last N tile of a K-major B runs MMAs only as wide as its
         // columns (rounded up to 16; the rest of the box is zero-filled and
         // the epilogue stores only columns < N): 784 = 6 x 128 + 16 spends
@@ -343,7 +344,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
           const uint32_t acc = tmem + (uint32_t)(b * BN);
           if (!mbar_wait(tempty0 + 8 * b, ((uint32_t)(chain / kAccBufs) & 1u) ^ 1u)) { ok = false; break; }
           tc_fence_after();
-          const int kb0 = ch * kChainBlocks, kb1 = min(nkb, kb0 + kChainBlocks);
+          const int kb0 = ch * g.chain, kb1 = min(nkb, kb0 + g.chain);
           for (int kb = kb0; kb < kb1; ++kb, ++kb_all) {
             const int s = kb_all % STAGES;
             const uint32_t ph = (uint32_t)(kb_all / STAGES) & 1u;
@@ -395,7 +396,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
       const int kbeg = slice * g.k_slice;
       const int kend = min(g.K, kbeg + g.k_slice);
       const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
-      const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+      const int nch = nkb > 0 ? (nkb + g.chain - 1) / g.chain : 1;
       const int m = m0 + quad * 32 + lane;
       // the thread's 64 columns: 16-wide groups half, half + 2, half + 4, half + 6
       float sum[BN / 32][16];
@@ -571,7 +572,7 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
         const int kbeg = slice * g.k_slice;
         const int kend = min(g.K, kbeg + g.k_slice);
         const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
-        const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+        const int nch = nkb > 0 ? (nkb + g.chain - 1) / g.chain : 1;
         for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
           const int b = chain % kAccBufs;
           const uint32_t acc = tmem + (uint32_t)(b * BN);
@@ -581,7 +582,7 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
             break;
           }
           tc_fence_after();
-          const int kb0 = ch * kChainBlocks, kb1 = min(nkb, kb0 + kChainBlocks);
+          const int kb0 = ch * g.chain, kb1 = min(nkb, kb0 + g.chain);
           for (int kb = kb0; kb < kb1; ++kb, ++kb_all) {
             const int s = kb_all % ST;
             const uint32_t ph = (uint32_t)(kb_all / ST) & 1u;
@@ -632,7 +633,7 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
       const int kbeg = slice * g.k_slice;
       const int kend = min(g.K, kbeg + g.k_slice);
       const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
-      const int nch = nkb > 0 ? (nkb + kChainBlocks - 1) / kChainBlocks : 1;
+      const int nch = nkb > 0 ? (nkb + g.chain - 1) / g.chain : 1;
       const int m = m0 + quad * 32 + lane;
       float sum[BN / 32][16];
 #pragma unroll
@@ -778,6 +779,7 @@ Geometry geometry(int M, int N, int K, int slices, bool a_mn, bool b_mn) {
   g.k_slice = (per > 0 ? per : 1) * BK;
   g.slices = K > 0 ? (K + g.k_slice - 1) / g.k_slice : 1;
   g.a_mn = a_mn; g.b_mn = b_mn;
+  g.chain = tc5::tc_chain_blocks(kChainBlocks);
   return g;
 }
 
@@ -791,7 +793,8 @@ int w1b_slices(int S, int I, int H) {
   return sl < 1 ? 1 : sl;
 }
 
-// hi / lo split of a Float32 array (n % 4 == 0 handled by the vector path).
+// hi / lo split of a Float32 array (n % 4 == 0 handled by the vector path),
+// both planes rounded to the nearest TF32 value.
 __global__ void split_kernel(const float* __restrict__ a, float* __restrict__ hi,
                              float* __restrict__ lo, int64_t n) {
   const int64_t n4 = n / 4;
@@ -799,41 +802,36 @@ __global__ void split_kernel(const float* __restrict__ a, float* __restrict__ hi
        i += (int64_t)gridDim.x * blockDim.x) {
     const float4 v = reinterpret_cast<const float4*>(a)[i];
     float4 h, l;
-    h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u); l.x = v.x - h.x;
-    h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u); l.y = v.y - h.y;
-    h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u); l.z = v.z - h.z;
-    h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u); l.w = v.w - h.w;
+    tc5::tf32_split(v.x, h.x, l.x);
+    tc5::tf32_split(v.y, h.y, l.y);
+    tc5::tf32_split(v.z, h.z, l.z);
+    tc5::tf32_split(v.w, h.w, l.w);
     reinterpret_cast<float4*>(hi)[i] = h;
     reinterpret_cast<float4*>(lo)[i] = l;
   }
   for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = a[i];
-    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-    hi[i] = h;
-    lo[i] = v - h;
-  }
+       i += (int64_t)gridDim.x * blockDim.x)
+    tc5::tf32_split(a[i], hi[i], lo[i]);
 }
 
-// lo = a - hi(a) only: the tensor core reads just the top 19 bits of a
-// Float32 operand (kind::tf32), so the array itself serves as its hi plane.
+// The lo plane only: the tensor core reads just the top 19 bits of a Float32
+// operand (kind::tf32), so the array itself serves as its (truncated) hi
+// plane and lo = rn(a - trunc(a)) completes it.
 __global__ void split_lo_kernel(const float* __restrict__ a, float* __restrict__ lo, int64_t n) {
   const int64_t n4 = n / 4;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float4 v = reinterpret_cast<const float4*>(a)[i];
     float4 l;
-    l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-    l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-    l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-    l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    l.x = tc5::tf32_lo_of_own(v.x);
+    l.y = tc5::tf32_lo_of_own(v.y);
+    l.z = tc5::tf32_lo_of_own(v.z);
+    l.w = tc5::tf32_lo_of_own(v.w);
     reinterpret_cast<float4*>(lo)[i] = l;
   }
   for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = a[i];
-    lo[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-  }
+       i += (int64_t)gridDim.x * blockDim.x)
+    lo[i] = tc5::tf32_lo_of_own(a[i]);
 }
 
 __global__ void w1b_finish_kernel(const float* __restrict__ part, int slices, int64_t MN,
@@ -945,6 +943,37 @@ int tma_take_error() {
 
 namespace stade {
 int conv_tc_take_error();
+
+namespace {
+__device__ int g_wait_check_out = 0;
+// One thread waits on an mbarrier that nothing arrives on, with the wait loop
+// of the tensor-core kernels and a limit of `cycles` SM clock cycles; the
+// wait gives up, records the timeout in the TMA kernels' error word and the
+// kernel returns. g_wait_check_out receives 1 if the wait returned false.
+__global__ void bounded_wait_check_kernel(long long cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = tc5::smem_u32(&bar);
+  if (threadIdx.x == 0) tc5::mbar_init(b, 1);
+  __syncthreads();
+  if (threadIdx.x == 0)
+    g_wait_check_out = tc5::mbar_wait_for(b, 0, &tma::g_tma_error, cycles) ? 0 : 1;
+}
+}  // namespace
+}  // namespace stade
+
+extern "C" stade_status stade_check_bounded_wait(int64_t wait_cycles, const stade_opts* opts) {
+  using namespace stade;
+  STADE_REQUIRE(wait_cycles >= 1000 && wait_cycles <= tc5::kWaitCycles,
+                "check_bounded_wait: wait_cycles %lld outside [1000, %lld]",
+                (long long)wait_cycles, (long long)tc5::kWaitCycles);
+  cudaStream_t s = stream_of(opts);
+  bounded_wait_check_kernel<<<1, 32, 0, s>>>((long long)wait_cycles);
+  STADE_CHECK_LAUNCH();
+  int host = 0;
+  STADE_CUDA(cudaMemcpyFromSymbolAsync(&host, g_wait_check_out, sizeof(int), 0,
+                                       cudaMemcpyDeviceToHost, s));
+  STADE_CUDA(cudaStreamSynchronize(s));
+  return host == 1 ? STADE_ETIMEDOUT : fail(STADE_ECUDA, "check_bounded_wait: the wait returned");
 }
 
 // The library's device error word: set when a bounded wait inside a

@@ -7,6 +7,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -40,17 +41,22 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: after ~2 s sets *err and returns false.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+// Bounded wait: after `limit` SM clock cycles sets *err and returns false.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, int* err,
+                                              long long limit) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicExch(err, 1);
       return false;
     }
   }
   return true;
+}
+// The kernels' waits: ~2 s.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+  return mbar_wait_for(bar, parity, err, kWaitCycles);
 }
 __device__ __forceinline__ void fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -273,10 +279,46 @@ inline int sm_count() {
   return n;
 }
 
-// TF32 hi part of a Float32 (low 13 mantissa bits cleared); lo = v - hi is exact.
-__device__ __forceinline__ float tf32_hi(float v) {
+// 3xTF32 operand planes. kind::tf32 reads the top 19 bits of a 32-bit operand
+// (sign, exponent, 10 mantissa bits) and ignores the rest: an operand whose
+// low 13 bits are not zero is truncated toward zero. Truncation shrinks every
+// operand (by up to 2^-10 of it for a hi plane, 2^-20 of the value for a lo
+// plane), a one-sided bias that does not cancel in long sums, so the planes
+// this library writes are rounded to the nearest TF32 value instead
+// (cvt.rna.tf32.f32: ties away from zero), which leaves the low 13 bits zero
+// and the MMA reads them exactly.
+__device__ __forceinline__ float tf32_rn(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+// K blocks (32 K each) per TMEM accumulation chain of the 3xTF32 kernels: the
+// tensor core's Float32 accumulation does not round to nearest, so its error
+// grows with the number of MMAs into one accumulator; each chain is drained
+// into round-to-nearest Float32 register sums. STADE_TC_CHAIN overrides the
+// default (1 .. 64).
+inline int tc_chain_blocks(int dflt) {
+  static int v = [dflt] {
+    const char* e = std::getenv("STADE_TC_CHAIN");
+    const int x = e ? std::atoi(e) : dflt;
+    return x >= 1 && x <= 64 ? x : dflt;
+  }();
+  return v;
+}
+
+// The value kind::tf32 reads from an array used as its own hi plane.
+__device__ __forceinline__ float tf32_trunc(float v) {
   return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
 }
+// hi = rn(v) and lo = rn(v - hi) (v - hi is exact): v = hi + lo within
+// 2^-22 of v, the error unbiased.
+__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
+  hi = tf32_rn(v);
+  lo = tf32_rn(v - hi);
+}
+// The lo plane of an array that serves as its own hi plane (the MMA reads its
+// truncation): rn(v - trunc(v)), v - trunc(v) exact.
+__device__ __forceinline__ float tf32_lo_of_own(float v) { return tf32_rn(v - tf32_trunc(v)); }
 
 }  // namespace tc5
 }  // namespace stade

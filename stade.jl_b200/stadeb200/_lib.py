@@ -54,6 +54,7 @@ SIGNATURES = {
     "stade_reset_kernel_launches": (None, []),
     "stade_workspace_cached_bytes": (C.c_size_t, []),
     "stade_device_error": (C.c_int, []),
+    "stade_check_bounded_wait": (ST, [I64, OPTS]),
     "stade_profile_enable": (None, [C.c_int]),
     "stade_profile_read": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(D), C.POINTER(C.c_int),
                                      C.c_int]),
@@ -101,6 +102,22 @@ SIGNATURES = {
     "stade_mlp2_ce_b_allreduce_reduced_f32": (ST, [P, C.c_void_p, OPTS]),
     "stade_mlp2_ce_b_check_replicas_f32": (ST, [P] * 5 + [I64] * 3 + [C.c_void_p,
                                                                       C.POINTER(C.c_uint64), OPTS]),
+    "stade_conv1d_relu_mse_b_reset_accum_f32": (ST, [P] + [I64] * 3 + [OPTS]),
+    "stade_conv1d_relu_mse_b_reset_reduced_f32": (ST, [P, OPTS]),
+    "stade_conv1d_relu_mse_b_reset_local_f32": (ST, [P] * 4 + [I64] * 5 + [OPTS]),
+    "stade_conv1d_relu_mse_b_allreduce_accum_f32": (ST, [P] + [I64] * 4 + [C.c_void_p,
+                                                                         C.POINTER(I64), OPTS]),
+    "stade_conv1d_relu_mse_b_allreduce_reduced_f32": (ST, [P, C.c_void_p, OPTS]),
+    "stade_conv1d_relu_mse_b_check_replicas_f32": (ST, [P] * 2 + [I64] * 3 + [
+        C.c_void_p, C.POINTER(C.c_uint64), OPTS]),
+    "stade_mlp2_ce_hv_reset_accum_f64": (ST, [P] * 8 + [I64] * 3 + [OPTS]),
+    "stade_mlp2_ce_hv_reset_reduced_f64": (ST, [P, P, OPTS]),
+    "stade_mlp2_ce_hv_reset_local_f64": (ST, [P] * 10 + [I64] * 4 + [OPTS]),
+    "stade_mlp2_ce_hv_allreduce_accum_f64": (ST, [P] * 8 + [I64] * 4 + [C.c_void_p,
+                                                                        C.POINTER(I64), OPTS]),
+    "stade_mlp2_ce_hv_allreduce_reduced_f64": (ST, [P, P, C.c_void_p, OPTS]),
+    "stade_mlp2_ce_hv_check_replicas_f64": (ST, [P] * 10 + [I64] * 3 + [
+        C.c_void_p, C.POINTER(C.c_uint64), OPTS]),
     "stade_fnv1a64": (C.c_uint64, [C.c_char_p]),
     "stade_fill_normal_f64": (None, [P, I64, C.c_uint64, D, D]),
     "stade_fill_normal_f32": (None, [P, I64, C.c_uint64, D, D]),

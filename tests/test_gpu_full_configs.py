@@ -21,16 +21,16 @@ Metrics per array (refmath):
   norm       max|a - b| / max|b|.
 Gate per array, with tol = 1e-5 (Float32) or 1e-12 (Float64), the north
 star's tolerances:
-  elem(1e-3)(gpu, exact) <= max(tol, elem(1e-3)(cpu, exact)), and
+  elem(1e-3)(gpu, exact) <= max(tol, 2 * elem(1e-3)(cpu, exact)), and
   norm(gpu, exact) <= tol,
 where cpu is the oracle in the kernel's precision (the generated sweep as the
 reference runs it on the CPU). A Float32 evaluation cannot hold 1e-5
 element-wise at elements far below the array's largest: the CPU sweep itself
 misses it (tanh outputs near zero, sums with cancellation), so the GPU must be
-at least as close to the exact result, element by element, as the
-reference's own CPU run is. This is the reference's verdict
-(val_truth_verdict_lines, src/STADE.jl:18915-18932) with its factor 20 cut
-to 1 and no 1e-10 ceiling. Where the sweep has no higher-precision truth
+within twice the reference's own CPU error of the exact result, element by
+element. This is the reference's verdict (val_truth_verdict_lines,
+src/STADE.jl:18915-18932) with its factor 20 cut to 2 and no 1e-10
+ceiling. Where the sweep has no higher-precision truth
 here (C1, C3 in Float64) the GPU is compared with the Float64 oracle at tol
 directly. Set STADE_PARITY_RECORD to a path to also write every figure as
 JSON.
@@ -48,6 +48,7 @@ pytestmark = pytest.mark.gpu
 
 F32_TOL = 1e-5
 F64_TOL = 1e-12
+CPU_FACTOR = 2.0     # the reference's verdict allows 20
 PHI = 1e-3
 THREADS = 0          # the oracle on every host thread
 RECORD = {}
@@ -69,7 +70,7 @@ def _check(fails, config, name, gate, tol, cpu=None, **pairs):
     same-precision oracle against the exact result) as the CPU's own error.
     The caller asserts once all arrays are recorded."""
     m = _record(config, name, **pairs)
-    bound = max(tol, m[cpu]["elem_1e-3"]) if cpu else tol
+    bound = max(tol, CPU_FACTOR * m[cpu]["elem_1e-3"]) if cpu else tol
     if not (m[gate]["elem_1e-3"] <= bound and m[gate]["norm"] <= tol):
         fails.append((name, m[gate], m[cpu] if cpu else None))
 
