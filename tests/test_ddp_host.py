@@ -409,3 +409,213 @@ def test_mean_loss_factor_refusals():
     for n, p in ((4096, 3), (6, 4), (10, 0)):
         with pytest.raises(ValueError):
             ddp.mean_loss_factor(n, p)
+
+
+# ---- C5: the hvp-mode bucket (b and bd shadows) over sample blocks ------------
+def _hv_rank_main(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q.put((rank,) + _hv_run(rank, world))
+    finally:
+        dist.destroy_process_group()
+
+
+def _hv_run(rank, world):
+    """One rank's hvp sweep between the epilogue's resets and sums (world = 1:
+    the whole batch, no communication)."""
+    import cases
+    from oracle import oracle as orc
+    n_s, n_i, n_h, n_o = 23, 9, 6, 4
+    st, _ = cases.mlp_hv_state(n_s, n_i, n_h, n_o, seeded=True, xd_nonzero=True)
+    rows = ddp.shard(n_s, rank, world)
+    lo, hi = rows.start, rows.stop
+    per = dict(x=n_i, xb=n_i, y=n_o, yb=n_o, h=n_h, hb=n_h, z=n_o, zb=n_o, p=n_o, pb=n_o)
+    bank = {}
+    for k, v in st.items():
+        base = k[:-1] if k.endswith("d") and k[:-1] in per else k
+        w = per.get(base)
+        bank[k] = v[lo * w:hi * w].copy() if w else v.copy()
+    backend = GlooBackend() if world > 1 else _NoComm()
+    epi = ddp.Epilogue(ddp.MLP2_CE, ["x", "y"], "hvp", backend)
+    epi.check_replicas(bank) if world > 1 else None
+    epi.reset_accum(bank)
+    epi.reset_reduced(bank)
+    epi.reset_local(bank)
+    orc.mlp2_ce_hv(*[bank[a] for a in cases.MLP_ARGS], hi - lo, n_i, n_h, n_o,
+                   *[bank[a] for a in cases.MLP_TAN])
+    n_global = epi.allreduce_accum(bank, hi - lo) if world > 1 else hi - lo
+    if world > 1:
+        epi.allreduce_reduced(bank)
+    return n_global, {b: bank[b].copy() for b in epi.accum + epi.reduced}
+
+
+class _NoComm:
+    def zero(self, bufs):
+        for b in bufs:
+            b[...] = 0
+
+
+def test_hvp_bucket_rank_invariance_gloo():
+    """C5's epilogue in hvp mode: two gloo ranks each run the HVP sweep on
+    their block of samples; the one bucket of the eight :accum shadows (b and
+    bd of w1, b1, w2, b2) and the :reduced loss / lossd summed across ranks
+    match one run over the whole batch (rtol 1e-12, test/validate_ddp.jl:
+    160-179), and the global sample count comes back."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_hv_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        rank, n_global, out = q.get(timeout=120)
+        res[rank] = (n_global, out)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    n_s, ref = _hv_run(0, 1)
+    assert sorted(ref) == sorted(["w1b", "b1b", "w2b", "b2b", "w1bd", "b1bd", "w2bd", "b2bd",
+                                  "loss", "lossd"])
+    for rank in (0, 1):
+        n_global, out = res[rank]
+        assert n_global == n_s
+        for b, v in ref.items():
+            err = np.max(np.abs(out[b] - v)) / max(np.max(np.abs(v)), 1e-300)
+            assert err <= 1e-12, (b, err)
+            assert np.array_equal(out[b], res[0][1][b])
+
+
+# ---- C3: row slabs with a halo row per neighbour per step ---------------------
+def _exchange(dist, first, last, rank, world):
+    """Sends this slab's first row to the rank above and its last row to the
+    rank below (periodic); returns (top halo, bottom halo): the rank above's
+    last row and the rank below's first row."""
+    import torch
+    up, down = (rank - 1) % world, (rank + 1) % world
+    top, bottom = torch.empty(first.size, dtype=torch.float64), torch.empty(first.size,
+                                                                             dtype=torch.float64)
+    reqs = [dist.isend(torch.from_numpy(first.copy()), up, tag=1),
+            dist.isend(torch.from_numpy(last.copy()), down, tag=2),
+            dist.irecv(bottom, down, tag=1), dist.irecv(top, up, tag=2)]
+    for r in reqs:
+        r.wait()
+    return top.numpy(), bottom.numpy()
+
+
+def _slab_gather(a_pad, lo, rows, n, alpha):
+    """ub of the slab's rows from the adjoint state a (halo-padded, rows + 2)
+    by the reverse stencil loop's additions, applied per cell in the order the
+    serial loop makes them (iteration index descending, then statement): the
+    schedule stade_heat2d_b_f64_slab's kernels follow."""
+    i = (lo + np.arange(rows))[:, None] % n
+    j = np.arange(n)[None, :]
+    own = a_pad[1:rows + 1]
+    k_self = i * n + j
+    k_b, k_a = ((i + 1) % n) * n + j, ((i - 1) % n) * n + j
+    k_r, k_l = i * n + (j + 1) % n, i * n + (j - 1) % n
+    a_b, a_a = alpha * a_pad[2:rows + 2], alpha * a_pad[0:rows]
+    a_r, a_l = alpha * np.roll(own, -1, axis=1), alpha * np.roll(own, 1, axis=1)
+    keys = np.stack([k_self + 0 * j, k_b + 0 * j, k_a + 0 * j, k_r + 0 * j, k_l + 0 * j,
+                     k_self + 0 * j]).astype(np.int64)
+    stmt = np.array([0, 1, 2, 3, 4, 5])[:, None, None]
+    vals = np.stack([own, a_b, a_a, a_r, a_l, 4.0 * -(alpha * own)])
+    order = np.lexsort((np.broadcast_to(stmt, keys.shape), -keys), axis=0)
+    acc = np.zeros_like(own)
+    for s in range(6):
+        acc = acc + np.take_along_axis(vals, order[s:s + 1], axis=0)[0]
+    return acc
+
+
+def _slab_sweep(dist, rank, world, u0, n, n_step, alpha):
+    """The slab form of heat2d_b on this rank's rows, as stade_heat2d_b_f64_slab
+    runs it: tape slots hold each state with a halo row above and below, the
+    forward exchanges the state's edge rows per step, the reverse exchanges the
+    adjoint state's edge rows per step, loss and alphab are summed across
+    slabs at the end."""
+    lo, hi = n * rank // world, n * (rank + 1) // world
+    rows = hi - lo
+    pad = lambda s, top, bot: np.vstack([top[None], s, bot[None]])
+    state = u0.reshape(n, n)[lo:hi].copy()
+    tape = []
+    for _ in range(n_step):
+        top, bot = _exchange(dist, state[0], state[-1], rank, world)
+        p = pad(state, top, bot)
+        tape.append(p)
+        c = p[1:rows + 1]
+        lap = (((p[0:rows] + p[2:rows + 2]) + np.roll(c, 1, axis=1)) + np.roll(c, -1, axis=1)) \
+            - 4.0 * c
+        state = c + alpha * lap
+    un = state
+    loss = 0.0
+    for v in un.ravel():
+        loss = loss + v * v
+    a = 0.0 + (2.0 * un)                     # unb (zero) + the loss seed's ub (lossb = 1)
+    alphab = 0.0
+    for t in range(n_step - 1, -1, -1):
+        top, bot = _exchange(dist, a[0], a[-1], rank, world)
+        a_pad = pad(a, top, bot)
+        p = tape[t]
+        c = p[1:rows + 1]
+        lap = (((p[0:rows] + p[2:rows + 2]) + np.roll(c, 1, axis=1)) + np.roll(c, -1, axis=1)) \
+            - 4.0 * c
+        for v in (lap * a).ravel()[::-1]:
+            alphab = alphab + v
+        a = _slab_gather(a_pad, lo, rows, n, alpha)
+    return lo, hi, a, un, tape, loss, alphab
+
+
+def _slab_rank_main(rank, world, port, n, n_step, q):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from stadeb200 import synth
+        u0 = synth.heat2d_inputs(n)["u"]
+        lo, hi, ub, un, tape, loss, alphab = _slab_sweep(dist, rank, world, u0, n, n_step, 0.2)
+        s = torch.tensor([loss, alphab], dtype=torch.float64)
+        dist.all_reduce(s)
+        q.put((rank, lo, hi, ub, un, tape, float(s[0]), float(s[1])))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,n,n_step", [(2, 12, 3), (3, 17, 4)])
+def test_heat2d_slabs_gloo(world, n, n_step):
+    """C3 on row slabs across gloo ranks, emulating the GPU slab schedule:
+    every rank's ub, final state and halo-padded tape slots equal the
+    single-grid oracle's bit for bit (the halo rows are the neighbours' edge
+    rows, periodic across the first and last rank); loss and alphab, summed
+    across slabs, within 1e-12."""
+    import torch.multiprocessing as mp
+    from oracle import oracle as orc
+    from stadeb200 import synth
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_slab_rank_main, args=(r, world, port, n, n_step, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    u = synth.heat2d_inputs(n)["u"].copy()
+    z = lambda: np.zeros(n * n)
+    loss, ub, un, unb, stack = np.zeros(1), z(), z(), z(), np.zeros(n_step * n * n)
+    alphab = orc.heat2d_b(loss, np.ones(1), u, ub, un, unb, 0.2, 0.0, n, n_step, stack)
+    tape = stack.reshape(n_step, n, n)
+    for rank, lo, hi, s_ub, s_un, s_tape, s_loss, s_alphab in res:
+        assert np.array_equal(s_ub, ub.reshape(n, n)[lo:hi]), rank
+        assert np.array_equal(s_un, un.reshape(n, n)[lo:hi]), rank
+        for t in range(n_step):
+            assert np.array_equal(s_tape[t][1:-1], tape[t][lo:hi]), (rank, t)
+            assert np.array_equal(s_tape[t][0], tape[t][(lo - 1) % n]), (rank, t)
+            assert np.array_equal(s_tape[t][-1], tape[t][hi % n]), (rank, t)
+        assert abs(s_loss - loss[0]) <= 1e-12 * abs(loss[0])
+        assert abs(s_alphab - alphab) <= 1e-12 * max(1.0, abs(alphab))
