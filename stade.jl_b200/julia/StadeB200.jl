@@ -199,4 +199,82 @@ function mlp2_ce_b_check_replicas(w1, b1, w2, b2, lossb, comm::Comm)
     return nothing
 end
 
+# conv1d_relu_mse, adjoint mode, per_sample = [:x, :t] (:accum wb, :reduced loss,
+# :local xb tb zb rb, :shared w, :seed lossb). Sizes from the arrays: w is
+# n_o x n_c x n_k, x is n_b x n_c x n_l.
+conv1d_relu_mse_b_reset_accum!(wb) = (fill!(wb, 0f0); nothing)
+conv1d_relu_mse_b_reset_reduced!(loss) = (fill!(loss, 0f0); nothing)
+conv1d_relu_mse_b_reset_local!(xb, tb, zb, rb) = (foreach(b -> fill!(b, 0f0), (xb, tb, zb, rb)); nothing)
+
+function conv1d_relu_mse_b_allreduce_accum!(wb, n_local, comm::Comm)
+    ng = Ref{Int64}(0)
+    check(ccall((:stade_conv1d_relu_mse_b_allreduce_accum_f32, libstade), Cint,
+        (CuPtr{Float32}, Int64, Int64, Int64, Int64, Ptr{Cvoid}, Ptr{Int64}, Ref{StadeOpts}),
+        wb, length(wb), 1, 1, n_local, comm.handle, ng, opts()))
+    return ng[]
+end
+
+function conv1d_relu_mse_b_allreduce_reduced!(loss, comm::Comm)
+    check(ccall((:stade_conv1d_relu_mse_b_allreduce_reduced_f32, libstade), Cint,
+        (CuPtr{Float32}, Ptr{Cvoid}, Ref{StadeOpts}), loss, comm.handle, opts()))
+    return nothing
+end
+
+function conv1d_relu_mse_b_check_replicas(w, lossb, comm::Comm)
+    mask = Ref{UInt64}(0)
+    code = ccall((:stade_conv1d_relu_mse_b_check_replicas_f32, libstade), Cint,
+        (CuPtr{Float32}, CuPtr{Float32}, Int64, Int64, Int64, Ptr{Cvoid}, Ptr{UInt64},
+         Ref{StadeOpts}), w, lossb, length(w), 1, 1, comm.handle, mask, opts())
+    if code == 6
+        bad = [n for (i, n) in enumerate(["w", "lossb"]) if (mask[] >> (i - 1)) & 1 == 1]
+        error("conv1d_relu_mse_b_check_replicas: `" * join(bad, "`, `") *
+              "` differ across ranks. A :shared or :seed buffer must hold identical values " *
+              "on every rank.")
+    end
+    check(code)
+    return nothing
+end
+
+# mlp2_ce, hvp mode: the `_hv` names (ddpgen_mode_suffix), per_sample = [:x, :y].
+mlp2_ce_hv_reset_accum!(w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd) =
+    (foreach(b -> fill!(b, 0.0), (w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd)); nothing)
+mlp2_ce_hv_reset_reduced!(loss, lossd) = (fill!(loss, 0.0); fill!(lossd, 0.0); nothing)
+mlp2_ce_hv_reset_local!(xb, yb, hb, zb, pb, xbd, ybd, hbd, zbd, pbd) =
+    (foreach(b -> fill!(b, 0.0), (xb, yb, hb, zb, pb, xbd, ybd, hbd, zbd, pbd)); nothing)
+
+function mlp2_ce_hv_allreduce_accum!(w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd, n_local,
+                                     comm::Comm)
+    ng = Ref{Int64}(0)
+    check(ccall((:stade_mlp2_ce_hv_allreduce_accum_f64, libstade), Cint,
+        (ntuple(_ -> CuPtr{Float64}, 8)..., Int64, Int64, Int64, Int64, Ptr{Cvoid}, Ptr{Int64},
+         Ref{StadeOpts}),
+        w1b, b1b, w2b, b2b, w1bd, b1bd, w2bd, b2bd, div(length(w1b), length(b1b)),
+        length(b1b), length(b2b), n_local, comm.handle, ng, opts()))
+    return ng[]
+end
+
+function mlp2_ce_hv_allreduce_reduced!(loss, lossd, comm::Comm)
+    check(ccall((:stade_mlp2_ce_hv_allreduce_reduced_f64, libstade), Cint,
+        (CuPtr{Float64}, CuPtr{Float64}, Ptr{Cvoid}, Ref{StadeOpts}), loss, lossd, comm.handle,
+        opts()))
+    return nothing
+end
+
+function mlp2_ce_hv_check_replicas(w1, b1, w2, b2, w1d, b1d, w2d, b2d, lossb, lossbd, comm::Comm)
+    mask = Ref{UInt64}(0)
+    code = ccall((:stade_mlp2_ce_hv_check_replicas_f64, libstade), Cint,
+        (ntuple(_ -> CuPtr{Float64}, 10)..., Int64, Int64, Int64, Ptr{Cvoid}, Ptr{UInt64},
+         Ref{StadeOpts}),
+        w1, b1, w2, b2, w1d, b1d, w2d, b2d, lossb, lossbd, div(length(w1), length(b1)),
+        length(b1), length(b2), comm.handle, mask, opts())
+    if code == 6
+        names = ["w1", "b1", "w2", "b2", "w1d", "b1d", "w2d", "b2d", "lossb", "lossbd"]
+        bad = [names[i + 1] for i in 0:9 if (mask[] >> i) & 1 == 1]
+        error("mlp2_ce_hv_check_replicas: `" * join(bad, "`, `") * "` differ across ranks. " *
+              "A :shared or :seed buffer must hold identical values on every rank.")
+    end
+    check(code)
+    return nothing
+end
+
 end # module
