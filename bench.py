@@ -260,12 +260,12 @@ def roofline(phases, phase_work, steps, peaks, peak_src, traffic):
         peak = peaks["hbm_gbs"]
         unit = "GB/s"
     elif kind == "fp64":
-        # no measured FP64 peak exists in MEASURED_PEAKS.json: the nominal B200
-        # FP64 (vector and tensor) rate, 148 SMs x 64 DFMA/clk x 2 x 1.965 GHz
+        # the Float64 tensor-core rate measured in this run (cuBLAS DGEMM,
+        # fp64_peak()); MEASURED_PEAKS.json carries no Float64 figure
         achieved = work / avg_s / 1e12
-        peak = 37.2
+        peak = peaks.get("fp64_tflops") or 37.2
         unit = "TFLOP/s"
-        peak_src = "nominal fp64 (no measured figure)"
+        peak_src = peaks.get("fp64_source", "nominal fp64 (no measured figure)")
     else:
         achieved = work / avg_s / 1e12
         peak = peaks["bf16_tflops"]
@@ -283,6 +283,27 @@ def roofline(phases, phase_work, steps, peaks, peak_src, traffic):
             "traffic": t,
             "launch_ms": ms / cnt, "share_of_step": ms / total_ms if total_ms else None,
             "note": note}, **extra}
+
+
+def fp64_peak(torch, n=8192, reps=5):
+    """Float64 GEMM throughput of this GPU: cuBLAS DGEMM (torch.matmul) on
+    n x n x n, best of `reps` launches after one warm-up, CUDA events on the
+    current stream. The denominator of the Float64 (DMMA) phases' roofline."""
+    a = torch.randn(n, n, dtype=torch.float64, device="cuda")
+    b = torch.randn(n, n, dtype=torch.float64, device="cuda")
+    c = a @ b
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.matmul(a, b, out=c)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    del a, b, c
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
 
 
 def load_traffic(config):
@@ -1147,6 +1168,9 @@ def main():
     stream = torch.cuda.current_stream()
     flush = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     peaks, peak_src = load_peaks()
+    if args.config == "mlp2_ce_hv" or (world == 1 and args.config == "mlp2_ce" and not args.no_extra):
+        peaks["fp64_tflops"] = fp64_peak(torch)
+        peaks["fp64_source"] = "measured (cuBLAS DGEMM 8192^3 in this run, best of 5)"
     clocks = ClockSampler(local)
     clocks.start()
 
@@ -1179,6 +1203,8 @@ def main():
                 "scaling": head.pop("scaling"), "vs_baseline": None, "dtype": head.pop("dtype"),
                 "data": "synthetic (seeded, shapes and distributions of the BASELINE config)",
                 **head}
+        if "fp64_tflops" in peaks:
+            line["fp64_peak"] = {"tflops": peaks["fp64_tflops"], "source": peaks["fp64_source"]}
         if extras:
             line["configs"] = {k: finish(v) for k, v in extras.items()}
             line["gpu_launches_all_configs"] = line["gpu_launches"] + sum(

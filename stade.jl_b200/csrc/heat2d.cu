@@ -21,10 +21,13 @@
 // keeping the rows above and below in registers; horizontal neighbours come
 // from the neighbouring lanes by warp shuffle. alphab and loss are summed per
 // block, then over blocks in a fixed order.
+#include <cstdlib>
+#include <cstring>
 #include <utility>
 
 #include "common.cuh"
 #include "halo.cuh"
+#include "tcgen05.cuh"
 
 namespace stade {
 namespace {
@@ -300,6 +303,158 @@ __global__ void heat_nostep_kernel(const double* __restrict__ u, double* __restr
   if (threadIdx.x == 0) part[blockIdx.x] = s;
 }
 
+// ---- TMA-staged reverse step (one grid, n a multiple of 128) ----------------------
+// A persistent kernel walks 32 x 128 tiles of the output. Per tile the
+// rows i0-1 .. i0+32 and columns j0-2 .. j0+129 of the adjoint state g and of
+// the taped state u are staged in shared memory by two TMA copies
+// (cp.async.bulk.tensor.2d; the box starts 2 columns left of the tile so its
+// innermost coordinate stays 16-byte aligned), three tiles in flight. The grid
+// is periodic and TMA fills outside the tensor with zeros, so a tile on the
+// grid's edge overwrites the halo cells it needs (row -1 <- row n-1, row n <-
+// row 0, column -1 <- column n-1, column n <- column 0) from global memory
+// before computing. Each thread owns two adjacent columns of 8 rows and
+// computes them with gather_point / lap_point, exactly as heat_bwd_kernel does
+// (the same ub bits); its alphab terms are summed per CTA in a fixed tile
+// order. Waits on the copies are bounded (~2 s); a wait that runs out sets
+// g_heat_error, the CTA stops, waits (bounded) for its copies in flight and
+// returns.
+constexpr int kTR = 32, kTC = 128;                 // output tile
+constexpr int kHR = kTR + 2, kHC = kTC + 4;        // staged region
+constexpr int kRegionBytes = kHR * kHC * 8;        // 35,904
+constexpr int kRegionStride = (kRegionBytes + 127) / 128 * 128;   // 128-byte aligned TMA targets
+constexpr int kTmaStages = 3;
+constexpr int kTmaThreads = 256;
+constexpr int kTmaSmem = kTmaStages * 2 * kRegionStride + 128 + 64;
+static_assert(kTmaSmem <= 227 * 1024, "shared memory of a CTA");
+__device__ int g_heat_error = 0;
+
+__global__ void __launch_bounds__(kTmaThreads, 1)
+heat_bwd_tma_kernel(const __grid_constant__ CUtensorMap gmap,
+                    const __grid_constant__ CUtensorMap umap, const double* __restrict__ g,
+                    const double* __restrict__ u, double* __restrict__ gdst, double alpha, int n,
+                    double* __restrict__ alpha_part, int first) {
+  using namespace tc5;
+  extern __shared__ unsigned char smraw[];
+  __shared__ double red[kTmaThreads / 32];
+  const uint32_t raw = smem_u32(smraw);
+  unsigned char* base = smraw + ((128u - (raw & 127u)) & 127u);
+  auto gt = [&](int s) { return reinterpret_cast<double*>(base + (2 * s) * kRegionStride); };
+  auto ut = [&](int s) { return reinterpret_cast<double*>(base + (2 * s + 1) * kRegionStride); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * kTmaStages * kRegionStride);
+  const int tid = threadIdx.x;
+  const int tiles_x = n / kTC, tiles = tiles_x * (n / kTR);
+  const int mine = (int)blockIdx.x < tiles ? (tiles - (int)blockIdx.x + (int)gridDim.x - 1) /
+                                                 (int)gridDim.x
+                                           : 0;
+  if (tid == 0) {
+    for (int s = 0; s < kTmaStages; ++s) mbar_init(smem_u32(bars + s), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  int issued = 0;
+  auto issue = [&](int k) {   // thread 0: stage the k-th tile of this CTA
+    const int t = (int)blockIdx.x + k * (int)gridDim.x;
+    const int s = k % kTmaStages;
+    const uint32_t bar = smem_u32(bars + s);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_tx(bar, 2 * kRegionBytes);
+    tma_load_2d(smem_u32(gt(s)), &gmap, (t % tiles_x) * kTC - 2, (t / tiles_x) * kTR - 1, bar);
+    tma_load_2d(smem_u32(ut(s)), &umap, (t % tiles_x) * kTC - 2, (t / tiles_x) * kTR - 1, bar);
+  };
+  if (tid == 0)
+    for (; issued < kTmaStages - 1 && issued < mine; ++issued) issue(issued);
+  const int cp = tid & 63, rg = tid >> 6;   // column pair, group of 8 rows
+  double asum = 0.0;
+  bool ok = true;
+  int k = 0;
+  for (; k < mine; ++k) {
+    if (tid == 0 && issued < mine) issue(issued++);
+    const int s = k % kTmaStages;
+    const bool got = mbar_wait_for(smem_u32(bars + s), (uint32_t)(k / kTmaStages) & 1u,
+                                   &g_heat_error, kWaitCycles);
+    ok = __syncthreads_and(got) != 0;
+    if (!ok) break;
+    const int t = (int)blockIdx.x + k * (int)gridDim.x;
+    const int i0 = (t / tiles_x) * kTR, j0 = (t % tiles_x) * kTC;
+    double* G = gt(s);
+    double* U = ut(s);
+    // periodic halos of an edge tile (TMA filled them with zeros)
+    if (i0 == 0 || i0 + kTR == n || j0 == 0 || j0 + kTC == n) {
+      for (int e = tid; e < 2 * kTC + 2 * kTR; e += kTmaThreads) {
+        int64_t src = -1;
+        int dst = 0;
+        if (e < kTC) {                          // row -1 <- row n-1
+          if (i0 == 0) { src = (int64_t)(n - 1) * n + j0 + e; dst = 2 + e; }
+        } else if (e < 2 * kTC) {               // row 32 <- row 0
+          const int c = e - kTC;
+          if (i0 + kTR == n) { src = j0 + c; dst = (kHR - 1) * kHC + 2 + c; }
+        } else if (e < 2 * kTC + kTR) {         // column -1 <- column n-1
+          const int r = e - 2 * kTC;
+          if (j0 == 0) { src = (int64_t)(i0 + r) * n + (n - 1); dst = (1 + r) * kHC + 1; }
+        } else {                                // column 128 <- column 0
+          const int r = e - 2 * kTC - kTR;
+          if (j0 + kTC == n) { src = (int64_t)(i0 + r) * n; dst = (1 + r) * kHC + 2 + kTC; }
+        }
+        if (src >= 0) {
+          G[dst] = g[src];
+          U[dst] = u[src];
+        }
+      }
+      __syncthreads();
+    }
+    const int c = 2 + 2 * cp;
+#pragma unroll 2
+    for (int r = 0; r < 8; ++r) {
+      const int R = 1 + rg * 8 + r;
+      const double2 gc = *reinterpret_cast<const double2*>(G + R * kHC + c);
+      const double2 gu = *reinterpret_cast<const double2*>(G + (R - 1) * kHC + c);
+      const double2 gd = *reinterpret_cast<const double2*>(G + (R + 1) * kHC + c);
+      const double g_lf = G[R * kHC + c - 1], g_rt = G[R * kHC + c + 2];
+      const double2 uc = *reinterpret_cast<const double2*>(U + R * kHC + c);
+      const double2 uu = *reinterpret_cast<const double2*>(U + (R - 1) * kHC + c);
+      const double2 ud = *reinterpret_cast<const double2*>(U + (R + 1) * kHC + c);
+      const double u_lf = U[R * kHC + c - 1], u_rt = U[R * kHC + c + 2];
+      double2 o;
+      o.x = gather_point(gc.x, gu.x, gd.x, g_lf, gc.y, alpha);
+      o.y = gather_point(gc.y, gu.y, gd.y, gc.x, g_rt, alpha);
+      *reinterpret_cast<double2*>(gdst + (int64_t)(i0 + R - 1) * n + j0 + 2 * cp) = o;
+      asum = fma(lap_point(uc.x, uu.x, ud.x, u_lf, uc.y), gc.x, asum);
+      asum = fma(lap_point(uc.y, uu.y, ud.y, uc.x, u_rt), gc.y, asum);
+    }
+    __syncthreads();   // the stage is free for the copy issued next iteration
+  }
+  if (!ok && tid == 0) {
+    // copies still in flight land before the CTA exits (bounded)
+    for (int j = k; j < issued; ++j)
+      mbar_wait_for(smem_u32(bars + j % kTmaStages), (uint32_t)(j / kTmaStages) & 1u,
+                    &g_heat_error, kWaitCycles);
+  }
+  asum = block_sum(asum, red);
+  if (tid == 0) alpha_part[blockIdx.x] = first ? asum : alpha_part[blockIdx.x] + asum;
+}
+
+// Tensor map of an n x n Float64 field for heat_bwd_tma_kernel: box of
+// 132 columns x 34 rows, no swizzle, zero fill outside.
+stade_status heat_map(CUtensorMap* map, const double* base, int64_t n) {
+  auto fn = tc5::encode_fn();
+  if (!fn) return fail(STADE_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t d[2] = {(cuuint64_t)n, (cuuint64_t)n}, st[1] = {(cuuint64_t)(n * 8)};
+  cuuint32_t bx[2] = {(cuuint32_t)kHC, (cuuint32_t)kHR}, es[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double*>(base), d, st, bx,
+                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(STADE_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return STADE_OK;
+}
+
+// The TMA-staged reverse step runs where its tiles cover the grid exactly;
+// STADE_HEAT_TMA=0 selects the register-tiled kernel instead.
+bool heat_tma_enabled(int64_t n) {
+  const char* e = std::getenv("STADE_HEAT_TMA");
+  if (e && std::strcmp(e, "0") == 0) return false;
+  return n % kTC == 0 && n >= kTC && n <= 65536;
+}
+
 struct Grid {
   dim3 fwd, bwd;
   int nfwd, nbwd;
@@ -433,16 +588,29 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
         heat_bwd_init1_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, a, nn);
       STADE_CHECK_LAUNCH();
     }
+    const bool tma = paired && heat_tma_enabled(n);
+    const int tma_grid = (int)std::min<int64_t>((n / kTC) * (n / kTR), tc5::sm_count());
+    if (tma)
+      STADE_CUDA(cudaFuncSetAttribute(heat_bwd_tma_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem));
     for (int64_t t = n_step; t >= 1; --t) {
       PhaseScope ph("bwd_step", s);
       const double* ut = u_stack + (t - 1) * nn;
       const int first = t == n_step ? 1 : 0;
-      if (paired)
+      if (tma) {
+        CUtensorMap gm, um;
+        st = heat_map(&gm, a, n);
+        if (st == STADE_OK) st = heat_map(&um, ut, n);
+        if (st != STADE_OK) return st;
+        heat_bwd_tma_kernel<<<tma_grid, kTmaThreads, kTmaSmem, s>>>(gm, um, a, ut, b, alpha, ni,
+                                                                    alpha_part, first);
+      } else if (paired) {
         heat_bwd_kernel<kRowsBwd, true><<<g.bwd, kThreads, 0, s>>>(
             a, ut, b, alpha, ni, 0, kRowsBwd, ni, alpha_part, first);
-      else
+      } else {
         heat_bwd1_kernel<kRowsBwd><<<g.bwd, kColsPerBlock, 0, s>>>(a, ut, b, alpha, ni,
                                                                     alpha_part, first);
+      }
       STADE_CHECK_LAUNCH();
       double* tmp = a; a = b; b = tmp;
     }
@@ -451,7 +619,7 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
       PhaseScope ph("zero_unb", s);
       STADE_CUDA(cudaMemsetAsync(unb, 0, (size_t)nn * sizeof(double), s));
     }
-    st = launch_sum_to_scalar(alpha_part, g.nbwd, alphab_dev, true, s);
+    st = launch_sum_to_scalar(alpha_part, tma ? tma_grid : g.nbwd, alphab_dev, true, s);
     if (st != STADE_OK) return st;
   }
   if (host_scalar) {
@@ -460,6 +628,19 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
   }
   return STADE_OK;
 }
+
+namespace stade {
+// Reads and clears the stencil kernel's error word (-1 when it cannot be read).
+int heat_take_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_heat_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_heat_error, &zero, sizeof(int));
+  }
+  return v;
+}
+}  // namespace stade
 
 
 // ---------------------------------------------------------------------------

@@ -943,6 +943,7 @@ int tma_take_error() {
 
 namespace stade {
 int conv_tc_take_error();
+int heat_take_error();
 
 namespace {
 __device__ int g_wait_check_out = 0;
@@ -982,6 +983,7 @@ extern "C" stade_status stade_check_bounded_wait(int64_t wait_cycles, const stad
 extern "C" int stade_device_error(void) {
   const int t = stade::tma_take_error();
   const int c = stade::conv_tc_take_error();
-  if (t < 0 || c < 0) return -1;
-  return t | c;
+  const int h = stade::heat_take_error();
+  if (t < 0 || c < 0 || h < 0) return -1;
+  return t | c | h;
 }
