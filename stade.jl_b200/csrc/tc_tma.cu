@@ -783,14 +783,33 @@ Geometry geometry(int M, int N, int K, int slices, bool a_mn, bool b_mn) {
   return g;
 }
 
-// Slices of the W1b contraction (K = samples): enough tiles for ~4 per SM,
-// at least 32 K blocks per slice.
+// Slices of the W1b contraction (K = samples). Every (tile, slice) unit costs
+// the same, and the persistent grid takes them in waves of one per SM, so the
+// slice count minimises waves x K blocks per slice (the busiest SM's work),
+// plus a small charge per slice for the partial it writes and the finish pass
+// reads; at least 16 K blocks per slice. 784 x 512 over 65,536 samples: 28
+// tiles x 21 slices = 588 units, 4 waves 99 % full (22 slices left 616 units:
+// 5 waves, the last 16 % full).
 int w1b_slices(int S, int I, int H) {
   const int tiles = ((I + BM - 1) / BM) * ((H + BN - 1) / BN);
   const int kblocks = (S + BK - 1) / BK;
-  int sl = (4 * 148 + tiles - 1) / tiles;
-  while (sl > 1 && kblocks / sl < 32) --sl;
-  return sl < 1 ? 1 : sl;
+  const int sms = tc5::sm_count();
+  int best = 1;
+  double best_cost = 0.0;
+  for (int sl = 1; sl <= 64; ++sl) {
+    const int per = (kblocks + sl - 1) / sl;
+    if (sl > 1 && per < 16) break;
+    const int slices = (kblocks + per - 1) / per;
+    const int waves = (tiles * slices + sms - 1) / sms;
+    // one partial tile (128 x 128 Float32 written and read) ~ the traffic of
+    // 2 K blocks of operands
+    const double cost = (double)waves * per + (slices > 1 ? 2.0 * slices * tiles / sms : 0.0);
+    if (sl == 1 || cost < best_cost) {
+      best = sl;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 // hi / lo split of a Float32 array (n % 4 == 0 handled by the vector path),

@@ -146,8 +146,11 @@ def test_heat2d_b_tma_stencil(n, n_step, seeded, monkeypatch):
         assert np.array_equal(out["u_stack"], ref["u_stack"])
         assert rel_err(out["ub"], ref["ub"]) <= F64_TOL
         assert abs(ab_gpu - ab_ref) <= F64_TOL * max(1.0, abs(ab_ref))
-        a = out["ub"].reshape(n, n)[1:-1, 1:-1]
-        assert np.array_equal(a, ref["ub"].reshape(n, n)[1:-1, 1:-1])
+        if n_step == 1:
+            # one step: interior cells add their contributions in the generated
+            # order (later steps carry the wrapped cells' other order inward)
+            a = out["ub"].reshape(n, n)[1:-1, 1:-1]
+            assert np.array_equal(a, ref["ub"].reshape(n, n)[1:-1, 1:-1])
     assert np.array_equal(outs["1"][0]["ub"], outs["0"][0]["ub"])
     assert np.array_equal(outs["1"][0]["unb"], outs["0"][0]["unb"])
 
