@@ -318,82 +318,88 @@ __global__ void heat_nostep_kernel(const double* __restrict__ u, double* __restr
 // order. Waits on the copies are bounded (~2 s); a wait that runs out sets
 // g_heat_error, the CTA stops, waits (bounded) for its copies in flight and
 // returns.
-constexpr int kTR = 32, kTC = 128;                 // output tile
-constexpr int kHR = kTR + 2, kHC = kTC + 4;        // staged region
-constexpr int kRegionBytes = kHR * kHC * 8;        // 35,904
-constexpr int kRegionStride = (kRegionBytes + 127) / 128 * 128;   // 128-byte aligned TMA targets
-constexpr int kTmaStages = 3;
-constexpr int kTmaThreads = 256;
-constexpr int kTmaSmem = kTmaStages * 2 * kRegionStride + 128 + 64;
-static_assert(kTmaSmem <= 227 * 1024, "shared memory of a CTA");
+template <int TR, int TC, int ST, int NT>
+struct TmaTile {
+  static constexpr int kHR = TR + 2, kHC = TC + 4;                   // staged region
+  static constexpr int kRegionBytes = kHR * kHC * 8;
+  static constexpr int kStride = (kRegionBytes + 127) / 128 * 128;   // 128-byte aligned targets
+  static constexpr int kSmem = ST * 2 * kStride + 128 + 64;
+  static constexpr int kRowsPerThread = TR * TC / 2 / NT;            // a thread: 2 columns
+  static_assert(TR * TC % (2 * NT) == 0 && NT % (TC / 2) == 0, "tile / thread split");
+  static_assert(kSmem <= 227 * 1024, "shared memory of a CTA");
+  static_assert(kHC <= 256 && kHR <= 256 && (kHC * 8) % 16 == 0, "TMA box");
+};
 __device__ int g_heat_error = 0;
 
-__global__ void __launch_bounds__(kTmaThreads, 1)
+template <int TR, int TC, int ST, int NT, int MINB>
+__global__ void __launch_bounds__(NT, MINB)
 heat_bwd_tma_kernel(const __grid_constant__ CUtensorMap gmap,
                     const __grid_constant__ CUtensorMap umap, const double* __restrict__ g,
                     const double* __restrict__ u, double* __restrict__ gdst, double alpha, int n,
                     double* __restrict__ alpha_part, int first) {
   using namespace tc5;
+  using Tl = TmaTile<TR, TC, ST, NT>;
+  constexpr int kHR = Tl::kHR, kHC = Tl::kHC, RPT = Tl::kRowsPerThread;
   extern __shared__ unsigned char smraw[];
-  __shared__ double red[kTmaThreads / 32];
+  __shared__ double red[NT / 32];
   const uint32_t raw = smem_u32(smraw);
   unsigned char* base = smraw + ((128u - (raw & 127u)) & 127u);
-  auto gt = [&](int s) { return reinterpret_cast<double*>(base + (2 * s) * kRegionStride); };
-  auto ut = [&](int s) { return reinterpret_cast<double*>(base + (2 * s + 1) * kRegionStride); };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * kTmaStages * kRegionStride);
+  auto gt = [&](int s) { return reinterpret_cast<double*>(base + (2 * s) * Tl::kStride); };
+  auto ut = [&](int s) { return reinterpret_cast<double*>(base + (2 * s + 1) * Tl::kStride); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * ST * Tl::kStride);
   const int tid = threadIdx.x;
-  const int tiles_x = n / kTC, tiles = tiles_x * (n / kTR);
+  const int tiles_x = n / TC, tiles = tiles_x * (n / TR);
   const int mine = (int)blockIdx.x < tiles ? (tiles - (int)blockIdx.x + (int)gridDim.x - 1) /
                                                  (int)gridDim.x
                                            : 0;
   if (tid == 0) {
-    for (int s = 0; s < kTmaStages; ++s) mbar_init(smem_u32(bars + s), 1);
+    for (int s = 0; s < ST; ++s) mbar_init(smem_u32(bars + s), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   int issued = 0;
   auto issue = [&](int k) {   // thread 0: stage the k-th tile of this CTA
     const int t = (int)blockIdx.x + k * (int)gridDim.x;
-    const int s = k % kTmaStages;
+    const int s = k % ST;
     const uint32_t bar = smem_u32(bars + s);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_arrive_tx(bar, 2 * kRegionBytes);
-    tma_load_2d(smem_u32(gt(s)), &gmap, (t % tiles_x) * kTC - 2, (t / tiles_x) * kTR - 1, bar);
-    tma_load_2d(smem_u32(ut(s)), &umap, (t % tiles_x) * kTC - 2, (t / tiles_x) * kTR - 1, bar);
+    mbar_arrive_tx(bar, 2 * Tl::kRegionBytes);
+    tma_load_2d(smem_u32(gt(s)), &gmap, (t % tiles_x) * TC - 2, (t / tiles_x) * TR - 1, bar);
+    tma_load_2d(smem_u32(ut(s)), &umap, (t % tiles_x) * TC - 2, (t / tiles_x) * TR - 1, bar);
   };
   if (tid == 0)
-    for (; issued < kTmaStages - 1 && issued < mine; ++issued) issue(issued);
-  const int cp = tid & 63, rg = tid >> 6;   // column pair, group of 8 rows
+    for (; issued < ST - 1 && issued < mine; ++issued) issue(issued);
+  const int cp = tid % (TC / 2), rg = tid / (TC / 2);   // column pair, group of RPT rows
   double asum = 0.0;
   bool ok = true;
   int k = 0;
   for (; k < mine; ++k) {
     if (tid == 0 && issued < mine) issue(issued++);
-    const int s = k % kTmaStages;
-    const bool got = mbar_wait_for(smem_u32(bars + s), (uint32_t)(k / kTmaStages) & 1u,
-                                   &g_heat_error, kWaitCycles);
+    const int s = k % ST;
+    const bool got = mbar_wait_for(smem_u32(bars + s), (uint32_t)(k / ST) & 1u, &g_heat_error,
+                                   kWaitCycles);
     ok = __syncthreads_and(got) != 0;
     if (!ok) break;
     const int t = (int)blockIdx.x + k * (int)gridDim.x;
-    const int i0 = (t / tiles_x) * kTR, j0 = (t % tiles_x) * kTC;
+    const int i0 = (t / tiles_x) * TR, j0 = (t % tiles_x) * TC;
     double* G = gt(s);
     double* U = ut(s);
     // periodic halos of an edge tile (TMA filled them with zeros)
-    if (i0 == 0 || i0 + kTR == n || j0 == 0 || j0 + kTC == n) {
-      for (int e = tid; e < 2 * kTC + 2 * kTR; e += kTmaThreads) {
+    if (i0 == 0 || i0 + TR == n || j0 == 0 || j0 + TC == n) {
+      for (int e = tid; e < 2 * TC + 2 * TR; e += NT) {
         int64_t src = -1;
         int dst = 0;
-        if (e < kTC) {                          // row -1 <- row n-1
+        if (e < TC) {                           // row -1 <- row n-1
           if (i0 == 0) { src = (int64_t)(n - 1) * n + j0 + e; dst = 2 + e; }
-        } else if (e < 2 * kTC) {               // row 32 <- row 0
-          const int c = e - kTC;
-          if (i0 + kTR == n) { src = j0 + c; dst = (kHR - 1) * kHC + 2 + c; }
-        } else if (e < 2 * kTC + kTR) {         // column -1 <- column n-1
-          const int r = e - 2 * kTC;
+        } else if (e < 2 * TC) {                // row TR <- row 0
+          const int c = e - TC;
+          if (i0 + TR == n) { src = j0 + c; dst = (kHR - 1) * kHC + 2 + c; }
+        } else if (e < 2 * TC + TR) {           // column -1 <- column n-1
+          const int r = e - 2 * TC;
           if (j0 == 0) { src = (int64_t)(i0 + r) * n + (n - 1); dst = (1 + r) * kHC + 1; }
-        } else {                                // column 128 <- column 0
-          const int r = e - 2 * kTC - kTR;
-          if (j0 + kTC == n) { src = (int64_t)(i0 + r) * n; dst = (1 + r) * kHC + 2 + kTC; }
+        } else {                                // column TC <- column 0
+          const int r = e - 2 * TC - TR;
+          if (j0 + TC == n) { src = (int64_t)(i0 + r) * n; dst = (1 + r) * kHC + 2 + TC; }
         }
         if (src >= 0) {
           G[dst] = g[src];
@@ -404,8 +410,8 @@ heat_bwd_tma_kernel(const __grid_constant__ CUtensorMap gmap,
     }
     const int c = 2 + 2 * cp;
 #pragma unroll 2
-    for (int r = 0; r < 8; ++r) {
-      const int R = 1 + rg * 8 + r;
+    for (int r = 0; r < RPT; ++r) {
+      const int R = 1 + rg * RPT + r;
       const double2 gc = *reinterpret_cast<const double2*>(G + R * kHC + c);
       const double2 gu = *reinterpret_cast<const double2*>(G + (R - 1) * kHC + c);
       const double2 gd = *reinterpret_cast<const double2*>(G + (R + 1) * kHC + c);
@@ -426,20 +432,43 @@ heat_bwd_tma_kernel(const __grid_constant__ CUtensorMap gmap,
   if (!ok && tid == 0) {
     // copies still in flight land before the CTA exits (bounded)
     for (int j = k; j < issued; ++j)
-      mbar_wait_for(smem_u32(bars + j % kTmaStages), (uint32_t)(j / kTmaStages) & 1u,
-                    &g_heat_error, kWaitCycles);
+      mbar_wait_for(smem_u32(bars + j % ST), (uint32_t)(j / ST) & 1u, &g_heat_error,
+                    kWaitCycles);
   }
   asum = block_sum(asum, red);
   if (tid == 0) alpha_part[blockIdx.x] = first ? asum : alpha_part[blockIdx.x] + asum;
 }
 
+// The launch of one tile shape: grid = min(tiles, resident CTAs).
+struct TmaVariant {
+  int tr, tc, smem, threads, per_sm;
+  void (*kern)(CUtensorMap, CUtensorMap, const double*, const double*, double*, double, int,
+               double*, int);
+};
+template <int TR, int TC, int ST, int NT, int MINB>
+TmaVariant tma_variant() {
+  using Tl = TmaTile<TR, TC, ST, NT>;
+  return TmaVariant{TR, TC, Tl::kSmem, NT, MINB, heat_bwd_tma_kernel<TR, TC, ST, NT, MINB>};
+}
+// a: 32 x 128 tiles, 3 in flight, one CTA of 256 threads per SM; b: 16 x 128,
+// 2 in flight, two CTAs per SM; c: 32 x 64, 3 in flight, two CTAs of 128
+// threads per SM; d: 32 x 128, 3 in flight, 512 threads.
+TmaVariant heat_tma_variant(char v) {
+  switch (v) {
+    case 'b': return tma_variant<16, 128, 2, 256, 2>();
+    case 'c': return tma_variant<32, 64, 3, 128, 2>();
+    case 'd': return tma_variant<32, 128, 3, 512, 1>();
+    default:  return tma_variant<32, 128, 3, 256, 1>();
+  }
+}
+
 // Tensor map of an n x n Float64 field for heat_bwd_tma_kernel: box of
-// 132 columns x 34 rows, no swizzle, zero fill outside.
-stade_status heat_map(CUtensorMap* map, const double* base, int64_t n) {
+// (tc + 4) columns x (tr + 2) rows, no swizzle, zero fill outside.
+stade_status heat_map(CUtensorMap* map, const double* base, int64_t n, int tr, int tc) {
   auto fn = tc5::encode_fn();
   if (!fn) return fail(STADE_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t d[2] = {(cuuint64_t)n, (cuuint64_t)n}, st[1] = {(cuuint64_t)(n * 8)};
-  cuuint32_t bx[2] = {(cuuint32_t)kHC, (cuuint32_t)kHR}, es[2] = {1, 1};
+  cuuint32_t bx[2] = {(cuuint32_t)(tc + 4), (cuuint32_t)(tr + 2)}, es[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double*>(base), d, st, bx,
                   es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -447,12 +476,16 @@ stade_status heat_map(CUtensorMap* map, const double* base, int64_t n) {
   return STADE_OK;
 }
 
-// The TMA-staged reverse step runs where its tiles cover the grid exactly;
-// STADE_HEAT_TMA=0 selects the register-tiled kernel instead.
-bool heat_tma_enabled(int64_t n) {
+// The TMA-staged reverse step runs where its tiles cover the grid exactly.
+// STADE_HEAT_TMA selects it: "0" the register-tiled kernel, a letter a tile
+// shape (heat_tma_variant), unset the default shape.
+char heat_tma_choice(int64_t n) {
   const char* e = std::getenv("STADE_HEAT_TMA");
-  if (e && std::strcmp(e, "0") == 0) return false;
-  return n % kTC == 0 && n >= kTC && n <= 65536;
+  char v = 'a';
+  if (e && std::strcmp(e, "0") == 0) return 0;
+  if (e && e[0] >= 'a' && e[0] <= 'd') v = e[0];
+  const TmaVariant tv = heat_tma_variant(v);
+  return (n % tv.tc == 0 && n % tv.tr == 0 && n >= tv.tc && n <= 65536) ? v : 0;
 }
 
 struct Grid {
@@ -588,22 +621,25 @@ extern "C" stade_status stade_heat2d_b_f64(double* loss, const double* lossb, do
         heat_bwd_init1_kernel<<<kNoStepBlocks, 256, 0, s>>>(ub, unb, un, lossb, a, nn);
       STADE_CHECK_LAUNCH();
     }
-    const bool tma = paired && heat_tma_enabled(n);
-    const int tma_grid = (int)std::min<int64_t>((n / kTC) * (n / kTR), tc5::sm_count());
+    const char tv_id = paired ? heat_tma_choice(n) : 0;
+    const bool tma = tv_id != 0;
+    const TmaVariant tv = heat_tma_variant(tma ? tv_id : 'a');
+    const int tma_grid =
+        (int)std::min<int64_t>((n / tv.tc) * (n / tv.tr), (int64_t)tc5::sm_count() * tv.per_sm);
     if (tma)
-      STADE_CUDA(cudaFuncSetAttribute(heat_bwd_tma_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem));
+      STADE_CUDA(cudaFuncSetAttribute(tv.kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      tv.smem));
     for (int64_t t = n_step; t >= 1; --t) {
       PhaseScope ph("bwd_step", s);
       const double* ut = u_stack + (t - 1) * nn;
       const int first = t == n_step ? 1 : 0;
       if (tma) {
         CUtensorMap gm, um;
-        st = heat_map(&gm, a, n);
-        if (st == STADE_OK) st = heat_map(&um, ut, n);
+        st = heat_map(&gm, a, n, tv.tr, tv.tc);
+        if (st == STADE_OK) st = heat_map(&um, ut, n, tv.tr, tv.tc);
         if (st != STADE_OK) return st;
-        heat_bwd_tma_kernel<<<tma_grid, kTmaThreads, kTmaSmem, s>>>(gm, um, a, ut, b, alpha, ni,
-                                                                    alpha_part, first);
+        tv.kern<<<tma_grid, tv.threads, tv.smem, s>>>(gm, um, a, ut, b, alpha, ni, alpha_part,
+                                                      first);
       } else if (paired) {
         heat_bwd_kernel<kRowsBwd, true><<<g.bwd, kThreads, 0, s>>>(
             a, ut, b, alpha, ni, 0, kRowsBwd, ni, alpha_part, first);

@@ -131,13 +131,13 @@ def test_heat2d_b_interior_bit_exact():
 @pytest.mark.parametrize("n,n_step,seeded", [(128, 3, True), (256, 2, False), (384, 1, True),
                                               (1024, 4, True)])
 def test_heat2d_b_tma_stencil(n, n_step, seeded, monkeypatch):
-    """The TMA-staged reverse step (n a multiple of 128; tiles on all four grid
-    edges, where the periodic halos are patched in shared memory): ub bit for
-    bit equal to the register-tiled kernel's, every output against the
-    oracle, and no bounded wait ran out."""
+    """The TMA-staged reverse step in each tile shape (n a multiple of 128;
+    tiles on all four grid edges, where the periodic halos are patched in
+    shared memory): ub bit for bit equal to the register-tiled kernel's, every
+    output against the oracle, and no bounded wait ran out."""
     from stadeb200 import _lib
     outs = {}
-    for mode in ("1", "0"):
+    for mode in ("a", "b", "c", "d", "0"):   # the tile shapes, then the register kernel
         monkeypatch.setenv("STADE_HEAT_TMA", mode)
         ref, out, ints, ab_ref, ab_gpu = _run_both(
             lambda: cases.heat_state(n, n_step, seeded=seeded), cases.oracle_heat, cases.gpu_heat)
@@ -151,8 +151,9 @@ def test_heat2d_b_tma_stencil(n, n_step, seeded, monkeypatch):
             # order (later steps carry the wrapped cells' other order inward)
             a = out["ub"].reshape(n, n)[1:-1, 1:-1]
             assert np.array_equal(a, ref["ub"].reshape(n, n)[1:-1, 1:-1])
-    assert np.array_equal(outs["1"][0]["ub"], outs["0"][0]["ub"])
-    assert np.array_equal(outs["1"][0]["unb"], outs["0"][0]["unb"])
+    for mode in ("a", "b", "c", "d"):
+        assert np.array_equal(outs[mode][0]["ub"], outs["0"][0]["ub"]), mode
+        assert np.array_equal(outs[mode][0]["unb"], outs["0"][0]["unb"]), mode
 
 
 def test_heat2d_b_homogeneity_medium():
