@@ -471,9 +471,16 @@ class Mlp2Ce:
         t = {k: v.to(dev) for k, v in self.host.items()}
         S, I, H, O = self.n_s, self.n_i, self.n_h, self.n_o
         z = lambda n: torch.zeros(n, dtype=f32, device=dev)
-        t.update(loss=z(1), xb=z(S * I), yb=z(S * O), w1b=z(I * H), b1b=z(H), w2b=z(H * O),
-                 b2b=z(O), h=z(S * H), hb=z(S * H), zz=z(S * O), zb=z(S * O), p=z(S * O),
-                 pb=z(S * O))
+        t.update(xb=z(S * I), yb=z(S * O), h=z(S * H), hb=z(S * H), zz=z(S * O), zb=z(S * O),
+                 p=z(S * O), pb=z(S * O))
+        # the :accum shadows and the :reduced loss back to back in one allocation:
+        # the step sums them with one NCCL all-reduce in place (no gather /
+        # scatter into a bucket)
+        self.bucket = z(I * H + H + H * O + O + 1)
+        off = 0
+        for k, n in (("w1b", I * H), ("b1b", H), ("w2b", H * O), ("b2b", O), ("loss", 1)):
+            t[k] = self.bucket[off:off + n]
+            off += n
         self.t = t
         self.ws = torch.empty(kernels.mlp2_ce_b_workspace(S, I, H, O), dtype=torch.uint8, device=dev)
         self.comm = comm_factory() if world > 1 else None
@@ -492,8 +499,8 @@ class Mlp2Ce:
                                     t["pb"], self.n_s, self.n_i, self.n_h, self.n_o,
                                     workspace=self.ws)
         if self.comm is not None:
-            d.allreduce_sum_(self.comm, t["w1b"], t["b1b"], t["w2b"], t["b2b"])
-            d.allreduce_sum_(self.comm, t["loss"])
+            # :accum and :reduced are summed every step here, so one collective
+            d.allreduce_sum_(self.comm, t["w1b"], t["b1b"], t["w2b"], t["b2b"], t["loss"])
 
     E2E_CHUNKS = 8
 
@@ -531,8 +538,7 @@ class Mlp2Ce:
                                         sl("zz", O), sl("zb", O), sl("p", O), sl("pb", O),
                                         hi - lo, I, H, O, workspace=self.ws)
         if self.comm is not None:
-            d.allreduce_sum_(self.comm, t["w1b"], t["b1b"], t["w2b"], t["b2b"])
-            d.allreduce_sum_(self.comm, t["loss"])
+            d.allreduce_sum_(self.comm, t["w1b"], t["b1b"], t["w2b"], t["b2b"], t["loss"])
         for k, v in self.grad_host.items():
             v.copy_(t[k], non_blocking=True)
 
@@ -913,6 +919,19 @@ class Mlp2CeHv:
         self.pinned = {k: torch.from_numpy(v).pin_memory() for k, v in d.items()}
         t = {k: v.to("cuda") for k, v in self.pinned.items()}
         S, I, H, O = self.S, self.I, self.H, self.O
+        from stadeb200 import ddp as _ddp
+        roles = _ddp.derive_roles(_ddp.MLP2_CE, ["x", "y"], "hvp")
+        summed = (_ddp.role_args(_ddp.MLP2_CE, roles, "hvp", "accum") +
+                  _ddp.role_args(_ddp.MLP2_CE, roles, "hvp", "reduced"))
+        # the eight :accum shadows and loss / lossd back to back: one NCCL
+        # all-reduce in place per step
+        lens = [kernels._mlp_len(nm, S, I, H, O) for nm in summed]
+        self.bucket = torch.zeros(sum(lens), dtype=torch.float64, device="cuda")
+        off = 0
+        for nm, n in zip(summed, lens):
+            t[nm] = self.bucket[off:off + n]
+            off += n
+        self.summed = summed
         for name in kernels.MLP_HV_ARGS + kernels.MLP_HV_TAN:
             if name not in t:
                 t[name] = torch.zeros(kernels._mlp_len(name, S, I, H, O), dtype=torch.float64,
@@ -937,8 +956,8 @@ class Mlp2CeHv:
                                      self.H, self.O, *[t[a] for a in self.kernels.MLP_HV_TAN],
                                      workspace=self.ws)
         if self.comm is not None:
-            e.backend.allreduce_sum([t[b] for b in e.accum])
-            e.allreduce_reduced(t)
+            # :accum and :reduced summed every step: one collective over the bucket
+            e.backend.allreduce_sum([t[b] for b in self.summed])
 
     def e2e_step(self):
         t, p = self.t, self.pinned
