@@ -203,6 +203,76 @@ mlp_head_b_kernel(const T* __restrict__ lossb, const T* __restrict__ y, T* __res
   }
 }
 
+// The same logits with four sample rows per warp pass (n_o <= 16, n_h a
+// multiple of 128): each w2 float4 read from shared memory serves four rows
+// (a quarter of the shared-memory traffic), and the 16 per-class partial sums
+// of a lane are reduced across the warp by halving exchanges (8 + 4 + 2 + 1
+// shuffles, then one to pair up: 16 per row instead of a 5-shuffle sum for
+// each class). Lane l ends with class ((l >> 4) & 1) * 8 + ((l >> 3) & 1) * 4
+// + ((l >> 2) & 1) * 2 + ((l >> 1) & 1), written by the even lanes.
+constexpr int kLogitRows = 4;
+__global__ void __launch_bounds__(256)
+mlp_logits_rows_kernel(const float* __restrict__ h, const float* __restrict__ w2,
+                       float* __restrict__ z0, int n_s, int n_h, int n_o) {
+  extern __shared__ __align__(16) float w2t[];   // 16 x n_h, class-major, zero-padded
+  for (int e = threadIdx.x; e < n_h * 16; e += blockDim.x) {
+    const int c = e / n_h, k = e % n_h;
+    w2t[e] = c < n_o ? w2[(int64_t)k * n_o + c] : 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int n4 = n_h >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w2t);
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const int groups = (n_s + kLogitRows - 1) / kLogitRows;
+  for (int gi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); gi < groups; gi += warps) {
+    const int s0 = gi * kLogitRows;
+    float acc[kLogitRows][16];
+#pragma unroll
+    for (int r = 0; r < kLogitRows; ++r)
+#pragma unroll
+      for (int c = 0; c < 16; ++c) acc[r][c] = 0.f;
+    for (int base = 0; base < n4; base += 32) {
+      const int k4 = base + lane;
+      float4 hv[kLogitRows];
+#pragma unroll
+      for (int r = 0; r < kLogitRows; ++r)
+        hv[r] = s0 + r < n_s ? reinterpret_cast<const float4*>(h + (int64_t)(s0 + r) * n_h)[k4]
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float4 w = w4[c * n4 + k4];
+#pragma unroll
+        for (int r = 0; r < kLogitRows; ++r) {
+          acc[r][c] = fmaf(hv[r].x, w.x, acc[r][c]);
+          acc[r][c] = fmaf(hv[r].y, w.y, acc[r][c]);
+          acc[r][c] = fmaf(hv[r].z, w.z, acc[r][c]);
+          acc[r][c] = fmaf(hv[r].w, w.w, acc[r][c]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kLogitRows; ++r) {
+      float* a = acc[r];
+      // halving exchanges: keep the half of the classes this lane's bit selects
+#pragma unroll
+      for (int w = 8, bit = 16; w >= 1; w >>= 1, bit >>= 1) {
+        const bool upper = (lane & bit) != 0;
+#pragma unroll
+        for (int i = 0; i < w; ++i) {
+          const float keep = upper ? a[i + w] : a[i];
+          const float send = upper ? a[i] : a[i + w];
+          a[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+        }
+      }
+      const float v = a[0] + __shfl_xor_sync(0xffffffffu, a[0], 1);
+      const int c = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
+                    ((lane >> 1) & 1);
+      if ((lane & 1) == 0 && c < n_o && s0 + r < n_s) z0[(int64_t)(s0 + r) * n_o + c] = v;
+    }
+  }
+}
+
 // Logits without bias for the TMA path, z0[s][c] = sum_k h[s, k] w2[k, c]
 // (the GEMM epilogue then only computes h, which takes the logits off its
 // critical path: forward GEMM 374 -> 270 us, this pass ~90 us, at 65,536 x
@@ -978,6 +1048,13 @@ struct MlpF32Ws {
   int head_blocks, w2_chunks, w1_splits;
 };
 
+// The four-rows-per-warp logits pass (STADE_LOGITS_ROWS=0 selects the
+// one-row pass).
+bool logits_rows_enabled() {
+  const char* e = std::getenv("STADE_LOGITS_ROWS");
+  return !(e && std::strcmp(e, "0") == 0);
+}
+
 // Contraction path of the Float32 adjoint: TMA-fed tcgen05 (default) or
 // CUDA-core SIMT (sizes TMA cannot describe; STADE_MLP_GEMM=simt forces it).
 enum class MlpPath { Tma, Simt };
@@ -1105,7 +1182,13 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
       PhaseScope ph("head", s);
       const int blocks = (S + 255) / 256;
       auto kern = O <= 16 ? mlp_head_small_kernel<float, 16> : mlp_head_small_kernel<float, 32>;
-      if (own_logits) {
+      if (own_logits && O <= 16 && H % 128 == 0 && logits_rows_enabled()) {
+        if (lsm > 48 * 1024)
+          STADE_CUDA(cudaFuncSetAttribute(mlp_logits_rows_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm));
+        mlp_logits_rows_kernel<<<2 * tc5::sm_count(), 256, lsm, s>>>(h, w2, w.zpart, S, H, O);
+        STADE_CHECK_LAUNCH();
+      } else if (own_logits) {
         auto lk = O <= 16 ? mlp_logits_kernel<16> : mlp_logits_kernel<32>;
         if (lsm > 48 * 1024)
           STADE_CUDA(cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize,

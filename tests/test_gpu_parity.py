@@ -256,6 +256,20 @@ def test_mlp2_ce_b_tensor_core_path(sizes, seeded, path, monkeypatch):
         assert np.all(out[k] == 0.0), k
 
 
+@pytest.mark.parametrize("rows", ["1", "0"])
+@pytest.mark.parametrize("sizes", [(1001, 784, 512, 10), (77, 64, 128, 3), (130, 32, 256, 16)])
+def test_mlp2_ce_b_logits_passes(sizes, rows, monkeypatch):
+    """The logits pass with four sample rows per warp (default; n_o <= 16,
+    n_h a multiple of 128, a ragged last group of rows included) and the
+    one-row pass, each against the oracle."""
+    monkeypatch.setenv("STADE_LOGITS_ROWS", rows)
+    ref, out, truth, ints = _run_f32(lambda: cases.mlp_state(*sizes, seeded=True),
+                                     cases.oracle_mlp, cases.gpu_mlp)
+    for k in ("z", "p", "yb", "w2b", "b2b", "hb", "loss", "w1b", "xb"):
+        ok, errs = f32_verdict(out[k], ref[k], truth[k])
+        assert ok, (k, errs)
+
+
 def test_mlp2_ce_b_large_batch_vs_truth():
     """4096 samples at the full widths: every output within 1e-5 of the exact
     result (the sweep in Float64) or at least as close as the Float32 oracle."""
