@@ -28,6 +28,8 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
+#include <vector>
 
 #include "tc_tma.cuh"
 #include "tcgen05.cuh"
@@ -132,10 +134,11 @@ __device__ __forceinline__ void epi_part_chunk(const EpiPartial& e, int m, int n
   }
 }
 
-// The fused epilogue of one tile, from the thread's register sums of its 64
-// columns (16-wide groups half, half + 2, half + 4, half + 6) of row m.
-template <int EPI_KIND, int NO>
-__device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m, int n0, int half,
+// The fused epilogue of one tile TN columns wide, from the thread's register
+// sums of its TN / 2 columns (16-wide groups half, half + 2, half + 4, ...) of
+// row m.
+template <int EPI_KIND, int NO, int TN>
+__device__ __forceinline__ void epi_tile(const float (&sum)[TN / 32][16], int m, int n0, int half,
                                          int slice, const EpiTanhLogits& el,
                                          const EpiAccumulate& ea, const EpiPartial& ep,
                                          const float* w2s) {
@@ -144,7 +147,7 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m,
 #pragma unroll
     for (int c = 0; c < NO; ++c) zp[c] = 0.f;
 #pragma unroll
-    for (int q = 0; q < BN / 32; ++q) {
+    for (int q = 0; q < TN / 32; ++q) {
       const int nn = n0 + (half + 2 * q) * 16;
       if (m < el.M) {
         float* o = el.h + (int64_t)m * el.ld + nn;
@@ -164,7 +167,8 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m,
         }
         // logits partial (when asked for); w2 rows are the same for the whole
         // warp (broadcast)
-        if (el.zpart == nullptr) {
+        // logits partials only from 128-wide tiles (the host never asks wider ones)
+        if (TN != BN || el.zpart == nullptr) {
         } else if (el.w2_stride > 0) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -195,8 +199,8 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m,
         }
       }
     }
-    if (m < el.M && el.zpart != nullptr) {
-      const int part = (n0 / BN) * 2 + half;
+    if (TN == BN && m < el.M && el.zpart != nullptr) {
+      const int part = (n0 / TN) * 2 + half;
       float* zr = el.zpart + ((int64_t)part * el.M + m) * el.n_o;
 #pragma unroll
       for (int cc = 0; cc < NO; ++cc)
@@ -204,7 +208,7 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[BN / 32][16], int m,
     }
   } else {
 #pragma unroll
-    for (int q = 0; q < BN / 32; ++q) {
+    for (int q = 0; q < TN / 32; ++q) {
       if constexpr (EPI_KIND == 1) epi_acc_chunk(ea, m, n0 + (half + 2 * q) * 16, sum[q]);
       else epi_part_chunk(ep, m, n0 + (half + 2 * q) * 16, slice, sum[q]);
     }
@@ -426,7 +430,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
         if (lane == 0) mbar_arrive(tempty0 + 8 * b);
       }
       if (!ok) break;
-      epi_tile<EPI_KIND, NO>(sum, m, n0, half, slice, el, ea, ep, w2s);
+      epi_tile<EPI_KIND, NO, BN>(sum, m, n0, half, slice, el, ea, ep, w2s);
     }
   }
 
@@ -443,44 +447,84 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
 
 // ---- CTA pairs ---------------------------------------------------------------------
 // The same contraction with a 2-SM MMA (tcgen05.mma.cta_group::2, M = 256 per
-// pair): the two CTAs of a cluster each load their own 128 rows of A and one
-// half (64 rows or columns) of the tile's B into their shared memory, and the
-// leader CTA's single MMA thread computes the 256 x 128 tile from both; each
-// CTA's TMEM holds its own 128 rows. Per SM and K block that is 48 KB of
-// operand planes instead of 64 KB, so four stages fit. Completion of both
-// CTAs' loads counts on the leader's `full` barrier; the leader's commits
-// arrive on `empty`, `tfull` and `done` in both CTAs; the epilogue warps of
-// both CTAs arrive on the leader's `tempty`. Every wait is bounded.
-constexpr int kPairStages = 4;
-constexpr int kPairBPlane = (BN / 2) * BK * 4;               // 8 KB: half of a B plane
-constexpr int kPairStageBytes = 2 * kTileBytes + 2 * kPairBPlane;  // 48 KB
-constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256;
-static_assert((2 * kPairStages + 2 * kAccBufs + 1) * 8 + 4 <= 256, "barrier block must fit");
-static_assert(kPairSmemBytes + kW2SmemBytes <= 232448, "shared memory of a CTA");
+// pair, N = TN): the two CTAs of a cluster each load their own 128 rows of A
+// and one half (TN / 2 rows or columns) of the tile's B into their shared
+// memory, and the leader CTA's single MMA thread computes the 256 x TN tile
+// from both; each CTA's TMEM holds its own 128 rows x TN columns. Per SM and K
+// block a TN = 256 tile moves 64 KB of operand planes for twice the MMA work
+// of a 128 x 128 tile (a TN = 128 pair: 48 KB for the same work). Completion
+// of both CTAs' loads counts on the leader's `full` barrier; the leader's
+// commits arrive on `empty`, `tfull` and `done` in both CTAs; the epilogue
+// warps of both CTAs arrive on the leader's `tempty`. Every wait is bounded.
+template <int TN>
+struct PairTile {
+  static constexpr int kBHalf = TN / 2;                        // B rows (N) per CTA
+  static constexpr int kBPlane = kBHalf * BK * 4;              // 8 KB / 16 KB
+  static constexpr int kStageBytes = 2 * kTileBytes + 2 * kBPlane;  // 48 KB / 64 KB
+  static constexpr int kStages = TN == 128 ? 4 : 3;
+  static constexpr int kAcc = 512 / TN;                        // TMEM accumulators
+  static constexpr int kBars = 2 * kStages + 2 * kAcc + 1;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+  static_assert(kBars * 8 + 4 <= 256, "barrier block must fit in 256 bytes");
+  static_assert(kSmem + kW2SmemBytes <= 232448, "shared memory of a CTA");
+};
 
-template <int EPI_KIND, int NO>
+// Tile of work unit t: slice, first row of the pair's 256-row tile, first
+// column, and the columns the MMAs run (`n_mma`: a ragged last tile runs only
+// as wide as its columns, rounded up to 32 for a K-major B, so each CTA holds
+// 16 or more rows of it, and to 64 for an MN-major B, so each CTA holds whole
+// 32-column swizzle atoms). Full-width tiles come first in the order, the
+// ragged column tiles after them, so that the pairs' strided walk over the
+// units gives every pair nearly the same mix of both.
+struct PairUnit {
+  int slice, m0, n0, n_mma;
+};
+template <int TN>
+__device__ __forceinline__ PairUnit pair_unit(int t, const Geometry& g) {
+  const int tiles_per_slice = g.m_tiles * g.n_tiles;
+  PairUnit u;
+  u.slice = t / tiles_per_slice;
+  const int r = t % tiles_per_slice;
+  const int n_full = g.N / TN;
+  int mt, nt;
+  if (r < g.m_tiles * n_full) {
+    mt = r / n_full;
+    nt = r % n_full;
+  } else {
+    mt = r - g.m_tiles * n_full;
+    nt = n_full;
+  }
+  u.m0 = mt * (2 * BM);
+  u.n0 = nt * TN;
+  u.n_mma = TN;
+  if (g.N - u.n0 < TN)
+    u.n_mma = g.b_mn ? min(TN, (g.N - u.n0 + 63) / 64 * 64) : (g.N - u.n0 + 31) / 32 * 32;
+  return u;
+}
+
+template <int EPI_KIND, int NO, int TN>
 __global__ void __launch_bounds__(kThreads, 1)
 tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
                      const __grid_constant__ CUtensorMap a_lo,
                      const __grid_constant__ CUtensorMap b_hi,
                      const __grid_constant__ CUtensorMap b_lo, Geometry g, EpiTanhLogits el,
                      EpiAccumulate ea, EpiPartial ep) {
-  constexpr int ST = kPairStages;
+  using P = PairTile<TN>;
+  constexpr int ST = P::kStages, NACC = P::kAcc;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
   uint8_t* tiles = smem_raw + pad;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + ST * kPairStageBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 2 * kAccBufs + 1);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + ST * P::kStageBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + P::kBars);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + ST);
   const uint32_t tfull0 = smem_u32(bars + 2 * ST);
-  const uint32_t tempty0 = smem_u32(bars + 2 * ST + kAccBufs);
-  const uint32_t done = smem_u32(bars + 2 * ST + 2 * kAccBufs);
+  const uint32_t tempty0 = smem_u32(bars + 2 * ST + NACC);
+  const uint32_t done = smem_u32(bars + 2 * ST + 2 * NACC);
   const uint32_t rank = tc5::cluster_rank();
   const bool leader = rank == 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_per_slice = g.m_tiles * g.n_tiles;   // m_tiles counts 256-row tiles
-  const int total = tiles_per_slice * g.slices;
+  const int total = g.m_tiles * g.n_tiles * g.slices;   // m_tiles counts 256-row tiles
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
@@ -488,7 +532,7 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    for (int b = 0; b < kAccBufs; ++b) {
+    for (int b = 0; b < NACC; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
       mbar_init(tempty0 + 8 * b, 2 * kEpiWarps);
     }
@@ -507,19 +551,19 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
       int kb_all = 0;
       bool ok = true;
       for (int t = pair; t < total && ok; t += npairs) {
-        const int slice = t / tiles_per_slice, r = t % tiles_per_slice;
-        const int m0 = (r / g.n_tiles) * (2 * BM) + (int)rank * BM;
-        const int nb = (r % g.n_tiles) * BN + (int)rank * (BN / 2);   // this CTA's half of B
-        const int kbeg = slice * g.k_slice;
+        const PairUnit u = pair_unit<TN>(t, g);
+        const int m0 = u.m0 + (int)rank * BM;
+        const int nb = u.n0 + (int)rank * (u.n_mma / 2);   // this CTA's half of B
+        const int kbeg = u.slice * g.k_slice;
         const int kend = min(g.K, kbeg + g.k_slice);
         const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
         for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
           const int s = kb_all % ST;
           const uint32_t ph = (uint32_t)(kb_all / ST) & 1u;
           if (!tc5::mbar_wait_cluster(empty0 + 8 * s, ph ^ 1u, &g_tma_error)) { ok = false; break; }
-          const uint32_t st = smem_u32(tiles + s * kPairStageBytes);
+          const uint32_t st = smem_u32(tiles + s * P::kStageBytes);
           const uint32_t fb = full0 + 8 * s;
-          if (leader) mbar_arrive_tx(fb, 2 * kPairStageBytes);
+          if (leader) mbar_arrive_tx(fb, 2 * P::kStageBytes);
           const int k0 = kbeg + kb * BK;
           if (!g.a_mn) {
             tc5::tma_load_2d_pair(st, &a_hi, k0, m0, fb);
@@ -534,12 +578,12 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
           const uint32_t sb = st + 2 * kTileBytes;
           if (!g.b_mn) {
             tc5::tma_load_2d_pair(sb, &b_hi, k0, nb, fb);
-            tc5::tma_load_2d_pair(sb + kPairBPlane, &b_lo, k0, nb, fb);
+            tc5::tma_load_2d_pair(sb + P::kBPlane, &b_lo, k0, nb, fb);
           } else {
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
+            for (int q = 0; q < P::kBHalf / 32; ++q) {
               tc5::tma_load_2d_pair(sb + q * 4096, &b_hi, nb + 32 * q, k0, fb);
-              tc5::tma_load_2d_pair(sb + kPairBPlane + q * 4096, &b_lo, nb + 32 * q, k0, fb);
+              tc5::tma_load_2d_pair(sb + P::kBPlane + q * 4096, &b_lo, nb + 32 * q, k0, fb);
             }
           }
         }
@@ -560,7 +604,6 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---- MMA issuer (leader CTA) ------------------------------------------------------
-      const uint32_t idesc = idesc_tf32(2 * BM, BN, g.a_mn, g.b_mn);
       const uint32_t a_lbo = g.a_mn ? 4096u : 16u, a_sbo = g.a_mn ? 512u : 1024u;
       const uint32_t b_lbo = g.b_mn ? 4096u : 16u, b_sbo = g.b_mn ? 512u : 1024u;
       const uint32_t a_lay = g.a_mn ? 1u : 2u, b_lay = g.b_mn ? 1u : 2u;
@@ -568,15 +611,16 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
       int kb_all = 0, chain = 0;
       bool ok = true;
       for (int t = pair; t < total && ok; t += npairs) {
-        const int slice = t / tiles_per_slice;
-        const int kbeg = slice * g.k_slice;
+        const PairUnit u = pair_unit<TN>(t, g);
+        const uint32_t idesc = idesc_tf32(2 * BM, u.n_mma, g.a_mn, g.b_mn);
+        const int kbeg = u.slice * g.k_slice;
         const int kend = min(g.K, kbeg + g.k_slice);
         const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
         const int nch = nkb > 0 ? (nkb + g.chain - 1) / g.chain : 1;
         for (int ch = 0; ch < nch && ok; ++ch, ++chain) {
-          const int b = chain % kAccBufs;
-          const uint32_t acc = tmem + (uint32_t)(b * BN);
-          if (!tc5::mbar_wait_cluster(tempty0 + 8 * b, ((uint32_t)(chain / kAccBufs) & 1u) ^ 1u,
+          const int b = chain % NACC;
+          const uint32_t acc = tmem + (uint32_t)(b * TN);
+          if (!tc5::mbar_wait_cluster(tempty0 + 8 * b, ((uint32_t)(chain / NACC) & 1u) ^ 1u,
                                       &g_tma_error)) {
             ok = false;
             break;
@@ -588,14 +632,14 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
             const uint32_t ph = (uint32_t)(kb_all / ST) & 1u;
             if (!tc5::mbar_wait_cluster(full0 + 8 * s, ph, &g_tma_error)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t st = smem_u32(tiles + s * kPairStageBytes);
+            const uint32_t st = smem_u32(tiles + s * P::kStageBytes);
             const uint32_t sb = st + 2 * kTileBytes;
 #pragma unroll
             for (int j = 0; j < BK / 8; ++j) {
               const uint64_t ahi = desc_sw128(st + a_step * j, a_lbo, a_sbo, a_lay);
               const uint64_t alo = desc_sw128(st + kTileBytes + a_step * j, a_lbo, a_sbo, a_lay);
               const uint64_t bhi = desc_sw128(sb + b_step * j, b_lbo, b_sbo, b_lay);
-              const uint64_t blo = desc_sw128(sb + kPairBPlane + b_step * j, b_lbo, b_sbo, b_lay);
+              const uint64_t blo = desc_sw128(sb + P::kBPlane + b_step * j, b_lbo, b_sbo, b_lay);
               tc5::mma_tf32_pair(acc, ahi, blo, idesc, (kb != kb0 || j != 0) ? 1u : 0u);
               tc5::mma_tf32_pair(acc, alo, bhi, idesc, 1u);
               tc5::mma_tf32_pair(acc, ahi, bhi, idesc, 1u);
@@ -628,32 +672,34 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
     int chain = 0;
     bool ok = true;
     for (int t = pair; t < total && ok; t += npairs) {
-      const int slice = t / tiles_per_slice, r = t % tiles_per_slice;
-      const int m0 = (r / g.n_tiles) * (2 * BM) + (int)rank * BM, n0 = (r % g.n_tiles) * BN;
-      const int kbeg = slice * g.k_slice;
+      const PairUnit u = pair_unit<TN>(t, g);
+      const int kbeg = u.slice * g.k_slice;
       const int kend = min(g.K, kbeg + g.k_slice);
       const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
       const int nch = nkb > 0 ? (nkb + g.chain - 1) / g.chain : 1;
-      const int m = m0 + quad * 32 + lane;
-      float sum[BN / 32][16];
+      const int m = u.m0 + (int)rank * BM + quad * 32 + lane;
+      float sum[TN / 32][16];
 #pragma unroll
-      for (int q = 0; q < BN / 32; ++q)
+      for (int q = 0; q < TN / 32; ++q)
 #pragma unroll
         for (int i = 0; i < 16; ++i) sum[q][i] = 0.f;
       for (int ch = 0; ch < nch; ++ch, ++chain) {
-        const int b = chain % kAccBufs;
-        ok = tc5::mbar_wait_cluster(tfull0 + 8 * b, (uint32_t)(chain / kAccBufs) & 1u, &g_tma_error);
+        const int b = chain % NACC;
+        ok = tc5::mbar_wait_cluster(tfull0 + 8 * b, (uint32_t)(chain / NACC) & 1u, &g_tma_error);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
         if (nkb > 0) {
-          const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN);
+          const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * TN);
 #pragma unroll
-          for (int q = 0; q < BN / 32; ++q) {
-            float v[16];
-            tmem_ld16(base + (uint32_t)((half + 2 * q) * 16), v);
+          for (int q = 0; q < TN / 32; ++q) {
+            // columns past the MMAs' width hold nothing of this tile (uniform per warp)
+            if ((half + 2 * q) * 16 < u.n_mma) {
+              float v[16];
+              tmem_ld16(base + (uint32_t)((half + 2 * q) * 16), v);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sum[q][i] += v[i];
+              for (int i = 0; i < 16; ++i) sum[q][i] += v[i];
+            }
           }
         }
         tc_fence_before();
@@ -661,7 +707,7 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
         if (lane == 0) tc5::mbar_arrive_remote(tempty_leader + 8 * b);
       }
       if (!ok) break;
-      epi_tile<EPI_KIND, NO>(sum, m, n0, half, slice, el, ea, ep, w2s);
+      epi_tile<EPI_KIND, NO, TN>(sum, m, u.n0, half, u.slice, el, ea, ep, w2s);
     }
   }
 
@@ -722,33 +768,40 @@ stade_status run(const Operand& A, const Operand& B, Geometry g, const EpiTanhLo
   return STADE_OK;
 }
 
-// The pair kernel for the same contraction: 256-row tiles, each CTA of a
-// 2-CTA cluster loading its rows of A and half of B (K-major B boxes of 64
-// rows). Opt-in (STADE_TMA_PAIR=1): it moves 25 % fewer operand bytes per MMA
-// but measured slower on the B200 than the one-CTA kernel with four TMEM
-// accumulators (C2 forward 0.41 vs 0.39 ms, input gradient 0.34 vs 0.31 ms),
-// so operand bandwidth is not what bounds these GEMMs.
-bool pair_enabled() {
+// Tile choice (STADE_TMA_PAIR): 0 one CTA per 128 x 128 tile; 1 CTA pairs
+// with 256 x 128 tiles for the forward and input-gradient contractions (25 %
+// fewer operand bytes per MMA than one CTA; measured slower than it on the
+// B200: C2 forward 0.41 vs 0.39 ms); 2 CTA pairs with 256 x 256 tiles (half
+// the operand bytes per MMA) for those two; 3 the same and the weight
+// gradient on 256 x 256 pairs too (hidden units as rows, inputs as columns).
+int pair_mode() {
   const char* e = std::getenv("STADE_TMA_PAIR");
-  return e && std::strcmp(e, "1") == 0;
+  if (e && e[0] >= '0' && e[0] <= '3' && e[1] == 0) return e[0] - '0';
+  return 0;
+}
+int pair_width() {
+  const int m = pair_mode();
+  return m == 1 ? 128 : m >= 2 ? 256 : 0;
 }
 
-template <int EPI_KIND, int NO>
+template <int EPI_KIND, int NO, int TN>
 stade_status run_pair(const Operand& A, const Operand& B, Geometry g, const EpiTanhLogits& el,
                       const EpiAccumulate& ea, const EpiPartial& ep, cudaStream_t s) {
+  using P = PairTile<TN>;
   CUtensorMap ah, al, bh, bl;
   stade_status st = operand_maps(A, &ah, &al);
   if (st != STADE_OK) return st;
   if (B.mn) {
     st = operand_maps(B, &bh, &bl);
   } else {
-    st = make_map(&bh, B.hi, B.rows, B.cols, B.ld, 32, BN / 2, false);
-    if (st == STADE_OK) st = make_map(&bl, B.lo, B.rows, B.cols, B.ld, 32, BN / 2, false);
+    st = make_map(&bh, B.hi, B.rows, B.cols, B.ld, 32, P::kBHalf, false);
+    if (st == STADE_OK) st = make_map(&bl, B.lo, B.rows, B.cols, B.ld, 32, P::kBHalf, false);
   }
   if (st != STADE_OK) return st;
   g.m_tiles = (g.M + 2 * BM - 1) / (2 * BM);
-  const int smem = kPairSmemBytes + (EPI_KIND == 0 && el.w2_stride > 0 ? kW2SmemBytes : 0);
-  auto kern = tma_gemm_pair_kernel<EPI_KIND, NO>;
+  g.n_tiles = (g.N + TN - 1) / TN;
+  const int smem = P::kSmem + (EPI_KIND == 0 && el.w2_stride > 0 ? kW2SmemBytes : 0);
+  auto kern = tma_gemm_pair_kernel<EPI_KIND, NO, TN>;
   STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int total = g.m_tiles * g.n_tiles * g.slices;
   const int pairs = total < sm_count() / 2 ? total : sm_count() / 2;
@@ -812,6 +865,44 @@ int w1b_slices(int S, int I, int H) {
   return best;
 }
 
+// Slices of a split-K contraction on 256 x TN CTA-pair tiles, from the same
+// kind of cost model: the pairs walk the (tile, slice) units with a stride of
+// the pair count, a ragged column tile costs its MMA width's share of a full
+// one, and the busiest pair's K blocks (plus a charge of 4 K blocks per
+// partial tile written and read back) is minimised; at least 16 K blocks per
+// slice.
+template <int TN>
+int pair_slices(int M, int N, int K, bool b_mn) {
+  const int m_tiles = (M + 2 * BM - 1) / (2 * BM), n_tiles = (N + TN - 1) / TN;
+  const int n_full = N / TN, tiles = m_tiles * n_tiles;
+  const int kblocks = (K + BK - 1) / BK;
+  const int pairs = tc5::sm_count() / 2;
+  const int rag = N - n_full * TN;
+  const double rag_cost =
+      rag == 0 ? 1.0 : (double)(b_mn ? (rag + 63) / 64 * 64 : (rag + 31) / 32 * 32) / TN;
+  int best = 1;
+  double best_cost = 0.0;
+  std::vector<double> load(pairs > 0 ? pairs : 1);
+  for (int sl = 1; sl <= 128; ++sl) {
+    const int per = (kblocks + sl - 1) / sl;
+    if (sl > 1 && per < 16) break;
+    const int slices = (kblocks + per - 1) / per;
+    std::fill(load.begin(), load.end(), 0.0);
+    for (int t = 0; t < tiles * slices; ++t) {
+      const int slice = t / tiles, r = t % tiles;
+      const int kb = std::min(per, kblocks - slice * per);
+      load[t % load.size()] += kb * (r < m_tiles * n_full ? 1.0 : rag_cost);
+    }
+    const double busiest = *std::max_element(load.begin(), load.end());
+    const double cost = busiest + (slices > 1 ? 4.0 * slices * tiles / load.size() : 0.0);
+    if (sl == 1 || cost < best_cost) {
+      best = sl;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 // hi / lo split of a Float32 array (n % 4 == 0 handled by the vector path),
 // both planes rounded to the nearest TF32 value.
 __global__ void split_kernel(const float* __restrict__ a, float* __restrict__ hi,
@@ -862,6 +953,26 @@ __global__ void w1b_finish_kernel(const float* __restrict__ part, int slices, in
   w1b[e] += acc;
 }
 
+// w1b[i][h] += sum over slices of part[slice][h][i], in slice order: the pair
+// form of the weight gradient has hidden units as rows. 32 x 32 tiles through
+// shared memory, so both the partial reads and the w1b updates are coalesced.
+__global__ void w1b_finish_t_kernel(const float* __restrict__ part, int slices, int H, int I,
+                                    float* __restrict__ w1b) {
+  __shared__ float tile[32][33];
+  const int i0 = blockIdx.x * 32, h0 = blockIdx.y * 32;
+  const int64_t plane = (int64_t)H * I;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int h = h0 + r, i = i0 + threadIdx.x;
+    tile[r][threadIdx.x] =
+        (h < H && i < I) ? ordered_sum(part + (int64_t)h * I + i, slices, plane) : 0.f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int i = i0 + r, h = h0 + threadIdx.x;
+    if (i < I && h < H) w1b[(int64_t)i * H + h] += tile[threadIdx.x][r];
+  }
+}
+
 }  // namespace tma
 
 // ---- entry points used by mlp2_ce -------------------------------------------------------
@@ -887,8 +998,15 @@ stade_status tma_split_lo(const float* a, float* lo, int64_t n, cudaStream_t s) 
   return STADE_OK;
 }
 
+// Slices of the weight gradient in the current tile mode (the pair form runs
+// hidden units as rows, inputs as columns).
+static int w1b_slice_count(int64_t n_s, int64_t n_i, int64_t n_h) {
+  if (tma::pair_mode() == 3) return tma::pair_slices<256>((int)n_h, (int)n_i, (int)n_s, true);
+  return tma::w1b_slices((int)n_s, (int)n_i, (int)n_h);
+}
+
 size_t tma_w1b_part_floats(int64_t n_s, int64_t n_i, int64_t n_h) {
-  return (size_t)tma::w1b_slices((int)n_s, (int)n_i, (int)n_h) * (size_t)n_i * (size_t)n_h;
+  return (size_t)w1b_slice_count(n_s, n_i, n_h) * (size_t)n_i * (size_t)n_h;
 }
 
 stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const float* w1_hi,
@@ -902,9 +1020,16 @@ stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const
   const int stride = (O + 3) / 4 * 4;
   const bool smem_w2 = zpart != nullptr && (int64_t)H * stride * 4 <= tma::kW2SmemBytes;
   tma::EpiTanhLogits el{h, b1, w2, zpart, H, S, H, O, 2, smem_w2 ? stride : 0};
-  if (tma::pair_enabled()) {
-    if (O <= 16) return tma::run_pair<0, 16>(A, B, g, el, {}, {}, s);
-    return tma::run_pair<0, 32>(A, B, g, el, {}, {}, s);
+  const int pw = tma::pair_width();
+  // 256-wide tiles give each thread's logits partial a different column set:
+  // they run only where the logits come from a pass of their own
+  if (pw == 256 && zpart == nullptr) {
+    if (O <= 16) return tma::run_pair<0, 16, 256>(A, B, g, el, {}, {}, s);
+    return tma::run_pair<0, 32, 256>(A, B, g, el, {}, {}, s);
+  }
+  if (pw != 0) {
+    if (O <= 16) return tma::run_pair<0, 16, 128>(A, B, g, el, {}, {}, s);
+    return tma::run_pair<0, 32, 128>(A, B, g, el, {}, {}, s);
   }
   if (O <= 16) return tma::run<0, 16>(A, B, g, el, {}, {}, s);
   return tma::run<0, 32>(A, B, g, el, {}, {}, s);
@@ -913,6 +1038,20 @@ stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const
 stade_status tma_weight_grad(const float* x_hi, const float* x_lo, const float* s1b_hi,
                              const float* s1b_lo, float* w1b, float* part, int S, int I, int H,
                              cudaStream_t s) {
+  if (tma::pair_mode() == 3) {
+    // A[m = hidden, k = sample] = s1b[k, m]: MN-major. B[n = input, k = sample] = x[k, n]:
+    // MN-major. part[slice][hidden][input], summed and transposed into w1b.
+    tma::Operand A{s1b_hi, s1b_lo, S, H, H, true};
+    tma::Operand B{x_hi, x_lo, S, I, I, true};
+    tma::Geometry g = tma::geometry(H, I, S, w1b_slice_count(S, I, H), true, true);
+    tma::EpiPartial ep{part, H, I};
+    stade_status st = tma::run_pair<2, 1, 256>(A, B, g, {}, {}, ep, s);
+    if (st != STADE_OK) return st;
+    tma::w1b_finish_t_kernel<<<dim3(ceil_div_u(I, 32), ceil_div_u(H, 32)), dim3(32, 8), 0, s>>>(
+        part, g.slices, H, I, w1b);
+    STADE_CHECK_LAUNCH();
+    return STADE_OK;
+  }
   // A[m = input, k = sample] = x[k, m]: MN-major. B[n = hidden, k = sample] = s1b[k, n]: MN-major.
   tma::Operand A{x_hi, x_lo, S, I, I, true};
   tma::Operand B{s1b_hi, s1b_lo, S, H, H, true};
@@ -933,7 +1072,9 @@ stade_status tma_input_grad(const float* s1b_hi, const float* s1b_lo, const floa
   tma::Operand B{w1_hi, w1_lo, I, H, H, false};
   tma::Geometry g = tma::geometry(S, I, H, 1, false, false);
   tma::EpiAccumulate ea{xb, I, S, I};
-  if (tma::pair_enabled()) return tma::run_pair<1, 1>(A, B, g, {}, ea, {}, s);
+  const int pw = tma::pair_width();
+  if (pw == 256) return tma::run_pair<1, 1, 256>(A, B, g, {}, ea, {}, s);
+  if (pw == 128) return tma::run_pair<1, 1, 128>(A, B, g, {}, ea, {}, s);
   return tma::run<1, 1>(A, B, g, {}, ea, {}, s);
 }
 

@@ -232,20 +232,22 @@ def test_mlp2_ce_hv(sizes, seeded, xd, f64_gemm, monkeypatch):
         assert np.all(out[k] == 0.0), k
 
 
-@pytest.mark.parametrize("path", ["tma", "tma2"])
+@pytest.mark.parametrize("path", ["tma", "tma2", "tma3", "tma4"])
 @pytest.mark.parametrize("sizes,seeded", [((256, 784, 512, 10), False),
                                           ((300, 132, 200, 10), True),
                                           ((1000, 784, 512, 10), True),
                                           ((129, 4, 8, 3), True),
                                           ((2000, 68, 260, 10), True)])
 def test_mlp2_ce_b_tensor_core_path(sizes, seeded, path, monkeypatch):
-    """The TMA-fed tcgen05 3xTF32 contractions (default: one CTA per tile;
-    tma2: CTA pairs with the 2-SM MMA for the forward and input-gradient
-    GEMMs), against the oracle (M, N and K tails included), and no bounded
-    wait ran out."""
+    """The TMA-fed tcgen05 3xTF32 contractions (tma: one CTA per 128 x 128
+    tile; tma2 / tma3: CTA pairs with the 2-SM MMA and 256 x 128 / 256 x 256
+    tiles for the forward and input-gradient GEMMs, ragged last column tiles
+    with narrower MMAs; tma4: the weight gradient on 256 x 256 pairs too,
+    split over samples and transposed in its finish pass), against the oracle
+    (M, N and K tails included), and no bounded wait ran out."""
     from stadeb200 import _lib
     monkeypatch.setenv("STADE_MLP_GEMM", "tma")
-    monkeypatch.setenv("STADE_TMA_PAIR", "1" if path == "tma2" else "0")
+    monkeypatch.setenv("STADE_TMA_PAIR", {"tma": "0", "tma2": "1", "tma3": "2", "tma4": "3"}[path])
     ref, out, truth, ints = _run_f32(lambda: cases.mlp_state(*sizes, seeded=seeded),
                                      cases.oracle_mlp, cases.gpu_mlp)
     assert _lib.lib().stade_device_error() == 0
