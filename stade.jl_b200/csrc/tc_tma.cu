@@ -10,6 +10,12 @@
 // hi*hi + hi*lo + lo*hi (lo*lo is below Float32 rounding), three
 // tcgen05.mma.kind::tf32 per K step into one TMEM accumulator.
 //
+// Two kernels share this scheme: tma_gemm_pair_kernel (the default for C2's
+// three GEMMs) runs 256 x 256 tiles on CTA pairs with the 2-SM MMA and writes
+// its output with TMA stores / reductions; tma_gemm_kernel runs one
+// 128 x 128 tile per CTA and stores from registers (where a pair tile does not
+// apply: logits partials in the forward epilogue, outputs not 16-byte aligned,
+// or STADE_TMA_PAIR=0). The one-CTA form:
 // Persistent kernel, one CTA per SM, warp-specialised:
 //   warp 0  one thread issues TMA loads (cp.async.bulk.tensor, each copy into its own CTA)
 //           of the four 128 x 32 operand tiles of a K block into a 3-stage
@@ -79,7 +85,7 @@ __device__ __forceinline__ void tc_fence_before() { tc5::fence_before(); }
 __device__ __forceinline__ void tc_fence_after() { tc5::fence_after(); }
 
 // ---- epilogues: a thread owns one accumulator row and gets 16 columns at a time
-__device__ __forceinline__ bool aligned16(const void* p) {
+__host__ __device__ __forceinline__ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
@@ -134,11 +140,12 @@ __device__ __forceinline__ void epi_part_chunk(const EpiPartial& e, int m, int n
   }
 }
 
-// The fused epilogue of one tile TN columns wide, from the thread's register
-// sums of its TN / 2 columns (16-wide groups half, half + 2, half + 4, ...) of
-// row m.
-template <int EPI_KIND, int NO, int TN>
-__device__ __forceinline__ void epi_tile(const float (&sum)[TN / 32][16], int m, int n0, int half,
+// The fused epilogue of one tile, from the thread's register sums of its 64
+// columns of row m: 16-wide groups g0, g0 + GS, g0 + 2 GS, g0 + 3 GS (GS = 2:
+// two column halves of a 128-wide tile; GS = 4: four column quarters of a
+// 256-wide one).
+template <int EPI_KIND, int NO, int GS>
+__device__ __forceinline__ void epi_tile(const float (&sum)[4][16], int m, int n0, int g0,
                                          int slice, const EpiTanhLogits& el,
                                          const EpiAccumulate& ea, const EpiPartial& ep,
                                          const float* w2s) {
@@ -147,8 +154,8 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[TN / 32][16], int m,
 #pragma unroll
     for (int c = 0; c < NO; ++c) zp[c] = 0.f;
 #pragma unroll
-    for (int q = 0; q < TN / 32; ++q) {
-      const int nn = n0 + (half + 2 * q) * 16;
+    for (int q = 0; q < 4; ++q) {
+      const int nn = n0 + (g0 + GS * q) * 16;
       if (m < el.M) {
         float* o = el.h + (int64_t)m * el.ld + nn;
         float hv[16];
@@ -168,7 +175,7 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[TN / 32][16], int m,
         // logits partial (when asked for); w2 rows are the same for the whole
         // warp (broadcast)
         // logits partials only from 128-wide tiles (the host never asks wider ones)
-        if (TN != BN || el.zpart == nullptr) {
+        if (GS != 2 || el.zpart == nullptr) {
         } else if (el.w2_stride > 0) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -199,8 +206,8 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[TN / 32][16], int m,
         }
       }
     }
-    if (TN == BN && m < el.M && el.zpart != nullptr) {
-      const int part = (n0 / TN) * 2 + half;
+    if (GS == 2 && m < el.M && el.zpart != nullptr) {
+      const int part = (n0 / BN) * 2 + g0;
       float* zr = el.zpart + ((int64_t)part * el.M + m) * el.n_o;
 #pragma unroll
       for (int cc = 0; cc < NO; ++cc)
@@ -208,9 +215,9 @@ __device__ __forceinline__ void epi_tile(const float (&sum)[TN / 32][16], int m,
     }
   } else {
 #pragma unroll
-    for (int q = 0; q < TN / 32; ++q) {
-      if constexpr (EPI_KIND == 1) epi_acc_chunk(ea, m, n0 + (half + 2 * q) * 16, sum[q]);
-      else epi_part_chunk(ep, m, n0 + (half + 2 * q) * 16, slice, sum[q]);
+    for (int q = 0; q < 4; ++q) {
+      if constexpr (EPI_KIND == 1) epi_acc_chunk(ea, m, n0 + (g0 + GS * q) * 16, sum[q]);
+      else epi_part_chunk(ep, m, n0 + (g0 + GS * q) * 16, slice, sum[q]);
     }
   }
 
@@ -430,7 +437,7 @@ tma_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant_
         if (lane == 0) mbar_arrive(tempty0 + 8 * b);
       }
       if (!ok) break;
-      epi_tile<EPI_KIND, NO, BN>(sum, m, n0, half, slice, el, ea, ep, w2s);
+      epi_tile<EPI_KIND, NO, 2>(sum, m, n0, half, slice, el, ea, ep, w2s);
     }
   }
 
@@ -463,10 +470,18 @@ struct PairTile {
   static constexpr int kStageBytes = 2 * kTileBytes + 2 * kBPlane;  // 48 KB / 64 KB
   static constexpr int kStages = TN == 128 ? 4 : 3;
   static constexpr int kAcc = 512 / TN;                        // TMEM accumulators
+  // epilogue warps: four per TMEM lane quarter, each thread 64 columns of its row
+  static constexpr int kEpiW = TN / 16;                        // 8 / 16
+  static constexpr int kThreads = (2 + kEpiW) * 32;            // 320 / 576
+  // 256-wide tiles write their output with TMA stores from a 2 KB block per
+  // epilogue warp (after the barrier block, where 128-wide ones may stage W2)
+  static constexpr bool kTmaOut = TN == 256;
+  static constexpr int kStageOutBytes = kTmaOut ? kEpiW * 2048 : 0;
   static constexpr int kBars = 2 * kStages + 2 * kAcc + 1;
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
   static_assert(kBars * 8 + 4 <= 256, "barrier block must fit in 256 bytes");
   static_assert(kSmem + kW2SmemBytes <= 232448, "shared memory of a CTA");
+  static_assert(kSmem + kStageOutBytes <= 232448, "shared memory of a CTA");
 };
 
 // Tile of work unit t: slice, first row of the pair's 256-row tile, first
@@ -503,11 +518,12 @@ __device__ __forceinline__ PairUnit pair_unit(int t, const Geometry& g) {
 }
 
 template <int EPI_KIND, int NO, int TN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(PairTile<TN>::kThreads, 1)
 tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
                      const __grid_constant__ CUtensorMap a_lo,
                      const __grid_constant__ CUtensorMap b_hi,
-                     const __grid_constant__ CUtensorMap b_lo, Geometry g, EpiTanhLogits el,
+                     const __grid_constant__ CUtensorMap b_lo,
+                     const __grid_constant__ CUtensorMap out, Geometry g, EpiTanhLogits el,
                      EpiAccumulate ea, EpiPartial ep) {
   using P = PairTile<TN>;
   constexpr int ST = P::kStages, NACC = P::kAcc;
@@ -534,7 +550,7 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
     }
     for (int b = 0; b < NACC; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 2 * kEpiWarps);
+      mbar_init(tempty0 + 8 * b, 2 * P::kEpiW);
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -656,19 +672,22 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
   } else {
     // ---- epilogue warps (both CTAs) -----------------------------------------------------
     const int e = warp - 2;
-    const int quad = warp & 3;
-    const int half = e >> 2;
+    const int quad = warp & 3;       // TMEM lanes 32 quad .. 32 quad + 31
+    const int cg = e >> 2;           // column group: 16-wide groups cg + (kEpiW / 4) q
     float* w2s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
     if constexpr (EPI_KIND == 0) {
       if (el.w2_stride > 0) {
-        for (int i = threadIdx.x - 64; i < el.N * el.w2_stride; i += kEpiWarps * 32) {
+        for (int i = threadIdx.x - 64; i < el.N * el.w2_stride; i += P::kEpiW * 32) {
           const int kk = i / el.w2_stride, c = i % el.w2_stride;
           w2s[i] = c < el.n_o ? el.w2[(int64_t)kk * el.n_o + c] : 0.f;
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"r"(P::kEpiW * 32) : "memory");
       }
     }
     const uint32_t tempty_leader = tc5::mapa(tempty0, 0);
+    // the warp's 2 KB staging block for TMA stores (32 rows x 16 Float32)
+    float* stage = w2s + e * 512;
+    const uint32_t stage_s = smem_u32(stage);
     int chain = 0;
     bool ok = true;
     for (int t = pair; t < total && ok; t += npairs) {
@@ -678,9 +697,10 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
       const int nkb = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
       const int nch = nkb > 0 ? (nkb + g.chain - 1) / g.chain : 1;
       const int m = u.m0 + (int)rank * BM + quad * 32 + lane;
-      float sum[TN / 32][16];
+      constexpr int GS = P::kEpiW / 4;
+      float sum[4][16];
 #pragma unroll
-      for (int q = 0; q < TN / 32; ++q)
+      for (int q = 0; q < 4; ++q)
 #pragma unroll
         for (int i = 0; i < 16; ++i) sum[q][i] = 0.f;
       for (int ch = 0; ch < nch; ++ch, ++chain) {
@@ -692,11 +712,11 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
         if (nkb > 0) {
           const uint32_t base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * TN);
 #pragma unroll
-          for (int q = 0; q < TN / 32; ++q) {
+          for (int q = 0; q < 4; ++q) {
             // columns past the MMAs' width hold nothing of this tile (uniform per warp)
-            if ((half + 2 * q) * 16 < u.n_mma) {
+            if ((cg + GS * q) * 16 < u.n_mma) {
               float v[16];
-              tmem_ld16(base + (uint32_t)((half + 2 * q) * 16), v);
+              tmem_ld16(base + (uint32_t)((cg + GS * q) * 16), v);
 #pragma unroll
               for (int i = 0; i < 16; ++i) sum[q][i] += v[i];
             }
@@ -707,7 +727,47 @@ tma_gemm_pair_kernel(const __grid_constant__ CUtensorMap a_hi,
         if (lane == 0) tc5::mbar_arrive_remote(tempty_leader + 8 * b);
       }
       if (!ok) break;
-      epi_tile<EPI_KIND, NO, TN>(sum, m, u.n0, half, u.slice, el, ea, ep, w2s);
+      if constexpr (P::kTmaOut) {
+        // the warp's 32 rows x 16 columns at a time through its shared-memory
+        // block, written (h, W1b slices) or added (xb) by one TMA operation
+        const int row0 = u.m0 + (int)rank * BM + quad * 32;
+        const int M = EPI_KIND == 0 ? el.M : EPI_KIND == 1 ? ea.M : ep.M;
+        const int N = EPI_KIND == 0 ? el.N : EPI_KIND == 1 ? ea.N : ep.N;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int nn = u.n0 + (cg + GS * q) * 16;
+          if (nn >= N || row0 >= M) continue;   // nothing of the box is inside (uniform)
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if constexpr (EPI_KIND == 0)
+              v[i] = (nn + i < N) ? tanhf(sum[q][i] + __ldg(el.b1 + nn + i)) : 0.f;
+            else
+              v[i] = sum[q][i];
+          }
+          // the block's previous store has been read out of shared memory
+          if (lane == 0) tc5::bulk_wait_read();
+          __syncwarp();
+          float4* row = reinterpret_cast<float4*>(stage + lane * 16);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            row[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          tc5::fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (EPI_KIND == 0) tc5::tma_store_2d(&out, stage_s, nn, row0);
+            else if constexpr (EPI_KIND == 1) tc5::tma_reduce_add_2d(&out, stage_s, nn, row0);
+            else tc5::tma_store_3d(&out, stage_s, nn, row0, u.slice);
+            tc5::bulk_commit();
+          }
+        }
+      } else {
+        epi_tile<EPI_KIND, NO, GS>(sum, m, u.n0, cg, u.slice, el, ea, ep, w2s);
+      }
+    }
+    if constexpr (P::kTmaOut) {
+      if (lane == 0) tc5::bulk_wait();   // every store of this warp has landed
+      __syncwarp();
     }
   }
 
@@ -769,15 +829,22 @@ stade_status run(const Operand& A, const Operand& B, Geometry g, const EpiTanhLo
 }
 
 // Tile choice (STADE_TMA_PAIR): 0 one CTA per 128 x 128 tile; 1 CTA pairs
-// with 256 x 128 tiles for the forward and input-gradient contractions (25 %
-// fewer operand bytes per MMA than one CTA; measured slower than it on the
-// B200: C2 forward 0.41 vs 0.39 ms); 2 CTA pairs with 256 x 256 tiles (half
-// the operand bytes per MMA) for those two; 3 the same and the weight
-// gradient on 256 x 256 pairs too (hidden units as rows, inputs as columns).
+// with 256 x 128 tiles for the forward and input-gradient contractions; 2 CTA
+// pairs with 256 x 256 tiles for those two; 3 (the default) the same and the
+// weight gradient on 256 x 256 pairs too (hidden units as rows, inputs as
+// columns).
+// Why pairs of 256 x 256: one CTA's 128 x 128 tile reads 96 KB of operands
+// out of shared memory per K block for its 12 MMAs while TMA writes 64 KB in,
+// ~1250 cycles of shared-memory traffic against 768 cycles of TF32 MMA, so
+// the tensor pipe idles ~40 % (measured 51-65 % busy). A 2-SM 256 x 256 tile
+// has each SM read 144 KB and take 64 KB in per 1536 MMA cycles (~94 %).
+// Measured, C2 at 65,536 samples (ms, one CTA per tile -> pairs): forward
+// 0.273 -> 0.210, weight gradient 0.281 -> 0.249, input gradient 0.301 ->
+// 0.246.
 int pair_mode() {
   const char* e = std::getenv("STADE_TMA_PAIR");
   if (e && e[0] >= '0' && e[0] <= '3' && e[1] == 0) return e[0] - '0';
-  return 0;
+  return 3;
 }
 int pair_width() {
   const int m = pair_mode();
@@ -800,14 +867,32 @@ stade_status run_pair(const Operand& A, const Operand& B, Geometry g, const EpiT
   if (st != STADE_OK) return st;
   g.m_tiles = (g.M + 2 * BM - 1) / (2 * BM);
   g.n_tiles = (g.N + TN - 1) / TN;
-  const int smem = P::kSmem + (EPI_KIND == 0 && el.w2_stride > 0 ? kW2SmemBytes : 0);
+  // the output as TMA stores see it: boxes of 16 columns x 32 rows (x 1 slice)
+  CUtensorMap om = ah;   // unused by 128-wide tiles
+  if constexpr (P::kTmaOut) {
+    const uint32_t box[3] = {16, 32, 1};
+    if constexpr (EPI_KIND == 0) {
+      const int64_t d[2] = {el.N, el.M}, pitch[1] = {el.ld};
+      st = tc5::make_out_map_f32(&om, el.h, 2, d, pitch, box);
+    } else if constexpr (EPI_KIND == 1) {
+      const int64_t d[2] = {ea.N, ea.M}, pitch[1] = {ea.ld};
+      st = tc5::make_out_map_f32(&om, ea.out, 2, d, pitch, box);
+    } else {
+      const int64_t d[3] = {ep.N, ep.M, g.slices};
+      const int64_t pitch[2] = {ep.N, (int64_t)ep.M * ep.N};
+      st = tc5::make_out_map_f32(&om, ep.part, 3, d, pitch, box);
+    }
+    if (st != STADE_OK) return st;
+  }
+  const int smem = P::kSmem + P::kStageOutBytes +
+                   (EPI_KIND == 0 && el.w2_stride > 0 ? kW2SmemBytes : 0);
   auto kern = tma_gemm_pair_kernel<EPI_KIND, NO, TN>;
   STADE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int total = g.m_tiles * g.n_tiles * g.slices;
   const int pairs = total < sm_count() / 2 ? total : sm_count() / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(P::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -817,7 +902,7 @@ stade_status run_pair(const Operand& A, const Operand& B, Geometry g, const EpiT
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  STADE_CUDA(cudaLaunchKernelEx(&cfg, kern, ah, al, bh, bl, g, el, ea, ep));
+  STADE_CUDA(cudaLaunchKernelEx(&cfg, kern, ah, al, bh, bl, om, g, el, ea, ep));
   count_launch();
   return STADE_OK;
 }
@@ -1022,8 +1107,9 @@ stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const
   tma::EpiTanhLogits el{h, b1, w2, zpart, H, S, H, O, 2, smem_w2 ? stride : 0};
   const int pw = tma::pair_width();
   // 256-wide tiles give each thread's logits partial a different column set:
-  // they run only where the logits come from a pass of their own
-  if (pw == 256 && zpart == nullptr) {
+  // they run only where the logits come from a pass of their own (and store
+  // h with TMA, which needs it 16-byte aligned)
+  if (pw == 256 && zpart == nullptr && tma::aligned16(h)) {
     if (O <= 16) return tma::run_pair<0, 16, 256>(A, B, g, el, {}, {}, s);
     return tma::run_pair<0, 32, 256>(A, B, g, el, {}, {}, s);
   }
@@ -1073,7 +1159,8 @@ stade_status tma_input_grad(const float* s1b_hi, const float* s1b_lo, const floa
   tma::Geometry g = tma::geometry(S, I, H, 1, false, false);
   tma::EpiAccumulate ea{xb, I, S, I};
   const int pw = tma::pair_width();
-  if (pw == 256) return tma::run_pair<1, 1, 256>(A, B, g, {}, ea, {}, s);
+  // 256-wide tiles add into xb with TMA reductions: xb 16-byte aligned
+  if (pw == 256 && tma::aligned16(xb)) return tma::run_pair<1, 1, 256>(A, B, g, {}, ea, {}, s);
   if (pw == 128) return tma::run_pair<1, 1, 128>(A, B, g, {}, ea, {}, s);
   return tma::run<1, 1>(A, B, g, {}, ea, {}, s);
 }
