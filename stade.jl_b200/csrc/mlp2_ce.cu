@@ -1327,7 +1327,6 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   MlpF64HvWs w;
   mlp_hv_layout(ca, &w, n_s, n_i, n_h, n_o);
   const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
-  constexpr int RM = kF64RM, RN = kF64RN, BK = kF64BK;
 
   // forward: S1 = x W1; s1d = x W1d + xd W1, h, hd
   {
