@@ -26,9 +26,6 @@
 // Float32 accumulation error grows with chain length) and run the epilogue.
 // Every wait is bounded; on timeout the kernel sets g_conv_error, stops,
 // waits (bounded) for its own copies and MMAs, frees TMEM and returns.
-#include <cstdlib>
-#include <cstring>
-
 #include "conv_tc.cuh"
 #include "tcgen05.cuh"
 
@@ -63,27 +60,7 @@ struct FwdOut {  // the forward epilogue's arrays
   float *z, *r, *zb, *rb, *tb, *g_hi, *g_lo, *loss_part;
   const float *t, *lossb;
   float inv_n;
-  int prefetch;   // 1: the epilogue's input rows of a tile go to L2 when the tile starts
 };
-
-// The epilogue's input rows of a tile into L2 while its MMAs run: for each of
-// `n_arr` arrays laid out [b][col][row] (row innermost, `rows_total` per
-// column), columns col0 .. col0 + n_cols - 1 (< cols_total), rows m0 .. m0 + 127.
-// One bulk prefetch per (array, column); skipped where the range is not
-// 16-byte aligned.
-__device__ __forceinline__ void prefetch_tile_rows(const float* const* arr, int n_arr, int b,
-                                                   int col0, int n_cols, int cols_total,
-                                                   int m0, int rows_total, int et, int nthreads) {
-  const int rows = min(128, rows_total - m0);
-  const uint32_t bytes = (uint32_t)(rows * 4) & ~15u;
-  if (rows <= 0 || bytes == 0) return;
-  for (int i = et; i < n_arr * n_cols; i += nthreads) {
-    const int a = i / n_cols, col = col0 + i % n_cols;
-    if (col >= cols_total) continue;
-    const float* p = arr[a] + ((int64_t)b * cols_total + col) * rows_total + m0;
-    if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) tc5::prefetch_l2(p, bytes);
-  }
-}
 
 template <int MODE>
 struct Cfg;
@@ -283,17 +260,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const Tile tl = decode<MODE>(g, t);
       const int nch = tl.nkb > 0 ? (tl.nkb + g.chain - 1) / g.chain : 1;
-      if (fo.prefetch) {
-        if (MODE == 0) {
-          const float* arr[4] = {fo.t, fo.rb, fo.zb, fo.tb};
-          prefetch_tile_rows(arr, 4, tl.b, tl.n0, BN, g.O, tl.m0, g.Lo, threadIdx.x - 64,
-                             kEpiWarps * 32);
-        } else if (MODE == 2) {
-          const float* arr[1] = {xb};
-          prefetch_tile_rows(arr, 1, tl.b, tl.n0, BN, g.C, tl.m0, g.L, threadIdx.x - 64,
-                             kEpiWarps * 32);
-        }
-      }
       float sum[BN / 32][16];
 #pragma unroll
       for (int q = 0; q < BN / 32; ++q)
@@ -641,10 +607,8 @@ stade_status conv_tc_run(const ConvShape& sh, float* loss, const float* lossb, c
     mk(&gm_lo, W.g_lo, dg, pg, mbox, true);
     if (st != STADE_OK) return st;
   }
-  // STADE_CONV_PREFETCH=0 leaves the epilogue's inputs to its own loads
-  const char* pf = std::getenv("STADE_CONV_PREFETCH");
   FwdOut fo{z, r, zb, rb, tb, W.g_hi, W.g_lo, W.loss_part, t, lossb,
-            1.0f / (float)(B * O * Lo), (pf && std::strcmp(pf, "0") == 0) ? 0 : 1};
+            1.0f / (float)(B * O * Lo)};
   stade_status st;
   {
     PhaseScope ph("conv_fwd", s);

@@ -1,14 +1,14 @@
-// Float64 GEMM on the FP64 tensor cores (DMMA, mma.sync m8n8k4 .f64 — the
-// only f64 tensor-core instruction: tcgen05 has no f64 kind), with the same
-// functor operand loaders, functor epilogues and deterministic split-K as
-// gemm_simt: C[m, n] = sum_k A(m, k) B(k, n).
+// Float64 GEMM on the FP64 tensor cores (DMMA: mma.sync .f64 — tcgen05 has no
+// f64 kind), with the same functor operand loaders, functor epilogues and
+// deterministic split-K as gemm_simt: C[m, n] = sum_k A(m, k) B(k, n).
 //
 // Block tile 128 x 128, K staged 16 at a time through double-buffered
 // shared memory (operands pass through registers, so any loader works);
-// 8 warps in a 2 x 4 grid, each warp owns a 64 x 32 tile = 8 x 4 DMMA tiles
-// (64 accumulators per thread). Fragment reads from shared memory are
-// conflict-free with rows padded to 132 doubles. A split-K slice writes its
-// own partial tile; gemm_splitk_finish_kernel sums the slices in order.
+// 8 warps in a 2 x 4 grid, each warp owns a 64 x 32 tile = 4 x 4 tiles of
+// mma.sync.m16n8k8.f64 (64 accumulators per thread; one instruction is 1024
+// multiply-adds, eight times an m8n8k4's). Fragment reads from shared memory
+// are conflict-free with rows padded to 132 doubles. A split-K slice writes
+// its own partial tile; gemm_splitk_finish_kernel sums the slices in order.
 #pragma once
 
 #include "gemm_simt.cuh"
@@ -21,10 +21,16 @@ constexpr int LDA = BM + 4, LDB = BN + 4;
 constexpr int A_PER = BM * BK / 256, B_PER = BN * BK / 256;
 constexpr size_t kSmemBytes = sizeof(double) * 2 * BK * (LDA + LDB);
 
-__device__ __forceinline__ void mma_m8n8k4(double& d0, double& d1, double a, double b) {
-  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
-               : "+d"(d0), "+d"(d1)
-               : "d"(a), "d"(b));
+// D (16 x 8) += A (16 x 8, row) B (8 x 8, col). Fragments, g = lane / 4,
+// t = lane % 4: a = {A[g][t], A[g+8][t], A[g][t+4], A[g+8][t+4]};
+// b = {B[t][g], B[t+4][g]}; d = {D[g][2t], D[g][2t+1], D[g+8][2t], D[g+8][2t+1]}.
+__device__ __forceinline__ void mma_m16n8k8(double (&d)[4], double a0, double a1, double a2,
+                                            double a3, double b0, double b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+      : "d"(a0), "d"(a1), "d"(a2), "d"(a3), "d"(b0), "d"(b1));
 }
 }  // namespace dmma
 
@@ -79,11 +85,13 @@ gemm_dmma_kernel(int M, int N, int K, int k_slice, LA la, LB lb, double* __restr
     }
   };
 
-  double acc[8][4][2];
+  double acc[4][4][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) acc[i][j][h] = 0.0;
 
   int buf = 0;
   if (kbeg < kend) {
@@ -96,16 +104,21 @@ gemm_dmma_kernel(int M, int N, int K, int k_slice, LA la, LB lb, double* __restr
       const double* a_s = As + buf * BK * LDA;
       const double* b_s = Bs + buf * BK * LDB;
 #pragma unroll
-      for (int ks = 0; ks < BK; ks += 4) {
-        double af[8], bf[4];
+      for (int ks = 0; ks < BK; ks += 8) {
+        double bf[4][2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) af[i] = a_s[(ks + q) * LDA + wm + 8 * i + g];
+        for (int j = 0; j < 4; ++j) {
+          bf[j][0] = b_s[(ks + q) * LDB + wn + 8 * j + g];
+          bf[j][1] = b_s[(ks + q + 4) * LDB + wn + 8 * j + g];
+        }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) bf[j] = b_s[(ks + q) * LDB + wn + 8 * j + g];
+        for (int i = 0; i < 4; ++i) {
+          const double* ap = a_s + (ks + q) * LDA + wm + 16 * i + g;
+          const double a0 = ap[0], a1 = ap[8], a2 = ap[4 * LDA], a3 = ap[4 * LDA + 8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dmma::mma_m8n8k4(acc[i][j][0], acc[i][j][1], af[i], bf[j]);
+          for (int j = 0; j < 4; ++j)
+            dmma::mma_m16n8k8(acc[i][j], a0, a1, a2, a3, bf[j][0], bf[j][1]);
+        }
       }
       if (more) {
         sstore(buf ^ 1);
@@ -116,19 +129,22 @@ gemm_dmma_kernel(int M, int N, int K, int k_slice, LA la, LB lb, double* __restr
   }
 
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int m = m0 + wm + 8 * i + g;
-    if (m >= M) continue;
+  for (int i = 0; i < 4; ++i) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int hm = 0; hm < 2; ++hm) {
+      const int m = m0 + wm + 16 * i + 8 * hm + g;
+      if (m >= M) continue;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = n0 + wn + 8 * j + 2 * q + h;
-        if (n >= N) continue;
-        if (partial)
-          partial[((int64_t)blockIdx.z * M + m) * N + n] = acc[i][j][h];
-        else
-          epi(m, n, acc[i][j][h]);
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n = n0 + wn + 8 * j + 2 * q + h;
+          if (n >= N) continue;
+          if (partial)
+            partial[((int64_t)blockIdx.z * M + m) * N + n] = acc[i][j][2 * hm + h];
+          else
+            epi(m, n, acc[i][j][2 * hm + h]);
+        }
       }
     }
   }

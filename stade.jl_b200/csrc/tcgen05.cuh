@@ -108,13 +108,6 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
       "r"(src), "r"(c0), "r"(c1)
       : "memory");
 }
-// Hint: bring `bytes` (a multiple of 16) of global memory at `p` (16-byte
-// aligned) into L2.
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
-               "r"(bytes)
-               : "memory");
-}
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
