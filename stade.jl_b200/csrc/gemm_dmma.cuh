@@ -93,6 +93,10 @@ gemm_dmma_kernel(int M, int N, int K, int k_slice, LA la, LB lb, double* __restr
 #pragma unroll
       for (int h = 0; h < 4; ++h) acc[i][j][h] = 0.0;
 
+  // m16 / n8 tiles of the warp's 64 x 32 that hold any row / column of C
+  // (warp-uniform): a ragged last tile skips the MMAs of its empty part
+  const int mi = min(4, max(0, (M - m0 - wm + 15) / 16));
+  const int nj = min(4, max(0, (N - n0 - wn + 7) / 8));
   int buf = 0;
   if (kbeg < kend) {
     gload(kbeg);
@@ -113,11 +117,12 @@ gemm_dmma_kernel(int M, int N, int K, int k_slice, LA la, LB lb, double* __restr
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
+          if (i >= mi) break;
           const double* ap = a_s + (ks + q) * LDA + wm + 16 * i + g;
           const double a0 = ap[0], a1 = ap[8], a2 = ap[4 * LDA], a3 = ap[4 * LDA + 8];
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            dmma::mma_m16n8k8(acc[i][j], a0, a1, a2, a3, bf[j][0], bf[j][1]);
+            if (j < nj) dmma::mma_m16n8k8(acc[i][j], a0, a1, a2, a3, bf[j][0], bf[j][1]);
         }
       }
       if (more) {
@@ -149,6 +154,31 @@ gemm_dmma_kernel(int M, int N, int K, int k_slice, LA la, LB lb, double* __restr
     }
   }
   if (!partial) epi.finish((int64_t)blockIdx.y * gridDim.x + blockIdx.x);
+}
+
+// Split-K slices for the DMMA kernel (one 128 x 128 block per SM at a time:
+// 242-252 registers x 256 threads): the slice count minimising whole waves of
+// blocks x K blocks per slice, plus a charge of 4 K blocks per partial tile
+// written and summed back; at least 8 K blocks per slice. The weight
+// gradients of mlp2_ce_hv (28 tiles, K = 16,384 / 32,768) get 5 slices: 140
+// blocks, one wave, where a target of two blocks per SM (11 slices, 308
+// blocks) left a third wave 8 % full.
+inline int dmma_splits(int tiles, int K, int sms) {
+  const int kb = (K + dmma::BK - 1) / dmma::BK;
+  int best = 1;
+  double best_cost = 0.0;
+  for (int sl = 1; sl <= 64; ++sl) {
+    const int per = (kb + sl - 1) / sl;
+    if (sl > 1 && per < 8) break;
+    const int slices = (kb + per - 1) / per;
+    const int waves = (tiles * slices + sms - 1) / sms;
+    const double cost = (double)waves * per + (slices > 1 ? 4.0 * slices * tiles / sms : 0.0);
+    if (sl == 1 || cost < best_cost) {
+      best = sl;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 // Same contract as gemm_simt<double, ...> (splits and partial included).

@@ -669,6 +669,12 @@ stade_status gemm_f64(int M, int N, int K, LA la, LB lb, Epi epi, double* partia
 template <class T, int RM, int RN, int BK>
 int splits_for(int M, int N, int K) {
   const int tiles = ((M + 64 * RM - 1) / (64 * RM)) * ((N + 64 * RN - 1) / (64 * RN));
+  if constexpr (std::is_same<T, double>::value) {
+    // the DMMA kernel's 128 x 128 tiles, one block per SM
+    if (f64_dmma())
+      return dmma_splits(((M + dmma::BM - 1) / dmma::BM) * ((N + dmma::BN - 1) / dmma::BN), K,
+                         tc5::sm_count());
+  }
   return split_plan(tiles, K, BK, 64).splits;
 }
 
