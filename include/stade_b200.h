@@ -116,7 +116,7 @@ stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
  * the reference. For callers that cannot allocate device memory where they
  * run the sweep (all device memory handed to their own pool, a fixed memory
  * plan, a thread that must not block on cudaMalloc) and cannot size and pass
- * a workspace: the per-block partial sums live in a fixed 2 MiB array in the
+ * a workspace: the per-block partial sums live in a fixed 4 MiB array in the
  * library's own device memory, held by every GPU that loads the library until
  * the process exits. The call makes no cudaMalloc, cudaFree or other
  * allocating call; opts->workspace is ignored. Every call looks up the
@@ -125,7 +125,7 @@ stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
  * first call on a device also loads the library's device code there, so make
  * that first call before any stream capture. Sizes whose
  * partial sums exceed the array (stade_affine_ls_b_f64_noalloc_max_scratch()
- * bytes; the full 1024 x 64 x 32 configuration needs 1.03 MiB) return
+ * bytes; the full 1024 x 64 x 32 configuration needs 2.03 MiB) return
  * STADE_EINVAL. All calls share the one array: calls that overlap on the GPU
  * (different streams, no ordering between them) race on it. Results equal
  * those of stade_affine_ls_b_f64. */

@@ -9,9 +9,12 @@
 //
 // The generated CUDA.jl port turns `wb[o,k] += ...` into atomics on 2,048
 // addresses from 1,024 samples (cgen_device_assign, src/STADE.jl:11941).
-// Here each block owns a contiguous chunk of samples and writes its partial
-// wb / bb / loss; a second kernel sums the partials in block order. No
-// floating-point atomics, bit-identical results from call to call.
+// Here each block owns a contiguous chunk of samples, stages everything it
+// reads in shared memory with all of those loads in flight at once, and
+// writes its partial wb / bb / loss; a second kernel sums the partials in a
+// fixed order. No floating-point atomics, bit-identical results from call to
+// call. The whole sweep is a few microseconds of arithmetic, so what these
+// two kernels are built around is memory latency, not bandwidth.
 //
 // y, tb and xb follow the oracle's statement order with separate multiply and
 // add roundings (no FMA contraction), so they match it bit for bit.
@@ -21,7 +24,51 @@
 namespace stade {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
+
+// Global -> shared copy with `U` loads per thread in flight before any store
+// (one memory latency for a block's whole staging instead of one per pass).
+template <int U>
+__device__ __forceinline__ void stage(double* __restrict__ dst, const double* __restrict__ src,
+                                      int n) {
+  for (int base = threadIdx.x; base < n; base += U * kThreads) {
+    double r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * kThreads;
+      r[u] = i < n ? src[i] : 0.0;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * kThreads;
+      if (i < n) dst[i] = r[u];
+    }
+  }
+}
+
+// Rows of `cols` doubles copied to a pitch of `ld` (U loads in flight).
+template <int U>
+__device__ __forceinline__ void stage_rows(double* __restrict__ dst, int ld,
+                                           const double* __restrict__ src, int rows, int cols) {
+  const int n = rows * cols;
+  for (int base = threadIdx.x; base < n; base += U * kThreads) {
+    double r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * kThreads;
+      r[u] = i < n ? src[i] : 0.0;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * kThreads;
+      if (i < n) dst[(i / cols) * ld + i % cols] = r[u];
+    }
+  }
+}
+
+// Pitch of w's rows in shared memory: odd, so the forward's 32 lanes (32
+// outputs o, the same k) read 32 different banks instead of one.
+__host__ __device__ constexpr int w_pitch(int n_i) { return n_i | 1; }
 
 __global__ void __launch_bounds__(kThreads)
 affine_ls_chunk_kernel(const double* __restrict__ lossb, const double* __restrict__ w,
@@ -31,16 +78,27 @@ affine_ls_chunk_kernel(const double* __restrict__ lossb, const double* __restric
                        double* __restrict__ yb, int64_t n_s, int n_o, int n_i,
                        int chunk, double* __restrict__ part) {
   extern __shared__ double sm[];
-  double* ws = sm;                     // n_o * n_i
-  double* xs = ws + (size_t)n_o * n_i; // chunk * n_i
-  double* gs = xs + (size_t)chunk * n_i;  // chunk * n_o
+  const int ldw = w_pitch(n_i);
+  double* ws = sm;                           // n_o rows of pitch ldw
+  double* xs = ws + (size_t)n_o * ldw;       // chunk * n_i
+  double* xbs = xs + (size_t)chunk * n_i;    // chunk * n_i
+  double* gs = xbs + (size_t)chunk * n_i;    // chunk * n_o: t, then g
+  double* tbs = gs + (size_t)chunk * n_o;    // chunk * n_o
+  double* ybs = tbs + (size_t)chunk * n_o;   // chunk * n_o
+  double* bs = ybs + (size_t)chunk * n_o;    // n_o
   __shared__ double red[kThreads / 32];
 
   const int64_t s0 = (int64_t)blockIdx.x * chunk;
   const int ns = (int)((int64_t)chunk < n_s - s0 ? (int64_t)chunk : n_s - s0);
   const int nw = n_o * n_i;
-  for (int e = threadIdx.x; e < nw; e += blockDim.x) ws[e] = w[e];
-  for (int e = threadIdx.x; e < ns * n_i; e += blockDim.x) xs[e] = x[s0 * n_i + e];
+  // everything the block reads, staged up front
+  stage_rows<8>(ws, ldw, w, n_o, n_i);
+  stage<4>(xs, x + s0 * n_i, ns * n_i);
+  stage<4>(xbs, xb + s0 * n_i, ns * n_i);
+  stage<2>(gs, t + s0 * n_o, ns * n_o);
+  stage<2>(tbs, tb + s0 * n_o, ns * n_o);
+  stage<2>(ybs, yb + s0 * n_o, ns * n_o);
+  stage<1>(bs, b, n_o);
   __syncthreads();
 
   const double lb = lossb[0];
@@ -48,57 +106,96 @@ affine_ls_chunk_kernel(const double* __restrict__ lossb, const double* __restric
   // forward and the residual adjoint, one thread per (sample, output)
   for (int e = threadIdx.x; e < ns * n_o; e += blockDim.x) {
     const int sl = e / n_o, o = e % n_o;
-    double s = b[o];
-    const double* wr = ws + (size_t)o * n_i;
+    double s = bs[o];
+    const double* wr = ws + (size_t)o * ldw;
     const double* xr = xs + (size_t)sl * n_i;
     for (int k = 0; k < n_i; ++k) s = __dadd_rn(s, __dmul_rn(wr[k], xr[k]));
     const int64_t gi = s0 * n_o + e;
     y[gi] = s;
-    const double d = __dadd_rn(s, -t[gi]);
+    const double d = __dadd_rn(s, -gs[e]);
     loss_acc = __dadd_rn(loss_acc, __dmul_rn(0.5, __dmul_rn(d, d)));
     const double r = __dmul_rn(__dmul_rn(0.5, __dmul_rn(2.0, d)), lb);
-    tb[gi] = __dadd_rn(tb[gi], -r);
-    gs[e] = __dadd_rn(yb[gi], r);  // yb += r, then consumed
+    tb[gi] = __dadd_rn(tbs[e], -r);
+    gs[e] = __dadd_rn(ybs[e], r);  // yb += r, then consumed
     yb[gi] = 0.0;
   }
   __syncthreads();
-  // xb[s,k] += sum over o = n_o-1 .. 0 of w[o,k] g[s,o] (the oracle's order)
-  for (int e = threadIdx.x; e < ns * n_i; e += blockDim.x) {
-    const int sl = e / n_i, k = e % n_i;
-    const int64_t gi = s0 * n_i + e;
-    double acc = xb[gi];
-    const double* gr = gs + (size_t)sl * n_o;
-    for (int o = n_o - 1; o >= 0; --o) acc = __dadd_rn(acc, __dmul_rn(ws[(size_t)o * n_i + k], gr[o]));
-    xb[gi] = acc;
-  }
-  // partial wb[o,k] and bb[o] over this chunk, samples in descending order
-  double* my = part + (size_t)blockIdx.x * (nw + n_o + 1);
-  for (int e = threadIdx.x; e < nw + n_o; e += blockDim.x) {
-    double acc = 0.0;
-    if (e < nw) {
-      const int o = e / n_i, k = e % n_i;
-      for (int sl = ns - 1; sl >= 0; --sl)
-        acc = fma(xs[(size_t)sl * n_i + k], gs[(size_t)sl * n_o + o], acc);
-    } else {
-      const int o = e - nw;
-      for (int sl = ns - 1; sl >= 0; --sl) acc += gs[(size_t)sl * n_o + o];
+  // xb[s,k] += sum over o = n_o-1 .. 0 of w[o,k] g[s,o] (the oracle's order);
+  // each thread runs two elements' chains side by side (the additions of one
+  // chain depend on each other: two chains hide half the latency)
+  const int nx = ns * n_i;
+  for (int e0 = threadIdx.x; e0 < nx; e0 += 2 * kThreads) {
+    const int e1 = e0 + kThreads < nx ? e0 + kThreads : e0;
+    const int k0 = e0 % n_i, k1 = e1 % n_i;
+    const double* g0 = gs + (size_t)(e0 / n_i) * n_o;
+    const double* g1 = gs + (size_t)(e1 / n_i) * n_o;
+    double a0 = xbs[e0], a1 = xbs[e1];
+    for (int o = n_o - 1; o >= 0; --o) {
+      const double* wr = ws + (size_t)o * ldw;
+      a0 = __dadd_rn(a0, __dmul_rn(wr[k0], g0[o]));
+      a1 = __dadd_rn(a1, __dmul_rn(wr[k1], g1[o]));
     }
-    my[e] = acc;
+    xb[s0 * n_i + e0] = a0;
+    if (e1 != e0) xb[s0 * n_i + e1] = a1;
+  }
+  // partial wb[o,k] and bb[o] over this chunk, samples in descending order,
+  // four elements' chains side by side
+  double* my = part + (size_t)blockIdx.x * (nw + n_o + 1);
+  const int np = nw + n_o;
+  for (int e0 = threadIdx.x; e0 < np; e0 += 4 * kThreads) {
+    double acc[4];
+    int oo[4], kk[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * kThreads < np ? e0 + u * kThreads : e0;
+      acc[u] = 0.0;
+      oo[u] = e < nw ? e / n_i : e - nw;
+      kk[u] = e < nw ? e % n_i : -1;   // -1: a bb element (sum of g alone)
+    }
+    for (int sl = ns - 1; sl >= 0; --sl) {
+      const double* xr = xs + (size_t)sl * n_i;
+      const double* gr = gs + (size_t)sl * n_o;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        acc[u] = kk[u] >= 0 ? fma(xr[kk[u]], gr[oo[u]], acc[u]) : acc[u] + gr[oo[u]];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (u == 0 || e0 + u * kThreads < np) my[e0 + u * kThreads] = acc[u];
   }
   loss_acc = block_sum(loss_acc, red);
   if (threadIdx.x == 0) my[nw + n_o] = loss_acc;
 }
 
-// wb, bb and loss are contiguous-free caller arrays: one fixed-order pass
-// over the block partials adds into each of them.
-__global__ void affine_ls_finish_kernel(const double* __restrict__ part, int nblk, int n_o,
-                                        int n_i, double* __restrict__ wb,
-                                        double* __restrict__ bb, double* __restrict__ loss) {
+// wb, bb and loss: each element's block partials summed by 8 lanes (lane j
+// adds blocks j, j + 8, ... in order, all its loads in flight), then the 8
+// lane sums in a fixed tree; the same order on every call.
+constexpr int kFinLanes = 8;
+__global__ void __launch_bounds__(256)
+affine_ls_finish_kernel(const double* __restrict__ part, int nblk, int n_o, int n_i,
+                        double* __restrict__ wb, double* __restrict__ bb,
+                        double* __restrict__ loss) {
   const int nw = n_o * n_i;
   const int len = nw + n_o + 1;
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= len) return;
-  const double acc = ordered_sum(part + e, nblk, len, true);
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int e = tid / kFinLanes, j = tid % kFinLanes;
+  double acc = 0.0;
+  if (e < len) {
+    constexpr int U = 8;
+    for (int q0 = j; q0 < nblk; q0 += U * kFinLanes) {
+      double r[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int q = q0 + u * kFinLanes;
+        r[u] = q < nblk ? part[(size_t)q * len + e] : 0.0;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) acc += r[u];
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < kFinLanes; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (e >= len || j != 0) return;
   if (e < nw) wb[e] += acc;
   else if (e < nw + n_o) bb[e - nw] += acc;
   else loss[0] += acc;
@@ -111,11 +208,13 @@ struct Plan {
 
 Plan plan(int64_t n_s, int64_t n_o, int64_t n_i) {
   Plan p;
-  // about 16 samples per block: enough blocks to spread the 3 * n_s * n_o * n_i
-  // multiply-adds, few enough partials to sum quickly
-  p.chunk = 16;
+  // 8 samples per block: the sweep is latency-bound (a few microseconds of
+  // arithmetic), so it is spread over as many SMs as the batch allows (1024
+  // samples: 128 blocks); the partials stay few enough to sum in one pass
+  p.chunk = 8;
   p.nblk = (int)((n_s + p.chunk - 1) / p.chunk);
-  p.smem = sizeof(double) * ((size_t)n_o * n_i + (size_t)p.chunk * n_i + (size_t)p.chunk * n_o);
+  p.smem = sizeof(double) * ((size_t)n_o * w_pitch((int)n_i) + 2 * (size_t)p.chunk * n_i +
+                             3 * (size_t)p.chunk * n_o + n_o);
   return p;
 }
 
@@ -160,8 +259,8 @@ extern "C" stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
                                                           (int)n_o, (int)n_i, p.chunk, part);
   STADE_CHECK_LAUNCH();
   const int len = (int)(n_o * n_i + n_o + 1);
-  affine_ls_finish_kernel<<<ceil_div_u(len, 256), 256, 0, s>>>(part, p.nblk, (int)n_o, (int)n_i,
-                                                                wb, bb, loss);
+  affine_ls_finish_kernel<<<ceil_div_u((int64_t)len * kFinLanes, 256), 256, 0, s>>>(
+      part, p.nblk, (int)n_o, (int)n_i, wb, bb, loss);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }
@@ -181,8 +280,8 @@ extern "C" stade_status stade_affine_ls_b_f64(double* loss, const double* lossb,
 namespace stade {
 namespace {
 
-// 2 MiB: enough for the full configuration (1024 x 64 x 32 needs 1.03 MiB).
-constexpr size_t kNoAllocScratchDoubles = (size_t(2) << 20) / sizeof(double);
+// 4 MiB: enough for the full configuration (1024 x 64 x 32 needs 2.03 MiB).
+constexpr size_t kNoAllocScratchDoubles = (size_t(4) << 20) / sizeof(double);
 static __device__ __align__(256) double g_affine_noalloc_scratch[kNoAllocScratchDoubles];
 
 // Device address of the scratch array on the current device. In host code the
@@ -241,8 +340,8 @@ extern "C" stade_status stade_affine_ls_b_f64_noalloc(double* loss, const double
                                                           (int)n_o, (int)n_i, p.chunk, part);
   STADE_CHECK_LAUNCH();
   const int len = (int)(n_o * n_i + n_o + 1);
-  affine_ls_finish_kernel<<<ceil_div_u(len, 256), 256, 0, s>>>(part, p.nblk, (int)n_o, (int)n_i,
-                                                                wb, bb, loss);
+  affine_ls_finish_kernel<<<ceil_div_u((int64_t)len * kFinLanes, 256), 256, 0, s>>>(
+      part, p.nblk, (int)n_o, (int)n_i, wb, bb, loss);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }
