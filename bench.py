@@ -471,8 +471,13 @@ class Mlp2Ce:
         t = {k: v.to(dev) for k, v in self.host.items()}
         S, I, H, O = self.n_s, self.n_i, self.n_h, self.n_o
         z = lambda n: torch.zeros(n, dtype=f32, device=dev)
-        t.update(xb=z(S * I), yb=z(S * O), h=z(S * H), hb=z(S * H), zz=z(S * O), zb=z(S * O),
-                 p=z(S * O), pb=z(S * O))
+        t.update(h=z(S * H), zz=z(S * O), p=z(S * O))
+        # the local shadows back to back too: reset_local! clears them with one memset
+        local = z(S * I + S * O + S * H + S * O + S * O)
+        off = 0
+        for k, n in (("xb", S * I), ("yb", S * O), ("hb", S * H), ("zb", S * O), ("pb", S * O)):
+            t[k] = local[off:off + n]
+            off += n
         # the :accum shadows and the :reduced loss back to back in one allocation:
         # the step sums them with one NCCL all-reduce in place (no gather /
         # scatter into a bucket)

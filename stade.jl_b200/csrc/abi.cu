@@ -184,12 +184,24 @@ stade_status stade_ddp_zero(void* const* bufs, const int64_t* counts, int nbuf, 
   STADE_REQUIRE(dtype == STADE_F32 || dtype == STADE_F64, "stade_ddp_zero: bad dtype %d", dtype);
   const size_t es = dtype == STADE_F32 ? 4 : 8;
   cudaStream_t s = stade::stream_of(opts);
+  // buffers that follow each other in memory are cleared by one memset
+  char* run = nullptr;
+  size_t run_bytes = 0;
   for (int i = 0; i < nbuf; ++i) {
     STADE_REQUIRE(counts[i] >= 0, "stade_ddp_zero: negative count for buffer %d", i);
     if (counts[i] == 0) continue;
     STADE_REQUIRE(bufs[i] != nullptr, "stade_ddp_zero: null buffer %d", i);
-    STADE_CUDA(cudaMemsetAsync(bufs[i], 0, (size_t)counts[i] * es, s));
+    char* p = static_cast<char*>(bufs[i]);
+    const size_t bytes = (size_t)counts[i] * es;
+    if (run && run + run_bytes == p) {
+      run_bytes += bytes;
+      continue;
+    }
+    if (run) STADE_CUDA(cudaMemsetAsync(run, 0, run_bytes, s));
+    run = p;
+    run_bytes = bytes;
   }
+  if (run) STADE_CUDA(cudaMemsetAsync(run, 0, run_bytes, s));
   return STADE_OK;
 }
 

@@ -121,3 +121,25 @@ def test_mlp2_ce_hv_epilogue(comm):
     assert mask.value == 0
     assert role("shared") + role("seed") == ["w1", "b1", "w2", "b2", "w1d", "b1d", "w2d", "b2d",
                                              "lossb", "lossbd"]
+
+
+def test_ddp_zero_runs_of_adjacent_buffers():
+    """stade_ddp_zero clears buffers that follow each other in memory with one
+    memset per run: a mix of adjacent and separate buffers (in any order) is
+    zeroed exactly, and the elements around them are left alone."""
+    L = _lib.lib()
+    big = torch.arange(1, 1001, dtype=torch.float32, device="cuda")
+    other = torch.arange(1, 65, dtype=torch.float32, device="cuda")
+    spans = [(10, 30), (30, 31), (31, 100), (200, 260), (500, 500), (600, 700)]
+    bufs = [big[a:b] for a, b in spans] + [other[8:40]]
+    ptrs = (C.c_void_p * len(bufs))(*[C.c_void_p(b.data_ptr()) for b in bufs])
+    counts = (C.c_int64 * len(bufs))(*[b.numel() for b in bufs])
+    _lib.check(L.stade_ddp_zero(ptrs, counts, len(bufs), 0, None))
+    torch.cuda.synchronize()
+    want = np.arange(1, 1001, dtype=np.float32)
+    for a, b in spans:
+        want[a:b] = 0
+    want_o = np.arange(1, 65, dtype=np.float32)
+    want_o[8:40] = 0
+    assert np.array_equal(big.cpu().numpy(), want)
+    assert np.array_equal(other.cpu().numpy(), want_o)
