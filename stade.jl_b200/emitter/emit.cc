@@ -2515,7 +2515,7 @@ class Emitter {
   }
 
   std::string kernel_body_src(const Unit& u) {
-    std::ostringstream o;
+    std::ostringstream o, decl;   // decl: device arrays the kernel needs, before it
     KArgs k = kernel_args(u);
     std::string name = "stade_k" + std::to_string(u.id);
     if (u.par) {
@@ -2525,7 +2525,8 @@ class Emitter {
       for (auto& d : k.decl) o << ", " << d;
       o << ") {\n";
       // accumulations into one loop-invariant target from one site: a block
-      // sum and one atomic per block (the generated loss and scalar-adjoint sums)
+      // sum per block, the blocks' sums added in block order by the last block
+      // (the generated loss and scalar-adjoint sums)
       std::vector<std::pair<std::string, std::string>> blk;   // register, target
       red_sites_.clear();
       {
@@ -2563,7 +2564,7 @@ class Emitter {
         }
       }
       // a kernel with block sums strides over the iterations with a grid the
-      // SMs hold at once, so that one atomic per resident block remains
+      // SMs hold at once, so that one slot per resident block remains
       const std::string ind = blk.empty() ? "  " : "    ";
       std::ostringstream pv, rd;
       std::set<std::string> locals{L.var};
@@ -2615,7 +2616,25 @@ class Emitter {
         stmts(o, L.body, body_locals, u, 4);
         flush_pending(o, "    ", {}, true);
         o << "  }\n";
+        // each block's sums go to a slot of their own; the last block to
+        // finish adds the slots to the targets in block order (no float
+        // atomics: the same sums in the same order on every call)
+        const std::string parts = "stade_bpart" + std::to_string(u.id) + "_";
+        const std::string ticket = "stade_bticket" + std::to_string(u.id) + "_";
+        decl << "__device__ " << T_ << " " << parts << "[" << blk.size() << " * STADE_MAX_RES_BLOCKS];\n"
+             << "__device__ unsigned " << ticket << " = 0;\n";
+        o << "#ifdef STADE_EMIT_HOST\n";
         for (auto& [reg, tgt] : blk) o << "  jl_block_add(" << tgt << ", " << reg << ");\n";
+        o << "#else\n";
+        for (size_t j = 0; j < blk.size(); ++j)
+          o << "  jl_block_part(" << parts << " + " << j << " * STADE_MAX_RES_BLOCKS, "
+            << blk[j].first << ");\n";
+        o << "  if (jl_block_last(&" << ticket << ")) {\n";
+        for (size_t j = 0; j < blk.size(); ++j)
+          o << "    jl_block_finish(" << blk[j].second << ", " << parts << " + " << j
+            << " * STADE_MAX_RES_BLOCKS);\n";
+        o << "    if (threadIdx.x == 0) " << ticket << " = 0;\n  }\n";
+        o << "#endif\n";
       }
       pending_ = nullptr;
       red_sites_.clear();
@@ -2635,7 +2654,7 @@ class Emitter {
       stmts(o, u.stmts, locals, u, 2);
       o << "}\n";
     }
-    return o.str();
+    return decl.str() + o.str();
   }
 
   std::string text_loop(Stmt& s) {
@@ -2708,6 +2727,7 @@ class Emitter {
               o << pad << "    static int cap_ = 0;\n" << pad
                 << "    if (cap_ == 0) cap_ = stade_resident_blocks((const void*)" << name << ");\n";
               grid = "(unsigned)((n_ + 255) / 256 < cap_ ? (n_ + 255) / 256 : cap_)";
+              o << pad << "    if (cap_ > STADE_MAX_RES_BLOCKS) cap_ = STADE_MAX_RES_BLOCKS;\n";
             }
             o << pad << "    STADE_LAUNCH(" << name << ", " << grid << ", 256, s_, lo_, st_, n_, (int64_t)0";
             for (auto& p : k.pass) o << ", " << p;
@@ -3028,6 +3048,8 @@ class Emitter {
 #include <math.h>
 #include <vector>
 static int64_t stade_launches_ = 0;   // kernels this module has launched
+// the grid of a kernel with block sums: at most this many blocks (one slot each)
+#define STADE_MAX_RES_BLOCKS 4096
 #ifdef STADE_EMIT_HOST
 // Host build of the same program (tests): kernels run as loops over their
 // threads, in thread order; atomics are plain adds.
@@ -3096,20 +3118,52 @@ template <class T> static inline int64_t jl_bits(T) { return 0; }
 template <class T> static inline T jl_after(T v, int64_t) { return v; }
 #define STADE_ASC 0
 #else
-// Sum over the block, then one atomic add: every thread of the block calls it.
+// Block sums without float atomics. jl_block_part: the block's sum (warp
+// shuffles, then the warps' sums, a fixed tree) into this block's slot;
+// jl_block_last: true in the block that finished last (an integer ticket);
+// jl_block_finish (that block): the slots summed in block order (each thread
+// a contiguous run, then the same fixed tree) and added to the target. With
+// the grid fixed (the resident grid of the device), the same sums in the same
+// order on every call.
 template <class T>
-__device__ __forceinline__ void jl_block_add(T* p, T v) {
+__device__ __forceinline__ T jl_block_reduce(T v) {
   __shared__ T part_[32];
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   __syncthreads();
   if (l == 0) part_[w] = v;
   __syncthreads();
+  T t = (T)0;
   if (w == 0) {
-    T t = l < (int)(blockDim.x >> 5) ? part_[l] : (T)0;
+    t = l < (int)(blockDim.x >> 5) ? part_[l] : (T)0;
     for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (l == 0) atomicAdd(p, t);
   }
+  return t;   // the block's sum in thread 0
+}
+template <class T>
+__device__ __forceinline__ void jl_block_part(T* parts, T v) {
+  const T t = jl_block_reduce(v);
+  if (threadIdx.x == 0) parts[blockIdx.x] = t;
+}
+__device__ __forceinline__ bool jl_block_last(unsigned* ticket) {
+  __shared__ bool last_;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();   // this block's slots are visible before its ticket
+    last_ = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last_) __threadfence();
+  return last_;
+}
+template <class T>
+__device__ __forceinline__ void jl_block_finish(T* p, const T* parts) {
+  const int n = (int)gridDim.x, per = (n + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int b0 = (int)threadIdx.x * per, b1 = b0 + per < n ? b0 + per : n;
+  T s = (T)0;
+  for (int b = b0; b < b1; ++b) s += ((const volatile T*)parts)[b];
+  const T t = jl_block_reduce(s);
+  if (threadIdx.x == 0) *p += t;
 }
 // the bits of a loaded value, and v made to depend on them (d is 0 at run time)
 __device__ __forceinline__ int64_t jl_bits(double x) { return __double_as_longlong(x); }
