@@ -426,23 +426,27 @@ mlp_head_small_kernel(const T* __restrict__ zpart, int nchunks, const T* __restr
 // The s1b pass of the TMA path, two adjacent hidden units per thread (8-byte
 // loads and stores, few registers, many blocks in flight):
 // s1b = (1 - h^2) (hb + sum_c w2[k, c] g[s, c]), c descending (the generated
-// order), written as TF32 hi / lo planes; hb consumed to zero (stored only
+// order, multiply-adds fused: this pass was issue-bound, 73 instructions per
+// element), written as TF32 hi / lo planes; hb consumed to zero (stored only
 // where it held a seed); the chunk's W2b (sum_s h g), b2b (sum_s g) and b1b
 // (sum_s s1b) partials. NO = the class count rounded to a template (exact for
-// 10 classes). Block = 128 threads x 2 units = 256 units of a chunk of
-// samples; partial record [chunk][n_h*n_o (W2b) + n_o (b2b) + n_h (b1b)].
+// 10 classes); a sample's g sits in shared memory at a pitch of NO rounded up
+// to 4. Block = 128 threads x 2 units = 256 units of a
+// chunk of samples; partial record [chunk][n_h*n_o (W2b) + n_o (b2b) + n_h
+// (b1b)].
 template <int NO>
 __global__ void __launch_bounds__(128)
 mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
                       const float* __restrict__ gbuf, const float* __restrict__ w2,
                       float* __restrict__ s1b_hi, float* __restrict__ s1b_lo, int n_s, int n_h,
                       int n_o, int chunk, float* __restrict__ part) {
+  constexpr int GP = (NO + 3) / 4 * 4;           // g's pitch in shared memory
   extern __shared__ __align__(16) unsigned char smraw[];
-  float* gs = reinterpret_cast<float*>(smraw);  // chunk x NO (zero padded)
+  float* gs = reinterpret_cast<float*>(smraw);  // chunk x GP (zero padded)
   const int s0 = blockIdx.x * chunk;
   const int ns = min(n_s, s0 + chunk) - s0;
-  for (int e = threadIdx.x; e < ns * NO; e += blockDim.x) {
-    const int i = e / NO, c = e % NO;
+  for (int e = threadIdx.x; e < ns * GP; e += blockDim.x) {
+    const int i = e / GP, c = e % GP;
     gs[e] = c < n_o ? gbuf[(int64_t)(s0 + i) * n_o + c] : 0.f;
   }
   __syncthreads();
@@ -460,7 +464,7 @@ mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
     float2 bsum = make_float2(0.f, 0.f);
     auto one = [&](int i, float2 hv, float2 acc2) {
       const int64_t off = (int64_t)(s0 + i) * n_h + k;
-      const float* g = gs + i * NO;
+      const float* g = gs + i * GP;
       float hh[2] = {hv.x, hv.y};
       float ac[2] = {acc2.x, acc2.y};
 #pragma unroll
@@ -469,7 +473,7 @@ mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
           const float gc = g[c];
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
-            ac[j] = __fadd_rn(ac[j], __fmul_rn(w[j][c], gc));
+            ac[j] = fmaf(w[j][c], gc, ac[j]);
             a[j][c] = fmaf(hh[j], gc, a[j][c]);
           }
         }
@@ -516,7 +520,7 @@ mlp_s1b_planes_kernel(const float* __restrict__ h, float* __restrict__ hb,
   if (blockIdx.y == 0 && threadIdx.x < n_o) {
     const int c = threadIdx.x;
     float acc = 0.f;
-    for (int i = 0; i < ns; ++i) acc += gs[i * NO + c];
+    for (int i = 0; i < ns; ++i) acc += gs[i * GP + c];
     my[(int64_t)n_h * n_o + c] = acc;
   }
 }
@@ -1212,7 +1216,7 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
     {
       PhaseScope ph("w2b", s);
       const int chunks = (S + kW2ChunkTc - 1) / kW2ChunkTc;
-      const int no = O == 10 ? 10 : O <= 16 ? 16 : 32;
+      const int no = O == 10 ? 12 : O <= 16 ? 16 : 32;   // g's pitch in shared memory
       const size_t smem = sizeof(float) * (size_t)kW2ChunkTc * no;
       auto kern = O == 10 ? mlp_s1b_planes_kernel<10>
                           : O <= 16 ? mlp_s1b_planes_kernel<16> : mlp_s1b_planes_kernel<32>;
