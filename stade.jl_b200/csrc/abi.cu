@@ -184,6 +184,7 @@ stade_status stade_ddp_zero(void* const* bufs, const int64_t* counts, int nbuf, 
   STADE_REQUIRE(dtype == STADE_F32 || dtype == STADE_F64, "stade_ddp_zero: bad dtype %d", dtype);
   const size_t es = dtype == STADE_F32 ? 4 : 8;
   cudaStream_t s = stade::stream_of(opts);
+  stade::PhaseScope ph("reset", s);
   // buffers that follow each other in memory are cleared by one memset
   char* run = nullptr;
   size_t run_bytes = 0;

@@ -338,6 +338,7 @@ stade_status stade_ddp_allreduce_sum(stade_comm* c, void* const* bufs, const int
   stade_status st = build_segs(bufs, counts, nbuf, &sg, &contiguous, es);
   if (st != STADE_OK) return st;
   cudaStream_t s = stream_of(opts);
+  PhaseScope ph("allreduce", s);
   const int64_t total = sg.off[nbuf];
   void* data = nbuf > 0 ? bufs[0] : nullptr;
   if (total > 0 && !contiguous) {
