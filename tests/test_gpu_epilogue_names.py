@@ -143,3 +143,19 @@ def test_ddp_zero_runs_of_adjacent_buffers():
     want_o[8:40] = 0
     assert np.array_equal(big.cpu().numpy(), want)
     assert np.array_equal(other.cpu().numpy(), want_o)
+
+
+def test_ddp_zero_large_runs():
+    """A 6 MB run of two adjacent buffers (one memset) that ends mid-array and
+    not on a 16-byte boundary: cleared exactly, the bytes around it kept."""
+    L = _lib.lib()
+    n = (6 << 20) // 4 + 3                       # 6 MB + 12 bytes of Float32
+    big = torch.full((n + 64,), 7.0, dtype=torch.float32, device="cuda")
+    bufs = [big[16:16 + n // 2], big[16 + n // 2:16 + n]]   # adjacent: one run
+    ptrs = (C.c_void_p * 2)(*[C.c_void_p(b.data_ptr()) for b in bufs])
+    counts = (C.c_int64 * 2)(*[b.numel() for b in bufs])
+    _lib.check(L.stade_ddp_zero(ptrs, counts, 2, 0, None))
+    torch.cuda.synchronize()
+    host = big.cpu().numpy()
+    assert not np.any(host[16:16 + n])
+    assert np.all(host[:16] == 7.0) and np.all(host[16 + n:] == 7.0)
