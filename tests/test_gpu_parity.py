@@ -302,3 +302,20 @@ def test_mlp2_ce_b_unaligned_inputs():
     for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
         ok, errs = f32_verdict(dev[k].cpu().numpy(), ref[k], truth[k])
         assert ok, (k, errs)
+
+
+@pytest.mark.parametrize("chain", ["1", "8"])
+def test_mlp2_ce_b_tc_chain_lengths(chain):
+    """STADE_TC_CHAIN (K blocks per TMEM accumulation chain; read once per
+    process, so each length runs in a process of its own): the default
+    tensor-core path's cases at chains of 1 and 8 against the oracle."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, STADE_TC_CHAIN=chain)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-m", "gpu", "-p", "no:cacheprovider",
+                        "tests/test_gpu_parity.py", "-k", "tensor_core_path and tma4"],
+                       env=env, cwd=root, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert "5 passed" in r.stdout, r.stdout[-2000:]
