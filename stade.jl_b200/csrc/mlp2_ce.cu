@@ -1173,8 +1173,7 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
       PhaseScope ph("split", s);
       // x and W1 serve as their own hi planes (kind::tf32 reads the top 19
       // bits); only their lo planes are written
-      st = tma_split_lo(x, w.x_lo, n_s * n_i, s);
-      if (st == STADE_OK) st = tma_split_lo(w1, w.w1_lo, n_i * n_h, s);
+      st = tma_split_lo2(x, w.x_lo, n_s * n_i, w1, w.w1_lo, n_i * n_h, s);
     }
     if (st != STADE_OK) return st;
     // 1. h = tanh(x W1 + b1), TMA-fed tensor cores (the logits in a pass of

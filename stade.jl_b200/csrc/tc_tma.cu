@@ -988,34 +988,22 @@ int pair_slices(int M, int N, int K, bool b_mn) {
   return best;
 }
 
-// hi / lo split of a Float32 array (n % 4 == 0 handled by the vector path),
-// both planes rounded to the nearest TF32 value.
-__global__ void split_kernel(const float* __restrict__ a, float* __restrict__ hi,
-                             float* __restrict__ lo, int64_t n) {
+// The lo plane of an array that serves as its own hi plane: the tensor core
+// reads just the top 19 bits of a Float32 operand (kind::tf32), so the array
+// itself is its (truncated) hi plane and lo = rn(a - trunc(a)) completes it.
+// Two arrays' lo planes in one launch: blocks [0, nb0) take the first, the
+// rest the second (W1's 0.4 M elements ride along with x's 51 M).
+__global__ void split_lo2_kernel(const float* __restrict__ a0, float* __restrict__ lo0, int64_t n0,
+                                 const float* __restrict__ a1, float* __restrict__ lo1, int64_t n1,
+                                 int nb0) {
+  const bool second = (int)blockIdx.x >= nb0;
+  const float* a = second ? a1 : a0;
+  float* lo = second ? lo1 : lo0;
+  const int64_t n = second ? n1 : n0;
+  const int64_t b = second ? blockIdx.x - nb0 : blockIdx.x;
+  const int64_t nb = second ? (int64_t)gridDim.x - nb0 : nb0;
   const int64_t n4 = n / 4;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float4 v = reinterpret_cast<const float4*>(a)[i];
-    float4 h, l;
-    tc5::tf32_split(v.x, h.x, l.x);
-    tc5::tf32_split(v.y, h.y, l.y);
-    tc5::tf32_split(v.z, h.z, l.z);
-    tc5::tf32_split(v.w, h.w, l.w);
-    reinterpret_cast<float4*>(hi)[i] = h;
-    reinterpret_cast<float4*>(lo)[i] = l;
-  }
-  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    tc5::tf32_split(a[i], hi[i], lo[i]);
-}
-
-// The lo plane only: the tensor core reads just the top 19 bits of a Float32
-// operand (kind::tf32), so the array itself serves as its (truncated) hi
-// plane and lo = rn(a - trunc(a)) completes it.
-__global__ void split_lo_kernel(const float* __restrict__ a, float* __restrict__ lo, int64_t n) {
-  const int64_t n4 = n / 4;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = b * blockDim.x + threadIdx.x; i < n4; i += nb * blockDim.x) {
     const float4 v = reinterpret_cast<const float4*>(a)[i];
     float4 l;
     l.x = tc5::tf32_lo_of_own(v.x);
@@ -1024,8 +1012,7 @@ __global__ void split_lo_kernel(const float* __restrict__ a, float* __restrict__
     l.w = tc5::tf32_lo_of_own(v.w);
     reinterpret_cast<float4*>(lo)[i] = l;
   }
-  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
+  for (int64_t i = n4 * 4 + b * blockDim.x + threadIdx.x; i < n; i += nb * blockDim.x)
     lo[i] = tc5::tf32_lo_of_own(a[i]);
 }
 
@@ -1061,24 +1048,15 @@ __global__ void w1b_finish_t_kernel(const float* __restrict__ part, int slices, 
 }  // namespace tma
 
 // ---- entry points used by mlp2_ce -------------------------------------------------------
-stade_status tma_split(const float* a, float* hi, float* lo, int64_t n, cudaStream_t s) {
-  if (n <= 0) return STADE_OK;
-  const int64_t threads = 256;
-  int64_t blocks = (n / 4 + threads - 1) / threads;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  if (blocks < 1) blocks = 1;
-  tma::split_kernel<<<(unsigned)blocks, (unsigned)threads, 0, s>>>(a, hi, lo, n);
-  STADE_CHECK_LAUNCH();
-  return STADE_OK;
-}
-
-stade_status tma_split_lo(const float* a, float* lo, int64_t n, cudaStream_t s) {
-  if (n <= 0) return STADE_OK;
-  const int64_t threads = 256;
-  int64_t blocks = (n / 4 + threads - 1) / threads;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  if (blocks < 1) blocks = 1;
-  tma::split_lo_kernel<<<(unsigned)blocks, (unsigned)threads, 0, s>>>(a, lo, n);
+stade_status tma_split_lo2(const float* a0, float* lo0, int64_t n0, const float* a1, float* lo1,
+                           int64_t n1, cudaStream_t s) {
+  auto blocks_for = [](int64_t n) {
+    int64_t b = (n / 4 + 255) / 256;
+    if (b > 148 * 16) b = 148 * 16;
+    return (int)(b < 1 ? 1 : b);
+  };
+  const int nb0 = blocks_for(n0), nb1 = blocks_for(n1);
+  tma::split_lo2_kernel<<<nb0 + nb1, 256, 0, s>>>(a0, lo0, n0, a1, lo1, n1, nb0);
   STADE_CHECK_LAUNCH();
   return STADE_OK;
 }

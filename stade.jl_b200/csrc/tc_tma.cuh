@@ -15,9 +15,10 @@ bool tma_mlp_supported(int64_t n_s, int64_t n_i, int64_t n_h);
 // units.
 int tma_logit_parts(int64_t n_h);
 
-stade_status tma_split(const float* a, float* hi, float* lo, int64_t n, cudaStream_t s);
-// lo plane only (the array is its own hi plane for kind::tf32)
-stade_status tma_split_lo(const float* a, float* lo, int64_t n, cudaStream_t s);
+// x's and W1's TF32 lo planes in one launch (each array is its own hi plane
+// for kind::tf32; n0, n1 > 0)
+stade_status tma_split_lo2(const float* a0, float* lo0, int64_t n0, const float* a1, float* lo1,
+                           int64_t n1, cudaStream_t s);
 size_t tma_w1b_part_floats(int64_t n_s, int64_t n_i, int64_t n_h);
 stade_status tma_forward_tanh_logits(const float* x_hi, const float* x_lo, const float* w1_hi,
                                      const float* w1_lo, const float* b1, const float* w2,
