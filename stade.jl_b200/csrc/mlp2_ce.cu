@@ -32,7 +32,28 @@ namespace stade {
 namespace {
 
 constexpr int kHeadWarps = 8;   // samples in flight per block
+// Sum over the 32 lanes of a[0..15] (each lane its own sixteen values): four
+// halving exchanges leave each lane pair one class's sum, class
+// ((l >> 4) & 1) * 8 + ((l >> 3) & 1) * 4 + ((l >> 2) & 1) * 2 + ((l >> 1) & 1).
+__device__ __forceinline__ double halving_sum16(double (&a)[16], int lane) {
+#pragma unroll
+  for (int w = 8, bit = 16; w >= 1; w >>= 1, bit >>= 1) {
+    const bool upper = (lane & bit) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const double keep = upper ? a[i + w] : a[i];
+      const double send = upper ? a[i] : a[i + w];
+      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+    }
+  }
+  return a[0] + __shfl_xor_sync(0xffffffffu, a[0], 1);
+}
+// A lane that holds class c's sum after halving_sum16.
+__device__ __forceinline__ int class_lane16(int c) {
+  return (((c >> 3) & 1) << 4) | (((c >> 2) & 1) << 3) | (((c >> 1) & 1) << 2) | ((c & 1) << 1);
+}
 constexpr int kW2Chunk = 256;   // samples per W2b partial
+constexpr int kW2ChunkHv = 64;  // samples per W2b / W2bd partial of the Float64 HVP
 
 template <class T> __device__ __forceinline__ T dtanh(T x);
 template <> __device__ __forceinline__ float dtanh(float x) { return tanhf(x); }
@@ -713,7 +734,8 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
                    double* __restrict__ pd, double* __restrict__ pbd,
                    double* __restrict__ gbuf, double* __restrict__ gdbuf,
                    double* __restrict__ s1b, double* __restrict__ s1bd, int n_s, int n_h, int n_o,
-                   double* __restrict__ loss_part, double* __restrict__ lossd_part, int w2_smem) {
+                   double* __restrict__ loss_part, double* __restrict__ lossd_part, int w2_smem,
+                   int rows_smem) {
   __shared__ double red[2][kHeadWarps];
   // w2 and w2d staged class-major with an odd row stride: the class lanes of
   // the logits loop and the hidden-unit lanes of the s1b loop both read
@@ -741,18 +763,78 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
   const int c = cl ? lane : 0;
   const double lb = lossb[0], lbd = lossbd[0];
   double loss_acc = 0.0, lossd_acc = 0.0;
+  // rows_smem (with w2_smem): each warp stages its sample's h and hd rows in
+  // shared memory (after w2 / w2d) with one coalesced load each, all in
+  // flight at once; otherwise the rows are read from memory unit by unit
+  double* hs = w2sm + 2 * (size_t)n_o * LD + (size_t)warp * 2 * n_h;
+  double* hds = hs + n_h;
   for (int s = blockIdx.x * kHeadWarps + warp; s < n_s; s += gridDim.x * kHeadWarps) {
     const double* hr = h + (int64_t)s * n_h;
     const double* hdr = hd + (int64_t)s * n_h;
     const int64_t row = (int64_t)s * n_o;
-    // logits and tangents, hidden units in order (the primal's sequential sum)
+    // the class lane's per-sample values, loaded together up front (read in
+    // order below, each would otherwise wait out a memory latency of its own)
+    double y_c = 0.0, yd_c = 0.0, yb_c = 0.0, ybd_c = 0.0, pb_c = 0.0, pbd_c = 0.0, zb_c = 0.0,
+           zbd_c = 0.0;
+    if (cl) {
+      y_c = y[row + c]; yd_c = yd[row + c]; yb_c = yb[row + c]; ybd_c = ybd[row + c];
+      pb_c = pb[row + c]; pbd_c = pbd[row + c]; zb_c = zb[row + c]; zbd_c = zbd[row + c];
+    }
+    if (rows_smem) {
+      __syncwarp();   // the previous sample's reads of the rows are done
+      for (int k0 = 0; k0 < n_h; k0 += 32 * 8) {
+        double r[8], rd[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = k0 + 32 * j + lane;
+          r[j] = k < n_h ? hr[k] : 0.0;
+          rd[j] = k < n_h ? hdr[k] : 0.0;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int k = k0 + 32 * j + lane;
+          if (k < n_h) { hs[k] = r[j]; hds[k] = rd[j]; }
+        }
+      }
+      __syncwarp();
+    }
+    const double* hrow = rows_smem ? hs : hr;
+    const double* hdrow = rows_smem ? hds : hdr;
+    // logits and tangents
     double zv = b2[c], zdv = b2d[c];
+    if (rows_smem && n_o <= 16) {
+      // every lane sums its own hidden units (l, l + 32, ...) for all classes
+      // (sixteen independent chains per array), then the lanes' sums meet in
+      // a fixed halving tree: the same order on every call (the generated
+      // sweep's single chain per class held ten lanes of a warp for 512
+      // dependent additions per sample)
+      double za[16], zda[16];
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) { za[cc] = 0.0; zda[cc] = 0.0; }
+      for (int k = lane; k < n_h; k += 32) {
+        const double hv = hs[k], hdv = hds[k];
+#pragma unroll
+        for (int cc = 0; cc < 16; ++cc) {
+          if (cc < n_o) {
+            const double wv = W(k, cc);
+            zda[cc] = zda[cc] + (hv * WD(k, cc) + wv * hdv);
+            za[cc] = fma(wv, hv, za[cc]);
+          }
+        }
+      }
+      const double zs = halving_sum16(za, lane), zds = halving_sum16(zda, lane);
+      const int src = class_lane16(c);
+      const double zsum = __shfl_sync(F, zs, src), zdsum = __shfl_sync(F, zds, src);
+      zv = zv + zsum;
+      zdv = zdv + zdsum;
+    } else {
 #pragma unroll 8
-    for (int k = 0; k < n_h; ++k) {
-      const double hv = hr[k], hdv = hdr[k];
-      const double wv = W(k, c);
-      zdv = zdv + (hv * WD(k, c) + wv * hdv);
-      zv = zv + wv * hv;
+      for (int k = 0; k < n_h; ++k) {
+        const double hv = hrow[k], hdv = hdrow[k];
+        const double wv = W(k, c);
+        zdv = zdv + (hv * WD(k, c) + wv * hdv);
+        zv = zv + wv * hv;
+      }
     }
     // running max over classes with its tangent
     double m = __shfl_sync(F, zv, 0), md = __shfl_sync(F, zdv, 0);
@@ -771,8 +853,8 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
     double yv = 0.0, ydv = 0.0;
     double lq = 0.0, lqd = 0.0, q = 1.0, qd = 0.0;
     if (cl) {
-      yv = y[row + c];
-      ydv = yd[row + c];
+      yv = y_c;
+      ydv = yd_c;
       q = e / rs;
       qd = ed / rs - (e / (rs * rs)) * rsd;
       lq = log(q);
@@ -783,15 +865,15 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
     // reverse of the loss statement with tangents
     double pbv = 0.0, pbdv = 0.0, rsb_c = 0.0, rsbd_c = 0.0;
     if (cl) {
-      ybd[row + c] = ybd[row + c] + -(lqd * lb + lq * lbd);
-      yb[row + c] = yb[row + c] + -(lq) * lb;
+      ybd[row + c] = ybd_c + -(lqd * lb + lq * lbd);
+      yb[row + c] = yb_c + -(lq) * lb;
       const double inv_q = 1.0 / q, inv_qd = -(qd / (q * q));
       const double ny = -(yv) * lb, nyd = -(ydv * lb + yv * lbd);
       const double qbd = inv_qd * ny + inv_q * nyd;
       const double qb = inv_q * ny;
       const double inv_rs = 1.0 / rs, inv_rsd = -(rsd / (rs * rs));
-      pbdv = pbd[row + c] + (inv_rsd * qb + inv_rs * qbd);
-      pbv = pb[row + c] + inv_rs * qb;
+      pbdv = pbd_c + (inv_rsd * qb + inv_rs * qbd);
+      pbv = pb_c + inv_rs * qb;
       const double pr2 = e / (rs * rs);
       const double pr2d = ed / (rs * rs) - (e / (rs * rs)) * ((2.0 * rs * rsd) / (rs * rs));
       rsbd_c = -(pr2d * qb + pr2 * qbd);
@@ -803,8 +885,8 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
       const double oldbd = pbdv + rsbd, oldb = pbv + rsb;
       csed = ed * oldb + e * oldbd;
       cse = e * oldb;
-      gd = zbd[row + c] + csed;
-      g = zb[row + c] + cse;
+      gd = zbd_c + csed;
+      g = zb_c + cse;
     }
     double mb = warp_sum(-cse), mbd = warp_sum(-csed);
     // reverse of the running max, classes n_o - 1 .. 1
@@ -859,9 +941,10 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
       for (int j = 0; j < 8; ++j) {
         const int k = k0 + 32 * j + lane;
         if (k < n_h) {
-          const double th = hr[k];
+          const double th = hrow[k];
+          const double thd = hdrow[k];
           const double gg = 1.0 - th * th;
-          s1bdr[k] = acc[j] * -((2.0 * th) * hdr[k]) + gg * accd[j];
+          s1bdr[k] = acc[j] * -((2.0 * th) * thd) + gg * accd[j];
           s1br[k] = gg * acc[j];
           hbr[k] = 0.0;
           hbdr[k] = 0.0;
@@ -883,62 +966,70 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
 }
 
 // W2b, W2bd, b2b, b2bd partials of one chunk of samples; layout
-// [chunk][n_h*n_o (W2b) + n_h*n_o (W2bd) + n_o (b2b) + n_o (b2bd)].
+// [chunk][n_h*n_o (W2b) + n_h*n_o (W2bd) + n_o (b2b) + n_o (b2bd)]. One thread
+// per hidden unit k (a block's 256 units read each h / hd row coalesced, four
+// samples' loads in flight), the samples of the chunk in order; the chunk's g
+// and gd staged in shared memory (broadcast reads).
 template <int NO>
 __global__ void __launch_bounds__(256)
 mlp_w2b_hv_partial_kernel(const double* __restrict__ h, const double* __restrict__ hd,
                           const double* __restrict__ gbuf, const double* __restrict__ gdbuf,
                           int n_s, int n_h, int n_o, int chunk, double* __restrict__ part) {
+  extern __shared__ double gsm[];   // [chunk][2 NO]: g, then gd (zero padded)
   const int s0 = blockIdx.x * chunk;
-  const int s1 = min(n_s, s0 + chunk);
+  const int ns = min(n_s, s0 + chunk) - s0;
+  for (int e = threadIdx.x; e < ns * NO; e += blockDim.x) {
+    const int i = e / NO, c = e % NO;
+    const int64_t src = (int64_t)(s0 + i) * n_o + c;
+    gsm[i * 2 * NO + c] = c < n_o ? gbuf[src] : 0.0;
+    gsm[i * 2 * NO + NO + c] = c < n_o ? gdbuf[src] : 0.0;
+  }
+  __syncthreads();
   const int64_t nw = (int64_t)n_h * n_o;
   double* my = part + (int64_t)blockIdx.x * (2 * nw + 2 * n_o);
-  // block (chunk, 32 hidden units); a warp holds 4 units x 8 sample lanes,
-  // the sample lanes summed by shuffles in a fixed order
-  const int lane = threadIdx.x & 31, sl = lane & 7;
-  const int k = blockIdx.y * 32 + (threadIdx.x >> 5) * 4 + (lane >> 3);
-  double acc[NO], accd[NO];
-#pragma unroll
-  for (int c = 0; c < NO; ++c) { acc[c] = 0.0; accd[c] = 0.0; }
+  const int k = blockIdx.y * blockDim.x + threadIdx.x;
   if (k < n_h) {
-#pragma unroll 4
-    for (int s = s0 + sl; s < s1; s += 8) {
-      const double hv = h[(int64_t)s * n_h + k], hdv = hd[(int64_t)s * n_h + k];
-      const double* gr = gbuf + (int64_t)s * n_o;
-      const double* gdr = gdbuf + (int64_t)s * n_o;
+    double acc[NO], accd[NO];
+#pragma unroll
+    for (int c = 0; c < NO; ++c) { acc[c] = 0.0; accd[c] = 0.0; }
+    auto one = [&](int i, double hv, double hdv) {
+      const double* gr = gsm + i * 2 * NO;
 #pragma unroll
       for (int c = 0; c < NO; ++c) {
         if (c < n_o) {
-          accd[c] += gr[c] * hdv + hv * gdr[c];
+          accd[c] += gr[c] * hdv + hv * gr[NO + c];
           acc[c] = fma(hv, gr[c], acc[c]);
         }
       }
-    }
-  }
+    };
+    int i = 0;
+    for (; i + 4 <= ns; i += 4) {
+      double hv[4], hdv[4];
 #pragma unroll
-  for (int c = 0; c < NO; ++c) {
-    if (c < n_o) {
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], o);
-        accd[c] += __shfl_xor_sync(0xffffffffu, accd[c], o);
+      for (int u = 0; u < 4; ++u) {
+        const int64_t off = (int64_t)(s0 + i + u) * n_h + k;
+        hv[u] = h[off];
+        hdv[u] = hd[off];
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) one(i + u, hv[u], hdv[u]);
     }
-  }
-  if (k < n_h && sl == 0) {
+    for (; i < ns; ++i) {
+      const int64_t off = (int64_t)(s0 + i) * n_h + k;
+      one(i, h[off], hd[off]);
+    }
 #pragma unroll
     for (int c = 0; c < NO; ++c) {
       if (c < n_o) {
-        my[k * n_o + c] = acc[c];
-        my[nw + k * n_o + c] = accd[c];
+        my[(int64_t)k * n_o + c] = acc[c];
+        my[nw + (int64_t)k * n_o + c] = accd[c];
       }
     }
   }
   if (blockIdx.y == 0 && threadIdx.x < 2 * n_o) {
-    const int c = threadIdx.x % n_o;
-    const double* src = threadIdx.x < n_o ? gbuf : gdbuf;
+    const int c = threadIdx.x % n_o, off = threadIdx.x < n_o ? 0 : NO;
     double a = 0.0;
-    for (int s = s0; s < s1; ++s) a += src[(int64_t)s * n_o + c];
+    for (int i = 0; i < ns; ++i) a += gsm[i * 2 * NO + off + c];
     my[2 * nw + threadIdx.x] = a;
   }
 }
@@ -1020,7 +1111,7 @@ void mlp_hv_layout(Alloc& a, MlpF64HvWs* w, int64_t n_s, int64_t n_i, int64_t n_
   // warps stride over the samples; eight blocks of eight warps per SM
   const int head_need = (int)((n_s + kHeadWarps - 1) / kHeadWarps);
   const int head_blocks = head_need < 8 * 148 ? head_need : 8 * 148;
-  const int w2_chunks = (int)((n_s + kW2Chunk - 1) / kW2Chunk);
+  const int w2_chunks = (int)((n_s + kW2ChunkHv - 1) / kW2ChunkHv);
   const int w1_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, (int)n_s);
   const int w1d_splits = splits_for<double, kF64RM, kF64RN, kF64BK>((int)n_i + 1, (int)n_h, 2 * (int)n_s);
   const int maxs = w1_splits > w1d_splits ? w1_splits : w1d_splits;
@@ -1351,29 +1442,41 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   if (st != STADE_OK) return st;
   // head
   PhaseScope ph_head("hv_head", s);
-  const size_t hsm = sizeof(double) * 2 * (size_t)O * (size_t)(H + 1);
-  const int w2_smem = hsm <= 160 * 1024;
+  // w2 / w2d class-major, then (where they fit) each warp's h and hd rows
+  const size_t w2_bytes = sizeof(double) * 2 * (size_t)O * (size_t)(H + 1);
+  const size_t rows_bytes = sizeof(double) * kHeadWarps * 2 * (size_t)H;
+  const int w2_smem = w2_bytes <= 160 * 1024;
+  const int rows_smem = w2_smem && w2_bytes + rows_bytes <= 200 * 1024;
+  const size_t hsm = w2_bytes + (rows_smem ? rows_bytes : 0);
   if (w2_smem && hsm > 48 * 1024)
     STADE_CUDA(cudaFuncSetAttribute(mlp_head_hv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)hsm));
-  // with w2 in shared memory, one wave of blocks (each stages w2 once)
-  const int hgrid = w2_smem ? std::min(w.head_blocks, 2 * tc5::sm_count()) : w.head_blocks;
+  // with w2 in shared memory, one wave of the blocks the SMs hold at once
+  // (each stages w2 once)
+  int head_per_sm = 0;
+  STADE_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&head_per_sm, mlp_head_hv_kernel,
+                                                           kHeadWarps * 32, w2_smem ? hsm : 0));
+  if (head_per_sm < 1) head_per_sm = 1;
+  const int hgrid =
+      w2_smem ? std::min(w.head_blocks, head_per_sm * tc5::sm_count()) : w.head_blocks;
   mlp_head_hv_kernel<<<hgrid, kHeadWarps * 32, w2_smem ? hsm : 0, s>>>(
       lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
-      pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part, w2_smem);
+      pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part, w2_smem,
+      rows_smem);
   STADE_CHECK_LAUNCH();
   st = launch_sum_to_scalar(w.loss_part, hgrid, loss, true, s);
   if (st != STADE_OK) return st;
   st = launch_sum_to_scalar(w.lossd_part, hgrid, lossd, true, s);
   if (st != STADE_OK) return st;
   // W2b, W2bd, b2b, b2bd
-  const dim3 w2g(w.w2_chunks, (H + 31) / 32);
+  const dim3 w2g(w.w2_chunks, (H + 255) / 256);
+  const size_t w2sm = sizeof(double) * kW2ChunkHv * 2 * (O <= 16 ? 16 : 32);
   if (O <= 16)
-    mlp_w2b_hv_partial_kernel<16><<<w2g, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O, kW2Chunk,
-                                                      w.w2_part);
+    mlp_w2b_hv_partial_kernel<16><<<w2g, 256, w2sm, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O,
+                                                         kW2ChunkHv, w.w2_part);
   else
-    mlp_w2b_hv_partial_kernel<32><<<w2g, 256, 0, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O, kW2Chunk,
-                                                      w.w2_part);
+    mlp_w2b_hv_partial_kernel<32><<<w2g, 256, w2sm, s>>>(h, hd, w.gbuf, w.gdbuf, S, H, O,
+                                                         kW2ChunkHv, w.w2_part);
   STADE_CHECK_LAUNCH();
   finish_four_kernel<<<ceil_div_u(2 * n_h * n_o + 2 * n_o, 256), 256, 0, s>>>(
       w.w2_part, w.w2_chunks, n_h * n_o, O, w2b, w2bd, b2b, b2bd);
