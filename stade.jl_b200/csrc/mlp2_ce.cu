@@ -32,6 +32,7 @@ namespace stade {
 namespace {
 
 constexpr int kHeadWarps = 8;   // samples in flight per block
+constexpr int kHvHeadWarps = 16;  // the same for the Float64 HVP head (one block per SM)
 // Sum over the 32 lanes of a[0..15] (each lane its own sixteen values): four
 // halving exchanges leave each lane pair one class's sum, class
 // ((l >> 4) & 1) * 8 + ((l >> 3) & 1) * 4 + ((l >> 2) & 1) * 2 + ((l >> 1) & 1).
@@ -721,7 +722,7 @@ stade_status gemm_f64(int M, int N, int K, LA la, LB lb, Epi epi, double* partia
 // run in every lane over values passed by shuffle; sums over classes are
 // warp sums. Lanes then own hidden units for s1b = (1 - h^2)(hb + W2 g) and
 // its tangent, with g and gd broadcast class by class.
-__global__ void __launch_bounds__(kHeadWarps * 32)
+__global__ void __launch_bounds__(kHvHeadWarps * 32)
 mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ lossbd,
                    const double* __restrict__ y, double* __restrict__ yb,
                    const double* __restrict__ yd, double* __restrict__ ybd,
@@ -736,7 +737,7 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
                    double* __restrict__ s1b, double* __restrict__ s1bd, int n_s, int n_h, int n_o,
                    double* __restrict__ loss_part, double* __restrict__ lossd_part, int w2_smem,
                    int rows_smem) {
-  __shared__ double red[2][kHeadWarps];
+  __shared__ double red[2][kHvHeadWarps];
   // w2 and w2d staged class-major with an odd row stride: the class lanes of
   // the logits loop and the hidden-unit lanes of the s1b loop both read
   // distinct banks (read from global memory instead, [k][c], when they do
@@ -768,7 +769,7 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
   // flight at once; otherwise the rows are read from memory unit by unit
   double* hs = w2sm + 2 * (size_t)n_o * LD + (size_t)warp * 2 * n_h;
   double* hds = hs + n_h;
-  for (int s = blockIdx.x * kHeadWarps + warp; s < n_s; s += gridDim.x * kHeadWarps) {
+  for (int s = blockIdx.x * kHvHeadWarps + warp; s < n_s; s += gridDim.x * kHvHeadWarps) {
     const double* hr = h + (int64_t)s * n_h;
     const double* hdr = hd + (int64_t)s * n_h;
     const int64_t row = (int64_t)s * n_o;
@@ -959,7 +960,7 @@ mlp_head_hv_kernel(const double* __restrict__ lossb, const double* __restrict__ 
   __syncthreads();
   if (threadIdx.x == 0) {
     double a = 0.0, b = 0.0;
-    for (int w = 0; w < kHeadWarps; ++w) { a += red[0][w]; b += red[1][w]; }
+    for (int w = 0; w < kHvHeadWarps; ++w) { a += red[0][w]; b += red[1][w]; }
     loss_part[blockIdx.x] = a;
     lossd_part[blockIdx.x] = b;
   }
@@ -1444,9 +1445,9 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   PhaseScope ph_head("hv_head", s);
   // w2 / w2d class-major, then (where they fit) each warp's h and hd rows
   const size_t w2_bytes = sizeof(double) * 2 * (size_t)O * (size_t)(H + 1);
-  const size_t rows_bytes = sizeof(double) * kHeadWarps * 2 * (size_t)H;
+  const size_t rows_bytes = sizeof(double) * kHvHeadWarps * 2 * (size_t)H;
   const int w2_smem = w2_bytes <= 160 * 1024;
-  const int rows_smem = w2_smem && w2_bytes + rows_bytes <= 200 * 1024;
+  const int rows_smem = w2_smem && w2_bytes + rows_bytes <= 220 * 1024;
   const size_t hsm = w2_bytes + (rows_smem ? rows_bytes : 0);
   if (w2_smem && hsm > 48 * 1024)
     STADE_CUDA(cudaFuncSetAttribute(mlp_head_hv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1455,11 +1456,11 @@ extern "C" stade_status stade_mlp2_ce_hv_f64(
   // (each stages w2 once)
   int head_per_sm = 0;
   STADE_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&head_per_sm, mlp_head_hv_kernel,
-                                                           kHeadWarps * 32, w2_smem ? hsm : 0));
+                                                           kHvHeadWarps * 32, w2_smem ? hsm : 0));
   if (head_per_sm < 1) head_per_sm = 1;
   const int hgrid =
       w2_smem ? std::min(w.head_blocks, head_per_sm * tc5::sm_count()) : w.head_blocks;
-  mlp_head_hv_kernel<<<hgrid, kHeadWarps * 32, w2_smem ? hsm : 0, s>>>(
+  mlp_head_hv_kernel<<<hgrid, kHvHeadWarps * 32, w2_smem ? hsm : 0, s>>>(
       lossb, lossbd, y, yb, yd, ybd, w2, b2, w2d, b2d, h, hb, hd, hbd, z, zb, zd, zbd, p, pb, pd,
       pbd, w.gbuf, w.gdbuf, w.s1b, w.s1bd, S, H, O, w.loss_part, w.lossd_part, w2_smem,
       rows_smem);
