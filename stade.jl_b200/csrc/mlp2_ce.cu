@@ -78,10 +78,8 @@ template <class T> __device__ __forceinline__ T jmax(T a, T b) {
 }
 template <class T> __device__ __forceinline__ T radd(T a, T b);
 template <> __device__ __forceinline__ float radd(float a, float b) { return __fadd_rn(a, b); }
-template <> __device__ __forceinline__ double radd(double a, double b) { return __dadd_rn(a, b); }
 template <class T> __device__ __forceinline__ T rmul(T a, T b);
 template <> __device__ __forceinline__ float rmul(float a, float b) { return __fmul_rn(a, b); }
-template <> __device__ __forceinline__ double rmul(double a, double b) { return __dmul_rn(a, b); }
 
 // ---------------------------------------------------------------------------
 // Per-sample head of the adjoint (Float32 or Float64), one warp per sample.
