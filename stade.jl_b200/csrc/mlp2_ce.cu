@@ -1252,9 +1252,13 @@ extern "C" stade_status stade_mlp2_ce_b_f32(float* loss, const float* lossb, con
   mlp_f32_layout(ca, &w, n_s, n_i, n_h, n_o);
   const int S = (int)n_s, I = (int)n_i, H = (int)n_h, O = (int)n_o;
   MlpPath path = mlp_path(n_s, n_i, n_h);
-  // the TMA path reads x and W1 in place: their base addresses must be 16-byte aligned
+  // the TMA path reads x and W1 in place through TMA, and its logits and s1b
+  // passes read h (and hb) with 8- and 16-byte vector loads: those base
+  // addresses must be 16-byte aligned (h and xb written by the GEMMs are
+  // checked there: a misaligned one takes register stores)
   if (path == MlpPath::Tma &&
-      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w1)) & 15u))
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w1) |
+        reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(hb)) & 15u))
     path = MlpPath::Simt;
 
   if (path == MlpPath::Tma) {

@@ -304,6 +304,34 @@ def test_mlp2_ce_b_unaligned_inputs():
         assert ok, (k, errs)
 
 
+@pytest.mark.parametrize("arrays", [("h",), ("xb",), ("h", "xb")])
+def test_mlp2_ce_b_unaligned_outputs(arrays):
+    """h and / or xb at addresses that are not 16-byte aligned (x and W1
+    aligned). The tensor-core path's logits and s1b passes read h with vector
+    loads, so an unaligned h (or hb) sends the sweep to the CUDA-core
+    contractions; an unaligned xb keeps the tensor-core path, whose input
+    gradient then adds into xb with the one-CTA kernel's register stores
+    instead of TMA reductions. Correct either way, and no fault."""
+    import torch
+    import stadeb200
+    from stadeb200 import _lib
+    st, ints = cases.mlp_state(1000, 784, 512, 10, seeded=True)
+    ref, truth = cases.copy_state(st), _truth(st, ints, cases.oracle_mlp)
+    cases.oracle_mlp(ref, ints)
+    dev = {k: torch.from_numpy(v).cuda() for k, v in st.items()}
+    for k in arrays:
+        big = torch.zeros(dev[k].numel() + 1, dtype=torch.float32, device="cuda")
+        big[1:] = dev[k]
+        dev[k] = big[1:]          # 4-byte offset
+        assert dev[k].data_ptr() % 16 != 0
+    stadeb200.mlp2_ce_b_cuda(*[dev[a] for a in cases.MLP_ARGS], ints["n_s"], ints["n_i"],
+                             ints["n_h"], ints["n_o"])
+    assert _lib.lib().stade_device_error() == 0
+    for k in ("h", "z", "p", "yb", "xb", "w1b", "b1b", "w2b", "b2b", "loss"):
+        ok, errs = f32_verdict(dev[k].cpu().numpy(), ref[k], truth[k])
+        assert ok, (k, errs)
+
+
 @pytest.mark.parametrize("chain", ["1", "8"])
 def test_mlp2_ce_b_tc_chain_lengths(chain):
     """STADE_TC_CHAIN (K blocks per TMEM accumulation chain; read once per
