@@ -3,7 +3,7 @@ as generated text (test/val-corpus/<name>.jl), run by the interpreter
 tests/jlsub.py on seeded inputs, with the reference text's sha256.
 
 Run here, where the reference checkout exists (it does not travel to the GPU
-box): python tests/golden/make_exemplar_golden.py [path to the reference]
+box): python tests/golden/make_exemplar_golden.py <path to the reference>
 
 Each fixture holds the generated argument order, the inputs ("in_<arg>"),
 the outputs after the call ("out_<arg>"), the returned scalars ("ret"), and
@@ -125,4 +125,8 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("STADE_REFERENCE_DIR")
+    if not ref:
+        sys.exit("usage: make_exemplar_golden.py <path to the STADE.jl checkout> "
+                 "(or set STADE_REFERENCE_DIR)")
+    main(ref)
